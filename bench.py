@@ -1,0 +1,358 @@
+#!/usr/bin/env python3
+"""Benchmark of the PTO-WSP cuda_sm100a task loop (one JSON line on rank 0).
+
+Default workload: BASELINE config 2, the row-softmax tile workload
+X[32,2048,32,256] f32 (Tile[32,256], P(batch) x P(tiles)), through the
+reference-facing C ABI.  A *step* is one pass of the task loop over the whole
+workload.
+
+* ``value``  -- GB/s (algorithmic bytes: 2 x 4 B per element) with X and Y
+  resident in HBM; K back-to-back steps timed with CUDA events on the launch
+  stream, max over ranks.  Inputs (2 GiB) exceed L2 (126 MB), so no flush.
+* ``e2e``    -- the same metric through the same call with pinned host numpy
+  buffers: every step stages X host->device and Y device->host.
+* ``roofline`` -- achieved bytes per launch / measured launch time vs the
+  measured HBM copy peak (MEASURED_PEAKS.json); ``traffic`` from the ncu
+  summary in profiles/ when one exists.
+* ``cpu_baseline`` -- the C port of the CPU-sim loops (oracle/cpu_kernels.c) on
+  the host cores, rank 0 at N=1, bounded sample.
+
+``--impl reference`` times only that CPU implementation (all host threads) and
+prints its own line.  Multi-GPU (torchrun): each rank runs the same per-rank
+shard (weak scaling, no data-path collective).
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    "softmax": {"config": "config 2: row softmax Tile[32,256] f32, X[32,2048,32,256]", "batch": 32, "tiles": 2048,
+                "rows": 32, "cols": 256},
+    "rmsnorm": {"config": "config 1: RMSNorm Tile[16,128] f32, X[64,4096,16,128] (GPU scale)", "batch": 64,
+                "tiles": 4096, "rows": 16, "cols": 128},
+}
+
+
+def _env_int(k: str, d: int) -> int:
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles(kernel: str, workload: str) -> float | None:
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        v = d.get(f"{workload}:{kernel}")
+        return float(v["bytes_per_launch"]) if v else None
+    except Exception:  # noqa: BLE001
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = [r for r in csv.reader(io.StringIO(getattr(self, "out", ""))) if len(r) >= 9]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                s, m, pw = float(r[1]), float(r[2]), float(r[3])
+            except ValueError:
+                continue
+            mx = m
+            if pw > 250.0:  # under load
+                sm.append(s)
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples_under_load": len(sm), "samples": len(rows)}
+
+
+def gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        if local_rank < len(parts) and parts[local_rank].strip().isdigit():
+            return int(parts[local_rank])
+    return local_rank
+
+
+def make_softmax_inputs(torch, B, T, R, Cc, device, seed=0):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    x = torch.randn((B, T, R, Cc), generator=g, device=device, dtype=torch.float32) * 4.0
+    mask = torch.rand((B, T, R, Cc), generator=g, device=device) < 0.01
+    x[mask] = 30.0
+    return x
+
+
+def make_rmsnorm_inputs(torch, B, T, R, Cc, device, seed=0):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return torch.randn((B, T, R, Cc), generator=g, device=device, dtype=torch.float32)
+
+
+def cpu_baseline(kind: str, x_host, rows: int, cols: int, budget_s: float = 12.0) -> dict:
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+
+    import cpu_native
+
+    nth = cpu_native.threads()
+    tiles_total = x_host.size // (rows * cols)
+    flat = x_host.reshape(tiles_total, rows, cols)
+    n = min(tiles_total, 2048)
+    y = np.empty_like(flat[:n])
+    t0 = time.perf_counter()
+    cpu_native.row_tiles(kind, np.ascontiguousarray(flat[:n]), y, rows, cols, nth)
+    dt = time.perf_counter() - t0
+    # grow the sample to ~budget_s of CPU work (bounded by the workload)
+    n2 = int(min(tiles_total, max(n, n * budget_s / max(dt, 1e-6) * 0.5)))
+    y = np.empty((n2, rows, cols), np.float32)
+    t0 = time.perf_counter()
+    cpu_native.row_tiles(kind, flat[:n2], y, rows, cols, nth)
+    dt = time.perf_counter() - t0
+    gbs = n2 * rows * cols * 8 / dt / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": nth, "kind": "port",
+            "sample": f"{n2} of {tiles_total} tiles ({n2 * rows * cols * 4 / 2**20:.0f} MiB in), {dt:.2f} s, "
+                      f"C port of the CPU-sim tile loop (oracle/cpu_kernels.c), {nth} threads"}
+
+
+def run_reference(args, wl: dict, rank: int) -> None:
+    if rank != 0:
+        return
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import cpu_native
+
+    rows, cols = wl["rows"], wl["cols"]
+    tiles = wl["batch"] * wl["tiles"]
+    sample_tiles = min(tiles, 8192)
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal((sample_tiles, rows, cols), dtype=np.float32) * (4.0 if args.workload == "softmax" else 1.0))
+    if args.workload == "softmax":
+        x[rng.random(x.shape) < 0.01] = 30.0
+    y = np.empty_like(x)
+    nth = cpu_native.threads()
+    for _ in range(args.warmup):
+        cpu_native.row_tiles(args.workload, x, y, rows, cols, nth)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_native.row_tiles(args.workload, x, y, rows, cols, nth)
+    dt = time.perf_counter() - t0
+    gbs = sample_tiles * rows * cols * 8 * args.steps / dt / 1e9
+    line = {
+        "impl": "reference", "metric": f"{args.workload} task-loop throughput (algorithmic HBM bytes)",
+        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy)",
+        "config": {"workload": wl["config"], "sample_tiles_per_step": sample_tiles},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nth, "kind": "port",
+                         "sample": f"{sample_tiles} tiles per step of {tiles}; C port of the CPU-sim tile loop "
+                                   f"(oracle/cpu_kernels.c), {nth} threads (reference CPU-sim needs the absent pto-isa)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="softmax", choices=sorted(WORKLOADS))
+    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default: --steps, max 20)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    wl = WORKLOADS[args.workload]
+
+    rank = _env_int("RANK", 0)
+    world = _env_int("WORLD_SIZE", 1)
+    local_rank = _env_int("LOCAL_RANK", 0)
+
+    if args.impl == "reference":
+        run_reference(args, wl, rank)
+        return
+
+    import numpy as np
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from pto_wsp_b200 import workloads
+    from pto_wsp_b200.runtime import CudaExecutable
+
+    B, T, R, Cc = wl["batch"], wl["tiles"], wl["rows"], wl["cols"]
+    plan = (workloads.softmax_plan if args.workload == "softmax" else workloads.rmsnorm_plan)(B, T, R, Cc)
+    ex = CudaExecutable(plan, device=local_rank)
+    stream = torch.cuda.current_stream(dev)
+    ex.set_stream(stream)
+    ex.set_option("sync", 0)
+    mk = make_softmax_inputs if args.workload == "softmax" else make_rmsnorm_inputs
+    x = mk(torch, B, T, R, Cc, dev, seed=1000 + rank)
+    y = torch.empty_like(x)
+    elems = x.numel()
+    alg_bytes = elems * 8  # read x + write y, f32
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident value ----
+    for _ in range(args.warmup):
+        ex.run_with_symbols([x, y], {}, {}, {})
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    with ClockSampler(gpu_index(local_rank)) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            ex.run_with_symbols([x, y], {}, {}, {})
+            launches += int(ex.timing()["launches"])
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        ms_max = max_over_ranks(ms)
+
+        # ---- end-to-end through the same call with pinned host buffers ----
+        ex.set_option("sync", 1)
+        xh_t = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        yh_t = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh_t.copy_(x)
+        xh, yh = xh_t.numpy(), yh_t.numpy()
+        e2e_steps = args.e2e_steps or min(args.steps, 20)
+        ex.run_with_symbols([xh, yh], {}, {}, {})  # warm: device staging buffers
+        barrier()
+        t0 = time.perf_counter()
+        h2d = d2h = 0
+        for _ in range(e2e_steps):
+            ex.run_with_symbols([xh, yh], {}, {}, {})
+            tm = ex.timing()
+            h2d += tm["h2d_bytes"]
+            d2h += tm["d2h_bytes"]
+        barrier()
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+    clocks = clk.summary()
+
+    value = world * alg_bytes * args.steps / (ms_max / 1e3) / 1e9
+    e2e = world * alg_bytes * e2e_steps / e2e_s / 1e9
+    peak, peak_kind = peaks()
+    per_launch_ms = ms / args.steps
+    achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
+    kernel_name = "softmax_rows" if args.workload == "softmax" else "rmsnorm_rows"
+    traffic = traffic_from_profiles(kernel_name, args.workload)
+
+    # spot-check the last device result against the numpy definition on a few tiles
+    xs = x.reshape(-1, R, Cc)[:64].double().cpu().numpy()
+    ys = y.reshape(-1, R, Cc)[:64].double().cpu().numpy()
+    if args.workload == "softmax":
+        ref = np.exp(xs - xs.max(-1, keepdims=True))
+        ref /= ref.sum(-1, keepdims=True)
+    else:
+        ref = xs / np.sqrt((xs * xs).mean(-1, keepdims=True))
+    check = float(np.max(np.abs(ys - ref) / (np.abs(ref) + 1e-30)))
+
+    if rank == 0:
+        line = {
+            "metric": f"{args.workload} task-loop throughput (algorithmic HBM bytes)",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded torch.randn on device)",
+            "config": {"workload": wl["config"], "global_batch": B * world, "per_rank_batch": B, "tiles": T,
+                       "tile": [R, Cc], "parallelism": f"P(batch) sharded, {world} rank(s)",
+                       "l2": "inputs 2 GiB > 126 MB L2 (no flush needed)"},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": kernel_name, "bytes_per_launch": alg_bytes},
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d // e2e_steps,
+                    "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps,
+                    "path": "CodegenExecutable-style run_with_symbols with pinned numpy buffers"},
+            "clocks": clocks,
+            "max_rel_err_vs_fp64_sample": check,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.workload, xh, R, Cc)
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,162 @@
+/*
+ * ptowsp_cuda.h -- C ABI of the PTO-WSP cuda_sm100a execution target.
+ *
+ * The reference builds, per workload, a CPU-sim shared library whose entry
+ * point is `uint64_t <module>_main(RuntimeContext*, CSPTContext*)` and loads it
+ * with dlopen/dlsym (reference: src/python/pto_codegen.cpp:3510-3576).  This
+ * library is the CUDA replacement: a workload *plan* (the reference ir::Module
+ * serialised as JSON, format "ptowsp-plan/1") is compiled once into a program
+ * handle, and each run walks the task loop on the host, builds a device task
+ * table and launches sm_100a kernels.  No torch types cross this boundary:
+ * plain pointers, sizes and the reference's own callback structs.
+ *
+ * Threading: a program handle is used by one thread at a time (the reference
+ * makes one call per execute(), program.py:678-681).  Errors are reported
+ * through return codes plus ptowsp_cuda_last_error() -- the side channel the
+ * reference entry ABI does not have.
+ */
+#ifndef PTOWSP_CUDA_H
+#define PTOWSP_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PTOWSP_API __attribute__((visibility("default")))
+#else
+#define PTOWSP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------- */
+/* Reference ABI structs, same field order and types as the reference headers */
+/* ------------------------------------------------------------------------- */
+
+/* Per-task descriptor (reference: include/pto/wsp/codegen/abi/kernel_abi.hpp:21-41). */
+struct KernelTaskDesc {
+    const uint64_t* args;        /* axis args, (valid_row, valid_col) per tensor param, scalars */
+    uint32_t num_args;
+    uint32_t num_axis_args;
+    void* const* tensor_ptrs;    /* tile base pointers (device memory for this target) */
+    const uint64_t* tensor_strides; /* [s3, s4] per tensor param, in elements */
+    uint32_t num_tensors;
+    uint32_t kernel_id;
+    uint32_t task_id;
+};
+
+/* Reference: kernel_abi.hpp:47-62. */
+struct TimingConfig {
+    uint64_t loop_overhead;
+    uint64_t dispatch_overhead;
+    uint64_t channel_latency;
+};
+
+struct CSPTContext {
+    void* ctx;
+    void (*advance_cycles)(void* ctx, uint64_t cycles);
+    uint64_t (*get_time)(void* ctx);
+    const struct TimingConfig* timing;
+};
+
+/* Reference: kernel_abi.hpp:70. */
+typedef uint64_t (*KernelFn)(const struct KernelTaskDesc* task, struct CSPTContext* cspt);
+
+/* Run-time bindings of one execute() (reference: include/pto/wsp/codegen/abi/workload_abi.hpp:17-41).
+ * get_tensor_ptr may return host memory (staged to HBM around the run) or
+ * device memory (used in place); the runtime asks the driver which. */
+struct RuntimeContext {
+    int64_t (*get_axis_size)(void* ctx, const char* name);
+    uint64_t (*get_symbol_u64)(void* ctx, uint64_t symbol_id);
+    void* (*get_symbol_ptr)(void* ctx, uint64_t symbol_id);
+    uint64_t (*get_slot_u64)(void* ctx, uint32_t slot);
+    void (*set_slot_u64)(void* ctx, uint32_t slot, uint64_t value);
+    void* (*get_tensor_ptr)(void* ctx, uint32_t tensor_id);
+    uint64_t (*get_tensor_stride)(void* ctx, uint32_t tensor_id, uint32_t dim);
+    KernelFn (*get_kernel)(void* ctx, uint32_t kernel_id);
+    void* ctx;
+};
+
+/* Reference: workload_abi.hpp:71. */
+typedef uint64_t (*WorkloadFn)(struct RuntimeContext* ctx, struct CSPTContext* cspt);
+
+/* ------------------------------------------------------------------------- */
+/* cuda_sm100a target                                                          */
+/* ------------------------------------------------------------------------- */
+
+typedef struct ptowsp_program ptowsp_program;
+
+enum ptowsp_status {
+    PTOWSP_OK = 0,
+    PTOWSP_ERR_PLAN = 1,          /* malformed plan / type error (reference: CompileError) */
+    PTOWSP_ERR_UNSUPPORTED = 2,   /* op, node or kernel body the GPU target cannot run */
+    PTOWSP_ERR_CUDA = 3,          /* CUDA runtime error */
+    PTOWSP_ERR_ARG = 4,           /* bad argument (null pointer, missing tensor, ...) */
+    PTOWSP_ERR_DEVICE = 5,        /* a kernel reported an error status (bounds, timeout) */
+    PTOWSP_ERR_LIMIT = 6          /* a size beyond a documented limit */
+};
+
+/* Compile a plan into a program for CUDA device `device`.
+ * Replaces compile_codegen(module, CompileOptions{target}) for target
+ * "cuda_sm100a" (reference: src/python/pto_codegen.cpp:3352-3434): type checks,
+ * matches every kernel to a CUDA implementation, and fails with
+ * PTOWSP_ERR_UNSUPPORTED (never a CPU fallback) when one has none. */
+PTOWSP_API int ptowsp_cuda_compile(const char* plan_json, size_t plan_len, int device, ptowsp_program** out);
+
+/* Run the workload once.  Replaces the generated entry point
+ * `<module>_main(RuntimeContext*, CSPTContext*)` (reference:
+ * include/pto/wsp/codegen/abi/workload_abi.hpp:71, emitted by
+ * src/python/pto_codegen.cpp:1468-2709).  Returns the makespan of the
+ * reference cycle model (Scheduler::issue, pto_codegen.cpp:1562-1606), the same
+ * u64 the CPU-sim returns; 0 with ptowsp_cuda_status() != 0 on failure.
+ * Blocks until the device work and copies of this run are done. */
+PTOWSP_API uint64_t ptowsp_cuda_main(ptowsp_program* prog, struct RuntimeContext* ctx, struct CSPTContext* cspt);
+
+/* Run one task of kernel `kernel_name` (all tensor pointers in `task` are
+ * device pointers).  Replaces the per-kernel entry
+ * `<kernel>(const KernelTaskDesc*, CSPTContext*)` (reference:
+ * include/pto/wsp/codegen/abi/kernel_abi.hpp:70; called per task by the NPU
+ * dispatcher, src/python/pto_codegen.cpp:3263-3268).  Returns the kernel's
+ * model cycle charge. */
+PTOWSP_API uint64_t ptowsp_cuda_run_task(ptowsp_program* prog, const char* kernel_name, const struct KernelTaskDesc* task);
+
+/* Status of the last call on `prog` (0 = ok) and a thread-local message. */
+PTOWSP_API int ptowsp_cuda_status(const ptowsp_program* prog);
+PTOWSP_API const char* ptowsp_cuda_last_error(void);
+
+/* Launch on this CUDA stream (cudaStream_t); NULL = the program's own stream. */
+PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
+
+/* Integer options: "pipeline_chunks" (host-staged runs overlap copy and
+ * compute in this many chunks, default 4), "cache_plans" (reuse the task table
+ * of static workloads across runs, default 1), "sync" (block in main, default 1). */
+PTOWSP_API int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value);
+
+typedef struct ptowsp_timing {
+    double gpu_ms;        /* kernel time of the last run (CUDA events) */
+    double total_ms;      /* wall time of the last ptowsp_cuda_main call */
+    uint64_t launches;    /* kernel launches of the last run */
+    uint64_t tasks;       /* tasks executed */
+    uint64_t waves;       /* dependency waves */
+    uint64_t h2d_bytes;   /* host->device bytes staged */
+    uint64_t d2h_bytes;   /* device->host bytes staged */
+} ptowsp_timing;
+
+PTOWSP_API int ptowsp_cuda_last_timing(const ptowsp_program* prog, ptowsp_timing* out);
+
+/* JSON description of the compiled program (kernel -> implementation, task
+ * windows, launch shapes).  Owned by `prog`, valid until the next call. */
+PTOWSP_API const char* ptowsp_cuda_describe(ptowsp_program* prog);
+
+PTOWSP_API void ptowsp_cuda_destroy(ptowsp_program* prog);
+
+/* Number of CUDA devices visible to this library (0 without a GPU). */
+PTOWSP_API int ptowsp_cuda_device_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PTOWSP_CUDA_H */

@@ -1,0 +1,116 @@
+// Structures shared by the host runtime and the sm_100a kernels.
+//
+// A launch executes a *task batch*: a slice of the device task table.  Each
+// task record holds, per kernel tensor param, the element offset of the task's
+// tile view from the tensor base (base + sum(idx * stride), the pointer the
+// reference computes per task at src/python/pto_codegen.cpp:2570-2592), then
+// the task's axis args and scalar args (the u64 `args` of KernelTaskDesc,
+// include/pto/wsp/codegen/abi/kernel_abi.hpp:21-41).
+#pragma once
+
+#include <cstdint>
+
+#ifdef __CUDACC__
+#include <cuda_runtime.h>
+#else
+#include <cuda_runtime_api.h>
+#endif
+
+namespace ptowsp::dev {
+
+constexpr int kMaxParams = 8;
+
+// Device status word bits (set by kernels, read by the host after a run).
+enum : int {
+    kErrBounds = 1,      // an index computed from task data left its tensor
+    kErrTimeout = 2,     // a bounded wait gave up
+    kErrShape = 4,       // a runtime size exceeded a kernel's static limit
+};
+
+enum ParamType : int { PT_F32 = 0, PT_F16 = 1, PT_I32 = 2, PT_U32 = 3, PT_I64 = 4, PT_U64 = 5, PT_OTHER = 6 };
+
+struct ParamDesc {
+    char* base;       // device base pointer of the tensor
+    int64_t s3, s4;   // row / column stride of the tile view, in elements
+    int64_t numel_span;  // elements addressable from base (bounds checks)
+    int rows, cols;   // static tile shape of the kernel param
+    int type;         // ParamType
+    int elem_bytes;
+};
+
+struct TaskBatch {
+    const int64_t* rec;  // [ntasks][stride]
+    int64_t ntasks;
+    int stride;          // nparams + naxis + nscalar
+    int nparams, naxis, nscalar;
+    ParamDesc p[kMaxParams];
+    int* err;            // device status word
+};
+
+// ---------------------------------------------------------------------------
+// Generic tile program (any pto.* kernel without a hand-written kernel).
+// Mirrors the op set of the reference kernel emitter
+// (src/python/pto_codegen.cpp:785-1231).
+// ---------------------------------------------------------------------------
+
+enum TPOp : int {
+    TP_LOAD = 1, TP_STORE, TP_BIN, TP_BINS, TP_EXP, TP_RSQRT, TP_ROWSUM, TP_ROWMAX, TP_ROWMEAN,
+    TP_MATMUL, TP_IOTA, TP_TSORT32, TP_EXTRACT, TP_MOV
+};
+enum TPBin : int { BIN_ADD = 0, BIN_SUB, BIN_MUL, BIN_DIV, BIN_MAX, BIN_MIN };
+enum TPMode : int { MODE_FULL = 0, MODE_ROW, MODE_COL };
+enum TPWord : int { W_F32 = 0, W_I32 = 1, W_U32 = 2 };
+
+struct TPSlot {
+    int off;      // word offset in shared memory
+    int rows, cols, pitch;
+    int word;     // TPWord
+};
+
+struct TPInstr {
+    int op, sub, mode;
+    int dst, a, b;      // slot ids (or param index for LOAD/STORE)
+    int param;          // tensor param index (LOAD/STORE)
+    int rows, cols, k;  // shape info
+    int scalar_src;     // BINS: -1 = literal `fval`/`ival`; >=0 scalar param index
+    int scalar_first;   // BINS div: scalar / tile
+    float fval;
+    int ival;
+};
+
+constexpr int kTPMaxSlots = 32;
+constexpr int kTPMaxInstr = 64;
+
+struct TileProgram {
+    int ninstr, nslots, smem_words;
+    TPSlot slots[kTPMaxSlots];
+    TPInstr ins[kTPMaxInstr];
+    int scalar_types[kMaxParams];  // per scalar param: 0 f32, 1 i32, 2 i64, 3 bool
+};
+
+// ---------------------------------------------------------------------------
+// Launchers (defined in the .cu files).  All return cudaSuccess or the launch
+// error; `workers` caps the number of CTAs (task window), 0 = automatic.
+// ---------------------------------------------------------------------------
+
+cudaError_t launch_rmsnorm_rows(const TaskBatch& b, int workers, cudaStream_t s);
+cudaError_t launch_softmax_rows(const TaskBatch& b, int workers, cudaStream_t s);
+cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev, int smem_bytes, int workers,
+                                cudaStream_t s);
+int tile_program_max_smem();
+
+// Matmul tile task: C[M,N] (f32) = A[M,K] (f16) . B[K,N] (f16) (+ C if accumulate).
+// Params: 0 = A, 1 = B, 2 = C (same tensor for InOut).
+cudaError_t launch_matmul_tiles(const TaskBatch& b, int accumulate, int workers, cudaStream_t s);
+
+// Built-ins.
+cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int num_kv_heads, int workers, void* scratch,
+                                size_t scratch_bytes, cudaStream_t s);
+size_t paged_decode_scratch_bytes(const TaskBatch& b, int page_size);
+cudaError_t launch_indexer_score(const TaskBatch& b, int workers, cudaStream_t s);
+cudaError_t launch_topk_select(const TaskBatch& b, int workers, void* scratch, size_t scratch_bytes, cudaStream_t s);
+size_t topk_select_scratch_bytes(const TaskBatch& b);
+
+int sm_count();
+
+}  // namespace ptowsp::dev

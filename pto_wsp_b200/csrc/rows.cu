@@ -1,0 +1,436 @@
+// Row-wise tile kernels for sm_100a: RMSNorm, softmax, and the generic tile
+// program.  These are HBM-bound: each element is read once and written once,
+// so the kernels stream rows with 128-bit non-temporal loads, keep a row in
+// registers (one warp per row), reduce with warp shuffles and store with
+// streaming stores.  A launch covers one task batch; tiles are found through
+// the device task table (see device.hpp).
+//
+// Semantics follow the tile-op sequences the reference emits:
+//   RMSNorm  TMUL -> TROWSUM -> TDIVS(cols) -> TRSQRT -> TROWEXPANDMUL -> TSTORE
+//            (src/python/pto_codegen.cpp:990-1110, 1112-1130, 1194-1221)
+//   softmax  TROWMAX -> TROWEXPANDSUB -> TEXP -> TROWSUM -> TROWEXPANDDIV
+// The reference RMSNorm has no epsilon (examples/e2e_rmsnorm/golden.py:6-10).
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "device.hpp"
+
+namespace ptowsp::dev {
+
+namespace {
+
+__device__ __forceinline__ float4 ld_stream(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream(float* p, float4 v) {
+    asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+struct RmsNormOp {
+    template <int V>
+    __device__ __forceinline__ static void apply(float4 (&x)[V], int cols) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < V; ++j) ss += x[j].x * x[j].x + x[j].y * x[j].y + x[j].z * x[j].z + x[j].w * x[j].w;
+        ss = warp_sum(ss);
+        const float mean = ss / static_cast<float>(cols);   // TROWSUM, TDIVS(cols)
+        const float inv = 1.0f / sqrtf(mean);                // TRSQRT
+#pragma unroll
+        for (int j = 0; j < V; ++j) {                        // TROWEXPANDMUL
+            x[j].x *= inv;
+            x[j].y *= inv;
+            x[j].z *= inv;
+            x[j].w *= inv;
+        }
+    }
+};
+
+struct SoftmaxOp {
+    template <int V>
+    __device__ __forceinline__ static void apply(float4 (&x)[V], int) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < V; ++j) m = fmaxf(m, fmaxf(fmaxf(x[j].x, x[j].y), fmaxf(x[j].z, x[j].w)));
+        m = warp_max(m);                                     // TROWMAX
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < V; ++j) {                        // TROWEXPANDSUB, TEXP
+            x[j].x = expf(x[j].x - m);
+            x[j].y = expf(x[j].y - m);
+            x[j].z = expf(x[j].z - m);
+            x[j].w = expf(x[j].w - m);
+            s += (x[j].x + x[j].y) + (x[j].z + x[j].w);
+        }
+        s = warp_sum(s);                                     // TROWSUM
+#pragma unroll
+        for (int j = 0; j < V; ++j) {                        // TROWEXPANDDIV
+            x[j].x = x[j].x / s;
+            x[j].y = x[j].y / s;
+            x[j].z = x[j].z / s;
+            x[j].w = x[j].w / s;
+        }
+    }
+};
+
+// One warp per row; each warp keeps RPW rows (V float4 per lane each) in
+// flight.  Param 0 = input tile, param 1 = output tile (both f32, s4 == 1,
+// 16-byte aligned rows -- checked by the host before choosing this kernel).
+template <class Op, int V, int RPW>
+__global__ void __launch_bounds__(256) row_kernel(TaskBatch b) {
+    const int R = b.p[0].rows;
+    const int cols = V * 128;
+    const int64_t total_rows = b.ntasks * static_cast<int64_t>(R);
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const float* __restrict__ xb = reinterpret_cast<const float*>(b.p[0].base);
+    float* __restrict__ yb = reinterpret_cast<float*>(b.p[1].base);
+    const int64_t xs3 = b.p[0].s3, ys3 = b.p[1].s3;
+
+    for (int64_t row0 = warp * RPW; row0 < total_rows; row0 += nwarps * RPW) {
+        float4 v[RPW][V];
+        int64_t yoff[RPW];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            const int64_t row = row0 + r;
+            yoff[r] = -1;
+            if (row < total_rows) {
+                const int64_t task = row / R;
+                const int rr = static_cast<int>(row - task * R);
+                const int64_t* rec = b.rec + task * b.stride;
+                const int64_t xo = rec[0] + rr * xs3;
+                yoff[r] = rec[1] + rr * ys3;
+                const float* px = xb + xo + lane * 4;
+#pragma unroll
+                for (int j = 0; j < V; ++j) v[r][j] = ld_stream(px + j * 128);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            if (yoff[r] < 0) continue;
+            Op::template apply<V>(v[r], cols);
+            float* py = yb + yoff[r] + lane * 4;
+#pragma unroll
+            for (int j = 0; j < V; ++j) st_stream(py + j * 128, v[r][j]);
+        }
+    }
+}
+
+template <class Op, int V, int RPW>
+cudaError_t launch_rows_t(const TaskBatch& b, int workers, cudaStream_t s) {
+    const int threads = 256;
+    const int64_t total_rows = b.ntasks * static_cast<int64_t>(b.p[0].rows);
+    const int64_t rows_per_block = (threads / 32) * RPW;
+    int64_t blocks = (total_rows + rows_per_block - 1) / rows_per_block;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_kernel<Op, V, RPW>, threads, 0);
+    const int64_t cap = static_cast<int64_t>(std::max(per_sm, 1)) * sm_count();
+    blocks = std::min(blocks, cap);
+    if (workers > 0) blocks = std::min<int64_t>(blocks, workers);
+    blocks = std::max<int64_t>(blocks, 1);
+    row_kernel<Op, V, RPW><<<static_cast<unsigned>(blocks), threads, 0, s>>>(b);
+    return cudaGetLastError();
+}
+
+template <class Op>
+cudaError_t launch_rows(const TaskBatch& b, int workers, cudaStream_t s) {
+    switch (b.p[0].cols) {
+        case 128: return launch_rows_t<Op, 1, 8>(b, workers, s);
+        case 256: return launch_rows_t<Op, 2, 4>(b, workers, s);
+        case 512: return launch_rows_t<Op, 4, 2>(b, workers, s);
+        case 1024: return launch_rows_t<Op, 8, 1>(b, workers, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Generic tile program: one CTA per task, tiles in shared memory as 32-bit
+// words, instructions executed in order with a barrier between them.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float load_elem_f(const ParamDesc& p, int64_t off) {
+    switch (p.type) {
+        case PT_F32: return reinterpret_cast<const float*>(p.base)[off];
+        case PT_F16: return __half2float(reinterpret_cast<const __half*>(p.base)[off]);
+        case PT_I32: return static_cast<float>(reinterpret_cast<const int32_t*>(p.base)[off]);
+        case PT_U32: return static_cast<float>(reinterpret_cast<const uint32_t*>(p.base)[off]);
+        case PT_I64: return static_cast<float>(reinterpret_cast<const int64_t*>(p.base)[off]);
+        case PT_U64: return static_cast<float>(reinterpret_cast<const uint64_t*>(p.base)[off]);
+        default: return 0.f;
+    }
+}
+
+__device__ __forceinline__ uint32_t load_elem_w(const ParamDesc& p, int64_t off, int word) {
+    if (word == W_F32) return __float_as_uint(load_elem_f(p, off));
+    switch (p.type) {
+        case PT_I32: case PT_U32: return reinterpret_cast<const uint32_t*>(p.base)[off];
+        case PT_I64: case PT_U64: return static_cast<uint32_t>(reinterpret_cast<const uint64_t*>(p.base)[off]);
+        case PT_F32: return static_cast<uint32_t>(static_cast<int32_t>(reinterpret_cast<const float*>(p.base)[off]));
+        case PT_F16: return static_cast<uint32_t>(static_cast<int32_t>(__half2float(reinterpret_cast<const __half*>(p.base)[off])));
+        default: return 0u;
+    }
+}
+
+__device__ __forceinline__ void store_elem(const ParamDesc& p, int64_t off, uint32_t w, int word) {
+    const float f = word == W_F32 ? __uint_as_float(w) : (word == W_I32 ? static_cast<float>(static_cast<int32_t>(w)) : static_cast<float>(w));
+    switch (p.type) {
+        case PT_F32: reinterpret_cast<float*>(p.base)[off] = f; break;
+        case PT_F16: reinterpret_cast<__half*>(p.base)[off] = __float2half_rn(f); break;
+        case PT_I32: reinterpret_cast<int32_t*>(p.base)[off] = word == W_F32 ? static_cast<int32_t>(f) : static_cast<int32_t>(w); break;
+        case PT_U32: reinterpret_cast<uint32_t*>(p.base)[off] = word == W_F32 ? static_cast<uint32_t>(f) : w; break;
+        case PT_I64: reinterpret_cast<int64_t*>(p.base)[off] = word == W_F32 ? static_cast<int64_t>(f) : static_cast<int64_t>(static_cast<int32_t>(w)); break;
+        case PT_U64: reinterpret_cast<uint64_t*>(p.base)[off] = word == W_F32 ? static_cast<uint64_t>(f) : static_cast<uint64_t>(w); break;
+        default: break;
+    }
+}
+
+__device__ __forceinline__ float bin_f(int op, float a, float b) {
+    switch (op) {
+        case BIN_ADD: return __fadd_rn(a, b);
+        case BIN_SUB: return __fsub_rn(a, b);
+        case BIN_MUL: return __fmul_rn(a, b);
+        case BIN_DIV: return __fdiv_rn(a, b);
+        case BIN_MAX: return fmaxf(a, b);
+        default: return fminf(a, b);
+    }
+}
+
+__device__ __forceinline__ int32_t bin_i(int op, int32_t a, int32_t b) {
+    switch (op) {
+        case BIN_ADD: return a + b;
+        case BIN_SUB: return a - b;
+        case BIN_MUL: return a * b;
+        case BIN_DIV: return b ? a / b : 0;
+        case BIN_MAX: return a > b ? a : b;
+        default: return a < b ? a : b;
+    }
+}
+
+__global__ void __launch_bounds__(256) tile_program_kernel(TaskBatch b, const TileProgram* __restrict__ prog) {
+    extern __shared__ uint32_t sm[];
+    const int ninstr = prog->ninstr;
+    for (int64_t task = blockIdx.x; task < b.ntasks; task += gridDim.x) {
+        const int64_t* rec = b.rec + task * b.stride;
+        for (int ii = 0; ii < ninstr; ++ii) {
+            const TPInstr in = prog->ins[ii];
+            switch (in.op) {
+                case TP_LOAD: {
+                    const TPSlot d = prog->slots[in.dst];
+                    const ParamDesc& p = b.p[in.param];
+                    const int64_t base = rec[in.param];
+                    for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
+                        const int r = e / in.cols, c = e - r * in.cols;
+                        const int64_t off = base + r * p.s3 + c * p.s4;
+                        uint32_t w = 0;
+                        if (off >= 0 && off < p.numel_span) w = load_elem_w(p, off, d.word);
+                        else atomicOr(b.err, kErrBounds);
+                        sm[d.off + r * d.pitch + c] = w;
+                    }
+                    break;
+                }
+                case TP_STORE: {
+                    const TPSlot a = prog->slots[in.a];
+                    const ParamDesc& p = b.p[in.param];
+                    const int64_t base = rec[in.param];
+                    for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
+                        const int r = e / in.cols, c = e - r * in.cols;
+                        const int64_t off = base + r * p.s3 + c * p.s4;
+                        const uint32_t w = (r < a.rows && c < a.cols) ? sm[a.off + r * a.pitch + c] : 0u;
+                        if (off >= 0 && off < p.numel_span) store_elem(p, off, w, a.word);
+                        else atomicOr(b.err, kErrBounds);
+                    }
+                    break;
+                }
+                case TP_MOV: {
+                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                    for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
+                        const int r = e / d.cols, c = e - r * d.cols;
+                        sm[d.off + r * d.pitch + c] = sm[a.off + r * a.pitch + c];
+                    }
+                    break;
+                }
+                case TP_BIN: {
+                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], bb = prog->slots[in.b];
+                    for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
+                        const int r = e / d.cols, c = e - r * d.cols;
+                        const uint32_t wa = sm[a.off + r * a.pitch + c];
+                        const int bi = in.mode == MODE_FULL ? (bb.off + r * bb.pitch + c)
+                                       : in.mode == MODE_ROW ? (bb.off + r) : (bb.off + c);
+                        const uint32_t wb = sm[bi];
+                        uint32_t out;
+                        if (d.word == W_F32) out = __float_as_uint(bin_f(in.sub, __uint_as_float(wa), __uint_as_float(wb)));
+                        else out = static_cast<uint32_t>(bin_i(in.sub, static_cast<int32_t>(wa), static_cast<int32_t>(wb)));
+                        sm[d.off + r * d.pitch + c] = out;
+                    }
+                    break;
+                }
+                case TP_BINS: {
+                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                    float fs = in.fval;
+                    int32_t is = in.ival;
+                    if (in.scalar_src >= 0) {
+                        const uint64_t raw = static_cast<uint64_t>(rec[b.nparams + b.naxis + in.scalar_src]);
+                        const int st = prog->scalar_types[in.scalar_src];
+                        if (st == 0) {
+                            fs = __uint_as_float(static_cast<uint32_t>(raw));
+                            is = static_cast<int32_t>(fs);
+                        } else {
+                            is = static_cast<int32_t>(raw);
+                            fs = st == 2 ? static_cast<float>(static_cast<int64_t>(raw)) : static_cast<float>(is);
+                        }
+                    }
+                    for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
+                        const int r = e / d.cols, c = e - r * d.cols;
+                        const uint32_t wa = sm[a.off + r * a.pitch + c];
+                        uint32_t out;
+                        if (d.word == W_F32) {
+                            const float x = __uint_as_float(wa);
+                            out = __float_as_uint(in.scalar_first ? bin_f(in.sub, fs, x) : bin_f(in.sub, x, fs));
+                        } else {
+                            const int32_t x = static_cast<int32_t>(wa);
+                            out = static_cast<uint32_t>(in.scalar_first ? bin_i(in.sub, is, x) : bin_i(in.sub, x, is));
+                        }
+                        sm[d.off + r * d.pitch + c] = out;
+                    }
+                    break;
+                }
+                case TP_EXP:
+                case TP_RSQRT: {
+                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                    for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
+                        const int r = e / d.cols, c = e - r * d.cols;
+                        const float x = __uint_as_float(sm[a.off + r * a.pitch + c]);
+                        const float y = in.op == TP_EXP ? expf(x) : __fdiv_rn(1.0f, sqrtf(x));
+                        sm[d.off + r * d.pitch + c] = __float_as_uint(y);
+                    }
+                    break;
+                }
+                case TP_ROWSUM:
+                case TP_ROWMAX:
+                case TP_ROWMEAN: {
+                    // Sequential column order per row (one thread per row).
+                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                    for (int r = threadIdx.x; r < d.rows; r += blockDim.x) {
+                        float acc = in.op == TP_ROWMAX ? -INFINITY : 0.f;
+                        for (int c = 0; c < a.cols; ++c) {
+                            const float x = __uint_as_float(sm[a.off + r * a.pitch + c]);
+                            acc = in.op == TP_ROWMAX ? fmaxf(acc, x) : __fadd_rn(acc, x);
+                        }
+                        if (in.op == TP_ROWMEAN) acc = __fdiv_rn(acc, static_cast<float>(in.k));
+                        sm[d.off + r * d.pitch] = __float_as_uint(acc);
+                    }
+                    break;
+                }
+                case TP_MATMUL: {
+                    // f32 accumulation in k order with separate multiply and add roundings.
+                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], bb = prog->slots[in.b];
+                    for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
+                        const int r = e / in.cols, c = e - r * in.cols;
+                        float acc = 0.f;
+                        for (int kk = 0; kk < in.k; ++kk)
+                            acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(sm[a.off + r * a.pitch + kk]),
+                                                           __uint_as_float(sm[bb.off + kk * bb.pitch + c])));
+                        sm[d.off + r * d.pitch + c] = __float_as_uint(acc);
+                    }
+                    break;
+                }
+                case TP_IOTA: {
+                    const TPSlot d = prog->slots[in.dst];
+                    for (int c = threadIdx.x; c < d.cols; c += blockDim.x) sm[d.off + c] = static_cast<uint32_t>(c);
+                    break;
+                }
+                case TP_TSORT32: {
+                    // Stable descending sort of n (<= rows*cols) scores with their indices:
+                    // rank_i = #{j : s_j > s_i or (s_j == s_i and j < i)}; dst = interleaved (score, index).
+                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], ix = prog->slots[in.b];
+                    const int n = in.k;
+                    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                        const float si = __uint_as_float(sm[a.off + (i / a.cols) * a.pitch + (i % a.cols)]);
+                        int rank = 0;
+                        for (int j = 0; j < n; ++j) {
+                            const float sj = __uint_as_float(sm[a.off + (j / a.cols) * a.pitch + (j % a.cols)]);
+                            rank += (sj > si) || (sj == si && j < i);
+                        }
+                        const uint32_t idx = sm[ix.off + (i / ix.cols) * ix.pitch + (i % ix.cols)];
+                        const int p0 = 2 * rank, p1 = 2 * rank + 1;
+                        if (p1 < d.rows * d.cols) {
+                            sm[d.off + (p0 / d.cols) * d.pitch + (p0 % d.cols)] = __float_as_uint(si);
+                            sm[d.off + (p1 / d.cols) * d.pitch + (p1 % d.cols)] = __float_as_uint(static_cast<float>(idx));
+                        }
+                    }
+                    break;
+                }
+                case TP_EXTRACT: {
+                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                    for (int i = threadIdx.x; i < in.k; i += blockDim.x) {
+                        const int p = 2 * i + 1;
+                        const float f = __uint_as_float(sm[a.off + (p / a.cols) * a.pitch + (p % a.cols)]);
+                        if (i < d.rows * d.cols) sm[d.off + (i / d.cols) * d.pitch + (i % d.cols)] = static_cast<uint32_t>(static_cast<int32_t>(f));
+                    }
+                    break;
+                }
+                default:
+                    break;
+            }
+            __syncthreads();
+        }
+    }
+}
+
+}  // namespace
+
+int sm_count() {
+    static int n = [] {
+        int dev = 0, v = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
+    return n;
+}
+
+cudaError_t launch_rmsnorm_rows(const TaskBatch& b, int workers, cudaStream_t s) {
+    return launch_rows<RmsNormOp>(b, workers, s);
+}
+
+cudaError_t launch_softmax_rows(const TaskBatch& b, int workers, cudaStream_t s) {
+    return launch_rows<SoftmaxOp>(b, workers, s);
+}
+
+int tile_program_max_smem() { return 227 * 1024; }
+
+cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev, int smem_bytes, int workers,
+                                cudaStream_t s) {
+    if (smem_bytes > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(tile_program_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+        if (e != cudaSuccess) return e;
+    }
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tile_program_kernel, 256, smem_bytes);
+    int64_t blocks = std::min<int64_t>(b.ntasks, static_cast<int64_t>(std::max(per_sm, 1)) * sm_count());
+    if (workers > 0) blocks = std::min<int64_t>(blocks, workers);
+    blocks = std::max<int64_t>(blocks, 1);
+    tile_program_kernel<<<static_cast<unsigned>(blocks), 256, smem_bytes, s>>>(b, prog_dev);
+    return cudaGetLastError();
+}
+
+}  // namespace ptowsp::dev

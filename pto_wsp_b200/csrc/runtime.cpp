@@ -1,0 +1,867 @@
+// Run-time half of the cuda_sm100a target: the task loop.
+//
+// The generated CPU-sim `<module>_main` walks the workload tree and, per task,
+// builds a KernelTaskDesc, calls the kernel synchronously and feeds its cycle
+// charge to a makespan scheduler (src/python/pto_codegen.cpp:2245-2697).  Here
+// the same walk *enqueues* tasks instead of running them: each task becomes a
+// record of the device task table (view offsets, axis args, scalar args) and
+// is placed in the current dependency wave.  A wave closes when a task touches
+// a tile that an earlier task of the wave writes (or writes one it reads), so
+// everything inside a wave runs concurrently and waves run in program order --
+// the same results as the sequential CPU-sim.  The reference scheduler model
+// (Scheduler::issue, :1562-1606) runs alongside, so the returned makespan is
+// the CPU-sim's own u64.
+//
+// Workloads without data-dependent control flow (no cond / select / slots)
+// are walked once per distinct set of run-time sizes; later runs replay the
+// cached waves and task table straight from device memory.
+#include <cuda_runtime_api.h>
+
+#include <algorithm>
+#include <chrono>
+#include <functional>
+#include <cstring>
+#include <queue>
+#include <sstream>
+#include <unordered_set>
+
+#include "runtime.hpp"
+
+namespace ptowsp {
+
+uint64_t reference_kernel_cycles(const KernelDef& kd);
+
+namespace {
+
+thread_local std::string g_err;
+
+#define PW_CUDA(call)                                                                              \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess)                                                                     \
+            throw Error(PTOWSP_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));     \
+    } while (0)
+
+// The reference makespan model (Scheduler::issue, pto_codegen.cpp:1562-1606).
+struct Scheduler {
+    uint32_t n;
+    uint64_t window;
+    uint64_t issue_time = 0;
+    std::vector<uint64_t> avail;
+    std::priority_queue<uint64_t, std::vector<uint64_t>, std::greater<uint64_t>> in_flight;
+    Scheduler(uint32_t workers, uint64_t w) : n(workers ? workers : 1), window(w), avail(n, 0) {}
+    void advance_to(uint64_t t) {
+        if (t > issue_time) issue_time = t;
+        while (!in_flight.empty() && in_flight.top() <= issue_time) in_flight.pop();
+    }
+    uint64_t issue(uint64_t dur, uint32_t wid, uint64_t ready) {
+        if (wid >= n) wid = 0;
+        advance_to(ready);
+        if (window > 0)
+            while (in_flight.size() >= window) advance_to(in_flight.top());
+        const uint64_t start = avail[wid] > issue_time ? avail[wid] : issue_time;
+        const uint64_t end = start + dur;
+        avail[wid] = end;
+        in_flight.push(end);
+        return end;
+    }
+};
+
+struct Val {
+    Expr::Ty ty;
+    uint64_t v;
+};
+
+int64_t as_i64(uint64_t v) { return static_cast<int64_t>(v); }
+
+dev::ParamType ptype(DType d) {
+    switch (d) {
+        case DType::F32: return dev::PT_F32;
+        case DType::F16: return dev::PT_F16;
+        case DType::I32: return dev::PT_I32;
+        case DType::U32: return dev::PT_U32;
+        case DType::I64: return dev::PT_I64;
+        case DType::U64: return dev::PT_U64;
+        default: return dev::PT_OTHER;
+    }
+}
+
+struct Walker {
+    Program& P;
+    RuntimeContext* ctx;
+    std::vector<TensorBinding>& T;
+    LaunchProgram& L;
+    std::vector<std::pair<const std::string*, int64_t>> env;  // loop var -> value
+    Scheduler sched;
+    uint64_t rr = 0;
+    // current wave
+    std::unordered_set<uint64_t> wave_reads, wave_writes;
+    std::unordered_map<const Node*, size_t> wave_batch;  // task node -> batch index in current wave
+    std::vector<std::string>& log;
+    std::function<void()> flush;
+    std::vector<uint8_t> written_any;  // tensors written by a task so far
+    // full-overwrite tracking: elements stored per tensor and whether any two stores hit the same tile
+    std::vector<int64_t> write_elems;
+    std::vector<std::unordered_set<uint64_t>> write_keys;
+    std::vector<uint8_t> write_partial;
+    bool fully_written(size_t tid) const {
+        int64_t numel = 1;
+        for (auto d : P.plan.tensors[tid].shape) numel *= d;
+        return written_any[tid] && !write_partial[tid] && write_elems[tid] == numel;
+    }
+
+    Walker(Program& p, RuntimeContext* c, std::vector<TensorBinding>& t, LaunchProgram& l, std::vector<std::string>& lg)
+        : P(p), ctx(c), T(t), L(l),
+          sched(static_cast<uint32_t>(p.plan.schedule.num_targets > 0 ? p.plan.schedule.num_targets
+                                      : (p.plan.schedule.streams > 0 ? p.plan.schedule.streams : 1)),
+                static_cast<uint64_t>(p.plan.schedule.window_tasks)),
+          log(lg) {
+        written_any.assign(p.plan.tensors.size(), 0);
+        write_elems.assign(p.plan.tensors.size(), 0);
+        write_keys.resize(p.plan.tensors.size());
+        write_partial.assign(p.plan.tensors.size(), 0);
+        L.waves.emplace_back();
+    }
+
+    int64_t var(const std::string& name) const {
+        for (auto it = env.rbegin(); it != env.rend(); ++it)
+            if (*it->first == name) return it->second;
+        throw Error(PTOWSP_ERR_PLAN, "loop variable '" + name + "' is not in scope");
+    }
+    bool var_by_id(uint64_t id, int64_t& out) const {
+        for (auto it = env.rbegin(); it != env.rend(); ++it)
+            if (fnv1a_64(*it->first) == id) {
+                out = it->second;
+                return true;
+            }
+        return false;
+    }
+
+    std::unordered_set<std::string> seen;
+    void note(std::string q) {
+        if (seen.insert(q).second) log.push_back(std::move(q));
+    }
+    uint64_t symbol_u64(uint64_t id) {
+        uint64_t v = ctx->get_symbol_u64 ? ctx->get_symbol_u64(ctx->ctx, id) : 0;
+        note("s" + std::to_string(id) + "=" + std::to_string(v));
+        return v;
+    }
+    int64_t axis_size(const std::string& name) {
+        int64_t v = ctx->get_axis_size ? ctx->get_axis_size(ctx->ctx, name.c_str()) : 0;
+        note("a" + name + "=" + std::to_string(v));
+        return v;
+    }
+    uint64_t slot(uint32_t i) { return ctx->get_slot_u64 ? ctx->get_slot_u64(ctx->ctx, i) : 0; }
+
+    Val eval(const Expr& e, const std::vector<uint64_t>* task_args) {
+        switch (e.op) {
+            case Expr::Op::Lit: return {e.ty, e.v};
+            case Expr::Op::Axis: {
+                int64_t v;
+                if (!var_by_id(e.v, v)) throw Error(PTOWSP_ERR_PLAN, "emit_scalar_expr_cpp: axis_var not in scope");
+                return {Expr::Ty::I64, static_cast<uint64_t>(v)};
+            }
+            case Expr::Op::Sym:
+            case Expr::Op::Tag: return {Expr::Ty::U64, symbol_u64(e.v)};
+            case Expr::Op::Slot: {
+                uint64_t v = slot(static_cast<uint32_t>(e.v));
+                if (e.ty == Expr::Ty::Bool) return {Expr::Ty::Bool, v != 0 ? 1ull : 0ull};
+                return {e.ty, v};
+            }
+            case Expr::Op::TaskParam: {
+                if (!task_args) throw Error(PTOWSP_ERR_PLAN, "task_param() outside a task");
+                return {Expr::Ty::U64, e.v < task_args->size() ? (*task_args)[e.v] : 0ull};
+            }
+            case Expr::Op::Unary: {
+                Val a = eval(*e.a, task_args);
+                if (e.fn == "!") return {Expr::Ty::Bool, a.v == 0 ? 1ull : 0ull};
+                if (e.fn == "-") return {a.ty == Expr::Ty::U64 ? Expr::Ty::U64 : Expr::Ty::I64, ~a.v + 1};
+                return {a.ty == Expr::Ty::U64 ? Expr::Ty::U64 : Expr::Ty::I64, ~a.v};
+            }
+            case Expr::Op::Ternary: {
+                Val c = eval(*e.c, task_args);
+                return c.v ? eval(*e.a, task_args) : eval(*e.b, task_args);
+            }
+            case Expr::Op::Cast: {
+                Val a = eval(*e.a, task_args);
+                if (e.ty == Expr::Ty::Bool) return {Expr::Ty::Bool, a.v != 0 ? 1ull : 0ull};
+                return {e.ty, a.v};
+            }
+            case Expr::Op::Binary: {
+                Val a = eval(*e.a, task_args);
+                Val b = eval(*e.b, task_args);
+                const std::string& f = e.fn;
+                if (f == "&&") return {Expr::Ty::Bool, (a.v && b.v) ? 1ull : 0ull};
+                if (f == "||") return {Expr::Ty::Bool, (a.v || b.v) ? 1ull : 0ull};
+                const bool u = a.ty == Expr::Ty::U64 || b.ty == Expr::Ty::U64;  // usual arithmetic conversions
+                const Expr::Ty rt = u ? Expr::Ty::U64 : Expr::Ty::I64;
+                auto cmp = [&](auto op) -> Val {
+                    bool r = u ? op(a.v, b.v) : op(as_i64(a.v), as_i64(b.v));
+                    return {Expr::Ty::Bool, r ? 1ull : 0ull};
+                };
+                if (f == "<") return cmp([](auto x, auto y) { return x < y; });
+                if (f == "<=") return cmp([](auto x, auto y) { return x <= y; });
+                if (f == ">") return cmp([](auto x, auto y) { return x > y; });
+                if (f == ">=") return cmp([](auto x, auto y) { return x >= y; });
+                if (f == "==") return cmp([](auto x, auto y) { return x == y; });
+                if (f == "!=") return cmp([](auto x, auto y) { return x != y; });
+                uint64_t r = 0;
+                if (f == "+") r = a.v + b.v;
+                else if (f == "-") r = a.v - b.v;
+                else if (f == "*") r = a.v * b.v;
+                else if (f == "/") {
+                    if (b.v == 0) throw Error(PTOWSP_ERR_ARG, "scalar expression divides by zero");
+                    r = u ? a.v / b.v : static_cast<uint64_t>(as_i64(a.v) / as_i64(b.v));
+                } else if (f == "%") {
+                    if (b.v == 0) throw Error(PTOWSP_ERR_ARG, "scalar expression divides by zero");
+                    r = u ? a.v % b.v : static_cast<uint64_t>(as_i64(a.v) % as_i64(b.v));
+                } else if (f == "&") r = a.v & b.v;
+                else if (f == "|") r = a.v | b.v;
+                else if (f == "^") r = a.v ^ b.v;
+                else if (f == "<<") r = a.v << (b.v & 63);
+                else if (f == ">>") r = u ? (a.v >> (b.v & 63)) : static_cast<uint64_t>(as_i64(a.v) >> (b.v & 63));
+                else throw Error(PTOWSP_ERR_PLAN, "unknown scalar operator " + f);
+                return {rt, r};
+            }
+        }
+        return {Expr::Ty::U64, 0};
+    }
+
+    uint64_t arg_value(const ArgSpec& a) {
+        switch (a.kind) {
+            case ArgSpec::Kind::Var: return static_cast<uint64_t>(var(a.var));
+            case ArgSpec::Kind::Sym: return symbol_u64(a.v);
+            default: return a.v;
+        }
+    }
+
+    // view offset (elements) of a tensor arg at the current loop values
+    int64_t view_offset(const TensorArg& ta) {
+        const auto& st = T[ta.tensor].strides;
+        int64_t off = 0;
+        for (size_t d = 0; d < ta.index.size(); ++d) {
+            int64_t v = ta.index[d].is_var ? var(ta.index[d].var) : ta.index[d].c;
+            off += v * (d < st.size() ? st[d] : 0);
+        }
+        return off;
+    }
+
+    uint64_t view_key(const TensorArg& ta) {
+        int depth = std::max(P.tensor_key_depth[ta.tensor], 0);
+        uint64_t h = 0x9E3779B97F4A7C15ull ^ (static_cast<uint64_t>(ta.tensor) * 0xC2B2AE3D27D4EB4Full);
+        for (int d = 0; d < depth && d < static_cast<int>(ta.index.size()); ++d) {
+            int64_t v = ta.index[d].is_var ? var(ta.index[d].var) : ta.index[d].c;
+            h ^= static_cast<uint64_t>(v) + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+        }
+        return h;
+    }
+
+    void close_wave() {
+        if (L.waves.back().batches.empty()) return;
+        L.waves.emplace_back();
+        wave_reads.clear();
+        wave_writes.clear();
+        wave_batch.clear();
+    }
+
+    uint64_t node(const Node& n, uint64_t ready) {
+        switch (n.kind) {
+            case Node::Kind::SlotSet:
+                if (ctx->set_slot_u64) ctx->set_slot_u64(ctx->ctx, n.slot, n.slot_value);
+                return ready;
+            case Node::Kind::SlotLoad: {
+                const TensorArg& ta = n.slot_tensor;
+                const TensorBinding& tb = T[ta.tensor];
+                const int64_t base = view_offset(ta);
+                int64_t s3 = 0, s4 = 1;
+                if (ta.view_rank >= 2) {
+                    s3 = tb.strides[ta.base_rank - ta.view_rank];
+                    s4 = tb.strides[ta.base_rank - ta.view_rank + 1];
+                } else if (ta.view_rank == 1) {
+                    s4 = tb.strides[ta.base_rank - 1];
+                }
+                const int64_t off = base + n.row * s3 + n.col * s4;
+                if (off < 0 || off >= tb.span) throw Error(PTOWSP_ERR_ARG, "slot_load_u64 reads outside its tensor");
+                const DType dt = P.plan.tensors[ta.tensor].dtype;
+                const int eb = dtype_bytes(dt);
+                alignas(8) unsigned char buf[8] = {0};
+                if (tb.on_device || written_any[ta.tensor]) {
+                    flush();  // device data: finish the enqueued waves, then read the element back
+                    PW_CUDA(cudaMemcpy(buf, tb.dev + off * eb, eb, cudaMemcpyDeviceToHost));
+                } else {
+                    std::memcpy(buf, static_cast<const char*>(tb.user_ptr) + off * eb, eb);
+                }
+                uint64_t v = 0;
+                switch (dt) {  // (uint64_t)((item*)ptr)[...] of the emitted code
+                    case DType::F32: { float f; std::memcpy(&f, buf, 4); v = static_cast<uint64_t>(static_cast<int64_t>(f)); break; }
+                    case DType::F64: { double f; std::memcpy(&f, buf, 8); v = static_cast<uint64_t>(static_cast<int64_t>(f)); break; }
+                    case DType::I32: { int32_t x; std::memcpy(&x, buf, 4); v = static_cast<uint64_t>(static_cast<int64_t>(x)); break; }
+                    case DType::U32: { uint32_t x; std::memcpy(&x, buf, 4); v = x; break; }
+                    case DType::I64: case DType::U64: std::memcpy(&v, buf, 8); break;
+                    case DType::I16: { int16_t x; std::memcpy(&x, buf, 2); v = static_cast<uint64_t>(static_cast<int64_t>(x)); break; }
+                    case DType::U16: { uint16_t x; std::memcpy(&x, buf, 2); v = x; break; }
+                    case DType::I8: { int8_t x; std::memcpy(&x, buf, 1); v = static_cast<uint64_t>(static_cast<int64_t>(x)); break; }
+                    case DType::U8: case DType::Bool: v = buf[0]; break;
+                    default: throw Error(PTOWSP_ERR_UNSUPPORTED, "slot_load_u64 from this dtype");
+                }
+                if (ctx->set_slot_u64) ctx->set_slot_u64(ctx->ctx, n.slot, v);
+                return ready;
+            }
+            case Node::Kind::ParallelFor:
+            case Node::Kind::ForEach: {
+                int64_t ub = 0;
+                if (n.axis.kind == Axis::Kind::Dense) {
+                    ub = n.axis.size;
+                } else if (n.axis.kind == Axis::Kind::DenseDyn) {
+                    ub = axis_size(n.var);
+                } else {
+                    int64_t outer = static_cast<int64_t>(symbol_u64(n.axis.outer_sym));
+                    const int32_t* lens = ctx->get_symbol_ptr
+                                              ? static_cast<const int32_t*>(ctx->get_symbol_ptr(ctx->ctx, n.axis.lengths_sym))
+                                              : nullptr;
+                    if (lens)
+                        for (int64_t i = 0; i < outer; ++i) ub += lens[i];
+                    note("r" + std::to_string(n.axis.lengths_sym) + "=" + std::to_string(ub));
+                }
+                uint64_t done = ready, cur = ready;
+                env.push_back({&n.var, 0});
+                for (int64_t i = 0; i < ub; ++i) {
+                    env.back().second = i;
+                    if (n.kind == Node::Kind::ParallelFor) done = std::max(done, node(*n.body, ready));
+                    else cur = node(*n.body, cur);
+                }
+                env.pop_back();
+                return n.kind == Node::Kind::ParallelFor ? done : cur;
+            }
+            case Node::Kind::Select: {
+                int64_t outer = static_cast<int64_t>(symbol_u64(n.outer_sym));
+                const int32_t* indptr = ctx->get_symbol_ptr ? static_cast<const int32_t*>(ctx->get_symbol_ptr(ctx->ctx, n.indptr_sym)) : nullptr;
+                const int32_t* indices = ctx->get_symbol_ptr ? static_cast<const int32_t*>(ctx->get_symbol_ptr(ctx->ctx, n.indices_sym)) : nullptr;
+                int64_t nnz = indptr ? indptr[outer] : 0;
+                uint64_t done = ready;
+                env.push_back({&n.var, 0});
+                for (int64_t p = 0; p < nnz; ++p) {
+                    env.back().second = indices ? indices[p] : 0;
+                    done = std::max(done, node(*n.body, ready));
+                }
+                env.pop_back();
+                return done;
+            }
+            case Node::Kind::Cond: {
+                Val c = eval(*n.pred, nullptr);
+                return node(c.v ? *n.then_n : *n.else_n, ready);
+            }
+            case Node::Kind::Combine: {
+                uint64_t done = ready;
+                for (auto& ch : n.children) done = std::max(done, node(*ch, ready));
+                return done;
+            }
+            case Node::Kind::Sequential: {
+                uint64_t cur = ready;
+                for (auto& ch : n.children) cur = node(*ch, cur);
+                return cur;
+            }
+            case Node::Kind::Task: return task(n, ready);
+        }
+        return ready;
+    }
+
+    uint64_t task(const Node& n, uint64_t ready) {
+        const KernelDef& kd = P.plan.kernels[n.kernel_index];
+        const KernelImpl& ki = P.impls[n.kernel_index];
+        // u64 args: axis args, (valid_row, valid_col) per tensor param, scalar args (pto_codegen.cpp:2526-2545)
+        std::vector<uint64_t> args;
+        args.reserve(n.axis_args.size() + 2 * kd.num_tensor_params + n.scalar_args.size());
+        for (const auto& a : n.axis_args) args.push_back(arg_value(a));
+        for (const auto& p : kd.params)
+            if (p.tensor_index >= 0) {
+                args.push_back(static_cast<uint64_t>(p.v.rows));
+                args.push_back(static_cast<uint64_t>(p.v.cols));
+            }
+        std::vector<uint64_t> scal;
+        for (const auto& a : n.scalar_args) scal.push_back(arg_value(a));
+        args.insert(args.end(), scal.begin(), scal.end());
+
+        // dependency wave
+        uint64_t rkeys[dev::kMaxParams], wkeys[dev::kMaxParams];
+        int nr = 0, nw = 0;
+        bool conflict = false;
+        for (int ti = 0; ti < kd.num_tensor_params; ++ti) {
+            const TensorArg& ta = n.tensor_args[n.param_to_arg[ti]];
+            uint64_t key = view_key(ta);
+            if (ki.param_write[ti]) {
+                wkeys[nw++] = key;
+                if (wave_reads.count(key) || wave_writes.count(key)) conflict = true;
+            }
+            if (ki.param_read[ti]) {
+                rkeys[nr++] = key;
+                if (wave_writes.count(key)) conflict = true;
+            }
+        }
+        if (conflict) close_wave();
+        for (int i = 0; i < nr; ++i) wave_reads.insert(rkeys[i]);
+        for (int i = 0; i < nw; ++i) wave_writes.insert(wkeys[i]);
+
+        Wave& w = L.waves.back();
+        auto it = wave_batch.find(&n);
+        if (it == wave_batch.end()) {
+            Batch b;
+            b.kernel = n.kernel_index;
+            b.node = &n;
+            b.stride = kd.num_tensor_params + static_cast<int>(n.axis_args.size()) + kd.num_scalar_params;
+            w.batches.push_back(std::move(b));
+            it = wave_batch.emplace(&n, w.batches.size() - 1).first;
+        }
+        Batch& b = w.batches[it->second];
+        for (int ti = 0; ti < kd.num_tensor_params; ++ti) {
+            const TensorArg& ta = n.tensor_args[n.param_to_arg[ti]];
+            const int64_t off = view_offset(ta);
+            b.rec.push_back(off);
+            if ((off & 3) != 0) b.aligned_rows = false;
+            if (ki.param_write[ti]) {
+                written_any[ta.tensor] = 1;
+                // a store covers its whole view block when the tile has exactly the block's size
+                const auto& shape = P.plan.tensors[ta.tensor].shape;
+                int64_t block = 1;
+                for (size_t d = ta.index.size(); d < shape.size(); ++d) block *= shape[d];
+                const KernelParam* kp = nullptr;
+                for (const auto& p : kd.params)
+                    if (p.tensor_index == ti) kp = &p;
+                const bool exact = kp && static_cast<int64_t>(kp->v.rows) * kp->v.cols == block &&
+                                   static_cast<int>(ta.index.size()) == P.tensor_key_depth[ta.tensor];
+                if (!exact || !write_keys[ta.tensor].insert(view_key(ta)).second) write_partial[ta.tensor] = 1;
+                else write_elems[ta.tensor] += block;
+            }
+        }
+        for (size_t i = 0; i < n.axis_args.size(); ++i) b.rec.push_back(static_cast<int64_t>(args[i]));
+        for (uint64_t s : scal) b.rec.push_back(static_cast<int64_t>(s));
+        b.ntasks++;
+        L.tasks++;
+
+        // worker choice + makespan (pto_codegen.cpp:2679-2692)
+        const Schedule& sc = P.plan.schedule;
+        uint32_t wid = 0;
+        if (!sc.dispatch_policy.empty()) {
+            if (sc.dispatch_policy == "round_robin" || sc.dispatch_policy == "work_steal") {
+                wid = static_cast<uint32_t>(rr++ % sched.n);
+            } else {
+                Val key = eval(*sc.dispatch_key, &args);
+                wid = static_cast<uint32_t>(key.v % sched.n);
+            }
+        }
+        return sched.issue(ki.cycles, wid, ready);
+    }
+};
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+
+void set_error(const std::string& msg) { g_err = msg; }
+const char* last_error() { return g_err.c_str(); }
+
+Program::~Program() {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    if (cached && cached->rec_dev) cudaFree(cached->rec_dev);
+    for (auto& ki : impls)
+        if (ki.tp_dev) cudaFree(ki.tp_dev);
+    for (char* b : dev_bufs)
+        if (b) cudaFree(b);
+    if (scratch) cudaFree(scratch);
+    if (err_dev) cudaFree(err_dev);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (own_stream) cudaStreamDestroy(own_stream);
+    if (prev >= 0) cudaSetDevice(prev);
+}
+
+namespace {
+
+void ensure_device_state(Program& p) {
+    if (!p.own_stream) {
+        PW_CUDA(cudaStreamCreateWithFlags(&p.own_stream, cudaStreamNonBlocking));
+        if (!p.stream) p.stream = p.own_stream;
+        PW_CUDA(cudaEventCreate(&p.ev0));
+        PW_CUDA(cudaEventCreate(&p.ev1));
+        PW_CUDA(cudaMalloc(&p.err_dev, sizeof(int)));
+        PW_CUDA(cudaMemset(p.err_dev, 0, sizeof(int)));
+    }
+    for (auto& ki : p.impls) {
+        if (ki.tp_ok && !ki.tp_dev) {
+            PW_CUDA(cudaMalloc(&ki.tp_dev, sizeof(dev::TileProgram)));
+            PW_CUDA(cudaMemcpy(ki.tp_dev, &ki.tp, sizeof(dev::TileProgram), cudaMemcpyHostToDevice));
+        }
+    }
+}
+
+void* ensure_scratch(Program& p, size_t bytes) {
+    if (bytes == 0) return nullptr;
+    if (p.scratch_cap < bytes) {
+        if (p.scratch) PW_CUDA(cudaFree(p.scratch));
+        p.scratch = nullptr;
+        p.scratch_cap = 0;
+        PW_CUDA(cudaMalloc(&p.scratch, bytes));
+        p.scratch_cap = bytes;
+    }
+    return p.scratch;
+}
+
+// Launch one batch.  `node` is the task node whose tensor bindings the batch uses.
+void launch_batch(Program& P, const Batch& B, const Node& node, std::vector<TensorBinding>& T, const int64_t* rec_dev,
+                  uint64_t& launches) {
+    const KernelDef& kd = P.plan.kernels[B.kernel];
+    KernelImpl& ki = P.impls[B.kernel];
+    dev::TaskBatch tb{};
+    tb.rec = rec_dev + B.dev_off;
+    tb.ntasks = B.ntasks;
+    tb.stride = B.stride;
+    tb.nparams = kd.num_tensor_params;
+    tb.naxis = static_cast<int>(node.axis_args.size());
+    tb.nscalar = kd.num_scalar_params;
+    tb.err = P.err_dev;
+    if (kd.num_tensor_params > dev::kMaxParams) throw Error(PTOWSP_ERR_LIMIT, "kernel has more than 8 tile params");
+    bool rows_ok = B.aligned_rows;
+    for (const auto& kp : kd.params) {
+        if (kp.tensor_index < 0) continue;
+        const TensorArg& ta = node.tensor_args[node.param_to_arg[kp.tensor_index]];
+        const TensorBinding& b = T[ta.tensor];
+        dev::ParamDesc& pd = tb.p[kp.tensor_index];
+        pd.base = b.dev;
+        if (ta.view_rank >= 2) {
+            pd.s3 = b.strides[ta.base_rank - ta.view_rank];
+            pd.s4 = b.strides[ta.base_rank - ta.view_rank + 1];
+        } else if (ta.view_rank == 1) {
+            pd.s3 = 0;
+            pd.s4 = b.strides[ta.base_rank - 1];
+        } else {
+            pd.s3 = 0;
+            pd.s4 = 1;
+        }
+        pd.numel_span = b.span;
+        pd.rows = kp.v.rows;
+        pd.cols = kp.v.cols;
+        pd.type = ptype(kp.v.dtype);
+        pd.elem_bytes = dtype_bytes(kp.v.dtype);
+        if (pd.s4 != 1 || (pd.s3 & 3) != 0 || (reinterpret_cast<uintptr_t>(pd.base) & 15) != 0) rows_ok = false;
+    }
+    const int workers = P.plan.schedule.window_tasks > 0 ? static_cast<int>(std::min<int64_t>(P.plan.schedule.window_tasks, 1 << 30)) : 0;
+    cudaError_t e = cudaSuccess;
+    ImplKind kind = ki.kind;
+    if ((kind == ImplKind::RmsNorm || kind == ImplKind::Softmax)) {
+        const int c = kd.params[0].v.cols;
+        if (!rows_ok || !(c == 128 || c == 256 || c == 512 || c == 1024)) kind = ImplKind::TileProgram;
+    }
+    if (kind == ImplKind::Matmul || kind == ImplKind::MatmulAcc) kind = ImplKind::TileProgram;  // tcgen05 path below
+    switch (kind) {
+        case ImplKind::RmsNorm: e = dev::launch_rmsnorm_rows(tb, workers, P.stream); break;
+        case ImplKind::Softmax: e = dev::launch_softmax_rows(tb, workers, P.stream); break;
+        case ImplKind::TileProgram:
+            if (!ki.tp_ok) throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
+            e = dev::launch_tile_program(tb, ki.tp_dev, ki.tp_smem, workers, P.stream);
+            break;
+        case ImplKind::PagedDecode: {
+            size_t sb = dev::paged_decode_scratch_bytes(tb, 16);
+            void* s = ensure_scratch(P, sb);
+            e = dev::launch_paged_decode(tb, 16, 0, workers, s, sb, P.stream);
+            break;
+        }
+        case ImplKind::IndexerScore: e = dev::launch_indexer_score(tb, workers, P.stream); break;
+        case ImplKind::TopK: {
+            size_t sb = dev::topk_select_scratch_bytes(tb);
+            void* s = ensure_scratch(P, sb);
+            e = dev::launch_topk_select(tb, workers, s, sb, P.stream);
+            break;
+        }
+        default: throw Error(PTOWSP_ERR_UNSUPPORTED, "no launcher");
+    }
+    if (e != cudaSuccess) throw Error(PTOWSP_ERR_CUDA, "launch of " + kd.name + ": " + cudaGetErrorString(e));
+    launches++;
+}
+
+}  // namespace
+
+uint64_t run_program(Program& P, RuntimeContext* ctx) {
+    auto t_start = std::chrono::steady_clock::now();
+    if (!ctx) throw Error(PTOWSP_ERR_ARG, "RuntimeContext is null");
+    PW_CUDA(cudaSetDevice(P.device));
+    ensure_device_state(P);
+    P.timing = ptowsp_timing{};
+    const Plan& plan = P.plan;
+
+    // ---- bind tensors ----
+    std::vector<TensorBinding> T(plan.tensors.size());
+    bool all_device = true;
+    for (size_t tid = 0; tid < plan.tensors.size(); ++tid) {
+        TensorBinding& b = T[tid];
+        const TensorInfo& ti = plan.tensors[tid];
+        b.user_ptr = ctx->get_tensor_ptr ? ctx->get_tensor_ptr(ctx->ctx, static_cast<uint32_t>(tid)) : nullptr;
+        b.strides.resize(ti.shape.size());
+        int64_t span = 1;
+        for (size_t d = 0; d < ti.shape.size(); ++d) {
+            b.strides[d] = ctx->get_tensor_stride ? static_cast<int64_t>(ctx->get_tensor_stride(ctx->ctx, static_cast<uint32_t>(tid), static_cast<uint32_t>(d))) : 0;
+            if (b.strides[d] < 0) throw Error(PTOWSP_ERR_ARG, "negative tensor strides are not supported");
+            if (ti.shape[d] <= 0) span = 0;
+            else if (span > 0) span += (ti.shape[d] - 1) * b.strides[d];
+        }
+        b.span = span;
+        b.bytes = static_cast<size_t>(span) * dtype_bytes(ti.dtype);
+        if (!b.user_ptr && b.bytes) throw Error(PTOWSP_ERR_ARG, "tensor " + std::to_string(tid) + " has no data pointer");
+        cudaPointerAttributes attr{};
+        if (b.user_ptr && cudaPointerGetAttributes(&attr, b.user_ptr) == cudaSuccess &&
+            (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged)) {
+            b.on_device = true;
+            b.dev = static_cast<char*>(b.user_ptr);
+        }
+        cudaGetLastError();
+        if (!b.on_device && b.bytes) all_device = false;
+    }
+    // read / written sets per tensor from the kernels' param sets
+    std::function<void(const Node&)> mark = [&](const Node& n) {
+        switch (n.kind) {
+            case Node::Kind::ParallelFor: case Node::Kind::ForEach: case Node::Kind::Select: mark(*n.body); break;
+            case Node::Kind::Combine: case Node::Kind::Sequential: for (auto& c : n.children) mark(*c); break;
+            case Node::Kind::Cond: mark(*n.then_n); mark(*n.else_n); break;
+            case Node::Kind::Task: {
+                const KernelImpl& ki = P.impls[n.kernel_index];
+                for (size_t ti = 0; ti < n.param_to_arg.size(); ++ti) {
+                    auto& b = T[n.tensor_args[n.param_to_arg[ti]].tensor];
+                    if (ki.param_read[ti]) b.read = true;
+                    if (ki.param_write[ti]) b.written = true;
+                }
+                break;
+            }
+            case Node::Kind::SlotLoad: T[n.slot_tensor.tensor].read = true; break;
+            default: break;
+        }
+    };
+    mark(*plan.body);
+    // host staging buffers
+    if (P.dev_bufs.size() < T.size()) {
+        P.dev_bufs.resize(T.size(), nullptr);
+        P.dev_caps.resize(T.size(), 0);
+    }
+    for (size_t tid = 0; tid < T.size(); ++tid) {
+        TensorBinding& b = T[tid];
+        if (b.on_device || b.bytes == 0) continue;
+        if (P.dev_caps[tid] < b.bytes) {
+            if (P.dev_bufs[tid]) PW_CUDA(cudaFree(P.dev_bufs[tid]));
+            P.dev_bufs[tid] = nullptr;
+            P.dev_caps[tid] = 0;
+            PW_CUDA(cudaMalloc(&P.dev_bufs[tid], b.bytes));
+            P.dev_caps[tid] = b.bytes;
+        }
+        b.dev = P.dev_bufs[tid];
+    }
+    const bool async_run = !P.opt_sync && all_device;
+
+    // ---- replay check for static workloads ----
+    std::string stride_sig = "#";
+    for (auto& b : T)
+        for (auto s : b.strides) stride_sig += std::to_string(s) + ",";
+    bool replay = false;
+    if (P.cacheable && P.opt_cache && P.cached) {
+        replay = !P.cached->key.empty() && P.cached->key.back() == stride_sig;
+        for (size_t i = 0; replay && i + 1 < P.cached->key.size(); ++i) {
+            const std::string& q = P.cached->key[i];
+            const char kind = q[0];
+            size_t eq = q.find('=');
+            std::string name = q.substr(1, eq - 1);
+            uint64_t want = std::stoull(q.substr(eq + 1));
+            uint64_t got = 0;
+            if (kind == 's') got = ctx->get_symbol_u64 ? ctx->get_symbol_u64(ctx->ctx, std::stoull(name)) : 0;
+            else if (kind == 'a') got = static_cast<uint64_t>(ctx->get_axis_size ? ctx->get_axis_size(ctx->ctx, name.c_str()) : 0);
+            else replay = false;  // ragged lengths: walk again
+            if (got != want) replay = false;
+        }
+    }
+
+    std::unique_ptr<LaunchProgram> fresh;
+    LaunchProgram* L = nullptr;
+    std::vector<std::string> log;
+    uint64_t launches = 0;
+    size_t launched_waves = 0;
+    std::unique_ptr<Walker> W;
+
+    auto upload_and_launch = [&](size_t upto) {
+        size_t need = L->rec_elems;
+        for (size_t wi = launched_waves; wi < upto; ++wi)
+            for (auto& b : L->waves[wi].batches) need += b.rec.size();
+        if (need > L->rec_cap) {
+            int64_t* nb = nullptr;
+            size_t cap = std::max<size_t>(need, L->rec_cap * 2);
+            PW_CUDA(cudaMalloc(&nb, cap * sizeof(int64_t)));
+            if (L->rec_dev) {
+                PW_CUDA(cudaMemcpyAsync(nb, L->rec_dev, L->rec_elems * sizeof(int64_t), cudaMemcpyDeviceToDevice, P.stream));
+                PW_CUDA(cudaStreamSynchronize(P.stream));
+                PW_CUDA(cudaFree(L->rec_dev));
+            }
+            L->rec_dev = nb;
+            L->rec_cap = cap;
+        }
+        for (size_t wi = launched_waves; wi < upto; ++wi)
+            for (auto& b : L->waves[wi].batches) {
+                b.dev_off = L->rec_elems;
+                if (!b.rec.empty())
+                    PW_CUDA(cudaMemcpyAsync(L->rec_dev + b.dev_off, b.rec.data(), b.rec.size() * sizeof(int64_t),
+                                            cudaMemcpyHostToDevice, P.stream));
+                L->rec_elems += b.rec.size();
+            }
+        for (size_t wi = launched_waves; wi < upto; ++wi)
+            for (auto& b : L->waves[wi].batches) launch_batch(P, b, *b.node, T, L->rec_dev, launches);
+        launched_waves = upto;
+    };
+
+    // ---- static workloads: walk before staging (the walk knows which outputs are fully overwritten) ----
+    if (replay) {
+        L = P.cached.get();
+    } else if (P.cacheable) {
+        fresh = std::make_unique<LaunchProgram>();
+        L = fresh.get();
+        W = std::make_unique<Walker>(P, ctx, T, *L, log);
+        W->flush = [] { throw Error(PTOWSP_ERR_PLAN, "internal: flush in a static workload"); };
+        L->makespan = W->node(*plan.body, 0);
+        W->close_wave();
+        L->key = log;
+        L->key.push_back(stride_sig);
+        L->full_write.assign(T.size(), 0);
+        for (size_t tid = 0; tid < T.size(); ++tid)
+            L->full_write[tid] = W->fully_written(tid) ? 1 : 0;
+    }
+
+    // ---- stage host tensors into HBM ----
+    for (size_t tid = 0; tid < T.size(); ++tid) {
+        TensorBinding& b = T[tid];
+        if (b.on_device || b.bytes == 0) continue;
+        // Host tensors a task touches are staged in -- outputs too, unless the
+        // task loop provably overwrites every element without reading it, so
+        // that elements no task writes come back unchanged.
+        const bool skip = L && !b.read && !L->full_write.empty() && L->full_write[tid];
+        if ((b.read || b.written) && !skip) {
+            PW_CUDA(cudaMemcpyAsync(b.dev, b.user_ptr, b.bytes, cudaMemcpyHostToDevice, P.stream));
+            P.timing.h2d_bytes += b.bytes;
+        }
+    }
+
+    PW_CUDA(cudaEventRecord(P.ev0, P.stream));
+    if (replay) {
+        for (size_t wi = 0; wi < L->waves.size(); ++wi)
+            for (auto& b : L->waves[wi].batches) launch_batch(P, b, *b.node, T, L->rec_dev, launches);
+    } else if (P.cacheable) {
+        upload_and_launch(L->waves.size());
+    } else {
+        // data-dependent control flow: walk while launching (slot loads of device data flush)
+        fresh = std::make_unique<LaunchProgram>();
+        L = fresh.get();
+        W = std::make_unique<Walker>(P, ctx, T, *L, log);
+        W->flush = [&]() {
+            W->close_wave();
+            upload_and_launch(L->waves.size());
+            PW_CUDA(cudaStreamSynchronize(P.stream));
+        };
+        L->makespan = W->node(*plan.body, 0);
+        W->close_wave();
+        upload_and_launch(L->waves.size());
+    }
+    PW_CUDA(cudaEventRecord(P.ev1, P.stream));
+
+    // ---- bring written host tensors back ----
+    for (size_t tid = 0; tid < T.size(); ++tid) {
+        TensorBinding& b = T[tid];
+        if (b.on_device || !b.written || b.bytes == 0) continue;
+        PW_CUDA(cudaMemcpyAsync(b.user_ptr, b.dev, b.bytes, cudaMemcpyDeviceToHost, P.stream));
+        P.timing.d2h_bytes += b.bytes;
+    }
+    P.timing.launches = launches;
+    P.timing.tasks = L->tasks;
+    for (auto& w : L->waves) P.timing.waves += w.batches.empty() ? 0 : 1;
+    const uint64_t makespan = L->makespan;
+    int err_host = 0;
+    if (!async_run) {
+        // the status word accumulates over asynchronous runs; read, then clear it
+        PW_CUDA(cudaMemcpyAsync(&err_host, P.err_dev, sizeof(int), cudaMemcpyDeviceToHost, P.stream));
+        PW_CUDA(cudaMemsetAsync(P.err_dev, 0, sizeof(int), P.stream));
+        PW_CUDA(cudaStreamSynchronize(P.stream));
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, P.ev0, P.ev1);
+        P.timing.gpu_ms = ms;
+    } else {
+        P.timing.gpu_ms = -1.0;  // asynchronous run: not known yet
+    }
+    if (fresh) {
+        if (P.cacheable && P.opt_cache) {
+            if (async_run) PW_CUDA(cudaStreamSynchronize(P.stream));  // host records must outlive their copies
+            for (auto& w : fresh->waves)
+                for (auto& b : w.batches) std::vector<int64_t>().swap(b.rec);  // records live on the device now
+            if (P.cached && P.cached->rec_dev) {
+                PW_CUDA(cudaStreamSynchronize(P.stream));
+                cudaFree(P.cached->rec_dev);
+            }
+            P.cached = std::move(fresh);
+        } else {
+            PW_CUDA(cudaStreamSynchronize(P.stream));
+            if (fresh->rec_dev) cudaFree(fresh->rec_dev);
+            fresh->rec_dev = nullptr;
+        }
+    }
+    P.timing.total_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_start).count();
+    if (err_host) {
+        throw Error(PTOWSP_ERR_DEVICE, std::string("device status ") + std::to_string(err_host) +
+                                           ((err_host & dev::kErrBounds) ? " (index out of bounds)" : "") +
+                                           ((err_host & dev::kErrTimeout) ? " (wait timed out)" : "") +
+                                           ((err_host & dev::kErrShape) ? " (size beyond kernel limit)" : ""));
+    }
+    return makespan;
+}
+
+uint64_t run_single_task(Program& P, const std::string& kernel, const KernelTaskDesc* task) {
+    int ki_idx = P.plan.kernel_index(kernel);
+    if (ki_idx < 0) throw Error(PTOWSP_ERR_ARG, "unknown kernel " + kernel);
+    if (!task) throw Error(PTOWSP_ERR_ARG, "KernelTaskDesc is null");
+    const KernelDef& kd = P.plan.kernels[ki_idx];
+    if (static_cast<int>(task->num_tensors) != kd.num_tensor_params)
+        throw Error(PTOWSP_ERR_ARG, "tensor count does not match kernel " + kernel);
+    PW_CUDA(cudaSetDevice(P.device));
+    ensure_device_state(P);
+    // A one-task plan node: each param views its own base pointer (offset 0).
+    Node n;
+    n.kind = Node::Kind::Task;
+    n.kernel = kernel;
+    n.kernel_index = ki_idx;
+    const int naxis = static_cast<int>(task->num_axis_args) - 2 * kd.num_tensor_params;
+    for (int i = 0; i < std::max(naxis, 0); ++i) n.axis_args.push_back(ArgSpec{ArgSpec::Kind::U64, "", task->args[i]});
+    std::vector<TensorBinding> T(kd.num_tensor_params);
+    Batch b;
+    b.kernel = ki_idx;
+    b.ntasks = 1;
+    b.stride = kd.num_tensor_params + std::max(naxis, 0) + kd.num_scalar_params;
+    for (int ti = 0; ti < kd.num_tensor_params; ++ti) {
+        TensorArg ta;
+        ta.tensor = static_cast<uint32_t>(ti);
+        ta.base_rank = 2;
+        ta.view_rank = 2;
+        n.tensor_args.push_back(ta);
+        n.param_to_arg.push_back(ti);
+        T[ti].dev = static_cast<char*>(task->tensor_ptrs[ti]);
+        T[ti].strides = {static_cast<int64_t>(task->tensor_strides[2 * ti]), static_cast<int64_t>(task->tensor_strides[2 * ti + 1])};
+        T[ti].span = INT64_MAX / 16;
+        b.rec.push_back(0);
+    }
+    for (int i = 0; i < std::max(naxis, 0); ++i) b.rec.push_back(static_cast<int64_t>(task->args[i]));
+    for (int i = 0; i < kd.num_scalar_params; ++i) b.rec.push_back(static_cast<int64_t>(task->args[task->num_axis_args + i]));
+    int64_t* rec_dev = nullptr;
+    PW_CUDA(cudaMalloc(&rec_dev, b.rec.size() * sizeof(int64_t)));
+    PW_CUDA(cudaMemcpyAsync(rec_dev, b.rec.data(), b.rec.size() * sizeof(int64_t), cudaMemcpyHostToDevice, P.stream));
+    uint64_t launches = 0;
+    launch_batch(P, b, n, T, rec_dev, launches);
+    int err_host = 0;
+    PW_CUDA(cudaMemcpyAsync(&err_host, P.err_dev, sizeof(int), cudaMemcpyDeviceToHost, P.stream));
+    PW_CUDA(cudaMemsetAsync(P.err_dev, 0, sizeof(int), P.stream));
+    PW_CUDA(cudaStreamSynchronize(P.stream));
+    cudaFree(rec_dev);
+    if (err_host) throw Error(PTOWSP_ERR_DEVICE, "device status " + std::to_string(err_host));
+    return P.impls[ki_idx].cycles;
+}
+
+}  // namespace ptowsp

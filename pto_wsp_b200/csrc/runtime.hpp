@@ -1,0 +1,110 @@
+// Host runtime of the cuda_sm100a target.
+#pragma once
+
+#include <cuda_runtime_api.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <unordered_set>
+#include <vector>
+
+#include "../../include/ptowsp_cuda.h"
+#include "device.hpp"
+#include "plan.hpp"
+
+namespace ptowsp {
+
+enum class ImplKind : uint8_t { RmsNorm, Softmax, TileProgram, Matmul, MatmulAcc, PagedDecode, IndexerScore, TopK };
+
+const char* impl_name(ImplKind k);
+
+// How one kernel definition runs on the GPU.
+struct KernelImpl {
+    ImplKind kind = ImplKind::TileProgram;
+    uint64_t cycles = 0;                 // reference cycle-model charge per task
+    std::vector<uint8_t> param_read;     // per tensor param
+    std::vector<uint8_t> param_write;    // per tensor param
+    dev::TileProgram tp{};               // generic tile program (also the fallback of RmsNorm/Softmax)
+    int tp_smem = 0;
+    bool tp_ok = false;                  // tile program fits the device
+    std::string tp_error;
+    dev::TileProgram* tp_dev = nullptr;  // device copy
+    int scalar_page_size = 16, scalar_kv_heads = 1;  // paged decode static params
+};
+
+// Per-tensor binding of one run.
+struct TensorBinding {
+    void* user_ptr = nullptr;       // pointer from RuntimeContext
+    bool on_device = false;         // user_ptr is device memory
+    char* dev = nullptr;            // device pointer used by kernels
+    std::vector<int64_t> strides;   // elements
+    int64_t span = 0;               // addressable elements from base
+    size_t bytes = 0;
+    bool read = false, written = false;
+};
+
+struct Batch {  // tasks of one kernel inside one wave
+    int kernel = -1;
+    const Node* node = nullptr;    // task node whose tensor bindings the batch uses
+    std::vector<int64_t> rec;      // host records
+    int64_t ntasks = 0;
+    int stride = 0;
+    size_t dev_off = 0;            // element offset in the device record buffer
+    bool aligned_rows = true;      // fast row kernels usable
+};
+
+struct Wave {
+    std::vector<Batch> batches;
+};
+
+struct LaunchProgram {  // result of one walk, reusable for static workloads
+    std::vector<Wave> waves;
+    uint64_t makespan = 0;
+    uint64_t tasks = 0;
+    size_t rec_elems = 0;
+    int64_t* rec_dev = nullptr;
+    size_t rec_cap = 0;
+    std::vector<std::string> key;  // replay log of runtime queries
+    std::vector<uint8_t> full_write;  // per tensor: every element overwritten, never read
+};
+
+struct Program {
+    Plan plan;
+    std::vector<KernelImpl> impls;
+    std::vector<int> tensor_key_depth;   // coarsest index depth per tensor (hazard keys)
+    bool cacheable = true;                // no data-dependent control flow
+    int device = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    int* err_dev = nullptr;
+    int status = 0;
+    int64_t opt_cache = 1, opt_chunks = 4, opt_sync = 1;
+    std::vector<char*> dev_bufs;         // host-staged tensor buffers (by tensor id)
+    std::vector<size_t> dev_caps;
+    void* scratch = nullptr;
+    size_t scratch_cap = 0;
+    std::unique_ptr<LaunchProgram> cached;
+    ptowsp_timing timing{};
+    std::string describe_json;
+
+    ~Program();
+};
+
+std::unique_ptr<Program> compile_program(const char* text, size_t len, int device);
+uint64_t run_program(Program& p, RuntimeContext* ctx);
+uint64_t run_single_task(Program& p, const std::string& kernel, const KernelTaskDesc* task);
+std::string describe_program(const Program& p);
+
+// Error helpers (thread-local message).
+void set_error(const std::string& msg);
+const char* last_error();
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+}  // namespace ptowsp

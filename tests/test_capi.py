@@ -1,0 +1,85 @@
+"""The C-ABI library loads, exports every declared symbol, and fails loudly without a GPU (CPU)."""
+
+import re
+from pathlib import Path
+
+import pytest
+
+from golden_cases import load_cases
+from pto_wsp_b200 import runtime, workloads
+from pto_wsp_b200.plan import dumps
+
+HDR = Path(__file__).resolve().parents[1] / "include" / "ptowsp_cuda.h"
+
+
+def declared_functions() -> list[str]:
+    text = HDR.read_text()
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(ptowsp_cuda_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "ptowsp_cuda_compile" in names and "ptowsp_cuda_main" in names and "ptowsp_cuda_run_task" in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = runtime.load_library()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+@pytest.mark.parametrize("idx", range(len(load_cases())))
+def test_compile_fixture_plans(idx):
+    case = load_cases()[idx]
+    ex = runtime.CudaExecutable(case["plan"])
+    d = ex.describe()
+    assert len(d["kernels"]) == len(case["plan"]["kernels"])
+
+
+@pytest.mark.parametrize("plan,impls", [
+    (workloads.rmsnorm_plan(4, 64), ["rmsnorm_rows"]),
+    (workloads.softmax_plan(32, 2048), ["softmax_rows"]),
+    (workloads.bgemm_plan(2, 256, 256, 512), ["matmul_tcgen05"]),
+    (workloads.bgemm_plan(2, 256, 256, 512, accumulate=True), ["matmul_tcgen05_acc"]),
+    (workloads.decode_plan(4, 8, 4, 128, 100, 64), ["paged_decode_gqa"]),
+    (workloads.indexer_plan(2, 8, 64, 128, 1024, 64), ["lightning_indexer_score", "topk_select"]),
+])
+def test_config_kernels_match_hand_written_impls(plan, impls):
+    d = runtime.CudaExecutable(plan).describe()
+    assert [k["impl"] for k in d["kernels"]] == impls
+
+
+def test_cpu_body_kernels_are_rejected():
+    plan = workloads.rmsnorm_plan(1, 1)
+    plan["kernels"][0]["attrs"] = {"cpp_src": "  // CPU body\n"}
+    with pytest.raises(runtime.PtoWspCudaError) as e:
+        runtime.CudaExecutable(plan)
+    assert e.value.code == 2 and "CPU C++ body" in str(e.value)
+
+
+def test_malformed_plans_are_rejected():
+    with pytest.raises(runtime.PtoWspCudaError) as e:
+        runtime.CudaExecutable({"format": "ptowsp-plan/1", "name": "x", "tensors": [], "kernels": [],
+                                "body": {"kind": "task", "kernel": "missing", "axis_args": [], "scalar_args": [],
+                                         "tensor_args": []}})
+    assert e.value.code == 1 and "Missing kernel def" in str(e.value)
+    lib = runtime.load_library()
+    import ctypes as C
+
+    h = C.c_void_p()
+    bad = b"{not json"
+    assert lib.ptowsp_cuda_compile(bad, len(bad), 0, C.byref(h)) == 1
+
+
+def test_run_without_gpu_fails_loudly():
+    if runtime.device_count() > 0:
+        pytest.skip("a GPU is present")
+    import numpy as np
+
+    ex = runtime.CudaExecutable(workloads.rmsnorm_plan(1, 2))
+    x = np.ones((1, 2, 16, 128), np.float32)
+    y = np.zeros_like(x)
+    with pytest.raises(runtime.PtoWspCudaError) as e:
+        ex.run_with_symbols([x, y], {}, {}, {})
+    assert e.value.code == 3
+    assert not y.any()  # no CPU fallback wrote anything
