@@ -126,12 +126,16 @@ PTOWSP_API uint64_t ptowsp_cuda_run_task(ptowsp_program* prog, const char* kerne
 PTOWSP_API int ptowsp_cuda_status(const ptowsp_program* prog);
 PTOWSP_API const char* ptowsp_cuda_last_error(void);
 
-/* Launch on this CUDA stream (cudaStream_t); NULL = the program's own stream. */
+/* Launch on this CUDA stream (cudaStream_t); NULL = the CUDA default stream.
+ * Until this is called a program uses a private non-blocking stream. */
 PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
 
 /* Integer options: "pipeline_chunks" (host-staged runs overlap copy and
  * compute in this many chunks, default 4), "cache_plans" (reuse the task table
- * of static workloads across runs, default 1), "sync" (block in main, default 1). */
+ * of static workloads across runs, default 1), "sync" (0: when every tensor
+ * is device memory, return without waiting; errors surface at the next
+ * synchronous run, default 1), "dry_run" (1: walk the task loop on the host
+ * only -- makespan, task and wave counts -- with no CUDA call, default 0). */
 PTOWSP_API int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value);
 
 typedef struct ptowsp_timing {

@@ -79,7 +79,8 @@ const char* ptowsp_cuda_last_error(void) { return ptowsp::last_error(); }
 
 int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream) {
     if (!prog || !prog->p) return PTOWSP_ERR_ARG;
-    prog->p->stream = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : prog->p->own_stream;
+    prog->p->stream = static_cast<cudaStream_t>(cuda_stream);  // nullptr: the CUDA default stream
+    prog->p->stream_set = true;
     return PTOWSP_OK;
 }
 
@@ -91,6 +92,7 @@ int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value)
         p.opt_cache = value != 0;
         if (!p.opt_cache) p.cached.reset();
     } else if (!std::strcmp(key, "sync")) p.opt_sync = value != 0;
+    else if (!std::strcmp(key, "dry_run")) p.opt_dry = value != 0;
     else {
         ptowsp::set_error(std::string("unknown option ") + key);
         return PTOWSP_ERR_ARG;

@@ -94,11 +94,13 @@ struct Walker {
     std::vector<std::pair<const std::string*, int64_t>> env;  // loop var -> value
     Scheduler sched;
     uint64_t rr = 0;
-    // current wave
-    std::unordered_set<uint64_t> wave_reads, wave_writes;
-    std::unordered_map<const Node*, size_t> wave_batch;  // task node -> batch index in current wave
+    // Dependency levels: a task goes to the first wave after the last wave that
+    // wrote a tile it touches, or read a tile it writes (RAW, WAR, WAW).
+    std::unordered_map<uint64_t, size_t> last_write, max_read;
+    size_t wave_floor = 0;  // waves below this were launched by a flush
     std::vector<std::string>& log;
     std::function<void()> flush;
+    bool dry = false;
     std::vector<uint8_t> written_any;  // tensors written by a task so far
     // full-overwrite tracking: elements stored per tensor and whether any two stores hit the same tile
     std::vector<int64_t> write_elems;
@@ -120,7 +122,6 @@ struct Walker {
         write_elems.assign(p.plan.tensors.size(), 0);
         write_keys.resize(p.plan.tensors.size());
         write_partial.assign(p.plan.tensors.size(), 0);
-        L.waves.emplace_back();
     }
 
     int64_t var(const std::string& name) const {
@@ -246,22 +247,29 @@ struct Walker {
         return off;
     }
 
+    static uint64_t mix64(uint64_t z) {  // splitmix64 finaliser
+        z += 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    }
+    // Tile key: tensor id + the view's leading indices, cut to the coarsest
+    // index depth any view of that tensor uses (so views at different depths
+    // that overlap get the same key).
     uint64_t view_key(const TensorArg& ta) {
         int depth = std::max(P.tensor_key_depth[ta.tensor], 0);
-        uint64_t h = 0x9E3779B97F4A7C15ull ^ (static_cast<uint64_t>(ta.tensor) * 0xC2B2AE3D27D4EB4Full);
+        uint64_t h = mix64(0x51ED27A0ull + ta.tensor);
         for (int d = 0; d < depth && d < static_cast<int>(ta.index.size()); ++d) {
             int64_t v = ta.index[d].is_var ? var(ta.index[d].var) : ta.index[d].c;
-            h ^= static_cast<uint64_t>(v) + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+            h = mix64(h ^ (static_cast<uint64_t>(v) * 0xD6E8FEB86659FD93ull + static_cast<uint64_t>(d)));
         }
         return h;
     }
 
+    // After a flush every later task must land in a wave that was not launched yet.
     void close_wave() {
-        if (L.waves.back().batches.empty()) return;
-        L.waves.emplace_back();
-        wave_reads.clear();
-        wave_writes.clear();
-        wave_batch.clear();
+        while (!L.waves.empty() && L.waves.back().batches.empty()) L.waves.pop_back();
+        wave_floor = L.waves.size();
     }
 
     uint64_t node(const Node& n, uint64_t ready) {
@@ -285,7 +293,7 @@ struct Walker {
                 const DType dt = P.plan.tensors[ta.tensor].dtype;
                 const int eb = dtype_bytes(dt);
                 alignas(8) unsigned char buf[8] = {0};
-                if (tb.on_device || written_any[ta.tensor]) {
+                if (!dry && (tb.on_device || written_any[ta.tensor])) {
                     flush();  // device data: finish the enqueued waves, then read the element back
                     PW_CUDA(cudaMemcpy(buf, tb.dev + off * eb, eb, cudaMemcpyDeviceToHost));
                 } else {
@@ -382,35 +390,39 @@ struct Walker {
         for (const auto& a : n.scalar_args) scal.push_back(arg_value(a));
         args.insert(args.end(), scal.begin(), scal.end());
 
-        // dependency wave
+        // dependency level
         uint64_t rkeys[dev::kMaxParams], wkeys[dev::kMaxParams];
         int nr = 0, nw = 0;
-        bool conflict = false;
+        size_t level = wave_floor;
         for (int ti = 0; ti < kd.num_tensor_params; ++ti) {
             const TensorArg& ta = n.tensor_args[n.param_to_arg[ti]];
             uint64_t key = view_key(ta);
             if (ki.param_write[ti]) {
                 wkeys[nw++] = key;
-                if (wave_reads.count(key) || wave_writes.count(key)) conflict = true;
+                if (auto f = last_write.find(key); f != last_write.end()) level = std::max(level, f->second + 1);
+                if (auto f = max_read.find(key); f != max_read.end()) level = std::max(level, f->second + 1);
             }
             if (ki.param_read[ti]) {
                 rkeys[nr++] = key;
-                if (wave_writes.count(key)) conflict = true;
+                if (auto f = last_write.find(key); f != last_write.end()) level = std::max(level, f->second + 1);
             }
         }
-        if (conflict) close_wave();
-        for (int i = 0; i < nr; ++i) wave_reads.insert(rkeys[i]);
-        for (int i = 0; i < nw; ++i) wave_writes.insert(wkeys[i]);
+        for (int i = 0; i < nw; ++i) last_write[wkeys[i]] = level;
+        for (int i = 0; i < nr; ++i) {
+            auto& m = max_read[rkeys[i]];
+            m = std::max(m, level);
+        }
+        while (L.waves.size() <= level) L.waves.emplace_back();
 
-        Wave& w = L.waves.back();
-        auto it = wave_batch.find(&n);
-        if (it == wave_batch.end()) {
+        Wave& w = L.waves[level];
+        auto it = w.by_node.find(&n);
+        if (it == w.by_node.end()) {
             Batch b;
             b.kernel = n.kernel_index;
             b.node = &n;
             b.stride = kd.num_tensor_params + static_cast<int>(n.axis_args.size()) + kd.num_scalar_params;
             w.batches.push_back(std::move(b));
-            it = wave_batch.emplace(&n, w.batches.size() - 1).first;
+            it = w.by_node.emplace(&n, w.batches.size() - 1).first;
         }
         Batch& b = w.batches[it->second];
         for (int ti = 0; ti < kd.num_tensor_params; ++ti) {
@@ -482,7 +494,7 @@ namespace {
 void ensure_device_state(Program& p) {
     if (!p.own_stream) {
         PW_CUDA(cudaStreamCreateWithFlags(&p.own_stream, cudaStreamNonBlocking));
-        if (!p.stream) p.stream = p.own_stream;
+        if (!p.stream_set) p.stream = p.own_stream;
         PW_CUDA(cudaEventCreate(&p.ev0));
         PW_CUDA(cudaEventCreate(&p.ev1));
         PW_CUDA(cudaMalloc(&p.err_dev, sizeof(int)));
@@ -585,8 +597,11 @@ void launch_batch(Program& P, const Batch& B, const Node& node, std::vector<Tens
 uint64_t run_program(Program& P, RuntimeContext* ctx) {
     auto t_start = std::chrono::steady_clock::now();
     if (!ctx) throw Error(PTOWSP_ERR_ARG, "RuntimeContext is null");
-    PW_CUDA(cudaSetDevice(P.device));
-    ensure_device_state(P);
+    const bool dry = P.opt_dry != 0;  // host-only walk: no CUDA calls at all
+    if (!dry) {
+        PW_CUDA(cudaSetDevice(P.device));
+        ensure_device_state(P);
+    }
     P.timing = ptowsp_timing{};
     const Plan& plan = P.plan;
 
@@ -609,12 +624,12 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         b.bytes = static_cast<size_t>(span) * dtype_bytes(ti.dtype);
         if (!b.user_ptr && b.bytes) throw Error(PTOWSP_ERR_ARG, "tensor " + std::to_string(tid) + " has no data pointer");
         cudaPointerAttributes attr{};
-        if (b.user_ptr && cudaPointerGetAttributes(&attr, b.user_ptr) == cudaSuccess &&
+        if (!dry && b.user_ptr && cudaPointerGetAttributes(&attr, b.user_ptr) == cudaSuccess &&
             (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged)) {
             b.on_device = true;
             b.dev = static_cast<char*>(b.user_ptr);
         }
-        cudaGetLastError();
+        if (!dry) cudaGetLastError();
         if (!b.on_device && b.bytes) all_device = false;
     }
     // read / written sets per tensor from the kernels' param sets
@@ -642,7 +657,7 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         P.dev_bufs.resize(T.size(), nullptr);
         P.dev_caps.resize(T.size(), 0);
     }
-    for (size_t tid = 0; tid < T.size(); ++tid) {
+    for (size_t tid = 0; tid < T.size() && !dry; ++tid) {
         TensorBinding& b = T[tid];
         if (b.on_device || b.bytes == 0) continue;
         if (P.dev_caps[tid] < b.bytes) {
@@ -728,6 +743,31 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         L->full_write.assign(T.size(), 0);
         for (size_t tid = 0; tid < T.size(); ++tid)
             L->full_write[tid] = W->fully_written(tid) ? 1 : 0;
+    }
+
+    if (dry) {
+        if (!L) {  // data-dependent workload: walk reading host memory only
+            fresh = std::make_unique<LaunchProgram>();
+            L = fresh.get();
+            W = std::make_unique<Walker>(P, ctx, T, *L, log);
+            W->flush = [] {};
+            W->dry = true;
+            L->makespan = W->node(*plan.body, 0);
+            W->close_wave();
+            L->full_write.assign(T.size(), 0);
+        }
+        for (size_t tid = 0; tid < T.size(); ++tid) {
+            const TensorBinding& b = T[tid];
+            const bool skip = !b.read && !L->full_write.empty() && L->full_write[tid];
+            if ((b.read || b.written) && !skip) P.timing.h2d_bytes += b.bytes;
+            if (b.written) P.timing.d2h_bytes += b.bytes;
+        }
+        P.timing.tasks = L->tasks;
+        for (auto& w : L->waves) {
+            P.timing.waves += w.batches.empty() ? 0 : 1;
+            P.timing.launches += w.batches.size();
+        }
+        return L->makespan;
     }
 
     // ---- stage host tensors into HBM ----

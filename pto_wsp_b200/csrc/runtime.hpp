@@ -57,6 +57,7 @@ struct Batch {  // tasks of one kernel inside one wave
 
 struct Wave {
     std::vector<Batch> batches;
+    std::unordered_map<const Node*, size_t> by_node;  // task node -> batch index
 };
 
 struct LaunchProgram {  // result of one walk, reusable for static workloads
@@ -78,10 +79,11 @@ struct Program {
     int device = 0;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
+    bool stream_set = false;           // caller chose a stream (nullptr = CUDA default stream)
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     int* err_dev = nullptr;
     int status = 0;
-    int64_t opt_cache = 1, opt_chunks = 4, opt_sync = 1;
+    int64_t opt_cache = 1, opt_chunks = 4, opt_sync = 1, opt_dry = 0;
     std::vector<char*> dev_bufs;         // host-staged tensor buffers (by tensor id)
     std::vector<size_t> dev_caps;
     void* scratch = nullptr;

@@ -257,9 +257,9 @@ class CudaExecutable:
         return int(cycles)
 
     def set_stream(self, stream: Any) -> None:
-        """Launch on a CUDA stream (torch.cuda.Stream, raw handle int, or None)."""
+        """Launch on a CUDA stream (torch.cuda.Stream or raw cudaStream_t handle; 0 = default stream)."""
         handle = getattr(stream, "cuda_stream", stream)
-        self._lib.ptowsp_cuda_set_stream(self._h, C.c_void_p(int(handle) if handle else 0))
+        self._lib.ptowsp_cuda_set_stream(self._h, C.c_void_p(int(handle) if handle else None))
 
     def set_option(self, key: str, value: int) -> None:
         rc = self._lib.ptowsp_cuda_set_option(self._h, key.encode(), int(value))

@@ -83,3 +83,45 @@ def test_run_without_gpu_fails_loudly():
         ex.run_with_symbols([x, y], {}, {}, {})
     assert e.value.code == 3
     assert not y.any()  # no CPU fallback wrote anything
+
+
+@pytest.mark.parametrize("idx", range(len(load_cases())), ids=[c["name"] for c in load_cases()])
+def test_native_cycle_model_matches_oracle_dry_run(idx):
+    """The C++ walk + cycle model gives the CPU-sim makespan for every reference case (host only)."""
+    from golden_cases import materialize
+
+    case = load_cases()[idx]
+    roots, arrays, axis, syms, sptr = materialize(case, idx)
+    ex = runtime.CudaExecutable(case["plan"])
+    ex.set_option("dry_run", 1)
+    assert ex.run_with_symbols(arrays, axis, syms, sptr) == case["cycles"]
+
+
+def test_dry_run_waves_and_staging():
+    import numpy as np
+
+    ex = runtime.CudaExecutable(workloads.softmax_plan(4, 16))
+    ex.set_option("dry_run", 1)
+    x = np.zeros((4, 16, 32, 256), np.float32)
+    y = np.zeros_like(x)
+    c = ex.run_with_symbols([x, y], {}, {}, {})
+    t = ex.timing()
+    assert t["tasks"] == 64 and t["waves"] == 1 and t["launches"] == 1
+    assert t["h2d_bytes"] == x.nbytes and t["d2h_bytes"] == y.nbytes  # write-only output is not staged in
+    assert c > 0
+
+
+def test_dry_run_inout_chain_waves():
+    import numpy as np
+
+    # bgemm k-tile accumulation form: C[b][i][j] += A . B over P.seq(k) -> one wave per k step
+    from golden_cases import case_index, materialize
+
+    cases = load_cases()
+    idx = case_index(cases, "example:bgemm#0")
+    roots, arrays, axis, syms, sptr = materialize(cases[idx], idx)
+    ex = runtime.CudaExecutable(cases[idx]["plan"])
+    ex.set_option("dry_run", 1)
+    ex.run_with_symbols(arrays, axis, syms, sptr)
+    t = ex.timing()
+    assert t["tasks"] == 64 and t["waves"] == 4
