@@ -102,6 +102,8 @@ int tile_program_max_smem();
 // Matmul tile task: C[M,N] (f32) = A[M,K] (f16) . B[K,N] (f16) (+ C if accumulate).
 // Params: 0 = A, 1 = B, 2 = C (same tensor for InOut).
 cudaError_t launch_matmul_tiles(const TaskBatch& b, int accumulate, int workers, cudaStream_t s);
+// Shape/stride/alignment conditions of the tcgen05 path (per-task offsets are checked by the host).
+bool matmul_tiles_supported(const TaskBatch& b);
 
 // Built-ins.
 cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int num_kv_heads, int workers, void* scratch,

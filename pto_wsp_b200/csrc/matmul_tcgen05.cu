@@ -1,0 +1,456 @@
+// Matmul tile tasks on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// A task is the reference's Matmul kernel instance (src/python/pto_codegen.cpp:
+// 817-929): C[M,N] (f32) = A[M,K] (f16) . B[K,N] (f16), optionally C += A.B
+// (the InOut accumulate form of examples/bgemm/pto_wsp_impl.py:56-76).  M = 128
+// rows; N in {64,128,256}; K a multiple of 64.
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: per 64-wide K step, one 128x64 A box (K-major)
+//               and N/64 boxes of 64(N)x64(K) B (MN-major, straight from the
+//               row-major B view -- no transpose pass), 128-byte swizzle, into a
+//               STAGES-deep shared-memory ring guarded by mbarriers.
+//   warp 1      owns TMEM (2 accumulators of N f32 columns) and issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N, K=16) from one
+//               thread; tcgen05.commit frees ring slots / publishes finished
+//               accumulators.
+//   warps 2-5   epilogue: tcgen05.ld 32x32b rows out of TMEM (warp w reads TMEM
+//               lanes 32*(w%4)..), optional C add, 128-bit stores.  Two TMEM
+//               accumulators let the epilogue of tile i overlap tile i+1's MMAs.
+// Every mbarrier wait is bounded (~2 s of %globaltimer): on timeout the CTA
+// records kErrTimeout, drains its own copies and MMAs, frees TMEM and returns.
+// No cluster multicast anywhere (loads read this GPU's memory only, per CTA).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+
+#include "device.hpp"
+
+namespace ptowsp::dev {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int THREADS = 192;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+struct MMArgs {
+    const int64_t* rec;
+    int64_t ntasks;
+    int stride;
+    int64_t a_pitch, b_pitch;  // elements per row of the A / B tensor maps
+    float* c;                  // C base
+    int64_t c_pitch;           // C row stride (elements)
+    int k_steps;               // K / 64
+    int accumulate;
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false on abort (set by another role) or timeout (sets the flags).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+    uint64_t start = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u) {
+            if (*abort_flag) return false;
+            const uint64_t now = globaltimer();
+            if (start == 0) {
+                start = now;
+            } else if (now - start > kTimeoutNs) {
+                atomicOr(err, kErrTimeout);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05): start>>4 [0,14), LBO>>4 [16,30),
+// SBO>>4 [32,46), version 1 [46,48), layout type [61,64) (2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;
+    d |= 2ull << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: D f32 [4,6)=1, A f16 [7,10)=0, B f16
+// [10,13)=0, A K-major [15]=0, B MN-major [16]=1, N>>3 [17,23), M>>4 [24,29).
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN>
+struct Smem {
+    // as many ring stages as fit in ~200 KB (6 for N=128, 4 for N=256)
+    static constexpr int STAGES_FIT = (200 * 1024) / (BM * BK * 2 + BN * BK * 2);
+    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+    static constexpr int A_BYTES = BM * BK * 2;              // 16 KB
+    static constexpr int B_BYTES = BN * BK * 2;              // BN/64 boxes of 8 KB
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int RING = STAGES * STAGE_BYTES;
+    static_assert(STAGES >= 2, "ring too small");
+    static constexpr int BAR_OFF = RING;                      // barriers after the ring
+    static constexpr int TOTAL = RING + 256 + 1024;           // + barriers/flags + alignment slack
+    static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+};
+
+template <int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+    matmul_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          MMArgs args) {
+    using S = Smem<BN>;
+    constexpr int STAGES = S::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+    // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], drain
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* tfull = bars + 2 * STAGES;
+    uint64_t* tempty = bars + 2 * STAGES + 2;
+    uint64_t* drain = bars + 2 * STAGES + 4;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 5);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&tfull[a]), 1);
+            mbar_init(smem_u32(&tempty[a]), 4 * 32);
+        }
+        mbar_init(smem_u32(drain), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(S::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int64_t first = blockIdx.x, step = gridDim.x;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, last_parity = 0;
+            for (int64_t t = first; t < args.ntasks && !*abort_flag; t += step) {
+                const int64_t* rec = args.rec + t * args.stride;
+                const int64_t oa = rec[0], ob = rec[1];
+                const int32_t ax = static_cast<int32_t>(oa % args.a_pitch), ay = static_cast<int32_t>(oa / args.a_pitch);
+                const int32_t bx = static_cast<int32_t>(ob % args.b_pitch), by = static_cast<int32_t>(ob / args.b_pitch);
+                for (int kb = 0; kb < args.k_steps; ++kb) {
+                    if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, args.err)) break;
+                    const uint32_t fb = smem_u32(&full[stage]);
+                    mbar_expect_tx(fb, S::STAGE_BYTES);
+                    uint8_t* sa = smem + stage * S::STAGE_BYTES;
+                    uint8_t* sb = sa + S::A_BYTES;
+                    tma_load_2d(smem_u32(sa), &tmap_a, ax + kb * BK, ay, fb);
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j) tma_load_2d(smem_u32(sb + j * 8192), &tmap_b, bx + j * 64, by + kb * BK, fb);
+                    issued_mask |= 1u << stage;
+                    last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // drain: every copy this CTA issued has landed before shared memory goes away
+            for (int s = 0; s < STAGES; ++s)
+                if (issued_mask & (1u << s)) {
+                    const uint32_t fb = smem_u32(&full[s]);
+                    const uint32_t par = (last_parity >> s) & 1u;
+                    uint64_t start = globaltimer();
+                    while (!mbar_try_wait(fb, par)) {
+                        if (globaltimer() - start > kTimeoutNs) {
+                            atomicOr(args.err, kErrTimeout);
+                            break;
+                        }
+                    }
+                }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = idesc_f16(BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool issued = false;
+            for (int64_t t = first; t < args.ntasks && !*abort_flag; t += step) {
+                if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, args.err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                bool ok = true;
+                for (int kb = 0; kb < args.k_steps; ++kb) {
+                    if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, args.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * S::STAGE_BYTES);
+                    const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        // A: K-major, 128-byte rows, 8-row atoms 1024 B apart; step 32 B per K=16.
+                        const uint64_t ad = smem_desc(sa + kk * 32, 16, 1024);
+                        // B: MN-major, 64-element (128 B) N chunks 8 KB apart (LBO), 8-row K atoms 1 KB apart (SBO);
+                        // step 16 K-rows (2 KB) per K=16.
+                        const uint64_t bd = smem_desc(sb + kk * 2048, 8192, 1024);
+                        mma_f16(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(smem_u32(&empty[stage]));
+                    issued = true;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(smem_u32(&tfull[acc]));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            // drain: all MMAs this thread issued have completed before TMEM is freed
+            if (issued) {
+                mma_commit(smem_u32(drain));
+                const uint64_t start = globaltimer();
+                while (!mbar_try_wait(smem_u32(drain), 0)) {
+                    if (globaltimer() - start > kTimeoutNs) {
+                        atomicOr(args.err, kErrTimeout);
+                        break;
+                    }
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int64_t t = first; t < args.ntasks && !*abort_flag; t += step) {
+            if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, args.err)) break;
+            tc_fence_after();
+            const int64_t oc = args.rec[t * args.stride + 2];
+            float* crow = args.c + oc + static_cast<int64_t>(row) * args.c_pitch;
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; ++cc) {
+                float v[32];
+                tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN + cc * 32), v);
+                float4* dst = reinterpret_cast<float4*>(crow + cc * 32);
+                if (args.accumulate) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 o = dst[i];
+                        v[4 * i + 0] += o.x;
+                        v[4 * i + 1] += o.y;
+                        v[4 * i + 2] += o.z;
+                        v[4 * i + 3] += o.w;
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&tempty[acc]));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(S::TMEM_COLS) : "memory");
+    }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D f16 tensor map over a row-pitched buffer: inner dim = pitch elements, `rows` rows.
+bool make_map(CUtensorMap* m, const void* base, int64_t pitch, int64_t rows, uint32_t box_x, uint32_t box_y) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(pitch), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch * 2)};
+    cuuint32_t box[2] = {box_x, box_y};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+cudaError_t launch_bn(const TaskBatch& b, int accumulate, int workers, cudaStream_t s) {
+    const ParamDesc& A = b.p[0];
+    const ParamDesc& B = b.p[1];
+    const ParamDesc& C = b.p[2];
+    CUtensorMap ma, mb;
+    const int64_t a_rows = (A.numel_span + A.s3 - 1) / A.s3;
+    const int64_t b_rows = (B.numel_span + B.s3 - 1) / B.s3;
+    if (!make_map(&ma, A.base, A.s3, a_rows, BK, BM)) return cudaErrorInvalidValue;
+    if (!make_map(&mb, B.base, B.s3, b_rows, 64, BK)) return cudaErrorInvalidValue;
+    MMArgs args;
+    args.rec = b.rec;
+    args.ntasks = b.ntasks;
+    args.stride = b.stride;
+    args.a_pitch = A.s3;
+    args.b_pitch = B.s3;
+    args.c = reinterpret_cast<float*>(C.base);
+    args.c_pitch = C.s3;
+    args.k_steps = A.cols / BK;
+    args.accumulate = accumulate;
+    args.err = b.err;
+    const int smem = Smem<BN>::TOTAL;
+    cudaError_t e = cudaFuncSetAttribute(matmul_tcgen05_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int64_t grid = std::min<int64_t>(b.ntasks, sm_count());
+    if (workers > 0) grid = std::min<int64_t>(grid, workers);
+    grid = std::max<int64_t>(grid, 1);
+    matmul_tcgen05_kernel<BN><<<static_cast<unsigned>(grid), THREADS, smem, s>>>(ma, mb, args);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool matmul_tiles_supported(const TaskBatch& b) {
+    const ParamDesc& A = b.p[0];
+    const ParamDesc& B = b.p[1];
+    const ParamDesc& C = b.p[2];
+    if (A.rows != BM || A.cols % BK != 0 || A.cols < BK || B.rows != A.cols) return false;
+    if (!(B.cols == 64 || B.cols == 128 || B.cols == 256) || C.rows != BM || C.cols != B.cols) return false;
+    if (A.s4 != 1 || B.s4 != 1 || C.s4 != 1) return false;
+    if (A.s3 % 8 || B.s3 % 8 || C.s3 % 4) return false;
+    if ((reinterpret_cast<uintptr_t>(A.base) | reinterpret_cast<uintptr_t>(B.base) | reinterpret_cast<uintptr_t>(C.base)) & 15)
+        return false;
+    return encode_fn() != nullptr;
+}
+
+cudaError_t launch_matmul_tiles(const TaskBatch& b, int accumulate, int workers, cudaStream_t s) {
+    switch (b.p[1].cols) {
+        case 64: return launch_bn<64>(b, accumulate, workers, s);
+        case 128: return launch_bn<128>(b, accumulate, workers, s);
+        case 256: return launch_bn<256>(b, accumulate, workers, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace ptowsp::dev

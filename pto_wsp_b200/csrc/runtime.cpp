@@ -521,7 +521,7 @@ void* ensure_scratch(Program& p, size_t bytes) {
 }
 
 // Launch one batch.  `node` is the task node whose tensor bindings the batch uses.
-void launch_batch(Program& P, const Batch& B, const Node& node, std::vector<TensorBinding>& T, const int64_t* rec_dev,
+void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBinding>& T, const int64_t* rec_dev,
                   uint64_t& launches) {
     const KernelDef& kd = P.plan.kernels[B.kernel];
     KernelImpl& ki = P.impls[B.kernel];
@@ -565,10 +565,35 @@ void launch_batch(Program& P, const Batch& B, const Node& node, std::vector<Tens
         const int c = kd.params[0].v.cols;
         if (!rows_ok || !(c == 128 || c == 256 || c == 512 || c == 1024)) kind = ImplKind::TileProgram;
     }
-    if (kind == ImplKind::Matmul || kind == ImplKind::MatmulAcc) kind = ImplKind::TileProgram;  // tcgen05 path below
+    if ((kind == ImplKind::Matmul || kind == ImplKind::MatmulAcc) && !ki.tp_ok && B.fast_ok == 0)
+        throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': operands do not meet the tcgen05 layout "
+                                            "conditions and the tiles exceed the generic tile program");
+    if (kind == ImplKind::Matmul || kind == ImplKind::MatmulAcc) {
+        // tcgen05 path: shape/stride/alignment conditions, then every task's TMA coordinates
+        if (B.fast_ok < 0) {
+            bool ok = dev::matmul_tiles_supported(tb) && !B.rec.empty();
+            const dev::ParamDesc &A = tb.p[0], &Bm = tb.p[1], &Cm = tb.p[2];
+            const int64_t K = A.cols, N = Bm.cols;
+            const int64_t a_rows = ok ? (A.numel_span + A.s3 - 1) / A.s3 : 0;
+            const int64_t b_rows = ok ? (Bm.numel_span + Bm.s3 - 1) / Bm.s3 : 0;
+            for (int64_t t = 0; ok && t < B.ntasks; ++t) {
+                const int64_t* r = &B.rec[t * B.stride];
+                const int64_t oa = r[0], ob = r[1], oc = r[2];
+                ok = oa >= 0 && ob >= 0 && oc >= 0 && oa % 8 == 0 && ob % 8 == 0 && oc % 4 == 0 &&
+                     (oa % A.s3) + K <= A.s3 && (oa / A.s3) + 128 <= a_rows && (ob % Bm.s3) + N <= Bm.s3 &&
+                     (ob / Bm.s3) + K <= b_rows && oc + 127 * Cm.s3 + N <= Cm.numel_span;
+            }
+            B.fast_ok = ok ? 1 : 0;
+        }
+        if (!B.fast_ok) kind = ImplKind::TileProgram;
+    }
     switch (kind) {
         case ImplKind::RmsNorm: e = dev::launch_rmsnorm_rows(tb, workers, P.stream); break;
         case ImplKind::Softmax: e = dev::launch_softmax_rows(tb, workers, P.stream); break;
+        case ImplKind::Matmul:
+        case ImplKind::MatmulAcc:
+            e = dev::launch_matmul_tiles(tb, kind == ImplKind::MatmulAcc ? 1 : 0, workers, P.stream);
+            break;
         case ImplKind::TileProgram:
             if (!ki.tp_ok) throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
             e = dev::launch_tile_program(tb, ki.tp_dev, ki.tp_smem, workers, P.stream);

@@ -53,6 +53,7 @@ struct Batch {  // tasks of one kernel inside one wave
     int stride = 0;
     size_t dev_off = 0;            // element offset in the device record buffer
     bool aligned_rows = true;      // fast row kernels usable
+    int8_t fast_ok = -1;           // hand-written kernel usable for every task (-1: not checked yet)
 };
 
 struct Wave {

@@ -363,3 +363,17 @@ def indexer_plan(batch: int, queries: int, heads: int, head_dim: int, context: i
     tensors = [("f16", [batch, queries * heads, head_dim]), ("f16", [batch, context, head_dim]),
                ("f32", [batch, queries, heads]), ("f32", [batch, queries, context]), ("i32", [batch, queries, topk])]
     return _plan(name, [*tensors], [ks.build(), kt.build()], {"kind": "combine", "children": [n1, n2]}, _schedule())
+
+
+def bgemm_views(a, b, c, tile_m: int = 128, tile_n: int = 128):
+    """The bgemm plan's tensor views of contiguous A[B,M,K], B[B,K,N], C[B,M,N] (numpy or torch)."""
+    Bn, M, K = a.shape
+    N = b.shape[2]
+    av = a.reshape(Bn, M // tile_m, tile_m, K)
+    if hasattr(b, "permute"):
+        bv = b.reshape(Bn, K, N // tile_n, tile_n).permute(0, 2, 1, 3)
+        cv = c.reshape(Bn, M // tile_m, tile_m, N // tile_n, tile_n).permute(0, 1, 3, 2, 4)
+    else:
+        bv = b.reshape(Bn, K, N // tile_n, tile_n).transpose(0, 2, 1, 3)
+        cv = c.reshape(Bn, M // tile_m, tile_m, N // tile_n, tile_n).transpose(0, 1, 3, 2, 4)
+    return av, bv, cv
