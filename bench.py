@@ -43,6 +43,8 @@ WORKLOADS = {
                 "rows": 32, "cols": 256},
     "rmsnorm": {"config": "config 1: RMSNorm Tile[16,128] f32, X[64,4096,16,128] (GPU scale)", "batch": 64,
                 "tiles": 4096, "rows": 16, "cols": 128},
+    "bgemm": {"config": "config 3: bgemm 64 x (2048x2048x2048), f16 in, f32 acc/out, 128x128 output tiles",
+              "batch": 64, "m": 2048, "n": 2048, "k": 2048},
 }
 
 
@@ -53,14 +55,14 @@ def _env_int(k: str, d: int) -> int:
         return d
 
 
-def peaks() -> tuple[float, str]:
+def peaks(key: str = "hbm_gbs") -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+            return float(json.loads(p.read_text())[key]), "measured"
         except Exception:  # noqa: BLE001
             pass
-    return 6650.0, "fallback"
+    return (6650.0 if key == "hbm_gbs" else 1590.0), "fallback"
 
 
 def traffic_from_profiles(kernel: str, workload: str) -> float | None:
@@ -213,6 +215,181 @@ def run_reference(args, wl: dict, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def gemm_cpu_baseline(a_host, b_host, tiles: int = 128, budget_s: float = 10.0) -> dict:
+    """C port of the CPU-sim gemm task (TLOAD, TMATMUL f32 acc, TSTORE) on a bounded batch sample."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+
+    import cpu_native
+
+    nth = cpu_native.threads()
+    B, M, K = a_host.shape
+    N = b_host.shape[2]
+    nb = 1
+    t0 = time.perf_counter()
+    c = np.empty((nb, M, N), np.float32)
+    cpu_native.gemm_tiles(a_host[:nb], b_host[:nb], c, tiles, tiles, nth)
+    dt = time.perf_counter() - t0
+    nb2 = int(max(1, min(B, budget_s / max(dt, 1e-6))))
+    if nb2 > 1:
+        c = np.empty((nb2, M, N), np.float32)
+        t0 = time.perf_counter()
+        cpu_native.gemm_tiles(a_host[:nb2], b_host[:nb2], c, tiles, tiles, nth)
+        dt = time.perf_counter() - t0
+    else:
+        nb2 = nb
+    tf = 2.0 * nb2 * M * N * K / dt / 1e12
+    return {"value": round(tf, 5), "unit": "TFLOP/s", "cores": nth, "kind": "port",
+            "sample": f"{nb2} of {B} batch elements ({dt:.2f} s), C port of the CPU-sim gemm tile task "
+                      f"(oracle/cpu_kernels.c, f32 accumulation), {nth} threads"}
+
+
+def run_bgemm(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
+    B, M, N, K = wl["batch"], wl["m"], wl["n"], wl["k"]
+    flops = 2.0 * B * M * N * K
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import numpy as np
+
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import cpu_native
+
+        rng = np.random.default_rng(0)
+        nb = 1
+        a = rng.uniform(-1, 1, (nb, M, K)).astype(np.float16)
+        b = rng.uniform(-1, 1, (nb, K, N)).astype(np.float16)
+        c = np.empty((nb, M, N), np.float32)
+        nth = cpu_native.threads()
+        # bounded step: a 512-row slab of one batch element per step
+        rows = 512
+        for _ in range(args.warmup):
+            cpu_native.gemm_tiles(a[:, :rows], b, c[:, :rows], 128, 128, nth)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            cpu_native.gemm_tiles(a[:, :rows], b, c[:, :rows], 128, 128, nth)
+        dt = time.perf_counter() - t0
+        tf = 2.0 * rows * N * K * args.steps / dt / 1e12
+        print(json.dumps({
+            "impl": "reference", "metric": "bgemm task-loop throughput", "value": round(tf, 5), "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 in / f32 acc", "data": "synthetic (seeded numpy)",
+            "config": {"workload": wl["config"], "sample_per_step": f"{rows}x{N}x{K} slab of one batch element"},
+            "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOP/s", "cores": nth, "kind": "port",
+                             "sample": f"{rows}-row slab per step; C port of the CPU-sim gemm task, {nth} threads"},
+            "e2e": {"value": round(tf, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
+
+    import numpy as np
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from pto_wsp_b200 import workloads
+    from pto_wsp_b200.runtime import CudaExecutable
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + rank)
+    a = (torch.rand((B, M, K), generator=g, device=dev) * 2 - 1).half()
+    b = (torch.rand((B, K, N), generator=g, device=dev) * 2 - 1).half()
+    c = torch.empty((B, M, N), device=dev, dtype=torch.float32)
+    ex = CudaExecutable(workloads.bgemm_plan(B, M, N, K), device=local_rank)
+    stream = torch.cuda.current_stream(dev)
+    ex.set_stream(stream)
+    ex.set_option("sync", 0)
+    views = list(workloads.bgemm_views(a, b, c))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        ex.run_with_symbols(views, {}, {}, {})
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    with ClockSampler(gpu_index(local_rank)) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            ex.run_with_symbols(views, {}, {}, {})
+            launches += int(ex.timing()["launches"])
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        ms_max = max_over_ranks(ms)
+        # end to end with pinned host buffers
+        ex.set_option("sync", 1)
+        ah_t = torch.empty(a.shape, dtype=a.dtype, pin_memory=True)
+        bh_t = torch.empty(b.shape, dtype=b.dtype, pin_memory=True)
+        ch_t = torch.empty(c.shape, dtype=c.dtype, pin_memory=True)
+        ah_t.copy_(a)
+        bh_t.copy_(b)
+        ah, bh, ch = ah_t.numpy(), bh_t.numpy(), ch_t.numpy()
+        hviews = list(workloads.bgemm_views(ah, bh, ch))
+        ex.run_with_symbols(hviews, {}, {}, {})
+        e2e_steps = args.e2e_steps or min(args.steps, 10)
+        barrier()
+        t0 = time.perf_counter()
+        h2d = d2h = 0
+        for _ in range(e2e_steps):
+            ex.run_with_symbols(hviews, {}, {}, {})
+            tm = ex.timing()
+            h2d += tm["h2d_bytes"]
+            d2h += tm["d2h_bytes"]
+        barrier()
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+    clocks = clk.summary()
+    value = world * flops * args.steps / (ms_max / 1e3) / 1e12
+    e2e = world * flops * e2e_steps / e2e_s / 1e12
+    peak, peak_kind = peaks("bf16_tflops")
+    achieved = flops / (ms / args.steps / 1e3) / 1e12
+    ref = (a[0].double() @ b[0].double())
+    err = float(((c[0].double() - ref).abs() / (ref.abs() + ref.pow(2).mean().sqrt())).max())
+    if rank == 0:
+        line = {
+            "metric": "bgemm task-loop throughput", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 acc",
+            "data": "synthetic (seeded torch.rand on device, U(-1,1))",
+            "config": {"workload": wl["config"], "global_batch": B * world, "per_rank_batch": B,
+                       "parallelism": f"P(batch) sharded, {world} rank(s)",
+                       "l2": "operands 1 GiB > 126 MB L2 (no flush needed)"},
+            "gpu_launches": launches,
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles("matmul_tcgen05", "bgemm"),
+                         "peak_kind": peak_kind + " (cuBLAS bf16 burst; fp16 runs at the same tensor rate)",
+                         "kernel": "matmul_tcgen05", "flops_per_launch": flops},
+            "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d // e2e_steps,
+                    "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps},
+            "clocks": clocks,
+            "max_rel_err_vs_fp64_batch0": err,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = gemm_cpu_baseline(ah, bh)
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -234,6 +411,9 @@ def main() -> None:
     world = _env_int("WORLD_SIZE", 1)
     local_rank = _env_int("LOCAL_RANK", 0)
 
+    if args.workload == "bgemm":
+        run_bgemm(args, wl, rank, world, local_rank)
+        return
     if args.impl == "reference":
         run_reference(args, wl, rank)
         return

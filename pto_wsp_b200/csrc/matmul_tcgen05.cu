@@ -163,9 +163,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 template <int BN>
 struct Smem {
-    // as many ring stages as fit in ~200 KB (6 for N=128, 4 for N=256)
-    static constexpr int STAGES_FIT = (200 * 1024) / (BM * BK * 2 + BN * BK * 2);
-    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+    // as many ring stages as fit next to the barriers in the 227 KB per CTA (7 for N=128, 4 for N=256)
+    static constexpr int STAGES_FIT = (232448 - 1280) / (BM * BK * 2 + BN * BK * 2);
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int A_BYTES = BM * BK * 2;              // 16 KB
     static constexpr int B_BYTES = BN * BK * 2;              // BN/64 boxes of 8 KB
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;

@@ -469,6 +469,14 @@ struct Walker {
 
 // ---------------------------------------------------------------------------
 
+Batch::~Batch() {
+    if (fast_rec_dev) cudaFree(fast_rec_dev);
+}
+
+LaunchProgram::~LaunchProgram() {
+    if (rec_dev) cudaFree(rec_dev);
+}
+
 void set_error(const std::string& msg) { g_err = msg; }
 const char* last_error() { return g_err.c_str(); }
 
@@ -476,7 +484,7 @@ Program::~Program() {
     int prev = -1;
     cudaGetDevice(&prev);
     cudaSetDevice(device);
-    if (cached && cached->rec_dev) cudaFree(cached->rec_dev);
+    cached.reset();
     for (auto& ki : impls)
         if (ki.tp_dev) cudaFree(ki.tp_dev);
     for (char* b : dev_bufs)
@@ -584,8 +592,36 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                      (ob / Bm.s3) + K <= b_rows && oc + 127 * Cm.s3 + N <= Cm.numel_span;
             }
             B.fast_ok = ok ? 1 : 0;
+            B.fast_n = static_cast<int>(N);
+            B.fast_ntasks = B.ntasks;
+            // pair tasks (t, t+1) that share A and cover adjacent N tiles of B and C
+            if (ok && N == 128 && B.ntasks % 2 == 0) {
+                bool pair = true;
+                for (int64_t t = 0; pair && t < B.ntasks; t += 2) {
+                    const int64_t* r0 = &B.rec[t * B.stride];
+                    const int64_t* r1 = &B.rec[(t + 1) * B.stride];
+                    pair = r1[0] == r0[0] && r1[1] == r0[1] + N && r1[2] == r0[2] + N &&
+                           (r0[1] % Bm.s3) + 2 * N <= Bm.s3 && r0[2] + 127 * Cm.s3 + 2 * N <= Cm.numel_span;
+                }
+                if (pair) {
+                    std::vector<int64_t> m(static_cast<size_t>(B.ntasks / 2) * 3);
+                    for (int64_t t = 0; t < B.ntasks; t += 2)
+                        for (int j = 0; j < 3; ++j) m[(t / 2) * 3 + j] = B.rec[t * B.stride + j];
+                    PW_CUDA(cudaMalloc(&B.fast_rec_dev, m.size() * sizeof(int64_t)));
+                    PW_CUDA(cudaMemcpy(B.fast_rec_dev, m.data(), m.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
+                    B.fast_ntasks = B.ntasks / 2;
+                    B.fast_n = 2 * static_cast<int>(N);
+                }
+            }
         }
         if (!B.fast_ok) kind = ImplKind::TileProgram;
+        if (B.fast_ok && B.fast_rec_dev) {
+            tb.rec = B.fast_rec_dev;
+            tb.ntasks = B.fast_ntasks;
+            tb.stride = 3;
+            tb.p[1].cols = B.fast_n;
+            tb.p[2].cols = B.fast_n;
+        }
     }
     switch (kind) {
         case ImplKind::RmsNorm: e = dev::launch_rmsnorm_rows(tb, workers, P.stream); break;
@@ -859,15 +895,11 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
             if (async_run) PW_CUDA(cudaStreamSynchronize(P.stream));  // host records must outlive their copies
             for (auto& w : fresh->waves)
                 for (auto& b : w.batches) std::vector<int64_t>().swap(b.rec);  // records live on the device now
-            if (P.cached && P.cached->rec_dev) {
-                PW_CUDA(cudaStreamSynchronize(P.stream));
-                cudaFree(P.cached->rec_dev);
-            }
+            if (P.cached) PW_CUDA(cudaStreamSynchronize(P.stream));
             P.cached = std::move(fresh);
         } else {
             PW_CUDA(cudaStreamSynchronize(P.stream));
-            if (fresh->rec_dev) cudaFree(fresh->rec_dev);
-            fresh->rec_dev = nullptr;
+            fresh.reset();
         }
     }
     P.timing.total_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_start).count();

@@ -54,6 +54,23 @@ struct Batch {  // tasks of one kernel inside one wave
     size_t dev_off = 0;            // element offset in the device record buffer
     bool aligned_rows = true;      // fast row kernels usable
     int8_t fast_ok = -1;           // hand-written kernel usable for every task (-1: not checked yet)
+    // tcgen05 matmul: pairs of tasks that share their A tile and cover adjacent
+    // N tiles run as one 128x(2N) tile; their merged records live here.
+    int64_t* fast_rec_dev = nullptr;
+    int64_t fast_ntasks = 0;
+    int fast_n = 0;
+    Batch() = default;
+    Batch(Batch&& o) noexcept { *this = std::move(o); }
+    Batch& operator=(Batch&& o) noexcept {
+        kernel = o.kernel; node = o.node; rec = std::move(o.rec); ntasks = o.ntasks; stride = o.stride;
+        dev_off = o.dev_off; aligned_rows = o.aligned_rows; fast_ok = o.fast_ok; fast_rec_dev = o.fast_rec_dev;
+        fast_ntasks = o.fast_ntasks; fast_n = o.fast_n;
+        o.fast_rec_dev = nullptr;
+        return *this;
+    }
+    Batch(const Batch&) = delete;
+    Batch& operator=(const Batch&) = delete;
+    ~Batch();
 };
 
 struct Wave {
@@ -70,6 +87,10 @@ struct LaunchProgram {  // result of one walk, reusable for static workloads
     size_t rec_cap = 0;
     std::vector<std::string> key;  // replay log of runtime queries
     std::vector<uint8_t> full_write;  // per tensor: every element overwritten, never read
+    LaunchProgram() = default;
+    LaunchProgram(const LaunchProgram&) = delete;
+    LaunchProgram& operator=(const LaunchProgram&) = delete;
+    ~LaunchProgram();
 };
 
 struct Program {
