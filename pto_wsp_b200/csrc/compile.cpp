@@ -529,7 +529,8 @@ void setup_builtin(const KernelDef& kd, KernelImpl& ki) {
             pt.dtype != DType::I32 || tparam(kd, 4).v.dtype != DType::I32 || tparam(kd, 5).v.dtype != DType::F16)
             throw Error(PTOWSP_ERR_PLAN, "paged_decode_gqa: dtypes must be q/k/v/out f16, page_table/kv_len i32");
         if (q.cols != 128) throw Error(PTOWSP_ERR_UNSUPPORTED, "paged_decode_gqa: head_dim must be 128");
-        if (q.rows < 1 || q.rows > 16) throw Error(PTOWSP_ERR_UNSUPPORTED, "paged_decode_gqa: GQA group of 1..16 query heads");
+        if (q.rows != 1 && q.rows != 2 && q.rows != 4 && q.rows != 8)
+            throw Error(PTOWSP_ERR_UNSUPPORTED, "paged_decode_gqa: GQA group of 1, 2, 4 or 8 query heads");
         ki.param_write[5] = 1;
         ki.param_read[5] = 0;
         // Model charge with the static maximum length (page_table width x page size):
@@ -549,8 +550,8 @@ void setup_builtin(const KernelDef& kd, KernelImpl& ki) {
         if (q.cols != 128 || k.cols != 128) throw Error(PTOWSP_ERR_UNSUPPORTED, "lightning_indexer_score: head_dim must be 128");
         if (w.rows * w.cols != q.rows || s.rows != w.rows || s.cols != k.rows)
             throw Error(PTOWSP_ERR_PLAN, "lightning_indexer_score: shapes q[Q*H,D] k[T,D] w[Q,H] scores[Q,T]");
-        if (w.cols != 64 || (w.rows != 8 && w.rows != 4 && w.rows != 2 && w.rows != 1) || k.rows % 128 != 0)
-            throw Error(PTOWSP_ERR_UNSUPPORTED, "lightning_indexer_score: 64 heads, 1..8 queries, keys multiple of 128");
+        if (w.cols != 64 || w.rows != 8 || k.rows % 128 != 0)
+            throw Error(PTOWSP_ERR_UNSUPPORTED, "lightning_indexer_score: 8 queries x 64 heads, keys a multiple of 128");
         ki.param_write[3] = 1;
         ki.param_read[3] = 0;
         const uint64_t QH = q.rows, D = q.cols, T = k.rows, Q = w.rows;

@@ -1,0 +1,416 @@
+// Built-in paged GQA decode and top-k selection (config 5).
+//
+// paged_decode_gqa -- one task = (request r, kv head h): the G query heads
+// sharing KV head h attend over the request's L = kv_len[r] cached tokens,
+// found through the page table (page p of the request holds tokens
+// [16p, 16p+16)).  Math as the reference toy kernel
+// (examples/flashinfer_decode/pto_wsp_impl.py:38-54, golden.py:7-12):
+// softmax(q K^T / sqrt(D)) V, f32 softmax, f16 output (round to nearest even).
+//
+// HBM-bound: every K/V byte is used for 2*G FLOP (G = 4: ~4 FLOP/B), below the
+// CUDA-core ridge, so this runs on CUDA cores, not tensor cores.  Split-KV:
+// each task is cut into 512-token chunks (one CTA each, empty chunks exit at
+// once); a chunk computes its scores lane-per-token (K rows read once, L1
+// cached), softmax statistics, then P.V lane-per-dimension (V rows read
+// coalesced), and writes (max, sum, acc[G][128]) to scratch; a second kernel
+// merges the chunks of a task with the log-sum-exp rule and stores f16.
+//
+// topk_select -- indices of the K largest of N scores, ordered by score
+// descending, ties by lower index (examples/deepseek_lightning_indexer/
+// golden.py:6-25).  One CTA per row: the row is staged in shared memory as
+// order-preserving 32-bit keys, an 8-bit radix select finds the K-th key, the
+// K winners (ties at the threshold taken in index order) are gathered and
+// bitonic-sorted by (key desc, index asc).  Bit-exact by construction.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "device.hpp"
+
+namespace ptowsp::dev {
+
+namespace {
+
+constexpr int kChunk = 512;       // tokens per split-KV chunk
+constexpr int kDecThreads = 128;  // 4 warps
+constexpr int kHeadDim = 128;
+
+template <int G>
+__global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBatch b, int page_size, int chunks,
+                                                                        float* __restrict__ scratch) {
+    __shared__ float q_s[G][kHeadDim];
+    __shared__ float s_s[G][kChunk];
+    __shared__ float red_s[4][G][kHeadDim];
+    __shared__ float stat_s[2][4][G];
+
+    const int64_t task = blockIdx.x / chunks;
+    const int chunk = blockIdx.x % chunks;
+    if (task >= b.ntasks) return;
+    const int64_t* rec = b.rec + task * b.stride;
+    const ParamDesc& Pq = b.p[0];
+    const ParamDesc& Pk = b.p[1];
+    const ParamDesc& Pv = b.p[2];
+    const ParamDesc& Ppt = b.p[3];
+    const ParamDesc& Pl = b.p[4];
+    const int h = static_cast<int>(rec[b.nparams + 1]);
+    int32_t L = reinterpret_cast<const int32_t*>(Pl.base)[rec[4]];
+    if (L > Ppt.cols * page_size) {  // more tokens than the page table row can address
+        if (chunk == 0) atomicOr(b.err, kErrShape);
+        L = Ppt.cols * page_size;
+    }
+    const int t0 = chunk * kChunk;
+    if (t0 >= L) return;  // empty chunk (also L <= 0: the merge kernel writes zeros)
+    const int n = min(kChunk, L - t0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
+
+    // q -> shared (f32), pre-scaled by 1/sqrt(D)
+    const __half* q = reinterpret_cast<const __half*>(Pq.base) + rec[0];
+    for (int e = tid; e < G * kHeadDim; e += kDecThreads) {
+        const int g = e / kHeadDim, d = e % kHeadDim;
+        q_s[g][d] = __half2float(q[g * Pq.s3 + d]) * scale;
+    }
+    __syncthreads();
+
+    const int32_t* pt = reinterpret_cast<const int32_t*>(Ppt.base) + rec[3];
+    const int64_t max_page_k = (Pk.numel_span - (int64_t)(page_size - 1) * Pk.s4 - h * kHeadDim - kHeadDim) / Pk.s3;
+    const int64_t max_page_v = (Pv.numel_span - (int64_t)(page_size - 1) * Pv.s4 - h * kHeadDim - kHeadDim) / Pv.s3;
+    const int64_t max_page = min(max_page_k, max_page_v);
+    const __half* kb = reinterpret_cast<const __half*>(Pk.base);
+    const __half* vb = reinterpret_cast<const __half*>(Pv.base);
+
+    // ---- scores, lane per token ----
+    float mloc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) mloc[g] = -INFINITY;
+    for (int i = tid; i < n; i += kDecThreads) {
+        const int tok = t0 + i;
+        const int64_t page = pt[static_cast<int64_t>(tok / page_size) * Ppt.s4];
+        float acc[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g] = 0.f;
+        if (page < 0 || page > max_page) {
+            atomicOr(b.err, kErrBounds);
+        } else {
+            const uint4* kr = reinterpret_cast<const uint4*>(kb + page * Pk.s3 + (tok % page_size) * Pk.s4 + h * kHeadDim);
+            uint4 raw[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) raw[j] = __ldg(kr + j);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const __half2* hp = reinterpret_cast<const __half2*>(&raw[j]);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float2 kf = __half22float2(hp[u]);
+                    const int d = j * 8 + u * 2;
+#pragma unroll
+                    for (int g = 0; g < G; ++g) acc[g] = fmaf(kf.x, q_s[g][d], fmaf(kf.y, q_s[g][d + 1], acc[g]));
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            s_s[g][i] = acc[g];
+            mloc[g] = fmaxf(mloc[g], acc[g]);
+        }
+    }
+    // ---- chunk max ----
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float m = mloc[g];
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) stat_s[0][warp][g] = m;
+    }
+    __syncthreads();
+    float mx[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) mx[g] = fmaxf(fmaxf(stat_s[0][0][g], stat_s[0][1][g]), fmaxf(stat_s[0][2][g], stat_s[0][3][g]));
+    // ---- p = exp(s - m), chunk sum ----
+    float lsum[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) lsum[g] = 0.f;
+    for (int i = tid; i < n; i += kDecThreads) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float p = expf(s_s[g][i] - mx[g]);
+            s_s[g][i] = p;
+            lsum[g] += p;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float s = lsum[g];
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) stat_s[1][warp][g] = s;
+    }
+    __syncthreads();
+    // ---- P.V, lane per 4 head dims, warps split the tokens ----
+    float acc[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[g][u] = 0.f;
+    const int per_warp = (n + 3) / 4;
+    const int i0 = warp * per_warp, i1 = min(n, i0 + per_warp);
+    int i = i0;
+    for (; i + 4 <= i1; i += 4) {
+        uint2 raw[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int tok = t0 + i + u;
+            int64_t page = pt[static_cast<int64_t>(tok / page_size) * Ppt.s4];
+            if (page < 0 || page > max_page) page = 0;  // flagged in the score pass; read page 0 harmlessly
+            raw[u] = __ldg(reinterpret_cast<const uint2*>(vb + page * Pv.s3 + (tok % page_size) * Pv.s4 + h * kHeadDim) + lane);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const __half2* hp = reinterpret_cast<const __half2*>(&raw[u]);
+            const float2 v01 = __half22float2(hp[0]), v23 = __half22float2(hp[1]);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float p = s_s[g][i + u];
+                acc[g][0] = fmaf(p, v01.x, acc[g][0]);
+                acc[g][1] = fmaf(p, v01.y, acc[g][1]);
+                acc[g][2] = fmaf(p, v23.x, acc[g][2]);
+                acc[g][3] = fmaf(p, v23.y, acc[g][3]);
+            }
+        }
+    }
+    for (; i < i1; ++i) {
+        const int tok = t0 + i;
+        int64_t page = pt[static_cast<int64_t>(tok / page_size) * Ppt.s4];
+        if (page < 0 || page > max_page) page = 0;
+        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(vb + page * Pv.s3 + (tok % page_size) * Pv.s4 + h * kHeadDim) + lane);
+        const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+        const float2 v01 = __half22float2(hp[0]), v23 = __half22float2(hp[1]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float p = s_s[g][i];
+            acc[g][0] = fmaf(p, v01.x, acc[g][0]);
+            acc[g][1] = fmaf(p, v01.y, acc[g][1]);
+            acc[g][2] = fmaf(p, v23.x, acc[g][2]);
+            acc[g][3] = fmaf(p, v23.y, acc[g][3]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) red_s[warp][g][lane * 4 + u] = acc[g][u];
+    __syncthreads();
+    // ---- partial (max, sum, acc) -> scratch ----
+    float* part = scratch + static_cast<int64_t>(blockIdx.x) * (G * kHeadDim + 2 * G);
+    for (int e = tid; e < G * kHeadDim; e += kDecThreads) {
+        const int g = e / kHeadDim, d = e % kHeadDim;
+        part[e] = red_s[0][g][d] + red_s[1][g][d] + red_s[2][g][d] + red_s[3][g][d];
+    }
+    if (tid < G) {
+        part[G * kHeadDim + tid] = mx[tid];
+        part[G * kHeadDim + G + tid] = stat_s[1][0][tid] + stat_s[1][1][tid] + stat_s[1][2][tid] + stat_s[1][3][tid];
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kDecThreads) paged_decode_merge_kernel(TaskBatch b, int page_size, int chunks,
+                                                                        const float* __restrict__ scratch) {
+    const int64_t task = blockIdx.x;
+    if (task >= b.ntasks) return;
+    const int64_t* rec = b.rec + task * b.stride;
+    const int32_t L = min(reinterpret_cast<const int32_t*>(b.p[4].base)[rec[4]], b.p[3].cols * page_size);
+    __half* out = reinterpret_cast<__half*>(b.p[5].base) + rec[5];
+    const int64_t os3 = b.p[5].s3;
+    const int nch = L > 0 ? min(chunks, (L + kChunk - 1) / kChunk) : 0;
+    const int stride = G * kHeadDim + 2 * G;
+    const float* base = scratch + task * chunks * static_cast<int64_t>(stride);
+    for (int e = threadIdx.x; e < G * kHeadDim; e += kDecThreads) {
+        const int g = e / kHeadDim, d = e % kHeadDim;
+        float M = -INFINITY;
+        for (int c = 0; c < nch; ++c) M = fmaxf(M, base[c * stride + G * kHeadDim + g]);
+        float num = 0.f, den = 0.f;
+        for (int c = 0; c < nch; ++c) {
+            const float w = expf(base[c * stride + G * kHeadDim + g] - M);
+            num = fmaf(base[c * stride + e], w, num);
+            den = fmaf(base[c * stride + G * kHeadDim + G + g], w, den);
+        }
+        out[g * os3 + d] = __float2half_rn(nch > 0 ? num / den : 0.f);
+    }
+}
+
+int decode_chunks(const TaskBatch& b, int page_size) {
+    const int64_t max_tokens = static_cast<int64_t>(b.p[3].cols) * page_size;
+    return static_cast<int>(std::max<int64_t>(1, (max_tokens + kChunk - 1) / kChunk));
+}
+
+template <int G>
+cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cudaStream_t s) {
+    const int chunks = decode_chunks(b, page_size);
+    const int64_t grid = b.ntasks * chunks;
+    if (grid <= 0) return cudaSuccess;
+    if (grid > 0x7fffffff) return cudaErrorInvalidValue;
+    paged_decode_chunk_kernel<G><<<static_cast<unsigned>(grid), kDecThreads, 0, s>>>(b, page_size, chunks,
+                                                                                     static_cast<float*>(scratch));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    paged_decode_merge_kernel<G><<<static_cast<unsigned>(b.ntasks), kDecThreads, 0, s>>>(b, page_size, chunks,
+                                                                                         static_cast<const float*>(scratch));
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// top-k
+// ---------------------------------------------------------------------------
+
+constexpr int kTopkThreads = 1024;
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+    // Larger float -> larger unsigned key; -0.0 and +0.0 map to the same key.
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) == 0) u = 0;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) {
+    extern __shared__ uint32_t ks[];  // N keys, then 2K composite slots (u64)
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t sel_prefix, sel_remaining, n_gt, n_eq_taken;
+    const int64_t task = blockIdx.x;
+    if (task >= b.ntasks) return;
+    const int64_t* rec = b.rec + task * b.stride;
+    const ParamDesc& S = b.p[0];
+    const ParamDesc& O = b.p[1];
+    const int N = S.cols, K = O.cols;
+    int K2 = 1;
+    while (K2 < K) K2 <<= 1;
+    unsigned long long* comp = reinterpret_cast<unsigned long long*>(ks + ((N + 1) & ~1));
+    const float* src = reinterpret_cast<const float*>(S.base) + rec[0];
+    const int64_t ss = S.s4;
+    for (int i = threadIdx.x; i < N; i += kTopkThreads) ks[i] = order_key(src[i * ss]);
+    if (threadIdx.x == 0) {
+        sel_prefix = 0;
+        sel_remaining = K;
+    }
+    __syncthreads();
+    // radix select, 8 bits per pass, most significant first
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += kTopkThreads) hist[i] = 0;
+        __syncthreads();
+        const uint32_t prefix = sel_prefix;
+        const uint32_t hi_mask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
+        for (int i = threadIdx.x; i < N; i += kTopkThreads) {
+            const uint32_t k = ks[i];
+            if ((k & hi_mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xffu], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t rem = sel_remaining;
+            int digit = 255;
+            for (; digit > 0; --digit) {
+                if (hist[digit] >= rem) break;
+                rem -= hist[digit];
+            }
+            sel_prefix = prefix | (static_cast<uint32_t>(digit) << shift);
+            sel_remaining = rem;  // how many of the threshold-equal keys (so far) are still needed
+        }
+        __syncthreads();
+    }
+    const uint32_t thr = sel_prefix;      // the K-th largest key
+    const uint32_t need_eq = sel_remaining;  // how many keys equal to thr are taken (lowest indices first)
+    // gather: every key > thr, plus the first need_eq keys == thr in index order
+    if (threadIdx.x == 0) {
+        n_gt = 0;
+        n_eq_taken = 0;
+    }
+    for (int i = threadIdx.x; i < K2; i += kTopkThreads) comp[i] = 0ull;
+    __syncthreads();
+    for (int i = threadIdx.x; i < N; i += kTopkThreads) {
+        const uint32_t k = ks[i];
+        if (k > thr) {
+            const uint32_t slot = atomicAdd(&n_gt, 1u);
+            if (slot < static_cast<uint32_t>(K)) comp[slot] = (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+        }
+    }
+    __syncthreads();
+    const uint32_t gt = n_gt;
+    // equal keys: scan in index order chunk by chunk so the lowest indices win
+    for (int base = 0; base < N && n_eq_taken < need_eq; base += kTopkThreads) {
+        const int i = base + threadIdx.x;
+        const bool eq = i < N && ks[i] == thr;
+        const unsigned mask = __ballot_sync(0xffffffffu, eq);
+        __shared__ uint32_t warp_cnt[kTopkThreads / 32];
+        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+        if (lane == 0) warp_cnt[w] = __popc(mask);
+        __syncthreads();
+        uint32_t before = n_eq_taken;
+        for (int j = 0; j < w; ++j) before += warp_cnt[j];
+        before += __popc(mask & ((1u << lane) - 1u));
+        if (eq && before < need_eq) {
+            const uint32_t slot = gt + before;
+            if (slot < static_cast<uint32_t>(K)) comp[slot] = (static_cast<unsigned long long>(thr) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t tot = 0;
+            for (int j = 0; j < kTopkThreads / 32; ++j) tot += warp_cnt[j];
+            n_eq_taken += tot;
+        }
+        __syncthreads();
+    }
+    // bitonic sort of K2 composites, descending (key desc, then index asc via the inverted index)
+    for (int size = 2; size <= K2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < K2 / 2; i += kTopkThreads) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi = lo + stride;
+                const bool desc = ((lo & size) == 0);
+                const unsigned long long a = comp[lo], c = comp[hi];
+                if ((a < c) == desc) {
+                    comp[lo] = c;
+                    comp[hi] = a;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    int32_t* dst = reinterpret_cast<int32_t*>(O.base) + rec[1];
+    for (int i = threadIdx.x; i < K; i += kTopkThreads)
+        dst[i * O.s4] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(comp[i] & 0xffffffffull));
+}
+
+}  // namespace
+
+size_t paged_decode_scratch_bytes(const TaskBatch& b, int page_size) {
+    const int G = b.p[0].rows;
+    return static_cast<size_t>(b.ntasks) * decode_chunks(b, page_size) * (G * kHeadDim + 2 * G) * sizeof(float);
+}
+
+cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int, int, void* scratch, size_t scratch_bytes,
+                                cudaStream_t s) {
+    if (scratch_bytes < paged_decode_scratch_bytes(b, page_size)) return cudaErrorInvalidValue;
+    switch (b.p[0].rows) {
+        case 1: return launch_decode_g<1>(b, page_size, scratch, s);
+        case 2: return launch_decode_g<2>(b, page_size, scratch, s);
+        case 4: return launch_decode_g<4>(b, page_size, scratch, s);
+        case 8: return launch_decode_g<8>(b, page_size, scratch, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+size_t topk_select_scratch_bytes(const TaskBatch&) { return 0; }
+
+int topk_smem_bytes(int n, int k) {
+    int k2 = 1;
+    while (k2 < k) k2 <<= 1;
+    return ((n + 1) & ~1) * 4 + k2 * 8;
+}
+
+cudaError_t launch_topk_select(const TaskBatch& b, int, void*, size_t, cudaStream_t s) {
+    const int smem = topk_smem_bytes(b.p[0].cols, b.p[1].cols);
+    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    if (b.ntasks <= 0) return cudaSuccess;
+    topk_select_kernel<<<static_cast<unsigned>(b.ntasks), kTopkThreads, smem, s>>>(b);
+    return cudaGetLastError();
+}
+
+}  // namespace ptowsp::dev

@@ -110,6 +110,7 @@ cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int num_kv_he
                                 size_t scratch_bytes, cudaStream_t s);
 size_t paged_decode_scratch_bytes(const TaskBatch& b, int page_size);
 cudaError_t launch_indexer_score(const TaskBatch& b, int workers, cudaStream_t s);
+bool indexer_score_supported(const TaskBatch& b);
 cudaError_t launch_topk_select(const TaskBatch& b, int workers, void* scratch, size_t scratch_bytes, cudaStream_t s);
 size_t topk_select_scratch_bytes(const TaskBatch& b);
 

@@ -1,0 +1,318 @@
+// Built-in lightning-indexer scoring on tcgen05.
+//
+// One task = one batch element b:  scores[q, t] = sum_h w[q, h] * relu(q_{q,h} . k_t)
+// for Q = 8 queries x H = 64 index heads, D = 128, T keys (the score the
+// reference's toy top-k example takes as input, examples/deepseek_lightning_
+// indexer/golden.py; DeepSeek "lightning indexer").  The contraction is
+// Q*H x D x T per batch: 2*512*128 FLOP per 256-byte key row = 512 FLOP/B,
+// above the HBM ridge, so it runs on the tensor cores:
+//
+//   * the batch's 512 q rows stay resident in shared memory (128 KB, four
+//     128-byte-swizzled TMA boxes, K-major), loaded once per task;
+//   * key tiles of 128 rows stream through a 3-stage TMA ring (A operand,
+//     K-major straight from the row-major key matrix);
+//   * per key tile two tcgen05.mma groups (M = 128 keys, N = 256 = 4 queries x
+//     64 heads, K = 128 in 8 steps) fill two 256-column TMEM accumulators;
+//   * the epilogue warps read a key's 4 x 64 logits with tcgen05.ld, apply
+//     relu, reduce over heads with the per-query weights (sequential head
+//     order) and store 4 coalesced score rows -- while the MMA warp already
+//     fills the other accumulator.
+// Bounded waits and drains as in matmul_tcgen05.cu.  No cluster multicast.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "device.hpp"
+#include "tc_common.cuh"
+
+namespace ptowsp::dev {
+
+namespace {
+
+using namespace tc;
+
+constexpr int KT = 128;           // keys per tile (MMA M)
+constexpr int QH = 512;           // q rows per task (8 queries x 64 heads)
+constexpr int NH = 256;           // q rows per MMA (N)
+constexpr int HEADS = 64;
+constexpr int D = 128;
+constexpr int STAGES = 3;
+constexpr int THREADS = 192;
+constexpr int Q_BYTES = QH * D * 2;        // 128 KB
+constexpr int Q_BOX = NH * 64 * 2;         // 32 KB: 256 rows x 64 d
+constexpr int K_STAGE = KT * D * 2;        // 32 KB: two 16 KB boxes of 128 keys x 64 d
+constexpr int K_BOX = KT * 64 * 2;
+constexpr int BAR_OFF = Q_BYTES + STAGES * K_STAGE;
+constexpr int SMEM = BAR_OFF + 256 + 1024;
+constexpr int TMEM_COLS = 512;
+
+struct IdxArgs {
+    const int64_t* rec;
+    int64_t ntasks;
+    int stride;
+    int tiles;                   // key tiles per task
+    const float* w;              // weights base
+    int64_t w_s3;
+    float* s;                    // scores base
+    int64_t s_s3;
+    int queries;                 // 8
+    int* err;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    indexer_score_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                         IdxArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* qs = smem;
+    uint8_t* ks = smem + Q_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* tfull = bars + 2 * STAGES;
+    uint64_t* tempty = bars + 2 * STAGES + 2;
+    uint64_t* qfull = bars + 2 * STAGES + 4;
+    uint64_t* qempty = bars + 2 * STAGES + 5;
+    uint64_t* drain = bars + 2 * STAGES + 6;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 7);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&tfull[a]), 1);
+            mbar_init(smem_u32(&tempty[a]), 4 * 32);
+        }
+        mbar_init(smem_u32(qfull), 1);
+        mbar_init(smem_u32(qempty), 1);
+        mbar_init(smem_u32(drain), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_k)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int64_t U = args.ntasks * args.tiles;
+    const int64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0, issued_mask = 0, last_parity = 0;
+            int64_t cur = -1;
+            uint32_t nswitch = 0;
+            bool q_loaded = false;
+            for (int64_t u = u0; u < u1 && !*abort_flag; ++u) {
+                const int64_t task = u / args.tiles;
+                const int tile = static_cast<int>(u % args.tiles);
+                const int64_t* rec = args.rec + task * args.stride;
+                if (task != cur) {
+                    if (nswitch > 0 && !mbar_wait(smem_u32(qempty), (nswitch - 1) & 1u, abort_flag, args.err)) break;
+                    const uint32_t qb = smem_u32(qfull);
+                    mbar_expect_tx(qb, Q_BYTES);
+                    const int32_t qrow = static_cast<int32_t>(rec[0] / D);
+#pragma unroll
+                    for (int hq = 0; hq < 2; ++hq)
+#pragma unroll
+                        for (int dh = 0; dh < 2; ++dh)
+                            tma_load_2d(smem_u32(qs + (hq * 2 + dh) * Q_BOX), &tmap_q, dh * 64, qrow + hq * NH, qb);
+                    q_loaded = true;
+                    ++nswitch;
+                    cur = task;
+                }
+                if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, args.err)) break;
+                const uint32_t fb = smem_u32(&full[stage]);
+                mbar_expect_tx(fb, K_STAGE);
+                const int32_t krow = static_cast<int32_t>(rec[1] / D) + tile * KT;
+#pragma unroll
+                for (int dh = 0; dh < 2; ++dh)
+                    tma_load_2d(smem_u32(ks + stage * K_STAGE + dh * K_BOX), &tmap_k, dh * 64, krow, fb);
+                issued_mask |= 1u << stage;
+                last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            // drain the copies this CTA issued
+            const uint64_t start = globaltimer();
+            for (int s = 0; s < STAGES; ++s)
+                if (issued_mask & (1u << s))
+                    while (!mbar_try_wait(smem_u32(&full[s]), (last_parity >> s) & 1u))
+                        if (globaltimer() - start > kTimeoutNs) {
+                            atomicOr(args.err, kErrTimeout);
+                            break;
+                        }
+            if (q_loaded)
+                while (!mbar_try_wait(smem_u32(qfull), (nswitch - 1) & 1u))
+                    if (globaltimer() - start > kTimeoutNs) {
+                        atomicOr(args.err, kErrTimeout);
+                        break;
+                    }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(KT, NH, 0);
+            int stage = 0, slot = 0;
+            uint32_t phase = 0, slot_phase = 0;
+            int64_t cur = -1;
+            uint32_t nswitch = 0;
+            bool issued = false;
+            for (int64_t u = u0; u < u1 && !*abort_flag; ++u) {
+                const int64_t task = u / args.tiles;
+                if (task != cur) {
+                    if (!mbar_wait(smem_u32(qfull), nswitch & 1u, abort_flag, args.err)) break;
+                    ++nswitch;
+                    cur = task;
+                }
+                if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, args.err)) break;
+                tc_fence_after();
+                const uint32_t ka = smem_u32(ks + stage * K_STAGE);
+                bool ok = true;
+                for (int hq = 0; hq < 2; ++hq) {
+                    if (!mbar_wait(smem_u32(&tempty[slot]), slot_phase ^ 1u, abort_flag, args.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * NH);
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        const uint64_t ad = smem_desc(ka + (kk >> 2) * K_BOX + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = smem_desc(smem_u32(qs + (hq * 2 + (kk >> 2)) * Q_BOX) + (kk & 3) * 32, 16, 1024);
+                        mma_f16(d_tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(smem_u32(&tfull[slot]));
+                    issued = true;
+                    if (++slot == 2) {
+                        slot = 0;
+                        slot_phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(smem_u32(&empty[stage]));
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+                if (u + 1 == u1 || (u + 1) / args.tiles != task) mma_commit(smem_u32(qempty));
+            }
+            if (issued) {
+                mma_commit(smem_u32(drain));
+                const uint64_t start = globaltimer();
+                while (!mbar_try_wait(smem_u32(drain), 0))
+                    if (globaltimer() - start > kTimeoutNs) {
+                        atomicOr(args.err, kErrTimeout);
+                        break;
+                    }
+            }
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        int slot = 0;
+        uint32_t slot_phase = 0;
+        for (int64_t u = u0; u < u1 && !*abort_flag; ++u) {
+            const int64_t task = u / args.tiles;
+            const int tile = static_cast<int>(u % args.tiles);
+            const int64_t* rec = args.rec + task * args.stride;
+            const float* w = args.w + rec[2];
+            float* s = args.s + rec[3] + static_cast<int64_t>(tile) * KT + row;
+            bool ok = true;
+            for (int hq = 0; hq < 2; ++hq) {
+                if (!mbar_wait(smem_u32(&tfull[slot]), slot_phase, abort_flag, args.err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int ql = 0; ql < 4; ++ql) {
+                    const int q = hq * 4 + ql;
+                    const float* wq = w + q * args.w_s3;
+                    float acc = 0.f;
+#pragma unroll 1
+                    for (int hc = 0; hc < 2; ++hc) {
+                        float v[32];
+                        tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                      static_cast<uint32_t>(slot * NH + ql * HEADS + hc * 32),
+                                  v);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) acc = fmaf(__ldg(wq + hc * 32 + j), fmaxf(v[j], 0.f), acc);
+                    }
+                    s[q * args.s_s3] = acc;
+                }
+                tc_fence_before();
+                mbar_arrive(smem_u32(&tempty[slot]));
+                if (++slot == 2) {
+                    slot = 0;
+                    slot_phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+}
+
+}  // namespace
+
+bool indexer_score_supported(const TaskBatch& b) {
+    const ParamDesc& Q = b.p[0];
+    const ParamDesc& K = b.p[1];
+    const ParamDesc& W = b.p[2];
+    const ParamDesc& S = b.p[3];
+    if (Q.rows != QH || Q.cols != D || K.cols != D || K.rows % KT || W.rows != 8 || W.cols != HEADS) return false;
+    if (S.rows != 8 || S.cols != K.rows) return false;
+    if (Q.s3 != D || K.s3 != D || Q.s4 != 1 || K.s4 != 1 || W.s4 != 1 || S.s4 != 1) return false;
+    if ((reinterpret_cast<uintptr_t>(Q.base) | reinterpret_cast<uintptr_t>(K.base)) & 15) return false;
+    return true;
+}
+
+cudaError_t launch_indexer_score(const TaskBatch& b, int workers, cudaStream_t s) {
+    if (!indexer_score_supported(b)) return cudaErrorInvalidValue;
+    const ParamDesc& Q = b.p[0];
+    const ParamDesc& K = b.p[1];
+    CUtensorMap mq, mk;
+    if (!make_map_f16(&mq, Q.base, D, (Q.numel_span + D - 1) / D, 64, NH)) return cudaErrorInvalidValue;
+    if (!make_map_f16(&mk, K.base, D, (K.numel_span + D - 1) / D, 64, KT)) return cudaErrorInvalidValue;
+    IdxArgs a;
+    a.rec = b.rec;
+    a.ntasks = b.ntasks;
+    a.stride = b.stride;
+    a.tiles = K.rows / KT;
+    a.w = reinterpret_cast<const float*>(b.p[2].base);
+    a.w_s3 = b.p[2].s3;
+    a.s = reinterpret_cast<float*>(b.p[3].base);
+    a.s_s3 = b.p[3].s3;
+    a.queries = 8;
+    a.err = b.err;
+    cudaError_t e = cudaFuncSetAttribute(indexer_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    const int64_t units = b.ntasks * a.tiles;
+    int64_t grid = std::min<int64_t>(units, sm_count());
+    if (workers > 0) grid = std::min<int64_t>(grid, workers);
+    grid = std::max<int64_t>(grid, 1);
+    indexer_score_kernel<<<static_cast<unsigned>(grid), THREADS, SMEM, s>>>(mq, mk, a);
+    return cudaGetLastError();
+}
+
+}  // namespace ptowsp::dev

@@ -635,12 +635,31 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
             e = dev::launch_tile_program(tb, ki.tp_dev, ki.tp_smem, workers, P.stream);
             break;
         case ImplKind::PagedDecode: {
+            const dev::ParamDesc &K = tb.p[1], &V = tb.p[2];
+            const bool aligned = K.s3 % 8 == 0 && K.s4 % 8 == 0 && V.s3 % 4 == 0 && V.s4 % 4 == 0 &&
+                                 ((reinterpret_cast<uintptr_t>(K.base) & 15) | (reinterpret_cast<uintptr_t>(V.base) & 7)) == 0;
+            if (!aligned)
+                throw Error(PTOWSP_ERR_UNSUPPORTED, "paged_decode_gqa: KV cache rows must be 16-byte aligned");
             size_t sb = dev::paged_decode_scratch_bytes(tb, 16);
             void* s = ensure_scratch(P, sb);
             e = dev::launch_paged_decode(tb, 16, 0, workers, s, sb, P.stream);
             break;
         }
-        case ImplKind::IndexerScore: e = dev::launch_indexer_score(tb, workers, P.stream); break;
+        case ImplKind::IndexerScore: {
+            if (B.fast_ok < 0) {
+                bool ok = dev::indexer_score_supported(tb) && !B.rec.empty();
+                for (int64_t t = 0; ok && t < B.ntasks; ++t) {
+                    const int64_t* r = &B.rec[t * B.stride];
+                    ok = r[0] % 128 == 0 && r[1] % 128 == 0 && r[0] + 512 * 128 <= tb.p[0].numel_span &&
+                         r[1] + tb.p[1].rows * 128 <= tb.p[1].numel_span;
+                }
+                B.fast_ok = ok ? 1 : 0;
+            }
+            if (!B.fast_ok)
+                throw Error(PTOWSP_ERR_UNSUPPORTED, "lightning_indexer_score: q/k views must be dense [rows,128] f16 tiles");
+            e = dev::launch_indexer_score(tb, workers, P.stream);
+            break;
+        }
         case ImplKind::TopK: {
             size_t sb = dev::topk_select_scratch_bytes(tb);
             void* s = ensure_scratch(P, sb);

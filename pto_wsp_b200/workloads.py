@@ -377,3 +377,55 @@ def bgemm_views(a, b, c, tile_m: int = 128, tile_n: int = 128):
         bv = b.reshape(Bn, K, N // tile_n, tile_n).transpose(0, 2, 1, 3)
         cv = c.reshape(Bn, M // tile_m, tile_m, N // tile_n, tile_n).transpose(0, 1, 3, 2, 4)
     return av, bv, cv
+
+
+def topk_plan(rows: int, n: int, k: int, name: str = "topk_rows") -> dict:
+    """Top-k rows alone: ``for b in P(rows): topk[b](scores=S[b], out=I[b])`` (S [rows,1,n], I [rows,1,k])."""
+    kt = KernelBuilder("topk")
+    kt.param("scores", "f32", 1, n)
+    kt.param("out", "i32", 1, k)
+    kt.attrs = {"cpp_src": TOPK_CPU_BODY}
+    v0 = _VAR_NAMES[0]
+    body = _pfor(v0, rows, _task("topk", [v0], [_targ("scores", 0, 3, [v0]), _targ("out", 1, 3, [v0])]))
+    return _plan(name, [("f32", [rows, 1, n]), ("i32", [rows, 1, k])], [kt.build()], body, _schedule())
+
+
+# ---------------------------------------------------------------------------
+# Seeded synthetic inputs (BASELINE.json distributions)
+# ---------------------------------------------------------------------------
+
+
+def decode_inputs(rng, requests: int, kv_heads: int = 8, group: int = 4, head_dim: int = 128, page_size: int = 16,
+                  lengths=None, lo: int = 512, hi: int = 8192, max_pages: int | None = None):
+    """Q/K/V ~ N(0,1) f16, KV lengths ~ U{lo..hi}, pages = one random permutation of all pages."""
+    import numpy as np
+
+    lens = np.asarray(lengths if lengths is not None else rng.integers(lo, hi + 1, size=requests), dtype=np.int64)
+    npages = (lens + page_size - 1) // page_size
+    maxp = int(max_pages if max_pages is not None else max(1, int(npages.max(initial=1))))
+    total = int(npages.sum())
+    perm = rng.permutation(max(total, 1)).astype(np.int32)
+    pt = np.zeros((requests, maxp), dtype=np.int32)
+    off = 0
+    for r in range(requests):
+        pt[r, : npages[r]] = perm[off: off + npages[r]]
+        off += int(npages[r])
+    q = rng.standard_normal((requests, kv_heads, group, head_dim), dtype=np.float32).astype(np.float16)
+    kc = rng.standard_normal((max(total, 1), page_size, kv_heads, head_dim), dtype=np.float32).astype(np.float16)
+    vc = rng.standard_normal((max(total, 1), page_size, kv_heads, head_dim), dtype=np.float32).astype(np.float16)
+    kl = lens.astype(np.int32).reshape(requests, 1)
+    out = np.zeros((requests, kv_heads, group, head_dim), dtype=np.float16)
+    plan = decode_plan(requests, kv_heads, group, head_dim, max(total, 1), maxp, page_size)
+    return plan, [q, kc, vc, pt, kl, out]
+
+
+def indexer_inputs(rng, batch: int, context: int, topk: int, queries: int = 8, heads: int = 64, head_dim: int = 128):
+    """q, k ~ N(0,1) f16; w ~ U(0,1) f32."""
+    import numpy as np
+
+    q = rng.standard_normal((batch, queries * heads, head_dim), dtype=np.float32).astype(np.float16)
+    k = rng.standard_normal((batch, context, head_dim), dtype=np.float32).astype(np.float16)
+    w = rng.uniform(0, 1, (batch, queries, heads)).astype(np.float32)
+    s = np.zeros((batch, queries, context), np.float32)
+    idx = np.zeros((batch, queries, topk), np.int32)
+    return indexer_plan(batch, queries, heads, head_dim, context, topk), [q, k, w, s, idx]
