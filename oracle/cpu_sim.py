@@ -643,7 +643,10 @@ def builtin_run(name: str, km: KernelModel, views: list[TaskView], axis_args: li
         page_size, kvh = int(scalars[0]), int(scalars[1])
         h = int(axis_args[1])
         L = int(len_p[1].ref.flat(len_p[1].off, 1)[0])
-        cycles = G * D + 2 * L * D + G * D * L + 5 * G * L + 2 * G + G * L * D + G * D
+        L = min(L, pt_p[0]["cols"] * page_size)
+        # model charge: shape-static, with the page-table capacity as the length
+        Ls = pt_p[0]["cols"] * page_size
+        cycles = G * D + 2 * Ls * D + G * D * Ls + 5 * G * Ls + 2 * G + G * Ls * D + G * D
         if not execute or L <= 0:
             if execute and L <= 0:
                 o_p[1].ref.tile(o_p[1].off, G, D, o_p[1].s3, o_p[1].s4)[...] = 0

@@ -125,3 +125,35 @@ def test_dry_run_inout_chain_waves():
     ex.run_with_symbols(arrays, axis, syms, sptr)
     t = ex.timing()
     assert t["tasks"] == 64 and t["waves"] == 4
+
+
+@pytest.mark.parametrize("name", ["rmsnorm", "softmax", "bgemm", "decode", "indexer", "topk"])
+def test_native_cycles_match_oracle_for_config_plans(name):
+    """Dry-run makespan of the native runtime == the oracle's, for every config workload form."""
+    import numpy as np
+    from cpu_sim import CpuSim
+
+    rng = np.random.default_rng(0)
+    axis = {}
+    if name == "rmsnorm":
+        plan = workloads.rmsnorm_plan(2, 3)
+        arrays = [np.zeros((2, 3, 16, 128), np.float32) for _ in range(2)]
+    elif name == "softmax":
+        plan = workloads.softmax_plan(2, 3)
+        arrays = [np.zeros((2, 3, 32, 256), np.float32) for _ in range(2)]
+    elif name == "bgemm":
+        plan = workloads.bgemm_plan(1, 256, 256, 128)
+        a, b, c = np.zeros((1, 256, 128), np.float16), np.zeros((1, 128, 256), np.float16), np.zeros((1, 256, 256), np.float32)
+        arrays = list(workloads.bgemm_views(a, b, c))
+    elif name == "decode":
+        plan, arrays = workloads.decode_inputs(rng, 3, lengths=[5, 40, 0])
+        axis = {"b": 3}
+    elif name == "indexer":
+        plan, arrays = workloads.indexer_inputs(rng, 1, 256, 16)
+    else:
+        plan = workloads.topk_plan(3, 256, 16)
+        arrays = [np.zeros((3, 1, 256), np.float32), np.zeros((3, 1, 16), np.int32)]
+    want = CpuSim(plan).run([x.copy() for x in arrays], axis_sizes=axis, execute=False)
+    ex = runtime.CudaExecutable(plan)
+    ex.set_option("dry_run", 1)
+    assert ex.run_with_symbols(arrays, axis, {}, {}) == want
