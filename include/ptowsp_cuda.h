@@ -156,6 +156,43 @@ PTOWSP_API const char* ptowsp_cuda_describe(ptowsp_program* prog);
 
 PTOWSP_API void ptowsp_cuda_destroy(ptowsp_program* prog);
 
+/* ------------------------------------------------------------------------- */
+/* Paged GQA decode that allocates no device memory.  No counterpart in the    */
+/* reference (whose CPU-sim allocates nothing on a device); added for callers  */
+/* that must not let a library call cudaMalloc/cudaFree during a call: serving */
+/* engines that reserve all device memory up front for their own KV-cache pool */
+/* (an extra allocation can fail or eat into that pool), and hosts running     */
+/* other streams that cannot take the implicit synchronisation those calls can */
+/* cause.  The scratch space (task records, split-KV partials, status word)    */
+/* lives in one fixed 24 MiB array owned by this library in device memory;     */
+/* every GPU that loads the library holds it until the process exits.          */
+/*                                                                             */
+/* All pointers are device memory on the calling thread's current device:     */
+/*   q          f16 [num_requests][num_kv_heads][group][head_dim]              */
+/*   k_cache,   f16 [num_pages][page_size][num_kv_heads][head_dim]             */
+/*   v_cache                                                                   */
+/*   page_table i32 [num_requests][max_pages]   (page ids of each request)     */
+/*   kv_len     i32 [num_requests]              (tokens of each request)       */
+/*   out        f16 [num_requests][num_kv_heads][group][head_dim]              */
+/* head_dim must be 128 and group 1, 2, 4 or 8.  Same math as the             */
+/* paged_decode_gqa built-in.  Blocks until the work on `stream` (NULL = the  */
+/* default stream) has finished and returns a ptowsp_status:                   */
+/* PTOWSP_ERR_LIMIT when the work needs more than the fixed array              */
+/* (ptowsp_cuda_noalloc_scratch_bytes tells how much it needs),                */
+/* PTOWSP_ERR_DEVICE for a page id outside the cache or a length beyond the   */
+/* page table.  Calls share the array: two calls that overlap on the GPU race. */
+/* The first call on a device looks up the array's address; make it before    */
+/* any stream capture.                                                         */
+PTOWSP_API int ptowsp_cuda_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                                const int32_t* page_table, const int32_t* kv_len, void* out,
+                                                int num_requests, int num_kv_heads, int group, int head_dim,
+                                                int page_size, int max_pages, int64_t num_pages, void* stream);
+
+/* Bytes of the fixed array a ptowsp_cuda_paged_decode_noalloc call with these
+ * sizes needs; with num_requests <= 0 and num_kv_heads <= 0, the array's size. */
+PTOWSP_API size_t ptowsp_cuda_noalloc_scratch_bytes(int num_requests, int num_kv_heads, int group, int max_pages,
+                                                    int page_size);
+
 /* Number of CUDA devices visible to this library (0 without a GPU). */
 PTOWSP_API int ptowsp_cuda_device_count(void);
 

@@ -114,6 +114,23 @@ const char* ptowsp_cuda_describe(ptowsp_program* prog) {
 
 void ptowsp_cuda_destroy(ptowsp_program* prog) { delete prog; }
 
+int ptowsp_cuda_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                      const int32_t* page_table, const int32_t* kv_len, void* out, int num_requests,
+                                      int num_kv_heads, int group, int head_dim, int page_size, int max_pages,
+                                      int64_t num_pages, void* stream) {
+    const char* msg = "";
+    const int rc = ptowsp::dev::paged_decode_noalloc(q, k_cache, v_cache, page_table, kv_len, out, num_requests,
+                                                     num_kv_heads, group, head_dim, page_size, max_pages, num_pages,
+                                                     static_cast<cudaStream_t>(stream), &msg);
+    ptowsp::set_error(msg);
+    return rc;
+}
+
+size_t ptowsp_cuda_noalloc_scratch_bytes(int num_requests, int num_kv_heads, int group, int max_pages, int page_size) {
+    if (num_requests <= 0 && num_kv_heads <= 0) return ptowsp::dev::noalloc_scratch_capacity();
+    return ptowsp::dev::noalloc_bytes_needed(num_requests, num_kv_heads, group, max_pages, page_size);
+}
+
 int ptowsp_cuda_device_count(void) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) {

@@ -25,6 +25,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "device.hpp"
 
@@ -411,6 +412,198 @@ cudaError_t launch_topk_select(const TaskBatch& b, int, void*, size_t, cudaStrea
     if (b.ntasks <= 0) return cudaSuccess;
     topk_select_kernel<<<static_cast<unsigned>(b.ntasks), kTopkThreads, smem, s>>>(b);
     return cudaGetLastError();
+}
+
+}  // namespace ptowsp::dev
+
+namespace ptowsp::dev {
+
+// ===========================================================================
+// Paged GQA decode without any device allocation.
+//
+// Some callers cannot let a library call cudaMalloc on their hot path: a
+// serving engine that reserved all device memory up front for its own KV-cache
+// pool (an extra allocation can fail, or carve memory out of that pool), or a
+// host that runs other streams concurrently and cannot afford the implicit
+// device-wide synchronisation cudaMalloc/cudaFree can cause.  For them this
+// entry point keeps its scratch (task records, split-KV partial results and
+// the status word) in one fixed array in device memory that belongs to this
+// library, instead of the program's grown-on-demand buffer.
+//
+// Costs and rules, in the caller's terms:
+//  * the array is kPtowspNoAllocScratchBytes (24 MiB) and every GPU that loads
+//    this library keeps it until the process exits;
+//  * a workload that needs more (records + partials, see
+//    ptowsp_noalloc_bytes_needed) is rejected with PTOWSP_ERR_LIMIT;
+//  * all calls share the one array and it keeps whatever the last call left:
+//    the call clears the status word itself, and everything else it reads it
+//    writes first -- but two calls whose work overlaps on the GPU (different
+//    streams, or different host threads) race on the array;
+//  * the first call on a device looks up the array's device address (with that
+//    device current); make that first call before any stream capture.
+// ===========================================================================
+
+namespace {
+
+constexpr size_t kPtowspNoAllocScratchBytes = size_t(24) << 20;
+constexpr int kNoAllocRecStride = 10;  // 6 view offsets, 2 axis args, 2 scalar args
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kPtowspNoAllocScratchBytes];
+
+// Layout inside the array: [status word | 252 B pad | task records | partials].
+constexpr size_t kNoAllocRecOffset = 256;
+
+__global__ void noalloc_fill_records(int64_t* rec, int requests, int kv_heads, int group, int head_dim, int max_pages,
+                                     int page_size) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= static_cast<int64_t>(requests) * kv_heads) return;
+    const int64_t r = t / kv_heads, h = t % kv_heads;
+    int64_t* o = rec + t * kNoAllocRecStride;
+    o[0] = t * group * head_dim;  // q[r][h]
+    o[1] = 0;                     // k cache (whole pool)
+    o[2] = 0;                     // v cache (whole pool)
+    o[3] = r * max_pages;         // page_table[r]
+    o[4] = r;                     // kv_len[r]
+    o[5] = t * group * head_dim;  // out[r][h]
+    o[6] = r;
+    o[7] = h;
+    o[8] = page_size;
+    o[9] = kv_heads;
+}
+
+void* noalloc_scratch_address(int device, cudaError_t* err) {
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    if (device < 0 || device >= 64) {
+        *err = cudaErrorInvalidDevice;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[device]) {
+        void* p = nullptr;
+        *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // device `device` is current here
+        if (*err != cudaSuccess) return nullptr;
+        addr[device] = p;
+    }
+    *err = cudaSuccess;
+    return addr[device];
+}
+
+}  // namespace
+
+size_t noalloc_scratch_capacity() { return kPtowspNoAllocScratchBytes; }
+
+size_t noalloc_bytes_needed(int requests, int kv_heads, int group, int max_pages, int page_size) {
+    const size_t tasks = static_cast<size_t>(requests) * kv_heads;
+    const int64_t max_tokens = static_cast<int64_t>(max_pages) * page_size;
+    const size_t chunks = static_cast<size_t>(std::max<int64_t>(1, (max_tokens + kChunk - 1) / kChunk));
+    return kNoAllocRecOffset + tasks * kNoAllocRecStride * sizeof(int64_t) +
+           tasks * chunks * (static_cast<size_t>(group) * kHeadDim + 2 * group) * sizeof(float);
+}
+
+// Returns a ptowsp_status code; *msg names the failure.
+int paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* page_table,
+                         const int32_t* kv_len, void* out, int requests, int kv_heads, int group, int head_dim,
+                         int page_size, int max_pages, int64_t num_pages, cudaStream_t s, const char** msg) {
+    *msg = "";
+    if (!q || !k_cache || !v_cache || !page_table || !kv_len || !out) {
+        *msg = "paged_decode_noalloc: null pointer";
+        return 4;
+    }
+    if (requests <= 0 || kv_heads <= 0 || page_size <= 0 || max_pages <= 0 || num_pages <= 0) {
+        *msg = "paged_decode_noalloc: sizes must be positive";
+        return 4;
+    }
+    if (head_dim != kHeadDim || !(group == 1 || group == 2 || group == 4 || group == 8)) {
+        *msg = "paged_decode_noalloc: head_dim must be 128 and the GQA group 1, 2, 4 or 8";
+        return 2;
+    }
+    const size_t need = noalloc_bytes_needed(requests, kv_heads, group, max_pages, page_size);
+    if (need > kPtowspNoAllocScratchBytes) {
+        *msg = "paged_decode_noalloc: requests x kv_heads x ceil(max_pages*page_size/512) x (group*128+2*group)*4 B "
+               "of partials plus task records exceed the fixed 24 MiB scratch array";
+        return 6;
+    }
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) {
+        *msg = cudaGetErrorString(e);
+        return 3;
+    }
+    char* base = static_cast<char*>(noalloc_scratch_address(device, &e));
+    if (!base) {
+        *msg = cudaGetErrorString(e);
+        return 3;
+    }
+    int* status = reinterpret_cast<int*>(base);
+    int64_t* rec = reinterpret_cast<int64_t*>(base + kNoAllocRecOffset);
+    const size_t tasks = static_cast<size_t>(requests) * kv_heads;
+    float* partials = reinterpret_cast<float*>(base + kNoAllocRecOffset + tasks * kNoAllocRecStride * sizeof(int64_t));
+
+    e = cudaMemsetAsync(status, 0, sizeof(int), s);  // the status word must start at zero
+    if (e == cudaSuccess) {
+        noalloc_fill_records<<<static_cast<unsigned>((tasks + 127) / 128), 128, 0, s>>>(rec, requests, kv_heads, group,
+                                                                                        kHeadDim, max_pages, page_size);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) {
+        *msg = cudaGetErrorString(e);
+        return 3;
+    }
+    TaskBatch b{};
+    b.rec = rec;
+    b.ntasks = static_cast<int64_t>(tasks);
+    b.stride = kNoAllocRecStride;
+    b.nparams = 6;
+    b.naxis = 2;
+    b.nscalar = 2;
+    b.err = status;
+    const int64_t cache_span = num_pages * page_size * kv_heads * static_cast<int64_t>(kHeadDim);
+    auto param = [](void* p, int64_t s3, int64_t s4, int64_t span, int rows, int cols, int type, int eb) {
+        ParamDesc d{};
+        d.base = static_cast<char*>(p);
+        d.s3 = s3;
+        d.s4 = s4;
+        d.numel_span = span;
+        d.rows = rows;
+        d.cols = cols;
+        d.type = type;
+        d.elem_bytes = eb;
+        return d;
+    };
+    const int64_t qspan = static_cast<int64_t>(tasks) * group * kHeadDim;
+    b.p[0] = param(const_cast<void*>(q), kHeadDim, 1, qspan, group, kHeadDim, PT_F16, 2);
+    b.p[1] = param(const_cast<void*>(k_cache), static_cast<int64_t>(page_size) * kv_heads * kHeadDim,
+                   static_cast<int64_t>(kv_heads) * kHeadDim, cache_span, page_size, kv_heads * kHeadDim, PT_F16, 2);
+    b.p[2] = param(const_cast<void*>(v_cache), static_cast<int64_t>(page_size) * kv_heads * kHeadDim,
+                   static_cast<int64_t>(kv_heads) * kHeadDim, cache_span, page_size, kv_heads * kHeadDim, PT_F16, 2);
+    b.p[3] = param(const_cast<int32_t*>(page_table), 0, 1, static_cast<int64_t>(requests) * max_pages, 1, max_pages,
+                   PT_I32, 4);
+    b.p[4] = param(const_cast<int32_t*>(kv_len), 0, 1, requests, 1, 1, PT_I32, 4);
+    b.p[5] = param(out, kHeadDim, 1, qspan, group, kHeadDim, PT_F16, 2);
+    switch (group) {
+        case 1: e = launch_decode_g<1>(b, page_size, partials, s); break;
+        case 2: e = launch_decode_g<2>(b, page_size, partials, s); break;
+        case 4: e = launch_decode_g<4>(b, page_size, partials, s); break;
+        default: e = launch_decode_g<8>(b, page_size, partials, s); break;
+    }
+    if (e != cudaSuccess) {
+        *msg = cudaGetErrorString(e);
+        return 3;
+    }
+    int host_status = 0;
+    e = cudaMemcpyAsync(&host_status, status, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        *msg = cudaGetErrorString(e);
+        return 3;
+    }
+    if (host_status) {
+        *msg = (host_status & kErrBounds) ? "paged_decode_noalloc: a page id is outside the KV cache"
+                                          : "paged_decode_noalloc: kv_len exceeds max_pages * page_size";
+        return 5;
+    }
+    return 0;
 }
 
 }  // namespace ptowsp::dev

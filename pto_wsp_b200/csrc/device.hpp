@@ -116,4 +116,12 @@ size_t topk_select_scratch_bytes(const TaskBatch& b);
 
 int sm_count();
 
+// Allocation-free paged decode over a fixed device array (decode.cu); returns a
+// ptowsp_status code and sets *msg.
+int paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* page_table,
+                         const int32_t* kv_len, void* out, int requests, int kv_heads, int group, int head_dim,
+                         int page_size, int max_pages, int64_t num_pages, cudaStream_t s, const char** msg);
+size_t noalloc_scratch_capacity();
+size_t noalloc_bytes_needed(int requests, int kv_heads, int group, int max_pages, int page_size);
+
 }  // namespace ptowsp::dev
