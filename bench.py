@@ -45,6 +45,10 @@ WORKLOADS = {
                 "tiles": 4096, "rows": 16, "cols": 128},
     "bgemm": {"config": "config 3: bgemm 64 x (2048x2048x2048), f16 in, f32 acc/out, 128x128 output tiles",
               "batch": 64, "m": 2048, "n": 2048, "k": 2048},
+    "decode": {"config": "config 4: paged GQA decode, 64 requests, 32 q / 8 kv heads, d=128, f16, page 16, "
+                         "KV len U[512,8192]", "batch": 64},
+    "indexer": {"config": "config 5: lightning indexer 16 batches x 8 queries, 64 heads, d=128, 32768 keys, "
+                          "top-2048", "batch": 16, "context": 32768, "topk": 2048},
 }
 
 
@@ -390,6 +394,183 @@ def run_bgemm(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+def _dist_setup(world: int, local_rank: int):
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    return torch, dev, dist
+
+
+def run_builtin(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
+    """Configs 4 (paged decode, GB/s) and 5 (indexer scoring + top-k, TFLOP/s of the scoring)."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from cpu_sim import CpuSim
+
+        from pto_wsp_b200 import workloads
+
+        rng = np.random.default_rng(0)
+        if args.workload == "decode":
+            plan, arrays = workloads.decode_inputs(rng, 4)  # bounded sample: 4 requests x 8 kv heads per step
+            unit_bytes = int(arrays[4].astype(np.int64).sum()) * 8 * 128 * 2 * 2
+            work, unit = unit_bytes, "GB/s"
+            axis = {"b": 4}
+        else:
+            plan, arrays = workloads.indexer_inputs(rng, 1, wl["context"], wl["topk"])
+            work, unit = 2.0 * 512 * 128 * wl["context"], "TFLOP/s"
+            axis = {}
+        sim = CpuSim(plan)
+        for _ in range(min(args.warmup, 1)):
+            sim.run([a.copy() for a in arrays], axis_sizes=axis)
+        steps = max(1, min(args.steps, 5))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            sim.run([a.copy() for a in arrays], axis_sizes=axis)
+        dt = time.perf_counter() - t0
+        v = work * steps / dt / (1e9 if unit == "GB/s" else 1e12)
+        sample = ("4 requests x 8 kv heads per step" if args.workload == "decode" else "1 batch element per step")
+        print(json.dumps({
+            "impl": "reference", "metric": f"{args.workload} task-loop throughput", "value": round(v, 5), "unit": unit,
+            "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": round(dt / steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32",
+            "data": "synthetic (seeded numpy)", "config": {"workload": wl["config"], "sample_per_step": sample},
+            "cpu_baseline": {"value": round(v, 5), "unit": unit, "cores": 1, "kind": "port",
+                             "sample": sample + "; numpy restatement of the CPU-sim task (oracle/cpu_sim.py)"},
+            "e2e": {"value": round(v, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
+
+    torch, dev, dist = _dist_setup(world, local_rank)
+    from pto_wsp_b200 import workloads
+    from pto_wsp_b200.runtime import CudaExecutable
+
+    rng = np.random.default_rng(3000 + rank)
+    if args.workload == "decode":
+        R = wl["batch"]
+        plan, host = workloads.decode_inputs(rng, R)
+        lens = host[4].astype(np.int64).reshape(-1)
+        work = float(lens.sum() * 8 * 128 * 2 * 2 + R * 32 * 128 * 2 * 2)  # K+V of every token + Q + O
+        unit, scale, kname, bound = "GB/s", 1e9, "paged_decode_chunk", "hbm"
+        axis = {"b": R}
+    else:
+        B, T, K = wl["batch"], wl["context"], wl["topk"]
+        plan, host = workloads.indexer_inputs(rng, B, T, K)
+        work = 2.0 * B * 512 * 128 * T
+        unit, scale, kname, bound = "TFLOP/s", 1e12, "indexer_score", "tensor"
+        axis = {}
+    ex = CudaExecutable(plan, device=local_rank)
+    stream = torch.cuda.current_stream(dev)
+    ex.set_stream(stream)
+    ex.set_option("sync", 0)
+    darr = [torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in host]
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        ex.run_with_symbols(darr, axis, {}, {})
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    with ClockSampler(gpu_index(local_rank)) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            ex.run_with_symbols(darr, axis, {}, {})
+            launches += int(ex.timing()["launches"])
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        ms_max = max_over_ranks(ms)
+        ex.set_option("sync", 1)
+        pinned = []
+        for a in host:
+            t = torch.empty(a.shape, dtype=torch.from_numpy(a[:0].copy()).dtype, pin_memory=True)
+            t.copy_(torch.from_numpy(np.ascontiguousarray(a)))
+            pinned.append(t.numpy())
+        ex.run_with_symbols(pinned, axis, {}, {})
+        e2e_steps = args.e2e_steps or min(args.steps, 10)
+        barrier()
+        t0 = time.perf_counter()
+        h2d = d2h = 0
+        for _ in range(e2e_steps):
+            ex.run_with_symbols(pinned, axis, {}, {})
+            tm = ex.timing()
+            h2d += tm["h2d_bytes"]
+            d2h += tm["d2h_bytes"]
+        barrier()
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+    clocks = clk.summary()
+    value = world * work * args.steps / (ms_max / 1e3) / scale
+    e2e = world * work * e2e_steps / e2e_s / scale
+    peak, peak_kind = peaks("hbm_gbs" if bound == "hbm" else "bf16_tflops")
+    achieved = work / (ms / args.steps / 1e3) / scale
+    if rank == 0:
+        line = {
+            "metric": f"{args.workload} task-loop throughput", "value": round(value, 3), "unit": unit,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 softmax|acc",
+            "data": "synthetic (seeded numpy, BASELINE.json distributions)",
+            "config": {"workload": wl["config"], "per_rank_batch": wl["batch"], "global_batch": wl["batch"] * world,
+                       "parallelism": f"P(batch) sharded, {world} rank(s)",
+                       "l2": "KV / keys > 126 MB L2 (no flush needed)"},
+            "gpu_launches": launches,
+            "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(kname, args.workload),
+                         "peak_kind": peak_kind, "kernel": kname,
+                         ("bytes_per_launch" if bound == "hbm" else "flops_per_launch"): work,
+                         "note": "step = all launches of the task loop (decode: chunk + merge; indexer: scoring + "
+                                 "top-k); achieved uses the whole step time"},
+            "e2e": {"value": round(e2e, 4), "unit": unit, "h2d_bytes_per_step": h2d // e2e_steps,
+                    "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            from cpu_sim import CpuSim
+
+            if args.workload == "decode":
+                sub_plan, sub = workloads.decode_inputs(np.random.default_rng(1), 2)
+                sub_work = float(sub[4].astype(np.int64).sum() * 8 * 128 * 2 * 2)
+                ax = {"b": 2}
+                what = "2 requests x 8 kv heads"
+            else:
+                sub_plan, sub = workloads.indexer_inputs(np.random.default_rng(1), 1, wl["context"], wl["topk"])
+                sub_work = 2.0 * 512 * 128 * wl["context"]
+                ax = {}
+                what = "1 batch element (scoring + top-k)"
+            t0 = time.perf_counter()
+            CpuSim(sub_plan).run(sub, axis_sizes=ax)
+            dt = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": round(sub_work / dt / scale, 6), "unit": unit, "cores": 1,
+                                    "kind": "port", "sample": f"{what}, {dt:.2f} s, numpy restatement of the "
+                                                              f"CPU-sim task (oracle/cpu_sim.py)"}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -413,6 +594,9 @@ def main() -> None:
 
     if args.workload == "bgemm":
         run_bgemm(args, wl, rank, world, local_rank)
+        return
+    if args.workload in ("decode", "indexer"):
+        run_builtin(args, wl, rank, world, local_rank)
         return
     if args.impl == "reference":
         run_reference(args, wl, rank)
