@@ -37,11 +37,42 @@ constexpr int kChunk = 512;       // tokens per split-KV chunk
 constexpr int kDecThreads = 128;  // 4 warps
 constexpr int kHeadDim = 128;
 
+// Sum 16 per-lane values over the 16 lanes of a half-warp so that lane l ends
+// up holding the total of value (l & 15): each stage halves the values a lane
+// carries, so 16 sums cost 15 shuffles instead of 4 x 16.
+__device__ __forceinline__ float halfwarp_transpose_reduce(float (&v)[16], int lane) {
+#pragma unroll
+    for (int n = 16, o = 8; n > 1; n >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = up ? v[i] : v[i + n / 2];
+            const float keep = up ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    return v[0];
+}
+
+__device__ __forceinline__ void h8_to_f8(const uint4& r, float (&f)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const float2 x = __half22float2(h[u]);
+        f[2 * u] = x.x;
+        f[2 * u + 1] = x.y;
+    }
+}
+
+// One CTA = one 512-token chunk of one (request, kv head) task.  A half-warp
+// owns one token at a time, each of its 16 lanes 8 of the 128 head dims
+// (one 16-byte load per K or V row); STEPS = 16/G tokens per half-warp are in
+// flight per iteration.
 template <int G>
 __global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBatch b, int page_size, int chunks,
                                                                         float* __restrict__ scratch) {
-    __shared__ float q_s[G][kHeadDim];
-    __shared__ float s_s[G][kChunk];
+    constexpr int STEPS = 16 / G;
+    __shared__ __align__(16) float p_s[kChunk][G];  // scores, then probabilities, token-major
     __shared__ float red_s[4][G][kHeadDim];
     __shared__ float stat_s[2][4][G];
 
@@ -64,62 +95,76 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBat
     if (t0 >= L) return;  // empty chunk (also L <= 0: the merge kernel writes zeros)
     const int n = min(kChunk, L - t0);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hl = lane & 15;        // lane within the half-warp: head dims [8*hl, 8*hl + 8)
+    const int hw = tid >> 4;         // half-warp id, 0..7
     const float scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
 
-    // q -> shared (f32), pre-scaled by 1/sqrt(D)
-    const __half* q = reinterpret_cast<const __half*>(Pq.base) + rec[0];
-    for (int e = tid; e < G * kHeadDim; e += kDecThreads) {
-        const int g = e / kHeadDim, d = e % kHeadDim;
-        q_s[g][d] = __half2float(q[g * Pq.s3 + d]) * scale;
+    // q slice of this lane (pre-scaled by 1/sqrt(D)) in registers
+    float qf[G][8];
+    {
+        const __half* q = reinterpret_cast<const __half*>(Pq.base) + rec[0];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const uint4 r = *reinterpret_cast<const uint4*>(q + g * Pq.s3 + hl * 8);
+            h8_to_f8(r, qf[g]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) qf[g][j] *= scale;
+        }
     }
-    __syncthreads();
-
     const int32_t* pt = reinterpret_cast<const int32_t*>(Ppt.base) + rec[3];
     const int64_t max_page_k = (Pk.numel_span - (int64_t)(page_size - 1) * Pk.s4 - h * kHeadDim - kHeadDim) / Pk.s3;
     const int64_t max_page_v = (Pv.numel_span - (int64_t)(page_size - 1) * Pv.s4 - h * kHeadDim - kHeadDim) / Pv.s3;
     const int64_t max_page = min(max_page_k, max_page_v);
-    const __half* kb = reinterpret_cast<const __half*>(Pk.base);
-    const __half* vb = reinterpret_cast<const __half*>(Pv.base);
-
-    // ---- scores, lane per token ----
-    float mloc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) mloc[g] = -INFINITY;
-    for (int i = tid; i < n; i += kDecThreads) {
-        const int tok = t0 + i;
-        const int64_t page = pt[static_cast<int64_t>(tok / page_size) * Ppt.s4];
-        float acc[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) acc[g] = 0.f;
+    const __half* kb = reinterpret_cast<const __half*>(Pk.base) + h * kHeadDim + hl * 8;
+    const __half* vb = reinterpret_cast<const __half*>(Pv.base) + h * kHeadDim + hl * 8;
+    auto page_of = [&](int tok, bool flag) -> int64_t {
+        int64_t page = pt[static_cast<int64_t>(tok / page_size) * Ppt.s4];
         if (page < 0 || page > max_page) {
-            atomicOr(b.err, kErrBounds);
-        } else {
-            const uint4* kr = reinterpret_cast<const uint4*>(kb + page * Pk.s3 + (tok % page_size) * Pk.s4 + h * kHeadDim);
-            uint4 raw[16];
+            if (flag) atomicOr(b.err, kErrBounds);
+            page = 0;  // read page 0 harmlessly; the run reports the error
+        }
+        return page;
+    };
+
+    // ---- scores: half-warp per token, STEPS tokens per half-warp in flight ----
+    const int my_g = hl % G;  // after the transpose reduction a lane always holds query my_g
+    float mymax = -INFINITY;
+    for (int base = 0; base < n; base += 8 * STEPS) {
+        uint4 raw[STEPS];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) raw[j] = __ldg(kr + j);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const __half2* hp = reinterpret_cast<const __half2*>(&raw[j]);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float2 kf = __half22float2(hp[u]);
-                    const int d = j * 8 + u * 2;
-#pragma unroll
-                    for (int g = 0; g < G; ++g) acc[g] = fmaf(kf.x, q_s[g][d], fmaf(kf.y, q_s[g][d + 1], acc[g]));
-                }
+        for (int st = 0; st < STEPS; ++st) {
+            const int i = base + st * 8 + hw;
+            raw[st] = make_uint4(0, 0, 0, 0);
+            if (i < n) {
+                const int tok = t0 + i;
+                const int64_t page = page_of(tok, true);
+                raw[st] = __ldg(reinterpret_cast<const uint4*>(kb + page * Pk.s3 + (tok % page_size) * Pk.s4));
             }
         }
+        float part[16];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            s_s[g][i] = acc[g];
-            mloc[g] = fmaxf(mloc[g], acc[g]);
+        for (int st = 0; st < STEPS; ++st) {
+            float kf[8];
+            h8_to_f8(raw[st], kf);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float a = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a = fmaf(kf[j], qf[g][j], a);
+                part[st * G + g] = a;
+            }
+        }
+        const float tot = halfwarp_transpose_reduce(part, hl);  // value index hl = st * G + g
+        const int i = base + (hl / G) * 8 + hw;
+        if (i < n) {
+            p_s[i][my_g] = tot;
+            mymax = fmaxf(mymax, tot);
         }
     }
     // ---- chunk max ----
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        float m = mloc[g];
+        float m = my_g == g ? mymax : -INFINITY;
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) stat_s[0][warp][g] = m;
     }
@@ -134,80 +179,77 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBat
     for (int i = tid; i < n; i += kDecThreads) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const float p = expf(s_s[g][i] - mx[g]);
-            s_s[g][i] = p;
-            lsum[g] += p;
+            const float pv = expf(p_s[i][g] - mx[g]);
+            p_s[i][g] = pv;
+            lsum[g] += pv;
         }
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        float s = lsum[g];
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) stat_s[1][warp][g] = s;
+        float sm = lsum[g];
+        for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+        if (lane == 0) stat_s[1][warp][g] = sm;
     }
     __syncthreads();
-    // ---- P.V, lane per 4 head dims, warps split the tokens ----
-    float acc[G][4];
+    // ---- P.V: half-warp per token, lane per 8 head dims ----
+    float acc[G][8];
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc[g][u] = 0.f;
-    const int per_warp = (n + 3) / 4;
-    const int i0 = warp * per_warp, i1 = min(n, i0 + per_warp);
-    int i = i0;
-    for (; i + 4 <= i1; i += 4) {
-        uint2 raw[4];
+        for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
+    constexpr int PV_STEPS = 4;
+    for (int base = 0; base < n; base += 8 * PV_STEPS) {
+        uint4 raw[PV_STEPS];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int tok = t0 + i + u;
-            int64_t page = pt[static_cast<int64_t>(tok / page_size) * Ppt.s4];
-            if (page < 0 || page > max_page) page = 0;  // flagged in the score pass; read page 0 harmlessly
-            raw[u] = __ldg(reinterpret_cast<const uint2*>(vb + page * Pv.s3 + (tok % page_size) * Pv.s4 + h * kHeadDim) + lane);
+        for (int st = 0; st < PV_STEPS; ++st) {
+            const int i = base + st * 8 + hw;
+            raw[st] = make_uint4(0, 0, 0, 0);
+            if (i < n) {
+                const int tok = t0 + i;
+                const int64_t page = page_of(tok, false);
+                raw[st] = __ldg(reinterpret_cast<const uint4*>(vb + page * Pv.s3 + (tok % page_size) * Pv.s4));
+            }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const __half2* hp = reinterpret_cast<const __half2*>(&raw[u]);
-            const float2 v01 = __half22float2(hp[0]), v23 = __half22float2(hp[1]);
+        for (int st = 0; st < PV_STEPS; ++st) {
+            const int i = base + st * 8 + hw;
+            if (i < n) {
+                float vf[8];
+                h8_to_f8(raw[st], vf);
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float p = s_s[g][i + u];
-                acc[g][0] = fmaf(p, v01.x, acc[g][0]);
-                acc[g][1] = fmaf(p, v01.y, acc[g][1]);
-                acc[g][2] = fmaf(p, v23.x, acc[g][2]);
-                acc[g][3] = fmaf(p, v23.y, acc[g][3]);
+                for (int g = 0; g < G; ++g) {
+                    const float pg = p_s[i][g];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(pg, vf[j], acc[g][j]);
+                }
             }
         }
     }
-    for (; i < i1; ++i) {
-        const int tok = t0 + i;
-        int64_t page = pt[static_cast<int64_t>(tok / page_size) * Ppt.s4];
-        if (page < 0 || page > max_page) page = 0;
-        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(vb + page * Pv.s3 + (tok % page_size) * Pv.s4 + h * kHeadDim) + lane);
-        const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-        const float2 v01 = __half22float2(hp[0]), v23 = __half22float2(hp[1]);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float p = s_s[g][i];
-            acc[g][0] = fmaf(p, v01.x, acc[g][0]);
-            acc[g][1] = fmaf(p, v01.y, acc[g][1]);
-            acc[g][2] = fmaf(p, v23.x, acc[g][2]);
-            acc[g][3] = fmaf(p, v23.y, acc[g][3]);
-        }
-    }
+    // the two half-warps of a warp hold different tokens: add them, then one row per warp
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) red_s[warp][g][lane * 4 + u] = acc[g][u];
+        for (int j = 0; j < 8; ++j) acc[g][j] += __shfl_xor_sync(0xffffffffu, acc[g][j], 16);
+    if (lane < 16) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) red_s[warp][g][hl * 8 + j] = acc[g][j];
+    }
     __syncthreads();
     // ---- partial (max, sum, acc) -> scratch ----
-    float* part = scratch + static_cast<int64_t>(blockIdx.x) * (G * kHeadDim + 2 * G);
+    float* part_out = scratch + static_cast<int64_t>(blockIdx.x) * (G * kHeadDim + 2 * G);
     for (int e = tid; e < G * kHeadDim; e += kDecThreads) {
         const int g = e / kHeadDim, d = e % kHeadDim;
-        part[e] = red_s[0][g][d] + red_s[1][g][d] + red_s[2][g][d] + red_s[3][g][d];
+        part_out[e] = (red_s[0][g][d] + red_s[1][g][d]) + (red_s[2][g][d] + red_s[3][g][d]);
     }
     if (tid < G) {
-        part[G * kHeadDim + tid] = mx[tid];
-        part[G * kHeadDim + G + tid] = stat_s[1][0][tid] + stat_s[1][1][tid] + stat_s[1][2][tid] + stat_s[1][3][tid];
+        float m = 0.f;
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            if (g == tid) m = mx[g];  // static register indexing
+        part_out[G * kHeadDim + tid] = m;
+        part_out[G * kHeadDim + G + tid] = stat_s[1][0][tid] + stat_s[1][1][tid] + stat_s[1][2][tid] + stat_s[1][3][tid];
     }
 }
 
@@ -272,6 +314,9 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 
 __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) {
     extern __shared__ uint32_t ks[];  // N keys, then 2K composite slots (u64)
+    // Per-warp histograms: scores of one row share few exponent bytes, so a
+    // single shared histogram would serialise thousands of atomics on 2-3 bins.
+    __shared__ uint32_t whist[kTopkThreads / 32][256];
     __shared__ uint32_t hist[256];
     __shared__ uint32_t sel_prefix, sel_remaining, n_gt, n_eq_taken;
     const int64_t task = blockIdx.x;
@@ -285,6 +330,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     unsigned long long* comp = reinterpret_cast<unsigned long long*>(ks + ((N + 1) & ~1));
     const float* src = reinterpret_cast<const float*>(S.base) + rec[0];
     const int64_t ss = S.s4;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     for (int i = threadIdx.x; i < N; i += kTopkThreads) ks[i] = order_key(src[i * ss]);
     if (threadIdx.x == 0) {
         sel_prefix = 0;
@@ -293,13 +339,23 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     __syncthreads();
     // radix select, 8 bits per pass, most significant first
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int i = threadIdx.x; i < 256; i += kTopkThreads) hist[i] = 0;
+        for (int i = lane; i < 256; i += 32) whist[wid][i] = 0;
         __syncthreads();
         const uint32_t prefix = sel_prefix;
         const uint32_t hi_mask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
-        for (int i = threadIdx.x; i < N; i += kTopkThreads) {
-            const uint32_t k = ks[i];
-            if ((k & hi_mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xffu], 1u);
+        for (int base = 0; base < N; base += kTopkThreads) {
+            const int i = base + threadIdx.x;
+            const uint32_t k = i < N ? ks[i] : 0u;
+            const bool in = i < N && (k & hi_mask) == prefix;
+            const uint32_t bin = in ? ((k >> shift) & 0xffu) : 256u + lane;  // unique dummy bins for idle lanes
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (in && lane == __ffs(peers) - 1) whist[wid][bin] += __popc(peers);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < 256; i += kTopkThreads) {
+            uint32_t t = 0;
+            for (int w = 0; w < kTopkThreads / 32; ++w) t += whist[w][i];
+            hist[i] = t;
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -323,10 +379,16 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     }
     for (int i = threadIdx.x; i < K2; i += kTopkThreads) comp[i] = 0ull;
     __syncthreads();
-    for (int i = threadIdx.x; i < N; i += kTopkThreads) {
-        const uint32_t k = ks[i];
-        if (k > thr) {
-            const uint32_t slot = atomicAdd(&n_gt, 1u);
+    for (int base = 0; base < N; base += kTopkThreads) {
+        const int i = base + threadIdx.x;
+        const uint32_t k = i < N ? ks[i] : 0u;
+        const bool gt = i < N && k > thr;
+        const unsigned m = __ballot_sync(0xffffffffu, gt);  // one shared atomic per warp
+        uint32_t wbase = 0;
+        if (lane == 0 && m) wbase = atomicAdd(&n_gt, static_cast<uint32_t>(__popc(m)));
+        wbase = __shfl_sync(0xffffffffu, wbase, 0);
+        if (gt) {
+            const uint32_t slot = wbase + __popc(m & ((1u << lane) - 1u));
             if (slot < static_cast<uint32_t>(K)) comp[slot] = (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
         }
     }
@@ -338,7 +400,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
         const bool eq = i < N && ks[i] == thr;
         const unsigned mask = __ballot_sync(0xffffffffu, eq);
         __shared__ uint32_t warp_cnt[kTopkThreads / 32];
-        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+        const int w = wid;
         if (lane == 0) warp_cnt[w] = __popc(mask);
         __syncthreads();
         uint32_t before = n_eq_taken;
@@ -406,7 +468,7 @@ int topk_smem_bytes(int n, int k) {
 
 cudaError_t launch_topk_select(const TaskBatch& b, int, void*, size_t, cudaStream_t s) {
     const int smem = topk_smem_bytes(b.p[0].cols, b.p[1].cols);
-    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    if (smem > 180 * 1024) return cudaErrorInvalidValue;  // + 33 KB static histograms
     cudaError_t e = cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     if (b.ntasks <= 0) return cudaSuccess;

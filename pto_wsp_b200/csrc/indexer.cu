@@ -243,8 +243,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
                 for (int ql = 0; ql < 4; ++ql) {
                     const int q = hq * 4 + ql;
-                    const float* wq = w + q * args.w_s3;
-                    float acc = 0.f;
+                    const float4* wq = reinterpret_cast<const float4*>(w + q * args.w_s3);
+                    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums over heads h = 4j + c
 #pragma unroll 1
                     for (int hc = 0; hc < 2; ++hc) {
                         float v[32];
@@ -252,9 +252,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                                       static_cast<uint32_t>(slot * NH + ql * HEADS + hc * 32),
                                   v);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) acc = fmaf(__ldg(wq + hc * 32 + j), fmaxf(v[j], 0.f), acc);
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 wv = __ldg(wq + hc * 8 + j);  // same address in every lane: one L1 broadcast
+                            acc[0] = fmaf(wv.x, fmaxf(v[4 * j + 0], 0.f), acc[0]);
+                            acc[1] = fmaf(wv.y, fmaxf(v[4 * j + 1], 0.f), acc[1]);
+                            acc[2] = fmaf(wv.z, fmaxf(v[4 * j + 2], 0.f), acc[2]);
+                            acc[3] = fmaf(wv.w, fmaxf(v[4 * j + 3], 0.f), acc[3]);
+                        }
                     }
-                    s[q * args.s_s3] = acc;
+                    s[q * args.s_s3] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
                 }
                 tc_fence_before();
                 mbar_arrive(smem_u32(&tempty[slot]));
@@ -282,6 +288,7 @@ bool indexer_score_supported(const TaskBatch& b) {
     const ParamDesc& S = b.p[3];
     if (Q.rows != QH || Q.cols != D || K.cols != D || K.rows % KT || W.rows != 8 || W.cols != HEADS) return false;
     if (S.rows != 8 || S.cols != K.rows) return false;
+    if (W.s3 % 4 || (reinterpret_cast<uintptr_t>(W.base) & 15)) return false;  // float4 weight rows
     if (Q.s3 != D || K.s3 != D || Q.s4 != 1 || K.s4 != 1 || W.s4 != 1 || S.s4 != 1) return false;
     if ((reinterpret_cast<uintptr_t>(Q.base) | reinterpret_cast<uintptr_t>(K.base)) & 15) return false;
     return true;

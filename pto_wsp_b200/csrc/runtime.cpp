@@ -636,8 +636,11 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
             break;
         case ImplKind::PagedDecode: {
             const dev::ParamDesc &K = tb.p[1], &V = tb.p[2];
-            const bool aligned = K.s3 % 8 == 0 && K.s4 % 8 == 0 && V.s3 % 4 == 0 && V.s4 % 4 == 0 &&
-                                 ((reinterpret_cast<uintptr_t>(K.base) & 15) | (reinterpret_cast<uintptr_t>(V.base) & 7)) == 0;
+            const dev::ParamDesc& Q = tb.p[0];
+            const bool aligned = K.s3 % 8 == 0 && K.s4 % 8 == 0 && V.s3 % 8 == 0 && V.s4 % 8 == 0 && Q.s3 % 8 == 0 &&
+                                 Q.s4 == 1 &&
+                                 ((reinterpret_cast<uintptr_t>(K.base) | reinterpret_cast<uintptr_t>(V.base) |
+                                   reinterpret_cast<uintptr_t>(Q.base)) & 15) == 0;
             if (!aligned)
                 throw Error(PTOWSP_ERR_UNSUPPORTED, "paged_decode_gqa: KV cache rows must be 16-byte aligned");
             size_t sb = dev::paged_decode_scratch_bytes(tb, 16);
@@ -650,7 +653,7 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                 bool ok = dev::indexer_score_supported(tb) && !B.rec.empty();
                 for (int64_t t = 0; ok && t < B.ntasks; ++t) {
                     const int64_t* r = &B.rec[t * B.stride];
-                    ok = r[0] % 128 == 0 && r[1] % 128 == 0 && r[0] + 512 * 128 <= tb.p[0].numel_span &&
+                    ok = r[0] % 128 == 0 && r[1] % 128 == 0 && r[2] % 4 == 0 && r[0] + 512 * 128 <= tb.p[0].numel_span &&
                          r[1] + tb.p[1].rows * 128 <= tb.p[1].numel_span;
                 }
                 B.fast_ok = ok ? 1 : 0;
