@@ -28,6 +28,7 @@
 #include <mutex>
 
 #include "device.hpp"
+#include "tc_common.cuh"
 
 namespace ptowsp::dev {
 
@@ -253,6 +254,279 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBat
     }
 }
 
+// ---------------------------------------------------------------------------
+// TMA-fed variant (the default for contiguous 16-token page pools).  A producer
+// warp streams, page by page, the task's head slice of K and V (16 rows x 256 B
+// each, one TMA box apiece) into an 8-stage shared-memory ring; four consumer
+// warps each own every 4th page of the chunk and run an online softmax over
+// it from shared memory (half-warp per token, lane per 8 head dims), so HBM
+// latency is hidden by the ring instead of by thread count.  The warps'
+// (max, sum, acc) are combined with the log-sum-exp rule into the same chunk
+// partial the merge kernel reads.  Bounded waits; the producer drains its
+// copies before the CTA exits.
+// ---------------------------------------------------------------------------
+
+constexpr int kTmaStages = 8;
+constexpr int kTmaConsumers = 4;
+constexpr int kTmaThreads = 32 * (kTmaConsumers + 1);
+constexpr int kTmaPage = 16;
+constexpr int kTmaPageBytes = kTmaPage * kHeadDim * 2;  // 4 KB
+
+template <int G>
+struct TmaSmem {
+    static constexpr int RING = kTmaStages * 2 * kTmaPageBytes;                 // K and V per stage
+    static constexpr int BAR = RING;                                             // full[S], empty[S], abort
+    static constexpr int PW = BAR + 256;                                         // per-warp p[16][G]
+    static constexpr int CW = PW + kTmaConsumers * kTmaPage * G * 4;             // per-warp (m, l, acc)
+    static constexpr int CW_STRIDE = 2 * G + G * kHeadDim;                       // floats
+    static constexpr int TOTAL = CW + kTmaConsumers * CW_STRIDE * 4 + 128;       // + alignment slack
+};
+
+// Sum V per-lane values over the 16 lanes of a half-warp; afterwards lane l
+// holds V/16 totals, for value indices (V/16) * (l & 15) + j.
+template <int V>
+__device__ __forceinline__ void halfwarp_transpose_reduce_v(float (&v)[V], int lane) {
+#pragma unroll
+    for (int n = V, o = 8; o >= 1; n >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = up ? v[i] : v[i + n / 2];
+            const float keep = up ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap mk,
+                                                                     const __grid_constant__ CUtensorMap mv, TaskBatch b,
+                                                                     int chunks, float* __restrict__ scratch) {
+    using S = TmaSmem<G>;
+    constexpr int V = 8 * G;      // partial dot products per lane per page (8 tokens x G queries)
+    constexpr int PER = V / 16;   // totals per lane after the reduction
+    static_assert(V >= 16, "GQA group of at least 2");
+    extern __shared__ uint8_t dsm_raw[];
+    uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 127) & ~uintptr_t(127));
+    uint64_t* full = reinterpret_cast<uint64_t*>(dsm + S::BAR);
+    uint64_t* empty = full + kTmaStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kTmaStages);
+
+    const int64_t task = blockIdx.x / chunks;
+    const int chunk = blockIdx.x % chunks;
+    if (task >= b.ntasks) return;
+    const int64_t* rec = b.rec + task * b.stride;
+    const ParamDesc& Pq = b.p[0];
+    const ParamDesc& Ppt = b.p[3];
+    const ParamDesc& Pl = b.p[4];
+    const int h = static_cast<int>(rec[b.nparams + 1]);
+    int32_t L = reinterpret_cast<const int32_t*>(Pl.base)[rec[4]];
+    if (L > Ppt.cols * kTmaPage) {
+        if (chunk == 0 && threadIdx.x == 0) atomicOr(b.err, kErrShape);
+        L = Ppt.cols * kTmaPage;
+    }
+    const int t0 = chunk * kChunk;
+    if (t0 >= L) return;  // whole CTA leaves together: no barrier has been touched
+    const int n = min(kChunk, L - t0);
+    const int npages = (n + kTmaPage - 1) / kTmaPage;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kTmaStages; ++st) {
+            tc::mbar_init(tc::smem_u32(&full[st]), 1);
+            tc::mbar_init(tc::smem_u32(&empty[st]), 1);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kTmaConsumers) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const int32_t* pt = reinterpret_cast<const int32_t*>(Ppt.base) + rec[3];
+            const int64_t max_page = b.p[1].numel_span / (int64_t(kTmaPage) * b.p[1].s4) - 1;
+            int issued = 0;
+            for (int j = 0; j < npages && !*abort_flag; ++j) {
+                const int st = j % kTmaStages;
+                if (j >= kTmaStages &&
+                    !tc::mbar_wait(tc::smem_u32(&empty[st]), ((j / kTmaStages) - 1) & 1, abort_flag, b.err))
+                    break;
+                int64_t page = pt[static_cast<int64_t>(t0 / kTmaPage + j) * Ppt.s4];
+                if (page < 0 || page > max_page) {
+                    atomicOr(b.err, kErrBounds);
+                    page = 0;
+                }
+                const uint32_t fb = tc::smem_u32(&full[st]);
+                tc::mbar_expect_tx(fb, 2 * kTmaPageBytes);
+                uint8_t* kd = dsm + st * 2 * kTmaPageBytes;
+                tc::tma_load_2d(tc::smem_u32(kd), &mk, h * kHeadDim, static_cast<int32_t>(page * kTmaPage), fb);
+                tc::tma_load_2d(tc::smem_u32(kd + kTmaPageBytes), &mv, h * kHeadDim, static_cast<int32_t>(page * kTmaPage), fb);
+                ++issued;
+            }
+            // drain: the last copy into each stage has landed
+            const uint64_t start = tc::globaltimer();
+            for (int j = max(0, issued - kTmaStages); j < issued; ++j)
+                while (!tc::mbar_try_wait(tc::smem_u32(&full[j % kTmaStages]), (j / kTmaStages) & 1))
+                    if (tc::globaltimer() - start > tc::kTimeoutNs) {
+                        atomicOr(b.err, kErrTimeout);
+                        break;
+                    }
+        }
+    } else {
+        // ---------------- consumers ----------------
+        const int hl = lane & 15, hh = lane >> 4;
+        float qf[G][8];
+        {
+            const __half* q = reinterpret_cast<const __half*>(Pq.base) + rec[0];
+            const float scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                h8_to_f8(*reinterpret_cast<const uint4*>(q + g * Pq.s3 + hl * 8), qf[g]);
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) qf[g][jj] *= scale;
+            }
+        }
+        float m[G], l[G], acc[G][8];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            m[g] = -INFINITY;
+            l[g] = 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) acc[g][jj] = 0.f;
+        }
+        float* pw = reinterpret_cast<float*>(dsm + S::PW) + warp * kTmaPage * G;
+        for (int j = warp; j < npages && !*abort_flag; j += kTmaConsumers) {
+            const int st = j % kTmaStages;
+            if (!tc::mbar_wait(tc::smem_u32(&full[st]), (j / kTmaStages) & 1, abort_flag, b.err)) break;
+            const uint8_t* ksm = dsm + st * 2 * kTmaPageBytes;
+            const uint8_t* vsm = ksm + kTmaPageBytes;
+            const int valid = min(kTmaPage, n - j * kTmaPage);
+            // scores of this half-warp's 8 tokens
+            float part[V];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                float kf[8];
+                h8_to_f8(*reinterpret_cast<const uint4*>(ksm + (hh * 8 + t) * 256 + hl * 16), kf);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float a = 0.f;
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) a = fmaf(kf[jj], qf[g][jj], a);
+                    part[t * G + g] = a;
+                }
+            }
+            halfwarp_transpose_reduce_v<V>(part, hl);
+            // this lane now holds scores of value indices PER*hl + k (token = idx / G, query = idx % G)
+            float pmax[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) pmax[g] = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int idx = PER * hl + k;
+                if (hh * 8 + idx / G >= valid) part[k] = -INFINITY;  // past the last token of the chunk
+                const int gk = idx % G;
+#pragma unroll
+                for (int g = 0; g < G; ++g) pmax[g] = fmaxf(pmax[g], gk == g ? part[k] : -INFINITY);  // selects only
+            }
+            float corr[G], mnew[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float x = pmax[g];
+                for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+                mnew[g] = fmaxf(m[g], x);
+                corr[g] = expf(m[g] - mnew[g]);  // 0 on the first page (m = -inf)
+            }
+            float psum[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) psum[g] = 0.f;
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int idx = PER * hl + k;
+                const int tok = hh * 8 + idx / G;
+                const int gk = idx % G;
+                float mk = mnew[0];
+#pragma unroll
+                for (int g = 1; g < G; ++g) mk = gk == g ? mnew[g] : mk;
+                const float pg = expf(part[k] - mk);
+#pragma unroll
+                for (int g = 0; g < G; ++g) psum[g] += gk == g ? pg : 0.f;
+                pw[tok * G + gk] = pg;
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float x = psum[g];
+                for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+                l[g] = l[g] * corr[g] + x;
+                m[g] = mnew[g];
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) acc[g][jj] *= corr[g];
+            }
+            __syncwarp();
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const int tok = hh * 8 + t;
+                float vf[8];
+                h8_to_f8(*reinterpret_cast<const uint4*>(vsm + tok * 256 + hl * 16), vf);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float pg = pw[tok * G + g];
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) acc[g][jj] = fmaf(pg, vf[jj], acc[g][jj]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(tc::smem_u32(&empty[st]));
+        }
+        // the two half-warps saw different tokens of the same pages: add them
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) acc[g][jj] += __shfl_xor_sync(0xffffffffu, acc[g][jj], 16);
+        float* cw = reinterpret_cast<float*>(dsm + S::CW) + warp * S::CW_STRIDE;
+        if (lane < 16) {
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) cw[2 * G + g * kHeadDim + hl * 8 + jj] = acc[g][jj];
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                cw[g] = m[g];
+                cw[G + g] = l[g];
+            }
+        }
+    }
+    __syncthreads();
+    // ---- combine the consumer warps -> chunk partial (same format as the non-TMA kernel) ----
+    const float* cw0 = reinterpret_cast<const float*>(dsm + S::CW);
+    float* part_out = scratch + static_cast<int64_t>(blockIdx.x) * (G * kHeadDim + 2 * G);
+    for (int e = threadIdx.x; e < G * kHeadDim; e += kTmaThreads) {
+        const int g = e / kHeadDim;
+        float M = -INFINITY;
+        for (int w = 0; w < kTmaConsumers; ++w) M = fmaxf(M, cw0[w * S::CW_STRIDE + g]);
+        float a = 0.f;
+        for (int w = 0; w < kTmaConsumers; ++w) {
+            const float mw = cw0[w * S::CW_STRIDE + g];
+            if (mw != -INFINITY) a = fmaf(cw0[w * S::CW_STRIDE + 2 * G + e], expf(mw - M), a);
+        }
+        part_out[e] = a;
+    }
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float M = -INFINITY;
+        for (int w = 0; w < kTmaConsumers; ++w) M = fmaxf(M, cw0[w * S::CW_STRIDE + g]);
+        float lt = 0.f;
+        for (int w = 0; w < kTmaConsumers; ++w) {
+            const float mw = cw0[w * S::CW_STRIDE + g];
+            if (mw != -INFINITY) lt = fmaf(cw0[w * S::CW_STRIDE + G + g], expf(mw - M), lt);
+        }
+        part_out[G * kHeadDim + g] = M;
+        part_out[G * kHeadDim + G + g] = lt;
+    }
+}
+
 template <int G>
 __global__ void __launch_bounds__(kDecThreads) paged_decode_merge_kernel(TaskBatch b, int page_size, int chunks,
                                                                         const float* __restrict__ scratch) {
@@ -284,14 +558,41 @@ int decode_chunks(const TaskBatch& b, int page_size) {
     return static_cast<int>(std::max<int64_t>(1, (max_tokens + kChunk - 1) / kChunk));
 }
 
+bool decode_tma_ok(const TaskBatch& b, int page_size, int group) {
+    const ParamDesc& K = b.p[1];
+    const ParamDesc& V = b.p[2];
+    return group >= 2 && page_size == kTmaPage && K.s3 == kTmaPage * K.s4 && V.s3 == kTmaPage * V.s4 &&
+           K.s4 == V.s4 && K.s4 % 8 == 0 && K.s4 >= kHeadDim &&
+           ((reinterpret_cast<uintptr_t>(K.base) | reinterpret_cast<uintptr_t>(V.base)) & 15) == 0;
+}
+
 template <int G>
 cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cudaStream_t s) {
     const int chunks = decode_chunks(b, page_size);
     const int64_t grid = b.ntasks * chunks;
     if (grid <= 0) return cudaSuccess;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    paged_decode_chunk_kernel<G><<<static_cast<unsigned>(grid), kDecThreads, 0, s>>>(b, page_size, chunks,
-                                                                                     static_cast<float*>(scratch));
+    bool launched = false;
+    if constexpr (G >= 2) {
+        if (decode_tma_ok(b, page_size, G)) {
+            const ParamDesc& K = b.p[1];
+            const ParamDesc& V = b.p[2];
+            CUtensorMap mk, mv;
+            const uint64_t krows = (K.numel_span + K.s4 - 1) / K.s4, vrows = (V.numel_span + V.s4 - 1) / V.s4;
+            if (tc::make_map_f16_plain(&mk, K.base, K.s4, krows, K.s4 * 2, kHeadDim, kTmaPage) &&
+                tc::make_map_f16_plain(&mv, V.base, V.s4, vrows, V.s4 * 2, kHeadDim, kTmaPage)) {
+                const int smem = TmaSmem<G>::TOTAL;
+                cudaError_t e = cudaFuncSetAttribute(paged_decode_tma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                if (e != cudaSuccess) return e;
+                paged_decode_tma_kernel<G><<<static_cast<unsigned>(grid), kTmaThreads, smem, s>>>(
+                    mk, mv, b, chunks, static_cast<float*>(scratch));
+                launched = true;
+            }
+        }
+    }
+    if (!launched)
+        paged_decode_chunk_kernel<G><<<static_cast<unsigned>(grid), kDecThreads, 0, s>>>(b, page_size, chunks,
+                                                                                         static_cast<float*>(scratch));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     paged_decode_merge_kernel<G><<<static_cast<unsigned>(b.ntasks), kDecThreads, 0, s>>>(b, page_size, chunks,
@@ -312,12 +613,11 @@ __device__ __forceinline__ uint32_t order_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+template <int KPT>
 __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) {
     extern __shared__ uint32_t ks[];  // N keys, then 2K composite slots (u64)
-    // Per-warp histograms: scores of one row share few exponent bytes, so a
-    // single shared histogram would serialise thousands of atomics on 2-3 bins.
-    __shared__ uint32_t whist[kTopkThreads / 32][256];
-    __shared__ uint32_t hist[256];
+    __shared__ uint32_t wcount[kTopkThreads / 32];
+    __shared__ uint32_t total_s;
     __shared__ uint32_t sel_prefix, sel_remaining, n_gt, n_eq_taken;
     const int64_t task = blockIdx.x;
     if (task >= b.ntasks) return;
@@ -331,46 +631,51 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     const float* src = reinterpret_cast<const float*>(S.base) + rec[0];
     const int64_t ss = S.s4;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < N; i += kTopkThreads) ks[i] = order_key(src[i * ss]);
-    if (threadIdx.x == 0) {
-        sel_prefix = 0;
-        sel_remaining = K;
+    // keys: in shared memory (for the gather) and, KPT per thread, in registers (for counting)
+    uint32_t kr[KPT];
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+        const int i = j * kTopkThreads + threadIdx.x;
+        kr[j] = 0u;  // slots past N are skipped by the i < N test when counting
+        if (i < N) {
+            kr[j] = order_key(src[i * ss]);
+            ks[i] = kr[j];
+        }
     }
     __syncthreads();
-    // radix select, 8 bits per pass, most significant first
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int i = lane; i < 256; i += 32) whist[wid][i] = 0;
+    // Exact K-th largest key by binary search on its bits, most significant
+    // first: keep bit b if at least K keys are >= (prefix | bit b).  No atomics.
+    auto count_ge = [&](uint32_t cand) -> uint32_t {
+        uint32_t c = 0;
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            const int i = j * kTopkThreads + threadIdx.x;
+            c += (i < N && kr[j] >= cand) ? 1u : 0u;
+        }
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (lane == 0) wcount[wid] = c;
         __syncthreads();
-        const uint32_t prefix = sel_prefix;
-        const uint32_t hi_mask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
-        for (int base = 0; base < N; base += kTopkThreads) {
-            const int i = base + threadIdx.x;
-            const uint32_t k = i < N ? ks[i] : 0u;
-            const bool in = i < N && (k & hi_mask) == prefix;
-            const uint32_t bin = in ? ((k >> shift) & 0xffu) : 256u + lane;  // unique dummy bins for idle lanes
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (in && lane == __ffs(peers) - 1) whist[wid][bin] += __popc(peers);
+        if (wid == 0) {
+            uint32_t t = lane < kTopkThreads / 32 ? wcount[lane] : 0u;
+            t = __reduce_add_sync(0xffffffffu, t);
+            if (lane == 0) total_s = t;
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < 256; i += kTopkThreads) {
-            uint32_t t = 0;
-            for (int w = 0; w < kTopkThreads / 32; ++w) t += whist[w][i];
-            hist[i] = t;
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            uint32_t rem = sel_remaining;
-            int digit = 255;
-            for (; digit > 0; --digit) {
-                if (hist[digit] >= rem) break;
-                rem -= hist[digit];
-            }
-            sel_prefix = prefix | (static_cast<uint32_t>(digit) << shift);
-            sel_remaining = rem;  // how many of the threshold-equal keys (so far) are still needed
-        }
-        __syncthreads();
+        return total_s;
+    };
+    uint32_t thr = 0;
+    for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = thr | (1u << bit);
+        if (count_ge(cand) >= static_cast<uint32_t>(K)) thr = cand;
+        __syncthreads();  // total_s is rewritten by the next count
     }
-    const uint32_t thr = sel_prefix;      // the K-th largest key
+    // K >= 1 keys are >= thr and fewer than K are > thr: count_ge(thr + 1) < K (or thr is the maximum key).
+    const uint32_t cnt_gt = thr == 0xffffffffu ? 0u : count_ge(thr + 1u);
+    if (threadIdx.x == 0) {
+        sel_prefix = thr;
+        sel_remaining = static_cast<uint32_t>(K) - cnt_gt;
+    }
+    __syncthreads();
     const uint32_t need_eq = sel_remaining;  // how many keys equal to thr are taken (lowest indices first)
     // gather: every key > thr, plus the first need_eq keys == thr in index order
     if (threadIdx.x == 0) {
@@ -466,14 +771,26 @@ int topk_smem_bytes(int n, int k) {
     return ((n + 1) & ~1) * 4 + k2 * 8;
 }
 
-cudaError_t launch_topk_select(const TaskBatch& b, int, void*, size_t, cudaStream_t s) {
-    const int smem = topk_smem_bytes(b.p[0].cols, b.p[1].cols);
-    if (smem > 180 * 1024) return cudaErrorInvalidValue;  // + 33 KB static histograms
-    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+template <int KPT>
+cudaError_t launch_topk_kpt(const TaskBatch& b, int smem, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel<KPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    if (b.ntasks <= 0) return cudaSuccess;
-    topk_select_kernel<<<static_cast<unsigned>(b.ntasks), kTopkThreads, smem, s>>>(b);
+    topk_select_kernel<KPT><<<static_cast<unsigned>(b.ntasks), kTopkThreads, smem, s>>>(b);
     return cudaGetLastError();
+}
+
+cudaError_t launch_topk_select(const TaskBatch& b, int, void*, size_t, cudaStream_t s) {
+    const int n = b.p[0].cols;
+    const int smem = topk_smem_bytes(n, b.p[1].cols);
+    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    if (b.ntasks <= 0) return cudaSuccess;
+    const int kpt = (n + kTopkThreads - 1) / kTopkThreads;
+    if (kpt <= 4) return launch_topk_kpt<4>(b, smem, s);
+    if (kpt <= 8) return launch_topk_kpt<8>(b, smem, s);
+    if (kpt <= 16) return launch_topk_kpt<16>(b, smem, s);
+    if (kpt <= 32) return launch_topk_kpt<32>(b, smem, s);
+    if (kpt <= 48) return launch_topk_kpt<48>(b, smem, s);
+    return cudaErrorInvalidValue;  // rows beyond 49152 scores
 }
 
 }  // namespace ptowsp::dev

@@ -641,8 +641,10 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                                  Q.s4 == 1 &&
                                  ((reinterpret_cast<uintptr_t>(K.base) | reinterpret_cast<uintptr_t>(V.base) |
                                    reinterpret_cast<uintptr_t>(Q.base)) & 15) == 0;
-            if (!aligned)
-                throw Error(PTOWSP_ERR_UNSUPPORTED, "paged_decode_gqa: KV cache rows must be 16-byte aligned");
+            bool q_rows_ok = true;  // q rows are read 16 bytes at a time
+            for (int64_t t = 0; t < B.ntasks && !B.rec.empty(); ++t) q_rows_ok = q_rows_ok && B.rec[t * B.stride] % 8 == 0;
+            if (!aligned || !q_rows_ok)
+                throw Error(PTOWSP_ERR_UNSUPPORTED, "paged_decode_gqa: q and KV cache rows must be 16-byte aligned");
             size_t sb = dev::paged_decode_scratch_bytes(tb, 16);
             void* s = ensure_scratch(P, sb);
             e = dev::launch_paged_decode(tb, 16, 0, workers, s, sb, P.stream);

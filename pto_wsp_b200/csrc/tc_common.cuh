@@ -132,4 +132,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // point is unavailable or the encoder rejects the parameters.
 bool make_map_f16(CUtensorMap* m, const void* base, int64_t pitch, int64_t rows, uint32_t box_x, uint32_t box_y);
 
+// Host: general 2-D f16 tensor map: `inner` elements per row, `rows` rows
+// `row_bytes` apart (a multiple of 16), box `box_x` x `box_y`, no swizzle.
+bool make_map_f16_plain(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                        uint32_t box_x, uint32_t box_y);
+
 }  // namespace ptowsp::dev::tc
