@@ -130,8 +130,12 @@ PTOWSP_API const char* ptowsp_cuda_last_error(void);
  * Until this is called a program uses a private non-blocking stream. */
 PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
 
-/* Integer options: "pipeline_chunks" (host-staged runs overlap copy and
- * compute in this many chunks, default 4), "cache_plans" (reuse the task table
+/* Integer options: "pipeline_chunks" (a static single-batch workload whose
+ * host tensors hold 64 MiB or more, with outputs that are fully overwritten and
+ * not read, runs as up to this many chunks of tasks whose host->device copies,
+ * kernels and device->host copies overlap on three streams; chunks carry at
+ * least 4 MiB of host traffic; 1 turns it off; default 32.  Pinned host memory
+ * is needed for the copies to overlap), "cache_plans" (reuse the task table
  * of static workloads across runs, default 1), "sync" (0: when every tensor
  * is device memory, return without waiting; errors surface at the next
  * synchronous run, default 1), "dry_run" (1: walk the task loop on the host
@@ -139,7 +143,7 @@ PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
 PTOWSP_API int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value);
 
 typedef struct ptowsp_timing {
-    double gpu_ms;        /* kernel time of the last run (CUDA events) */
+    double gpu_ms;        /* kernel time of the last run (CUDA events; overlapped runs: first to last kernel, copies between them included) */
     double total_ms;      /* wall time of the last ptowsp_cuda_main call */
     uint64_t launches;    /* kernel launches of the last run */
     uint64_t tasks;       /* tasks executed */

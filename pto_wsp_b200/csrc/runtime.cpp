@@ -493,6 +493,9 @@ Program::~Program() {
     if (err_dev) cudaFree(err_dev);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
+    for (auto e : pipe_events) cudaEventDestroy(e);
+    if (h2d_stream) cudaStreamDestroy(h2d_stream);
+    if (d2h_stream) cudaStreamDestroy(d2h_stream);
     if (own_stream) cudaStreamDestroy(own_stream);
     if (prev >= 0) cudaSetDevice(prev);
 }
@@ -677,6 +680,164 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
     launches++;
 }
 
+
+// Host-staged runs of a single-batch workload, overlapped: the batch is cut
+// into chunks of consecutive tasks; chunk c's input ranges are copied in on a
+// copy stream, its kernel waits for them on the compute stream, and its output
+// ranges go back on a second copy stream while later chunks compute.  Inputs
+// are copied once (ranges already staged by an earlier chunk are skipped).
+// Only for workloads whose written tensors are fully overwritten and never read
+// (so a chunk's output range can be copied back without staging it in).
+// Returns false (nothing done) when the workload does not qualify.
+bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, uint64_t& launches) {
+    if (!P.cacheable || P.opt_chunks < 2) return false;
+    Batch* B = nullptr;
+    int nb = 0;
+    for (auto& w : L.waves)
+        for (auto& b : w.batches) {
+            ++nb;
+            B = &b;
+        }
+    if (nb != 1 || B->ntasks < 2) return false;
+    const KernelImpl& ki = P.impls[B->kernel];
+    if (ki.kind != ImplKind::RmsNorm && ki.kind != ImplKind::Softmax && ki.kind != ImplKind::TileProgram) return false;
+    const KernelDef& kd = P.plan.kernels[B->kernel];
+    const Node& node = *B->node;
+    const int np = kd.num_tensor_params;
+    std::vector<int> tens(np);
+    size_t host_bytes = 0;
+    for (int ti = 0; ti < np; ++ti) tens[ti] = static_cast<int>(node.tensor_args[node.param_to_arg[ti]].tensor);
+    for (int ti = 0; ti < np; ++ti) {
+        const TensorBinding& tb = T[tens[ti]];
+        if (tb.on_device) continue;
+        host_bytes += tb.bytes;
+        for (int tj = 0; tj < np; ++tj)  // a tensor both read and written by the batch: not pipelined
+            if (tens[tj] == tens[ti] && ((ki.param_write[ti] && ki.param_read[tj]) || (ki.param_read[ti] && ki.param_write[tj])))
+                return false;
+        if (ki.param_write[ti] && (L.full_write.empty() || !L.full_write[tens[ti]])) return false;
+    }
+    if (host_bytes < (size_t(64) << 20)) return false;  // small copies: not worth the extra streams
+    // chunks of at least 4 MiB of host traffic: smaller copies do not reach the copy engines' rate
+    const int64_t by_size = std::max<int64_t>(2, static_cast<int64_t>(host_bytes >> 22));
+    const int C = static_cast<int>(std::min<int64_t>(std::min<int64_t>(P.opt_chunks, B->ntasks), by_size));
+    // per-chunk element ranges of every param (from the host records of the first run)
+    std::vector<int64_t> ext(np);
+    for (const auto& kp : kd.params) {
+        if (kp.tensor_index < 0) continue;
+        const TensorArg& ta = node.tensor_args[node.param_to_arg[kp.tensor_index]];
+        const TensorBinding& tb = T[ta.tensor];
+        int64_t s3 = 0, s4 = 1;
+        if (ta.view_rank >= 2) {
+            s3 = tb.strides[ta.base_rank - ta.view_rank];
+            s4 = tb.strides[ta.base_rank - ta.view_rank + 1];
+        } else if (ta.view_rank == 1) {
+            s4 = tb.strides[ta.base_rank - 1];
+        }
+        ext[kp.tensor_index] = (kp.v.rows - 1) * s3 + (kp.v.cols - 1) * s4 + 1;
+    }
+    if (B->chunk_n != C) {
+        // the host records of a cached task table are dropped after its first run: read them back once
+        std::vector<int64_t> back;
+        const int64_t* rec = B->rec.data();
+        if (B->rec.empty()) {
+            back.resize(static_cast<size_t>(B->ntasks) * B->stride);
+            PW_CUDA(cudaMemcpyAsync(back.data(), L.rec_dev + B->dev_off, back.size() * sizeof(int64_t),
+                                    cudaMemcpyDeviceToHost, P.stream));
+            PW_CUDA(cudaStreamSynchronize(P.stream));
+            rec = back.data();
+        }
+        B->chunk_ranges.assign(static_cast<size_t>(C) * np * 2, 0);
+        for (int c = 0; c < C; ++c) {
+            const int64_t t0 = B->ntasks * c / C, t1 = B->ntasks * (c + 1) / C;
+            for (int ti = 0; ti < np; ++ti) {
+                int64_t lo = INT64_MAX, hi = 0;
+                for (int64_t t = t0; t < t1; ++t) {
+                    const int64_t off = rec[t * B->stride + ti];
+                    lo = std::min(lo, off);
+                    hi = std::max(hi, off + ext[ti]);
+                }
+                B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2] = lo;
+                B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2 + 1] = hi;
+            }
+        }
+        B->chunk_n = C;
+    }
+    auto range = [&](int c, int ti, int k) { return B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2 + k]; };
+    for (int ti = 0; ti < np; ++ti)  // ranges must stay inside the tensors
+        for (int c = 0; c < C; ++c)
+            if (range(c, ti, 0) < 0 || range(c, ti, 1) > T[tens[ti]].span) return false;
+
+    if (!P.h2d_stream) {
+        PW_CUDA(cudaStreamCreateWithFlags(&P.h2d_stream, cudaStreamNonBlocking));
+        PW_CUDA(cudaStreamCreateWithFlags(&P.d2h_stream, cudaStreamNonBlocking));
+    }
+    while (P.pipe_events.size() < static_cast<size_t>(2 * C + 2)) {
+        cudaEvent_t e;
+        PW_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        P.pipe_events.push_back(e);
+    }
+    cudaEvent_t ev_start = P.pipe_events[2 * C], ev_end = P.pipe_events[2 * C + 1];
+    PW_CUDA(cudaEventRecord(ev_start, P.stream));  // copies wait for earlier work on the compute stream
+    PW_CUDA(cudaStreamWaitEvent(P.h2d_stream, ev_start, 0));
+    PW_CUDA(cudaStreamWaitEvent(P.d2h_stream, ev_start, 0));
+    // inputs are copied once: the staged part of each tensor is kept one interval [lo, hi), grown on both sides
+    std::vector<int64_t> staged_lo(T.size(), 0), staged_hi(T.size(), -1);
+    PW_CUDA(cudaEventRecord(P.ev0, P.stream));
+    for (int c = 0; c < C; ++c) {
+        for (int ti = 0; ti < np; ++ti) {
+            TensorBinding& tb = T[tens[ti]];
+            if (tb.on_device || !ki.param_read[ti]) continue;
+            const size_t eb = tb.bytes / static_cast<size_t>(std::max<int64_t>(tb.span, 1));
+            int64_t& s_lo = staged_lo[tens[ti]];
+            int64_t& s_hi = staged_hi[tens[ti]];
+            const int64_t lo = range(c, ti, 0), hi = range(c, ti, 1);
+            auto copy_in = [&](int64_t a, int64_t b) {
+                if (b <= a) return;
+                PW_CUDA(cudaMemcpyAsync(tb.dev + a * eb, static_cast<char*>(tb.user_ptr) + a * eb, (b - a) * eb,
+                                        cudaMemcpyHostToDevice, P.h2d_stream));
+                P.timing.h2d_bytes += (b - a) * eb;
+            };
+            if (s_hi < 0) {
+                copy_in(lo, hi);
+                s_lo = lo;
+                s_hi = hi;
+            } else {
+                if (lo < s_lo) copy_in(lo, s_lo);  // gaps are filled so the staged part stays one interval
+                if (hi > s_hi) copy_in(s_hi, hi);
+                s_lo = std::min(s_lo, lo);
+                s_hi = std::max(s_hi, hi);
+            }
+        }
+        PW_CUDA(cudaEventRecord(P.pipe_events[2 * c], P.h2d_stream));
+        PW_CUDA(cudaStreamWaitEvent(P.stream, P.pipe_events[2 * c], 0));
+        Batch part;
+        part.kernel = B->kernel;
+        part.node = B->node;
+        part.stride = B->stride;
+        part.aligned_rows = B->aligned_rows;
+        part.fast_ok = B->fast_ok;
+        const int64_t t0 = B->ntasks * c / C, t1 = B->ntasks * (c + 1) / C;
+        part.ntasks = t1 - t0;
+        part.dev_off = B->dev_off + static_cast<size_t>(t0) * B->stride;
+        launch_batch(P, part, node, T, L.rec_dev, launches);
+        PW_CUDA(cudaEventRecord(P.pipe_events[2 * c + 1], P.stream));
+        PW_CUDA(cudaStreamWaitEvent(P.d2h_stream, P.pipe_events[2 * c + 1], 0));
+        for (int ti = 0; ti < np; ++ti) {
+            TensorBinding& tb = T[tens[ti]];
+            if (tb.on_device || !ki.param_write[ti]) continue;
+            const int64_t lo = range(c, ti, 0), hi = range(c, ti, 1);
+            const size_t eb = tb.bytes / static_cast<size_t>(std::max<int64_t>(tb.span, 1));
+            PW_CUDA(cudaMemcpyAsync(static_cast<char*>(tb.user_ptr) + lo * eb, tb.dev + lo * eb, (hi - lo) * eb,
+                                    cudaMemcpyDeviceToHost, P.d2h_stream));
+            P.timing.d2h_bytes += (hi - lo) * eb;
+        }
+    }
+    PW_CUDA(cudaEventRecord(P.ev1, P.stream));
+    PW_CUDA(cudaEventRecord(ev_end, P.d2h_stream));
+    PW_CUDA(cudaStreamWaitEvent(P.stream, ev_end, 0));  // the run's final sync on the compute stream covers the copies
+    return true;
+}
+
 }  // namespace
 
 uint64_t run_program(Program& P, RuntimeContext* ctx) {
@@ -855,8 +1016,39 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         return L->makespan;
     }
 
+    // ---- overlapped copy / compute for host-staged single-batch workloads ----
+    bool pipelined = false;
+    if (L && !all_device) {
+        if (replay || P.cacheable) {
+            if (!replay) {
+                // records must be on the device before any chunk launches
+                size_t need = 0;
+                for (auto& w : L->waves)
+                    for (auto& b : w.batches) need += b.rec.size();
+                if (need > L->rec_cap) {
+                    PW_CUDA(cudaMalloc(&L->rec_dev, need * sizeof(int64_t)));
+                    L->rec_cap = need;
+                }
+                for (auto& w : L->waves)
+                    for (auto& b : w.batches) {
+                        b.dev_off = L->rec_elems;
+                        if (!b.rec.empty())
+                            PW_CUDA(cudaMemcpyAsync(L->rec_dev + b.dev_off, b.rec.data(), b.rec.size() * sizeof(int64_t),
+                                                    cudaMemcpyHostToDevice, P.stream));
+                        L->rec_elems += b.rec.size();
+                    }
+                launched_waves = L->waves.size();  // records uploaded: the generic path must not upload again
+            }
+            pipelined = run_pipelined(P, *L, T, launches);
+            if (!pipelined && !replay) {
+                // not pipelined after all: launch what was uploaded the ordinary way below
+                replay = true;
+            }
+        }
+    }
+
     // ---- stage host tensors into HBM ----
-    for (size_t tid = 0; tid < T.size(); ++tid) {
+    for (size_t tid = 0; tid < T.size() && !pipelined; ++tid) {
         TensorBinding& b = T[tid];
         if (b.on_device || b.bytes == 0) continue;
         // Host tensors a task touches are staged in -- outputs too, unless the
@@ -869,8 +1061,10 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         }
     }
 
-    PW_CUDA(cudaEventRecord(P.ev0, P.stream));
-    if (replay) {
+    if (!pipelined) PW_CUDA(cudaEventRecord(P.ev0, P.stream));
+    if (pipelined) {
+        // kernels and copies were enqueued by run_pipelined
+    } else if (replay) {
         for (size_t wi = 0; wi < L->waves.size(); ++wi)
             for (auto& b : L->waves[wi].batches) launch_batch(P, b, *b.node, T, L->rec_dev, launches);
     } else if (P.cacheable) {
@@ -889,10 +1083,10 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         W->close_wave();
         upload_and_launch(L->waves.size());
     }
-    PW_CUDA(cudaEventRecord(P.ev1, P.stream));
+    if (!pipelined) PW_CUDA(cudaEventRecord(P.ev1, P.stream));
 
     // ---- bring written host tensors back ----
-    for (size_t tid = 0; tid < T.size(); ++tid) {
+    for (size_t tid = 0; tid < T.size() && !pipelined; ++tid) {
         TensorBinding& b = T[tid];
         if (b.on_device || !b.written || b.bytes == 0) continue;
         PW_CUDA(cudaMemcpyAsync(b.user_ptr, b.dev, b.bytes, cudaMemcpyDeviceToHost, P.stream));

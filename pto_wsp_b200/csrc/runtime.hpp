@@ -59,12 +59,15 @@ struct Batch {  // tasks of one kernel inside one wave
     int64_t* fast_rec_dev = nullptr;
     int64_t fast_ntasks = 0;
     int fast_n = 0;
+    // host-staged pipelining: per chunk and tensor param, the [lo, hi) element range its tasks touch
+    int chunk_n = 0;
+    std::vector<int64_t> chunk_ranges;
     Batch() = default;
     Batch(Batch&& o) noexcept { *this = std::move(o); }
     Batch& operator=(Batch&& o) noexcept {
         kernel = o.kernel; node = o.node; rec = std::move(o.rec); ntasks = o.ntasks; stride = o.stride;
         dev_off = o.dev_off; aligned_rows = o.aligned_rows; fast_ok = o.fast_ok; fast_rec_dev = o.fast_rec_dev;
-        fast_ntasks = o.fast_ntasks; fast_n = o.fast_n;
+        fast_ntasks = o.fast_ntasks; fast_n = o.fast_n; chunk_n = o.chunk_n; chunk_ranges = std::move(o.chunk_ranges);
         o.fast_rec_dev = nullptr;
         return *this;
     }
@@ -103,9 +106,11 @@ struct Program {
     cudaStream_t stream = nullptr;
     bool stream_set = false;           // caller chose a stream (nullptr = CUDA default stream)
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;  // copy engines of pipelined runs
+    std::vector<cudaEvent_t> pipe_events;
     int* err_dev = nullptr;
     int status = 0;
-    int64_t opt_cache = 1, opt_chunks = 4, opt_sync = 1, opt_dry = 0;
+    int64_t opt_cache = 1, opt_chunks = 32, opt_sync = 1, opt_dry = 0;
     std::vector<char*> dev_bufs;         // host-staged tensor buffers (by tensor id)
     std::vector<size_t> dev_caps;
     void* scratch = nullptr;
