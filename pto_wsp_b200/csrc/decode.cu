@@ -7,13 +7,15 @@
 // (examples/flashinfer_decode/pto_wsp_impl.py:38-54, golden.py:7-12):
 // softmax(q K^T / sqrt(D)) V, f32 softmax, f16 output (round to nearest even).
 //
-// HBM-bound: every K/V byte is used for 2*G FLOP (G = 4: ~4 FLOP/B), below the
-// CUDA-core ridge, so this runs on CUDA cores, not tensor cores.  Split-KV:
-// each task is cut into 512-token chunks (one CTA each, empty chunks exit at
-// once); a chunk computes its scores lane-per-token (K rows read once, L1
-// cached), softmax statistics, then P.V lane-per-dimension (V rows read
-// coalesced), and writes (max, sum, acc[G][128]) to scratch; a second kernel
-// merges the chunks of a task with the log-sum-exp rule and stores f16.
+// HBM-bound: every K/V byte is used for 2*G FLOP (G = 4: ~4 FLOP/B).
+// Split-KV: each task is cut into 512-token chunks (one CTA each, empty
+// chunks exit at once).  For the usual pool layout (16-token pages, 16-byte
+// aligned rows) a TMA producer warp streams the pages and four consumer warps
+// run both contractions of a page on warp-level MMAs (paged_decode_tma_kernel,
+// below); the last CTA of a task merges its chunk partials.  Other layouts use
+// a CUDA-core kernel (scores lane-per-token, P.V lane-per-dimension) that
+// writes (max, sum, acc[G][128]) per chunk, merged by a second kernel with
+// the log-sum-exp rule.  Both store f16.
 //
 // topk_select -- indices of the K largest of N scores, ordered by score
 // descending, ties by lower index (examples/deepseek_lightning_indexer/
@@ -255,62 +257,87 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBat
 }
 
 // ---------------------------------------------------------------------------
-// TMA-fed variant (the default for contiguous 16-token page pools).  A producer
-// warp streams, page by page, the task's head slice of K and V (16 rows x 256 B
-// each, one TMA box apiece) into an 8-stage shared-memory ring; four consumer
-// warps each own every 4th page of the chunk and run an online softmax over
-// it from shared memory (half-warp per token, lane per 8 head dims), so HBM
-// latency is hidden by the ring instead of by thread count.  The warps'
-// (max, sum, acc) are combined with the log-sum-exp rule into the same chunk
-// partial the merge kernel reads.  Bounded waits; the producer drains its
-// copies before the CTA exits.
+// TMA + warp-MMA variant (the default for contiguous 16-token page pools).
+//
+// A producer warp streams, page by page, the task's head slice of K and V
+// into an 8-stage shared-memory ring: per page four TMA boxes of 16 tokens x
+// 64 dims (2 KB each, 128-byte swizzled so the fragment loads below are free
+// of bank conflicts).  Four consumer warps each own every 4th page of the
+// chunk.  Per page a warp computes S^T = K Q^T (16 tokens x 8 queries, the G
+// real queries padded to 8) with 8 m16n8k16 f16 MMAs, updates its online
+// softmax (base-2, scores pre-scaled by log2(e)/sqrt(D)), and accumulates
+// O^T += V^T P^T (128 dims x 8 queries) with 8 more; P goes through a
+// 256-byte per-warp buffer to change from accumulator to operand layout.
+// The contraction per page (16 tokens x G <= 8 queries) is far below the
+// 64/128-row minimum of a tcgen05 tile, so warp-level MMAs are the tool here;
+// they cut the per-page instruction count about eightfold against CUDA-core
+// dot products, which leaves the kernel bound by HBM, not issue.
+//
+// Chunks of one task are merged by the last of its CTAs to finish (a
+// per-task arrival counter, zeroed before each launch): partials go to
+// scratch, the last arriving CTA combines them in chunk order (so the result
+// does not depend on which CTA came last) and stores f16.  A task with one
+// chunk stores directly.  Bounded waits; the producer drains its copies
+// before the CTA exits; every CTA that has work arrives on its counter, also
+// after a timed-out wait.
 // ---------------------------------------------------------------------------
 
-constexpr int kTmaStages = 8;
-constexpr int kTmaConsumers = 4;
-constexpr int kTmaThreads = 32 * (kTmaConsumers + 1);
-constexpr int kTmaPage = 16;
-constexpr int kTmaPageBytes = kTmaPage * kHeadDim * 2;  // 4 KB
+constexpr int kMmaStages = 8;
+constexpr int kMmaConsumers = 4;
+constexpr int kMmaThreads = 32 * (kMmaConsumers + 1);
+constexpr int kMmaPage = 16;
+constexpr int kHalfBox = kMmaPage * 64 * 2;   // 16 tokens x 64 dims f16 = 2 KB
+constexpr int kStageBytes = 4 * kHalfBox;     // K lo, K hi, V lo, V hi
+constexpr int kRingBytes = kMmaStages * kStageBytes;
+constexpr int kBarOffset = kRingBytes;  // full[S], empty[S], abort, last flag (136 B); the chunk's page ids at +256
+constexpr int kPbufOffset = kBarOffset + 384;                 // per-warp P buffer, 16 tokens x 8 queries f16
+constexpr int kMmaSmemBytes = kPbufOffset + kMmaConsumers * 256 + 1024;  // + 1024-byte alignment slack
 
 template <int G>
-struct TmaSmem {
-    static constexpr int RING = kTmaStages * 2 * kTmaPageBytes;                 // K and V per stage
-    static constexpr int BAR = RING;                                             // full[S], empty[S], abort
-    static constexpr int PW = BAR + 256;                                         // per-warp p[16][G]
-    static constexpr int CW = PW + kTmaConsumers * kTmaPage * G * 4;             // per-warp (m, l, acc)
-    static constexpr int CW_STRIDE = 2 * G + G * kHeadDim;                       // floats
-    static constexpr int TOTAL = CW + kTmaConsumers * CW_STRIDE * 4 + 128;       // + alignment slack
+struct MmaCombine {  // per consumer warp, aliased onto the ring once every page has been consumed
+    static constexpr int STRIDE = 2 * G + G * kHeadDim;  // m[G], l[G], acc[G][128] (floats)
+    static_assert(kMmaConsumers * STRIDE * 4 <= kRingBytes, "combine area fits in the ring");
 };
 
-// Sum V per-lane values over the 16 lanes of a half-warp; afterwards lane l
-// holds V/16 totals, for value indices (V/16) * (l & 15) + j.
-template <int V>
-__device__ __forceinline__ void halfwarp_transpose_reduce_v(float (&v)[V], int lane) {
-#pragma unroll
-    for (int n = V, o = 8; o >= 1; n >>= 1, o >>= 1) {
-        const bool up = (lane & o) != 0;
-#pragma unroll
-        for (int i = 0; i < n / 2; ++i) {
-            const float send = up ? v[i] : v[i + n / 2];
-            const float keep = up ? v[i + n / 2] : v[i];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-    }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+// D (16x8 f32) += A (16x16 f16, row) * B (16x8 f16, col)
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// Byte offset of (token, dim) inside one page's 128-byte-swizzled K or V slice.
+__device__ __forceinline__ uint32_t swz(int tok, int d) {
+    return static_cast<uint32_t>((d >> 6) * kHalfBox + tok * 128 + ((((d & 63) >> 3) ^ (tok & 7)) << 4));
 }
 
 template <int G>
-__global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap mk,
+__global__ void __launch_bounds__(kMmaThreads) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap mk,
                                                                      const __grid_constant__ CUtensorMap mv, TaskBatch b,
-                                                                     int chunks, float* __restrict__ scratch) {
-    using S = TmaSmem<G>;
-    constexpr int V = 8 * G;      // partial dot products per lane per page (8 tokens x G queries)
-    constexpr int PER = V / 16;   // totals per lane after the reduction
-    static_assert(V >= 16, "GQA group of at least 2");
+                                                                     int chunks, float* __restrict__ partials,
+                                                                     unsigned* __restrict__ arrivals) {
+    using CB = MmaCombine<G>;
     extern __shared__ uint8_t dsm_raw[];
-    uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 127) & ~uintptr_t(127));
-    uint64_t* full = reinterpret_cast<uint64_t*>(dsm + S::BAR);
-    uint64_t* empty = full + kTmaStages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kTmaStages);
+    uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(dsm + kBarOffset);
+    uint64_t* empty = full + kMmaStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMmaStages);
+    volatile int* last_flag = abort_flag + 1;
 
     const int64_t task = blockIdx.x / chunks;
     const int chunk = blockIdx.x % chunks;
@@ -321,18 +348,25 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(const __g
     const ParamDesc& Pl = b.p[4];
     const int h = static_cast<int>(rec[b.nparams + 1]);
     int32_t L = reinterpret_cast<const int32_t*>(Pl.base)[rec[4]];
-    if (L > Ppt.cols * kTmaPage) {
+    if (L > Ppt.cols * kMmaPage) {
         if (chunk == 0 && threadIdx.x == 0) atomicOr(b.err, kErrShape);
-        L = Ppt.cols * kTmaPage;
+        L = Ppt.cols * kMmaPage;
     }
     const int t0 = chunk * kChunk;
+    if (L <= 0 && chunk == 0) {  // no cached tokens: the output is zero
+        __half* out = reinterpret_cast<__half*>(b.p[5].base) + rec[5];
+        for (int e = threadIdx.x; e < G * kHeadDim; e += kMmaThreads)
+            out[(e / kHeadDim) * b.p[5].s3 + e % kHeadDim] = __float2half_rn(0.f);
+        return;
+    }
     if (t0 >= L) return;  // whole CTA leaves together: no barrier has been touched
+    const int nch = (L + kChunk - 1) / kChunk;
     const int n = min(kChunk, L - t0);
-    const int npages = (n + kTmaPage - 1) / kTmaPage;
+    const int npages = (n + kMmaPage - 1) / kMmaPage;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int st = 0; st < kTmaStages; ++st) {
+        for (int st = 0; st < kMmaStages; ++st) {
             tc::mbar_init(tc::smem_u32(&full[st]), 1);
             tc::mbar_init(tc::smem_u32(&empty[st]), 1);
         }
@@ -341,33 +375,55 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(const __g
     }
     __syncthreads();
 
-    if (warp == kTmaConsumers) {
+    // consumer state: lane = (g = lane / 4, tq = lane % 4); this lane's queries are 2tq and 2tq+1
+    const int g = lane >> 2, tq = lane & 3;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[8][4];
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[mt][k] = 0.f;
+
+    if (warp == kMmaConsumers) {
         // ---------------- producer ----------------
-        if (lane == 0) {
+        // the chunk's page ids (at most 32) are fetched at once, one per lane, and handed to lane 0 in shared memory
+        static_assert(kChunk / kMmaPage <= 32, "one page id per producer lane");
+        int* page_ids = reinterpret_cast<int*>(dsm + kBarOffset + 256);
+        {
             const int32_t* pt = reinterpret_cast<const int32_t*>(Ppt.base) + rec[3];
-            const int64_t max_page = b.p[1].numel_span / (int64_t(kTmaPage) * b.p[1].s4) - 1;
-            int issued = 0;
-            for (int j = 0; j < npages && !*abort_flag; ++j) {
-                const int st = j % kTmaStages;
-                if (j >= kTmaStages &&
-                    !tc::mbar_wait(tc::smem_u32(&empty[st]), ((j / kTmaStages) - 1) & 1, abort_flag, b.err))
-                    break;
-                int64_t page = pt[static_cast<int64_t>(t0 / kTmaPage + j) * Ppt.s4];
+            const int64_t max_page = b.p[1].numel_span / (int64_t(kMmaPage) * b.p[1].s4) - 1;
+            if (lane < npages) {
+                int64_t page = pt[static_cast<int64_t>(t0 / kMmaPage + lane) * Ppt.s4];
                 if (page < 0 || page > max_page) {
                     atomicOr(b.err, kErrBounds);
                     page = 0;
                 }
+                page_ids[lane] = static_cast<int>(page);
+            }
+            __syncwarp();
+        }
+        if (lane == 0) {
+            int issued = 0;
+            for (int j = 0; j < npages && !*abort_flag; ++j) {
+                const int st = j % kMmaStages;
+                if (j >= kMmaStages &&
+                    !tc::mbar_wait(tc::smem_u32(&empty[st]), ((j / kMmaStages) - 1) & 1, abort_flag, b.err))
+                    break;
+                const int64_t page = page_ids[j];
                 const uint32_t fb = tc::smem_u32(&full[st]);
-                tc::mbar_expect_tx(fb, 2 * kTmaPageBytes);
-                uint8_t* kd = dsm + st * 2 * kTmaPageBytes;
-                tc::tma_load_2d(tc::smem_u32(kd), &mk, h * kHeadDim, static_cast<int32_t>(page * kTmaPage), fb);
-                tc::tma_load_2d(tc::smem_u32(kd + kTmaPageBytes), &mv, h * kHeadDim, static_cast<int32_t>(page * kTmaPage), fb);
+                tc::mbar_expect_tx(fb, kStageBytes);
+                const uint32_t dst = tc::smem_u32(dsm + st * kStageBytes);
+                const int32_t y = static_cast<int32_t>(page * kMmaPage);
+                tc::tma_load_2d(dst, &mk, h * kHeadDim, y, fb);
+                tc::tma_load_2d(dst + kHalfBox, &mk, h * kHeadDim + 64, y, fb);
+                tc::tma_load_2d(dst + 2 * kHalfBox, &mv, h * kHeadDim, y, fb);
+                tc::tma_load_2d(dst + 3 * kHalfBox, &mv, h * kHeadDim + 64, y, fb);
                 ++issued;
             }
             // drain: the last copy into each stage has landed
             const uint64_t start = tc::globaltimer();
-            for (int j = max(0, issued - kTmaStages); j < issued; ++j)
-                while (!tc::mbar_try_wait(tc::smem_u32(&full[j % kTmaStages]), (j / kTmaStages) & 1))
+            for (int j = max(0, issued - kMmaStages); j < issued; ++j)
+                while (!tc::mbar_try_wait(tc::smem_u32(&full[j % kMmaStages]), (j / kMmaStages) & 1))
                     if (tc::globaltimer() - start > tc::kTimeoutNs) {
                         atomicOr(b.err, kErrTimeout);
                         break;
@@ -375,155 +431,157 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(const __g
         }
     } else {
         // ---------------- consumers ----------------
-        const int hl = lane & 15, hh = lane >> 4;
-        float qf[G][8];
+        // Q^T as the B operand of S^T = K Q^T: b0 = Q[g][16kk + 2tq .. +1], b1 = Q[g][16kk + 2tq + 8 .. +9]
+        uint32_t qb[8][2];
         {
-            const __half* q = reinterpret_cast<const __half*>(Pq.base) + rec[0];
-            const float scale = 1.0f / sqrtf(static_cast<float>(kHeadDim));
+            const __half* q = reinterpret_cast<const __half*>(Pq.base) + rec[0] + static_cast<int64_t>(g) * Pq.s3;
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                h8_to_f8(*reinterpret_cast<const uint4*>(q + g * Pq.s3 + hl * 8), qf[g]);
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) qf[g][jj] *= scale;
+            for (int kk = 0; kk < 8; ++kk) {
+                qb[kk][0] = g < G ? *reinterpret_cast<const uint32_t*>(q + 16 * kk + 2 * tq) : 0u;
+                qb[kk][1] = g < G ? *reinterpret_cast<const uint32_t*>(q + 16 * kk + 2 * tq + 8) : 0u;
             }
         }
-        float m[G], l[G], acc[G][8];
+        const float sc = 1.4426950408889634f / sqrtf(static_cast<float>(kHeadDim));  // log2(e) / sqrt(D)
+        uint8_t* pbuf = dsm + kPbufOffset + warp * 256;
+        const uint32_t pbuf_u = tc::smem_u32(pbuf);
+        const int mi = lane >> 3, r8 = lane & 7;
+        for (int j = warp; j < npages && !*abort_flag; j += kMmaConsumers) {
+            const int st = j % kMmaStages;
+            if (!tc::mbar_wait(tc::smem_u32(&full[st]), (j / kMmaStages) & 1, abort_flag, b.err)) break;
+            const uint32_t kb = tc::smem_u32(dsm + st * kStageBytes);
+            const uint32_t vb = kb + 2 * kHalfBox;
+            const int valid = min(kMmaPage, n - j * kMmaPage);
+            // S^T (16 tokens x 8 queries): A = K rows (token-major), 8 k-steps over the head dims
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            m[g] = -INFINITY;
-            l[g] = 0.f;
+            for (int kk = 0; kk < 8; ++kk) {
+                uint32_t a[4];
+                ldsm_x4(kb + swz(r8 + 8 * (mi & 1), 16 * kk + 8 * (mi >> 1)), a);
+                mma_16816(s, a, qb[kk][0], qb[kk][1]);
+            }
+            // s[0], s[1]: token g, queries 2tq, 2tq+1; s[2], s[3]: token g+8
+            const float s00 = g < valid ? s[0] * sc : -INFINITY;
+            const float s01 = g < valid ? s[1] * sc : -INFINITY;
+            const float s10 = g + 8 < valid ? s[2] * sc : -INFINITY;
+            const float s11 = g + 8 < valid ? s[3] * sc : -INFINITY;
+            float x0 = fmaxf(s00, s10), x1 = fmaxf(s01, s11);
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) acc[g][jj] = 0.f;
-        }
-        float* pw = reinterpret_cast<float*>(dsm + S::PW) + warp * kTmaPage * G;
-        for (int j = warp; j < npages && !*abort_flag; j += kTmaConsumers) {
-            const int st = j % kTmaStages;
-            if (!tc::mbar_wait(tc::smem_u32(&full[st]), (j / kTmaStages) & 1, abort_flag, b.err)) break;
-            const uint8_t* ksm = dsm + st * 2 * kTmaPageBytes;
-            const uint8_t* vsm = ksm + kTmaPageBytes;
-            const int valid = min(kTmaPage, n - j * kTmaPage);
-            // scores of this half-warp's 8 tokens
-            float part[V];
+            for (int off = 4; off < 32; off <<= 1) {
+                x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, off));
+                x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
+            }
+            const float mn0 = fmaxf(m0, x0), mn1 = fmaxf(m1, x1);  // finite: token 0 of a page is always valid
+            const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+            const float p00 = exp2f(s00 - mn0), p10 = exp2f(s10 - mn0);
+            const float p01 = exp2f(s01 - mn1), p11 = exp2f(s11 - mn1);
+            l0 = fmaf(l0, c0, p00 + p10);
+            l1 = fmaf(l1, c1, p01 + p11);
+            m0 = mn0;
+            m1 = mn1;
+            if (__any_sync(0xffffffffu, c0 != 1.f || c1 != 1.f)) {
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                float kf[8];
-                h8_to_f8(*reinterpret_cast<const uint4*>(ksm + (hh * 8 + t) * 256 + hl * 16), kf);
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    float a = 0.f;
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) a = fmaf(kf[jj], qf[g][jj], a);
-                    part[t * G + g] = a;
+                for (int mt = 0; mt < 8; ++mt) {
+                    o[mt][0] *= c0;
+                    o[mt][1] *= c1;
+                    o[mt][2] *= c0;
+                    o[mt][3] *= c1;
                 }
             }
-            halfwarp_transpose_reduce_v<V>(part, hl);
-            // this lane now holds scores of value indices PER*hl + k (token = idx / G, query = idx % G)
-            float pmax[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) pmax[g] = -INFINITY;
-#pragma unroll
-            for (int k = 0; k < PER; ++k) {
-                const int idx = PER * hl + k;
-                if (hh * 8 + idx / G >= valid) part[k] = -INFINITY;  // past the last token of the chunk
-                const int gk = idx % G;
-#pragma unroll
-                for (int g = 0; g < G; ++g) pmax[g] = fmaxf(pmax[g], gk == g ? part[k] : -INFINITY);  // selects only
-            }
-            float corr[G], mnew[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float x = pmax[g];
-                for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
-                mnew[g] = fmaxf(m[g], x);
-                corr[g] = expf(m[g] - mnew[g]);  // 0 on the first page (m = -inf)
-            }
-            float psum[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) psum[g] = 0.f;
-#pragma unroll
-            for (int k = 0; k < PER; ++k) {
-                const int idx = PER * hl + k;
-                const int tok = hh * 8 + idx / G;
-                const int gk = idx % G;
-                float mk = mnew[0];
-#pragma unroll
-                for (int g = 1; g < G; ++g) mk = gk == g ? mnew[g] : mk;
-                const float pg = expf(part[k] - mk);
-#pragma unroll
-                for (int g = 0; g < G; ++g) psum[g] += gk == g ? pg : 0.f;
-                pw[tok * G + gk] = pg;
-            }
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float x = psum[g];
-                for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-                l[g] = l[g] * corr[g] + x;
-                m[g] = mnew[g];
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) acc[g][jj] *= corr[g];
-            }
+            // P (token-major, 16 B per token row) -> B operand P^T via a transposing fragment load
+            *reinterpret_cast<uint32_t*>(pbuf + g * 16 + tq * 4) = pack_h2(p00, p01);
+            *reinterpret_cast<uint32_t*>(pbuf + (g + 8) * 16 + tq * 4) = pack_h2(p10, p11);
             __syncwarp();
+            uint32_t pb0, pb1;
+            ldsm_x2_t(pbuf_u + (lane & 15) * 16, pb0, pb1);
+            // O^T (128 dims x 8 queries) += V^T P^T: A = V^T through transposing loads of the token-major rows
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const int tok = hh * 8 + t;
-                float vf[8];
-                h8_to_f8(*reinterpret_cast<const uint4*>(vsm + tok * 256 + hl * 16), vf);
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float pg = pw[tok * G + g];
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) acc[g][jj] = fmaf(pg, vf[jj], acc[g][jj]);
-                }
+            for (int mt = 0; mt < 8; ++mt) {
+                uint32_t a[4];
+                ldsm_x4_t(vb + swz(r8 + 8 * (mi >> 1), 16 * mt + 8 * (mi & 1)), a);
+                mma_16816(o[mt], a, pb0, pb1);
             }
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(tc::smem_u32(&empty[st]));
         }
-        // the two half-warps saw different tokens of the same pages: add them
+        // per-lane sums of the same query live in the 8 lanes of equal tq
 #pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) acc[g][jj] += __shfl_xor_sync(0xffffffffu, acc[g][jj], 16);
-        float* cw = reinterpret_cast<float*>(dsm + S::CW) + warp * S::CW_STRIDE;
-        if (lane < 16) {
-#pragma unroll
-            for (int g = 0; g < G; ++g)
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) cw[2 * G + g * kHeadDim + hl * 8 + jj] = acc[g][jj];
+        for (int off = 4; off < 32; off <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
         }
-        if (lane == 0) {
+    }
+    __syncthreads();  // every page consumed and every copy landed: the ring is free for the combine area
+    if (warp < kMmaConsumers) {
+        float* cw = reinterpret_cast<float*>(dsm) + warp * CB::STRIDE;
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                cw[g] = m[g];
-                cw[G + g] = l[g];
+        for (int k = 0; k < 2; ++k) {
+            const int q = 2 * tq + k;
+            if (q < G) {
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    cw[2 * G + q * kHeadDim + 16 * mt + g] = o[mt][k];
+                    cw[2 * G + q * kHeadDim + 16 * mt + g + 8] = o[mt][2 + k];
+                }
+                if (g == 0) {
+                    cw[q] = k ? m1 : m0;
+                    cw[G + q] = k ? l1 : l0;
+                }
             }
         }
     }
     __syncthreads();
-    // ---- combine the consumer warps -> chunk partial (same format as the non-TMA kernel) ----
-    const float* cw0 = reinterpret_cast<const float*>(dsm + S::CW);
-    float* part_out = scratch + static_cast<int64_t>(blockIdx.x) * (G * kHeadDim + 2 * G);
-    for (int e = threadIdx.x; e < G * kHeadDim; e += kTmaThreads) {
-        const int g = e / kHeadDim;
+    // ---- combine the consumer warps (log-sum-exp, base 2) ----
+    const float* cw0 = reinterpret_cast<const float*>(dsm);
+    const int pstride = G * kHeadDim + 2 * G;
+    __half* out = reinterpret_cast<__half*>(b.p[5].base) + rec[5];
+    const int64_t os3 = b.p[5].s3;
+    float* part = partials + static_cast<int64_t>(blockIdx.x) * pstride;
+    for (int e = threadIdx.x; e < G * kHeadDim + G; e += kMmaThreads) {
+        const int gq = e < G * kHeadDim ? e / kHeadDim : e - G * kHeadDim;
         float M = -INFINITY;
-        for (int w = 0; w < kTmaConsumers; ++w) M = fmaxf(M, cw0[w * S::CW_STRIDE + g]);
-        float a = 0.f;
-        for (int w = 0; w < kTmaConsumers; ++w) {
-            const float mw = cw0[w * S::CW_STRIDE + g];
-            if (mw != -INFINITY) a = fmaf(cw0[w * S::CW_STRIDE + 2 * G + e], expf(mw - M), a);
+#pragma unroll
+        for (int w = 0; w < kMmaConsumers; ++w) M = fmaxf(M, cw0[w * CB::STRIDE + gq]);
+        float a = 0.f, lt = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMmaConsumers; ++w) {
+            const float mw = cw0[w * CB::STRIDE + gq];
+            if (mw != -INFINITY) {
+                const float f = exp2f(mw - M);
+                if (e < G * kHeadDim) a = fmaf(cw0[w * CB::STRIDE + 2 * G + e], f, a);
+                lt = fmaf(cw0[w * CB::STRIDE + G + gq], f, lt);
+            }
         }
-        part_out[e] = a;
+        if (nch == 1) {
+            if (e < G * kHeadDim) out[gq * os3 + e % kHeadDim] = __float2half_rn(a / lt);
+        } else if (e < G * kHeadDim) {
+            part[e] = a;
+        } else {
+            part[G * kHeadDim + gq] = M;
+            part[G * kHeadDim + G + gq] = lt;
+        }
     }
-    if (threadIdx.x < G) {
-        const int g = threadIdx.x;
+    if (nch == 1) return;
+    // ---- the last CTA of the task to arrive merges its chunks ----
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) *last_flag = atomicAdd(&arrivals[task], 1u) == static_cast<unsigned>(nch - 1);
+    __syncthreads();
+    if (!*last_flag) return;
+    __threadfence();
+    const float* base = partials + task * chunks * static_cast<int64_t>(pstride);
+    for (int e = threadIdx.x; e < G * kHeadDim; e += kMmaThreads) {
+        const int gq = e / kHeadDim;
         float M = -INFINITY;
-        for (int w = 0; w < kTmaConsumers; ++w) M = fmaxf(M, cw0[w * S::CW_STRIDE + g]);
-        float lt = 0.f;
-        for (int w = 0; w < kTmaConsumers; ++w) {
-            const float mw = cw0[w * S::CW_STRIDE + g];
-            if (mw != -INFINITY) lt = fmaf(cw0[w * S::CW_STRIDE + G + g], expf(mw - M), lt);
+        for (int c = 0; c < nch; ++c) M = fmaxf(M, __ldcg(base + c * pstride + G * kHeadDim + gq));
+        float num = 0.f, den = 0.f;
+        for (int c = 0; c < nch; ++c) {
+            const float mc = __ldcg(base + c * pstride + G * kHeadDim + gq);
+            if (mc == -INFINITY) continue;
+            const float w = exp2f(mc - M);
+            num = fmaf(__ldcg(base + c * pstride + e), w, num);
+            den = fmaf(__ldcg(base + c * pstride + G * kHeadDim + G + gq), w, den);
         }
-        part_out[G * kHeadDim + g] = M;
-        part_out[G * kHeadDim + G + g] = lt;
+        out[gq * os3 + e % kHeadDim] = __float2half_rn(num / den);
     }
 }
 
@@ -558,13 +616,17 @@ int decode_chunks(const TaskBatch& b, int page_size) {
     return static_cast<int>(std::max<int64_t>(1, (max_tokens + kChunk - 1) / kChunk));
 }
 
-bool decode_tma_ok(const TaskBatch& b, int page_size, int group) {
+bool decode_tma_ok(const TaskBatch& b, int page_size) {
     const ParamDesc& K = b.p[1];
     const ParamDesc& V = b.p[2];
-    return group >= 2 && page_size == kTmaPage && K.s3 == kTmaPage * K.s4 && V.s3 == kTmaPage * V.s4 &&
-           K.s4 == V.s4 && K.s4 % 8 == 0 && K.s4 >= kHeadDim &&
-           ((reinterpret_cast<uintptr_t>(K.base) | reinterpret_cast<uintptr_t>(V.base)) & 15) == 0;
+    return page_size == kMmaPage && K.s3 == kMmaPage * K.s4 && V.s3 == kMmaPage * V.s4 && K.s4 == V.s4 &&
+           K.s4 % 64 == 0 && K.s4 >= kHeadDim && b.p[0].s3 % 2 == 0 &&
+           ((reinterpret_cast<uintptr_t>(K.base) | reinterpret_cast<uintptr_t>(V.base)) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(b.p[0].base) & 3) == 0;
 }
+
+// Scratch of one decode launch: [arrival counters, one per task, 256-byte padded | chunk partials].
+size_t decode_arrivals_bytes(int64_t ntasks) { return (static_cast<size_t>(ntasks) * sizeof(unsigned) + 255) & ~size_t(255); }
 
 template <int G>
 cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cudaStream_t s) {
@@ -572,31 +634,30 @@ cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cu
     const int64_t grid = b.ntasks * chunks;
     if (grid <= 0) return cudaSuccess;
     if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-    bool launched = false;
-    if constexpr (G >= 2) {
-        if (decode_tma_ok(b, page_size, G)) {
-            const ParamDesc& K = b.p[1];
-            const ParamDesc& V = b.p[2];
-            CUtensorMap mk, mv;
-            const uint64_t krows = (K.numel_span + K.s4 - 1) / K.s4, vrows = (V.numel_span + V.s4 - 1) / V.s4;
-            if (tc::make_map_f16_plain(&mk, K.base, K.s4, krows, K.s4 * 2, kHeadDim, kTmaPage) &&
-                tc::make_map_f16_plain(&mv, V.base, V.s4, vrows, V.s4 * 2, kHeadDim, kTmaPage)) {
-                const int smem = TmaSmem<G>::TOTAL;
-                cudaError_t e = cudaFuncSetAttribute(paged_decode_tma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-                if (e != cudaSuccess) return e;
-                paged_decode_tma_kernel<G><<<static_cast<unsigned>(grid), kTmaThreads, smem, s>>>(
-                    mk, mv, b, chunks, static_cast<float*>(scratch));
-                launched = true;
-            }
+    unsigned* arrivals = static_cast<unsigned*>(scratch);
+    float* partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + decode_arrivals_bytes(b.ntasks));
+    if (decode_tma_ok(b, page_size)) {
+        const ParamDesc& K = b.p[1];
+        const ParamDesc& V = b.p[2];
+        CUtensorMap mk, mv;
+        const int64_t krows = (K.numel_span + K.s4 - 1) / K.s4, vrows = (V.numel_span + V.s4 - 1) / V.s4;
+        if (tc::make_map_f16(&mk, K.base, K.s4, krows, 64, kMmaPage) &&
+            tc::make_map_f16(&mv, V.base, V.s4, vrows, 64, kMmaPage)) {
+            cudaError_t e = cudaSuccess;
+            if (chunks > 1) e = cudaMemsetAsync(arrivals, 0, static_cast<size_t>(b.ntasks) * sizeof(unsigned), s);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(paged_decode_tma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kMmaSmemBytes);
+            if (e != cudaSuccess) return e;
+            paged_decode_tma_kernel<G><<<static_cast<unsigned>(grid), kMmaThreads, kMmaSmemBytes, s>>>(
+                mk, mv, b, chunks, partials, arrivals);
+            return cudaGetLastError();
         }
     }
-    if (!launched)
-        paged_decode_chunk_kernel<G><<<static_cast<unsigned>(grid), kDecThreads, 0, s>>>(b, page_size, chunks,
-                                                                                         static_cast<float*>(scratch));
+    paged_decode_chunk_kernel<G><<<static_cast<unsigned>(grid), kDecThreads, 0, s>>>(b, page_size, chunks, partials);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    paged_decode_merge_kernel<G><<<static_cast<unsigned>(b.ntasks), kDecThreads, 0, s>>>(b, page_size, chunks,
-                                                                                         static_cast<const float*>(scratch));
+    paged_decode_merge_kernel<G><<<static_cast<unsigned>(b.ntasks), kDecThreads, 0, s>>>(b, page_size, chunks, partials);
     return cudaGetLastError();
 }
 
@@ -748,7 +809,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
 
 size_t paged_decode_scratch_bytes(const TaskBatch& b, int page_size) {
     const int G = b.p[0].rows;
-    return static_cast<size_t>(b.ntasks) * decode_chunks(b, page_size) * (G * kHeadDim + 2 * G) * sizeof(float);
+    return decode_arrivals_bytes(b.ntasks) +
+           static_cast<size_t>(b.ntasks) * decode_chunks(b, page_size) * (G * kHeadDim + 2 * G) * sizeof(float);
 }
 
 cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int, int, void* scratch, size_t scratch_bytes,
@@ -876,7 +938,7 @@ size_t noalloc_bytes_needed(int requests, int kv_heads, int group, int max_pages
     const size_t tasks = static_cast<size_t>(requests) * kv_heads;
     const int64_t max_tokens = static_cast<int64_t>(max_pages) * page_size;
     const size_t chunks = static_cast<size_t>(std::max<int64_t>(1, (max_tokens + kChunk - 1) / kChunk));
-    return kNoAllocRecOffset + tasks * kNoAllocRecStride * sizeof(int64_t) +
+    return kNoAllocRecOffset + tasks * kNoAllocRecStride * sizeof(int64_t) + decode_arrivals_bytes(tasks) +
            tasks * chunks * (static_cast<size_t>(group) * kHeadDim + 2 * group) * sizeof(float);
 }
 
@@ -900,7 +962,7 @@ int paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache
     const size_t need = noalloc_bytes_needed(requests, kv_heads, group, max_pages, page_size);
     if (need > kPtowspNoAllocScratchBytes) {
         *msg = "paged_decode_noalloc: requests x kv_heads x ceil(max_pages*page_size/512) x (group*128+2*group)*4 B "
-               "of partials plus task records exceed the fixed 24 MiB scratch array";
+               "of partials plus task records and counters exceed the fixed 24 MiB scratch array";
         return 6;
     }
     int device = 0;
@@ -917,7 +979,7 @@ int paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache
     int* status = reinterpret_cast<int*>(base);
     int64_t* rec = reinterpret_cast<int64_t*>(base + kNoAllocRecOffset);
     const size_t tasks = static_cast<size_t>(requests) * kv_heads;
-    float* partials = reinterpret_cast<float*>(base + kNoAllocRecOffset + tasks * kNoAllocRecStride * sizeof(int64_t));
+    void* dec_scratch = base + kNoAllocRecOffset + tasks * kNoAllocRecStride * sizeof(int64_t);
 
     e = cudaMemsetAsync(status, 0, sizeof(int), s);  // the status word must start at zero
     if (e == cudaSuccess) {
@@ -961,10 +1023,10 @@ int paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache
     b.p[4] = param(const_cast<int32_t*>(kv_len), 0, 1, requests, 1, 1, PT_I32, 4);
     b.p[5] = param(out, kHeadDim, 1, qspan, group, kHeadDim, PT_F16, 2);
     switch (group) {
-        case 1: e = launch_decode_g<1>(b, page_size, partials, s); break;
-        case 2: e = launch_decode_g<2>(b, page_size, partials, s); break;
-        case 4: e = launch_decode_g<4>(b, page_size, partials, s); break;
-        default: e = launch_decode_g<8>(b, page_size, partials, s); break;
+        case 1: e = launch_decode_g<1>(b, page_size, dec_scratch, s); break;
+        case 2: e = launch_decode_g<2>(b, page_size, dec_scratch, s); break;
+        case 4: e = launch_decode_g<4>(b, page_size, dec_scratch, s); break;
+        default: e = launch_decode_g<8>(b, page_size, dec_scratch, s); break;
     }
     if (e != cudaSuccess) {
         *msg = cudaGetErrorString(e);

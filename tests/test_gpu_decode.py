@@ -39,6 +39,12 @@ def test_decode_edge_lengths_vs_oracle(lengths, require_cuda):
     for r, L in enumerate(lengths):
         if L == 0:
             assert not got[5][r].any()
+    # device-resident output pre-filled with NaN: every element is written, zeros for L = 0 included
+    torch = pytest.importorskip("torch")
+    dev = [torch.from_numpy(a.copy()).cuda() for a in arrays]
+    dev[5].fill_(float("nan"))
+    ex.run_with_symbols(dev, {"b": len(lengths)}, {}, {})
+    check(dev[5].cpu().numpy(), ref[5])
 
 
 def test_decode_dense_dyn_axis_runs_fewer_requests(require_cuda):
@@ -69,3 +75,18 @@ def test_decode_config4_full_size(require_cuda):
         CpuSim(workloads.decode_plan(R, 8, 4, 128, arrays[1].shape[0], arrays[3].shape[1])).run(
             one, axis_sizes={"b": r + 1})
         check(out[r], one[5][r])
+
+
+@pytest.mark.parametrize("group", [1, 2, 8])
+def test_decode_gqa_groups_vs_oracle(group, require_cuda):
+    rng = np.random.default_rng(10 + group)
+    lengths = [1, 513, 1100, 2049, 16]
+    plan, arrays = workloads.decode_inputs(rng, len(lengths), kv_heads=4, group=group, lengths=lengths)
+    ref = [a.copy() for a in arrays]
+    cyc = CpuSim(plan).run(ref, axis_sizes={"b": len(lengths)})
+    ex = CudaExecutable(plan)
+    for _ in range(2):  # the second run reuses the per-task arrival counters of the first
+        got = [a.copy() for a in arrays]
+        got[5][...] = np.float16(np.nan)
+        assert ex.run_with_symbols(got, {"b": len(lengths)}, {}, {}) == cyc
+        check(got[5], ref[5])
