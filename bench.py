@@ -462,7 +462,7 @@ def run_builtin(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
         plan, host = workloads.decode_inputs(rng, R)
         lens = host[4].astype(np.int64).reshape(-1)
         work = float(lens.sum() * 8 * 128 * 2 * 2 + R * 32 * 128 * 2 * 2)  # K+V of every token + Q + O
-        unit, scale, kname, bound = "GB/s", 1e9, "paged_decode_chunk", "hbm"
+        unit, scale, kname, bound = "GB/s", 1e9, "paged_decode_tma", "hbm"
         axis = {"b": R}
     else:
         B, T, K = wl["batch"], wl["context"], wl["topk"]
@@ -540,7 +540,7 @@ def run_builtin(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
                          "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(kname, args.workload),
                          "peak_kind": peak_kind, "kernel": kname,
                          ("bytes_per_launch" if bound == "hbm" else "flops_per_launch"): work,
-                         "note": "step = all launches of the task loop (decode: chunk + merge; indexer: scoring + "
+                         "note": "step = all work of the task loop (decode: counter memset + TMA kernel with fused merge; indexer: scoring + "
                                  "top-k); achieved uses the whole step time"},
             "e2e": {"value": round(e2e, 4), "unit": unit, "h2d_bytes_per_step": h2d // e2e_steps,
                     "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps},

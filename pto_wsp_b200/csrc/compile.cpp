@@ -564,7 +564,9 @@ void setup_builtin(const KernelDef& kd, KernelImpl& ki) {
         if (s.dtype != DType::F32 || o.dtype != DType::I32 || s.rows != 1 || o.rows != 1)
             throw Error(PTOWSP_ERR_PLAN, "topk_select: scores f32 [1,N] -> indices i32 [1,K]");
         if (o.cols > s.cols) throw Error(PTOWSP_ERR_PLAN, "topk_select: K > N");
-        if (s.cols > 49152 || o.cols > 4096) throw Error(PTOWSP_ERR_LIMIT, "topk_select: N <= 49152, K <= 4096");
+        if (!dev::topk_supported(s.cols, o.cols))
+            throw Error(PTOWSP_ERR_LIMIT, "topk_select: K <= 4096 and 4 N + 8 K (K rounded up to a power of two) "
+                                          "+ 16 KB within 225 KB of shared memory (N <= 49152 at K = 2048)");
         ki.param_write[1] = 1;
         ki.param_read[1] = 0;
         const uint64_t N = s.cols, K = o.cols;

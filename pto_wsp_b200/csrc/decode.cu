@@ -8,8 +8,9 @@
 // softmax(q K^T / sqrt(D)) V, f32 softmax, f16 output (round to nearest even).
 //
 // HBM-bound: every K/V byte is used for 2*G FLOP (G = 4: ~4 FLOP/B).
-// Split-KV: each task is cut into 512-token chunks (one CTA each, empty
-// chunks exit at once).  For the usual pool layout (16-token pages, 16-byte
+// Split-KV: each task is cut into chunks (1536 tokens for the TMA kernel, the
+// best of 1024 / 1536 / 2048 measured on config 4; 512 for the CUDA-core
+// kernel), one CTA each; empty chunks exit at once.  For the usual pool layout (16-token pages, 16-byte
 // aligned rows) a TMA producer warp streams the pages and four consumer warps
 // run both contractions of a page on warp-level MMAs (paged_decode_tma_kernel,
 // below); the last CTA of a task merges its chunk partials.  Other layouts use
@@ -20,9 +21,10 @@
 // topk_select -- indices of the K largest of N scores, ordered by score
 // descending, ties by lower index (examples/deepseek_lightning_indexer/
 // golden.py:6-25).  One CTA per row: the row is staged in shared memory as
-// order-preserving 32-bit keys, an 8-bit radix select finds the K-th key, the
-// K winners (ties at the threshold taken in index order) are gathered and
-// bitonic-sorted by (key desc, index asc).  Bit-exact by construction.
+// order-preserving 32-bit keys, a 4-pass 8-bit radix select finds the K-th
+// key, the K winners (ties at the threshold taken in index order) are
+// gathered and bitonic-sorted by (key desc, index asc).  Bit-exact by
+// construction.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -36,7 +38,14 @@ namespace ptowsp::dev {
 
 namespace {
 
-constexpr int kChunk = 512;       // tokens per split-KV chunk
+#ifndef PTOWSP_DECODE_CHUNK
+#define PTOWSP_DECODE_CHUNK 1536
+#endif
+#ifndef PTOWSP_DECODE_STAGES
+#define PTOWSP_DECODE_STAGES 8
+#endif
+constexpr int kChunk = PTOWSP_DECODE_CHUNK;  // tokens per split-KV chunk of the TMA kernel
+constexpr int kFbChunk = 512;                // tokens per split-KV chunk of the CUDA-core kernel
 constexpr int kDecThreads = 128;  // 4 warps
 constexpr int kHeadDim = 128;
 
@@ -75,7 +84,7 @@ template <int G>
 __global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBatch b, int page_size, int chunks,
                                                                         float* __restrict__ scratch) {
     constexpr int STEPS = 16 / G;
-    __shared__ __align__(16) float p_s[kChunk][G];  // scores, then probabilities, token-major
+    __shared__ __align__(16) float p_s[kFbChunk][G];  // scores, then probabilities, token-major
     __shared__ float red_s[4][G][kHeadDim];
     __shared__ float stat_s[2][4][G];
 
@@ -94,9 +103,9 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBat
         if (chunk == 0) atomicOr(b.err, kErrShape);
         L = Ppt.cols * page_size;
     }
-    const int t0 = chunk * kChunk;
+    const int t0 = chunk * kFbChunk;
     if (t0 >= L) return;  // empty chunk (also L <= 0: the merge kernel writes zeros)
-    const int n = min(kChunk, L - t0);
+    const int n = min(kFbChunk, L - t0);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hl = lane & 15;        // lane within the half-warp: head dims [8*hl, 8*hl + 8)
     const int hw = tid >> 4;         // half-warp id, 0..7
@@ -282,15 +291,21 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_chunk_kernel(TaskBat
 // after a timed-out wait.
 // ---------------------------------------------------------------------------
 
-constexpr int kMmaStages = 8;
+constexpr int kMmaStages = PTOWSP_DECODE_STAGES;
 constexpr int kMmaConsumers = 4;
 constexpr int kMmaThreads = 32 * (kMmaConsumers + 1);
+// Consumer warp w takes pages w, w + 4, ...; with a stage count that is a
+// multiple of the consumer count every stage is always read by the same warp,
+// which has finished the stage's previous page before it waits on the stage
+// again -- so a parity wait can never see the phase before the one it wants.
+static_assert(kMmaStages % kMmaConsumers == 0, "each ring stage must belong to one consumer warp");
 constexpr int kMmaPage = 16;
 constexpr int kHalfBox = kMmaPage * 64 * 2;   // 16 tokens x 64 dims f16 = 2 KB
 constexpr int kStageBytes = 4 * kHalfBox;     // K lo, K hi, V lo, V hi
 constexpr int kRingBytes = kMmaStages * kStageBytes;
-constexpr int kBarOffset = kRingBytes;  // full[S], empty[S], abort, last flag (136 B); the chunk's page ids at +256
-constexpr int kPbufOffset = kBarOffset + 384;                 // per-warp P buffer, 16 tokens x 8 queries f16
+constexpr int kBarOffset = kRingBytes;  // full[S], empty[S], abort, last flag
+constexpr int kPageIdsOffset = kBarOffset + ((16 * kMmaStages + 8 + 127) / 128) * 128;  // the chunk's page ids
+constexpr int kPbufOffset = kPageIdsOffset + ((kChunk / 16 * 4 + 127) / 128) * 128;  // per-warp P, 16 tok x 8 q f16
 constexpr int kMmaSmemBytes = kPbufOffset + kMmaConsumers * 256 + 1024;  // + 1024-byte alignment slack
 
 template <int G>
@@ -386,19 +401,18 @@ __global__ void __launch_bounds__(kMmaThreads) paged_decode_tma_kernel(const __g
 
     if (warp == kMmaConsumers) {
         // ---------------- producer ----------------
-        // the chunk's page ids (at most 32) are fetched at once, one per lane, and handed to lane 0 in shared memory
-        static_assert(kChunk / kMmaPage <= 32, "one page id per producer lane");
-        int* page_ids = reinterpret_cast<int*>(dsm + kBarOffset + 256);
+        // the chunk's page ids are fetched at once by the whole warp and handed to lane 0 in shared memory
+        int* page_ids = reinterpret_cast<int*>(dsm + kPageIdsOffset);
         {
             const int32_t* pt = reinterpret_cast<const int32_t*>(Ppt.base) + rec[3];
             const int64_t max_page = b.p[1].numel_span / (int64_t(kMmaPage) * b.p[1].s4) - 1;
-            if (lane < npages) {
-                int64_t page = pt[static_cast<int64_t>(t0 / kMmaPage + lane) * Ppt.s4];
+            for (int i = lane; i < npages; i += 32) {
+                int64_t page = pt[static_cast<int64_t>(t0 / kMmaPage + i) * Ppt.s4];
                 if (page < 0 || page > max_page) {
                     atomicOr(b.err, kErrBounds);
                     page = 0;
                 }
-                page_ids[lane] = static_cast<int>(page);
+                page_ids[i] = static_cast<int>(page);
             }
             __syncwarp();
         }
@@ -594,7 +608,7 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_merge_kernel(TaskBat
     const int32_t L = min(reinterpret_cast<const int32_t*>(b.p[4].base)[rec[4]], b.p[3].cols * page_size);
     __half* out = reinterpret_cast<__half*>(b.p[5].base) + rec[5];
     const int64_t os3 = b.p[5].s3;
-    const int nch = L > 0 ? min(chunks, (L + kChunk - 1) / kChunk) : 0;
+    const int nch = L > 0 ? min(chunks, (L + kFbChunk - 1) / kFbChunk) : 0;
     const int stride = G * kHeadDim + 2 * G;
     const float* base = scratch + task * chunks * static_cast<int64_t>(stride);
     for (int e = threadIdx.x; e < G * kHeadDim; e += kDecThreads) {
@@ -611,9 +625,9 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_merge_kernel(TaskBat
     }
 }
 
-int decode_chunks(const TaskBatch& b, int page_size) {
+int decode_chunks(const TaskBatch& b, int page_size, int chunk_tokens) {
     const int64_t max_tokens = static_cast<int64_t>(b.p[3].cols) * page_size;
-    return static_cast<int>(std::max<int64_t>(1, (max_tokens + kChunk - 1) / kChunk));
+    return static_cast<int>(std::max<int64_t>(1, (max_tokens + chunk_tokens - 1) / chunk_tokens));
 }
 
 bool decode_tma_ok(const TaskBatch& b, int page_size) {
@@ -630,13 +644,13 @@ size_t decode_arrivals_bytes(int64_t ntasks) { return (static_cast<size_t>(ntask
 
 template <int G>
 cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cudaStream_t s) {
-    const int chunks = decode_chunks(b, page_size);
-    const int64_t grid = b.ntasks * chunks;
-    if (grid <= 0) return cudaSuccess;
-    if (grid > 0x7fffffff) return cudaErrorInvalidValue;
+    if (b.ntasks <= 0) return cudaSuccess;
     unsigned* arrivals = static_cast<unsigned*>(scratch);
     float* partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + decode_arrivals_bytes(b.ntasks));
     if (decode_tma_ok(b, page_size)) {
+        const int chunks = decode_chunks(b, page_size, kChunk);
+        const int64_t grid = b.ntasks * chunks;
+        if (grid > 0x7fffffff) return cudaErrorInvalidValue;
         const ParamDesc& K = b.p[1];
         const ParamDesc& V = b.p[2];
         CUtensorMap mk, mv;
@@ -654,6 +668,9 @@ cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cu
             return cudaGetLastError();
         }
     }
+    const int chunks = decode_chunks(b, page_size, kFbChunk);
+    const int64_t grid = b.ntasks * chunks;
+    if (grid > 0x7fffffff) return cudaErrorInvalidValue;
     paged_decode_chunk_kernel<G><<<static_cast<unsigned>(grid), kDecThreads, 0, s>>>(b, page_size, chunks, partials);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -666,6 +683,8 @@ cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cu
 // ---------------------------------------------------------------------------
 
 constexpr int kTopkThreads = 1024;
+constexpr int kTopkWarps = kTopkThreads / 32;
+constexpr int kHistCopies = 16;  // lane-private copies of the 256-bin histogram (lanes l and l+16 share one)
 
 __device__ __forceinline__ uint32_t order_key(float f) {
     // Larger float -> larger unsigned key; -0.0 and +0.0 map to the same key.
@@ -674,12 +693,62 @@ __device__ __forceinline__ uint32_t order_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-template <int KPT>
+struct TopkLayout {  // dynamic shared memory, in bytes
+    int keys, scratch, comp, total;
+    __host__ __device__ TopkLayout(int n, int k2) {
+        keys = 0;
+        scratch = ((n * 4 + 15) / 16) * 16;  // histogram during the select, (round, warp) counts during the gather
+        const int rounds = (n + kTopkThreads - 1) / kTopkThreads;
+        const int hist = 256 * kHistCopies * 4, counts = rounds * kTopkWarps * 4;
+        comp = scratch + ((hist > counts ? hist : counts) + 15) / 16 * 16;
+        total = comp + k2 * 8;
+    }
+};
+
+// Exclusive prefix sum over the block of one value per thread; returns this
+// thread's prefix, *total gets the sum.  Two barriers.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_tot, uint32_t* total) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    uint32_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += n;
+    }
+    if (lane == 31) warp_tot[wid] = inc;
+    __syncthreads();
+    if (wid == 0) {
+        const uint32_t t = warp_tot[lane];
+        uint32_t s = t;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t n = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += n;
+        }
+        warp_tot[lane] = s - t;  // exclusive prefix of the warp totals
+        if (lane == 31) *total = s;
+    }
+    __syncthreads();
+    return warp_tot[wid] + inc - v;
+}
+
+// One CTA per row.  (1) Keys: the row as order-preserving 32-bit keys in
+// shared memory.  (2) Select: the exact K-th largest key by a 4-pass 8-bit
+// radix select; each pass histograms the keys that match the digits chosen so
+// far into lane-private copies of a 256-bin histogram (no two lanes of a warp
+// add to the same counter in the same instruction), sums the copies, and one
+// warp finds the digit holding the K-th key.  (3) Gather in index order:
+// per (1024-index round, warp) counts of keys above the threshold and equal to
+// it, one block-wide scan, then every key above the threshold and the first
+// `need` equal keys (the lowest indices, as the reference's stable order
+// takes them) are written as (key, ~index) composites.  (4) Bitonic sort of
+// the composites, descending; compare-exchanges within a warp's 64 elements
+// synchronise only the warp.  Bit-exact by construction.
 __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) {
-    extern __shared__ uint32_t ks[];  // N keys, then 2K composite slots (u64)
-    __shared__ uint32_t wcount[kTopkThreads / 32];
-    __shared__ uint32_t total_s;
-    __shared__ uint32_t sel_prefix, sel_remaining, n_gt, n_eq_taken;
+    extern __shared__ __align__(16) uint8_t tsm[];
+    __shared__ uint32_t bin_tot[256];
+    __shared__ uint32_t warp_tot[32];
+    __shared__ uint32_t s_prefix, s_need, s_total;
     const int64_t task = blockIdx.x;
     if (task >= b.ntasks) return;
     const int64_t* rec = b.rec + task * b.stride;
@@ -688,107 +757,124 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     const int N = S.cols, K = O.cols;
     int K2 = 1;
     while (K2 < K) K2 <<= 1;
-    unsigned long long* comp = reinterpret_cast<unsigned long long*>(ks + ((N + 1) & ~1));
+    const TopkLayout lay(N, K2);
+    uint32_t* ks = reinterpret_cast<uint32_t*>(tsm + lay.keys);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(tsm + lay.scratch);
+    uint32_t* cnt = hist;  // reused after the select
+    unsigned long long* comp = reinterpret_cast<unsigned long long*>(tsm + lay.comp);
     const float* src = reinterpret_cast<const float*>(S.base) + rec[0];
     const int64_t ss = S.s4;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    // keys: in shared memory (for the gather) and, KPT per thread, in registers (for counting)
-    uint32_t kr[KPT];
-#pragma unroll
-    for (int j = 0; j < KPT; ++j) {
-        const int i = j * kTopkThreads + threadIdx.x;
-        kr[j] = 0u;  // slots past N are skipped by the i < N test when counting
-        if (i < N) {
-            kr[j] = order_key(src[i * ss]);
-            ks[i] = kr[j];
+    const int rounds = (N + kTopkThreads - 1) / kTopkThreads;
+
+    // (1) keys
+    for (int i = threadIdx.x; i < N; i += kTopkThreads) ks[i] = order_key(src[i * ss]);
+
+    // (2) radix select, most significant digit first
+    uint32_t prefix = 0, need = static_cast<uint32_t>(K);
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        const uint32_t hmask = pass == 0 ? 0u : (0xffffffffu << (shift + 8));
+        for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
+        __syncthreads();  // keys written (pass 0), previous totals read
+        for (int i = threadIdx.x; i < N; i += kTopkThreads) {
+            const uint32_t k = ks[i];
+            if ((k & hmask) == prefix) atomicAdd(&hist[((k >> shift) & 255u) * kHistCopies + (lane & (kHistCopies - 1))], 1u);
         }
-    }
-    __syncthreads();
-    // Exact K-th largest key by binary search on its bits, most significant
-    // first: keep bit b if at least K keys are >= (prefix | bit b).  No atomics.
-    auto count_ge = [&](uint32_t cand) -> uint32_t {
-        uint32_t c = 0;
-#pragma unroll
-        for (int j = 0; j < KPT; ++j) {
-            const int i = j * kTopkThreads + threadIdx.x;
-            c += (i < N && kr[j] >= cand) ? 1u : 0u;
+        __syncthreads();
+        for (int bin = wid * 8; bin < wid * 8 + 8; ++bin) {
+            const uint32_t v = lane < kHistCopies ? hist[bin * kHistCopies + lane] : 0u;
+            const uint32_t t = __reduce_add_sync(0xffffffffu, v);
+            if (lane == 0) bin_tot[bin] = t;
         }
-        c = __reduce_add_sync(0xffffffffu, c);
-        if (lane == 0) wcount[wid] = c;
         __syncthreads();
         if (wid == 0) {
-            uint32_t t = lane < kTopkThreads / 32 ? wcount[lane] : 0u;
-            t = __reduce_add_sync(0xffffffffu, t);
-            if (lane == 0) total_s = t;
+            // lane l holds bins 8l .. 8l+7; find digit d with count(digit > d) < need <= count(digit >= d)
+            uint32_t c[8], local = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = bin_tot[8 * lane + j];
+                local += c[j];
+            }
+            uint32_t suf = local;  // sum over lanes l .. 31
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t n = __shfl_down_sync(0xffffffffu, suf, o);
+                if (lane + o < 32) suf += n;
+            }
+            const uint32_t above = suf - local;
+            if (above < need && need <= suf) {
+                uint32_t acc = above;
+                int d = 8 * lane;
+                uint32_t rem = need - above;
+#pragma unroll
+                for (int j = 7; j >= 0; --j) {
+                    if (acc + c[j] >= need) {
+                        d = 8 * lane + j;
+                        rem = need - acc;
+                        break;
+                    }
+                    acc += c[j];
+                }
+                s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+                s_need = rem;
+            }
         }
         __syncthreads();
-        return total_s;
-    };
-    uint32_t thr = 0;
-    for (int bit = 31; bit >= 0; --bit) {
-        const uint32_t cand = thr | (1u << bit);
-        if (count_ge(cand) >= static_cast<uint32_t>(K)) thr = cand;
-        __syncthreads();  // total_s is rewritten by the next count
+        prefix = s_prefix;
+        need = s_need;
     }
-    // K >= 1 keys are >= thr and fewer than K are > thr: count_ge(thr + 1) < K (or thr is the maximum key).
-    const uint32_t cnt_gt = thr == 0xffffffffu ? 0u : count_ge(thr + 1u);
-    if (threadIdx.x == 0) {
-        sel_prefix = thr;
-        sel_remaining = static_cast<uint32_t>(K) - cnt_gt;
-    }
-    __syncthreads();
-    const uint32_t need_eq = sel_remaining;  // how many keys equal to thr are taken (lowest indices first)
-    // gather: every key > thr, plus the first need_eq keys == thr in index order
-    if (threadIdx.x == 0) {
-        n_gt = 0;
-        n_eq_taken = 0;
-    }
-    for (int i = threadIdx.x; i < K2; i += kTopkThreads) comp[i] = 0ull;
-    __syncthreads();
-    for (int base = 0; base < N; base += kTopkThreads) {
-        const int i = base + threadIdx.x;
+    const uint32_t thr = prefix;  // the K-th largest key; `need` keys equal to it are taken
+
+    // (3) gather in index order: counts per (round, warp), packed (above << 16 | equal)
+    for (int r = 0; r < rounds; ++r) {
+        const int i = r * kTopkThreads + threadIdx.x;
         const uint32_t k = i < N ? ks[i] : 0u;
-        const bool gt = i < N && k > thr;
-        const unsigned m = __ballot_sync(0xffffffffu, gt);  // one shared atomic per warp
-        uint32_t wbase = 0;
-        if (lane == 0 && m) wbase = atomicAdd(&n_gt, static_cast<uint32_t>(__popc(m)));
-        wbase = __shfl_sync(0xffffffffu, wbase, 0);
-        if (gt) {
-            const uint32_t slot = wbase + __popc(m & ((1u << lane) - 1u));
-            if (slot < static_cast<uint32_t>(K)) comp[slot] = (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
-        }
+        const unsigned mgt = __ballot_sync(0xffffffffu, i < N && k > thr);
+        const unsigned meq = __ballot_sync(0xffffffffu, i < N && k == thr);
+        if (lane == 0) cnt[r * kTopkWarps + wid] = (static_cast<uint32_t>(__popc(mgt)) << 16) | __popc(meq);
     }
     __syncthreads();
-    const uint32_t gt = n_gt;
-    // equal keys: scan in index order chunk by chunk so the lowest indices win
-    for (int base = 0; base < N && n_eq_taken < need_eq; base += kTopkThreads) {
-        const int i = base + threadIdx.x;
-        const bool eq = i < N && ks[i] == thr;
-        const unsigned mask = __ballot_sync(0xffffffffu, eq);
-        __shared__ uint32_t warp_cnt[kTopkThreads / 32];
-        const int w = wid;
-        if (lane == 0) warp_cnt[w] = __popc(mask);
-        __syncthreads();
-        uint32_t before = n_eq_taken;
-        for (int j = 0; j < w; ++j) before += warp_cnt[j];
-        before += __popc(mask & ((1u << lane) - 1u));
-        if (eq && before < need_eq) {
-            const uint32_t slot = gt + before;
-            if (slot < static_cast<uint32_t>(K)) comp[slot] = (static_cast<unsigned long long>(thr) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            uint32_t tot = 0;
-            for (int j = 0; j < kTopkThreads / 32; ++j) tot += warp_cnt[j];
-            n_eq_taken += tot;
-        }
-        __syncthreads();
+    {
+        // exclusive scan over the rounds * 32 entries in (round, warp) order; each thread scans up to 2 entries
+        const int E = rounds * kTopkWarps;
+        const int e0 = threadIdx.x * 2;
+        const uint32_t v0 = e0 < E ? cnt[e0] : 0u, v1 = e0 + 1 < E ? cnt[e0 + 1] : 0u;
+        const uint32_t pre = block_exclusive_scan(v0 + v1, warp_tot, &s_total);
+        if (e0 < E) cnt[e0] = pre;
+        if (e0 + 1 < E) cnt[e0 + 1] = pre + v0;
     }
-    // bitonic sort of K2 composites, descending (key desc, then index asc via the inverted index)
+    __syncthreads();
+    const uint32_t n_gt = s_total >> 16;  // keys strictly above the threshold (< K)
+    for (int i = threadIdx.x; i < K2; i += kTopkThreads)
+        if (i >= K) comp[i] = 0ull;  // padding sorts last
+    for (int r = 0; r < rounds; ++r) {
+        const int i = r * kTopkThreads + threadIdx.x;
+        const uint32_t k = i < N ? ks[i] : 0u;
+        const bool gt = i < N && k > thr, eq = i < N && k == thr;
+        const unsigned mgt = __ballot_sync(0xffffffffu, gt);
+        const unsigned meq = __ballot_sync(0xffffffffu, eq);
+        const uint32_t base = cnt[r * kTopkWarps + wid];
+        const unsigned below = (1u << lane) - 1u;
+        const unsigned long long c = (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+        if (gt) {
+            const uint32_t slot = (base >> 16) + __popc(mgt & below);
+            if (slot < static_cast<uint32_t>(K)) comp[slot] = c;
+        } else if (eq) {
+            const uint32_t rank = (base & 0xffffu) + __popc(meq & below);
+            if (rank < need && n_gt + rank < static_cast<uint32_t>(K)) comp[n_gt + rank] = c;
+        }
+    }
+    // (4) bitonic sort of K2 composites, descending (key desc, then index asc via the inverted index).
+    // Pair p touches elements of the 64-element block of warp p / 32, so a stage whose stride is
+    // below 64 and follows such a stage needs only the warp to be in step.
+    int prev_stride = 1 << 30;  // the gather wrote across warps: the first stage synchronises the block
     for (int size = 2; size <= K2; size <<= 1) {
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = threadIdx.x; i < K2 / 2; i += kTopkThreads) {
-                const int lo = 2 * i - (i & (stride - 1));
+            if (stride >= 32 * 2 || prev_stride >= 32 * 2) __syncthreads();
+            else __syncwarp();
+            for (int p = threadIdx.x; p < K2 / 2; p += kTopkThreads) {
+                const int lo = 2 * p - (p & (stride - 1));
                 const int hi = lo + stride;
                 const bool desc = ((lo & size) == 0);
                 const unsigned long long a = comp[lo], c = comp[hi];
@@ -797,9 +883,10 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
                     comp[hi] = a;
                 }
             }
-            __syncthreads();
+            prev_stride = stride;
         }
     }
+    __syncthreads();
     int32_t* dst = reinterpret_cast<int32_t*>(O.base) + rec[1];
     for (int i = threadIdx.x; i < K; i += kTopkThreads)
         dst[i * O.s4] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(comp[i] & 0xffffffffull));
@@ -808,9 +895,11 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
 }  // namespace
 
 size_t paged_decode_scratch_bytes(const TaskBatch& b, int page_size) {
+
     const int G = b.p[0].rows;
     return decode_arrivals_bytes(b.ntasks) +
-           static_cast<size_t>(b.ntasks) * decode_chunks(b, page_size) * (G * kHeadDim + 2 * G) * sizeof(float);
+           static_cast<size_t>(b.ntasks) * decode_chunks(b, page_size, std::min(kChunk, kFbChunk)) *
+               (G * kHeadDim + 2 * G) * sizeof(float);
 }
 
 cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int, int, void* scratch, size_t scratch_bytes,
@@ -830,29 +919,21 @@ size_t topk_select_scratch_bytes(const TaskBatch&) { return 0; }
 int topk_smem_bytes(int n, int k) {
     int k2 = 1;
     while (k2 < k) k2 <<= 1;
-    return ((n + 1) & ~1) * 4 + k2 * 8;
+    return TopkLayout(n, k2).total;
 }
 
-template <int KPT>
-cudaError_t launch_topk_kpt(const TaskBatch& b, int smem, cudaStream_t s) {
-    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel<KPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    topk_select_kernel<KPT><<<static_cast<unsigned>(b.ntasks), kTopkThreads, smem, s>>>(b);
-    return cudaGetLastError();
+bool topk_supported(int n, int k) {
+    return n >= 1 && k >= 1 && k <= n && k <= 4096 && topk_smem_bytes(n, k) <= 227 * 1024 - 2048;  // opt-in max less static
 }
 
 cudaError_t launch_topk_select(const TaskBatch& b, int, void*, size_t, cudaStream_t s) {
-    const int n = b.p[0].cols;
-    const int smem = topk_smem_bytes(n, b.p[1].cols);
-    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    if (!topk_supported(b.p[0].cols, b.p[1].cols)) return cudaErrorInvalidValue;
+    const int smem = topk_smem_bytes(b.p[0].cols, b.p[1].cols);
     if (b.ntasks <= 0) return cudaSuccess;
-    const int kpt = (n + kTopkThreads - 1) / kTopkThreads;
-    if (kpt <= 4) return launch_topk_kpt<4>(b, smem, s);
-    if (kpt <= 8) return launch_topk_kpt<8>(b, smem, s);
-    if (kpt <= 16) return launch_topk_kpt<16>(b, smem, s);
-    if (kpt <= 32) return launch_topk_kpt<32>(b, smem, s);
-    if (kpt <= 48) return launch_topk_kpt<48>(b, smem, s);
-    return cudaErrorInvalidValue;  // rows beyond 49152 scores
+    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    topk_select_kernel<<<static_cast<unsigned>(b.ntasks), kTopkThreads, smem, s>>>(b);
+    return cudaGetLastError();
 }
 
 }  // namespace ptowsp::dev
@@ -937,7 +1018,8 @@ size_t noalloc_scratch_capacity() { return kPtowspNoAllocScratchBytes; }
 size_t noalloc_bytes_needed(int requests, int kv_heads, int group, int max_pages, int page_size) {
     const size_t tasks = static_cast<size_t>(requests) * kv_heads;
     const int64_t max_tokens = static_cast<int64_t>(max_pages) * page_size;
-    const size_t chunks = static_cast<size_t>(std::max<int64_t>(1, (max_tokens + kChunk - 1) / kChunk));
+    const int64_t chunk_tokens = std::min(kChunk, kFbChunk);
+    const size_t chunks = static_cast<size_t>(std::max<int64_t>(1, (max_tokens + chunk_tokens - 1) / chunk_tokens));
     return kNoAllocRecOffset + tasks * kNoAllocRecStride * sizeof(int64_t) + decode_arrivals_bytes(tasks) +
            tasks * chunks * (static_cast<size_t>(group) * kHeadDim + 2 * group) * sizeof(float);
 }

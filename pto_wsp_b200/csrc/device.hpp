@@ -113,6 +113,8 @@ cudaError_t launch_indexer_score(const TaskBatch& b, int workers, cudaStream_t s
 bool indexer_score_supported(const TaskBatch& b);
 cudaError_t launch_topk_select(const TaskBatch& b, int workers, void* scratch, size_t scratch_bytes, cudaStream_t s);
 size_t topk_select_scratch_bytes(const TaskBatch& b);
+// Whether one row of N scores and K winners fits the one-CTA-per-row kernel's shared memory.
+bool topk_supported(int n, int k);
 
 int sm_count();
 

@@ -13,10 +13,12 @@
 //     K-major straight from the row-major key matrix);
 //   * per key tile two tcgen05.mma groups (M = 128 keys, N = 256 = 4 queries x
 //     64 heads, K = 128 in 8 steps) fill two 256-column TMEM accumulators;
-//   * the epilogue warps read a key's 4 x 64 logits with tcgen05.ld, apply
-//     relu, reduce over heads with the per-query weights (sequential head
-//     order) and store 4 coalesced score rows -- while the MMA warp already
-//     fills the other accumulator.
+//   * eight epilogue warps (two per TMEM lane quarter, each owning 2 of the
+//     slot's 4 queries) pull their 128 logits per key with four tcgen05.ld in
+//     flight and one wait, release the accumulator at once, then apply relu,
+//     reduce over heads with the per-query weights (fixed head order) and
+//     store coalesced score rows -- while the MMA warp already fills the slot
+//     again.
 // Bounded waits and drains as in matmul_tcgen05.cu.  No cluster multicast.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -39,7 +41,8 @@ constexpr int NH = 256;           // q rows per MMA (N)
 constexpr int HEADS = 64;
 constexpr int D = 128;
 constexpr int STAGES = 3;
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;      // two per TMEM lane quarter, each taking 2 of a slot's 4 queries
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int Q_BYTES = QH * D * 2;        // 128 KB
 constexpr int Q_BOX = NH * 64 * 2;         // 32 KB: 256 rows x 64 d
 constexpr int K_STAGE = KT * D * 2;        // 32 KB: two 16 KB boxes of 128 keys x 64 d
@@ -87,7 +90,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_u32(&tfull[a]), 1);
-            mbar_init(smem_u32(&tempty[a]), 4 * 32);
+            mbar_init(smem_u32(&tempty[a]), EPI_WARPS * 32);
         }
         mbar_init(smem_u32(qfull), 1);
         mbar_init(smem_u32(qempty), 1);
@@ -223,7 +226,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else {
-        const int quarter = warp & 3;
+        const int quarter = warp & 3;       // the TMEM lanes (keys) this warp may read
+        const int half = (warp - 2) >> 2;   // queries 2*half and 2*half+1 of each 4-query slot
         const int row = quarter * 32 + lane;
         int slot = 0;
         uint32_t slot_phase = 0;
@@ -240,30 +244,36 @@ __global__ void __launch_bounds__(THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-#pragma unroll 1
-                for (int ql = 0; ql < 4; ++ql) {
-                    const int q = hq * 4 + ql;
+                // this warp's 2 queries x 64 heads: four 32-column loads in flight, one wait
+                uint32_t v[4][32];
+                const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                       static_cast<uint32_t>(slot * NH + half * 2 * HEADS);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_ld32_async(tbase + static_cast<uint32_t>(c * 32), v[c]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) reg_fence(v[c]);
+                tc_fence_before();
+                mbar_arrive(smem_u32(&tempty[slot]));  // the accumulator is in registers: release it
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq) {
+                    const int q = hq * 4 + half * 2 + qq;
                     const float4* wq = reinterpret_cast<const float4*>(w + q * args.w_s3);
-                    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums over heads h = 4j + c
-#pragma unroll 1
+                    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums over heads h = 4j + c, j ascending
+#pragma unroll
                     for (int hc = 0; hc < 2; ++hc) {
-                        float v[32];
-                        tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                      static_cast<uint32_t>(slot * NH + ql * HEADS + hc * 32),
-                                  v);
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const float4 wv = __ldg(wq + hc * 8 + j);  // same address in every lane: one L1 broadcast
-                            acc[0] = fmaf(wv.x, fmaxf(v[4 * j + 0], 0.f), acc[0]);
-                            acc[1] = fmaf(wv.y, fmaxf(v[4 * j + 1], 0.f), acc[1]);
-                            acc[2] = fmaf(wv.z, fmaxf(v[4 * j + 2], 0.f), acc[2]);
-                            acc[3] = fmaf(wv.w, fmaxf(v[4 * j + 3], 0.f), acc[3]);
+                            const uint32_t* x = &v[2 * qq + hc][4 * j];
+                            acc[0] = fmaf(wv.x, fmaxf(__uint_as_float(x[0]), 0.f), acc[0]);
+                            acc[1] = fmaf(wv.y, fmaxf(__uint_as_float(x[1]), 0.f), acc[1]);
+                            acc[2] = fmaf(wv.z, fmaxf(__uint_as_float(x[2]), 0.f), acc[2]);
+                            acc[3] = fmaf(wv.w, fmaxf(__uint_as_float(x[3]), 0.f), acc[3]);
                         }
                     }
                     s[q * args.s_s3] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
                 }
-                tc_fence_before();
-                mbar_arrive(smem_u32(&tempty[slot]));
                 if (++slot == 2) {
                     slot = 0;
                     slot_phase ^= 1u;

@@ -43,7 +43,7 @@ def test_indexer_small_vs_fp64_and_topk_exact(require_cuda):
             assert idx[b, qq].tolist() == stable_topk(s[b, qq], 64).tolist()
 
 
-@pytest.mark.parametrize("kind", ["ties", "zeros", "mixed", "sorted", "reverse"])
+@pytest.mark.parametrize("kind", ["ties", "zeros", "mixed", "sorted", "reverse", "nan"])
 def test_topk_adversarial_rows_bit_exact(kind, require_cuda):
     rng = np.random.default_rng(1)
     rows, n, k = 6, 4096, 2048
@@ -57,10 +57,26 @@ def test_topk_adversarial_rows_bit_exact(kind, require_cuda):
         s[:, :, ::5] = np.float32(3.4e38)
         s[:, :, 1::11] = -np.inf
         s[:, :, 2::13] = np.inf
+    elif kind == "nan":
+        s = rng.standard_normal((rows, 1, n)).astype(np.float32)
+        s[:, :, ::9] = np.float32(np.nan)
+        s[:, :, 4::17] = -np.float32(np.nan)
     elif kind == "sorted":
         s = np.tile(np.arange(n, dtype=np.float32), (rows, 1, 1))
     else:
         s = np.tile(np.arange(n, dtype=np.float32)[::-1].copy(), (rows, 1, 1))
+    out = np.full((rows, 1, k), -7, np.int32)
+    CudaExecutable(workloads.topk_plan(rows, n, k)).run_with_symbols([s, out], {}, {}, {})
+    for r in range(rows):
+        assert out[r, 0].tolist() == stable_topk(s[r, 0], k).tolist()
+
+
+@pytest.mark.parametrize("n,k", [(1, 1), (100, 7), (1000, 1000), (1025, 1), (5000, 33), (32768, 2048),
+                                 (49152, 2048), (20000, 4096), (3000, 3000)])
+def test_topk_sizes_bit_exact(n, k, require_cuda):
+    rng = np.random.default_rng(n + k)
+    rows = 3
+    s = (rng.standard_normal((rows, 1, n)) * 10).astype(np.float16).astype(np.float32)  # f16 grid: many ties
     out = np.full((rows, 1, k), -7, np.int32)
     CudaExecutable(workloads.topk_plan(rows, n, k)).run_with_symbols([s, out], {}, {}, {})
     for r in range(rows):
