@@ -69,9 +69,10 @@ def peaks(key: str = "hbm_gbs") -> tuple[float, str]:
     return (6650.0 if key == "hbm_gbs" else 1590.0), "fallback"
 
 
-def traffic_from_profiles(kernel: str, workload: str) -> float | None:
+def traffic_from_profiles(kernel: str, workload: str, batch_override=None) -> float | None:
+    """DRAM bytes per launch of the full workload from the committed ncu summaries (None for --batch runs)."""
     p = ROOT / "profiles" / "traffic.json"
-    if not p.exists():
+    if batch_override is not None or not p.exists():
         return None
     try:
         d = json.loads(p.read_text())
@@ -378,7 +379,7 @@ def run_bgemm(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
                        "l2": "operands 1 GiB > 126 MB L2 (no flush needed)"},
             "gpu_launches": launches,
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles("matmul_tcgen05", "bgemm"),
+                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles("matmul_tcgen05", "bgemm", args.batch),
                          "peak_kind": peak_kind + " (cuBLAS bf16 burst; fp16 runs at the same tensor rate)",
                          "kernel": "matmul_tcgen05", "flops_per_launch": flops},
             "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d // e2e_steps,
@@ -537,7 +538,7 @@ def run_builtin(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
                        "l2": "KV / keys > 126 MB L2 (no flush needed)"},
             "gpu_launches": launches,
             "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
-                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(kname, args.workload),
+                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(kname, args.workload, args.batch),
                          "peak_kind": peak_kind, "kernel": kname,
                          ("bytes_per_launch" if bound == "hbm" else "flops_per_launch"): work,
                          "note": "step = all work of the task loop (decode: counter memset + TMA kernel with fused merge; indexer: scoring + "
@@ -685,7 +686,7 @@ def main() -> None:
     per_launch_ms = ms / args.steps
     achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
     kernel_name = "softmax_rows" if args.workload == "softmax" else "rmsnorm_rows"
-    traffic = traffic_from_profiles(kernel_name, args.workload)
+    traffic = traffic_from_profiles(kernel_name, args.workload, args.batch)
 
     # spot-check the last device result against the numpy definition on a few tiles
     xs = x.reshape(-1, R, Cc)[:64].double().cpu().numpy()
