@@ -48,6 +48,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false on abort (set by another role) or timeout (sets the flags).
+// `cluster_scope`: acquire at cluster scope, for barriers that the peer CTA of a pair arrives on.
+template <bool cluster_scope = false>
+__device__ __forceinline__ bool mbar_wait_t(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+    uint64_t start = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u) {
+            if (*abort_flag) return false;
+            const uint64_t now = globaltimer();
+            if (start == 0) {
+                start = now;
+            } else if (now - start > kTimeoutNs) {
+                atomicOr(err, kErrTimeout);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
 // Bounded wait: false on abort (set by another role) or timeout (sets the flags).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
     uint64_t start = 0;
@@ -72,6 +105,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
+}
+
+// L2 prefetch of a 2-D box (no shared memory, no barrier): warms L2 for a later tma_load_2d of the same box.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
 }
 
 // Shared-memory matrix descriptor (tcgen05): start>>4 [0,14), LBO>>4 [16,30),
@@ -101,6 +141,56 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b,
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accum)
         : "memory");
+}
+
+// ---- CTA pairs (cta_group::2): the two CTAs of a 2-CTA cluster share one MMA of M = 256 ----
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared variable in CTA `rank` of this cluster (a shared::cluster address).
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// Arrive on an mbarrier given by a shared::cluster address (this CTA's or the peer's).  CTA-scope release:
+// it only hands over TMEM (ordered by the tcgen05 fences around it), not data in global memory, and a
+// cluster-scope release would first wait for this thread's outstanding global stores.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Cluster-wide barrier; both CTAs of a pair reach it on every path (all waits before it are bounded).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA 2-D load into this CTA's shared memory whose completion bytes are counted on the mbarrier at
+// `bar_cluster` -- the leader CTA's barrier (a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+// MMA over the CTA pair (issued by the leader CTA only): A rows and B columns are split over the two CTAs'
+// shared memory at the same offsets, D rows over the two CTAs' TMEM.
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+// Completion of the pair's MMAs issued so far arrives (once) on the mbarrier at `bar_cluster`, a
+// shared::cluster address in either CTA of the pair; commit once per CTA that must see it.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
