@@ -866,8 +866,70 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
         }
     }
     // (4) bitonic sort of K2 composites, descending (key desc, then index asc via the inverted index).
-    // Pair p touches elements of the 64-element block of warp p / 32, so a stage whose stride is
-    // below 64 and follows such a stage needs only the warp to be in step.
+    int32_t* dst = reinterpret_cast<int32_t*>(O.base) + rec[1];
+    if (K2 >= 64 && K2 <= 2 * kTopkThreads) {
+        // Thread t holds elements 2t and 2t+1 in registers: stride 1 is a compare in the thread,
+        // strides 2..32 a shuffle with lane ^ (stride / 2); strides of 64 and more cross warps and go
+        // through shared memory, one block barrier each.
+        const int t = threadIdx.x;
+        const bool active = 2 * t < K2;  // K2 / 2 is a multiple of 32: whole warps are active or idle
+        __syncthreads();                 // the gather wrote across warps
+        unsigned long long e[2] = {active ? comp[2 * t] : 0ull, active ? comp[2 * t + 1] : 0ull};
+        for (int size = 2; size <= K2; size <<= 1) {
+            int stride = size >> 1;
+            if (stride >= 64) {
+                if (active) {
+                    comp[2 * t] = e[0];
+                    comp[2 * t + 1] = e[1];
+                }
+                for (; stride >= 64; stride >>= 1) {
+                    __syncthreads();
+                    if (active) {
+                        const int lo = 2 * t - (t & (stride - 1));
+                        const int hi = lo + stride;
+                        const bool desc = ((lo & size) == 0);
+                        const unsigned long long x = comp[lo], y = comp[hi];
+                        if ((x < y) == desc) {
+                            comp[lo] = y;
+                            comp[hi] = x;
+                        }
+                    }
+                }
+                __syncthreads();
+                if (active) {
+                    e[0] = comp[2 * t];
+                    e[1] = comp[2 * t + 1];
+                }
+            }
+            if (active) {
+                for (; stride >= 2; stride >>= 1) {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int i = 2 * t + j;
+                        const unsigned long long other = __shfl_xor_sync(0xffffffffu, e[j], stride >> 1);
+                        const bool keep_max = ((i & stride) == 0) == ((i & size) == 0);
+                        const unsigned long long hi_v = e[j] > other ? e[j] : other;
+                        const unsigned long long lo_v = e[j] > other ? other : e[j];
+                        e[j] = keep_max ? hi_v : lo_v;
+                    }
+                }
+                const bool desc = ((2 * t) & size) == 0;  // stride 1: the thread's own pair
+                if ((e[0] < e[1]) == desc) {
+                    const unsigned long long x = e[0];
+                    e[0] = e[1];
+                    e[1] = x;
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int i = 2 * t + j;
+            if (active && i < K) dst[i * O.s4] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(e[j] & 0xffffffffull));
+        }
+        return;
+    }
+    // other sizes: every stage in shared memory.  Pair p touches elements of the 64-element block of
+    // warp p / 32, so a stage whose stride is below 64 and follows such a stage needs only the warp.
     int prev_stride = 1 << 30;  // the gather wrote across warps: the first stage synchronises the block
     for (int size = 2; size <= K2; size <<= 1) {
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
@@ -887,7 +949,6 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
         }
     }
     __syncthreads();
-    int32_t* dst = reinterpret_cast<int32_t*>(O.base) + rec[1];
     for (int i = threadIdx.x; i < K; i += kTopkThreads)
         dst[i * O.s4] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(comp[i] & 0xffffffffull));
 }
