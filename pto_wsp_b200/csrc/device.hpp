@@ -104,6 +104,10 @@ int tile_program_max_smem();
 cudaError_t launch_matmul_tiles(const TaskBatch& b, int accumulate, int workers, cudaStream_t s);
 // Shape/stride/alignment conditions of the tcgen05 path (per-task offsets are checked by the host).
 bool matmul_tiles_supported(const TaskBatch& b);
+// CTA-pair (cta_group::2) matmul over `nunits` units of two tasks (records [oa, ob, oc] x 2, device memory) whose
+// A / C tiles are 128 rows apart and whose B tile is shared; false (nothing launched) when pairs cannot be scheduled.
+bool launch_matmul_pairs(const TaskBatch& b, const int64_t* units, int64_t nunits, int accumulate, int workers,
+                         cudaStream_t s, cudaError_t* err);
 
 // Built-ins.
 cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int num_kv_heads, int workers, void* scratch,

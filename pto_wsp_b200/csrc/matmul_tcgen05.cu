@@ -19,7 +19,8 @@
 //               accumulators let the epilogue of tile i overlap tile i+1's MMAs.
 // Every mbarrier wait is bounded (~2 s of %globaltimer): on timeout the CTA
 // records kErrTimeout, drains its own copies and MMAs, frees TMEM and returns.
-// No cluster multicast anywhere (loads read this GPU's memory only, per CTA).
+// When the tasks pair up along M the CTA-pair kernel below runs instead.
+// No cluster multicast anywhere (loads read this GPU's memory only).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -290,6 +291,285 @@ cudaError_t launch_bn(const TaskBatch& b, int accumulate, int workers, cudaStrea
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (the default when the tasks pair up along M).
+//
+// Two CTAs of a 2-CTA cluster share each MMA (tcgen05 cta_group::2, M = 256):
+// a unit is two tasks whose A tiles are 128 rows apart and whose B tile is the
+// same; CTA r computes task r's 128 x BN tile of C from its own A rows and its
+// half (BN/2 columns) of the shared B tile.  Per 64-wide K step an SM then
+// stages 16 KB of A and BN*64 B of B instead of 16 KB + BN*128 B, which both
+// cuts the L2 -> SM traffic by a third (BN = 256) and lets a deeper ring fit.
+// Barrier protocol as in the CTA-pair indexer kernel: both CTAs' TMA bytes
+// land on the leader's full barrier, the leader issues the MMAs and commits
+// to each CTA's barriers, one lane per epilogue warp of either CTA releases an
+// accumulator on the leader, and cluster barriers bracket setup and teardown.
+// ---------------------------------------------------------------------------
+
+template <int BN>
+struct PairSmem {
+    static constexpr int A_BYTES = BM * BK * 2;              // 16 KB
+    static constexpr int B_BYTES = (BN / 2) * BK * 2;        // this CTA's half of B: (BN/2)/64 boxes of 8 KB
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES_FIT = (232448 - 1280) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+    static constexpr int RING = STAGES * STAGE_BYTES;
+    static constexpr int BAR_OFF = RING;
+    static constexpr int TOTAL = RING + 256 + 1024;
+    static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+    matmul_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                       MMArgs args) {
+    using S = PairSmem<BN>;
+    constexpr int STAGES = S::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+    uint64_t* full = bars;                      // [STAGES]  waited on in the leader
+    uint64_t* empty = bars + STAGES;            // [STAGES]  both CTAs
+    uint64_t* tfull = bars + 2 * STAGES;        // [2]       both CTAs
+    uint64_t* tempty = bars + 2 * STAGES + 2;   // [2]       waited on in the leader
+    uint64_t* drain = bars + 2 * STAGES + 4;    //           leader
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 5);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+
+    const uint32_t rank = cluster_ctarank();  // 0: leader
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&tfull[a]), 1);
+            mbar_init(smem_u32(&tempty[a]), 2 * 4);  // one lane of each epilogue warp of both CTAs
+        }
+        mbar_init(smem_u32(drain), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(S::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t lead_bars = mapa_shared(smem_u32(bars), 0);
+    const uint32_t peer_bars = mapa_shared(smem_u32(bars), 1);
+    auto lead = [&](const uint64_t* b) { return lead_bars + static_cast<uint32_t>((b - bars) * 8); };
+    auto peer = [&](const uint64_t* b) { return peer_bars + static_cast<uint32_t>((b - bars) * 8); };
+    const int64_t first = blockIdx.x >> 1, step = gridDim.x >> 1;  // units: two tasks (6 record words)
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0, issued_mask = 0, last_parity = 0;
+            for (int64_t u = first; u < args.ntasks && !*abort_flag; u += step) {
+                const int64_t* rec = args.rec + u * 6 + rank * 3;
+                const int64_t oa = rec[0], ob = rec[1];
+                const int32_t ax = static_cast<int32_t>(oa % args.a_pitch), ay = static_cast<int32_t>(oa / args.a_pitch);
+                const int32_t bx = static_cast<int32_t>(ob % args.b_pitch) + static_cast<int32_t>(rank) * (BN / 2);
+                const int32_t by = static_cast<int32_t>(ob / args.b_pitch);
+                for (int kb = 0; kb < args.k_steps; ++kb) {
+                    if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, args.err)) break;
+                    if (rank == 0) mbar_expect_tx(smem_u32(&full[stage]), 2 * S::STAGE_BYTES);
+                    uint8_t* sa = smem + stage * S::STAGE_BYTES;
+                    uint8_t* sb = sa + S::A_BYTES;
+                    tma_load_2d_pair(smem_u32(sa), &tmap_a, ax + kb * BK, ay, lead(&full[stage]));
+#pragma unroll
+                    for (int j = 0; j < BN / 128; ++j)
+                        tma_load_2d_pair(smem_u32(sb + j * 8192), &tmap_b, bx + j * 64, by + kb * BK, lead(&full[stage]));
+                    issued_mask |= 1u << stage;
+                    last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (rank == 0) {
+                // drain: the pair's last copy into each stage has landed before shared memory goes away
+                const uint64_t start = globaltimer();
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued_mask & (1u << s))
+                        while (!mbar_try_wait(smem_u32(&full[s]), (last_parity >> s) & 1u))
+                            if (globaltimer() - start > kTimeoutNs) {
+                                atomicOr(args.err, kErrTimeout);
+                                break;
+                            }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_f16(2 * BM, BN);  // M = 256 over the pair, B MN-major
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            bool issued = false;
+            for (int64_t u = first; u < args.ntasks && !*abort_flag; u += step) {
+                if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, args.err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                bool ok = true;
+                for (int kb = 0; kb < args.k_steps; ++kb) {
+                    if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, args.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * S::STAGE_BYTES);
+                    const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t ad = smem_desc(sa + kk * 32, 16, 1024);
+                        const uint64_t bd = smem_desc(sb + kk * 2048, 8192, 1024);
+                        mma_f16_pair(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit_pair(lead(&empty[stage]));
+                    mma_commit_pair(peer(&empty[stage]));
+                    issued = true;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit_pair(lead(&tfull[acc]));
+                mma_commit_pair(peer(&tfull[acc]));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (issued) {
+                mma_commit_pair(lead(drain));
+                const uint64_t start = globaltimer();
+                while (!mbar_try_wait(smem_u32(drain), 0))
+                    if (globaltimer() - start > kTimeoutNs) {
+                        atomicOr(args.err, kErrTimeout);
+                        break;
+                    }
+            }
+        }
+    } else {
+        // epilogue (warps 2..5): this CTA's 128 rows x BN columns of its task's C tile
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int64_t u = first; u < args.ntasks && !*abort_flag; u += step) {
+            if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, args.err)) break;
+            tc_fence_after();
+            const int64_t oc = args.rec[u * 6 + rank * 3 + 2];
+            float* crow = args.c + oc + static_cast<int64_t>(row) * args.c_pitch;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; cc += 2) {
+                uint32_t v[2][32];
+                tmem_ld32_async(tbase + static_cast<uint32_t>(cc * 32), v[0]);
+                tmem_ld32_async(tbase + static_cast<uint32_t>(cc * 32 + 32), v[1]);
+                tmem_wait_ld();
+                reg_fence(v[0]);
+                reg_fence(v[1]);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float4* dst = reinterpret_cast<float4*>(crow + (cc + h) * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        float4 o = make_float4(__uint_as_float(v[h][4 * i]), __uint_as_float(v[h][4 * i + 1]),
+                                               __uint_as_float(v[h][4 * i + 2]), __uint_as_float(v[h][4 * i + 3]));
+                        if (args.accumulate) {
+                            const float4 c0 = dst[i];
+                            o.x += c0.x;
+                            o.y += c0.y;
+                            o.z += c0.z;
+                            o.w += c0.w;
+                        }
+                        dst[i] = o;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(lead(&tempty[acc]));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the leader has drained the pair's copies and MMAs
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(S::TMEM_COLS) : "memory");
+}
+
+// CTA-pair launch over `units` (6 record words each); false when the pairs cannot be scheduled.
+template <int BN>
+bool launch_pair_bn(const TaskBatch& b, const int64_t* units, int64_t nunits, int accumulate, int workers, cudaStream_t s,
+                    cudaError_t* err) {
+    const ParamDesc& A = b.p[0];
+    const ParamDesc& B = b.p[1];
+    const ParamDesc& C = b.p[2];
+    CUtensorMap ma, mb;
+    const int64_t a_rows = (A.numel_span + A.s3 - 1) / A.s3;
+    const int64_t b_rows = (B.numel_span + B.s3 - 1) / B.s3;
+    if (!make_map_f16(&ma, A.base, A.s3, a_rows, BK, BM)) return false;
+    if (!make_map_f16(&mb, B.base, B.s3, b_rows, 64, BK)) return false;
+    MMArgs args;
+    args.rec = units;
+    args.ntasks = nunits;
+    args.stride = 6;
+    args.a_pitch = A.s3;
+    args.b_pitch = B.s3;
+    args.c = reinterpret_cast<float*>(C.base);
+    args.c_pitch = C.s3;
+    args.k_steps = A.cols / BK;
+    args.accumulate = accumulate;
+    args.err = b.err;
+    const int smem = PairSmem<BN>::TOTAL;
+    if (cudaFuncSetAttribute(matmul_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int64_t pairs = std::max<int64_t>(1, sm_count() / 2);
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    int resident = 0;  // pairs that fit at once: the persistent schedule needs all of them resident
+    if (cudaOccupancyMaxActiveClusters(&resident, matmul_pair_kernel<BN>, &cfg) != cudaSuccess || resident < 1) {
+        cudaGetLastError();
+        return false;
+    }
+    pairs = std::min<int64_t>({pairs, resident, nunits});
+    if (workers > 0) pairs = std::min<int64_t>(pairs, std::max(1, workers / 2));
+    pairs = std::max<int64_t>(pairs, 1);
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    *err = cudaLaunchKernelEx(&cfg, matmul_pair_kernel<BN>, ma, mb, args);
+    return true;
+}
+
 }  // namespace
 
 bool matmul_tiles_supported(const TaskBatch& b) {
@@ -303,6 +583,15 @@ bool matmul_tiles_supported(const TaskBatch& b) {
     if ((reinterpret_cast<uintptr_t>(A.base) | reinterpret_cast<uintptr_t>(B.base) | reinterpret_cast<uintptr_t>(C.base)) & 15)
         return false;
     return true;
+}
+
+bool launch_matmul_pairs(const TaskBatch& b, const int64_t* units, int64_t nunits, int accumulate, int workers,
+                         cudaStream_t s, cudaError_t* err) {
+    switch (b.p[1].cols) {
+        case 128: return launch_pair_bn<128>(b, units, nunits, accumulate, workers, s, err);
+        case 256: return launch_pair_bn<256>(b, units, nunits, accumulate, workers, s, err);
+        default: return false;
+    }
 }
 
 cudaError_t launch_matmul_tiles(const TaskBatch& b, int accumulate, int workers, cudaStream_t s) {

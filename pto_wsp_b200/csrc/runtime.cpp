@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <chrono>
 #include <functional>
+#include <unordered_map>
 #include <cstring>
 #include <queue>
 #include <sstream>
@@ -471,6 +472,7 @@ struct Walker {
 
 Batch::~Batch() {
     if (fast_rec_dev) cudaFree(fast_rec_dev);
+    if (unit_rec_dev) cudaFree(unit_rec_dev);
 }
 
 LaunchProgram::~LaunchProgram() {
@@ -614,6 +616,52 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                     PW_CUDA(cudaMemcpy(B.fast_rec_dev, m.data(), m.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
                     B.fast_ntasks = B.ntasks / 2;
                     B.fast_n = 2 * static_cast<int>(N);
+                    B.units_ok = -1;
+                }
+            }
+            // CTA pairs: each (merged) task with the task 128 rows below it in A and C that shares its B tile
+            if (ok && B.units_ok < 0) {
+                std::vector<int64_t> r3;  // [oa, ob, oc] per task as launched
+                if (B.fast_rec_dev) {
+                    r3.resize(static_cast<size_t>(B.fast_ntasks) * 3);
+                    for (int64_t t = 0; t < B.ntasks; t += 2)
+                        for (int j = 0; j < 3; ++j) r3[(t / 2) * 3 + j] = B.rec[t * B.stride + j];
+                } else {
+                    r3.resize(static_cast<size_t>(B.ntasks) * 3);
+                    for (int64_t t = 0; t < B.ntasks; ++t)
+                        for (int j = 0; j < 3; ++j) r3[t * 3 + j] = B.rec[t * B.stride + j];
+                }
+                const int64_t n = static_cast<int64_t>(r3.size() / 3);
+                std::unordered_map<uint64_t, int64_t> at;  // (oa, ob) -> task
+                at.reserve(static_cast<size_t>(n) * 2);
+                constexpr int64_t BM_ROWS = 128;  // rows of a task's A / C tile
+                auto key = [](int64_t oa, int64_t ob) {  // splitmix64 finaliser of the pair
+                    uint64_t z = static_cast<uint64_t>(oa) * 0x9e3779b97f4a7c15ull ^ static_cast<uint64_t>(ob);
+                    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+                    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+                    return z ^ (z >> 31);
+                };
+                bool fine = n % 2 == 0 && (B.fast_n == 128 || B.fast_n == 256);
+                for (int64_t t = 0; fine && t < n; ++t) fine = at.emplace(key(r3[t * 3], r3[t * 3 + 1]), t).second;
+                std::vector<char> used(static_cast<size_t>(n), 0);
+                std::vector<int64_t> units;
+                units.reserve(static_cast<size_t>(n) * 3);
+                for (int64_t t = 0; fine && t < n; ++t) {
+                    if (used[t]) continue;
+                    const int64_t oa = r3[t * 3], ob = r3[t * 3 + 1], oc = r3[t * 3 + 2];
+                    auto it = at.find(key(oa + BM_ROWS * A.s3, ob));
+                    fine = it != at.end() && !used[it->second] && r3[it->second * 3] == oa + BM_ROWS * A.s3 &&
+                           r3[it->second * 3 + 1] == ob && r3[it->second * 3 + 2] == oc + BM_ROWS * Cm.s3;
+                    if (!fine) break;
+                    used[t] = used[it->second] = 1;
+                    for (int j = 0; j < 3; ++j) units.push_back(r3[t * 3 + j]);
+                    for (int j = 0; j < 3; ++j) units.push_back(r3[it->second * 3 + j]);
+                }
+                B.units_ok = fine ? 1 : 0;
+                if (fine) {
+                    PW_CUDA(cudaMalloc(&B.unit_rec_dev, units.size() * sizeof(int64_t)));
+                    PW_CUDA(cudaMemcpy(B.unit_rec_dev, units.data(), units.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
+                    B.nunits = static_cast<int64_t>(units.size() / 6);
                 }
             }
         }
@@ -630,9 +678,16 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
         case ImplKind::RmsNorm: e = dev::launch_rmsnorm_rows(tb, workers, P.stream); break;
         case ImplKind::Softmax: e = dev::launch_softmax_rows(tb, workers, P.stream); break;
         case ImplKind::Matmul:
-        case ImplKind::MatmulAcc:
-            e = dev::launch_matmul_tiles(tb, kind == ImplKind::MatmulAcc ? 1 : 0, workers, P.stream);
+        case ImplKind::MatmulAcc: {
+            const int acc = kind == ImplKind::MatmulAcc ? 1 : 0;
+            cudaError_t pe = cudaSuccess;
+            if (B.units_ok == 1 && dev::launch_matmul_pairs(tb, B.unit_rec_dev, B.nunits, acc, workers, P.stream, &pe)) {
+                e = pe;
+                break;
+            }
+            e = dev::launch_matmul_tiles(tb, acc, workers, P.stream);
             break;
+        }
         case ImplKind::TileProgram:
             if (!ki.tp_ok) throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
             e = dev::launch_tile_program(tb, ki.tp_dev, ki.tp_smem, workers, P.stream);

@@ -59,6 +59,11 @@ struct Batch {  // tasks of one kernel inside one wave
     int64_t* fast_rec_dev = nullptr;
     int64_t fast_ntasks = 0;
     int fast_n = 0;
+    // CTA-pair matmul: units of two (possibly N-merged) tasks 128 rows apart in A and C sharing B,
+    // records [oa, ob, oc] x 2 (-1: not checked yet, 0: the tasks do not pair up)
+    int64_t* unit_rec_dev = nullptr;
+    int64_t nunits = 0;
+    int8_t units_ok = -1;
     // host-staged pipelining: per chunk and tensor param, the [lo, hi) element range its tasks touch
     int chunk_n = 0;
     std::vector<int64_t> chunk_ranges;
@@ -68,7 +73,9 @@ struct Batch {  // tasks of one kernel inside one wave
         kernel = o.kernel; node = o.node; rec = std::move(o.rec); ntasks = o.ntasks; stride = o.stride;
         dev_off = o.dev_off; aligned_rows = o.aligned_rows; fast_ok = o.fast_ok; fast_rec_dev = o.fast_rec_dev;
         fast_ntasks = o.fast_ntasks; fast_n = o.fast_n; chunk_n = o.chunk_n; chunk_ranges = std::move(o.chunk_ranges);
+        unit_rec_dev = o.unit_rec_dev; nunits = o.nunits; units_ok = o.units_ok;
         o.fast_rec_dev = nullptr;
+        o.unit_rec_dev = nullptr;
         return *this;
     }
     Batch(const Batch&) = delete;
