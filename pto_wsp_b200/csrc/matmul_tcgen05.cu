@@ -311,18 +311,20 @@ struct PairSmem {
     static constexpr int A_BYTES = BM * BK * 2;              // 16 KB
     static constexpr int B_BYTES = (BN / 2) * BK * 2;        // this CTA's half of B: (BN/2)/64 boxes of 8 KB
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES_FIT = (232448 - 1280) / STAGE_BYTES;
+    static constexpr int OUT_BYTES = 4 * 2 * 32 * 32 * 4;    // epilogue staging: 2 tiles of 32 x 32 f32 per warp
+    static constexpr int STAGES_FIT = (232448 - 1280 - OUT_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int RING = STAGES * STAGE_BYTES;
-    static constexpr int BAR_OFF = RING;
-    static constexpr int TOTAL = RING + 256 + 1024;
+    static constexpr int OUT_OFF = RING;                      // 1024-aligned: the 128-byte swizzle repeats per 1 KB
+    static constexpr int BAR_OFF = OUT_OFF + OUT_BYTES;
+    static constexpr int TOTAL = BAR_OFF + 256 + 1024;
     static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
 };
 
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     matmul_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                       MMArgs args) {
+                       const __grid_constant__ CUtensorMap tmap_c, MMArgs args) {
     using S = PairSmem<BN>;
     constexpr int STAGES = S::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -462,42 +464,63 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else {
-        // epilogue (warps 2..5): this CTA's 128 rows x BN columns of its task's C tile
+        // epilogue (warps 2..5): this CTA's 128 rows x BN columns of its task's C tile.  Plain stores go
+        // through shared memory: each warp stages a 32 x 32 f32 tile (128-byte swizzled, so the row-per-lane
+        // writes hit distinct banks) and one lane sends it with a TMA store -- whole 128-byte rows instead of
+        // 16-byte pieces of 32 rows per instruction.  The accumulate form reads C back and stores directly.
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
+        uint8_t* out_stage = smem + S::OUT_OFF + (warp - 2) * (2 * 32 * 32 * 4);
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int64_t u = first; u < args.ntasks && !*abort_flag; u += step) {
             if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, args.err)) break;
             tc_fence_after();
             const int64_t oc = args.rec[u * 6 + rank * 3 + 2];
-            float* crow = args.c + oc + static_cast<int64_t>(row) * args.c_pitch;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+            if (args.accumulate) {
+                float* crow = args.c + oc + static_cast<int64_t>(row) * args.c_pitch;
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 32; cc += 2) {
-                uint32_t v[2][32];
-                tmem_ld32_async(tbase + static_cast<uint32_t>(cc * 32), v[0]);
-                tmem_ld32_async(tbase + static_cast<uint32_t>(cc * 32 + 32), v[1]);
-                tmem_wait_ld();
-                reg_fence(v[0]);
-                reg_fence(v[1]);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    float4* dst = reinterpret_cast<float4*>(crow + (cc + h) * 32);
+                for (int cc = 0; cc < BN / 32; ++cc) {
+                    uint32_t v[32];
+                    tmem_ld32_async(tbase + static_cast<uint32_t>(cc * 32), v);
+                    tmem_wait_ld();
+                    reg_fence(v);
+                    float4* dst = reinterpret_cast<float4*>(crow + cc * 32);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        float4 o = make_float4(__uint_as_float(v[h][4 * i]), __uint_as_float(v[h][4 * i + 1]),
-                                               __uint_as_float(v[h][4 * i + 2]), __uint_as_float(v[h][4 * i + 3]));
-                        if (args.accumulate) {
-                            const float4 c0 = dst[i];
-                            o.x += c0.x;
-                            o.y += c0.y;
-                            o.z += c0.z;
-                            o.w += c0.w;
-                        }
-                        dst[i] = o;
+                        const float4 c0 = dst[i];
+                        dst[i] = make_float4(__uint_as_float(v[4 * i]) + c0.x, __uint_as_float(v[4 * i + 1]) + c0.y,
+                                             __uint_as_float(v[4 * i + 2]) + c0.z, __uint_as_float(v[4 * i + 3]) + c0.w);
                     }
                 }
+            } else {
+                const int32_t cx = static_cast<int32_t>(oc % args.c_pitch);
+                const int32_t cy = static_cast<int32_t>(oc / args.c_pitch) + quarter * 32;
+#pragma unroll 1
+                for (int cc = 0; cc < BN / 32; ++cc) {
+                    uint32_t v[32];
+                    tmem_ld32_async(tbase + static_cast<uint32_t>(cc * 32), v);
+                    tmem_wait_ld();
+                    reg_fence(v);
+                    uint8_t* buf = out_stage + (cc & 1) * (32 * 32 * 4);
+                    if (cc >= 2) {
+                        if (lane == 0) tma_store_wait_read<1>();  // the store that last read `buf` is done with it
+                        __syncwarp();
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                            make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmap_c, cx + cc * 32, cy, smem_u32(buf));
+                        tma_store_commit();
+                    }
+                }
+                if (lane == 0) tma_store_wait_read<0>();  // the staging tiles are free for the next unit
+                __syncwarp();
             }
             tc_fence_before();
             __syncwarp();
@@ -507,6 +530,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 acc_phase ^= 1u;
             }
         }
+        if (lane == 0) tma_store_wait_all();  // every C tile written before the CTA retires
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -528,6 +553,9 @@ bool launch_pair_bn(const TaskBatch& b, const int64_t* units, int64_t nunits, in
     const int64_t b_rows = (B.numel_span + B.s3 - 1) / B.s3;
     if (!make_map_f16(&ma, A.base, A.s3, a_rows, BK, BM)) return false;
     if (!make_map_f16(&mb, B.base, B.s3, b_rows, 64, BK)) return false;
+    CUtensorMap mc;
+    const int64_t c_rows = (C.numel_span + C.s3 - 1) / C.s3;
+    if (!make_map_f32(&mc, C.base, C.s3, c_rows, 32, 32)) return false;
     MMArgs args;
     args.rec = units;
     args.ntasks = nunits;
@@ -566,7 +594,7 @@ bool launch_pair_bn(const TaskBatch& b, const int64_t* units, int64_t nunits, in
     if (workers > 0) pairs = std::min<int64_t>(pairs, std::max(1, workers / 2));
     pairs = std::max<int64_t>(pairs, 1);
     cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
-    *err = cudaLaunchKernelEx(&cfg, matmul_pair_kernel<BN>, ma, mb, args);
+    *err = cudaLaunchKernelEx(&cfg, matmul_pair_kernel<BN>, ma, mb, mc, args);
     return true;
 }
 

@@ -114,6 +114,25 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t 
                  : "memory");
 }
 
+// TMA 2-D tile store from this CTA's shared memory into global memory (bulk group); the staging buffer
+// may be rewritten once tma_store_wait_read allows it.  Coordinates must not be negative.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t x, int32_t y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// At most N of this thread's committed store groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Every committed store group of this thread has completed (its writes are performed).
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Generic-proxy writes to shared memory become visible to the async proxy (TMA) reading it next.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // Shared-memory matrix descriptor (tcgen05): start>>4 [0,14), LBO>>4 [16,30),
 // SBO>>4 [32,46), version 1 [46,48), layout type [61,64) (2 = 128-byte swizzle).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -244,6 +263,10 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
 // `pitch` elements, `rows` rows), 128-byte swizzle.  False if the driver entry
 // point is unavailable or the encoder rejects the parameters.
 bool make_map_f16(CUtensorMap* m, const void* base, int64_t pitch, int64_t rows, uint32_t box_x, uint32_t box_y);
+
+// Host: 2-D f32 tensor map over a row-pitched buffer (`pitch` elements per row, `rows` rows), 128-byte
+// swizzle -- the layout the epilogues stage their output tiles in for TMA stores.
+bool make_map_f32(CUtensorMap* m, const void* base, int64_t pitch, int64_t rows, uint32_t box_x, uint32_t box_y);
 
 // Host: general 2-D f16 tensor map: `inner` elements per row, `rows` rows
 // `row_bytes` apart (a multiple of 16), box `box_x` x `box_y`, no swizzle.
