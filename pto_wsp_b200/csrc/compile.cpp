@@ -673,6 +673,9 @@ std::unique_ptr<Program> compile_program(const char* text, size_t len, int devic
         else ki.kind = ImplKind::TileProgram;
         if (ki.kind == ImplKind::TileProgram && !ki.tp_ok)
             throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
+        // a generic kernel gets its fused row kernel built now (NVRTC, no GPU needed); the fast row ops build
+        // theirs only if a launch falls back to the tile program
+        if (ki.kind == ImplKind::TileProgram) jit_prepare(ki, kd, static_cast<int>(i));
     }
     prog->tensor_key_depth.assign(plan.tensors.size(), -1);
     collect_depths(plan, *plan.body, prog->tensor_key_depth);
@@ -687,8 +690,13 @@ std::string describe_program(const Program& p) {
       << "\",\"num_targets\":" << p.plan.schedule.num_targets << ",\"kernels\":[";
     for (size_t i = 0; i < p.impls.size(); ++i) {
         if (i) o << ",";
-        o << "{\"name\":\"" << p.plan.kernels[i].name << "\",\"impl\":\"" << impl_name(p.impls[i].kind)
-          << "\",\"cycles\":" << p.impls[i].cycles << ",\"tile_program_smem\":" << p.impls[i].tp_smem << "}";
+        const KernelImpl& ki = p.impls[i];
+        std::string note;
+        for (char c : ki.jit_note.substr(0, 200)) note += (c == '"' || c == '\\' || c < 32) ? ' ' : c;
+        const char* row = ki.jit_state == 1 ? "loaded" : ki.jit_state == 2 ? "compiled" : ki.jit_state == 0 ? "not built" : "interpreter";
+        o << "{\"name\":\"" << p.plan.kernels[i].name << "\",\"impl\":\"" << impl_name(ki.kind)
+          << "\",\"cycles\":" << ki.cycles << ",\"tile_program_smem\":" << ki.tp_smem << ",\"row_kernel\":\"" << row
+          << "\",\"row_kernel_note\":\"" << note << "\"}";
     }
     o << "]";
     if (p.cached) {

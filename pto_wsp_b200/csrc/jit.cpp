@@ -1,0 +1,405 @@
+// Row-program compiler: generic tile programs lowered to fused CUDA kernels.
+//
+// A tile program (the emitter's op set, src/python/pto_codegen.cpp:785-1231) is
+// "row-local" when every instruction works on whole rows of its tiles: loads
+// and stores of full tiles, element-wise binary / scalar / exp / rsqrt ops,
+// row-broadcast operands ([R,1] tiles) and row reductions.  Such a program --
+// RMSNorm or softmax of any width, scale/shift chains, row normalisations --
+// is lowered to one straight-line kernel specialised on its shapes, op
+// sequence and parameter types: one warp per tile row, the row's elements in
+// registers (lane l holds columns l, l+32, ...), reductions by warp shuffles,
+// no shared memory and no block barriers.  The source is compiled at the first
+// launch with NVRTC (loaded with dlopen) for sm_100a and loaded through the
+// driver API; a program that is not row-local, or any failure on the way,
+// keeps the shared-memory tile-program interpreter (rows.cu), which is also a
+// GPU kernel.  Element-wise results match the interpreter bit for bit; row
+// reductions add in tree order instead of column order (the hand-written row
+// kernels do the same), within the fp32 tolerance.
+#include "jit.hpp"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <sstream>
+#include <vector>
+
+namespace ptowsp::jit {
+
+namespace {
+
+using namespace dev;
+
+constexpr int kMaxCols = 1024;     // a lane holds at most 32 elements of one tile row
+constexpr int kMaxRegWords = 160;  // per lane, over all full-width tiles of the program (255 registers at most)
+
+// ---- NVRTC, resolved at run time (no link-time dependency) ----
+using nvrtcProgram_t = void*;
+struct Nvrtc {
+    int (*create)(nvrtcProgram_t*, const char*, const char*, int, const char* const*, const char* const*) = nullptr;
+    int (*compile)(nvrtcProgram_t, int, const char* const*) = nullptr;
+    int (*log_size)(nvrtcProgram_t, size_t*) = nullptr;
+    int (*log)(nvrtcProgram_t, char*) = nullptr;
+    int (*cubin_size)(nvrtcProgram_t, size_t*) = nullptr;
+    int (*cubin)(nvrtcProgram_t, char*) = nullptr;
+    int (*destroy)(nvrtcProgram_t*) = nullptr;
+    bool ok = false;
+};
+
+const Nvrtc& nvrtc() {
+    static Nvrtc n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char* names[] = {"libnvrtc.so.12", "libnvrtc.so", "/usr/local/cuda/lib64/libnvrtc.so.12",
+                               "/usr/local/cuda/lib64/libnvrtc.so"};
+        void* h = nullptr;
+        for (const char* nm : names)
+            if ((h = dlopen(nm, RTLD_NOW | RTLD_LOCAL)) != nullptr) break;
+        if (!h) return;
+        auto sym = [&](const char* s) { return dlsym(h, s); };
+        n.create = reinterpret_cast<decltype(n.create)>(sym("nvrtcCreateProgram"));
+        n.compile = reinterpret_cast<decltype(n.compile)>(sym("nvrtcCompileProgram"));
+        n.log_size = reinterpret_cast<decltype(n.log_size)>(sym("nvrtcGetProgramLogSize"));
+        n.log = reinterpret_cast<decltype(n.log)>(sym("nvrtcGetProgramLog"));
+        n.cubin_size = reinterpret_cast<decltype(n.cubin_size)>(sym("nvrtcGetCUBINSize"));
+        n.cubin = reinterpret_cast<decltype(n.cubin)>(sym("nvrtcGetCUBIN"));
+        n.destroy = reinterpret_cast<decltype(n.destroy)>(sym("nvrtcDestroyProgram"));
+        n.ok = n.create && n.compile && n.log_size && n.log && n.cubin_size && n.cubin && n.destroy;
+    });
+    return n;
+}
+
+// ---- driver API entry points ----
+struct Driver {
+    CUresult (*load)(CUmodule*, const void*) = nullptr;
+    CUresult (*get)(CUfunction*, CUmodule, const char*) = nullptr;
+    CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream,
+                       void**, void**) = nullptr;
+    bool ok = false;
+};
+
+const Driver& driver() {
+    static Driver d;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        auto entry = [](const char* name) -> void* {
+            void* p = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+                return nullptr;
+            return p;
+        };
+        d.load = reinterpret_cast<decltype(d.load)>(entry("cuModuleLoadData"));
+        d.get = reinterpret_cast<decltype(d.get)>(entry("cuModuleGetFunction"));
+        d.launch = reinterpret_cast<decltype(d.launch)>(entry("cuLaunchKernel"));
+        d.ok = d.load && d.get && d.launch;
+    });
+    return d;
+}
+
+const char* kPrelude = R"(
+typedef long long int64_t;
+typedef unsigned long long uint64_t;
+typedef int int32_t;
+typedef unsigned int uint32_t;
+struct ParamDesc { char* base; int64_t s3, s4; int64_t numel_span; int rows, cols; int type; int elem_bytes; };
+struct TaskBatch { const int64_t* rec; int64_t ntasks; int stride; int nparams, naxis, nscalar; ParamDesc p[MAXP]; int* err; };
+__device__ __forceinline__ float h2f(unsigned short h) { float f; asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h)); return f; }
+__device__ __forceinline__ unsigned short f2h(float f) { unsigned short h; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f)); return h; }
+)";
+
+// Load expression of element `off` of param p (type `pt`) as the 32-bit word `word` (load_elem_w semantics).
+std::string load_expr(int pt, int word, const std::string& p, const std::string& off) {
+    const std::string fe = [&] {
+        switch (pt) {
+            case PT_F32: return "((const float*)" + p + ".base)[" + off + "]";
+            case PT_F16: return "h2f(((const unsigned short*)" + p + ".base)[" + off + "])";
+            case PT_I32: return "(float)((const int*)" + p + ".base)[" + off + "]";
+            case PT_U32: return "(float)((const unsigned*)" + p + ".base)[" + off + "]";
+            case PT_I64: return "(float)((const long long*)" + p + ".base)[" + off + "]";
+            case PT_U64: return "(float)((const unsigned long long*)" + p + ".base)[" + off + "]";
+            default: return std::string("0.f");
+        }
+    }();
+    if (word == W_F32) return "__float_as_uint(" + fe + ")";
+    switch (pt) {
+        case PT_I32: case PT_U32: return "((const unsigned*)" + p + ".base)[" + off + "]";
+        case PT_I64: case PT_U64: return "(unsigned)((const unsigned long long*)" + p + ".base)[" + off + "]";
+        case PT_F32: return "(unsigned)(int)((const float*)" + p + ".base)[" + off + "]";
+        case PT_F16: return "(unsigned)(int)h2f(((const unsigned short*)" + p + ".base)[" + off + "])";
+        default: return "0u";
+    }
+}
+
+// Store statement of word `w` (type `word`) to element `off` of param p (store_elem semantics).
+std::string store_stmt(int pt, int word, const std::string& p, const std::string& off, const std::string& w) {
+    const std::string f = word == W_F32 ? "__uint_as_float(" + w + ")"
+                                        : (word == W_I32 ? "(float)(int)(" + w + ")" : "(float)(" + w + ")");
+    switch (pt) {
+        case PT_F32: return "((float*)" + p + ".base)[" + off + "] = " + f + ";";
+        case PT_F16: return "((unsigned short*)" + p + ".base)[" + off + "] = f2h(" + f + ");";
+        case PT_I32: return "((int*)" + p + ".base)[" + off + "] = " + (word == W_F32 ? "(int)" + f : "(int)(" + w + ")") + ";";
+        case PT_U32: return "((unsigned*)" + p + ".base)[" + off + "] = " + (word == W_F32 ? "(unsigned)" + f : "(" + w + ")") + ";";
+        case PT_I64: return "((long long*)" + p + ".base)[" + off + "] = " +
+                            (word == W_F32 ? "(long long)" + f : "(long long)(int)(" + w + ")") + ";";
+        case PT_U64: return "((unsigned long long*)" + p + ".base)[" + off + "] = " +
+                            (word == W_F32 ? "(unsigned long long)" + f : "(unsigned long long)(" + w + ")") + ";";
+        default: return ";";
+    }
+}
+
+std::string bin_expr(int word, int sub, const std::string& a, const std::string& b) {
+    if (word == W_F32) {
+        const std::string fa = "__uint_as_float(" + a + ")", fb = "__uint_as_float(" + b + ")";
+        switch (sub) {
+            case BIN_ADD: return "__float_as_uint(__fadd_rn(" + fa + ", " + fb + "))";
+            case BIN_SUB: return "__float_as_uint(__fsub_rn(" + fa + ", " + fb + "))";
+            case BIN_MUL: return "__float_as_uint(__fmul_rn(" + fa + ", " + fb + "))";
+            case BIN_DIV: return "__float_as_uint(__fdiv_rn(" + fa + ", " + fb + "))";
+            case BIN_MAX: return "__float_as_uint(fmaxf(" + fa + ", " + fb + "))";
+            default: return "__float_as_uint(fminf(" + fa + ", " + fb + "))";
+        }
+    }
+    const std::string ia = "(int)(" + a + ")", ib = "(int)(" + b + ")";
+    switch (sub) {
+        case BIN_ADD: return "(unsigned)(" + ia + " + " + ib + ")";
+        case BIN_SUB: return "(unsigned)(" + ia + " - " + ib + ")";
+        case BIN_MUL: return "(unsigned)(" + ia + " * " + ib + ")";
+        case BIN_DIV: return "(unsigned)(" + ib + " ? " + ia + " / " + ib + " : 0)";
+        case BIN_MAX: return "(unsigned)(" + ia + " > " + ib + " ? " + ia + " : " + ib + ")";
+        default: return "(unsigned)(" + ia + " < " + ib + " ? " + ia + " : " + ib + ")";
+    }
+}
+
+}  // namespace
+
+bool row_local(const TileProgram& tp, std::string* why) {
+    auto fail = [&](const std::string& m) {
+        if (why) *why = m;
+        return false;
+    };
+    if (tp.ninstr <= 0 || tp.nslots <= 0) return fail("empty program");
+    int R = -1, words = 0;
+    for (int i = 0; i < tp.nslots; ++i) {
+        const TPSlot& s = tp.slots[i];
+        if (R < 0) R = s.rows;
+        if (s.rows != R) return fail("tiles of different row counts");
+        if (s.cols < 1 || s.cols > kMaxCols) return fail("tile wider than 1024 columns");
+        if (s.cols > 1) words += (s.cols + 31) / 32;
+    }
+    if (R < 1) return fail("no rows");
+    if (words > kMaxRegWords) return fail("too many tile elements per lane");
+    for (int ii = 0; ii < tp.ninstr; ++ii) {
+        const TPInstr& in = tp.ins[ii];
+        switch (in.op) {
+            case TP_LOAD: {
+                const TPSlot& d = tp.slots[in.dst];
+                if (in.rows != d.rows || in.cols != d.cols) return fail("partial-tile load");
+                break;
+            }
+            case TP_STORE: {
+                const TPSlot& a = tp.slots[in.a];
+                if (in.rows != a.rows || in.cols != a.cols) return fail("partial-tile store");
+                break;
+            }
+            case TP_MOV: case TP_BINS: case TP_EXP: case TP_RSQRT: {
+                const TPSlot &d = tp.slots[in.dst], &a = tp.slots[in.a];
+                if (d.cols != a.cols) return fail("shape change in an element-wise op");
+                break;
+            }
+            case TP_BIN: {
+                const TPSlot &d = tp.slots[in.dst], &a = tp.slots[in.a], &b = tp.slots[in.b];
+                if (d.cols != a.cols) return fail("shape change in a binary op");
+                if (in.mode == MODE_FULL && b.cols != d.cols) return fail("binary op on different shapes");
+                if (in.mode == MODE_ROW && b.cols != 1) return fail("row broadcast of a wide tile");
+                if (in.mode == MODE_COL) return fail("column broadcast");
+                break;
+            }
+            case TP_ROWSUM: case TP_ROWMAX: case TP_ROWMEAN: {
+                if (tp.slots[in.dst].cols != 1) return fail("row reduction into a wide tile");
+                if (tp.slots[in.a].word != W_F32) return fail("integer row reduction");
+                break;
+            }
+            default: return fail("op outside the row-local set");
+        }
+    }
+    return true;
+}
+
+std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const std::string& name) {
+    const int R = tp.slots[0].rows;
+    std::ostringstream o;
+    o << "#define MAXP " << kMaxParams << "\n" << kPrelude;
+    o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(TaskBatch b) {\n";
+    o << "  const int lane = threadIdx.x & 31;\n";
+    o << "  const int64_t nrows = b.ntasks * " << R << "LL;\n";
+    o << "  for (int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); g < nrows; g += (int64_t)gridDim.x * 8) {\n";
+    o << "    const int64_t task = g / " << R << "; const int r = (int)(g - task * " << R << ");\n";
+    o << "    const int64_t* rec = b.rec + task * b.stride;\n";
+    for (int i = 0; i < tp.nslots; ++i) {
+        const TPSlot& s = tp.slots[i];
+        if (s.cols > 1) o << "    unsigned s" << i << "[" << (s.cols + 31) / 32 << "];\n";
+        else o << "    unsigned s" << i << " = 0u;\n";
+    }
+    auto elem = [&](int slot, const std::string& j) {
+        return tp.slots[slot].cols > 1 ? "s" + std::to_string(slot) + "[" + j + "]" : "s" + std::to_string(slot);
+    };
+    for (int ii = 0; ii < tp.ninstr; ++ii) {
+        const TPInstr& in = tp.ins[ii];
+        o << "    { // " << ii << "\n";
+        switch (in.op) {
+            case TP_LOAD: {
+                const TPSlot& d = tp.slots[in.dst];
+                const std::string p = "b.p[" + std::to_string(in.param) + "]";
+                const int nj = (d.cols + 31) / 32;
+                o << "      const int64_t base = rec[" << in.param << "] + (int64_t)r * " << p << ".s3;\n";
+                o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
+                o << "        const int c = lane + 32 * j; unsigned w = 0u;\n";
+                o << "        if (c < " << d.cols << ") { const int64_t off = base + (int64_t)c * " << p << ".s4;\n";
+                o << "          if (off >= 0 && off < " << p << ".numel_span) w = "
+                  << load_expr(param_types[in.param], d.word, p, "off") << ";\n";
+                o << "          else atomicOr(b.err, " << kErrBounds << "); }\n";
+                o << "        " << (d.cols > 1 ? "s" + std::to_string(in.dst) + "[j] = w;" : "if (j == 0) s" + std::to_string(in.dst) + " = __shfl_sync(0xffffffffu, w, 0);") << "\n";
+                o << "      }\n";
+                break;
+            }
+            case TP_STORE: {
+                const TPSlot& a = tp.slots[in.a];
+                const std::string p = "b.p[" + std::to_string(in.param) + "]";
+                const int nj = (a.cols + 31) / 32;
+                o << "      const int64_t base = rec[" << in.param << "] + (int64_t)r * " << p << ".s3;\n";
+                o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
+                o << "        const int c = lane + 32 * j;\n";
+                o << "        if (c < " << a.cols << ") { const int64_t off = base + (int64_t)c * " << p << ".s4;\n";
+                o << "          if (off >= 0 && off < " << p << ".numel_span) { "
+                  << store_stmt(param_types[in.param], a.word, p, "off", elem(in.a, "j")) << " }\n";
+                o << "          else atomicOr(b.err, " << kErrBounds << "); }\n";
+                o << "      }\n";
+                break;
+            }
+            case TP_MOV: case TP_BIN: case TP_BINS: case TP_EXP: case TP_RSQRT: {
+                const TPSlot& d = tp.slots[in.dst];
+                const int nj = (d.cols + 31) / 32;
+                if (in.op == TP_BINS) {
+                    // the scalar operand as the op's word type (TP_BINS semantics of the interpreter)
+                    const bool fw = d.word == W_F32;
+                    if (in.scalar_src >= 0) {
+                        o << "      const unsigned long long raw = (unsigned long long)rec[b.nparams + b.naxis + "
+                          << in.scalar_src << "];\n";
+                        const int st = tp.scalar_types[in.scalar_src];
+                        if (st == 0) o << (fw ? "      const unsigned ws = (unsigned)raw;\n"
+                                              : "      const unsigned ws = (unsigned)(int)__uint_as_float((unsigned)raw);\n");
+                        else if (st == 2) o << (fw ? "      const unsigned ws = __float_as_uint((float)(long long)raw);\n"
+                                                   : "      const unsigned ws = (unsigned)(int)raw;\n");
+                        else o << (fw ? "      const unsigned ws = __float_as_uint((float)(int)raw);\n"
+                                      : "      const unsigned ws = (unsigned)(int)raw;\n");
+                    } else {
+                        unsigned fbits;
+                        std::memcpy(&fbits, &in.fval, 4);
+                        o << "      const unsigned ws = " << (fw ? std::to_string(fbits) + "u" : "(unsigned)(" + std::to_string(in.ival) + ")")
+                          << ";\n";
+                    }
+                }
+                o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
+                std::string rhs;
+                const std::string a = elem(in.a, "j");
+                if (in.op == TP_MOV) rhs = a;
+                else if (in.op == TP_BIN) rhs = bin_expr(d.word, in.sub, a, in.mode == MODE_ROW ? elem(in.b, "0") : elem(in.b, "j"));
+                else if (in.op == TP_BINS) rhs = in.scalar_first ? bin_expr(d.word, in.sub, "ws", a) : bin_expr(d.word, in.sub, a, "ws");
+                else if (in.op == TP_EXP) rhs = "__float_as_uint(expf(__uint_as_float(" + a + ")))";
+                else rhs = "__float_as_uint(__fdiv_rn(1.0f, sqrtf(__uint_as_float(" + a + "))))";
+                o << "        " << elem(in.dst, "j") << " = " << rhs << ";\n";
+                o << "      }\n";
+                break;
+            }
+            case TP_ROWSUM: case TP_ROWMAX: case TP_ROWMEAN: {
+                const TPSlot& a = tp.slots[in.a];
+                const int nj = (a.cols + 31) / 32;
+                const bool mx = in.op == TP_ROWMAX;
+                o << "      float acc = " << (mx ? "-__int_as_float(0x7f800000)" : "0.f") << ";\n";
+                o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j)\n";
+                o << "        if (lane + 32 * j < " << a.cols << ") acc = "
+                  << (mx ? "fmaxf(acc, __uint_as_float(" + elem(in.a, "j") + "))"
+                         : "__fadd_rn(acc, __uint_as_float(" + elem(in.a, "j") + "))")
+                  << ";\n";
+                o << "      #pragma unroll\n      for (int o = 16; o > 0; o >>= 1) acc = "
+                  << (mx ? "fmaxf(acc, __shfl_xor_sync(0xffffffffu, acc, o))" : "__fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o))")
+                  << ";\n";
+                if (in.op == TP_ROWMEAN) o << "      acc = __fdiv_rn(acc, (float)" << in.k << ");\n";
+                o << "      s" << in.dst << " = __float_as_uint(acc);\n";
+                break;
+            }
+            default: break;
+        }
+        o << "    }\n";
+    }
+    o << "  }\n}\n";
+    return o.str();
+}
+
+bool compile_cubin(const std::string& src, const std::string& name, std::string* cubin, std::string* log) {
+    const Nvrtc& n = nvrtc();
+    if (!n.ok) {
+        *log = "NVRTC not found";
+        return false;
+    }
+    nvrtcProgram_t prog = nullptr;
+    if (n.create(&prog, src.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr) != 0) {
+        *log = "nvrtcCreateProgram failed";
+        return false;
+    }
+    const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17", "-default-device"};
+    const int rc = n.compile(prog, 3, opts);
+    size_t ls = 0;
+    n.log_size(prog, &ls);
+    if (ls > 1) {
+        log->resize(ls);
+        n.log(prog, log->data());
+    }
+    bool ok = rc == 0;
+    if (ok) {
+        size_t cs = 0;
+        ok = n.cubin_size(prog, &cs) == 0 && cs > 0;
+        if (ok) {
+            cubin->resize(cs);
+            ok = n.cubin(prog, cubin->data()) == 0;
+        }
+    }
+    n.destroy(&prog);
+    if (!ok && log->empty()) *log = "NVRTC compilation failed";
+    return ok;
+}
+
+bool load_cubin(const std::string& cubin, const std::string& name, void** fn, std::string* log) {
+    const Driver& d = driver();
+    if (!d.ok) {
+        *log = "driver entry points unavailable";
+        return false;
+    }
+    CUmodule mod = nullptr;  // kept for the life of the process: the program's kernels may run until exit
+    CUfunction f = nullptr;
+    if (d.load(&mod, cubin.data()) != CUDA_SUCCESS || d.get(&f, mod, name.c_str()) != CUDA_SUCCESS) {
+        *log = "module load failed";
+        return false;
+    }
+    *fn = reinterpret_cast<void*>(f);
+    return true;
+}
+
+cudaError_t launch_row_kernel(void* fn, const TaskBatch& b, int rows, int workers, cudaStream_t s) {
+    const Driver& d = driver();
+    const int64_t nrows = b.ntasks * rows;
+    int64_t blocks = std::min<int64_t>((nrows + 7) / 8, static_cast<int64_t>(sm_count()) * 8);
+    if (workers > 0) blocks = std::min<int64_t>(blocks, workers);
+    blocks = std::max<int64_t>(blocks, 1);
+    TaskBatch tb = b;
+    void* args[] = {&tb};
+    const CUresult r = d.launch(reinterpret_cast<CUfunction>(fn), static_cast<unsigned>(blocks), 1, 1, 256, 1, 1, 0,
+                                reinterpret_cast<CUstream>(s), args, nullptr);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorLaunchFailure;
+}
+
+}  // namespace ptowsp::jit

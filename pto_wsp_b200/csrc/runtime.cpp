@@ -26,6 +26,7 @@
 #include <sstream>
 #include <unordered_set>
 
+#include "jit.hpp"
 #include "runtime.hpp"
 
 namespace ptowsp {
@@ -690,7 +691,18 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
         }
         case ImplKind::TileProgram:
             if (!ki.tp_ok) throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
-            e = dev::launch_tile_program(tb, ki.tp_dev, ki.tp_smem, workers, P.stream);
+            if (ki.jit_state == 0) jit_prepare(ki, kd, B.kernel);  // a fast-path kernel that fell back here
+            if (ki.jit_state == 2) {
+                void* fn = nullptr;
+                if (jit::load_cubin(ki.jit_cubin, "ptowsp_rows_k" + std::to_string(B.kernel), &fn, &ki.jit_note)) {
+                    ki.jit_fn = fn;
+                    ki.jit_state = 1;
+                } else {
+                    ki.jit_state = -1;
+                }
+            }
+            if (ki.jit_state == 1) e = jit::launch_row_kernel(ki.jit_fn, tb, ki.tp.slots[0].rows, workers, P.stream);
+            else e = dev::launch_tile_program(tb, ki.tp_dev, ki.tp_smem, workers, P.stream);
             break;
         case ImplKind::PagedDecode: {
             const dev::ParamDesc &K = tb.p[1], &V = tb.p[2];
@@ -894,6 +906,16 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
 }
 
 }  // namespace
+
+void jit_prepare(KernelImpl& ki, const KernelDef& kd, int k) {
+    ki.jit_state = -1;
+    if (!ki.tp_ok || !jit::row_local(ki.tp, &ki.jit_note)) return;
+    int types[dev::kMaxParams] = {};
+    for (const auto& kp : kd.params)
+        if (kp.tensor_index >= 0 && kp.tensor_index < dev::kMaxParams) types[kp.tensor_index] = ptype(kp.v.dtype);
+    const std::string name = "ptowsp_rows_k" + std::to_string(k);
+    if (jit::compile_cubin(jit::gen_row_kernel(ki.tp, types, name), name, &ki.jit_cubin, &ki.jit_note)) ki.jit_state = 2;
+}
 
 uint64_t run_program(Program& P, RuntimeContext* ctx) {
     auto t_start = std::chrono::steady_clock::now();

@@ -32,7 +32,15 @@ struct KernelImpl {
     std::string tp_error;
     dev::TileProgram* tp_dev = nullptr;  // device copy
     int scalar_page_size = 16, scalar_kv_heads = 1;  // paged decode static params
+    // fused row kernel of a row-local tile program: 0 not tried, 2 compiled (cubin), 1 loaded, -1 interpreter
+    int jit_state = 0;
+    std::string jit_cubin;
+    void* jit_fn = nullptr;              // CUfunction once loaded
+    std::string jit_note;                // why the interpreter runs instead
 };
+
+// Build (NVRTC) the fused row kernel of kernel `k` when its tile program is row-local (jit_state -> 2 or -1).
+void jit_prepare(KernelImpl& ki, const KernelDef& kd, int k);
 
 // Per-tensor binding of one run.
 struct TensorBinding {

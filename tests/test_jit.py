@@ -1,0 +1,66 @@
+"""Row-program compiler, host side (no GPU needed).
+
+Generic row-local kernels (element-wise ops, row broadcasts, row reductions
+over whole tiles) get a fused kernel built with NVRTC when the program is
+compiled; other kernels keep the tile-program interpreter and say why.
+"""
+
+import pytest
+
+from pto_wsp_b200 import workloads
+from pto_wsp_b200.runtime import CudaExecutable
+from pto_wsp_b200.workloads import KernelBuilder, _pfor, _plan, _schedule, _targ, _task
+
+
+def rowmax_shift_plan(B, T, R, C, dtype_x="f32"):
+    """out = (x - rowmax(x)) * y: element-wise ops, a row reduction and a row broadcast."""
+    k = KernelBuilder("shift_scale")
+    x = k.param("x", dtype_x, R, C)
+    y = k.param("y", "f32", R, C)
+    out = k.param("out", "f32", R, C)
+    m = k.op("RowMax", [x], ("f32", R, 1))
+    d = k.op("Sub", [x, m], ("f32", R, C))
+    p = k.op("Mul", [d, y], ("f32", R, C))
+    k.store(out, p)
+    body = _pfor("b", B, _pfor("h", T, _task("shift_scale", ["b", "h"], [
+        _targ("x", 0, 4, ["b", "h"]), _targ("y", 1, 4, ["b", "h"]), _targ("out", 2, 4, ["b", "h"])])))
+    return _plan("shift_scale", [(dtype_x, [B, T, R, C]), ("f32", [B, T, R, C]), ("f32", [B, T, R, C])],
+                 [k.build()], body, _schedule())
+
+
+def nvrtc_available() -> bool:
+    return CudaExecutable(rowmax_shift_plan(1, 1, 4, 40)).describe()["kernels"][0]["row_kernel_note"] != "NVRTC not found"
+
+
+@pytest.mark.parametrize("cols,dtype", [(40, "f32"), (96, "f16"), (1000, "f32"), (1, "f32")])
+def test_generic_row_kernels_compile(cols, dtype):
+    if not nvrtc_available():
+        pytest.skip("NVRTC not installed")
+    d = CudaExecutable(rowmax_shift_plan(2, 3, 8, cols, dtype)).describe()["kernels"][0]
+    assert d["impl"] == "tile_program"
+    assert d["row_kernel"] == "compiled", d["row_kernel_note"]
+
+
+def col_broadcast_plan(R, C):
+    k = KernelBuilder("sub_col")
+    x = k.param("x", "f32", R, C)
+    v = k.param("v", "f32", 1, C)
+    out = k.param("out", "f32", R, C)
+    k.store(out, k.op("Sub", [x, v], ("f32", R, C)))
+    body = _pfor("b", 2, _task("sub_col", ["b"], [_targ("x", 0, 3, ["b"]), _targ("v", 1, 3, ["b"]),
+                                                   _targ("out", 2, 3, ["b"])]))
+    return _plan("sub_col", [("f32", [2, R, C]), ("f32", [2, 1, C]), ("f32", [2, R, C])], [k.build()], body,
+                 _schedule())
+
+
+def test_kernels_outside_the_row_local_set_keep_the_interpreter():
+    d = CudaExecutable(col_broadcast_plan(4, 64)).describe()["kernels"][0]
+    assert d["impl"] == "tile_program"
+    assert d["row_kernel"] == "interpreter" and d["row_kernel_note"]  # the [1, C] operand is not a row tile
+    wide = CudaExecutable(rowmax_shift_plan(1, 1, 2, 1100)).describe()["kernels"][0]  # 1100 > 1024 columns
+    assert wide["row_kernel"] == "interpreter" and "1024" in wide["row_kernel_note"]
+
+
+def test_fast_row_kernels_build_theirs_only_on_fallback():
+    d = CudaExecutable(workloads.rmsnorm_plan(2, 2, 16, 96)).describe()["kernels"][0]
+    assert d["impl"] == "rmsnorm_rows" and d["row_kernel"] == "not built"
