@@ -229,10 +229,15 @@ bool row_local(const TileProgram& tp, std::string* why) {
     return true;
 }
 
-std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const std::string& name) {
+namespace {
+
+// One kernel of the row program.  vec = false: lane l holds columns l, l+32, ... (4-byte accesses, any stride);
+// vec = true: lane l holds columns 128j+4l .. +3 (one 16-byte (f32/i32) or 8-byte (f16) access per quad;
+// unit column stride, 16-byte-aligned rows).
+void emit_row_kernel(std::ostringstream& o, const TileProgram& tp, const int* param_types, const std::string& name,
+                     bool vec) {
     const int R = tp.slots[0].rows;
-    std::ostringstream o;
-    o << "#define MAXP " << kMaxParams << "\n" << kPrelude;
+    auto nwords = [&](int cols) { return vec ? 4 * ((cols + 127) / 128) : (cols + 31) / 32; };
     o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(TaskBatch b) {\n";
     o << "  const int lane = threadIdx.x & 31;\n";
     o << "  const int64_t nrows = b.ntasks * " << R << "LL;\n";
@@ -240,55 +245,108 @@ std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const 
     o << "    const int64_t task = g / " << R << "; const int r = (int)(g - task * " << R << ");\n";
     o << "    const int64_t* rec = b.rec + task * b.stride;\n";
     for (int i = 0; i < tp.nslots; ++i) {
-        const TPSlot& s = tp.slots[i];
-        if (s.cols > 1) o << "    unsigned s" << i << "[" << (s.cols + 31) / 32 << "];\n";
+        const TPSlot& sl = tp.slots[i];
+        if (sl.cols > 1) o << "    unsigned s" << i << "[" << nwords(sl.cols) << "];\n";
         else o << "    unsigned s" << i << " = 0u;\n";
     }
     auto elem = [&](int slot, const std::string& j) {
         return tp.slots[slot].cols > 1 ? "s" + std::to_string(slot) + "[" + j + "]" : "s" + std::to_string(slot);
     };
+    // column of register word j of a lane
+    const std::string col = vec ? "(128 * (j >> 2) + 4 * lane + (j & 3))" : "(lane + 32 * j)";
     for (int ii = 0; ii < tp.ninstr; ++ii) {
         const TPInstr& in = tp.ins[ii];
-        o << "    { // " << ii << "\n";
+        o << "    { // instruction " << ii << "\n";
         switch (in.op) {
-            case TP_LOAD: {
-                const TPSlot& d = tp.slots[in.dst];
-                const std::string p = "b.p[" + std::to_string(in.param) + "]";
-                const int nj = (d.cols + 31) / 32;
-                o << "      const int64_t base = rec[" << in.param << "] + (int64_t)r * " << p << ".s3;\n";
-                o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
-                o << "        const int c = lane + 32 * j; unsigned w = 0u;\n";
-                o << "        if (c < " << d.cols << ") { const int64_t off = base + (int64_t)c * " << p << ".s4;\n";
-                o << "          if (off >= 0 && off < " << p << ".numel_span) w = "
-                  << load_expr(param_types[in.param], d.word, p, "off") << ";\n";
-                o << "          else atomicOr(b.err, " << kErrBounds << "); }\n";
-                o << "        " << (d.cols > 1 ? "s" + std::to_string(in.dst) + "[j] = w;" : "if (j == 0) s" + std::to_string(in.dst) + " = __shfl_sync(0xffffffffu, w, 0);") << "\n";
-                o << "      }\n";
-                break;
-            }
+            case TP_LOAD:
             case TP_STORE: {
-                const TPSlot& a = tp.slots[in.a];
+                const bool load = in.op == TP_LOAD;
+                const int slot = load ? in.dst : in.a;
+                const TPSlot& t = tp.slots[slot];
+                const int pt = param_types[in.param];
                 const std::string p = "b.p[" + std::to_string(in.param) + "]";
-                const int nj = (a.cols + 31) / 32;
                 o << "      const int64_t base = rec[" << in.param << "] + (int64_t)r * " << p << ".s3;\n";
+                if (vec && t.cols > 1) {
+                    const int nq = (t.cols + 127) / 128;
+                    const bool half = pt == PT_F16;
+                    o << "      #pragma unroll\n      for (int q = 0; q < " << nq << "; ++q) {\n";
+                    o << "        const int c0 = 128 * q + 4 * lane;\n";
+                    o << "        if (c0 < " << t.cols << ") { const int64_t off = base + c0;\n";
+                    o << "          if (off >= 0 && off + 3 < " << p << ".numel_span) {\n";
+                    if (load) {
+                        if (half) {
+                            o << "            const uint2 raw = *(const uint2*)(((const unsigned short*)" << p << ".base) + off);\n";
+                            o << "            const unsigned short h[4] = {(unsigned short)(raw.x & 0xffffu), (unsigned short)(raw.x >> 16), "
+                                 "(unsigned short)(raw.y & 0xffffu), (unsigned short)(raw.y >> 16)};\n";
+                            for (int e = 0; e < 4; ++e)
+                                o << "            s" << slot << "[4 * q + " << e << "] = "
+                                  << (t.word == W_F32 ? "__float_as_uint(h2f(h[" + std::to_string(e) + "]))"
+                                                      : "(unsigned)(int)h2f(h[" + std::to_string(e) + "])")
+                                  << ";\n";
+                        } else {
+                            o << "            const uint4 raw = *(const uint4*)(((const unsigned*)" << p << ".base) + off);\n";
+                            const char* comp[4] = {"raw.x", "raw.y", "raw.z", "raw.w"};
+                            for (int e = 0; e < 4; ++e) {
+                                std::string w;
+                                if (t.word == W_F32) {
+                                    if (pt == PT_F32) w = comp[e];
+                                    else if (pt == PT_I32) w = std::string("__float_as_uint((float)(int)") + comp[e] + ")";
+                                    else w = std::string("__float_as_uint((float)") + comp[e] + ")";
+                                } else {
+                                    w = pt == PT_F32 ? std::string("(unsigned)(int)__uint_as_float(") + comp[e] + ")" : comp[e];
+                                }
+                                o << "            s" << slot << "[4 * q + " << e << "] = " << w << ";\n";
+                            }
+                        }
+                    } else {
+                        std::string f[4];
+                        for (int e = 0; e < 4; ++e) {
+                            const std::string w = "s" + std::to_string(slot) + "[4 * q + " + std::to_string(e) + "]";
+                            f[e] = t.word == W_F32 ? "__uint_as_float(" + w + ")"
+                                                   : (t.word == W_I32 ? "(float)(int)(" + w + ")" : "(float)(" + w + ")");
+                            if (pt == PT_F16) f[e] = "f2h(" + f[e] + ")";
+                            else if (pt == PT_F32) f[e] = "__float_as_uint(" + f[e] + ")";
+                            else if (pt == PT_I32) f[e] = t.word == W_F32 ? "(unsigned)(int)" + f[e] : "(" + w + ")";
+                            else f[e] = t.word == W_F32 ? "(unsigned)" + f[e] : "(" + w + ")";
+                        }
+                        if (half)
+                            o << "            *(uint2*)(((unsigned short*)" << p << ".base) + off) = make_uint2((unsigned)" << f[0]
+                              << " | ((unsigned)" << f[1] << " << 16), (unsigned)" << f[2] << " | ((unsigned)" << f[3] << " << 16));\n";
+                        else
+                            o << "            *(uint4*)(((unsigned*)" << p << ".base) + off) = make_uint4(" << f[0] << ", " << f[1]
+                              << ", " << f[2] << ", " << f[3] << ");\n";
+                    }
+                    o << "          } else atomicOr(b.err, " << kErrBounds << "); }\n";
+                    o << "      }\n";
+                    break;
+                }
+                const int nj = (t.cols + 31) / 32;  // scalar accesses (also [R,1] tiles in the vector kernel)
                 o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
-                o << "        const int c = lane + 32 * j;\n";
-                o << "        if (c < " << a.cols << ") { const int64_t off = base + (int64_t)c * " << p << ".s4;\n";
-                o << "          if (off >= 0 && off < " << p << ".numel_span) { "
-                  << store_stmt(param_types[in.param], a.word, p, "off", elem(in.a, "j")) << " }\n";
+                o << "        const int c = lane + 32 * j;" << (load ? " unsigned w = 0u;" : "") << "\n";
+                o << "        if (c < " << t.cols << ") { const int64_t off = base + (int64_t)c * " << p << ".s4;\n";
+                if (load) {
+                    o << "          if (off >= 0 && off < " << p << ".numel_span) w = " << load_expr(pt, t.word, p, "off") << ";\n";
+                } else {
+                    o << "          if (off >= 0 && off < " << p << ".numel_span) { "
+                      << store_stmt(pt, t.word, p, "off", t.cols > 1 ? elem(slot, "j") : elem(slot, "0")) << " }\n";
+                }
                 o << "          else atomicOr(b.err, " << kErrBounds << "); }\n";
+                if (load) {
+                    if (t.cols > 1) o << "        " << elem(slot, "j") << " = w;\n";
+                    else o << "        if (j == 0) " << elem(slot, "0") << " = __shfl_sync(0xffffffffu, w, 0);\n";
+                }
                 o << "      }\n";
                 break;
             }
             case TP_MOV: case TP_BIN: case TP_BINS: case TP_EXP: case TP_RSQRT: {
                 const TPSlot& d = tp.slots[in.dst];
-                const int nj = (d.cols + 31) / 32;
+                const int nj = d.cols > 1 ? nwords(d.cols) : 1;
                 if (in.op == TP_BINS) {
                     // the scalar operand as the op's word type (TP_BINS semantics of the interpreter)
                     const bool fw = d.word == W_F32;
                     if (in.scalar_src >= 0) {
-                        o << "      const unsigned long long raw = (unsigned long long)rec[b.nparams + b.naxis + "
-                          << in.scalar_src << "];\n";
+                        o << "      const unsigned long long raw = (unsigned long long)rec[b.nparams + b.naxis + " << in.scalar_src
+                          << "];\n";
                         const int st = tp.scalar_types[in.scalar_src];
                         if (st == 0) o << (fw ? "      const unsigned ws = (unsigned)raw;\n"
                                               : "      const unsigned ws = (unsigned)(int)__uint_as_float((unsigned)raw);\n");
@@ -299,8 +357,8 @@ std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const 
                     } else {
                         unsigned fbits;
                         std::memcpy(&fbits, &in.fval, 4);
-                        o << "      const unsigned ws = " << (fw ? std::to_string(fbits) + "u" : "(unsigned)(" + std::to_string(in.ival) + ")")
-                          << ";\n";
+                        o << "      const unsigned ws = "
+                          << (fw ? std::to_string(fbits) + "u" : "(unsigned)(" + std::to_string(in.ival) + ")") << ";\n";
                     }
                 }
                 o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
@@ -317,11 +375,11 @@ std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const 
             }
             case TP_ROWSUM: case TP_ROWMAX: case TP_ROWMEAN: {
                 const TPSlot& a = tp.slots[in.a];
-                const int nj = (a.cols + 31) / 32;
+                const int nj = a.cols > 1 ? nwords(a.cols) : 1;
                 const bool mx = in.op == TP_ROWMAX;
                 o << "      float acc = " << (mx ? "-__int_as_float(0x7f800000)" : "0.f") << ";\n";
                 o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j)\n";
-                o << "        if (lane + 32 * j < " << a.cols << ") acc = "
+                o << "        if (" << (a.cols > 1 ? col : std::string("lane")) << " < " << (a.cols > 1 ? a.cols : 1) << ") acc = "
                   << (mx ? "fmaxf(acc, __uint_as_float(" + elem(in.a, "j") + "))"
                          : "__fadd_rn(acc, __uint_as_float(" + elem(in.a, "j") + "))")
                   << ";\n";
@@ -329,7 +387,7 @@ std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const 
                   << (mx ? "fmaxf(acc, __shfl_xor_sync(0xffffffffu, acc, o))" : "__fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o))")
                   << ";\n";
                 if (in.op == TP_ROWMEAN) o << "      acc = __fdiv_rn(acc, (float)" << in.k << ");\n";
-                o << "      s" << in.dst << " = __float_as_uint(acc);\n";
+                o << "      " << elem(in.dst, "0") << " = __float_as_uint(acc);\n";
                 break;
             }
             default: break;
@@ -337,6 +395,26 @@ std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const 
         o << "    }\n";
     }
     o << "  }\n}\n";
+}
+
+}  // namespace
+
+bool vector_form(const TileProgram& tp, const int* param_types) {
+    for (int ii = 0; ii < tp.ninstr; ++ii) {
+        const TPInstr& in = tp.ins[ii];
+        if (in.op != TP_LOAD && in.op != TP_STORE) continue;
+        const TPSlot& t = tp.slots[in.op == TP_LOAD ? in.dst : in.a];
+        const int pt = param_types[in.param];
+        if (t.cols > 1 && (t.cols % 4 != 0 || !(pt == PT_F32 || pt == PT_I32 || pt == PT_U32 || pt == PT_F16))) return false;
+    }
+    return true;
+}
+
+std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const std::string& name) {
+    std::ostringstream o;
+    o << "#define MAXP " << kMaxParams << "\n" << kPrelude;
+    emit_row_kernel(o, tp, param_types, name, false);
+    if (vector_form(tp, param_types)) emit_row_kernel(o, tp, param_types, name + "_v", true);
     return o.str();
 }
 
@@ -392,7 +470,7 @@ bool load_cubin(const std::string& cubin, const std::string& name, void** fn, st
 cudaError_t launch_row_kernel(void* fn, const TaskBatch& b, int rows, int workers, cudaStream_t s) {
     const Driver& d = driver();
     const int64_t nrows = b.ntasks * rows;
-    int64_t blocks = std::min<int64_t>((nrows + 7) / 8, static_cast<int64_t>(sm_count()) * 8);
+    int64_t blocks = std::min<int64_t>((nrows + 7) / 8, static_cast<int64_t>(sm_count()) * 8);  // 8 warps per block
     if (workers > 0) blocks = std::min<int64_t>(blocks, workers);
     blocks = std::max<int64_t>(blocks, 1);
     TaskBatch tb = b;

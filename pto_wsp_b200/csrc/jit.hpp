@@ -14,7 +14,10 @@ namespace ptowsp::jit {
 bool row_local(const dev::TileProgram& tp, std::string* why);
 
 // CUDA source of the fused kernel `name` for a row-local program; param_types[i] is the ParamType of param i.
+// When vector_form() holds the source also has `name`_v, the variant with 16-byte (8-byte for f16) accesses
+// for unit column strides and 16-byte-aligned rows.
 std::string gen_row_kernel(const dev::TileProgram& tp, const int* param_types, const std::string& name);
+bool vector_form(const dev::TileProgram& tp, const int* param_types);
 
 // Compile `src` for sm_100a with NVRTC (no GPU needed); false with `log` set when NVRTC is unavailable or the
 // compilation fails.

@@ -693,15 +693,21 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
             if (!ki.tp_ok) throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
             if (ki.jit_state == 0) jit_prepare(ki, kd, B.kernel);  // a fast-path kernel that fell back here
             if (ki.jit_state == 2) {
+                const std::string name = "ptowsp_rows_k" + std::to_string(B.kernel);
                 void* fn = nullptr;
-                if (jit::load_cubin(ki.jit_cubin, "ptowsp_rows_k" + std::to_string(B.kernel), &fn, &ki.jit_note)) {
+                if (jit::load_cubin(ki.jit_cubin, name, &fn, &ki.jit_note)) {
                     ki.jit_fn = fn;
                     ki.jit_state = 1;
+                    void* fv = nullptr;
+                    std::string note;
+                    if (jit::load_cubin(ki.jit_cubin, name + "_v", &fv, &note)) ki.jit_fn_vec = fv;  // absent: scalar only
                 } else {
                     ki.jit_state = -1;
                 }
             }
-            if (ki.jit_state == 1) e = jit::launch_row_kernel(ki.jit_fn, tb, ki.tp.slots[0].rows, workers, P.stream);
+            if (ki.jit_state == 1)
+                e = jit::launch_row_kernel(rows_ok && ki.jit_fn_vec ? ki.jit_fn_vec : ki.jit_fn, tb, ki.tp.slots[0].rows,
+                                           workers, P.stream);
             else e = dev::launch_tile_program(tb, ki.tp_dev, ki.tp_smem, workers, P.stream);
             break;
         case ImplKind::PagedDecode: {

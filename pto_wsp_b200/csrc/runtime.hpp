@@ -36,6 +36,7 @@ struct KernelImpl {
     int jit_state = 0;
     std::string jit_cubin;
     void* jit_fn = nullptr;              // CUfunction once loaded
+    void* jit_fn_vec = nullptr;          // its vector-access variant, when the program has one
     std::string jit_note;                // why the interpreter runs instead
 };
 
