@@ -582,12 +582,18 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default: --steps, max 20)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the per-rank batch (small profiling cases)")
+    ap.add_argument("--cols", type=int, default=None,
+                    help="rmsnorm/softmax: tile width other than the config's (widths without a hand-written row "
+                         "kernel run the fused row-program kernel built at run time)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = dict(WORKLOADS[args.workload])
     if args.batch:
         wl["batch"] = args.batch
         wl["config"] += f" [batch overridden to {args.batch}]"
+    if args.cols and "cols" in wl:
+        wl["cols"] = args.cols
+        wl["config"] += f" [tile width overridden to {args.cols}]"
 
     rank = _env_int("RANK", 0)
     world = _env_int("WORLD_SIZE", 1)
@@ -686,7 +692,9 @@ def main() -> None:
     per_launch_ms = ms / args.steps
     achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
     kernel_name = "softmax_rows" if args.workload == "softmax" else "rmsnorm_rows"
-    traffic = traffic_from_profiles(kernel_name, args.workload, args.batch)
+    if ex.describe()["kernels"][0].get("row_kernel") == "loaded":
+        kernel_name = "ptowsp_rows_k0 (row program built with NVRTC)"
+    traffic = traffic_from_profiles(kernel_name, args.workload, args.batch or args.cols)
 
     # spot-check the last device result against the numpy definition on a few tiles
     xs = x.reshape(-1, R, Cc)[:64].double().cpu().numpy()

@@ -397,6 +397,191 @@ void emit_row_kernel(std::ostringstream& o, const TileProgram& tp, const int* pa
     o << "  }\n}\n";
 }
 
+// Lanes per row for the vector kernel: the power of two L that leaves the fewest lanes idle on `quads`
+// 16-byte column groups, with at most 8 quads per lane (32 registers per tile); ties go to the larger L.
+int lanes_per_row(int quads) {
+    int best = 32, waste = 1 << 30;
+    for (int L = 32; L >= 1; L >>= 1) {
+        const int per = (quads + L - 1) / L;
+        if (per > 8) break;
+        const int w = per * L - quads;
+        if (w < waste) {
+            waste = w;
+            best = L;
+        }
+    }
+    return best;
+}
+
+// The vector kernel: each tile row is handled by a group of L lanes (32 / L rows per warp), lane `sub` of a
+// group holds the 4-column quads sub, sub + L, ... of the row; 16-byte (f32/i32) or 8-byte (f16) accesses;
+// row reductions by shuffles inside the group.  Needs unit column strides and 16-byte-aligned rows.
+void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* param_types, const std::string& name) {
+    const int R = tp.slots[0].rows;
+    int cmax = 4;
+    for (int i = 0; i < tp.nslots; ++i) cmax = std::max(cmax, tp.slots[i].cols);
+    const int L = lanes_per_row((cmax + 3) / 4);
+    const int RW = 32 / L;
+    auto nq = [&](int cols) { return (cols + 4 * L - 1) / (4 * L); };  // quads per lane
+    o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(TaskBatch b) {\n";
+    bool bcast_load = false;
+    for (int ii = 0; ii < tp.ninstr; ++ii)
+        if (tp.ins[ii].op == TP_LOAD && tp.slots[tp.ins[ii].dst].cols == 1) bcast_load = true;
+    o << "  const int lane = threadIdx.x & 31, sub = lane & " << L - 1 << ";\n";
+    if (bcast_load) o << "  const int leader = lane & ~" << L - 1 << ";\n";
+    o << "  const int64_t nrows = b.ntasks * " << R << "LL;\n";
+    o << "  for (int64_t g0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * " << RW << "; g0 < nrows; g0 += (int64_t)gridDim.x * "
+      << 8 * RW << ") {\n";
+    o << "    const int64_t g = g0 + (lane >> " << __builtin_ctz(L) << "); const bool v = g < nrows;\n";
+    o << "    const int64_t task = v ? g / " << R << " : 0; const int r = (int)(v ? g - task * " << R << " : 0);\n";
+    o << "    const int64_t* rec = b.rec + task * b.stride;\n";
+    for (int i = 0; i < tp.nslots; ++i) {
+        const TPSlot& sl = tp.slots[i];
+        if (sl.cols > 1) o << "    unsigned s" << i << "[" << 4 * nq(sl.cols) << "];\n";
+        else o << "    unsigned s" << i << " = 0u;\n";
+    }
+    auto elem = [&](int slot, const std::string& j) {
+        return tp.slots[slot].cols > 1 ? "s" + std::to_string(slot) + "[" + j + "]" : "s" + std::to_string(slot);
+    };
+    for (int ii = 0; ii < tp.ninstr; ++ii) {
+        const TPInstr& in = tp.ins[ii];
+        o << "    { // instruction " << ii << "\n";
+        switch (in.op) {
+            case TP_LOAD:
+            case TP_STORE: {
+                const bool load = in.op == TP_LOAD;
+                const int slot = load ? in.dst : in.a;
+                const TPSlot& t = tp.slots[slot];
+                const int pt = param_types[in.param];
+                const std::string p = "b.p[" + std::to_string(in.param) + "]";
+                o << "      const int64_t base = rec[" << in.param << "] + (int64_t)r * " << p << ".s3;\n";
+                if (t.cols == 1) {  // [R,1]: the group leader's element, broadcast inside the group
+                    if (load) {
+                        o << "      unsigned w = 0u;\n";
+                        o << "      if (v && sub == 0) { if (base >= 0 && base < " << p << ".numel_span) w = "
+                          << load_expr(pt, t.word, p, "base") << "; else atomicOr(b.err, " << kErrBounds << "); }\n";
+                        o << "      s" << slot << " = __shfl_sync(0xffffffffu, w, leader);\n";
+                    } else {
+                        o << "      if (v && sub == 0) { if (base >= 0 && base < " << p << ".numel_span) { "
+                          << store_stmt(pt, t.word, p, "base", "s" + std::to_string(slot)) << " } else atomicOr(b.err, "
+                          << kErrBounds << "); }\n";
+                    }
+                    break;
+                }
+                const bool half = pt == PT_F16;
+                o << "      #pragma unroll\n      for (int q = 0; q < " << nq(t.cols) << "; ++q) {\n";
+                o << "        const int c0 = 4 * (sub + " << L << " * q);\n";
+                o << "        if (v && c0 < " << t.cols << ") { const int64_t off = base + c0;\n";
+                o << "          if (off >= 0 && off + 3 < " << p << ".numel_span) {\n";
+                if (load) {
+                    if (half) {
+                        o << "            const uint2 raw = *(const uint2*)(((const unsigned short*)" << p << ".base) + off);\n";
+                        o << "            const unsigned short h[4] = {(unsigned short)(raw.x & 0xffffu), (unsigned short)(raw.x >> 16), "
+                             "(unsigned short)(raw.y & 0xffffu), (unsigned short)(raw.y >> 16)};\n";
+                        for (int e = 0; e < 4; ++e)
+                            o << "            s" << slot << "[4 * q + " << e << "] = "
+                              << (t.word == W_F32 ? "__float_as_uint(h2f(h[" + std::to_string(e) + "]))"
+                                                  : "(unsigned)(int)h2f(h[" + std::to_string(e) + "])")
+                              << ";\n";
+                    } else {
+                        o << "            const uint4 raw = *(const uint4*)(((const unsigned*)" << p << ".base) + off);\n";
+                        const char* comp[4] = {"raw.x", "raw.y", "raw.z", "raw.w"};
+                        for (int e = 0; e < 4; ++e) {
+                            std::string w;
+                            if (t.word == W_F32) {
+                                if (pt == PT_F32) w = comp[e];
+                                else if (pt == PT_I32) w = std::string("__float_as_uint((float)(int)") + comp[e] + ")";
+                                else w = std::string("__float_as_uint((float)") + comp[e] + ")";
+                            } else {
+                                w = pt == PT_F32 ? std::string("(unsigned)(int)__uint_as_float(") + comp[e] + ")" : comp[e];
+                            }
+                            o << "            s" << slot << "[4 * q + " << e << "] = " << w << ";\n";
+                        }
+                    }
+                } else {
+                    std::string f[4];
+                    for (int e = 0; e < 4; ++e) {
+                        const std::string w = "s" + std::to_string(slot) + "[4 * q + " + std::to_string(e) + "]";
+                        f[e] = t.word == W_F32 ? "__uint_as_float(" + w + ")"
+                                               : (t.word == W_I32 ? "(float)(int)(" + w + ")" : "(float)(" + w + ")");
+                        if (pt == PT_F16) f[e] = "f2h(" + f[e] + ")";
+                        else if (pt == PT_F32) f[e] = "__float_as_uint(" + f[e] + ")";
+                        else if (pt == PT_I32) f[e] = t.word == W_F32 ? "(unsigned)(int)" + f[e] : "(" + w + ")";
+                        else f[e] = t.word == W_F32 ? "(unsigned)" + f[e] : "(" + w + ")";
+                    }
+                    if (half)
+                        o << "            *(uint2*)(((unsigned short*)" << p << ".base) + off) = make_uint2((unsigned)" << f[0]
+                          << " | ((unsigned)" << f[1] << " << 16), (unsigned)" << f[2] << " | ((unsigned)" << f[3] << " << 16));\n";
+                    else
+                        o << "            *(uint4*)(((unsigned*)" << p << ".base) + off) = make_uint4(" << f[0] << ", " << f[1] << ", "
+                          << f[2] << ", " << f[3] << ");\n";
+                }
+                o << "          } else atomicOr(b.err, " << kErrBounds << "); }\n";
+                o << "      }\n";
+                break;
+            }
+            case TP_MOV: case TP_BIN: case TP_BINS: case TP_EXP: case TP_RSQRT: {
+                const TPSlot& d = tp.slots[in.dst];
+                const int nj = d.cols > 1 ? 4 * nq(d.cols) : 1;
+                if (in.op == TP_BINS) {
+                    const bool fw = d.word == W_F32;
+                    if (in.scalar_src >= 0) {
+                        o << "      const unsigned long long raw = (unsigned long long)rec[b.nparams + b.naxis + " << in.scalar_src
+                          << "];\n";
+                        const int st = tp.scalar_types[in.scalar_src];
+                        if (st == 0) o << (fw ? "      const unsigned ws = (unsigned)raw;\n"
+                                              : "      const unsigned ws = (unsigned)(int)__uint_as_float((unsigned)raw);\n");
+                        else if (st == 2) o << (fw ? "      const unsigned ws = __float_as_uint((float)(long long)raw);\n"
+                                                   : "      const unsigned ws = (unsigned)(int)raw;\n");
+                        else o << (fw ? "      const unsigned ws = __float_as_uint((float)(int)raw);\n"
+                                      : "      const unsigned ws = (unsigned)(int)raw;\n");
+                    } else {
+                        unsigned fbits;
+                        std::memcpy(&fbits, &in.fval, 4);
+                        o << "      const unsigned ws = "
+                          << (fw ? std::to_string(fbits) + "u" : "(unsigned)(" + std::to_string(in.ival) + ")") << ";\n";
+                    }
+                }
+                o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
+                std::string rhs;
+                const std::string a = elem(in.a, "j");
+                if (in.op == TP_MOV) rhs = a;
+                else if (in.op == TP_BIN) rhs = bin_expr(d.word, in.sub, a, in.mode == MODE_ROW ? elem(in.b, "0") : elem(in.b, "j"));
+                else if (in.op == TP_BINS) rhs = in.scalar_first ? bin_expr(d.word, in.sub, "ws", a) : bin_expr(d.word, in.sub, a, "ws");
+                else if (in.op == TP_EXP) rhs = "__float_as_uint(expf(__uint_as_float(" + a + ")))";
+                else rhs = "__float_as_uint(__fdiv_rn(1.0f, sqrtf(__uint_as_float(" + a + "))))";
+                o << "        " << elem(in.dst, "j") << " = " << rhs << ";\n";
+                o << "      }\n";
+                break;
+            }
+            case TP_ROWSUM: case TP_ROWMAX: case TP_ROWMEAN: {
+                const TPSlot& a = tp.slots[in.a];
+                const bool mx = in.op == TP_ROWMAX;
+                o << "      float acc = " << (mx ? "-__int_as_float(0x7f800000)" : "0.f") << ";\n";
+                if (a.cols > 1) {
+                    o << "      #pragma unroll\n      for (int j = 0; j < " << 4 * nq(a.cols) << "; ++j)\n";
+                    o << "        if (4 * (sub + " << L << " * (j >> 2)) + (j & 3) < " << a.cols << ") acc = "
+                      << (mx ? "fmaxf(acc, __uint_as_float(" + elem(in.a, "j") + "))"
+                             : "__fadd_rn(acc, __uint_as_float(" + elem(in.a, "j") + "))")
+                      << ";\n";
+                } else {
+                    o << "      if (sub == 0) acc = __uint_as_float(" << elem(in.a, "0") << ");\n";
+                }
+                if (L > 1)
+                    o << "      #pragma unroll\n      for (int o = " << L / 2 << "; o > 0; o >>= 1) acc = "
+                      << (mx ? "fmaxf(acc, __shfl_xor_sync(0xffffffffu, acc, o))" : "__fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o))")
+                      << ";\n";
+                if (in.op == TP_ROWMEAN) o << "      acc = __fdiv_rn(acc, (float)" << in.k << ");\n";
+                o << "      " << elem(in.dst, "0") << " = __float_as_uint(acc);\n";
+                break;
+            }
+            default: break;
+        }
+        o << "    }\n";
+    }
+    o << "  }\n}\n";
+}
+
 }  // namespace
 
 bool vector_form(const TileProgram& tp, const int* param_types) {
@@ -414,7 +599,7 @@ std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const 
     std::ostringstream o;
     o << "#define MAXP " << kMaxParams << "\n" << kPrelude;
     emit_row_kernel(o, tp, param_types, name, false);
-    if (vector_form(tp, param_types)) emit_row_kernel(o, tp, param_types, name + "_v", true);
+    if (vector_form(tp, param_types)) emit_group_kernel(o, tp, param_types, name + "_v");
     return o.str();
 }
 

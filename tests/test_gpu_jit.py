@@ -16,7 +16,7 @@ from pto_wsp_b200.runtime import CudaExecutable
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("cols,dtype", [(40, "f32"), (96, "f16"), (600, "f32"), (1, "f32")])
+@pytest.mark.parametrize("cols,dtype", [(40, "f32"), (96, "f16"), (600, "f32"), (1, "f32"), (4, "f32"), (12, "f16"), (200, "f16"), (1024, "f32")])
 def test_generic_row_kernel_bit_exact(cols, dtype, require_cuda):
     rng = np.random.default_rng(cols)
     B, T, R = 3, 5, 8
