@@ -673,9 +673,12 @@ std::unique_ptr<Program> compile_program(const char* text, size_t len, int devic
         else ki.kind = ImplKind::TileProgram;
         if (ki.kind == ImplKind::TileProgram && !ki.tp_ok)
             throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
-        // a generic kernel gets its fused row kernel built now (NVRTC, no GPU needed); the fast row ops build
-        // theirs only if a launch falls back to the tile program
-        if (ki.kind == ImplKind::TileProgram) jit_prepare(ki, kd, static_cast<int>(i));
+        // a generic kernel gets its fused row kernel built now (NVRTC, no GPU needed), and so does a fast row op
+        // whose tile width the hand-written kernel does not take; the others build theirs only if a launch falls
+        // back to the tile program (unaligned views)
+        const bool odd_width = (ki.kind == ImplKind::RmsNorm || ki.kind == ImplKind::Softmax) &&
+                               !dev::row_width_supported(kd.params[0].v.cols);
+        if (ki.kind == ImplKind::TileProgram || odd_width) jit_prepare(ki, kd, static_cast<int>(i));
     }
     prog->tensor_key_depth.assign(plan.tensors.size(), -1);
     collect_depths(plan, *plan.body, prog->tensor_key_depth);

@@ -93,6 +93,8 @@ struct TileProgram {
 // error; `workers` caps the number of CTAs (task window), 0 = automatic.
 // ---------------------------------------------------------------------------
 
+// Tile widths the hand-written RMSNorm / softmax row kernels take (others run the fused row program).
+inline bool row_width_supported(int cols) { return cols == 128 || cols == 256 || cols == 512 || cols == 1024; }
 cudaError_t launch_rmsnorm_rows(const TaskBatch& b, int workers, cudaStream_t s);
 cudaError_t launch_softmax_rows(const TaskBatch& b, int workers, cudaStream_t s);
 cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev, int smem_bytes, int workers,

@@ -423,7 +423,10 @@ void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* 
     const int L = lanes_per_row((cmax + 3) / 4);
     const int RW = 32 / L;
     auto nq = [&](int cols) { return (cols + 4 * L - 1) / (4 * L); };  // quads per lane
-    o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(TaskBatch b) {\n";
+    // occupancy: at most 256 / (words per lane + 36) blocks' worth of registers per thread, up to 4 blocks per SM
+    // (the loop is latency-bound on its loads; 4 x 8 warps hides them, measured on softmax rows of 200 columns)
+    const int minb = std::min(4, std::max(1, 256 / (4 * nq(cmax) + 36)));
+    o << "extern \"C\" __global__ void __launch_bounds__(256, " << minb << ") " << name << "(TaskBatch b) {\n";
     bool bcast_load = false;
     for (int ii = 0; ii < tp.ninstr; ++ii)
         if (tp.ins[ii].op == TP_LOAD && tp.slots[tp.ins[ii].dst].cols == 1) bcast_load = true;
@@ -469,13 +472,16 @@ void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* 
                     break;
                 }
                 const bool half = pt == PT_F16;
+                // the row is contiguous: one bounds check per row; quads below `full` are valid in every lane
+                o << "      const bool rok = v && base >= 0 && base + " << t.cols << " <= " << p << ".numel_span;\n";
+                o << "      if (v && !rok) atomicOr(b.err, " << kErrBounds << ");\n";
                 o << "      #pragma unroll\n      for (int q = 0; q < " << nq(t.cols) << "; ++q) {\n";
                 o << "        const int c0 = 4 * (sub + " << L << " * q);\n";
-                o << "        if (v && c0 < " << t.cols << ") { const int64_t off = base + c0;\n";
-                o << "          if (off >= 0 && off + 3 < " << p << ".numel_span) {\n";
+                o << "        if (rok && (q < " << t.cols / (4 * L) << " || c0 < " << t.cols << ")) { const int64_t off = base + c0;\n";
+                o << "          {\n";
                 if (load) {
                     if (half) {
-                        o << "            const uint2 raw = *(const uint2*)(((const unsigned short*)" << p << ".base) + off);\n";
+                        o << "            const uint2 raw = __ldcs((const uint2*)(((const unsigned short*)" << p << ".base) + off));\n";
                         o << "            const unsigned short h[4] = {(unsigned short)(raw.x & 0xffffu), (unsigned short)(raw.x >> 16), "
                              "(unsigned short)(raw.y & 0xffffu), (unsigned short)(raw.y >> 16)};\n";
                         for (int e = 0; e < 4; ++e)
@@ -484,7 +490,7 @@ void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* 
                                                   : "(unsigned)(int)h2f(h[" + std::to_string(e) + "])")
                               << ";\n";
                     } else {
-                        o << "            const uint4 raw = *(const uint4*)(((const unsigned*)" << p << ".base) + off);\n";
+                        o << "            const uint4 raw = __ldcs((const uint4*)(((const unsigned*)" << p << ".base) + off));\n";
                         const char* comp[4] = {"raw.x", "raw.y", "raw.z", "raw.w"};
                         for (int e = 0; e < 4; ++e) {
                             std::string w;
@@ -510,13 +516,13 @@ void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* 
                         else f[e] = t.word == W_F32 ? "(unsigned)" + f[e] : "(" + w + ")";
                     }
                     if (half)
-                        o << "            *(uint2*)(((unsigned short*)" << p << ".base) + off) = make_uint2((unsigned)" << f[0]
-                          << " | ((unsigned)" << f[1] << " << 16), (unsigned)" << f[2] << " | ((unsigned)" << f[3] << " << 16));\n";
+                        o << "            __stcs((uint2*)(((unsigned short*)" << p << ".base) + off), make_uint2((unsigned)" << f[0]
+                          << " | ((unsigned)" << f[1] << " << 16), (unsigned)" << f[2] << " | ((unsigned)" << f[3] << " << 16)));\n";
                     else
-                        o << "            *(uint4*)(((unsigned*)" << p << ".base) + off) = make_uint4(" << f[0] << ", " << f[1] << ", "
-                          << f[2] << ", " << f[3] << ");\n";
+                        o << "            __stcs((uint4*)(((unsigned*)" << p << ".base) + off), make_uint4(" << f[0] << ", " << f[1] << ", "
+                          << f[2] << ", " << f[3] << "));\n";
                 }
-                o << "          } else atomicOr(b.err, " << kErrBounds << "); }\n";
+                o << "          } }\n";
                 o << "      }\n";
                 break;
             }
@@ -560,7 +566,7 @@ void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* 
                 o << "      float acc = " << (mx ? "-__int_as_float(0x7f800000)" : "0.f") << ";\n";
                 if (a.cols > 1) {
                     o << "      #pragma unroll\n      for (int j = 0; j < " << 4 * nq(a.cols) << "; ++j)\n";
-                    o << "        if (4 * (sub + " << L << " * (j >> 2)) + (j & 3) < " << a.cols << ") acc = "
+                    o << "        if ((j >> 2) < " << a.cols / (4 * L) << " || 4 * (sub + " << L << " * (j >> 2)) < " << a.cols << ") acc = "
                       << (mx ? "fmaxf(acc, __uint_as_float(" + elem(in.a, "j") + "))"
                              : "__fadd_rn(acc, __uint_as_float(" + elem(in.a, "j") + "))")
                       << ";\n";

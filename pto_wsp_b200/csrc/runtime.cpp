@@ -19,8 +19,10 @@
 
 #include <algorithm>
 #include <chrono>
+#include <fstream>
 #include <functional>
 #include <unordered_map>
+#include <cstdlib>
 #include <cstring>
 #include <queue>
 #include <sstream>
@@ -577,7 +579,7 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
     ImplKind kind = ki.kind;
     if ((kind == ImplKind::RmsNorm || kind == ImplKind::Softmax)) {
         const int c = kd.params[0].v.cols;
-        if (!rows_ok || !(c == 128 || c == 256 || c == 512 || c == 1024)) kind = ImplKind::TileProgram;
+        if (!rows_ok || !dev::row_width_supported(c)) kind = ImplKind::TileProgram;
     }
     if ((kind == ImplKind::Matmul || kind == ImplKind::MatmulAcc) && !ki.tp_ok && B.fast_ok == 0)
         throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': operands do not meet the tcgen05 layout "
@@ -920,7 +922,12 @@ void jit_prepare(KernelImpl& ki, const KernelDef& kd, int k) {
     for (const auto& kp : kd.params)
         if (kp.tensor_index >= 0 && kp.tensor_index < dev::kMaxParams) types[kp.tensor_index] = ptype(kp.v.dtype);
     const std::string name = "ptowsp_rows_k" + std::to_string(k);
-    if (jit::compile_cubin(jit::gen_row_kernel(ki.tp, types, name), name, &ki.jit_cubin, &ki.jit_note)) ki.jit_state = 2;
+    const std::string src = jit::gen_row_kernel(ki.tp, types, name);
+    if (const char* dir = std::getenv("PTOWSP_JIT_DUMP")) {  // keep the generated source for inspection
+        std::ofstream f(std::string(dir) + "/" + name + ".cu");
+        f << src;
+    }
+    if (jit::compile_cubin(src, name, &ki.jit_cubin, &ki.jit_note)) ki.jit_state = 2;
 }
 
 uint64_t run_program(Program& P, RuntimeContext* ctx) {

@@ -61,6 +61,10 @@ def test_kernels_outside_the_row_local_set_keep_the_interpreter():
     assert wide["row_kernel"] == "interpreter" and "1024" in wide["row_kernel_note"]
 
 
-def test_fast_row_kernels_build_theirs_only_on_fallback():
-    d = CudaExecutable(workloads.rmsnorm_plan(2, 2, 16, 96)).describe()["kernels"][0]
+def test_fast_row_kernels_build_theirs_for_odd_widths_only():
+    # width 128 runs the hand-written kernel: its row program is built only if a launch falls back (unaligned views)
+    d = CudaExecutable(workloads.rmsnorm_plan(2, 2, 16, 128)).describe()["kernels"][0]
     assert d["impl"] == "rmsnorm_rows" and d["row_kernel"] == "not built"
+    # width 96 is not one the hand-written kernel takes: the fused row program is built at compile time
+    d = CudaExecutable(workloads.rmsnorm_plan(2, 2, 16, 96)).describe()["kernels"][0]
+    assert d["impl"] == "rmsnorm_rows" and d["row_kernel"] == "compiled"
