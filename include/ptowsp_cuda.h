@@ -150,6 +150,8 @@ typedef struct ptowsp_timing {
     uint64_t waves;       /* dependency waves */
     uint64_t h2d_bytes;   /* host->device bytes staged */
     uint64_t d2h_bytes;   /* device->host bytes staged */
+    uint64_t slot_syncs;  /* device reads made for slot_load_u64 (one per device input read, one per load of
+                             data that an enqueued task writes, after those tasks finish) */
 } ptowsp_timing;
 
 PTOWSP_API int ptowsp_cuda_last_timing(const ptowsp_program* prog, ptowsp_timing* out);

@@ -683,8 +683,10 @@ cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cu
 // ---------------------------------------------------------------------------
 
 constexpr int kTopkThreads = 1024;
-constexpr int kTopkWarps = kTopkThreads / 32;
-constexpr int kHistCopies = 16;  // lane-private copies of the 256-bin histogram (lanes l and l+16 share one)
+constexpr int kHistCopies = 16;                    // lane-private copies of the 256-bin histogram (lanes l, l+16 share one)
+constexpr int kTopkSmemMax = 227 * 1024 - 2048;    // opt-in dynamic shared memory less this kernel's static part
+constexpr int kCandMax = 4096;                     // candidate list of the last radix pass
+constexpr int kTieMax = 512;                       // ties at the threshold ranked pairwise up to this many
 
 __device__ __forceinline__ uint32_t order_key(float f) {
     // Larger float -> larger unsigned key; -0.0 and +0.0 map to the same key.
@@ -693,62 +695,159 @@ __device__ __forceinline__ uint32_t order_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// (key, index) composite: larger key first, then lower index first, as one unsigned compare.
+__device__ __forceinline__ unsigned long long topk_composite(uint32_t key, int index) {
+    return (static_cast<unsigned long long>(key) << 32) | (0xffffffffu - static_cast<uint32_t>(index));
+}
+
 struct TopkLayout {  // dynamic shared memory, in bytes
-    int keys, scratch, comp, total;
+    int keys, scratch, comp, cand, cand_cap, total;
     __host__ __device__ TopkLayout(int n, int k2) {
         keys = 0;
-        scratch = ((n * 4 + 15) / 16) * 16;  // histogram during the select, (round, warp) counts during the gather
-        const int rounds = (n + kTopkThreads - 1) / kTopkThreads;
-        const int hist = 256 * kHistCopies * 4, counts = rounds * kTopkWarps * 4;
-        comp = scratch + ((hist > counts ? hist : counts) + 15) / 16 * 16;
-        total = comp + k2 * 8;
+        scratch = ((n * 4 + 15) / 16) * 16;  // histogram during the select; tie list / per-warp counts after it
+        comp = scratch + 256 * kHistCopies * 4;
+        cand = comp + k2 * 8;
+        const int room = (kTopkSmemMax - cand) / 8;
+        cand_cap = room < 0 ? 0 : (room > kCandMax ? kCandMax : room);
+        total = cand + cand_cap * 8;
     }
 };
 
-// Exclusive prefix sum over the block of one value per thread; returns this
-// thread's prefix, *total gets the sum.  Two barriers.
-__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_tot, uint32_t* total) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    uint32_t inc = v;
+// Append `v` for every lane with `p` set to buf[*counter ...] (one shared atomic per warp; slots in lane
+// order within the warp).  The counter keeps counting past `cap`, so an overflow is visible; nothing is
+// stored at or beyond `cap`.
+__device__ __forceinline__ void warp_append(bool p, unsigned long long v, unsigned long long* buf, uint32_t* counter,
+                                            uint32_t cap, int lane) {
+    const unsigned bal = __ballot_sync(0xffffffffu, p);
+    if (bal == 0u) return;
+    uint32_t pos = 0;
+    if (lane == 0) pos = atomicAdd(counter, static_cast<uint32_t>(__popc(bal)));
+    pos = __shfl_sync(0xffffffffu, pos, 0) + __popc(bal & ((1u << lane) - 1u));
+    if (p && pos < cap) buf[pos] = v;
+}
+
+// warp_append for four values per lane with one atomic per warp: values of slot j of every lane come before
+// those of slot j + 1.
+__device__ __forceinline__ void warp_append4(const bool (&p)[4], const unsigned long long (&v)[4], unsigned long long* buf,
+                                             uint32_t* counter, uint32_t cap, int lane) {
+    unsigned bal[4];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t n = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += n;
+    for (int j = 0; j < 4; ++j) bal[j] = __ballot_sync(0xffffffffu, p[j]);
+    if ((bal[0] | bal[1] | bal[2] | bal[3]) == 0u) return;
+    uint32_t pos = 0;
+    if (lane == 0)
+        pos = atomicAdd(counter, static_cast<uint32_t>(__popc(bal[0]) + __popc(bal[1]) + __popc(bal[2]) + __popc(bal[3])));
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    const unsigned below = (1u << lane) - 1u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t at = pos + __popc(bal[j] & below);
+        if (p[j] && at < cap) buf[at] = v[j];
+        pos += __popc(bal[j]);
     }
-    if (lane == 31) warp_tot[wid] = inc;
-    __syncthreads();
-    if (wid == 0) {
-        const uint32_t t = warp_tot[lane];
-        uint32_t s = t;
+}
+
+// Bitonic sort, descending, of the K2 composites in `comp` with E of them per thread in registers: thread t
+// holds elements E*t .. E*t+E-1 (K2 / E threads, whole warps, take part).  Strides below E are compare-exchanges
+// inside the thread, strides below 32*E shuffles with lane ^ (stride / E), longer ones go through shared memory
+// (one block barrier each).  Then the first K indices are written to `dst`.  Every thread of the block calls it.
+template <int E>
+__device__ __forceinline__ void bitonic_sort_store(unsigned long long* comp, int K2, int K, int32_t* dst, int64_t ds) {
+    const int t = threadIdx.x;
+    const int nthr = K2 / E;
+    const bool active = t < nthr;
+    const int et = E * t;
+    unsigned long long e[E];
+    __syncthreads();  // the gather wrote across warps
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t n = __shfl_up_sync(0xffffffffu, s, o);
-            if (lane >= o) s += n;
+    for (int j = 0; j < E; ++j) e[j] = active ? comp[et + j] : 0ull;
+    for (int size = 2; size <= K2; size <<= 1) {
+        int stride = size >> 1;
+        if (stride >= 32 * E) {
+            if (active) {
+#pragma unroll
+                for (int j = 0; j < E; ++j) comp[et + j] = e[j];
+            }
+            for (; stride >= 32 * E; stride >>= 1) {
+                __syncthreads();
+                if (active) {
+#pragma unroll
+                    for (int q = 0; q < E / 2; ++q) {
+                        const int p = t + q * nthr;
+                        const int lo = 2 * p - (p & (stride - 1));
+                        const int hi = lo + stride;
+                        const bool desc = (lo & size) == 0;
+                        const unsigned long long x = comp[lo], y = comp[hi];
+                        if ((x < y) == desc) {
+                            comp[lo] = y;
+                            comp[hi] = x;
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            if (active) {
+#pragma unroll
+                for (int j = 0; j < E; ++j) e[j] = comp[et + j];
+            }
         }
-        warp_tot[lane] = s - t;  // exclusive prefix of the warp totals
-        if (lane == 31) *total = s;
+        if (active) {
+            // strides >= E: the partner is the same slot of lane ^ (stride / E); whether this thread keeps the
+            // larger value depends only on the thread (E*t + j and E*t agree on every bit >= E)
+            const bool up = (et & size) == 0;
+            for (; stride >= E; stride >>= 1) {
+                const bool keep_max = ((et & stride) == 0) == up;
+                const int lx = stride / E;
+#pragma unroll
+                for (int j = 0; j < E; ++j) {
+                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, e[j], lx);
+                    if ((other > e[j]) == keep_max) e[j] = other;
+                }
+            }
+#pragma unroll
+            for (int st = E / 2; st >= 1; st >>= 1) {
+                if (st <= stride) {
+#pragma unroll
+                    for (int j = 0; j < E; ++j) {
+                        if ((j & st) == 0) {
+                            const bool desc = size > E / 2 ? up : (j & size) == 0;
+                            const unsigned long long a = e[j], c = e[j + st];
+                            if ((a < c) == desc) {
+                                e[j] = c;
+                                e[j + st] = a;
+                            }
+                        }
+                    }
+                }
+            }
+        }
     }
-    __syncthreads();
-    return warp_tot[wid] + inc - v;
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+        const int i = et + j;
+        if (active && i < K) dst[i * ds] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(e[j] & 0xffffffffull));
+    }
 }
 
 // One CTA per row.  (1) Keys: the row as order-preserving 32-bit keys in
-// shared memory.  (2) Select: the exact K-th largest key by a 4-pass 8-bit
-// radix select; each pass histograms the keys that match the digits chosen so
-// far into lane-private copies of a 256-bin histogram (no two lanes of a warp
-// add to the same counter in the same instruction), sums the copies, and one
-// warp finds the digit holding the K-th key.  (3) Gather in index order:
-// per (1024-index round, warp) counts of keys above the threshold and equal to
-// it, one block-wide scan, then every key above the threshold and the first
-// `need` equal keys (the lowest indices, as the reference's stable order
-// takes them) are written as (key, ~index) composites.  (4) Bitonic sort of
-// the composites, descending; compare-exchanges within a warp's 64 elements
-// synchronise only the warp.  Bit-exact by construction.
+// shared memory, histogrammed by their top digit as they are stored.
+// (2) Select: the exact K-th largest key by a 4-pass 8-bit radix select; each
+// pass histograms the keys that match the digits chosen so far into
+// lane-private copies of a 256-bin histogram (no two lanes of a warp add to
+// the same counter in the same instruction), sums the copies, and one warp
+// finds the digit holding the K-th key.  Pass 2 also sorts the row out: keys
+// above the 16-bit prefix are winners whatever their last digits and go
+// straight to the composite buffer; keys that match it are listed as the
+// candidates that pass 3 scans instead of the row.  (3) Gather: the
+// candidates above the threshold join the winners; keys equal to the
+// threshold join them too when all are taken, otherwise the `need` of lowest
+// index (the reference's stable order) are ranked by index.  (4) Bitonic sort
+// of the (key, ~index) composites, descending.  Winners land in arbitrary
+// slots; the sort's total order makes the result exact.
 __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) {
     extern __shared__ __align__(16) uint8_t tsm[];
     __shared__ uint32_t bin_tot[256];
-    __shared__ uint32_t warp_tot[32];
-    __shared__ uint32_t s_prefix, s_need, s_total;
+    __shared__ uint32_t s_prefix, s_need, s_eq, s_ncand, s_nwin, s_ntie;
     const int64_t task = blockIdx.x;
     if (task >= b.ntasks) return;
     const int64_t* rec = b.rec + task * b.stride;
@@ -759,27 +858,105 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     while (K2 < K) K2 <<= 1;
     const TopkLayout lay(N, K2);
     uint32_t* ks = reinterpret_cast<uint32_t*>(tsm + lay.keys);
+    const uint4* ks4 = reinterpret_cast<const uint4*>(ks);
     uint32_t* hist = reinterpret_cast<uint32_t*>(tsm + lay.scratch);
-    uint32_t* cnt = hist;  // reused after the select
     unsigned long long* comp = reinterpret_cast<unsigned long long*>(tsm + lay.comp);
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(tsm + lay.cand);
+    const uint32_t cand_cap = static_cast<uint32_t>(lay.cand_cap);
     const float* src = reinterpret_cast<const float*>(S.base) + rec[0];
     const int64_t ss = S.s4;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int rounds = (N + kTopkThreads - 1) / kTopkThreads;
+    const int n4 = (N + 3) >> 2;  // 16-byte groups of keys (the last one may be partial; the buffer is padded)
+    uint32_t* hl = hist + (lane & (kHistCopies - 1));
 
-    // (1) keys
-    for (int i = threadIdx.x; i < N; i += kTopkThreads) ks[i] = order_key(src[i * ss]);
+    // (1) keys, histogrammed for the first pass on the way in
+    for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
+    if (threadIdx.x == 0) {
+        s_ncand = 0u;
+        s_nwin = 0u;
+        s_ntie = 0u;
+    }
+    __syncthreads();
+    int head = 0;  // keys [0, head) come in 16-byte vectors, eight per thread in flight
+    if (ss == 1 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const int f4 = N >> 2;
+        head = f4 << 2;
+        const float4* src4 = reinterpret_cast<const float4*>(src);
+        uint4* w4 = reinterpret_cast<uint4*>(ks);
+        for (int base = 0; base < f4; base += 8 * kTopkThreads) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * kTopkThreads + threadIdx.x;
+                if (i < f4) v[j] = __ldg(src4 + i);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * kTopkThreads + threadIdx.x;
+                if (i < f4) {
+                    const uint4 kk = make_uint4(order_key(v[j].x), order_key(v[j].y), order_key(v[j].z), order_key(v[j].w));
+                    w4[i] = kk;
+                    atomicAdd(hl + (kk.x >> 24) * kHistCopies, 1u);
+                    atomicAdd(hl + (kk.y >> 24) * kHistCopies, 1u);
+                    atomicAdd(hl + (kk.z >> 24) * kHistCopies, 1u);
+                    atomicAdd(hl + (kk.w >> 24) * kHistCopies, 1u);
+                }
+            }
+        }
+    }
+    for (int i0 = head; i0 < N; i0 += 8 * kTopkThreads) {  // strided rows and the ragged tail
+        uint32_t kk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = i0 + j * kTopkThreads + threadIdx.x;
+            kk[j] = i < N ? order_key(src[static_cast<int64_t>(i) * ss]) : 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = i0 + j * kTopkThreads + threadIdx.x;
+            if (i < N) {
+                ks[i] = kk[j];
+                atomicAdd(hl + (kk[j] >> 24) * kHistCopies, 1u);
+            }
+        }
+    }
 
     // (2) radix select, most significant digit first
     uint32_t prefix = 0, need = static_cast<uint32_t>(K);
     for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
         const uint32_t hmask = pass == 0 ? 0u : (0xffffffffu << (shift + 8));
-        for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
-        __syncthreads();  // keys written (pass 0), previous totals read
-        for (int i = threadIdx.x; i < N; i += kTopkThreads) {
-            const uint32_t k = ks[i];
-            if ((k & hmask) == prefix) atomicAdd(&hist[((k >> shift) & 255u) * kHistCopies + (lane & (kHistCopies - 1))], 1u);
+        if (pass > 0) {
+            for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
+            __syncthreads();  // previous totals read, counters zeroed
+            if (pass == 3 && s_ncand <= cand_cap) {
+                const int nc = static_cast<int>(s_ncand);
+                for (int i = threadIdx.x; i < nc; i += kTopkThreads) {
+                    const uint32_t k = static_cast<uint32_t>(cand[i] >> 32);
+                    if ((k & hmask) == prefix) atomicAdd(hl + (k & 255u) * kHistCopies, 1u);
+                }
+            } else {
+                for (int base = 0; base < n4; base += kTopkThreads) {  // warps step together (ballots below)
+                    const int q = base + threadIdx.x;
+                    const uint4 k4 = q < n4 ? ks4[q] : make_uint4(0u, 0u, 0u, 0u);
+                    const int lim = N - 4 * q;  // keys of this group inside the row
+                    const uint32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
+                    bool m[4], w[4];
+                    unsigned long long c[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t k = kk[j];
+                        m[j] = j < lim && (k & hmask) == prefix;
+                        w[j] = j < lim && (k & hmask) > prefix;
+                        c[j] = topk_composite(k, 4 * q + j);
+                        if (m[j]) atomicAdd(hl + ((k >> shift) & 255u) * kHistCopies, 1u);
+                    }
+                    if (pass == 2) {
+                        warp_append4(m, c, cand, &s_ncand, cand_cap, lane);
+                        warp_append4(w, c, comp, &s_nwin, static_cast<uint32_t>(K), lane);
+                    }
+                }
+            }
         }
         __syncthreads();
         for (int bin = wid * 8; bin < wid * 8 + 8; ++bin) {
@@ -806,126 +983,115 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
             if (above < need && need <= suf) {
                 uint32_t acc = above;
                 int d = 8 * lane;
-                uint32_t rem = need - above;
+                uint32_t rem = need - above, cnt_d = 0;
 #pragma unroll
                 for (int j = 7; j >= 0; --j) {
                     if (acc + c[j] >= need) {
                         d = 8 * lane + j;
                         rem = need - acc;
+                        cnt_d = c[j];
                         break;
                     }
                     acc += c[j];
                 }
                 s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
                 s_need = rem;
+                s_eq = cnt_d;  // after the last pass: how many keys equal the threshold
             }
         }
         __syncthreads();
         prefix = s_prefix;
         need = s_need;
     }
-    const uint32_t thr = prefix;  // the K-th largest key; `need` keys equal to it are taken
+    const uint32_t thr = prefix;       // the K-th largest key; `need` keys equal to it are taken
+    const bool all_eq = s_eq == need;  // no tie to break: every key equal to the threshold is taken
+    const uint32_t n_gt = static_cast<uint32_t>(K) - need;  // keys strictly above the threshold
+    unsigned long long* tie = reinterpret_cast<unsigned long long*>(hist);  // histogram no longer needed
 
-    // (3) gather in index order: counts per (round, warp), packed (above << 16 | equal)
-    for (int r = 0; r < rounds; ++r) {
-        const int i = r * kTopkThreads + threadIdx.x;
-        const uint32_t k = i < N ? ks[i] : 0u;
-        const unsigned mgt = __ballot_sync(0xffffffffu, i < N && k > thr);
-        const unsigned meq = __ballot_sync(0xffffffffu, i < N && k == thr);
-        if (lane == 0) cnt[r * kTopkWarps + wid] = (static_cast<uint32_t>(__popc(mgt)) << 16) | __popc(meq);
+    // (3) gather the rest of the winners from the candidates (or, if they overflowed, from the row)
+    if (s_ncand <= cand_cap) {
+        const int nc = static_cast<int>(s_ncand);
+        for (int base = 0; base < nc; base += kTopkThreads) {
+            const int i = base + threadIdx.x;
+            const unsigned long long c = i < nc ? cand[i] : 0ull;
+            const uint32_t k = static_cast<uint32_t>(c >> 32);
+            warp_append(i < nc && (k > thr || (all_eq && k == thr)), c, comp, &s_nwin, static_cast<uint32_t>(K), lane);
+            if (!all_eq) warp_append(i < nc && k == thr, c, tie, &s_ntie, kTieMax, lane);
+        }
+    } else {
+        const uint32_t p16 = thr & 0xffff0000u;
+        for (int base = 0; base < N; base += kTopkThreads) {
+            const int i = base + threadIdx.x;
+            const uint32_t k = i < N ? ks[i] : 0u;
+            const bool in = i < N && (k & 0xffff0000u) == p16;
+            warp_append(in && (k > thr || (all_eq && k == thr)), topk_composite(k, i), comp, &s_nwin,
+                        static_cast<uint32_t>(K), lane);
+            if (!all_eq) warp_append(in && k == thr, topk_composite(k, i), tie, &s_ntie, kTieMax, lane);
+        }
     }
     __syncthreads();
-    {
-        // exclusive scan over the rounds * 32 entries in (round, warp) order; each thread scans up to 2 entries
-        const int E = rounds * kTopkWarps;
-        const int e0 = threadIdx.x * 2;
-        const uint32_t v0 = e0 < E ? cnt[e0] : 0u, v1 = e0 + 1 < E ? cnt[e0 + 1] : 0u;
-        const uint32_t pre = block_exclusive_scan(v0 + v1, warp_tot, &s_total);
-        if (e0 < E) cnt[e0] = pre;
-        if (e0 + 1 < E) cnt[e0 + 1] = pre + v0;
+    if (!all_eq) {
+        if (s_ntie <= static_cast<uint32_t>(kTieMax)) {
+            // rank the equal keys by index (same key: the larger composite has the lower index)
+            const int m = static_cast<int>(s_ntie);
+            for (int j = threadIdx.x; j < m; j += kTopkThreads) {
+                const unsigned long long c = tie[j];
+                uint32_t r = 0;
+                for (int q = 0; q < m; ++q) r += tie[q] > c;
+                if (r < need) comp[n_gt + r] = c;
+            }
+        } else {
+            // many ties: an index-ordered sweep over the row.  Warp w owns the contiguous segment
+            // [w * seg, (w + 1) * seg); the ballots of each round stay in registers (lane r holds rounds r and
+            // r + 32), one scan of the warp totals gives each warp its first rank.
+            uint32_t* cnt = hist;
+            const int rounds = (N + kTopkThreads - 1) / kTopkThreads;
+            const int s0 = wid * rounds * 32;
+            unsigned eq_lo = 0, eq_hi = 0;
+            uint32_t n_w = 0;
+            for (int r = 0; r < rounds; ++r) {
+                const int i = s0 + r * 32 + lane;
+                const unsigned me = __ballot_sync(0xffffffffu, i < N && ks[i] == thr);
+                n_w += __popc(me);
+                if (lane == (r & 31)) {
+                    if (r < 32) eq_lo = me;
+                    else eq_hi = me;
+                }
+            }
+            __syncthreads();  // the tie list is no longer read
+            if (lane == 0) cnt[wid] = n_w;
+            __syncthreads();
+            if (wid == 0) {
+                const uint32_t v = cnt[lane];
+                uint32_t inc = v;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t n = __shfl_up_sync(0xffffffffu, inc, o);
+                    if (lane >= o) inc += n;
+                }
+                cnt[lane] = inc - v;
+            }
+            __syncthreads();
+            uint32_t pe = cnt[wid];
+            for (int r = 0; r < rounds && pe < need; ++r) {
+                const unsigned me = __shfl_sync(0xffffffffu, r < 32 ? eq_lo : eq_hi, r & 31);
+                const uint32_t rank = pe + __popc(me & ((1u << lane) - 1u));
+                if (((me >> lane) & 1u) && rank < need) comp[n_gt + rank] = topk_composite(thr, s0 + r * 32 + lane);
+                pe += __popc(me);
+            }
+        }
     }
-    __syncthreads();
-    const uint32_t n_gt = s_total >> 16;  // keys strictly above the threshold (< K)
     for (int i = threadIdx.x; i < K2; i += kTopkThreads)
         if (i >= K) comp[i] = 0ull;  // padding sorts last
-    for (int r = 0; r < rounds; ++r) {
-        const int i = r * kTopkThreads + threadIdx.x;
-        const uint32_t k = i < N ? ks[i] : 0u;
-        const bool gt = i < N && k > thr, eq = i < N && k == thr;
-        const unsigned mgt = __ballot_sync(0xffffffffu, gt);
-        const unsigned meq = __ballot_sync(0xffffffffu, eq);
-        const uint32_t base = cnt[r * kTopkWarps + wid];
-        const unsigned below = (1u << lane) - 1u;
-        const unsigned long long c = (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
-        if (gt) {
-            const uint32_t slot = (base >> 16) + __popc(mgt & below);
-            if (slot < static_cast<uint32_t>(K)) comp[slot] = c;
-        } else if (eq) {
-            const uint32_t rank = (base & 0xffffu) + __popc(meq & below);
-            if (rank < need && n_gt + rank < static_cast<uint32_t>(K)) comp[n_gt + rank] = c;
-        }
-    }
+
     // (4) bitonic sort of K2 composites, descending (key desc, then index asc via the inverted index).
     int32_t* dst = reinterpret_cast<int32_t*>(O.base) + rec[1];
-    if (K2 >= 64 && K2 <= 2 * kTopkThreads) {
-        // Thread t holds elements 2t and 2t+1 in registers: stride 1 is a compare in the thread,
-        // strides 2..32 a shuffle with lane ^ (stride / 2); strides of 64 and more cross warps and go
-        // through shared memory, one block barrier each.
-        const int t = threadIdx.x;
-        const bool active = 2 * t < K2;  // K2 / 2 is a multiple of 32: whole warps are active or idle
-        __syncthreads();                 // the gather wrote across warps
-        unsigned long long e[2] = {active ? comp[2 * t] : 0ull, active ? comp[2 * t + 1] : 0ull};
-        for (int size = 2; size <= K2; size <<= 1) {
-            int stride = size >> 1;
-            if (stride >= 64) {
-                if (active) {
-                    comp[2 * t] = e[0];
-                    comp[2 * t + 1] = e[1];
-                }
-                for (; stride >= 64; stride >>= 1) {
-                    __syncthreads();
-                    if (active) {
-                        const int lo = 2 * t - (t & (stride - 1));
-                        const int hi = lo + stride;
-                        const bool desc = ((lo & size) == 0);
-                        const unsigned long long x = comp[lo], y = comp[hi];
-                        if ((x < y) == desc) {
-                            comp[lo] = y;
-                            comp[hi] = x;
-                        }
-                    }
-                }
-                __syncthreads();
-                if (active) {
-                    e[0] = comp[2 * t];
-                    e[1] = comp[2 * t + 1];
-                }
-            }
-            if (active) {
-                for (; stride >= 2; stride >>= 1) {
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const int i = 2 * t + j;
-                        const unsigned long long other = __shfl_xor_sync(0xffffffffu, e[j], stride >> 1);
-                        const bool keep_max = ((i & stride) == 0) == ((i & size) == 0);
-                        const unsigned long long hi_v = e[j] > other ? e[j] : other;
-                        const unsigned long long lo_v = e[j] > other ? other : e[j];
-                        e[j] = keep_max ? hi_v : lo_v;
-                    }
-                }
-                const bool desc = ((2 * t) & size) == 0;  // stride 1: the thread's own pair
-                if ((e[0] < e[1]) == desc) {
-                    const unsigned long long x = e[0];
-                    e[0] = e[1];
-                    e[1] = x;
-                }
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int i = 2 * t + j;
-            if (active && i < K) dst[i * O.s4] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(e[j] & 0xffffffffull));
-        }
+    if (K2 >= 128 && K2 <= 4 * kTopkThreads) {
+        bitonic_sort_store<4>(comp, K2, K, dst, O.s4);
+        return;
+    }
+    if (K2 == 64) {
+        bitonic_sort_store<2>(comp, K2, K, dst, O.s4);
         return;
     }
     // other sizes: every stage in shared memory.  Pair p touches elements of the 64-element block of
@@ -984,7 +1150,7 @@ int topk_smem_bytes(int n, int k) {
 }
 
 bool topk_supported(int n, int k) {
-    return n >= 1 && k >= 1 && k <= n && k <= 4096 && topk_smem_bytes(n, k) <= 227 * 1024 - 2048;  // opt-in max less static
+    return n >= 1 && n <= 65535 && k >= 1 && k <= n && k <= 4096 && topk_smem_bytes(n, k) <= 227 * 1024 - 2048;  // opt-in max less static
 }
 
 cudaError_t launch_topk_select(const TaskBatch& b, int, void*, size_t, cudaStream_t s) {

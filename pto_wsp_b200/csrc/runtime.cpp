@@ -106,6 +106,10 @@ struct Walker {
     std::function<void()> flush;
     bool dry = false;
     std::vector<uint8_t> written_any;  // tensors written by a task so far
+    // host copies of device tensors read by slot_load_u64 that no task of this run has written (yet): one
+    // device-to-host copy serves every slot load from that tensor instead of a synchronising read per load
+    std::vector<std::vector<unsigned char>> slot_mirror;
+    static constexpr size_t kSlotMirrorMax = size_t(64) << 20;
     // full-overwrite tracking: elements stored per tensor and whether any two stores hit the same tile
     std::vector<int64_t> write_elems;
     std::vector<std::unordered_set<uint64_t>> write_keys;
@@ -123,6 +127,7 @@ struct Walker {
                 static_cast<uint64_t>(p.plan.schedule.window_tasks)),
           log(lg) {
         written_any.assign(p.plan.tensors.size(), 0);
+        slot_mirror.resize(p.plan.tensors.size());
         write_elems.assign(p.plan.tensors.size(), 0);
         write_keys.resize(p.plan.tensors.size());
         write_partial.assign(p.plan.tensors.size(), 0);
@@ -297,9 +302,19 @@ struct Walker {
                 const DType dt = P.plan.tensors[ta.tensor].dtype;
                 const int eb = dtype_bytes(dt);
                 alignas(8) unsigned char buf[8] = {0};
-                if (!dry && (tb.on_device || written_any[ta.tensor])) {
-                    flush();  // device data: finish the enqueued waves, then read the element back
+                if (!dry && tb.on_device && !written_any[ta.tensor] && tb.bytes <= kSlotMirrorMax) {
+                    // device input that no enqueued task writes: no wave has to finish before reading it
+                    std::vector<unsigned char>& m = slot_mirror[ta.tensor];
+                    if (m.empty()) {
+                        m.resize(tb.bytes);
+                        PW_CUDA(cudaMemcpy(m.data(), tb.dev, tb.bytes, cudaMemcpyDeviceToHost));
+                        ++P.timing.slot_syncs;
+                    }
+                    std::memcpy(buf, m.data() + off * eb, eb);
+                } else if (!dry && (tb.on_device || written_any[ta.tensor])) {
+                    flush();  // data written by enqueued tasks: finish the waves, then read the element back
                     PW_CUDA(cudaMemcpy(buf, tb.dev + off * eb, eb, cudaMemcpyDeviceToHost));
+                    ++P.timing.slot_syncs;
                 } else {
                     std::memcpy(buf, static_cast<const char*>(tb.user_ptr) + off * eb, eb);
                 }

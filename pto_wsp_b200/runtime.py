@@ -72,6 +72,7 @@ class Timing(C.Structure):
         ("waves", C.c_uint64),
         ("h2d_bytes", C.c_uint64),
         ("d2h_bytes", C.c_uint64),
+        ("slot_syncs", C.c_uint64),
     ]
 
 

@@ -71,6 +71,26 @@ def test_topk_adversarial_rows_bit_exact(kind, require_cuda):
         assert out[r, 0].tolist() == stable_topk(s[r, 0], k).tolist()
 
 
+@pytest.mark.parametrize("kind", ["three_values", "top_half_equal", "narrow_band"])
+def test_topk_wide_rows_with_many_candidates_bit_exact(kind, require_cuda):
+    # more keys share the threshold's 16-bit prefix than the candidate list holds (it overflows to a row sweep),
+    # and more keys equal the threshold than the pairwise tie ranking takes (an index-ordered sweep breaks them)
+    rng = np.random.default_rng(11)
+    rows, n, k = 3, 32768, 2048
+    if kind == "three_values":
+        s = rng.integers(0, 3, (rows, 1, n)).astype(np.float32)
+    elif kind == "top_half_equal":
+        s = rng.standard_normal((rows, 1, n)).astype(np.float32)
+        s[:, :, rng.permutation(n)[: n // 2]] = 5.0
+    else:  # distinct values inside one 16-bit key prefix: many candidates, no ties
+        s = (1.0 + rng.permutation(n).astype(np.float32) * 2.0 ** -23).astype(np.float32).reshape(1, 1, n)
+        s = np.repeat(s, rows, axis=0)
+    out = np.full((rows, 1, k), -7, np.int32)
+    CudaExecutable(workloads.topk_plan(rows, n, k)).run_with_symbols([s, out], {}, {}, {})
+    for r in range(rows):
+        assert out[r, 0].tolist() == stable_topk(s[r, 0], k).tolist()
+
+
 @pytest.mark.parametrize("n,k", [(1, 1), (100, 7), (1000, 1000), (1025, 1), (5000, 33), (32768, 2048),
                                  (49152, 2048), (20000, 4096), (3000, 3000)])
 def test_topk_sizes_bit_exact(n, k, require_cuda):
