@@ -13,6 +13,9 @@ What it restates (reference file:line):
   slot set / load, per-task ``args`` = axis args + (valid_row, valid_col) per
   tensor param + scalar args (``:2499-2545``), view pointer = base + sum(idx *
   stride) (``:2570-2592``), s3/s4 strides (``:2593-2621``);
+* CSP pipelines with CSPT time semantics -- the process threads, channel
+  send / recv / close and the max-of-process-clocks result (``:1611-1705``,
+  ``:1759-2220``), with the processes interleaved in a fixed order;
 * the makespan model ``Scheduler::issue`` (``:1562-1606``) with round-robin /
   key-based worker choice (``:2679-2692``) and the TaskWindow stall;
 * the kernel bodies ``emit_kernel_cpp`` (``:470-1241``) as tile-op sequences,
@@ -830,7 +833,140 @@ class CpuSim:
             return cur
         if k == "task":
             return self._task(n, ready, axis_env, vals)
+        if k == "pipeline":
+            return max(ready, self._pipeline(n))
         raise ValueError(f"Unhandled workload node kind {k}")
+
+    # ---- CSP pipelines: CSPT time semantics (pto_codegen.cpp:1611-1705 channel, :1759-2220 processes) ----
+    # Each process has its own clock; a task adds its cycle charge to it; a channel carries (token, send time);
+    # a receive raises the receiver's clock to send time + latency and records it as the channel's last pop
+    # time; a sender that waited for room (or a rendezvous) raises its clock to the last pop time.  The
+    # pipeline's result is the largest clock.  The reference runs the processes as threads; this restatement
+    # interleaves them deterministically: the first runnable process in declaration order runs until its next
+    # channel operation completes (then the choice is made again) or blocks.
+
+    def _pipeline(self, n: dict) -> int:
+        lat = self.rt.symbols_u64.get(fnv1a_64("__pto_wsp_channel_latency_cycles"), 0)
+        names = {c["name"]: i for i, c in enumerate(n["channels"])}
+        chans = [{"cap": max(0, int(c["capacity"])), "buf": [], "closed": False, "rw": False, "has": False,
+                  "rdv": (0, 0), "last_pop": 0} for c in n["channels"]]
+        procs = []
+        for p in n["processes"]:
+            st = {"t": 0, "blocked": None, "done": False}
+            procs.append((p, st, self._cspt(p["body"], st, chans, names, lat, {}, {})))
+
+        def wake(kind: str, ci: int) -> None:
+            for _, q, _ in procs:
+                if q["blocked"] == (kind, ci):
+                    q["blocked"] = None
+
+        self._cspt_wake = wake
+        while True:
+            pick = next((i for i, (_, st, _) in enumerate(procs) if not st["done"] and st["blocked"] is None), None)
+            if pick is None:
+                if all(st["done"] for _, st, _ in procs):
+                    break
+                raise RuntimeError("CSP pipeline deadlock: every unfinished process waits on a channel")
+            p, st, gen = procs[pick]
+            try:
+                next(gen)
+            except StopIteration:
+                st["done"] = True
+                for name in p["produces"]:
+                    ci = names[name]
+                    chans[ci]["closed"] = True
+                    wake("send", ci)
+                    wake("recv", ci)
+        return max((st["t"] for _, st, _ in procs), default=0)
+
+    def _cspt(self, n: dict, st: dict, chans: list, names: dict, lat: int, axis_env: dict, vals: dict):
+        k = n["kind"]
+        if k in ("slot_set", "slot_load"):
+            self._node(n, 0, axis_env, vals)
+        elif k == "task":
+            st["t"] += self._task_run(n, axis_env, vals)[0]
+        elif k in ("parallel_for", "for_each"):
+            if n["axis"]["kind"] not in ("dense", "dense_dyn"):
+                raise ValueError("CSPT codegen: unsupported axis kind in loop")
+            var = n["var"]
+            for i in range(self._bounds(n["axis"], var)):
+                yield from self._cspt(n["body"], st, chans, names, lat, {**axis_env, fnv1a_64(var): i},
+                                      {**vals, var: i})
+        elif k == "cond":
+            _, c = eval_expr(n["pred"], ExprEnv(self.rt, axis_env))
+            yield from self._cspt(n["then"] if c else n["else"], st, chans, names, lat, axis_env, vals)
+        elif k in ("combine", "sequential"):
+            for ch in n["children"]:
+                yield from self._cspt(ch, st, chans, names, lat, axis_env, vals)
+        elif k == "send":
+            task = n["value"]
+            dur, args = self._task_run(task, axis_env, vals)
+            st["t"] += dur
+            token = args[0] if task["axis_args"] else 0
+            yield from self._send(chans, names[n["channel"]], token, st)
+        elif k == "consume":
+            ci = names[n["channel"]]
+            var = n["var"]
+            while True:
+                got, tok = yield from self._recv(chans, ci, lat, st)
+                if not got:
+                    break
+                yield from self._cspt(n["body"], st, chans, names, lat, {**axis_env, fnv1a_64(var): tok},
+                                      {**vals, var: tok})
+        else:
+            raise ValueError("CSPT codegen: unsupported node kind in process body")
+
+    def _send(self, chans: list, ci: int, token: int, st: dict):
+        c = chans[ci]
+        if c["cap"] > 0:
+            while not c["closed"] and len(c["buf"]) >= c["cap"]:
+                st["blocked"] = ("send", ci)
+                yield
+                st["t"] = max(st["t"], c["last_pop"])
+            if not c["closed"]:
+                c["buf"].append((token, st["t"]))
+                self._cspt_wake("recv", ci)
+            yield
+            return
+        while not c["closed"] and not c["rw"]:  # rendezvous: a receiver must be waiting
+            st["blocked"] = ("send", ci)
+            yield
+        if c["closed"]:
+            yield
+            return
+        c["rdv"] = (token, st["t"])
+        c["has"] = True
+        self._cspt_wake("recv", ci)
+        while not c["closed"] and c["has"]:
+            st["blocked"] = ("send", ci)
+            yield
+        st["t"] = max(st["t"], c["last_pop"])
+        yield
+
+    def _recv(self, chans: list, ci: int, lat: int, st: dict):
+        c = chans[ci]
+        if c["cap"] > 0:
+            while not c["buf"] and not c["closed"]:
+                st["blocked"] = ("recv", ci)
+                yield
+            if not c["buf"]:
+                return False, 0
+            tok, ts = c["buf"].pop(0)
+        else:
+            c["rw"] = True
+            self._cspt_wake("send", ci)
+            while not c["closed"] and not c["has"]:
+                st["blocked"] = ("recv", ci)
+                yield
+            c["rw"] = False
+            if not c["has"]:
+                return False, 0
+            (tok, ts), c["has"] = c["rdv"], False
+        st["t"] = max(st["t"], ts + lat)
+        c["last_pop"] = st["t"]
+        self._cspt_wake("send", ci)
+        yield
+        return True, tok
 
     def _arg(self, a: dict, vals: dict[str, int]) -> int:
         if "var" in a:
@@ -840,6 +976,22 @@ class CpuSim:
         return _u64(a["u64"])
 
     def _task(self, n: dict, ready: int, axis_env: dict[int, int], vals: dict[str, int]) -> int:
+        dur, args = self._task_run(n, axis_env, vals)
+        disp = self.dispatch
+        if not disp:
+            wid = 0
+        elif disp["policy"] in ("round_robin", "work_steal"):
+            wid = self.rr % self.sched.n
+            self.rr += 1
+        else:
+            if disp.get("key") is None:
+                raise ValueError("dispatch policy requires ScalarExpr key")
+            _, key = eval_expr(disp["key"], ExprEnv(self.rt, axis_env, args))
+            wid = (key & M64) % self.sched.n
+        return self.sched.issue(dur, int(wid), ready)
+
+    def _task_run(self, n: dict, axis_env: dict[int, int], vals: dict[str, int]) -> tuple[int, list[int]]:
+        """Run one task on the arrays; (its cycle charge, its u64 args)."""
         km = self.models.get(n["kernel"])
         if km is None:
             raise ValueError(f"Missing kernel def for task: {n['kernel']}")
@@ -866,18 +1018,7 @@ class CpuSim:
                     km.static_cycles = dur
         if self.log_tasks:
             self.task_log.append((n["kernel"], dict(vals), dur))
-        disp = self.dispatch
-        if not disp:
-            wid = 0
-        elif disp["policy"] in ("round_robin", "work_steal"):
-            wid = self.rr % self.sched.n
-            self.rr += 1
-        else:
-            if disp.get("key") is None:
-                raise ValueError("dispatch policy requires ScalarExpr key")
-            _, key = eval_expr(disp["key"], ExprEnv(self.rt, axis_env, args))
-            wid = (key & M64) % self.sched.n
-        return self.sched.issue(dur, int(wid), ready)
+        return dur, args
 
 
 def run_plan(plan: dict, arrays: list[np.ndarray], **kw) -> int:

@@ -586,10 +586,13 @@ void collect_depths(const Plan& plan, const Node& n, std::vector<int>& depth) {
         case Node::Kind::ParallelFor:
         case Node::Kind::ForEach:
         case Node::Kind::Select:
+        case Node::Kind::Send:
+        case Node::Kind::Consume:
             collect_depths(plan, *n.body, depth);
             break;
         case Node::Kind::Combine:
         case Node::Kind::Sequential:
+        case Node::Kind::Pipeline:
             for (auto& c : n.children) collect_depths(plan, *c, depth);
             break;
         case Node::Kind::Cond:
@@ -616,9 +619,12 @@ bool data_dependent(const Node& n) {
             return true;
         case Node::Kind::ParallelFor:
         case Node::Kind::ForEach:
+        case Node::Kind::Send:
+        case Node::Kind::Consume:
             return data_dependent(*n.body);
         case Node::Kind::Combine:
         case Node::Kind::Sequential:
+        case Node::Kind::Pipeline:
             for (auto& c : n.children)
                 if (data_dependent(*c)) return true;
             return false;

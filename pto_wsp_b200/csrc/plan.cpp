@@ -3,6 +3,8 @@
 // kernel tensor params by name, pto_codegen.cpp:2550-2568).
 #include "plan.hpp"
 
+#include <algorithm>
+#include <functional>
 #include <stdexcept>
 
 namespace ptowsp {
@@ -203,6 +205,49 @@ NodePtr parse_node(const json::Value& j) {
         n->slot_tensor = parse_tensor_arg(j.at("tensor_arg"));
         n->row = j.at("row").as_i64();
         n->col = j.at("col").as_i64();
+    } else if (k == "pipeline") {
+        n->kind = Node::Kind::Pipeline;
+        std::map<std::string, int> index;
+        for (auto& c : j.at("channels").arr) {
+            ChannelDef cd;
+            cd.name = c.at("name").as_str();
+            cd.capacity = std::max<int64_t>(0, c.at("capacity").as_i64());
+            index[cd.name] = static_cast<int>(n->channels.size());
+            n->channels.push_back(std::move(cd));
+        }
+        auto resolve = [&](const std::string& name) {
+            auto it = index.find(name);
+            if (it == index.end()) throw std::runtime_error("CSPT codegen: unknown channel: " + name);
+            return it->second;
+        };
+        for (auto& pj : j.at("processes").arr) {
+            ProcessDef pd;
+            pd.name = pj.at("name").as_str();
+            for (auto& c : pj.at("produces").arr) pd.produces.push_back(resolve(c.as_str()));
+            for (auto& c : pj.at("consumes").arr) pd.consumes.push_back(resolve(c.as_str()));
+            n->processes.push_back(std::move(pd));
+            n->children.push_back(parse_node(pj.at("body")));
+        }
+        // channels named by send / consume nodes of the process bodies
+        std::function<void(Node&)> bind = [&](Node& x) {
+            if (x.kind == Node::Kind::Send || x.kind == Node::Kind::Consume) x.channel = resolve(x.channel_name);
+            if (x.kind == Node::Kind::Pipeline) throw std::runtime_error("CSPT codegen: nested pipeline");
+            if (x.body) bind(*x.body);
+            for (auto& c : x.children) bind(*c);
+            if (x.then_n) bind(*x.then_n);
+            if (x.else_n) bind(*x.else_n);
+        };
+        for (auto& c : n->children) bind(*c);
+    } else if (k == "send") {
+        n->kind = Node::Kind::Send;
+        n->channel_name = j.at("channel").as_str();
+        n->body = parse_node(j.at("value"));
+        if (n->body->kind != Node::Kind::Task) throw std::runtime_error("CSPT codegen: send value must be a Task node");
+    } else if (k == "consume") {
+        n->kind = Node::Kind::Consume;
+        n->channel_name = j.at("channel").as_str();
+        n->var = j.at("var").as_str();
+        n->body = parse_node(j.at("body"));
     } else {
         throw std::runtime_error("plan: Unhandled workload node kind " + k);
     }
@@ -261,10 +306,13 @@ void bind_tasks(Plan& plan, Node& n) {
         case Node::Kind::ParallelFor:
         case Node::Kind::ForEach:
         case Node::Kind::Select:
+        case Node::Kind::Send:
+        case Node::Kind::Consume:
             bind_tasks(plan, *n.body);
             break;
         case Node::Kind::Combine:
         case Node::Kind::Sequential:
+        case Node::Kind::Pipeline:
             for (auto& c : n.children) bind_tasks(plan, *c);
             break;
         case Node::Kind::Cond:

@@ -57,8 +57,19 @@ struct Axis {
     uint64_t outer_sym = 0, lengths_sym = 0;
 };
 
+// CSP pipeline pieces (include/pto/wsp/ir/csp.hpp): channels by index within their pipeline.
+struct ChannelDef {
+    std::string name;
+    int64_t capacity = 0;  // 0: rendezvous
+};
+struct ProcessDef {
+    std::string name;
+    std::vector<int> produces, consumes;  // channel indices
+};
+
 struct Node {
-    enum class Kind : uint8_t { ParallelFor, ForEach, Task, Combine, Sequential, Cond, Select, SlotSet, SlotLoad };
+    enum class Kind : uint8_t { ParallelFor, ForEach, Task, Combine, Sequential, Cond, Select, SlotSet, SlotLoad,
+                                Pipeline, Send, Consume };
     Kind kind = Kind::Task;
     // loops / select
     std::string var;
@@ -81,6 +92,12 @@ struct Node {
     uint64_t slot_value = 0;
     TensorArg slot_tensor;
     int64_t row = 0, col = 0;
+    // pipeline: `children` holds the process bodies, in process order
+    std::vector<ChannelDef> channels;
+    std::vector<ProcessDef> processes;
+    // send (body = the task whose first axis arg is the token) / consume (var = the token's name, body)
+    std::string channel_name;
+    int channel = -1;
 };
 using NodePtr = std::shared_ptr<Node>;
 

@@ -24,6 +24,7 @@
 #include <unordered_map>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <queue>
 #include <sstream>
 #include <unordered_set>
@@ -389,11 +390,33 @@ struct Walker {
                 return cur;
             }
             case Node::Kind::Task: return task(n, ready);
+            case Node::Kind::Pipeline: return std::max(ready, pipeline(n));
+            case Node::Kind::Send:
+            case Node::Kind::Consume:
+                throw Error(PTOWSP_ERR_PLAN, "send / consume outside a CSP pipeline process");
         }
         return ready;
     }
 
     uint64_t task(const Node& n, uint64_t ready) {
+        std::vector<uint64_t> args = enqueue(n);
+        const KernelImpl& ki = P.impls[n.kernel_index];
+        // worker choice + makespan (pto_codegen.cpp:2679-2692)
+        const Schedule& sc = P.plan.schedule;
+        uint32_t wid = 0;
+        if (!sc.dispatch_policy.empty()) {
+            if (sc.dispatch_policy == "round_robin" || sc.dispatch_policy == "work_steal") {
+                wid = static_cast<uint32_t>(rr++ % sched.n);
+            } else {
+                Val key = eval(*sc.dispatch_key, &args);
+                wid = static_cast<uint32_t>(key.v % sched.n);
+            }
+        }
+        return sched.issue(ki.cycles, wid, ready);
+    }
+
+    // Places one task in its dependency wave; returns its u64 args.
+    std::vector<uint64_t> enqueue(const Node& n) {
         const KernelDef& kd = P.plan.kernels[n.kernel_index];
         const KernelImpl& ki = P.impls[n.kernel_index];
         // u64 args: axis args, (valid_row, valid_col) per tensor param, scalar args (pto_codegen.cpp:2526-2545)
@@ -468,19 +491,242 @@ struct Walker {
         for (uint64_t s : scal) b.rec.push_back(static_cast<int64_t>(s));
         b.ntasks++;
         L.tasks++;
+        return args;
+    }
 
-        // worker choice + makespan (pto_codegen.cpp:2679-2692)
-        const Schedule& sc = P.plan.schedule;
-        uint32_t wid = 0;
-        if (!sc.dispatch_policy.empty()) {
-            if (sc.dispatch_policy == "round_robin" || sc.dispatch_policy == "work_steal") {
-                wid = static_cast<uint32_t>(rr++ % sched.n);
-            } else {
-                Val key = eval(*sc.dispatch_key, &args);
-                wid = static_cast<uint32_t>(key.v % sched.n);
+    // ---- CSP pipelines (CSPT time semantics, pto_codegen.cpp:1611-1705 and :1759-2220) ----
+    //
+    // Every process keeps its own clock; a task adds its kernel's cycle charge to the clock of the process that
+    // runs it; channels carry (token, send time) and a receive moves the receiver's clock to at least send time +
+    // channel latency; a sender that had to wait for room moves its clock to at least the time of the last
+    // receive.  The result is the largest process clock.  The reference runs each process on its own thread; here
+    // the processes are interleaved deterministically on the host: the first runnable process in declaration
+    // order runs until its next channel operation completes or blocks (a producer released by a receive runs
+    // before the receiver goes on, as a woken thread would), and every task it reaches is placed in the
+    // dependency waves in that order, so the GPU runs the tasks in an order the channels allow.
+    struct Chan {
+        int64_t cap = 0;
+        std::deque<std::pair<uint64_t, uint64_t>> buf;  // (token, send time)
+        bool closed = false, receiver_waiting = false, has_rdv = false;
+        std::pair<uint64_t, uint64_t> rdv{0, 0};
+        uint64_t last_pop = 0;
+    };
+    struct Frame {
+        const Node* node;
+        int64_t i = 0, ub = 0;
+        int state = 0;
+    };
+    struct Proc {
+        std::vector<Frame> stack;
+        std::vector<std::pair<const std::string*, int64_t>> env;
+        uint64_t t = 0, token = 0;
+        bool done = false, blocked = false, resumed = false;
+        int wait_send = -1, wait_recv = -1;  // channel this process waits on, as sender / receiver
+    };
+    enum class Step { Yield, Blocked, Done };
+
+    uint64_t pipeline(const Node& n) {
+        const uint64_t latency = symbol_u64(fnv1a_64("__pto_wsp_channel_latency_cycles"));
+        std::vector<Chan> ch(n.channels.size());
+        for (size_t c = 0; c < ch.size(); ++c) ch[c].cap = n.channels[c].capacity;
+        std::vector<Proc> pr(n.processes.size());
+        for (size_t p = 0; p < pr.size(); ++p) pr[p].stack.push_back(Frame{n.children[p].get()});
+        auto wake_senders = [&](int c) {
+            for (auto& q : pr)
+                if (q.blocked && q.wait_send == c) q.blocked = false, q.resumed = true;
+        };
+        auto wake_receivers = [&](int c) {
+            for (auto& q : pr)
+                if (q.blocked && q.wait_recv == c) q.blocked = false, q.resumed = true;
+        };
+        auto saved = std::move(env);
+        for (;;) {
+            size_t pick = pr.size();
+            for (size_t p = 0; p < pr.size(); ++p)
+                if (!pr[p].done && !pr[p].blocked) {
+                    pick = p;
+                    break;
+                }
+            if (pick == pr.size()) {
+                bool all = true;
+                for (auto& q : pr) all = all && q.done;
+                if (all) break;
+                env = std::move(saved);
+                throw Error(PTOWSP_ERR_PLAN, "CSP pipeline deadlock: every unfinished process waits on a channel");
+            }
+            Proc& p = pr[pick];
+            env = std::move(p.env);
+            const Step st = step(p, ch, latency, wake_senders, wake_receivers);
+            p.env = std::move(env);
+            if (st == Step::Done) {
+                p.done = true;
+                for (int c : n.processes[pick].produces) {  // close what this process produces
+                    ch[c].closed = true;
+                    wake_senders(c);
+                    wake_receivers(c);
+                }
             }
         }
-        return sched.issue(ki.cycles, wid, ready);
+        env = std::move(saved);
+        uint64_t makespan = 0;
+        for (auto& q : pr) makespan = std::max(makespan, q.t);
+        return makespan;
+    }
+
+    template <class WakeS, class WakeR>
+    Step step(Proc& p, std::vector<Chan>& ch, uint64_t latency, WakeS& wake_senders, WakeR& wake_receivers) {
+        const bool resumed = p.resumed;
+        p.resumed = false;
+        while (!p.stack.empty()) {
+            Frame& f = p.stack.back();
+            const Node& n = *f.node;
+            switch (n.kind) {
+                case Node::Kind::SlotSet:
+                case Node::Kind::SlotLoad:
+                    node(n, 0);
+                    p.stack.pop_back();
+                    break;
+                case Node::Kind::Task:
+                    enqueue(n);
+                    p.t += P.impls[n.kernel_index].cycles;
+                    p.stack.pop_back();
+                    break;
+                case Node::Kind::ParallelFor:
+                case Node::Kind::ForEach: {
+                    if (f.state == 0) {
+                        if (n.axis.kind == Axis::Kind::Dense) f.ub = n.axis.size;
+                        else if (n.axis.kind == Axis::Kind::DenseDyn) f.ub = axis_size(n.var);
+                        else throw Error(PTOWSP_ERR_UNSUPPORTED, "CSPT codegen: unsupported axis kind in loop");
+                        env.push_back({&n.var, 0});
+                        f.state = 1;
+                    }
+                    if (f.i < f.ub) {
+                        env.back().second = f.i++;
+                        p.stack.push_back(Frame{n.body.get()});
+                    } else {
+                        env.pop_back();
+                        p.stack.pop_back();
+                    }
+                    break;
+                }
+                case Node::Kind::Combine:
+                case Node::Kind::Sequential:
+                    if (f.i < static_cast<int64_t>(n.children.size())) p.stack.push_back(Frame{n.children[f.i++].get()});
+                    else p.stack.pop_back();
+                    break;
+                case Node::Kind::Cond: {
+                    const Node* br = eval(*n.pred, nullptr).v ? n.then_n.get() : n.else_n.get();
+                    p.stack.back() = Frame{br};
+                    break;
+                }
+                case Node::Kind::Send: {
+                    Chan& c = ch[n.channel];
+                    if (f.state == 0) {  // run the task, then offer its first axis arg
+                        const std::vector<uint64_t> args = enqueue(*n.body);
+                        p.t += P.impls[n.body->kernel_index].cycles;
+                        p.token = n.body->axis_args.empty() ? 0 : args[0];
+                        f.state = 1;
+                    }
+                    if (c.cap > 0) {
+                        if (f.state == 2 && resumed && c.last_pop > p.t) p.t = c.last_pop;  // waited for room
+                        if (c.closed) {
+                            p.stack.pop_back();
+                            return Step::Yield;
+                        }
+                        if (static_cast<int64_t>(c.buf.size()) >= c.cap) {
+                            f.state = 2;
+                            p.blocked = true;
+                            p.wait_send = n.channel;
+                            p.wait_recv = -1;
+                            return Step::Blocked;
+                        }
+                        c.buf.push_back({p.token, p.t});
+                        wake_receivers(n.channel);
+                        p.stack.pop_back();
+                        return Step::Yield;
+                    }
+                    // rendezvous: wait for a waiting receiver, hand the token over, wait until it is taken
+                    if (f.state == 1) {
+                        if (c.closed) {
+                            p.stack.pop_back();
+                            return Step::Yield;
+                        }
+                        if (!c.receiver_waiting) {
+                            p.blocked = true;
+                            p.wait_send = n.channel;
+                            p.wait_recv = -1;
+                            return Step::Blocked;
+                        }
+                        c.rdv = {p.token, p.t};
+                        c.has_rdv = true;
+                        wake_receivers(n.channel);
+                        f.state = 3;
+                    }
+                    if (!c.closed && c.has_rdv) {
+                        p.blocked = true;
+                        p.wait_send = n.channel;
+                        p.wait_recv = -1;
+                        return Step::Blocked;
+                    }
+                    if (c.last_pop > p.t) p.t = c.last_pop;
+                    p.stack.pop_back();
+                    return Step::Yield;
+                }
+                case Node::Kind::Consume: {
+                    Chan& c = ch[n.channel];
+                    if (f.state == 1) {  // body done: unbind the token, receive the next one
+                        env.pop_back();
+                        f.state = 0;
+                    }
+                    bool got = false;
+                    uint64_t tok = 0, ts = 0;
+                    if (c.cap > 0) {
+                        if (!c.buf.empty()) {
+                            tok = c.buf.front().first;
+                            ts = c.buf.front().second;
+                            c.buf.pop_front();
+                            got = true;
+                        } else if (!c.closed) {
+                            p.blocked = true;
+                            p.wait_recv = n.channel;
+                            p.wait_send = -1;
+                            return Step::Blocked;
+                        }
+                    } else {
+                        c.receiver_waiting = true;
+                        wake_senders(n.channel);
+                        if (!c.closed && !c.has_rdv) {
+                            p.blocked = true;
+                            p.wait_recv = n.channel;
+                            p.wait_send = -1;
+                            return Step::Blocked;
+                        }
+                        c.receiver_waiting = false;
+                        if (c.has_rdv) {
+                            tok = c.rdv.first;
+                            ts = c.rdv.second;
+                            c.has_rdv = false;
+                            got = true;
+                        }
+                    }
+                    if (!got) {  // closed and drained
+                        p.stack.pop_back();
+                        break;
+                    }
+                    const uint64_t deliver = ts + latency;
+                    if (deliver > p.t) p.t = deliver;
+                    c.last_pop = p.t;
+                    wake_senders(n.channel);
+                    env.push_back({&n.var, static_cast<int64_t>(tok)});
+                    f.state = 1;
+                    p.stack.push_back(Frame{n.body.get()});
+                    return Step::Yield;
+                }
+                default:
+                    throw Error(PTOWSP_ERR_UNSUPPORTED, "CSPT codegen: unsupported node kind in process body");
+            }
+        }
+        return Step::Done;
     }
 };
 
@@ -986,8 +1232,11 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
     // read / written sets per tensor from the kernels' param sets
     std::function<void(const Node&)> mark = [&](const Node& n) {
         switch (n.kind) {
-            case Node::Kind::ParallelFor: case Node::Kind::ForEach: case Node::Kind::Select: mark(*n.body); break;
-            case Node::Kind::Combine: case Node::Kind::Sequential: for (auto& c : n.children) mark(*c); break;
+            case Node::Kind::ParallelFor: case Node::Kind::ForEach: case Node::Kind::Select:
+            case Node::Kind::Send: case Node::Kind::Consume: mark(*n.body); break;
+            case Node::Kind::Combine: case Node::Kind::Sequential: case Node::Kind::Pipeline:
+                for (auto& c : n.children) mark(*c);
+                break;
             case Node::Kind::Cond: mark(*n.then_n); mark(*n.else_n); break;
             case Node::Kind::Task: {
                 const KernelImpl& ki = P.impls[n.kernel_index];

@@ -286,6 +286,18 @@ def _node(n: Any, cpp: Any) -> dict:
     if isinstance(n, cpp.SlotLoadU64Node):
         return {"kind": "slot_load", "slot": int(n.slot), "tensor_arg": _tensor_arg(n.tensor),
                 "row": int(n.row), "col": int(n.col)}
+    if isinstance(n, cpp.PipelineNode):
+        return {
+            "kind": "pipeline",
+            "channels": [{"name": str(c.name), "capacity": int(c.type.capacity)} for c in n.channels],
+            "processes": [{"name": str(p.name), "produces": [str(x) for x in p.produces],
+                           "consumes": [str(x) for x in p.consumes], "body": _node(p.body, cpp)}
+                          for p in n.processes],
+        }
+    if isinstance(n, cpp.SendNode):
+        return {"kind": "send", "channel": str(n.channel_name), "value": _node(n.value, cpp)}
+    if isinstance(n, cpp.ConsumeNode):
+        return {"kind": "consume", "channel": str(n.channel_name), "var": str(n.value_var), "body": _node(n.body, cpp)}
     raise ValueError(f"workload node {type(n).__name__} is not supported by the cuda_sm100a target")
 
 
