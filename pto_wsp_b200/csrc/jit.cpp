@@ -176,22 +176,37 @@ std::string bin_expr(int word, int sub, const std::string& a, const std::string&
 
 }  // namespace
 
+int program_rows(const TileProgram& tp) {
+    int R = 0;
+    for (int i = 0; i < tp.nslots; ++i) R = std::max(R, tp.slots[i].rows);
+    return R;
+}
+
+// A one-row tile in a program over R > 1 rows: the same for every row ([1,C] operands of column broadcasts).
+static bool row_invariant(const TileProgram& tp, int slot) { return tp.slots[slot].rows == 1 && program_rows(tp) > 1; }
+
+// Element offset of tile row r of a view: none for a row-invariant tile (row 0 of its view).
+static std::string row_offset(const TileProgram& tp, int slot, const std::string& p) {
+    return row_invariant(tp, slot) ? std::string() : " + (int64_t)r * " + p + ".s3";
+}
+
 bool row_local(const TileProgram& tp, std::string* why) {
     auto fail = [&](const std::string& m) {
         if (why) *why = m;
         return false;
     };
     if (tp.ninstr <= 0 || tp.nslots <= 0) return fail("empty program");
-    int R = -1, words = 0;
+    const int R = program_rows(tp);
+    int words = 0;
     for (int i = 0; i < tp.nslots; ++i) {
         const TPSlot& s = tp.slots[i];
-        if (R < 0) R = s.rows;
-        if (s.rows != R) return fail("tiles of different row counts");
+        if (s.rows != R && s.rows != 1) return fail("tiles of different row counts");
         if (s.cols < 1 || s.cols > kMaxCols) return fail("tile wider than 1024 columns");
         if (s.cols > 1) words += (s.cols + 31) / 32;
     }
     if (R < 1) return fail("no rows");
     if (words > kMaxRegWords) return fail("too many tile elements per lane");
+    auto inv = [&](int slot) { return row_invariant(tp, slot); };
     for (int ii = 0; ii < tp.ninstr; ++ii) {
         const TPInstr& in = tp.ins[ii];
         switch (in.op) {
@@ -203,24 +218,28 @@ bool row_local(const TileProgram& tp, std::string* why) {
             case TP_STORE: {
                 const TPSlot& a = tp.slots[in.a];
                 if (in.rows != a.rows || in.cols != a.cols) return fail("partial-tile store");
+                if (inv(in.a)) return fail("store of a one-row tile from a many-row program");
                 break;
             }
             case TP_MOV: case TP_BINS: case TP_EXP: case TP_RSQRT: {
                 const TPSlot &d = tp.slots[in.dst], &a = tp.slots[in.a];
-                if (d.cols != a.cols) return fail("shape change in an element-wise op");
+                if (d.cols != a.cols || inv(in.dst) != inv(in.a)) return fail("shape change in an element-wise op");
                 break;
             }
             case TP_BIN: {
                 const TPSlot &d = tp.slots[in.dst], &a = tp.slots[in.a], &b = tp.slots[in.b];
-                if (d.cols != a.cols) return fail("shape change in a binary op");
-                if (in.mode == MODE_FULL && b.cols != d.cols) return fail("binary op on different shapes");
-                if (in.mode == MODE_ROW && b.cols != 1) return fail("row broadcast of a wide tile");
-                if (in.mode == MODE_COL) return fail("column broadcast");
+                if (d.cols != a.cols || inv(in.dst) != inv(in.a)) return fail("shape change in a binary op");
+                if (in.mode == MODE_FULL && (b.cols != d.cols || inv(in.b) != inv(in.dst)))
+                    return fail("binary op on different shapes");
+                if (in.mode == MODE_ROW && (b.cols != 1 || inv(in.b) != inv(in.dst))) return fail("row broadcast of a wide tile");
+                if (in.mode == MODE_COL && (!inv(in.b) || b.cols != d.cols || inv(in.dst)))
+                    return fail("column broadcast of a many-row tile");
                 break;
             }
             case TP_ROWSUM: case TP_ROWMAX: case TP_ROWMEAN: {
                 if (tp.slots[in.dst].cols != 1) return fail("row reduction into a wide tile");
                 if (tp.slots[in.a].word != W_F32) return fail("integer row reduction");
+                if (inv(in.dst) != inv(in.a)) return fail("row reduction across tile shapes");
                 break;
             }
             default: return fail("op outside the row-local set");
@@ -231,13 +250,11 @@ bool row_local(const TileProgram& tp, std::string* why) {
 
 namespace {
 
-// One kernel of the row program.  vec = false: lane l holds columns l, l+32, ... (4-byte accesses, any stride);
-// vec = true: lane l holds columns 128j+4l .. +3 (one 16-byte (f32/i32) or 8-byte (f16) access per quad;
-// unit column stride, 16-byte-aligned rows).
-void emit_row_kernel(std::ostringstream& o, const TileProgram& tp, const int* param_types, const std::string& name,
-                     bool vec) {
-    const int R = tp.slots[0].rows;
-    auto nwords = [&](int cols) { return vec ? 4 * ((cols + 127) / 128) : (cols + 31) / 32; };
+// The scalar kernel of the row program: one warp per tile row, lane l holds columns l, l+32, ... (4-byte accesses,
+// any strides).
+void emit_row_kernel(std::ostringstream& o, const TileProgram& tp, const int* param_types, const std::string& name) {
+    const int R = program_rows(tp);
+    auto nwords = [&](int cols) { return (cols + 31) / 32; };
     o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(TaskBatch b) {\n";
     o << "  const int lane = threadIdx.x & 31;\n";
     o << "  const int64_t nrows = b.ntasks * " << R << "LL;\n";
@@ -252,8 +269,7 @@ void emit_row_kernel(std::ostringstream& o, const TileProgram& tp, const int* pa
     auto elem = [&](int slot, const std::string& j) {
         return tp.slots[slot].cols > 1 ? "s" + std::to_string(slot) + "[" + j + "]" : "s" + std::to_string(slot);
     };
-    // column of register word j of a lane
-    const std::string col = vec ? "(128 * (j >> 2) + 4 * lane + (j & 3))" : "(lane + 32 * j)";
+    const std::string col = "(lane + 32 * j)";  // column of register word j of a lane
     for (int ii = 0; ii < tp.ninstr; ++ii) {
         const TPInstr& in = tp.ins[ii];
         o << "    { // instruction " << ii << "\n";
@@ -265,62 +281,8 @@ void emit_row_kernel(std::ostringstream& o, const TileProgram& tp, const int* pa
                 const TPSlot& t = tp.slots[slot];
                 const int pt = param_types[in.param];
                 const std::string p = "b.p[" + std::to_string(in.param) + "]";
-                o << "      const int64_t base = rec[" << in.param << "] + (int64_t)r * " << p << ".s3;\n";
-                if (vec && t.cols > 1) {
-                    const int nq = (t.cols + 127) / 128;
-                    const bool half = pt == PT_F16;
-                    o << "      #pragma unroll\n      for (int q = 0; q < " << nq << "; ++q) {\n";
-                    o << "        const int c0 = 128 * q + 4 * lane;\n";
-                    o << "        if (c0 < " << t.cols << ") { const int64_t off = base + c0;\n";
-                    o << "          if (off >= 0 && off + 3 < " << p << ".numel_span) {\n";
-                    if (load) {
-                        if (half) {
-                            o << "            const uint2 raw = *(const uint2*)(((const unsigned short*)" << p << ".base) + off);\n";
-                            o << "            const unsigned short h[4] = {(unsigned short)(raw.x & 0xffffu), (unsigned short)(raw.x >> 16), "
-                                 "(unsigned short)(raw.y & 0xffffu), (unsigned short)(raw.y >> 16)};\n";
-                            for (int e = 0; e < 4; ++e)
-                                o << "            s" << slot << "[4 * q + " << e << "] = "
-                                  << (t.word == W_F32 ? "__float_as_uint(h2f(h[" + std::to_string(e) + "]))"
-                                                      : "(unsigned)(int)h2f(h[" + std::to_string(e) + "])")
-                                  << ";\n";
-                        } else {
-                            o << "            const uint4 raw = *(const uint4*)(((const unsigned*)" << p << ".base) + off);\n";
-                            const char* comp[4] = {"raw.x", "raw.y", "raw.z", "raw.w"};
-                            for (int e = 0; e < 4; ++e) {
-                                std::string w;
-                                if (t.word == W_F32) {
-                                    if (pt == PT_F32) w = comp[e];
-                                    else if (pt == PT_I32) w = std::string("__float_as_uint((float)(int)") + comp[e] + ")";
-                                    else w = std::string("__float_as_uint((float)") + comp[e] + ")";
-                                } else {
-                                    w = pt == PT_F32 ? std::string("(unsigned)(int)__uint_as_float(") + comp[e] + ")" : comp[e];
-                                }
-                                o << "            s" << slot << "[4 * q + " << e << "] = " << w << ";\n";
-                            }
-                        }
-                    } else {
-                        std::string f[4];
-                        for (int e = 0; e < 4; ++e) {
-                            const std::string w = "s" + std::to_string(slot) + "[4 * q + " + std::to_string(e) + "]";
-                            f[e] = t.word == W_F32 ? "__uint_as_float(" + w + ")"
-                                                   : (t.word == W_I32 ? "(float)(int)(" + w + ")" : "(float)(" + w + ")");
-                            if (pt == PT_F16) f[e] = "f2h(" + f[e] + ")";
-                            else if (pt == PT_F32) f[e] = "__float_as_uint(" + f[e] + ")";
-                            else if (pt == PT_I32) f[e] = t.word == W_F32 ? "(unsigned)(int)" + f[e] : "(" + w + ")";
-                            else f[e] = t.word == W_F32 ? "(unsigned)" + f[e] : "(" + w + ")";
-                        }
-                        if (half)
-                            o << "            *(uint2*)(((unsigned short*)" << p << ".base) + off) = make_uint2((unsigned)" << f[0]
-                              << " | ((unsigned)" << f[1] << " << 16), (unsigned)" << f[2] << " | ((unsigned)" << f[3] << " << 16));\n";
-                        else
-                            o << "            *(uint4*)(((unsigned*)" << p << ".base) + off) = make_uint4(" << f[0] << ", " << f[1]
-                              << ", " << f[2] << ", " << f[3] << ");\n";
-                    }
-                    o << "          } else atomicOr(b.err, " << kErrBounds << "); }\n";
-                    o << "      }\n";
-                    break;
-                }
-                const int nj = (t.cols + 31) / 32;  // scalar accesses (also [R,1] tiles in the vector kernel)
+                o << "      const int64_t base = rec[" << in.param << "]" << row_offset(tp, slot, p) << ";\n";
+                const int nj = (t.cols + 31) / 32;
                 o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
                 o << "        const int c = lane + 32 * j;" << (load ? " unsigned w = 0u;" : "") << "\n";
                 o << "        if (c < " << t.cols << ") { const int64_t off = base + (int64_t)c * " << p << ".s4;\n";
@@ -417,7 +379,7 @@ int lanes_per_row(int quads) {
 // group holds the 4-column quads sub, sub + L, ... of the row; 16-byte (f32/i32) or 8-byte (f16) accesses;
 // row reductions by shuffles inside the group.  Needs unit column strides and 16-byte-aligned rows.
 void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* param_types, const std::string& name) {
-    const int R = tp.slots[0].rows;
+    const int R = program_rows(tp);
     int cmax = 4;
     for (int i = 0; i < tp.nslots; ++i) cmax = std::max(cmax, tp.slots[i].cols);
     const int L = lanes_per_row((cmax + 3) / 4);
@@ -457,7 +419,7 @@ void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* 
                 const TPSlot& t = tp.slots[slot];
                 const int pt = param_types[in.param];
                 const std::string p = "b.p[" + std::to_string(in.param) + "]";
-                o << "      const int64_t base = rec[" << in.param << "] + (int64_t)r * " << p << ".s3;\n";
+                o << "      const int64_t base = rec[" << in.param << "]" << row_offset(tp, slot, p) << ";\n";
                 if (t.cols == 1) {  // [R,1]: the group leader's element, broadcast inside the group
                     if (load) {
                         o << "      unsigned w = 0u;\n";
@@ -604,7 +566,7 @@ bool vector_form(const TileProgram& tp, const int* param_types) {
 std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const std::string& name) {
     std::ostringstream o;
     o << "#define MAXP " << kMaxParams << "\n" << kPrelude;
-    emit_row_kernel(o, tp, param_types, name, false);
+    emit_row_kernel(o, tp, param_types, name);
     if (vector_form(tp, param_types)) emit_group_kernel(o, tp, param_types, name + "_v");
     return o.str();
 }

@@ -45,3 +45,37 @@ def test_row_ops_of_odd_widths_run_fused(kind, cols, require_cuda):
     assert ex.run_with_symbols([x, got], {}, {}, {}) == cyc
     assert ex.describe()["kernels"][0]["row_kernel"] == "loaded"  # the fast path does not take this width
     np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-7)
+
+
+def col_scale_plan(B, R, C, dtype_x="f32"):
+    """out = (x - v) * w with v, w one-row [1, C] operands (column broadcasts) and x [R, C]."""
+    from pto_wsp_b200.workloads import KernelBuilder, _pfor, _plan, _schedule, _targ, _task
+
+    k = KernelBuilder("col_scale")
+    x = k.param("x", dtype_x, R, C)
+    v = k.param("v", "f32", 1, C)
+    w = k.param("w", "f32", 1, C)
+    out = k.param("out", "f32", R, C)
+    d = k.op("Sub", [x, v], ("f32", R, C))
+    k.store(out, k.op("Mul", [d, w], ("f32", R, C)))
+    body = _pfor("b", B, _task("col_scale", ["b"], [_targ("x", 0, 3, ["b"]), _targ("v", 1, 3, ["b"]),
+                                                   _targ("w", 2, 3, ["b"]), _targ("out", 3, 3, ["b"])]))
+    return _plan("col_scale", [(dtype_x, [B, R, C]), ("f32", [B, 1, C]), ("f32", [B, 1, C]), ("f32", [B, R, C])],
+                 [k.build()], body, _schedule())
+
+
+@pytest.mark.parametrize("cols,dtype", [(64, "f32"), (36, "f16"), (33, "f32"), (1000, "f32")])
+def test_column_broadcast_row_kernel_bit_exact(cols, dtype, require_cuda):
+    rng = np.random.default_rng(cols + 1)
+    B, R = 6, 16
+    plan = col_scale_plan(B, R, cols, dtype)
+    x = rng.standard_normal((B, R, cols)).astype(np.float16 if dtype == "f16" else np.float32)
+    v = rng.standard_normal((B, 1, cols)).astype(np.float32)
+    w = rng.standard_normal((B, 1, cols)).astype(np.float32)
+    ref = np.full((B, R, cols), np.nan, np.float32)
+    cyc = CpuSim(plan).run([x, v, w, ref])
+    got = np.full_like(ref, np.nan)
+    ex = CudaExecutable(plan)
+    assert ex.run_with_symbols([x, v, w, got], {}, {}, {}) == cyc
+    assert ex.describe()["kernels"][0]["row_kernel"] == "loaded"
+    np.testing.assert_array_equal(got, ref)

@@ -53,10 +53,30 @@ def col_broadcast_plan(R, C):
                  _schedule())
 
 
-def test_kernels_outside_the_row_local_set_keep_the_interpreter():
+def col_store_plan(R, C):
+    """A many-row program that also stores a one-row tile: every row would write it, so it stays interpreted."""
+    k = KernelBuilder("col_store")
+    x = k.param("x", "f32", R, C)
+    v = k.param("v", "f32", 1, C)
+    out = k.param("out", "f32", R, C)
+    vo = k.param("vo", "f32", 1, C)
+    k.store(out, k.op("Sub", [x, v], ("f32", R, C)))
+    k.store(vo, k.op("Mul", [v, v], ("f32", 1, C)))
+    body = _pfor("b", 2, _task("col_store", ["b"], [_targ("x", 0, 3, ["b"]), _targ("v", 1, 3, ["b"]),
+                                                     _targ("out", 2, 3, ["b"]), _targ("vo", 3, 3, ["b"])]))
+    return _plan("col_store", [("f32", [2, R, C]), ("f32", [2, 1, C]), ("f32", [2, R, C]), ("f32", [2, 1, C])],
+                 [k.build()], body, _schedule())
+
+
+def test_column_broadcasts_are_row_local():
     d = CudaExecutable(col_broadcast_plan(4, 64)).describe()["kernels"][0]
+    assert d["impl"] == "tile_program" and d["row_kernel"] == "compiled", d["row_kernel_note"]
+
+
+def test_kernels_outside_the_row_local_set_keep_the_interpreter():
+    d = CudaExecutable(col_store_plan(4, 64)).describe()["kernels"][0]
     assert d["impl"] == "tile_program"
-    assert d["row_kernel"] == "interpreter" and d["row_kernel_note"]  # the [1, C] operand is not a row tile
+    assert d["row_kernel"] == "interpreter" and "one-row tile" in d["row_kernel_note"]
     wide = CudaExecutable(rowmax_shift_plan(1, 1, 2, 1100)).describe()["kernels"][0]  # 1100 > 1024 columns
     assert wide["row_kernel"] == "interpreter" and "1024" in wide["row_kernel_note"]
 
