@@ -583,7 +583,59 @@ __global__ void __launch_bounds__(kMmaThreads) paged_decode_tma_kernel(const __g
     if (!*last_flag) return;
     __threadfence();
     const float* base = partials + task * chunks * static_cast<int64_t>(pstride);
-    for (int e = threadIdx.x; e < G * kHeadDim; e += kMmaThreads) {
+    // The chunks' maxima and denominators go through shared memory once (the upper half of the ring, free now):
+    // per query the running maximum, each chunk's weight exp2(m_c - M) and the denominator; then every output
+    // element issues its chunks' loads together.  Same operations in the same order as a per-element loop.
+    static_assert(kMmaConsumers * CB::STRIDE * 4 <= kRingBytes / 2, "merge scratch above the combine area");
+    float* mw = reinterpret_cast<float*>(dsm + kRingBytes / 2);  // [nch][G] weights, [nch][G] sums, M[G], den[G]
+    if ((2 * nch + 2) * G * static_cast<int>(sizeof(float)) <= kRingBytes / 2) {
+        float* lsum = mw + nch * G;
+        float* Mq = lsum + nch * G;
+        float* Dq = Mq + G;
+        for (int i = threadIdx.x; i < nch * G; i += kMmaThreads) {
+            const int c = i / G, gq = i - c * G;
+            mw[i] = __ldcg(base + c * pstride + G * kHeadDim + gq);
+            lsum[i] = __ldcg(base + c * pstride + G * kHeadDim + G + gq);
+        }
+        __syncthreads();
+        if (threadIdx.x < G) {
+            const int gq = threadIdx.x;
+            float M = -INFINITY;
+            for (int c = 0; c < nch; ++c) M = fmaxf(M, mw[c * G + gq]);
+            float den = 0.f;
+            for (int c = 0; c < nch; ++c) {
+                const float mc = mw[c * G + gq];
+                float w = -1.f;  // chunk without a finite maximum: skipped
+                if (mc != -INFINITY) {
+                    w = exp2f(mc - M);
+                    den = fmaf(lsum[c * G + gq], w, den);
+                }
+                mw[c * G + gq] = w;
+            }
+            Mq[gq] = M;
+            Dq[gq] = den;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < G * kHeadDim; e += kMmaThreads) {
+            const int gq = e / kHeadDim;
+            float num = 0.f;
+            for (int c0 = 0; c0 < nch; c0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = c0 + j < nch ? __ldcg(base + (c0 + j) * pstride + e) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (c0 + j < nch) {
+                        const float w = mw[(c0 + j) * G + gq];
+                        if (w >= 0.f) num = fmaf(v[j], w, num);
+                    }
+                }
+            }
+            out[gq * os3 + e % kHeadDim] = __float2half_rn(num / Dq[gq]);
+        }
+        return;
+    }
+    for (int e = threadIdx.x; e < G * kHeadDim; e += kMmaThreads) {  // very long requests: per element
         const int gq = e / kHeadDim;
         float M = -INFINITY;
         for (int c = 0; c < nch; ++c) M = fmaxf(M, __ldcg(base + c * pstride + G * kHeadDim + gq));
@@ -662,6 +714,9 @@ cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cu
             if (e == cudaSuccess)
                 e = cudaFuncSetAttribute(paged_decode_tma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kMmaSmemBytes);
+            if (e == cudaSuccess)  // all of the unified L1 as shared memory: three CTAs per SM
+                e = cudaFuncSetAttribute(paged_decode_tma_kernel<G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
             paged_decode_tma_kernel<G><<<static_cast<unsigned>(grid), kMmaThreads, kMmaSmemBytes, s>>>(
                 mk, mv, b, chunks, partials, arrivals);
