@@ -31,6 +31,7 @@ import json
 import os
 import statistics
 import subprocess
+import threading
 import sys
 import time
 from pathlib import Path
@@ -82,6 +83,73 @@ def traffic_from_profiles(kernel: str, workload: str, batch_override=None) -> fl
         return None
 
 
+class NvmlClockSampler:
+    """SM clock, power and clock-event reasons read through NVML every millisecond while the timed region runs
+    (read-only queries; short timed regions still get several samples).  Falls back to nvidia-smi."""
+
+    REASONS = [("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap")]
+
+    def __init__(self, gpu_index: int, pci_bus_id: str | None = None):
+        self.idx, self.pci = gpu_index, pci_bus_id
+        self.fallback = None
+        self.rows: list[tuple[float, float, float, int]] = []
+
+    def __enter__(self):
+        try:
+            import pynvml as N
+
+            N.nvmlInit()
+            self.N = N
+            h = None
+            if self.pci:
+                try:
+                    h = N.nvmlDeviceGetHandleByPciBusId(self.pci)
+                except Exception:  # noqa: BLE001
+                    h = None
+            self.h = h if h is not None else N.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM))
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001
+            self.fallback = ClockSampler(self.idx).__enter__()
+        return self
+
+    def _run(self):
+        N = self.N
+        while not self.stop.is_set():
+            try:
+                self.rows.append((float(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)), self.max_mhz,
+                                  N.nvmlDeviceGetPowerUsage(self.h) / 1000.0,
+                                  int(N.nvmlDeviceGetCurrentClocksEventReasons(self.h))))
+            except Exception:  # noqa: BLE001
+                break
+            time.sleep(0.001)
+
+    def __exit__(self, *a):
+        if self.fallback is not None:
+            self.fallback.__exit__(*a)
+            return
+        self.stop.set()
+        self.thread.join(timeout=5)
+
+    def summary(self) -> dict:
+        if self.fallback is not None:
+            return self.fallback.summary()
+        reasons = set()
+        for _, _, _, bits in self.rows:
+            for name, attr in self.REASONS:
+                if bits & getattr(self.N, attr, 0):
+                    reasons.add(name)
+        sm = [r[0] for r in self.rows]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples_under_load": len(sm), "samples": len(sm), "source": "nvml, 1 ms",
+                "power_w_max": round(max((r[2] for r in self.rows), default=0.0), 1)}
+
+
 class ClockSampler:
     """nvidia-smi clocks + throttle reasons sampled while the timed region runs."""
 
@@ -128,6 +196,15 @@ class ClockSampler:
                         reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples_under_load": len(sm), "samples": len(rows)}
+
+
+def _pci_bus_id(torch, dev) -> str | None:
+    """The NVML-style PCI bus id of a torch CUDA device, when torch exposes it."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except Exception:  # noqa: BLE001
+        return None
 
 
 def gpu_index(local_rank: int) -> int:
@@ -330,7 +407,7 @@ def run_bgemm(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches = 0
-    with ClockSampler(gpu_index(local_rank)) as clk:
+    with NvmlClockSampler(gpu_index(local_rank), _pci_bus_id(torch, dev)) as clk:
         barrier()
         e0.record(stream)
         for _ in range(args.steps):
@@ -494,7 +571,7 @@ def run_builtin(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches = 0
-    with ClockSampler(gpu_index(local_rank)) as clk:
+    with NvmlClockSampler(gpu_index(local_rank), _pci_bus_id(torch, dev)) as clk:
         barrier()
         e0.record(stream)
         for _ in range(args.steps):
@@ -655,7 +732,7 @@ def main() -> None:
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches = 0
-    with ClockSampler(gpu_index(local_rank)) as clk:
+    with NvmlClockSampler(gpu_index(local_rank), _pci_bus_id(torch, dev)) as clk:
         barrier()
         e0.record(stream)
         for _ in range(args.steps):
