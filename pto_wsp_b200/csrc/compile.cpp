@@ -20,6 +20,7 @@ const char* impl_name(ImplKind k) {
         case ImplKind::TileProgram: return "tile_program";
         case ImplKind::Matmul: return "matmul_tcgen05";
         case ImplKind::MatmulAcc: return "matmul_tcgen05_acc";
+        case ImplKind::MatmulEpilogue: return "matmul_tcgen05+row_program";
         case ImplKind::PagedDecode: return "paged_decode_gqa";
         case ImplKind::IndexerScore: return "lightning_indexer_score";
         case ImplKind::TopK: return "topk_select";
@@ -677,6 +678,7 @@ std::unique_ptr<Program> compile_program(const char* text, size_t len, int devic
         else if (is_softmax(kd)) ki.kind = ImplKind::Softmax;
         else if (int f = matmul_form(kd)) ki.kind = f == 1 ? ImplKind::Matmul : ImplKind::MatmulAcc;
         else ki.kind = ImplKind::TileProgram;
+        if (ki.kind == ImplKind::TileProgram && split_matmul_epilogue(ki, kd, static_cast<int>(i))) continue;
         if (ki.kind == ImplKind::TileProgram && !ki.tp_ok)
             throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
         // a generic kernel gets its fused row kernel built now (NVRTC, no GPU needed), and so does a fast row op

@@ -13,6 +13,9 @@ namespace ptowsp::jit {
 // row broadcasts, row reductions); otherwise `why` names the first obstacle.
 bool row_local(const dev::TileProgram& tp, std::string* why);
 
+// Rows of the program's tiles (one-row operands of column broadcasts aside).
+int program_rows(const dev::TileProgram& tp);
+
 // CUDA source of the fused kernel `name` for a row-local program; param_types[i] is the ParamType of param i.
 // When vector_form() holds the source also has `name`_v, the variant with 16-byte (8-byte for f16) accesses
 // for unit column strides and 16-byte-aligned rows.

@@ -737,6 +737,8 @@ struct Walker {
 Batch::~Batch() {
     if (fast_rec_dev) cudaFree(fast_rec_dev);
     if (unit_rec_dev) cudaFree(unit_rec_dev);
+    if (ep_mm_rec_dev) cudaFree(ep_mm_rec_dev);
+    if (ep_rec_dev) cudaFree(ep_rec_dev);
 }
 
 LaunchProgram::~LaunchProgram() {
@@ -938,7 +940,96 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
             tb.p[2].cols = B.fast_n;
         }
     }
+    dev::ParamDesc ep_tile{};  // MatmulEpilogue: the scratch tile between the two launches
+    if (kind == ImplKind::MatmulEpilogue) {
+        const int np = kd.num_tensor_params;
+        const int64_t tile = int64_t(128) * ki.ep_n;
+        ep_tile.base = static_cast<char*>(ensure_scratch(P, static_cast<size_t>(B.ntasks) * tile * sizeof(float)));
+        ep_tile.s3 = ki.ep_n;
+        ep_tile.s4 = 1;
+        ep_tile.numel_span = B.ntasks * tile;
+        ep_tile.rows = 128;
+        ep_tile.cols = ki.ep_n;
+        ep_tile.type = dev::PT_F32;
+        ep_tile.elem_bytes = 4;
+        if (B.ep_ok < 0) {
+            // records of both stages, from the host records (read back once when a cached table dropped them)
+            std::vector<int64_t> back;
+            const int64_t* rec = B.rec.data();
+            if (B.rec.empty()) {
+                back.resize(static_cast<size_t>(B.ntasks) * B.stride);
+                PW_CUDA(cudaMemcpyAsync(back.data(), rec_dev + B.dev_off, back.size() * sizeof(int64_t),
+                                        cudaMemcpyDeviceToHost, P.stream));
+                PW_CUDA(cudaStreamSynchronize(P.stream));
+                rec = back.data();
+            }
+            dev::TaskBatch mtb{};
+            mtb.p[0] = tb.p[ki.ep_a];
+            mtb.p[1] = tb.p[ki.ep_b];
+            mtb.p[2] = ep_tile;
+            bool ok = dev::matmul_tiles_supported(mtb) && B.ntasks > 0;
+            const dev::ParamDesc &A = mtb.p[0], &Bm = mtb.p[1];
+            const int64_t K = ki.ep_k, N = ki.ep_n;
+            const int64_t a_rows = ok ? (A.numel_span + A.s3 - 1) / A.s3 : 0;
+            const int64_t b_rows = ok ? (Bm.numel_span + Bm.s3 - 1) / Bm.s3 : 0;
+            std::vector<int64_t> mm(static_cast<size_t>(B.ntasks) * 3), er(static_cast<size_t>(B.ntasks) * (B.stride + 1));
+            for (int64_t t = 0; ok && t < B.ntasks; ++t) {
+                const int64_t* r = rec + t * B.stride;
+                const int64_t oa = r[ki.ep_a], ob = r[ki.ep_b];
+                ok = oa >= 0 && ob >= 0 && oa % 8 == 0 && ob % 8 == 0 && (oa % A.s3) + K <= A.s3 &&
+                     (oa / A.s3) + 128 <= a_rows && (ob % Bm.s3) + N <= Bm.s3 && (ob / Bm.s3) + K <= b_rows;
+                mm[t * 3] = oa;
+                mm[t * 3 + 1] = ob;
+                mm[t * 3 + 2] = t * tile;
+                int64_t* o = &er[t * (B.stride + 1)];
+                for (int j = 0; j < np; ++j) o[j] = r[j];
+                o[np] = t * tile;
+                for (int j = np; j < B.stride; ++j) o[j + 1] = r[j];
+            }
+            B.ep_ok = ok ? 1 : 0;
+            if (ok) {
+                PW_CUDA(cudaMalloc(&B.ep_mm_rec_dev, mm.size() * sizeof(int64_t)));
+                PW_CUDA(cudaMemcpy(B.ep_mm_rec_dev, mm.data(), mm.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
+                PW_CUDA(cudaMalloc(&B.ep_rec_dev, er.size() * sizeof(int64_t)));
+                PW_CUDA(cudaMemcpy(B.ep_rec_dev, er.data(), er.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
+            }
+        }
+        if (ki.ep_jit_state == 2) {
+            const std::string name = "ptowsp_ep_k" + std::to_string(B.kernel);
+            std::string note;
+            if (jit::load_cubin(ki.ep_cubin, name, &ki.ep_fn, &note)) {
+                ki.ep_jit_state = 1;
+                if (!jit::load_cubin(ki.ep_cubin, name + "_v", &ki.ep_fn_vec, &note)) ki.ep_fn_vec = nullptr;
+            } else {
+                ki.ep_jit_state = -1;
+                ki.jit_note = note;
+            }
+        }
+        if (B.ep_ok != 1 || ki.ep_jit_state != 1) kind = ImplKind::TileProgram;  // the generic tile program
+    }
     switch (kind) {
+        case ImplKind::MatmulEpilogue: {
+            const int np = kd.num_tensor_params;
+            dev::TaskBatch mtb{};
+            mtb.p[0] = tb.p[ki.ep_a];
+            mtb.p[1] = tb.p[ki.ep_b];
+            mtb.p[2] = ep_tile;
+            mtb.rec = B.ep_mm_rec_dev;
+            mtb.ntasks = B.ntasks;
+            mtb.stride = 3;
+            mtb.nparams = 3;
+            mtb.err = P.err_dev;
+            e = dev::launch_matmul_tiles(mtb, 0, workers, P.stream);
+            if (e != cudaSuccess) break;
+            launches++;
+            dev::TaskBatch etb = tb;
+            etb.p[np] = ep_tile;
+            etb.nparams = np + 1;
+            etb.stride = B.stride + 1;
+            etb.rec = B.ep_rec_dev;
+            e = jit::launch_row_kernel(rows_ok && ki.ep_fn_vec ? ki.ep_fn_vec : ki.ep_fn, etb, 128, workers, P.stream);
+            break;
+        }
         case ImplKind::RmsNorm: e = dev::launch_rmsnorm_rows(tb, workers, P.stream); break;
         case ImplKind::Softmax: e = dev::launch_softmax_rows(tb, workers, P.stream); break;
         case ImplKind::Matmul:
@@ -969,8 +1060,8 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                 }
             }
             if (ki.jit_state == 1)
-                e = jit::launch_row_kernel(rows_ok && ki.jit_fn_vec ? ki.jit_fn_vec : ki.jit_fn, tb, ki.tp.slots[0].rows,
-                                           workers, P.stream);
+                e = jit::launch_row_kernel(rows_ok && ki.jit_fn_vec ? ki.jit_fn_vec : ki.jit_fn, tb,
+                                           jit::program_rows(ki.tp), workers, P.stream);
             else e = dev::launch_tile_program(tb, ki.tp_dev, ki.tp_smem, workers, P.stream);
             break;
         case ImplKind::PagedDecode: {
@@ -1176,19 +1267,127 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
 
 }  // namespace
 
-void jit_prepare(KernelImpl& ki, const KernelDef& kd, int k) {
-    ki.jit_state = -1;
-    if (!ki.tp_ok || !jit::row_local(ki.tp, &ki.jit_note)) return;
+namespace {
+
+// NVRTC build of the row program `tp` as kernel `name` (+ `name`_v); param types from the kernel's tile params,
+// plus f32 for the params at and after `extra_f32_from` (the epilogue's scratch tile).
+bool build_row_program(const dev::TileProgram& tp, const KernelDef& kd, int extra_f32_from, const std::string& name,
+                       std::string* cubin, std::string* note) {
+    if (!jit::row_local(tp, note)) return false;
     int types[dev::kMaxParams] = {};
     for (const auto& kp : kd.params)
         if (kp.tensor_index >= 0 && kp.tensor_index < dev::kMaxParams) types[kp.tensor_index] = ptype(kp.v.dtype);
-    const std::string name = "ptowsp_rows_k" + std::to_string(k);
-    const std::string src = jit::gen_row_kernel(ki.tp, types, name);
+    for (int i = extra_f32_from; i >= 0 && i < dev::kMaxParams; ++i) types[i] = dev::PT_F32;
+    const std::string src = jit::gen_row_kernel(tp, types, name);
     if (const char* dir = std::getenv("PTOWSP_JIT_DUMP")) {  // keep the generated source for inspection
         std::ofstream f(std::string(dir) + "/" + name + ".cu");
         f << src;
     }
-    if (jit::compile_cubin(src, name, &ki.jit_cubin, &ki.jit_note)) ki.jit_state = 2;
+    return jit::compile_cubin(src, name, cubin, note);
+}
+
+// Slot fields an instruction of the row-local set reads or writes; false for any other op.
+bool slot_fields(dev::TPInstr& in, std::vector<int*>& out) {
+    out.clear();
+    switch (in.op) {
+        case dev::TP_LOAD: out = {&in.dst}; return true;
+        case dev::TP_STORE: out = {&in.a}; return true;
+        case dev::TP_MOV: case dev::TP_BINS: case dev::TP_EXP: case dev::TP_RSQRT:
+        case dev::TP_ROWSUM: case dev::TP_ROWMAX: case dev::TP_ROWMEAN: out = {&in.dst, &in.a}; return true;
+        case dev::TP_BIN: case dev::TP_MATMUL: out = {&in.dst, &in.a, &in.b}; return true;
+        default: return false;
+    }
+}
+
+}  // namespace
+
+void jit_prepare(KernelImpl& ki, const KernelDef& kd, int k) {
+    ki.jit_state = -1;
+    if (!ki.tp_ok) return;
+    if (build_row_program(ki.tp, kd, -1, "ptowsp_rows_k" + std::to_string(k), &ki.jit_cubin, &ki.jit_note))
+        ki.jit_state = 2;
+}
+
+bool split_matmul_epilogue(KernelImpl& ki, const KernelDef& kd, int k) {
+    const dev::TileProgram& tp = ki.tp;
+    const int np = kd.num_tensor_params;
+    if (np + 1 > dev::kMaxParams) return false;
+    int mm = -1;
+    for (int i = 0; i < tp.ninstr; ++i)
+        if (tp.ins[i].op == dev::TP_MATMUL) {
+            if (mm >= 0) return false;  // one contraction per kernel
+            mm = i;
+        }
+    if (mm < 0) return false;
+    const dev::TPInstr& m = tp.ins[mm];
+    // the shapes of the tcgen05 tile kernel: 128 rows, 64/128/256 columns, K a multiple of 64
+    if (m.rows != 128 || !(m.cols == 64 || m.cols == 128 || m.cols == 256) || m.k < 64 || m.k % 64) return false;
+    if (tp.slots[m.dst].word != dev::W_F32) return false;
+    int la = -1, lb = -1;
+    for (int i = 0; i < mm; ++i) {
+        if (tp.ins[i].op != dev::TP_LOAD) continue;
+        if (tp.ins[i].dst == m.a) la = i;
+        if (tp.ins[i].dst == m.b) lb = i;
+    }
+    if (la < 0 || lb < 0 || la == lb) return false;
+    const int pa = tp.ins[la].param, pb = tp.ins[lb].param;
+    auto param_dtype = [&](int ti) {
+        for (const auto& kp : kd.params)
+            if (kp.tensor_index == ti) return kp.v.dtype;
+        return DType::F32;
+    };
+    if (pa == pb || param_dtype(pa) != DType::F16 || param_dtype(pb) != DType::F16) return false;
+    // the operand tiles and their params serve the matmul alone
+    std::vector<int*> f;
+    dev::TileProgram ep{};
+    ep.ninstr = 0;
+    for (int i = 0; i < tp.ninstr; ++i) {
+        if (i == la || i == lb) continue;
+        dev::TPInstr in = tp.ins[i];
+        if (i == mm) {
+            dev::TPInstr ld{};
+            ld.op = dev::TP_LOAD;
+            ld.dst = m.dst;
+            ld.param = np;  // the scratch tile
+            ld.rows = m.rows;
+            ld.cols = m.cols;
+            in = ld;
+        } else {
+            if (!slot_fields(in, f)) return false;
+            for (int* x : f)
+                if (*x == m.a || *x == m.b) return false;
+            if ((in.op == dev::TP_LOAD || in.op == dev::TP_STORE) && (in.param == pa || in.param == pb)) return false;
+        }
+        ep.ins[ep.ninstr++] = in;
+    }
+    // keep only the slots the epilogue uses, renumbered in order
+    std::vector<int> remap(tp.nslots, -1);
+    ep.nslots = 0;
+    for (int i = 0; i < ep.ninstr; ++i) {
+        slot_fields(ep.ins[i], f);
+        for (int* x : f) {
+            if (*x < 0 || *x >= tp.nslots) return false;
+            if (remap[*x] < 0) {
+                remap[*x] = ep.nslots;
+                ep.slots[ep.nslots++] = tp.slots[*x];
+            }
+            *x = remap[*x];
+        }
+    }
+    for (int i = 0; i < dev::kMaxParams; ++i) ep.scalar_types[i] = tp.scalar_types[i];
+    ep.smem_words = 0;
+    std::string cubin, note;
+    if (!build_row_program(ep, kd, np, "ptowsp_ep_k" + std::to_string(k), &cubin, &note)) return false;
+    ki.ep_tp = ep;
+    ki.ep_a = pa;
+    ki.ep_b = pb;
+    ki.ep_n = m.cols;
+    ki.ep_k = m.k;
+    ki.ep_cubin = std::move(cubin);
+    ki.ep_jit_state = 2;
+    ki.kind = ImplKind::MatmulEpilogue;
+    ki.jit_note = "matmul on tcgen05, the rest as a fused row program";
+    return true;
 }
 
 uint64_t run_program(Program& P, RuntimeContext* ctx) {

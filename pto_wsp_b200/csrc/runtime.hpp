@@ -16,7 +16,8 @@
 
 namespace ptowsp {
 
-enum class ImplKind : uint8_t { RmsNorm, Softmax, TileProgram, Matmul, MatmulAcc, PagedDecode, IndexerScore, TopK };
+enum class ImplKind : uint8_t { RmsNorm, Softmax, TileProgram, Matmul, MatmulAcc, MatmulEpilogue, PagedDecode,
+                                IndexerScore, TopK };
 
 const char* impl_name(ImplKind k);
 
@@ -38,10 +39,22 @@ struct KernelImpl {
     void* jit_fn = nullptr;              // CUfunction once loaded
     void* jit_fn_vec = nullptr;          // its vector-access variant, when the program has one
     std::string jit_note;                // why the interpreter runs instead
+    // MatmulEpilogue: the kernel's one f16 x f16 -> f32 matmul of params ep_a, ep_b (128 x ep_k by ep_k x ep_n)
+    // runs on the tcgen05 tile kernel into scratch; the rest is ep_tp, a row program that reads that tile as
+    // param num_tensor_params, built as its own fused kernel
+    dev::TileProgram ep_tp{};
+    int ep_a = -1, ep_b = -1, ep_n = 0, ep_k = 0;
+    int ep_jit_state = 0;                // as jit_state
+    std::string ep_cubin;
+    void* ep_fn = nullptr;
+    void* ep_fn_vec = nullptr;
 };
 
 // Build (NVRTC) the fused row kernel of kernel `k` when its tile program is row-local (jit_state -> 2 or -1).
 void jit_prepare(KernelImpl& ki, const KernelDef& kd, int k);
+// Split a generic kernel into a tcgen05 matmul and a fused row-program epilogue when its shape allows
+// (kind -> MatmulEpilogue); false leaves the kernel as it is.
+bool split_matmul_epilogue(KernelImpl& ki, const KernelDef& kd, int k);
 
 // Per-tensor binding of one run.
 struct TensorBinding {
@@ -73,6 +86,11 @@ struct Batch {  // tasks of one kernel inside one wave
     int64_t* unit_rec_dev = nullptr;
     int64_t nunits = 0;
     int8_t units_ok = -1;
+    // matmul + row-program epilogue: records of the matmul stage [oa, ob, scratch offset] and of the epilogue
+    // [the batch's records with the scratch offset after the view offsets] (-1 not built, 0 unusable, 1 built)
+    int64_t* ep_mm_rec_dev = nullptr;
+    int64_t* ep_rec_dev = nullptr;
+    int8_t ep_ok = -1;
     // host-staged pipelining: per chunk and tensor param, the [lo, hi) element range its tasks touch
     int chunk_n = 0;
     std::vector<int64_t> chunk_ranges;
@@ -83,8 +101,11 @@ struct Batch {  // tasks of one kernel inside one wave
         dev_off = o.dev_off; aligned_rows = o.aligned_rows; fast_ok = o.fast_ok; fast_rec_dev = o.fast_rec_dev;
         fast_ntasks = o.fast_ntasks; fast_n = o.fast_n; chunk_n = o.chunk_n; chunk_ranges = std::move(o.chunk_ranges);
         unit_rec_dev = o.unit_rec_dev; nunits = o.nunits; units_ok = o.units_ok;
+        ep_mm_rec_dev = o.ep_mm_rec_dev; ep_rec_dev = o.ep_rec_dev; ep_ok = o.ep_ok;
         o.fast_rec_dev = nullptr;
         o.unit_rec_dev = nullptr;
+        o.ep_mm_rec_dev = nullptr;
+        o.ep_rec_dev = nullptr;
         return *this;
     }
     Batch(const Batch&) = delete;

@@ -88,3 +88,12 @@ def test_fast_row_kernels_build_theirs_for_odd_widths_only():
     # width 96 is not one the hand-written kernel takes: the fused row program is built at compile time
     d = CudaExecutable(workloads.rmsnorm_plan(2, 2, 16, 96)).describe()["kernels"][0]
     assert d["impl"] == "rmsnorm_rows" and d["row_kernel"] == "compiled"
+
+
+def test_matmul_with_row_local_epilogue_is_split():
+    from _mm_epilogue import mm_epilogue_plan
+
+    if not nvrtc_available():
+        pytest.skip("NVRTC not installed")
+    d = CudaExecutable(mm_epilogue_plan(1, 256, 256, 256)).describe()["kernels"][0]
+    assert d["impl"] == "matmul_tcgen05+row_program", d
