@@ -185,12 +185,50 @@ int program_rows(const TileProgram& tp) {
 // A one-row tile in a program over R > 1 rows: the same for every row ([1,C] operands of column broadcasts).
 static bool row_invariant(const TileProgram& tp, int slot) { return tp.slots[slot].rows == 1 && program_rows(tp) > 1; }
 
-// Element offset of tile row r of a view: none for a row-invariant tile (row 0 of its view).
-static std::string row_offset(const TileProgram& tp, int slot, const std::string& p) {
+// Element offset of tile row r of a view: none for a row-invariant tile (row 0 of its view); element r of row 0 for
+// a load marked transposed (in.k == 1, see normalize).
+static std::string row_offset(const TileProgram& tp, int slot, const std::string& p, bool transposed = false) {
+    if (transposed) return " + (int64_t)r * " + p + ".s4";
     return row_invariant(tp, slot) ? std::string() : " + (int64_t)r * " + p + ".s3";
 }
 
-bool row_local(const TileProgram& tp, std::string* why) {
+// The emitter broadcasts a one-row [1, R] operand over rows too (TROWEXPAND*: when its length equals the row
+// count, element r goes to row r).  Such a tile, loaded from a param and used only that way, becomes an [R, 1]
+// tile whose load (marked in.k = 1) reads element r of the view's first row for row r.
+static TileProgram normalize(const TileProgram& tp) {
+    TileProgram out = tp;
+    const int R = program_rows(tp);
+    if (R <= 1) return out;
+    for (int s = 0; s < tp.nslots; ++s) {
+        if (tp.slots[s].rows != 1 || tp.slots[s].cols != R) continue;
+        int loads = 0, row_uses = 0, other = 0, ld = -1;
+        for (int i = 0; i < tp.ninstr; ++i) {
+            const TPInstr& in = tp.ins[i];
+            // the slot fields each op uses (the others are left at zero)
+            const bool d = in.op != TP_STORE && in.dst == s;
+            const bool a = in.op != TP_LOAD && in.a == s;
+            const bool b = (in.op == TP_BIN || in.op == TP_MATMUL) && in.b == s;
+            if (in.op == TP_LOAD && d) {
+                ++loads;
+                ld = i;
+            } else if (in.op == TP_BIN && in.mode == MODE_ROW && b && !a && !d) {
+                ++row_uses;
+            } else if (d || a || b) {
+                ++other;
+            }
+        }
+        if (loads != 1 || row_uses == 0 || other) continue;
+        out.slots[s].rows = R;
+        out.slots[s].cols = 1;
+        out.ins[ld].rows = R;
+        out.ins[ld].cols = 1;
+        out.ins[ld].k = 1;
+    }
+    return out;
+}
+
+bool row_local(const TileProgram& tp_in, std::string* why) {
+    const TileProgram tp = normalize(tp_in);
     auto fail = [&](const std::string& m) {
         if (why) *why = m;
         return false;
@@ -281,7 +319,7 @@ void emit_row_kernel(std::ostringstream& o, const TileProgram& tp, const int* pa
                 const TPSlot& t = tp.slots[slot];
                 const int pt = param_types[in.param];
                 const std::string p = "b.p[" + std::to_string(in.param) + "]";
-                o << "      const int64_t base = rec[" << in.param << "]" << row_offset(tp, slot, p) << ";\n";
+                o << "      const int64_t base = rec[" << in.param << "]" << row_offset(tp, slot, p, load && in.k == 1) << ";\n";
                 const int nj = (t.cols + 31) / 32;
                 o << "      #pragma unroll\n      for (int j = 0; j < " << nj << "; ++j) {\n";
                 o << "        const int c = lane + 32 * j;" << (load ? " unsigned w = 0u;" : "") << "\n";
@@ -419,7 +457,7 @@ void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* 
                 const TPSlot& t = tp.slots[slot];
                 const int pt = param_types[in.param];
                 const std::string p = "b.p[" + std::to_string(in.param) + "]";
-                o << "      const int64_t base = rec[" << in.param << "]" << row_offset(tp, slot, p) << ";\n";
+                o << "      const int64_t base = rec[" << in.param << "]" << row_offset(tp, slot, p, load && in.k == 1) << ";\n";
                 if (t.cols == 1) {  // [R,1]: the group leader's element, broadcast inside the group
                     if (load) {
                         o << "      unsigned w = 0u;\n";
@@ -552,7 +590,8 @@ void emit_group_kernel(std::ostringstream& o, const TileProgram& tp, const int* 
 
 }  // namespace
 
-bool vector_form(const TileProgram& tp, const int* param_types) {
+bool vector_form(const TileProgram& tp_in, const int* param_types) {
+    const TileProgram tp = normalize(tp_in);
     for (int ii = 0; ii < tp.ninstr; ++ii) {
         const TPInstr& in = tp.ins[ii];
         if (in.op != TP_LOAD && in.op != TP_STORE) continue;
@@ -563,7 +602,8 @@ bool vector_form(const TileProgram& tp, const int* param_types) {
     return true;
 }
 
-std::string gen_row_kernel(const TileProgram& tp, const int* param_types, const std::string& name) {
+std::string gen_row_kernel(const TileProgram& tp_in, const int* param_types, const std::string& name) {
+    const TileProgram tp = normalize(tp_in);
     std::ostringstream o;
     o << "#define MAXP " << kMaxParams << "\n" << kPrelude;
     emit_row_kernel(o, tp, param_types, name);

@@ -11,10 +11,10 @@ def f32_bits(x: float) -> str:
     return hex(struct.unpack("<I", struct.pack("<f", x))[0])
 
 
-def mm_epilogue_plan(batch, m, n, k, tn=256, scale=0.125):
+def mm_epilogue_plan(batch, m, n, k, tn=256, scale=0.125, bias_op="Sub"):
     """out = exp(s - rowmax(s)) with s = (A . B - bias) * scale per 128 x tn output tile; bias is a one-row [1, tn]
     operand (a column broadcast: tn != 128, else the emitter's row-broadcast rule takes a [1, 128] operand), scale
-    a scalar param.  Tensors as in the bgemm plan: 0 = A [B, M/128, 128, K] f16,
+    a scalar param.  With tn = 128 and bias_op "Add" the bias is a row broadcast instead (element r to row r).  Tensors as in the bgemm plan: 0 = A [B, M/128, 128, K] f16,
     1 = B viewed [B, N/tn, K, tn] f16, 2 = bias [B, N/tn, 1, tn] f32, 3 = out viewed [B, M/128, N/tn, 128, tn] f32."""
     kb = KernelBuilder("mm_softmax_tile")
     a = kb.param("a", "f16", 128, k)
@@ -23,7 +23,7 @@ def mm_epilogue_plan(batch, m, n, k, tn=256, scale=0.125):
     out = kb.param("out", "f32", 128, tn)
     sc = kb.param("scale", "f32")
     c = kb.op("Matmul", [a, b], ("f32", 128, tn))
-    d = kb.op("Sub", [c, bias], ("f32", 128, tn))
+    d = kb.op(bias_op, [c, bias], ("f32", 128, tn))
     e = kb.op("Mul", [d, sc], ("f32", 128, tn))
     mx = kb.op("RowMax", [e], ("f32", 128, 1))
     f = kb.op("Sub", [e, mx], ("f32", 128, tn))

@@ -79,3 +79,35 @@ def test_column_broadcast_row_kernel_bit_exact(cols, dtype, require_cuda):
     assert ex.run_with_symbols([x, v, w, got], {}, {}, {}) == cyc
     assert ex.describe()["kernels"][0]["row_kernel"] == "loaded"
     np.testing.assert_array_equal(got, ref)
+
+
+def row_vector_plan(B, R, C):
+    """out = (x + v) * v with v a one-row [1, R] operand: the emitter's row broadcast (element r to row r)."""
+    from pto_wsp_b200.workloads import KernelBuilder, _pfor, _plan, _schedule, _targ, _task
+
+    k = KernelBuilder("row_vec")
+    x = k.param("x", "f32", R, C)
+    v = k.param("v", "f32", 1, R)
+    out = k.param("out", "f32", R, C)
+    d = k.op("Add", [x, v], ("f32", R, C))
+    k.store(out, k.op("Mul", [d, v], ("f32", R, C)))
+    body = _pfor("b", B, _task("row_vec", ["b"], [_targ("x", 0, 3, ["b"]), _targ("v", 1, 3, ["b"]),
+                                                 _targ("out", 2, 3, ["b"])]))
+    return _plan("row_vec", [("f32", [B, R, C]), ("f32", [B, 1, R]), ("f32", [B, R, C])], [k.build()], body,
+                 _schedule())
+
+
+@pytest.mark.parametrize("R,C", [(16, 64), (8, 40), (32, 33)])
+def test_one_row_operand_broadcast_over_rows_bit_exact(R, C, require_cuda):
+    rng = np.random.default_rng(R * C)
+    B = 5
+    plan = row_vector_plan(B, R, C)
+    x = rng.standard_normal((B, R, C)).astype(np.float32)
+    v = rng.standard_normal((B, 1, R)).astype(np.float32)
+    ref = np.full((B, R, C), np.nan, np.float32)
+    cyc = CpuSim(plan).run([x, v, ref])
+    got = np.full_like(ref, np.nan)
+    ex = CudaExecutable(plan)
+    assert ex.run_with_symbols([x, v, got], {}, {}, {}) == cyc
+    assert ex.describe()["kernels"][0]["row_kernel"] == "loaded"
+    np.testing.assert_array_equal(got, ref)

@@ -12,14 +12,15 @@ from pto_wsp_b200.runtime import CudaExecutable
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("batch,m,n,k", [(2, 256, 512, 256), (1, 128, 256, 2048)])
-def test_matmul_epilogue_matches_oracle(batch, m, n, k, require_cuda):
+@pytest.mark.parametrize("batch,m,n,k,tn,op", [(2, 256, 512, 256, 256, "Sub"), (1, 128, 256, 2048, 256, "Sub"),
+                                               (2, 256, 256, 512, 128, "Add")])
+def test_matmul_epilogue_matches_oracle(batch, m, n, k, tn, op, require_cuda):
     rng = np.random.default_rng(m + n + k)
-    plan = mm_epilogue_plan(batch, m, n, k)
-    (A, B, bias, C), views = mm_epilogue_arrays(rng, batch, m, n, k)
+    plan = mm_epilogue_plan(batch, m, n, k, tn=tn, bias_op=op)
+    (A, B, bias, C), views = mm_epilogue_arrays(rng, batch, m, n, k, tn=tn)
     ref_views = [v.copy() if i < 3 else v for i, v in enumerate(views)]
     C_ref = np.full_like(C, np.nan)
-    ref_views[3] = C_ref.reshape(batch, m // 128, 128, n // 256, 256).transpose(0, 1, 3, 2, 4)
+    ref_views[3] = C_ref.reshape(batch, m // 128, 128, n // tn, tn).transpose(0, 1, 3, 2, 4)
     cyc = CpuSim(plan).run(ref_views)
     ex = CudaExecutable(plan)
     assert ex.describe()["kernels"][0]["impl"] == "matmul_tcgen05+row_program"
