@@ -739,6 +739,7 @@ Batch::~Batch() {
     if (unit_rec_dev) cudaFree(unit_rec_dev);
     if (ep_mm_rec_dev) cudaFree(ep_mm_rec_dev);
     if (ep_rec_dev) cudaFree(ep_rec_dev);
+    if (ep_unit_rec_dev) cudaFree(ep_unit_rec_dev);
 }
 
 LaunchProgram::~LaunchProgram() {
@@ -987,6 +988,39 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                 for (int j = np; j < B.stride; ++j) o[j + 1] = r[j];
             }
             B.ep_ok = ok ? 1 : 0;
+            if (ok && (N == 128 || N == 256) && B.ntasks % 2 == 0) {
+                // CTA pairs for the matmul stage: each task with the task 128 rows below it in A that reads the
+                // same B tile (each CTA stores its own scratch tile)
+                std::unordered_map<uint64_t, int64_t> at;
+                at.reserve(static_cast<size_t>(B.ntasks) * 2);
+                auto key = [](int64_t oa, int64_t ob) {  // splitmix64 finaliser of the pair
+                    uint64_t z = static_cast<uint64_t>(oa) * 0x9e3779b97f4a7c15ull ^ static_cast<uint64_t>(ob);
+                    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+                    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+                    return z ^ (z >> 31);
+                };
+                bool fine = true;
+                for (int64_t t = 0; fine && t < B.ntasks; ++t) fine = at.emplace(key(mm[t * 3], mm[t * 3 + 1]), t).second;
+                std::vector<char> used(static_cast<size_t>(B.ntasks), 0);
+                std::vector<int64_t> units;
+                units.reserve(static_cast<size_t>(B.ntasks) * 3);
+                for (int64_t t = 0; fine && t < B.ntasks; ++t) {
+                    if (used[t]) continue;
+                    auto it = at.find(key(mm[t * 3] + 128 * A.s3, mm[t * 3 + 1]));
+                    fine = it != at.end() && !used[it->second] && mm[it->second * 3] == mm[t * 3] + 128 * A.s3 &&
+                           mm[it->second * 3 + 1] == mm[t * 3 + 1];
+                    if (!fine) break;
+                    used[t] = used[it->second] = 1;
+                    for (int j = 0; j < 3; ++j) units.push_back(mm[t * 3 + j]);
+                    for (int j = 0; j < 3; ++j) units.push_back(mm[it->second * 3 + j]);
+                }
+                if (fine) {
+                    PW_CUDA(cudaMalloc(&B.ep_unit_rec_dev, units.size() * sizeof(int64_t)));
+                    PW_CUDA(cudaMemcpy(B.ep_unit_rec_dev, units.data(), units.size() * sizeof(int64_t),
+                                       cudaMemcpyHostToDevice));
+                    B.ep_nunits = static_cast<int64_t>(units.size() / 6);
+                }
+            }
             if (ok) {
                 PW_CUDA(cudaMalloc(&B.ep_mm_rec_dev, mm.size() * sizeof(int64_t)));
                 PW_CUDA(cudaMemcpy(B.ep_mm_rec_dev, mm.data(), mm.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
@@ -1019,7 +1053,11 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
             mtb.stride = 3;
             mtb.nparams = 3;
             mtb.err = P.err_dev;
-            e = dev::launch_matmul_tiles(mtb, 0, workers, P.stream);
+            cudaError_t pe = cudaSuccess;
+            if (B.ep_unit_rec_dev && dev::launch_matmul_pairs(mtb, B.ep_unit_rec_dev, B.ep_nunits, 0, workers, P.stream, &pe))
+                e = pe;
+            else
+                e = dev::launch_matmul_tiles(mtb, 0, workers, P.stream);
             if (e != cudaSuccess) break;
             launches++;
             dev::TaskBatch etb = tb;

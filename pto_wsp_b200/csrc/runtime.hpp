@@ -90,6 +90,8 @@ struct Batch {  // tasks of one kernel inside one wave
     // [the batch's records with the scratch offset after the view offsets] (-1 not built, 0 unusable, 1 built)
     int64_t* ep_mm_rec_dev = nullptr;
     int64_t* ep_rec_dev = nullptr;
+    int64_t* ep_unit_rec_dev = nullptr;  // matmul stage on CTA pairs: tasks 128 rows apart in A sharing B
+    int64_t ep_nunits = 0;
     int8_t ep_ok = -1;
     // host-staged pipelining: per chunk and tensor param, the [lo, hi) element range its tasks touch
     int chunk_n = 0;
@@ -102,6 +104,8 @@ struct Batch {  // tasks of one kernel inside one wave
         fast_ntasks = o.fast_ntasks; fast_n = o.fast_n; chunk_n = o.chunk_n; chunk_ranges = std::move(o.chunk_ranges);
         unit_rec_dev = o.unit_rec_dev; nunits = o.nunits; units_ok = o.units_ok;
         ep_mm_rec_dev = o.ep_mm_rec_dev; ep_rec_dev = o.ep_rec_dev; ep_ok = o.ep_ok;
+        ep_unit_rec_dev = o.ep_unit_rec_dev; ep_nunits = o.ep_nunits;
+        o.ep_unit_rec_dev = nullptr;
         o.fast_rec_dev = nullptr;
         o.unit_rec_dev = nullptr;
         o.ep_mm_rec_dev = nullptr;
