@@ -738,9 +738,10 @@ cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cu
 // ---------------------------------------------------------------------------
 
 constexpr int kTopkThreads = 1024;
+constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kHistCopies = 16;                    // lane-private copies of the 256-bin histogram (lanes l, l+16 share one)
 constexpr int kTopkSmemMax = 227 * 1024 - 2048;    // opt-in dynamic shared memory less this kernel's static part
-constexpr int kCandMax = 4096;                     // candidate list of the last radix pass
+constexpr int kCandMax = 8192;                     // candidate list (sampled bound, or the last radix pass)
 constexpr int kTieMax = 512;                       // ties at the threshold ranked pairwise up to this many
 
 __device__ __forceinline__ uint32_t order_key(float f) {
@@ -884,21 +885,82 @@ __device__ __forceinline__ void bitonic_sort_store(unsigned long long* comp, int
     }
 }
 
+// Radix-select digit choice from 256 bin totals: the digit d (bits shift .. shift+7) with
+// count(digit > d) < need <= count(digit >= d); every thread gets back the prefix extended by d and the rank
+// still needed inside that digit, s_eq the digit's count.  Call with bin_tot complete and visible to warp 0;
+// two block barriers.
+__device__ __forceinline__ void topk_pick_digit(const uint32_t* bin_tot, uint32_t* s_prefix, uint32_t* s_need,
+                                                uint32_t* s_eq, int shift, uint32_t& prefix, uint32_t& need, int lane,
+                                                int wid) {
+    if (wid == 0) {
+        // lane l holds bins 8l .. 8l+7
+        uint32_t c[8], local = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            c[j] = bin_tot[8 * lane + j];
+            local += c[j];
+        }
+        uint32_t suf = local;  // sum over lanes l .. 31
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t n = __shfl_down_sync(0xffffffffu, suf, o);
+            if (lane + o < 32) suf += n;
+        }
+        const uint32_t above = suf - local;
+        if (above < need && need <= suf) {
+            uint32_t acc = above;
+            int d = 8 * lane;
+            uint32_t rem = need - above, cnt_d = 0;
+#pragma unroll
+            for (int j = 7; j >= 0; --j) {
+                if (acc + c[j] >= need) {
+                    d = 8 * lane + j;
+                    rem = need - acc;
+                    cnt_d = c[j];
+                    break;
+                }
+                acc += c[j];
+            }
+            *s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+            *s_need = rem;
+            *s_eq = cnt_d;
+        }
+    }
+    __syncthreads();
+    prefix = *s_prefix;
+    need = *s_need;
+    __syncthreads();  // the totals and the shared results are free for the next pass
+}
+
+// Sums the lane-private histogram copies into bin_tot, then picks the digit (topk_pick_digit).
+__device__ __forceinline__ void topk_radix_digit(const uint32_t* hist, uint32_t* bin_tot, uint32_t* s_prefix,
+                                                 uint32_t* s_need, uint32_t* s_eq, int shift, uint32_t& prefix,
+                                                 uint32_t& need, int lane, int wid) {
+    __syncthreads();
+    for (int bin = wid * 8; bin < wid * 8 + 8; ++bin) {
+        const uint32_t v = lane < kHistCopies ? hist[bin * kHistCopies + lane] : 0u;
+        const uint32_t t = __reduce_add_sync(0xffffffffu, v);
+        if (lane == 0) bin_tot[bin] = t;
+    }
+    __syncthreads();
+    topk_pick_digit(bin_tot, s_prefix, s_need, s_eq, shift, prefix, need, lane, wid);
+}
+
 // One CTA per row.  (1) Keys: the row as order-preserving 32-bit keys in
-// shared memory, histogrammed by their top digit as they are stored.
-// (2) Select: the exact K-th largest key by a 4-pass 8-bit radix select; each
-// pass histograms the keys that match the digits chosen so far into
-// lane-private copies of a 256-bin histogram (no two lanes of a warp add to
-// the same counter in the same instruction), sums the copies, and one warp
-// finds the digit holding the K-th key.  Pass 2 also sorts the row out: keys
-// above the 16-bit prefix are winners whatever their last digits and go
-// straight to the composite buffer; keys that match it are listed as the
-// candidates that pass 3 scans instead of the row.  (3) Gather: the
-// candidates above the threshold join the winners; keys equal to the
-// threshold join them too when all are taken, otherwise the `need` of lowest
-// index (the reference's stable order) are ranked by index.  (4) Bitonic sort
-// of the (key, ~index) composites, descending.  Winners land in arbitrary
-// slots; the sort's total order makes the result exact.
+// shared memory.  (2) Sampled bound: the 16-bit bucket of a high-ranked key of
+// an evenly spaced 1024-key sample bounds the threshold from below; the keys
+// at or above it are listed (about 1.5 K of them for 2048 of 32768).
+// (3) Select: the exact K-th largest key by a 4-pass 8-bit radix select over
+// that list -- or, when the bound missed (skewed rows), over the row, pass 2
+// then sending keys above the 16-bit prefix straight to the composite buffer
+// and listing those matching it for pass 3.  Each pass histograms the keys
+// that match the digits chosen so far into lane-private copies of a 256-bin
+// histogram, sums the copies, and one warp finds the digit of the K-th key.
+// (4) Gather: the listed keys above the threshold join the winners; keys
+// equal to the threshold join them too when all are taken, otherwise the
+// `need` of lowest index (the reference's stable order) are ranked by index.
+// (5) Bitonic sort of the (key, ~index) composites, descending.  Winners land
+// in arbitrary slots; the sort's total order makes the result exact.
 __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) {
     extern __shared__ __align__(16) uint8_t tsm[];
     __shared__ uint32_t bin_tot[256];
@@ -924,14 +986,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     const int n4 = (N + 3) >> 2;  // 16-byte groups of keys (the last one may be partial; the buffer is padded)
     uint32_t* hl = hist + (lane & (kHistCopies - 1));
 
-    // (1) keys, histogrammed for the first pass on the way in
-    for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
+    // (1) keys
     if (threadIdx.x == 0) {
         s_ncand = 0u;
         s_nwin = 0u;
         s_ntie = 0u;
     }
-    __syncthreads();
     int head = 0;  // keys [0, head) come in 16-byte vectors, eight per thread in flight
     if (ss == 1 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
         const int f4 = N >> 2;
@@ -948,14 +1008,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int i = base + j * kTopkThreads + threadIdx.x;
-                if (i < f4) {
-                    const uint4 kk = make_uint4(order_key(v[j].x), order_key(v[j].y), order_key(v[j].z), order_key(v[j].w));
-                    w4[i] = kk;
-                    atomicAdd(hl + (kk.x >> 24) * kHistCopies, 1u);
-                    atomicAdd(hl + (kk.y >> 24) * kHistCopies, 1u);
-                    atomicAdd(hl + (kk.z >> 24) * kHistCopies, 1u);
-                    atomicAdd(hl + (kk.w >> 24) * kHistCopies, 1u);
-                }
+                if (i < f4) w4[i] = make_uint4(order_key(v[j].x), order_key(v[j].y), order_key(v[j].z), order_key(v[j].w));
             }
         }
     }
@@ -969,101 +1022,128 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int i = i0 + j * kTopkThreads + threadIdx.x;
-            if (i < N) {
-                ks[i] = kk[j];
-                atomicAdd(hl + (kk[j] >> 24) * kHistCopies, 1u);
+            if (i < N) ks[i] = kk[j];
+        }
+    }
+    __syncthreads();
+
+    // (2) A lower bound for the threshold from an evenly spaced sample of 1024 keys: the 16-bit bucket of the
+    // sample's r-th largest key, with r four standard deviations above the expected number of winners in the
+    // sample.  Every key at or above it is listed; when that gives between K and the list's capacity keys, the
+    // exact selection runs over the list alone.  Otherwise (a skewed row) the full-row passes below run.
+    bool from_cand = false;
+    {
+        const float expect = static_cast<float>(K) * kTopkThreads / static_cast<float>(N);
+        const int r = static_cast<int>(ceilf(expect + 4.f * sqrtf(expect) + 4.f));
+        if (N >= 4 * kTopkThreads && r < kTopkThreads / 4 && cand_cap >= static_cast<uint32_t>(K)) {
+            const uint32_t smp = ks[static_cast<int64_t>(threadIdx.x) * N / kTopkThreads];
+            uint32_t sp = 0, sn = static_cast<uint32_t>(r);
+            for (int pass = 0; pass < 2; ++pass) {
+                const int shift = 24 - 8 * pass;
+                const uint32_t hmask = pass == 0 ? 0u : 0xff000000u;
+                for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
+                __syncthreads();
+                if ((smp & hmask) == sp) atomicAdd(hl + ((smp >> shift) & 255u) * kHistCopies, 1u);
+                topk_radix_digit(hist, bin_tot, &s_prefix, &s_need, &s_eq, shift, sp, sn, lane, wid);
             }
+            const uint32_t lo = sp;  // lowest key of that 16-bit bucket
+            // every warp lists its keys >= lo into its own segment of the list (no shared counter), then the
+            // segments are packed to the front
+            const unsigned below = (1u << lane) - 1u;
+            const uint32_t seg = cand_cap / kTopkWarps;
+            uint32_t wc = 0;  // keys this warp found (the same in every lane)
+            for (int base = 0; base < n4; base += kTopkThreads) {  // warps step together (ballots)
+                const int q = base + threadIdx.x;
+                const uint4 k4 = q < n4 ? ks4[q] : make_uint4(0u, 0u, 0u, 0u);
+                const int lim = N - 4 * q;
+                const uint32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
+                unsigned bal[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) bal[j] = __ballot_sync(0xffffffffu, j < lim && kk[j] >= lo);
+                if ((bal[0] | bal[1] | bal[2] | bal[3]) == 0u) continue;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t at = wc + __popc(bal[j] & below);
+                    if (((bal[j] >> lane) & 1u) && at < seg) cand[wid * seg + at] = topk_composite(kk[j], 4 * q + j);
+                    wc += __popc(bal[j]);
+                }
+            }
+            uint32_t* wcnt = hist;  // the histogram is free until the next pass
+            if (lane == 0) wcnt[wid] = wc;
+            __syncthreads();
+            uint32_t off = 0, tot = 0;
+            bool over = false;
+            for (int w = 0; w < kTopkWarps; ++w) {
+                const uint32_t c = wcnt[w];
+                if (w < wid) off += c;
+                tot += c;
+                over = over || c > seg;
+            }
+            from_cand = !over && tot >= static_cast<uint32_t>(K) && tot <= cand_cap;
+            if (from_cand) {
+                unsigned long long v[kCandMax / kTopkWarps / 32];
+#pragma unroll
+                for (int e = 0; e < kCandMax / kTopkWarps / 32; ++e) {
+                    const uint32_t i = lane + 32u * e;
+                    v[e] = i < wc ? cand[wid * seg + i] : 0ull;
+                }
+                __syncthreads();  // every segment is in registers before any is overwritten
+#pragma unroll
+                for (int e = 0; e < kCandMax / kTopkWarps / 32; ++e) {
+                    const uint32_t i = lane + 32u * e;
+                    if (i < wc) cand[off + i] = v[e];
+                }
+                if (threadIdx.x == 0) s_ncand = tot;
+            }
+            __syncthreads();
         }
     }
 
-    // (2) radix select, most significant digit first
+    // (3) radix select, most significant digit first: over the listed keys, or over the row (pass 2 then sorts the
+    // row out: keys above the 16-bit prefix go straight to the composite buffer, keys matching it are listed for
+    // pass 3 and the gather)
     uint32_t prefix = 0, need = static_cast<uint32_t>(K);
     for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
         const uint32_t hmask = pass == 0 ? 0u : (0xffffffffu << (shift + 8));
-        if (pass > 0) {
-            for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
-            __syncthreads();  // previous totals read, counters zeroed
-            if (pass == 3 && s_ncand <= cand_cap) {
-                const int nc = static_cast<int>(s_ncand);
-                for (int i = threadIdx.x; i < nc; i += kTopkThreads) {
-                    const uint32_t k = static_cast<uint32_t>(cand[i] >> 32);
-                    if ((k & hmask) == prefix) atomicAdd(hl + (k & 255u) * kHistCopies, 1u);
-                }
-            } else {
-                for (int base = 0; base < n4; base += kTopkThreads) {  // warps step together (ballots below)
-                    const int q = base + threadIdx.x;
-                    const uint4 k4 = q < n4 ? ks4[q] : make_uint4(0u, 0u, 0u, 0u);
-                    const int lim = N - 4 * q;  // keys of this group inside the row
-                    const uint32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
-                    bool m[4], w[4];
-                    unsigned long long c[4];
+        for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
+        __syncthreads();  // previous totals read, counters zeroed
+        if (from_cand || (pass == 3 && s_ncand <= cand_cap)) {
+            const int nc = static_cast<int>(s_ncand);
+            for (int i = threadIdx.x; i < nc; i += kTopkThreads) {
+                const uint32_t k = static_cast<uint32_t>(cand[i] >> 32);
+                if ((k & hmask) == prefix) atomicAdd(hl + ((k >> shift) & 255u) * kHistCopies, 1u);
+            }
+        } else {
+            for (int base = 0; base < n4; base += kTopkThreads) {  // warps step together (ballots below)
+                const int q = base + threadIdx.x;
+                const uint4 k4 = q < n4 ? ks4[q] : make_uint4(0u, 0u, 0u, 0u);
+                const int lim = N - 4 * q;  // keys of this group inside the row
+                const uint32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
+                bool m[4], w[4];
+                unsigned long long c[4];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t k = kk[j];
-                        m[j] = j < lim && (k & hmask) == prefix;
-                        w[j] = j < lim && (k & hmask) > prefix;
-                        c[j] = topk_composite(k, 4 * q + j);
-                        if (m[j]) atomicAdd(hl + ((k >> shift) & 255u) * kHistCopies, 1u);
-                    }
-                    if (pass == 2) {
-                        warp_append4(m, c, cand, &s_ncand, cand_cap, lane);
-                        warp_append4(w, c, comp, &s_nwin, static_cast<uint32_t>(K), lane);
-                    }
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t k = kk[j];
+                    m[j] = j < lim && (k & hmask) == prefix;
+                    w[j] = j < lim && (k & hmask) > prefix;
+                    c[j] = topk_composite(k, 4 * q + j);
+                    if (m[j]) atomicAdd(hl + ((k >> shift) & 255u) * kHistCopies, 1u);
+                }
+                if (pass == 2) {
+                    warp_append4(m, c, cand, &s_ncand, cand_cap, lane);
+                    warp_append4(w, c, comp, &s_nwin, static_cast<uint32_t>(K), lane);
                 }
             }
         }
-        __syncthreads();
-        for (int bin = wid * 8; bin < wid * 8 + 8; ++bin) {
-            const uint32_t v = lane < kHistCopies ? hist[bin * kHistCopies + lane] : 0u;
-            const uint32_t t = __reduce_add_sync(0xffffffffu, v);
-            if (lane == 0) bin_tot[bin] = t;
-        }
-        __syncthreads();
-        if (wid == 0) {
-            // lane l holds bins 8l .. 8l+7; find digit d with count(digit > d) < need <= count(digit >= d)
-            uint32_t c[8], local = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                c[j] = bin_tot[8 * lane + j];
-                local += c[j];
-            }
-            uint32_t suf = local;  // sum over lanes l .. 31
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t n = __shfl_down_sync(0xffffffffu, suf, o);
-                if (lane + o < 32) suf += n;
-            }
-            const uint32_t above = suf - local;
-            if (above < need && need <= suf) {
-                uint32_t acc = above;
-                int d = 8 * lane;
-                uint32_t rem = need - above, cnt_d = 0;
-#pragma unroll
-                for (int j = 7; j >= 0; --j) {
-                    if (acc + c[j] >= need) {
-                        d = 8 * lane + j;
-                        rem = need - acc;
-                        cnt_d = c[j];
-                        break;
-                    }
-                    acc += c[j];
-                }
-                s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
-                s_need = rem;
-                s_eq = cnt_d;  // after the last pass: how many keys equal the threshold
-            }
-        }
-        __syncthreads();
-        prefix = s_prefix;
-        need = s_need;
+        topk_radix_digit(hist, bin_tot, &s_prefix, &s_need, &s_eq, shift, prefix, need, lane, wid);
     }
     const uint32_t thr = prefix;       // the K-th largest key; `need` keys equal to it are taken
     const bool all_eq = s_eq == need;  // no tie to break: every key equal to the threshold is taken
     const uint32_t n_gt = static_cast<uint32_t>(K) - need;  // keys strictly above the threshold
     unsigned long long* tie = reinterpret_cast<unsigned long long*>(hist);  // histogram no longer needed
 
-    // (3) gather the rest of the winners from the candidates (or, if they overflowed, from the row)
+    // (4) gather the rest of the winners from the candidates (or, if they overflowed, from the row)
     if (s_ncand <= cand_cap) {
         const int nc = static_cast<int>(s_ncand);
         for (int base = 0; base < nc; base += kTopkThreads) {
@@ -1139,7 +1219,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     for (int i = threadIdx.x; i < K2; i += kTopkThreads)
         if (i >= K) comp[i] = 0ull;  // padding sorts last
 
-    // (4) bitonic sort of K2 composites, descending (key desc, then index asc via the inverted index).
+    // (5) bitonic sort of K2 composites, descending (key desc, then index asc via the inverted index).
     int32_t* dst = reinterpret_cast<int32_t*>(O.base) + rec[1];
     if (K2 >= 128 && K2 <= 4 * kTopkThreads) {
         bitonic_sort_store<4>(comp, K2, K, dst, O.s4);
