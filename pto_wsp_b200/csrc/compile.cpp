@@ -611,11 +611,123 @@ void collect_depths(const Plan& plan, const Node& n, std::vector<int>& depth) {
     }
 }
 
+// ---- device-selected scalars ----
+
+bool same_index(const std::vector<IndexExpr>& a, const std::vector<IndexExpr>& b) {
+    if (a.size() != b.size()) return false;
+    for (size_t i = 0; i < a.size(); ++i)
+        if (a[i].is_var != b[i].is_var || a[i].var != b[i].var || a[i].c != b[i].c) return false;
+    return true;
+}
+
+bool same_task_shape(const Node& a, const Node& b) {  // kernel, axis args and views equal; scalars may differ
+    if (a.kernel_index != b.kernel_index || a.axis_args.size() != b.axis_args.size() ||
+        a.tensor_args.size() != b.tensor_args.size() || a.scalar_args.size() != b.scalar_args.size())
+        return false;
+    for (size_t i = 0; i < a.axis_args.size(); ++i)
+        if (a.axis_args[i].kind != b.axis_args[i].kind || a.axis_args[i].var != b.axis_args[i].var ||
+            a.axis_args[i].v != b.axis_args[i].v)
+            return false;
+    for (size_t i = 0; i < a.tensor_args.size(); ++i) {
+        const TensorArg &x = a.tensor_args[i], &y = b.tensor_args[i];
+        if (x.param != y.param || x.tensor != y.tensor || x.base_rank != y.base_rank || x.view_rank != y.view_rank ||
+            !same_index(x.index, y.index))
+            return false;
+    }
+    return true;
+}
+
+bool expr_mentions(const Expr* e, Expr::Op op, bool any_value, uint64_t v) {
+    if (!e) return false;
+    if (e->op == op && (any_value || e->v == v)) return true;
+    return expr_mentions(e->a.get(), op, any_value, v) || expr_mentions(e->b.get(), op, any_value, v) ||
+           expr_mentions(e->c.get(), op, any_value, v);
+}
+
+// Builds the DevSelect of cond tree `n` over slot `slot`; false when the tree has another shape.
+bool build_select(const Node& n, uint32_t slot, DevSelect& ds, int& code) {
+    if (n.kind == Node::Kind::Task) {
+        if (!ds.leaves.empty() && !same_task_shape(*ds.leaves[0], n)) return false;
+        ds.leaves.push_back(&n);
+        code = ~static_cast<int>(ds.leaves.size() - 1);
+        return true;
+    }
+    if (n.kind != Node::Kind::Cond || !n.pred || n.pred->op != Expr::Op::Binary) return false;
+    const Expr& p = *n.pred;
+    static const char* cmps[] = {"<", "<=", ">", ">=", "==", "!="};
+    if (std::find_if(std::begin(cmps), std::end(cmps), [&](const char* c) { return p.fn == c; }) == std::end(cmps))
+        return false;
+    const bool left = p.a && p.a->op == Expr::Op::Slot && p.a->v == slot;
+    const bool right = p.b && p.b->op == Expr::Op::Slot && p.b->v == slot;
+    if (left == right) return false;
+    const Expr* other = left ? p.b.get() : p.a.get();
+    const Expr* sl = left ? p.a.get() : p.b.get();
+    if (sl->ty == Expr::Ty::Bool) return false;  // a slot read as bool: keep the host path
+    if (expr_mentions(other, Expr::Op::Slot, true, 0) || expr_mentions(other, Expr::Op::TaskParam, true, 0))
+        return false;
+    const int me = static_cast<int>(ds.cmp.size());
+    ds.cmp.push_back(p.fn);
+    ds.slot_left.push_back(left ? 1 : 0);
+    ds.other.push_back(other);
+    ds.slot_expr.push_back(sl);
+    ds.then_c.push_back(0);
+    ds.else_c.push_back(0);
+    int t = 0, e = 0;
+    if (!build_select(*n.then_n, slot, ds, t) || !build_select(*n.else_n, slot, ds, e)) return false;
+    ds.then_c[me] = t;
+    ds.else_c[me] = e;
+    code = me;
+    return true;
+}
+
+// Every place slot `slot` is set or read, besides the load and tree of a candidate.
+int slot_uses(const Node& n, uint32_t slot) {
+    int u = 0;
+    if ((n.kind == Node::Kind::SlotLoad || n.kind == Node::Kind::SlotSet) && n.slot == slot) ++u;
+    if (n.kind == Node::Kind::Cond && expr_mentions(n.pred.get(), Expr::Op::Slot, false, slot)) ++u;
+    if (n.body) u += slot_uses(*n.body, slot);
+    for (auto& c : n.children) u += slot_uses(*c, slot);
+    if (n.then_n) u += slot_uses(*n.then_n, slot);
+    if (n.else_n) u += slot_uses(*n.else_n, slot);
+    return u;
+}
+
+int cond_count(const Node& n) { return n.kind == Node::Kind::Cond ? 1 + cond_count(*n.then_n) + cond_count(*n.else_n) : 0; }
+
+void find_dev_selects(Plan& plan, const std::vector<KernelImpl>& impls, Node& n) {
+    if (n.kind == Node::Kind::Pipeline) return;  // process bodies keep the host walk
+    if (n.kind == Node::Kind::Sequential || n.kind == Node::Kind::Combine) {
+        for (size_t i = 0; i + 1 < n.children.size(); ++i) {
+            Node& ld = *n.children[i];
+            Node& cd = *n.children[i + 1];
+            if (ld.kind != Node::Kind::SlotLoad || cd.kind != Node::Kind::Cond || cd.dev_select) continue;
+            // the slot serves this tree alone: one load, and read by this tree's conds only
+            if (slot_uses(*plan.body, ld.slot) != 1 + cond_count(cd)) continue;
+            if (plan.schedule.dispatch_key && expr_mentions(plan.schedule.dispatch_key.get(), Expr::Op::TaskParam, true, 0))
+                continue;  // a key over task params could tell the leaves apart
+            auto ds = std::make_shared<DevSelect>();
+            int code = 0;
+            if (!build_select(cd, ld.slot, *ds, code) || ds->leaves.size() < 2) continue;
+            // the leaves' kernel must read its scalars from the device records (the generic tile program)
+            if (impls[ds->leaves[0]->kernel_index].kind != ImplKind::TileProgram) continue;
+            const DType sdt = plan.tensors[ld.slot_tensor.tensor].dtype;
+            if (sdt == DType::F16 || sdt == DType::BF16) continue;
+            ds->load = &ld;
+            cd.dev_select = ds;
+            ld.dev_deferred = true;
+        }
+    }
+    if (n.body) find_dev_selects(plan, impls, *n.body);
+    for (auto& c : n.children) find_dev_selects(plan, impls, *c);
+}
+
 bool data_dependent(const Node& n) {
     switch (n.kind) {
         case Node::Kind::Cond:
-        case Node::Kind::Select:
+            return !n.dev_select;
         case Node::Kind::SlotLoad:
+            return !n.dev_deferred;
+        case Node::Kind::Select:
         case Node::Kind::SlotSet:
             return true;
         case Node::Kind::ParallelFor:
@@ -690,6 +802,7 @@ std::unique_ptr<Program> compile_program(const char* text, size_t len, int devic
     }
     prog->tensor_key_depth.assign(plan.tensors.size(), -1);
     collect_depths(plan, *plan.body, prog->tensor_key_depth);
+    find_dev_selects(plan, prog->impls, *plan.body);
     prog->cacheable = !data_dependent(*plan.body);
     return prog;
 }

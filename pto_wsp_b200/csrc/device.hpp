@@ -93,6 +93,14 @@ struct TileProgram {
 // error; `workers` caps the number of CTAs (task window), 0 = automatic.
 // ---------------------------------------------------------------------------
 
+// Device-selected scalars: per task row [task, element offset, signed-compare mask, other operand per cond,
+// leaf scalars], the cond tree as 4 ints per cond [compare (0 <, 1 <=, 2 >, 3 >=, 4 ==, 5 !=), slot on the
+// left, then, else] (children >= 0: cond, < 0: ~leaf); the element is read as slot_load_u64 does (src_type: the
+// plan DType code).  Writes the chosen leaf's scalars into the task's record.
+cudaError_t launch_select_scalars(int64_t* rec, int stride, int scalar_pos, const uint64_t* rows, int64_t nrows,
+                                  int row_words, const int* tree, int nconds, int nscalars, const void* src,
+                                  int src_type, int64_t src_span, int* err, cudaStream_t s);
+
 // Tile widths the hand-written RMSNorm / softmax row kernels take (others run the fused row program).
 inline bool row_width_supported(int cols) { return cols == 128 || cols == 256 || cols == 512 || cols == 1024; }
 cudaError_t launch_rmsnorm_rows(const TaskBatch& b, int workers, cudaStream_t s);

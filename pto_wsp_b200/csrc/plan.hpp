@@ -67,6 +67,23 @@ struct ProcessDef {
     std::vector<int> produces, consumes;  // channel indices
 };
 
+struct Node;
+
+// A `P.when` tree over one slot that `slot_load_u64` fills from a tensor just before it, whose leaves are tasks of
+// one kernel on the same views that differ only in their scalar args (the reference indexer's tiers): the walk
+// places one task and the GPU picks the leaf's scalars from the tensor element itself (no host read of the data).
+struct DevSelect {
+    const Node* load = nullptr;             // the slot_load_u64 node
+    std::vector<const Node*> leaves;        // task leaves in tree order
+    // per cond of the tree (index order): comparison, which side the slot is on, the other operand, children
+    // (>= 0: cond index, < 0: ~leaf index)
+    std::vector<std::string> cmp;
+    std::vector<uint8_t> slot_left;
+    std::vector<const Expr*> other;
+    std::vector<const Expr*> slot_expr;
+    std::vector<int> then_c, else_c;
+};
+
 struct Node {
     enum class Kind : uint8_t { ParallelFor, ForEach, Task, Combine, Sequential, Cond, Select, SlotSet, SlotLoad,
                                 Pipeline, Send, Consume };
@@ -98,6 +115,9 @@ struct Node {
     // send (body = the task whose first axis arg is the token) / consume (var = the token's name, body)
     std::string channel_name;
     int channel = -1;
+    // device-selected scalars: on the root cond of such a tree; the slot_load feeding it is deferred
+    std::shared_ptr<DevSelect> dev_select;
+    bool dev_deferred = false;
 };
 using NodePtr = std::shared_ptr<Node>;
 

@@ -433,4 +433,77 @@ cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev,
     return cudaGetLastError();
 }
 
+namespace {
+
+// DType codes of the plan (plan.hpp): F16, BF16, F32, F64, I8, I16, I32, I64, U8, U16, U32, U64, Bool.
+__device__ __forceinline__ uint64_t slot_value(const char* p, int t) {
+    switch (t) {
+        case 2: return static_cast<uint64_t>(static_cast<int64_t>(*reinterpret_cast<const float*>(p)));
+        case 3: return static_cast<uint64_t>(static_cast<int64_t>(*reinterpret_cast<const double*>(p)));
+        case 4: return static_cast<uint64_t>(static_cast<int64_t>(*reinterpret_cast<const int8_t*>(p)));
+        case 5: return static_cast<uint64_t>(static_cast<int64_t>(*reinterpret_cast<const int16_t*>(p)));
+        case 6: return static_cast<uint64_t>(static_cast<int64_t>(*reinterpret_cast<const int32_t*>(p)));
+        case 7: case 11: return *reinterpret_cast<const uint64_t*>(p);
+        case 8: case 12: return *reinterpret_cast<const uint8_t*>(p);
+        case 9: return *reinterpret_cast<const uint16_t*>(p);
+        case 10: return *reinterpret_cast<const uint32_t*>(p);
+        default: return 0;
+    }
+}
+
+__global__ void select_scalars_kernel(int64_t* rec, int stride, int scalar_pos, const uint64_t* rows, int64_t nrows,
+                                      int row_words, const int* tree, int nconds, int nscalars, const char* src,
+                                      int src_type, int elem_bytes, int64_t src_span, int* err) {
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < nrows;
+         r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t* row = rows + r * row_words;
+        const int64_t t = static_cast<int64_t>(row[0]), off = static_cast<int64_t>(row[1]);
+        const uint64_t mask = row[2];
+        if (off < 0 || off >= src_span) {
+            atomicOr(err, kErrBounds);
+            continue;
+        }
+        const uint64_t v = slot_value(src + off * elem_bytes, src_type);
+        int code = 0;
+        for (int guard = 0; code >= 0 && guard < nconds; ++guard) {
+            const int* c = tree + 4 * code;
+            const uint64_t o = row[3 + code];
+            const uint64_t x = c[1] ? v : o, y = c[1] ? o : v;
+            const bool sg = (mask >> code) & 1ull;
+            const int64_t xs = static_cast<int64_t>(x), ys = static_cast<int64_t>(y);
+            bool res = false;
+            switch (c[0]) {
+                case 0: res = sg ? xs < ys : x < y; break;
+                case 1: res = sg ? xs <= ys : x <= y; break;
+                case 2: res = sg ? xs > ys : x > y; break;
+                case 3: res = sg ? xs >= ys : x >= y; break;
+                case 4: res = x == y; break;
+                default: res = x != y; break;
+            }
+            code = res ? c[2] : c[3];
+        }
+        if (code >= 0) {
+            atomicOr(err, kErrShape);
+            continue;
+        }
+        const uint64_t* leaf = row + 3 + nconds + static_cast<int64_t>(~code) * nscalars;
+        for (int j = 0; j < nscalars; ++j) rec[t * stride + scalar_pos + j] = static_cast<int64_t>(leaf[j]);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_select_scalars(int64_t* rec, int stride, int scalar_pos, const uint64_t* rows, int64_t nrows,
+                                  int row_words, const int* tree, int nconds, int nscalars, const void* src,
+                                  int src_type, int64_t src_span, int* err, cudaStream_t s) {
+    if (nrows <= 0) return cudaSuccess;
+    static const int bytes[13] = {2, 2, 4, 8, 1, 2, 4, 8, 1, 2, 4, 8, 1};
+    if (src_type < 2 || src_type > 12) return cudaErrorInvalidValue;  // f16 / bf16 slot sources are not read
+    const int blocks = static_cast<int>(std::min<int64_t>((nrows + 255) / 256, 1024));
+    select_scalars_kernel<<<blocks, 256, 0, s>>>(rec, stride, scalar_pos, rows, nrows, row_words, tree, nconds,
+                                                 nscalars, static_cast<const char*>(src), src_type, bytes[src_type],
+                                                 src_span, err);
+    return cudaGetLastError();
+}
+
 }  // namespace ptowsp::dev

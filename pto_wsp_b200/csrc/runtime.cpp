@@ -300,6 +300,10 @@ struct Walker {
                 }
                 const int64_t off = base + n.row * s3 + n.col * s4;
                 if (off < 0 || off >= tb.span) throw Error(PTOWSP_ERR_ARG, "slot_load_u64 reads outside its tensor");
+                if (n.dev_deferred) {  // the cond tree after it is decided on the GPU from this element
+                    deferred_off = off;
+                    return ready;
+                }
                 const DType dt = P.plan.tensors[ta.tensor].dtype;
                 const int eb = dtype_bytes(dt);
                 alignas(8) unsigned char buf[8] = {0};
@@ -376,6 +380,7 @@ struct Walker {
                 return done;
             }
             case Node::Kind::Cond: {
+                if (n.dev_select) return dev_select(*n.dev_select, ready);
                 Val c = eval(*n.pred, nullptr);
                 return node(c.v ? *n.then_n : *n.else_n, ready);
             }
@@ -415,6 +420,47 @@ struct Walker {
         return sched.issue(ki.cycles, wid, ready);
     }
 
+    // One task whose scalars the GPU picks (dev_select): the template leaf is placed once, reading the slot's
+    // tensor element as well; its batch gets a row [task, element, signed mask, operands, leaf scalars].
+    int64_t deferred_off = -1;
+    Batch* last_batch = nullptr;
+    uint64_t dev_select(const DevSelect& ds, uint64_t ready) {
+        if (deferred_off < 0) throw Error(PTOWSP_ERR_PLAN, "device-selected cond without its slot load");
+        const int nc = static_cast<int>(ds.cmp.size());
+        const Node& leaf = *ds.leaves[0];
+        const TensorArg& st = ds.load->slot_tensor;
+        extra_read_key = view_key(st);
+        const uint64_t done = task(leaf, ready);
+        extra_read_key = 0;
+        Batch& b = *last_batch;
+        const int nscal = static_cast<int>(leaf.scalar_args.size());
+        const int words = 3 + nc + static_cast<int>(ds.leaves.size()) * nscal;
+        if (b.sel && (b.sel != &ds || b.sel_row_words != words))
+            throw Error(PTOWSP_ERR_PLAN, "one task node under two device-selected conds");
+        b.sel = &ds;
+        b.sel_tensor = st.tensor;
+        b.sel_row_words = words;
+        uint64_t mask = 0;
+        std::vector<uint64_t> row;
+        row.reserve(words);
+        row.push_back(static_cast<uint64_t>(b.ntasks - 1));
+        row.push_back(static_cast<uint64_t>(deferred_off));
+        row.push_back(0);
+        for (int c = 0; c < nc; ++c) {
+            const Val o = eval(*ds.other[c], nullptr);
+            if (ds.slot_expr[c]->ty != Expr::Ty::U64 && o.ty != Expr::Ty::U64) mask |= 1ull << c;  // signed compare
+            row.push_back(o.v);
+        }
+        if (nc > 64) throw Error(PTOWSP_ERR_LIMIT, "device-selected cond tree deeper than 64");
+        row[2] = mask;
+        for (const Node* lf : ds.leaves)
+            for (const auto& a : lf->scalar_args) row.push_back(arg_value(a));
+        b.sel_rows.insert(b.sel_rows.end(), row.begin(), row.end());
+        deferred_off = -1;
+        return done;
+    }
+    uint64_t extra_read_key = 0;
+
     // Places one task in its dependency wave; returns its u64 args.
     std::vector<uint64_t> enqueue(const Node& n) {
         const KernelDef& kd = P.plan.kernels[n.kernel_index];
@@ -433,7 +479,7 @@ struct Walker {
         args.insert(args.end(), scal.begin(), scal.end());
 
         // dependency level
-        uint64_t rkeys[dev::kMaxParams], wkeys[dev::kMaxParams];
+        uint64_t rkeys[dev::kMaxParams + 1], wkeys[dev::kMaxParams];
         int nr = 0, nw = 0;
         size_t level = wave_floor;
         for (int ti = 0; ti < kd.num_tensor_params; ++ti) {
@@ -448,6 +494,10 @@ struct Walker {
                 rkeys[nr++] = key;
                 if (auto f = last_write.find(key); f != last_write.end()) level = std::max(level, f->second + 1);
             }
+        }
+        if (extra_read_key) {  // the tensor element a device-selected cond reads
+            rkeys[nr++] = extra_read_key;
+            if (auto f = last_write.find(extra_read_key); f != last_write.end()) level = std::max(level, f->second + 1);
         }
         for (int i = 0; i < nw; ++i) last_write[wkeys[i]] = level;
         for (int i = 0; i < nr; ++i) {
@@ -491,6 +541,7 @@ struct Walker {
         for (uint64_t s : scal) b.rec.push_back(static_cast<int64_t>(s));
         b.ntasks++;
         L.tasks++;
+        last_batch = &b;
         return args;
     }
 
@@ -740,6 +791,8 @@ Batch::~Batch() {
     if (ep_mm_rec_dev) cudaFree(ep_mm_rec_dev);
     if (ep_rec_dev) cudaFree(ep_rec_dev);
     if (ep_unit_rec_dev) cudaFree(ep_unit_rec_dev);
+    if (sel_dev) cudaFree(sel_dev);
+    if (sel_tree_dev) cudaFree(sel_tree_dev);
 }
 
 LaunchProgram::~LaunchProgram() {
@@ -841,6 +894,34 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
     const int workers = P.plan.schedule.window_tasks > 0 ? static_cast<int>(std::min<int64_t>(P.plan.schedule.window_tasks, 1 << 30)) : 0;
     cudaError_t e = cudaSuccess;
     ImplKind kind = ki.kind;
+    if (B.sel) {
+        // the scalars of every task come from the leaf its tensor element picks: write them into the records first
+        if (!B.sel_dev) {
+            const DevSelect& ds = *B.sel;
+            std::vector<int> tree;
+            static const char* cmps[] = {"<", "<=", ">", ">=", "==", "!="};
+            for (size_t c = 0; c < ds.cmp.size(); ++c) {
+                int code = 5;
+                for (int k = 0; k < 6; ++k)
+                    if (ds.cmp[c] == cmps[k]) code = k;
+                tree.insert(tree.end(), {code, ds.slot_left[c], ds.then_c[c], ds.else_c[c]});
+            }
+            PW_CUDA(cudaMalloc(&B.sel_dev, B.sel_rows.size() * sizeof(uint64_t)));
+            PW_CUDA(cudaMemcpy(B.sel_dev, B.sel_rows.data(), B.sel_rows.size() * sizeof(uint64_t), cudaMemcpyHostToDevice));
+            PW_CUDA(cudaMalloc(&B.sel_tree_dev, tree.size() * sizeof(int)));
+            PW_CUDA(cudaMemcpy(B.sel_tree_dev, tree.data(), tree.size() * sizeof(int), cudaMemcpyHostToDevice));
+        }
+        const TensorBinding& sb = T[B.sel_tensor];
+        const int nscal = static_cast<int>(B.sel->leaves[0]->scalar_args.size());
+        e = dev::launch_select_scalars(const_cast<int64_t*>(rec_dev) + B.dev_off, B.stride,
+                                       kd.num_tensor_params + static_cast<int>(node.axis_args.size()), B.sel_dev,
+                                       static_cast<int64_t>(B.sel_rows.size() / B.sel_row_words), B.sel_row_words,
+                                       B.sel_tree_dev, static_cast<int>(B.sel->cmp.size()), nscal, sb.dev,
+                                       static_cast<int>(P.plan.tensors[B.sel_tensor].dtype), sb.span, P.err_dev,
+                                       P.stream);
+        if (e != cudaSuccess) throw Error(PTOWSP_ERR_CUDA, std::string("device-selected scalars: ") + cudaGetErrorString(e));
+        launches++;
+    }
     if ((kind == ImplKind::RmsNorm || kind == ImplKind::Softmax)) {
         const int c = kd.params[0].v.cols;
         if (!rows_ok || !dev::row_width_supported(c)) kind = ImplKind::TileProgram;
@@ -1163,7 +1244,7 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
             ++nb;
             B = &b;
         }
-    if (nb != 1 || B->ntasks < 2) return false;
+    if (nb != 1 || B->ntasks < 2 || B->sel) return false;
     const KernelImpl& ki = P.impls[B->kernel];
     if (ki.kind != ImplKind::RmsNorm && ki.kind != ImplKind::Softmax && ki.kind != ImplKind::TileProgram) return false;
     const KernelDef& kd = P.plan.kernels[B->kernel];

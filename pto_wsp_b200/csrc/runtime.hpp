@@ -93,6 +93,14 @@ struct Batch {  // tasks of one kernel inside one wave
     int64_t* ep_unit_rec_dev = nullptr;  // matmul stage on CTA pairs: tasks 128 rows apart in A sharing B
     int64_t ep_nunits = 0;
     int8_t ep_ok = -1;
+    // device-selected scalars: every task takes the scalars of the leaf of `sel` that its tensor element picks;
+    // rows [task, element offset, signed-compare mask, other operand per cond, leaf scalars...]
+    const DevSelect* sel = nullptr;
+    uint32_t sel_tensor = 0;
+    std::vector<uint64_t> sel_rows;
+    int sel_row_words = 0;
+    uint64_t* sel_dev = nullptr;
+    int* sel_tree_dev = nullptr;
     // host-staged pipelining: per chunk and tensor param, the [lo, hi) element range its tasks touch
     int chunk_n = 0;
     std::vector<int64_t> chunk_ranges;
@@ -106,6 +114,10 @@ struct Batch {  // tasks of one kernel inside one wave
         ep_mm_rec_dev = o.ep_mm_rec_dev; ep_rec_dev = o.ep_rec_dev; ep_ok = o.ep_ok;
         ep_unit_rec_dev = o.ep_unit_rec_dev; ep_nunits = o.ep_nunits;
         o.ep_unit_rec_dev = nullptr;
+        sel = o.sel; sel_tensor = o.sel_tensor; sel_rows = std::move(o.sel_rows); sel_row_words = o.sel_row_words;
+        sel_dev = o.sel_dev; sel_tree_dev = o.sel_tree_dev;
+        o.sel_dev = nullptr;
+        o.sel_tree_dev = nullptr;
         o.fast_rec_dev = nullptr;
         o.unit_rec_dev = nullptr;
         o.ep_mm_rec_dev = nullptr;

@@ -157,3 +157,24 @@ def test_native_cycles_match_oracle_for_config_plans(name):
     ex = runtime.CudaExecutable(plan)
     ex.set_option("dry_run", 1)
     assert ex.run_with_symbols(arrays, axis, {}, {}) == want
+
+
+def test_tensor_driven_tiers_are_device_selected_and_cacheable():
+    """`P.when` tiers over a slot loaded from a tensor, with leaves that differ only in scalars: the walk no longer
+    reads the data (the plan is cacheable) and its makespan still equals the oracle's."""
+    import numpy as np
+    from _dev_select import tiered_scale_plan
+    from cpu_sim import CpuSim
+
+    from pto_wsp_b200.runtime import CudaExecutable
+
+    plan = tiered_scale_plan(3, 5)
+    ex = CudaExecutable(plan)
+    assert ex.describe()["cacheable"]
+    rng = np.random.default_rng(0)
+    sel = rng.integers(-20, 200, (3, 5, 1, 1)).astype(np.int32)
+    x = rng.standard_normal((3, 5, 8, 64)).astype(np.float32)
+    out = np.zeros_like(x)
+    want = CpuSim(plan).run([sel, x, out.copy()])
+    ex.set_option("dry_run", 1)
+    assert ex.run_with_symbols([sel, x, out], {}, {}, {}) == want
