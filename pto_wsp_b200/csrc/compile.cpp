@@ -721,15 +721,22 @@ void find_dev_selects(Plan& plan, const std::vector<KernelImpl>& impls, Node& n)
     for (auto& c : n.children) find_dev_selects(plan, impls, *c);
 }
 
+// Whether the walk depends on data that the replay key (logged symbols, axis sizes, ragged length sums, CSR
+// contents) does not cover: slots (set from tensors or by the caller) read by a cond.
 bool data_dependent(const Node& n) {
     switch (n.kind) {
         case Node::Kind::Cond:
-            return !n.dev_select;
+            if (n.dev_select) return false;
+            if (expr_mentions(n.pred.get(), Expr::Op::Slot, true, 0) ||
+                expr_mentions(n.pred.get(), Expr::Op::TaskParam, true, 0))
+                return true;
+            return data_dependent(*n.then_n) || data_dependent(*n.else_n);
         case Node::Kind::SlotLoad:
             return !n.dev_deferred;
-        case Node::Kind::Select:
         case Node::Kind::SlotSet:
             return true;
+        case Node::Kind::Select:
+            return data_dependent(*n.body);
         case Node::Kind::ParallelFor:
         case Node::Kind::ForEach:
         case Node::Kind::Send:

@@ -79,6 +79,22 @@ struct Val {
 
 int64_t as_i64(uint64_t v) { return static_cast<int64_t>(v); }
 
+// FNV-1a over a CSR selection's indptr[0..outer] and indices[0..indptr[outer]) (the arrays a Select walk reads).
+uint64_t csr_hash(const int32_t* indptr, const int32_t* indices, int64_t outer) {
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&](int32_t v) {
+        for (int k = 0; k < 4; ++k) {
+            h ^= static_cast<uint64_t>((static_cast<uint32_t>(v) >> (8 * k)) & 0xffu);
+            h *= 1099511628211ull;
+        }
+    };
+    if (!indptr || outer < 0) return h;
+    for (int64_t i = 0; i <= outer; ++i) mix(indptr[i]);
+    const int64_t nnz = indptr[outer];
+    for (int64_t p = 0; indices && p < nnz; ++p) mix(indices[p]);
+    return h;
+}
+
 dev::ParamType ptype(DType d) {
     switch (d) {
         case DType::F32: return dev::PT_F32;
@@ -353,7 +369,8 @@ struct Walker {
                                               : nullptr;
                     if (lens)
                         for (int64_t i = 0; i < outer; ++i) ub += lens[i];
-                    note("r" + std::to_string(n.axis.lengths_sym) + "=" + std::to_string(ub));
+                    note("r" + std::to_string(n.axis.lengths_sym) + ":" + std::to_string(n.axis.outer_sym) + "=" +
+                         std::to_string(ub));
                 }
                 uint64_t done = ready, cur = ready;
                 env.push_back({&n.var, 0});
@@ -370,6 +387,9 @@ struct Walker {
                 const int32_t* indptr = ctx->get_symbol_ptr ? static_cast<const int32_t*>(ctx->get_symbol_ptr(ctx->ctx, n.indptr_sym)) : nullptr;
                 const int32_t* indices = ctx->get_symbol_ptr ? static_cast<const int32_t*>(ctx->get_symbol_ptr(ctx->ctx, n.indices_sym)) : nullptr;
                 int64_t nnz = indptr ? indptr[outer] : 0;
+                // the walk depends on the CSR arrays themselves: key a cached task table on their contents
+                note("c" + std::to_string(n.indptr_sym) + ":" + std::to_string(n.indices_sym) + ":" +
+                     std::to_string(n.outer_sym) + "=" + std::to_string(csr_hash(indptr, indices, outer)));
                 uint64_t done = ready;
                 env.push_back({&n.var, 0});
                 for (int64_t p = 0; p < nnz; ++p) {
@@ -1603,9 +1623,28 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
             std::string name = q.substr(1, eq - 1);
             uint64_t want = std::stoull(q.substr(eq + 1));
             uint64_t got = 0;
-            if (kind == 's') got = ctx->get_symbol_u64 ? ctx->get_symbol_u64(ctx->ctx, std::stoull(name)) : 0;
-            else if (kind == 'a') got = static_cast<uint64_t>(ctx->get_axis_size ? ctx->get_axis_size(ctx->ctx, name.c_str()) : 0);
-            else replay = false;  // ragged lengths: walk again
+            auto sym_u64 = [&](uint64_t id) { return ctx->get_symbol_u64 ? ctx->get_symbol_u64(ctx->ctx, id) : 0; };
+            auto sym_ptr = [&](uint64_t id) {
+                return ctx->get_symbol_ptr ? static_cast<const int32_t*>(ctx->get_symbol_ptr(ctx->ctx, id)) : nullptr;
+            };
+            if (kind == 's') {
+                got = sym_u64(std::stoull(name));
+            } else if (kind == 'a') {
+                got = static_cast<uint64_t>(ctx->get_axis_size ? ctx->get_axis_size(ctx->ctx, name.c_str()) : 0);
+            } else if (kind == 'r') {  // ragged axis: the sum of its lengths
+                const size_t c = name.find(':');
+                const int32_t* lens = sym_ptr(std::stoull(name.substr(0, c)));
+                const int64_t outer = static_cast<int64_t>(sym_u64(std::stoull(name.substr(c + 1))));
+                int64_t ub = 0;
+                for (int64_t i = 0; lens && i < outer; ++i) ub += lens[i];
+                got = static_cast<uint64_t>(ub);
+            } else if (kind == 'c') {  // CSR selection: its arrays' contents
+                const size_t c1 = name.find(':'), c2 = name.find(':', c1 + 1);
+                got = csr_hash(sym_ptr(std::stoull(name.substr(0, c1))), sym_ptr(std::stoull(name.substr(c1 + 1, c2 - c1 - 1))),
+                               static_cast<int64_t>(sym_u64(std::stoull(name.substr(c2 + 1)))));
+            } else {
+                replay = false;
+            }
             if (got != want) replay = false;
         }
     }

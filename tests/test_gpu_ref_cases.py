@@ -82,3 +82,28 @@ def test_reference_case_with_device_resident_tensors(idx, require_cuda):
         # picks each task's leaf from EffSeq itself, so the host never reads it
         assert ex.timing()["slot_syncs"] == 0
         assert ex.describe()["cacheable"]
+
+
+@pytest.mark.parametrize("name", ["reftest:test_codegen_select_sparse.py#0", "reftest:test_codegen_ragged_axis.py#1"])
+def test_runtime_sized_plans_replay_and_follow_new_structure(name, require_cuda):
+    """Sparse selections and ragged axes are cached on their data (CSR contents, length sums): the same arrays
+    replay the task table, changed ones are walked again -- each run against the oracle on its own inputs."""
+    from cpu_sim import CpuSim
+
+    idx = next(i for i, c in enumerate(CASES) if c["name"] == name)
+    case = CASES[idx]
+    ex = CudaExecutable(case["plan"])
+    assert ex.describe()["cacheable"]
+    for variant in range(3):
+        roots, arrays, axis, syms, sptr = materialize(case, idx)
+        if variant == 2:  # a different structure: other selected rows / other lengths
+            for k, v in sptr.items():
+                if "select" in name and v.size == 3 and v[0] == 0 and v[-1] == 1:  # indices [0, 2, 1] -> [3, 1, 0]
+                    v[...] = np.array([3, 1, 0], dtype=v.dtype)
+                if "ragged" in name:
+                    v[...] = np.array([2, 1], dtype=v.dtype)[: v.size]
+        want = [a.copy() for a in arrays]
+        cyc = CpuSim(case["plan"]).run(want, axis, syms, sptr)
+        assert ex.run_with_symbols(arrays, axis, syms, sptr) == cyc
+        for got, w in zip(arrays, want):
+            np.testing.assert_array_equal(got, w)
