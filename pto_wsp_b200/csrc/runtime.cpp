@@ -1266,7 +1266,11 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
         }
     if (nb != 1 || B->ntasks < 2 || B->sel) return false;
     const KernelImpl& ki = P.impls[B->kernel];
-    if (ki.kind != ImplKind::RmsNorm && ki.kind != ImplKind::Softmax && ki.kind != ImplKind::TileProgram) return false;
+    // tcgen05 matmul batches once their layout check has run (an earlier launch): each chunk then runs the one-CTA
+    // tile kernel on its own records -- the copies, not the contraction, set the pace of a host-staged run
+    const bool mm = ki.kind == ImplKind::Matmul && B->fast_ok == 1;
+    if (ki.kind != ImplKind::RmsNorm && ki.kind != ImplKind::Softmax && ki.kind != ImplKind::TileProgram && !mm)
+        return false;
     const KernelDef& kd = P.plan.kernels[B->kernel];
     const Node& node = *B->node;
     const int np = kd.num_tensor_params;

@@ -80,3 +80,28 @@ def test_pipelined_interleaved_layout(require_cuda):
     assert np.array_equal(np.ascontiguousarray(y), y1)
     assert t["h2d_bytes"] == xs.nbytes
     assert t["d2h_bytes"] >= xs.nbytes
+
+
+def test_pipelined_bgemm(require_cuda):
+    # tcgen05 matmul batches pipeline from their second host-staged run (the first checks the layout); each chunk
+    # runs the one-CTA tile kernel on its own tasks, so results agree with the serial run's CTA-pair launch
+    rng = np.random.default_rng(6)
+    B, M, N, K = 8, 1024, 1024, 1024  # 16 + 16 MiB f16 in, 32 MiB f32 out
+    plan = workloads.bgemm_plan(B, M, N, K)
+    a = (rng.random((B, M, K), dtype=np.float32) * 2 - 1).astype(np.float16)
+    b = (rng.random((B, K, N), dtype=np.float32) * 2 - 1).astype(np.float16)
+    c1 = np.full((B, M, N), np.nan, np.float32)
+    ex1 = CudaExecutable(plan)
+    ex1.set_option("pipeline_chunks", 1)
+    cyc1 = ex1.run_with_symbols(list(workloads.bgemm_views(a, b, c1)), {}, {}, {})
+    ex = CudaExecutable(plan)
+    ex.set_option("pipeline_chunks", 16)
+    for i in range(2):
+        c = np.full((B, M, N), np.nan, np.float32)
+        assert ex.run_with_symbols(list(workloads.bgemm_views(a, b, c)), {}, {}, {}) == cyc1
+        t = ex.timing()
+        assert t["h2d_bytes"] == a.nbytes + b.nbytes and t["d2h_bytes"] == c.nbytes
+        assert (t["launches"] == 16) == (i == 1)  # pipelined once the layout check has run
+        np.testing.assert_allclose(c, c1, rtol=1e-5, atol=1e-5)
+    ref = a[0].astype(np.float64) @ b[0].astype(np.float64)
+    assert np.max(np.abs(c[0] - ref) / (np.abs(ref) + np.sqrt(np.mean(ref ** 2)))) < 2e-3
