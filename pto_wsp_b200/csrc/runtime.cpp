@@ -18,6 +18,7 @@
 #include <cuda_runtime_api.h>
 
 #include <algorithm>
+#include <climits>
 #include <chrono>
 #include <fstream>
 #include <functional>
@@ -1247,51 +1248,38 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
 }
 
 
-// Host-staged runs of a single-batch workload, overlapped: the batch is cut
-// into chunks of consecutive tasks; chunk c's input ranges are copied in on a
-// copy stream, its kernel waits for them on the compute stream, and its output
-// ranges go back on a second copy stream while later chunks compute.  Inputs
-// are copied once (ranges already staged by an earlier chunk are skipped).
-// Only for workloads whose written tensors are fully overwritten and never read
-// (so a chunk's output range can be copied back without staging it in).
-// Returns false (nothing done) when the workload does not qualify.
-bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, uint64_t& launches) {
-    if (!P.cacheable || P.opt_chunks < 2) return false;
-    Batch* B = nullptr;
-    int nb = 0;
-    for (auto& w : L.waves)
-        for (auto& b : w.batches) {
-            ++nb;
-            B = &b;
-        }
-    if (nb != 1 || B->ntasks < 2 || B->sel) return false;
-    const KernelImpl& ki = P.impls[B->kernel];
-    // tcgen05 matmul batches once their layout check has run (an earlier launch): each chunk then runs the one-CTA
-    // tile kernel on its own records -- the copies, not the contraction, set the pace of a host-staged run
-    const bool mm = ki.kind == ImplKind::Matmul && B->fast_ok == 1;
-    if (ki.kind != ImplKind::RmsNorm && ki.kind != ImplKind::Softmax && ki.kind != ImplKind::TileProgram && !mm)
-        return false;
+// Host-staged runs overlapped: a workload whose waves hold one batch each (a
+// chain of kernels, e.g. scoring then top-k) is cut into chunks of consecutive
+// tasks of every batch; chunk c's input ranges are copied in on a copy stream,
+// its kernels (one per wave, in wave order) wait for them on the compute stream,
+// and its output ranges go back on a second copy stream while later chunks
+// compute.  Inputs are copied once (ranges already staged by an earlier chunk
+// are skipped).  Only for chains whose written host tensors are fully
+// overwritten, each by one wave and read only by later waves, where chunk c of
+// a reader reads inside what chunk c of the writer wrote.
+bool pipelinable_kind(const KernelImpl& ki, const Batch& B) {
+    switch (ki.kind) {
+        case ImplKind::RmsNorm:
+        case ImplKind::Softmax:
+        case ImplKind::TileProgram:
+        case ImplKind::TopK: return true;
+        // hand-written kernels whose per-batch layout check ran on an earlier launch: each chunk then runs the
+        // plain form of the kernel on its own records (the one-CTA tile kernel for tcgen05 matmuls)
+        case ImplKind::Matmul:
+        case ImplKind::IndexerScore: return B.fast_ok == 1;
+        default: return false;
+    }
+}
+
+// Per chunk and tensor param, the [lo, hi) element range the chunk's tasks touch, and whether the tiles of a param
+// cover each chunk's range exactly once (dense tiles, sorted offsets adjacent).
+void chunk_ranges(Program& P, LaunchProgram& L, const std::vector<TensorBinding>& T, Batch* B, int C) {
+    if (B->chunk_n == C) return;
     const KernelDef& kd = P.plan.kernels[B->kernel];
     const Node& node = *B->node;
     const int np = kd.num_tensor_params;
-    std::vector<int> tens(np);
-    size_t host_bytes = 0;
-    for (int ti = 0; ti < np; ++ti) tens[ti] = static_cast<int>(node.tensor_args[node.param_to_arg[ti]].tensor);
-    for (int ti = 0; ti < np; ++ti) {
-        const TensorBinding& tb = T[tens[ti]];
-        if (tb.on_device) continue;
-        host_bytes += tb.bytes;
-        for (int tj = 0; tj < np; ++tj)  // a tensor both read and written by the batch: not pipelined
-            if (tens[tj] == tens[ti] && ((ki.param_write[ti] && ki.param_read[tj]) || (ki.param_read[ti] && ki.param_write[tj])))
-                return false;
-        if (ki.param_write[ti] && (L.full_write.empty() || !L.full_write[tens[ti]])) return false;
-    }
-    if (host_bytes < (size_t(64) << 20)) return false;  // small copies: not worth the extra streams
-    // chunks of at least 4 MiB of host traffic: smaller copies do not reach the copy engines' rate
-    const int64_t by_size = std::max<int64_t>(2, static_cast<int64_t>(host_bytes >> 22));
-    const int C = static_cast<int>(std::min<int64_t>(std::min<int64_t>(P.opt_chunks, B->ntasks), by_size));
-    // per-chunk element ranges of every param (from the host records of the first run)
-    std::vector<int64_t> ext(np);
+    std::vector<int64_t> ext(np, 1);
+    std::vector<uint8_t> dense(np, 0);
     for (const auto& kp : kd.params) {
         if (kp.tensor_index < 0) continue;
         const TensorArg& ta = node.tensor_args[node.param_to_arg[kp.tensor_index]];
@@ -1304,38 +1292,124 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
             s4 = tb.strides[ta.base_rank - 1];
         }
         ext[kp.tensor_index] = (kp.v.rows - 1) * s3 + (kp.v.cols - 1) * s4 + 1;
+        dense[kp.tensor_index] = s4 == 1 && (kp.v.rows == 1 || s3 == kp.v.cols);
     }
-    if (B->chunk_n != C) {
-        // the host records of a cached task table are dropped after its first run: read them back once
-        std::vector<int64_t> back;
-        const int64_t* rec = B->rec.data();
-        if (B->rec.empty()) {
-            back.resize(static_cast<size_t>(B->ntasks) * B->stride);
-            PW_CUDA(cudaMemcpyAsync(back.data(), L.rec_dev + B->dev_off, back.size() * sizeof(int64_t),
-                                    cudaMemcpyDeviceToHost, P.stream));
-            PW_CUDA(cudaStreamSynchronize(P.stream));
-            rec = back.data();
+    // the host records of a cached task table are dropped after its first run: read them back once
+    std::vector<int64_t> back;
+    const int64_t* rec = B->rec.data();
+    if (B->rec.empty()) {
+        back.resize(static_cast<size_t>(B->ntasks) * B->stride);
+        PW_CUDA(cudaMemcpyAsync(back.data(), L.rec_dev + B->dev_off, back.size() * sizeof(int64_t),
+                                cudaMemcpyDeviceToHost, P.stream));
+        PW_CUDA(cudaStreamSynchronize(P.stream));
+        rec = back.data();
+    }
+    B->chunk_ranges.assign(static_cast<size_t>(C) * np * 2, 0);
+    B->chunk_exact.assign(static_cast<size_t>(np), 1);
+    std::vector<int64_t> offs;
+    for (int c = 0; c < C; ++c) {
+        const int64_t t0 = B->ntasks * c / C, t1 = B->ntasks * (c + 1) / C;
+        for (int ti = 0; ti < np; ++ti) {
+            int64_t lo = INT64_MAX, hi = 0;
+            offs.clear();
+            for (int64_t t = t0; t < t1; ++t) {
+                const int64_t off = rec[t * B->stride + ti];
+                lo = std::min(lo, off);
+                hi = std::max(hi, off + ext[ti]);
+                offs.push_back(off);
+            }
+            B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2] = lo;
+            B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2 + 1] = hi;
+            bool exact = dense[ti] != 0;
+            if (exact) {
+                std::sort(offs.begin(), offs.end());
+                for (size_t i = 1; exact && i < offs.size(); ++i) exact = offs[i] == offs[i - 1] + ext[ti];
+                exact = exact && !offs.empty() && offs.front() == lo && offs.back() + ext[ti] == hi;
+            }
+            if (!exact) B->chunk_exact[ti] = 0;
         }
-        B->chunk_ranges.assign(static_cast<size_t>(C) * np * 2, 0);
-        for (int c = 0; c < C; ++c) {
-            const int64_t t0 = B->ntasks * c / C, t1 = B->ntasks * (c + 1) / C;
-            for (int ti = 0; ti < np; ++ti) {
-                int64_t lo = INT64_MAX, hi = 0;
-                for (int64_t t = t0; t < t1; ++t) {
-                    const int64_t off = rec[t * B->stride + ti];
-                    lo = std::min(lo, off);
-                    hi = std::max(hi, off + ext[ti]);
-                }
-                B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2] = lo;
-                B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2 + 1] = hi;
+    }
+    B->chunk_n = C;
+}
+
+bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, uint64_t& launches) {
+    if (!P.cacheable || P.opt_chunks < 2 || L.waves.empty() || L.waves.size() > 8) return false;
+    std::vector<Batch*> chain;  // one batch per wave
+    int64_t min_tasks = INT64_MAX;
+    for (auto& w : L.waves) {
+        if (w.batches.size() != 1) return false;
+        Batch* B = &w.batches[0];
+        if (B->ntasks < 2 || B->sel || !pipelinable_kind(P.impls[B->kernel], *B)) return false;
+        chain.push_back(B);
+        min_tasks = std::min(min_tasks, B->ntasks);
+    }
+    const int nw = static_cast<int>(chain.size());
+    // host tensors: the wave writing each (one at most, fully overwritten, read only by later waves)
+    struct Use {
+        int wave, param;
+    };
+    std::vector<int> producer(T.size(), -1), producer_param(T.size(), -1), first_read(T.size(), INT_MAX);
+    std::vector<std::vector<Use>> reads(T.size());
+    size_t host_bytes = 0;
+    std::vector<uint8_t> counted(T.size(), 0);
+    for (int w = 0; w < nw; ++w) {
+        const Batch* B = chain[w];
+        const KernelImpl& ki = P.impls[B->kernel];
+        const Node& node = *B->node;
+        const int np = P.plan.kernels[B->kernel].num_tensor_params;
+        for (int ti = 0; ti < np; ++ti) {
+            const uint32_t tid = node.tensor_args[node.param_to_arg[ti]].tensor;
+            if (T[tid].on_device) continue;
+            if (!counted[tid]) {
+                counted[tid] = 1;
+                host_bytes += T[tid].bytes;
+            }
+            if (ki.param_write[ti]) {
+                if (producer[tid] >= 0 || first_read[tid] < w) return false;  // a second writer, or a write after a read
+                if (L.full_write.empty() || !L.full_write[tid]) return false;
+                producer[tid] = w;
+                producer_param[tid] = ti;
             }
         }
-        B->chunk_n = C;
+        for (int ti = 0; ti < np; ++ti) {
+            const uint32_t tid = node.tensor_args[node.param_to_arg[ti]].tensor;
+            if (T[tid].on_device || !ki.param_read[ti]) continue;
+            if (producer[tid] == w) return false;  // read and written by the same batch
+            first_read[tid] = std::min(first_read[tid], w);
+            reads[tid].push_back({w, ti});
+        }
     }
-    auto range = [&](int c, int ti, int k) { return B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2 + k]; };
-    for (int ti = 0; ti < np; ++ti)  // ranges must stay inside the tensors
-        for (int c = 0; c < C; ++c)
-            if (range(c, ti, 0) < 0 || range(c, ti, 1) > T[tens[ti]].span) return false;
+    if (host_bytes < (size_t(64) << 20)) return false;  // small copies: not worth the extra streams
+    // chunks of at least 4 MiB of host traffic: smaller copies do not reach the copy engines' rate
+    const int64_t by_size = std::max<int64_t>(2, static_cast<int64_t>(host_bytes >> 22));
+    const int C = static_cast<int>(std::min<int64_t>(std::min<int64_t>(P.opt_chunks, min_tasks), by_size));
+    for (Batch* B : chain) chunk_ranges(P, L, T, B, C);
+    auto range = [&](const Batch* B, int c, int ti, int k) {
+        const int np = P.plan.kernels[B->kernel].num_tensor_params;
+        return B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2 + k];
+    };
+    for (const Batch* B : chain) {  // ranges must stay inside the tensors
+        const Node& node = *B->node;
+        const int np = P.plan.kernels[B->kernel].num_tensor_params;
+        for (int ti = 0; ti < np; ++ti)
+            for (int c = 0; c < C; ++c)
+                if (range(B, c, ti, 0) < 0 ||
+                    range(B, c, ti, 1) > T[node.tensor_args[node.param_to_arg[ti]].tensor].span)
+                    return false;
+    }
+    // a tensor passed between waves: chunk c of each reader reads inside what chunk c of the writer wrote, and the
+    // writer's chunks cover their ranges exactly (no element of a range left to a later chunk)
+    for (size_t tid = 0; tid < T.size(); ++tid) {
+        if (producer[tid] < 0 || reads[tid].empty()) continue;
+        const Batch* Wb = chain[producer[tid]];
+        const int wp = producer_param[tid];
+        if (!Wb->chunk_exact[wp]) return false;
+        for (const Use& u : reads[tid])
+            for (int c = 0; c < C; ++c)
+                if (range(chain[u.wave], c, u.param, 0) < range(Wb, c, wp, 0) ||
+                    range(chain[u.wave], c, u.param, 1) > range(Wb, c, wp, 1))
+                    return false;
+    }
 
     if (!P.h2d_stream) {
         PW_CUDA(cudaStreamCreateWithFlags(&P.h2d_stream, cudaStreamNonBlocking));
@@ -1354,52 +1428,69 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
     std::vector<int64_t> staged_lo(T.size(), 0), staged_hi(T.size(), -1);
     PW_CUDA(cudaEventRecord(P.ev0, P.stream));
     for (int c = 0; c < C; ++c) {
-        for (int ti = 0; ti < np; ++ti) {
-            TensorBinding& tb = T[tens[ti]];
-            if (tb.on_device || !ki.param_read[ti]) continue;
-            const size_t eb = tb.bytes / static_cast<size_t>(std::max<int64_t>(tb.span, 1));
-            int64_t& s_lo = staged_lo[tens[ti]];
-            int64_t& s_hi = staged_hi[tens[ti]];
-            const int64_t lo = range(c, ti, 0), hi = range(c, ti, 1);
-            auto copy_in = [&](int64_t a, int64_t b) {
-                if (b <= a) return;
-                PW_CUDA(cudaMemcpyAsync(tb.dev + a * eb, static_cast<char*>(tb.user_ptr) + a * eb, (b - a) * eb,
-                                        cudaMemcpyHostToDevice, P.h2d_stream));
-                P.timing.h2d_bytes += (b - a) * eb;
-            };
-            if (s_hi < 0) {
-                copy_in(lo, hi);
-                s_lo = lo;
-                s_hi = hi;
-            } else {
-                if (lo < s_lo) copy_in(lo, s_lo);  // gaps are filled so the staged part stays one interval
-                if (hi > s_hi) copy_in(s_hi, hi);
-                s_lo = std::min(s_lo, lo);
-                s_hi = std::max(s_hi, hi);
+        for (int w = 0; w < nw; ++w) {
+            const Batch* B = chain[w];
+            const KernelImpl& ki = P.impls[B->kernel];
+            const Node& node = *B->node;
+            const int np = P.plan.kernels[B->kernel].num_tensor_params;
+            for (int ti = 0; ti < np; ++ti) {
+                const uint32_t tid = node.tensor_args[node.param_to_arg[ti]].tensor;
+                TensorBinding& tb = T[tid];
+                if (tb.on_device || !ki.param_read[ti] || producer[tid] >= 0) continue;  // produced in the chain
+                const size_t eb = tb.bytes / static_cast<size_t>(std::max<int64_t>(tb.span, 1));
+                int64_t& s_lo = staged_lo[tid];
+                int64_t& s_hi = staged_hi[tid];
+                const int64_t lo = range(B, c, ti, 0), hi = range(B, c, ti, 1);
+                auto copy_in = [&](int64_t a, int64_t b) {
+                    if (b <= a) return;
+                    PW_CUDA(cudaMemcpyAsync(tb.dev + a * eb, static_cast<char*>(tb.user_ptr) + a * eb, (b - a) * eb,
+                                            cudaMemcpyHostToDevice, P.h2d_stream));
+                    P.timing.h2d_bytes += (b - a) * eb;
+                };
+                if (s_hi < 0) {
+                    copy_in(lo, hi);
+                    s_lo = lo;
+                    s_hi = hi;
+                } else {
+                    if (lo < s_lo) copy_in(lo, s_lo);  // gaps are filled so the staged part stays one interval
+                    if (hi > s_hi) copy_in(s_hi, hi);
+                    s_lo = std::min(s_lo, lo);
+                    s_hi = std::max(s_hi, hi);
+                }
             }
         }
         PW_CUDA(cudaEventRecord(P.pipe_events[2 * c], P.h2d_stream));
         PW_CUDA(cudaStreamWaitEvent(P.stream, P.pipe_events[2 * c], 0));
-        Batch part;
-        part.kernel = B->kernel;
-        part.node = B->node;
-        part.stride = B->stride;
-        part.aligned_rows = B->aligned_rows;
-        part.fast_ok = B->fast_ok;
-        const int64_t t0 = B->ntasks * c / C, t1 = B->ntasks * (c + 1) / C;
-        part.ntasks = t1 - t0;
-        part.dev_off = B->dev_off + static_cast<size_t>(t0) * B->stride;
-        launch_batch(P, part, node, T, L.rec_dev, launches);
+        for (int w = 0; w < nw; ++w) {
+            const Batch* B = chain[w];
+            Batch part;
+            part.kernel = B->kernel;
+            part.node = B->node;
+            part.stride = B->stride;
+            part.aligned_rows = B->aligned_rows;
+            part.fast_ok = B->fast_ok;
+            const int64_t t0 = B->ntasks * c / C, t1 = B->ntasks * (c + 1) / C;
+            part.ntasks = t1 - t0;
+            part.dev_off = B->dev_off + static_cast<size_t>(t0) * B->stride;
+            launch_batch(P, part, *B->node, T, L.rec_dev, launches);
+        }
         PW_CUDA(cudaEventRecord(P.pipe_events[2 * c + 1], P.stream));
         PW_CUDA(cudaStreamWaitEvent(P.d2h_stream, P.pipe_events[2 * c + 1], 0));
-        for (int ti = 0; ti < np; ++ti) {
-            TensorBinding& tb = T[tens[ti]];
-            if (tb.on_device || !ki.param_write[ti]) continue;
-            const int64_t lo = range(c, ti, 0), hi = range(c, ti, 1);
-            const size_t eb = tb.bytes / static_cast<size_t>(std::max<int64_t>(tb.span, 1));
-            PW_CUDA(cudaMemcpyAsync(static_cast<char*>(tb.user_ptr) + lo * eb, tb.dev + lo * eb, (hi - lo) * eb,
-                                    cudaMemcpyDeviceToHost, P.d2h_stream));
-            P.timing.d2h_bytes += (hi - lo) * eb;
+        for (int w = 0; w < nw; ++w) {
+            const Batch* B = chain[w];
+            const KernelImpl& ki = P.impls[B->kernel];
+            const Node& node = *B->node;
+            const int np = P.plan.kernels[B->kernel].num_tensor_params;
+            for (int ti = 0; ti < np; ++ti) {
+                const uint32_t tid = node.tensor_args[node.param_to_arg[ti]].tensor;
+                TensorBinding& tb = T[tid];
+                if (tb.on_device || !ki.param_write[ti]) continue;
+                const int64_t lo = range(B, c, ti, 0), hi = range(B, c, ti, 1);
+                const size_t eb = tb.bytes / static_cast<size_t>(std::max<int64_t>(tb.span, 1));
+                PW_CUDA(cudaMemcpyAsync(static_cast<char*>(tb.user_ptr) + lo * eb, tb.dev + lo * eb, (hi - lo) * eb,
+                                        cudaMemcpyDeviceToHost, P.d2h_stream));
+                P.timing.d2h_bytes += (hi - lo) * eb;
+            }
         }
     }
     PW_CUDA(cudaEventRecord(P.ev1, P.stream));
@@ -1704,6 +1795,27 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         L->full_write.assign(T.size(), 0);
         for (size_t tid = 0; tid < T.size(); ++tid)
             L->full_write[tid] = W->fully_written(tid) ? 1 : 0;
+        // a tensor that the waves overwrite entirely before any task reads it (an intermediate, like the
+        // indexer's scores) need not be staged in either
+        std::vector<size_t> last_w(T.size(), 0), first_r(T.size(), SIZE_MAX);
+        std::vector<uint8_t> any_w(T.size(), 0);
+        for (size_t wi = 0; wi < L->waves.size(); ++wi)
+            for (const auto& b : L->waves[wi].batches) {
+                const KernelImpl& ki = P.impls[b.kernel];
+                const Node& n = *b.node;
+                for (int ti = 0; ti < plan.kernels[b.kernel].num_tensor_params; ++ti) {
+                    const uint32_t tid = n.tensor_args[n.param_to_arg[ti]].tensor;
+                    if (ki.param_write[ti]) {
+                        any_w[tid] = 1;
+                        last_w[tid] = std::max(last_w[tid], wi);
+                    }
+                    if (ki.param_read[ti]) first_r[tid] = std::min(first_r[tid], wi);
+                }
+                if (b.sel) first_r[b.sel_tensor] = std::min(first_r[b.sel_tensor], wi);
+            }
+        L->write_first.assign(T.size(), 0);
+        for (size_t tid = 0; tid < T.size(); ++tid)
+            L->write_first[tid] = L->full_write[tid] && any_w[tid] && last_w[tid] < first_r[tid] ? 1 : 0;
     }
 
     if (dry) {
@@ -1719,7 +1831,8 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         }
         for (size_t tid = 0; tid < T.size(); ++tid) {
             const TensorBinding& b = T[tid];
-            const bool skip = !b.read && !L->full_write.empty() && L->full_write[tid];
+            const bool skip = !L->full_write.empty() && L->full_write[tid] &&
+                              (!b.read || (!L->write_first.empty() && L->write_first[tid]));
             if ((b.read || b.written) && !skip) P.timing.h2d_bytes += b.bytes;
             if (b.written) P.timing.d2h_bytes += b.bytes;
         }
@@ -1767,9 +1880,10 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         TensorBinding& b = T[tid];
         if (b.on_device || b.bytes == 0) continue;
         // Host tensors a task touches are staged in -- outputs too, unless the
-        // task loop provably overwrites every element without reading it, so
-        // that elements no task writes come back unchanged.
-        const bool skip = L && !b.read && !L->full_write.empty() && L->full_write[tid];
+        // task loop provably overwrites every element, in waves before any
+        // task reads it, so that elements no task writes come back unchanged.
+        const bool skip = L && !L->full_write.empty() && L->full_write[tid] &&
+                          (!b.read || (!L->write_first.empty() && L->write_first[tid]));
         if ((b.read || b.written) && !skip) {
             PW_CUDA(cudaMemcpyAsync(b.dev, b.user_ptr, b.bytes, cudaMemcpyHostToDevice, P.stream));
             P.timing.h2d_bytes += b.bytes;

@@ -104,12 +104,14 @@ struct Batch {  // tasks of one kernel inside one wave
     // host-staged pipelining: per chunk and tensor param, the [lo, hi) element range its tasks touch
     int chunk_n = 0;
     std::vector<int64_t> chunk_ranges;
+    std::vector<uint8_t> chunk_exact;  // per param: every chunk's tiles cover its range exactly once
     Batch() = default;
     Batch(Batch&& o) noexcept { *this = std::move(o); }
     Batch& operator=(Batch&& o) noexcept {
         kernel = o.kernel; node = o.node; rec = std::move(o.rec); ntasks = o.ntasks; stride = o.stride;
         dev_off = o.dev_off; aligned_rows = o.aligned_rows; fast_ok = o.fast_ok; fast_rec_dev = o.fast_rec_dev;
         fast_ntasks = o.fast_ntasks; fast_n = o.fast_n; chunk_n = o.chunk_n; chunk_ranges = std::move(o.chunk_ranges);
+        chunk_exact = std::move(o.chunk_exact);
         unit_rec_dev = o.unit_rec_dev; nunits = o.nunits; units_ok = o.units_ok;
         ep_mm_rec_dev = o.ep_mm_rec_dev; ep_rec_dev = o.ep_rec_dev; ep_ok = o.ep_ok;
         ep_unit_rec_dev = o.ep_unit_rec_dev; ep_nunits = o.ep_nunits;
@@ -142,7 +144,8 @@ struct LaunchProgram {  // result of one walk, reusable for static workloads
     int64_t* rec_dev = nullptr;
     size_t rec_cap = 0;
     std::vector<std::string> key;  // replay log of runtime queries
-    std::vector<uint8_t> full_write;  // per tensor: every element overwritten, never read
+    std::vector<uint8_t> full_write;  // per tensor: every element overwritten
+    std::vector<uint8_t> write_first; // per tensor: every element overwritten in waves before any task reads it
     LaunchProgram() = default;
     LaunchProgram(const LaunchProgram&) = delete;
     LaunchProgram& operator=(const LaunchProgram&) = delete;

@@ -111,6 +111,29 @@ def test_dry_run_waves_and_staging():
     assert c > 0
 
 
+def test_dry_run_intermediate_written_before_read_is_not_staged_in():
+    import numpy as np
+
+    # the indexer's scores: written in full by the scoring wave, read only by the top-k wave after it
+    plan, arrays = workloads.indexer_inputs(np.random.default_rng(0), 2, 4096, 256)
+    ex = runtime.CudaExecutable(plan)
+    ex.set_option("dry_run", 1)
+    ex.run_with_symbols(arrays, {}, {}, {})
+    t = ex.timing()
+    assert t["waves"] == 2
+    assert t["h2d_bytes"] == sum(a.nbytes for a in arrays[:3])  # q, k, w
+    assert t["d2h_bytes"] == arrays[3].nbytes + arrays[4].nbytes  # scores and indices come back
+    # accumulate form: C is read by the task that writes it, so it is staged in
+    plan = workloads.bgemm_plan(1, 256, 256, 128, accumulate=True)
+    ex = runtime.CudaExecutable(plan)
+    ex.set_option("dry_run", 1)
+    a = np.zeros((1, 256, 128), np.float16)
+    b = np.zeros((1, 128, 256), np.float16)
+    c = np.zeros((1, 256, 256), np.float32)
+    ex.run_with_symbols(list(workloads.bgemm_views(a, b, c)), {}, {}, {})
+    assert ex.timing()["h2d_bytes"] == a.nbytes + b.nbytes + c.nbytes
+
+
 def test_dry_run_inout_chain_waves():
     import numpy as np
 

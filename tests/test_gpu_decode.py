@@ -59,6 +59,25 @@ def test_decode_dense_dyn_axis_runs_fewer_requests(require_cuda):
     assert not got[5][3:].any()
 
 
+def test_decode_dense_dyn_axis_of_size_zero(require_cuda):
+    # no request at all: no task, no launch, the output comes back as it went in (the oracle's 0 cycles)
+    rng = np.random.default_rng(2)
+    plan, arrays = workloads.decode_inputs(rng, 3, lengths=[10, 20, 30])
+    got = [a.copy() for a in arrays]
+    got[5][...] = np.float16(1.5)
+    ex = CudaExecutable(plan)
+    assert ex.run_with_symbols(got, {"b": 0}, {}, {}) == CpuSim(plan).run([a.copy() for a in arrays],
+                                                                          axis_sizes={"b": 0}) == 0
+    assert ex.timing()["launches"] == 0 and ex.timing()["tasks"] == 0
+    assert np.all(got[5] == np.float16(1.5))
+    ex.run_with_symbols(got, {"b": 2}, {}, {})  # the same executable then runs a non-empty share
+    ref = [a.copy() for a in arrays]
+    ref[5][...] = np.float16(1.5)
+    CpuSim(plan).run(ref, axis_sizes={"b": 2})
+    check(got[5][:2], ref[5][:2])
+    assert np.all(got[5][2] == np.float16(1.5))
+
+
 def test_decode_config4_full_size(require_cuda):
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(4)

@@ -105,3 +105,27 @@ def test_pipelined_bgemm(require_cuda):
         np.testing.assert_allclose(c, c1, rtol=1e-5, atol=1e-5)
     ref = a[0].astype(np.float64) @ b[0].astype(np.float64)
     assert np.max(np.abs(c[0] - ref) / (np.abs(ref) + np.sqrt(np.mean(ref ** 2)))) < 2e-3
+
+
+def test_pipelined_indexer_chain(require_cuda):
+    # two waves (scoring, then top-k over the scores) run chunk by chunk: chunk c's top-k reads the scores chunk c
+    # just wrote; the scores are never staged in (written before they are read) and both outputs come back
+    rng = np.random.default_rng(7)
+    plan, arrays = workloads.indexer_inputs(rng, 8, 32768, 2048)  # 64 MiB of keys
+    serial = [a.copy() for a in arrays]
+    ex1 = CudaExecutable(plan)
+    ex1.set_option("pipeline_chunks", 1)
+    cyc1 = ex1.run_with_symbols(serial, {}, {}, {})
+    ex = CudaExecutable(plan)
+    ex.set_option("pipeline_chunks", 16)
+    for i in range(2):
+        got = [a.copy() for a in arrays]
+        got[3][...] = np.nan
+        got[4][...] = -1
+        assert ex.run_with_symbols(got, {}, {}, {}) == cyc1
+        t = ex.timing()
+        assert t["h2d_bytes"] == sum(a.nbytes for a in arrays[:3])
+        assert t["d2h_bytes"] == arrays[3].nbytes + arrays[4].nbytes
+        assert (t["launches"] == 16) == (i == 1)  # 8 chunks x (scoring, top-k) once the layout check has run
+        np.testing.assert_allclose(got[3], serial[3], rtol=1e-6, atol=1e-6)
+        assert np.array_equal(got[4], serial[4])
