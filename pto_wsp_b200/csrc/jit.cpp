@@ -25,6 +25,8 @@
 #include <cstring>
 #include <mutex>
 #include <sstream>
+#include <string>
+#include <unordered_map>
 #include <vector>
 
 namespace ptowsp::jit {
@@ -611,7 +613,24 @@ std::string gen_row_kernel(const TileProgram& tp_in, const int* param_types, con
     return o.str();
 }
 
+namespace {
+// Process-wide caches: a generated source is compiled once, and a cubin is loaded once per device, however many
+// programs use it (programs built from the same plan generate the same sources).
+std::mutex g_cache_mu;
+std::unordered_map<std::string, std::string> g_cubins;  // name + '\0' + source -> cubin
+std::unordered_map<std::string, CUmodule> g_modules;    // device + ':' + cubin -> module (lives until exit)
+}  // namespace
+
 bool compile_cubin(const std::string& src, const std::string& name, std::string* cubin, std::string* log) {
+    const std::string key = name + '\0' + src;
+    {
+        std::lock_guard<std::mutex> g(g_cache_mu);
+        auto it = g_cubins.find(key);
+        if (it != g_cubins.end()) {
+            *cubin = it->second;
+            return true;
+        }
+    }
     const Nvrtc& n = nvrtc();
     if (!n.ok) {
         *log = "NVRTC not found";
@@ -641,6 +660,10 @@ bool compile_cubin(const std::string& src, const std::string& name, std::string*
     }
     n.destroy(&prog);
     if (!ok && log->empty()) *log = "NVRTC compilation failed";
+    if (ok) {
+        std::lock_guard<std::mutex> g(g_cache_mu);
+        g_cubins.emplace(key, *cubin);
+    }
     return ok;
 }
 
@@ -650,10 +673,25 @@ bool load_cubin(const std::string& cubin, const std::string& name, void** fn, st
         *log = "driver entry points unavailable";
         return false;
     }
-    CUmodule mod = nullptr;  // kept for the life of the process: the program's kernels may run until exit
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        *log = "no current device";
+        return false;
+    }
     CUfunction f = nullptr;
-    if (d.load(&mod, cubin.data()) != CUDA_SUCCESS || d.get(&f, mod, name.c_str()) != CUDA_SUCCESS) {
-        *log = "module load failed";
+    std::lock_guard<std::mutex> g(g_cache_mu);
+    const std::string key = std::to_string(dev) + ':' + cubin;
+    auto it = g_modules.find(key);
+    if (it == g_modules.end()) {
+        CUmodule mod = nullptr;  // kept for the life of the process: kernels of any program may run until exit
+        if (d.load(&mod, cubin.data()) != CUDA_SUCCESS) {
+            *log = "module load failed";
+            return false;
+        }
+        it = g_modules.emplace(key, mod).first;
+    }
+    if (d.get(&f, it->second, name.c_str()) != CUDA_SUCCESS) {
+        *log = "kernel '" + name + "' not in the module";
         return false;
     }
     *fn = reinterpret_cast<void*>(f);
