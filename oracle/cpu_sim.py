@@ -228,6 +228,29 @@ def _root(a: np.ndarray) -> np.ndarray:
     return r
 
 
+def fma_f32(a: np.ndarray, b: np.ndarray, c: np.ndarray) -> np.ndarray:
+    """round_f32(a * b + c) with a single rounding (IEEE fusedMultiplyAdd on binary32, round to nearest even).
+
+    The f32 x f32 product is exact in f64; the f64 sum s = RN53(x) of the exact x = a*b + c is turned into
+    round-to-odd (truncate toward zero, set the last bit when inexact) from its TwoSum error, and rounding a
+    round-to-odd value with at least two extra bits to nearest gives RN24(x) exactly (Boldo & Melquiond,
+    "Emulation of FMA and correctly rounded sums: proved algorithms using rounding to odd", IEEE TC 2008).
+    """
+    a64 = np.asarray(a, dtype=np.float32).astype(np.float64)
+    b64 = np.asarray(b, dtype=np.float32).astype(np.float64)
+    c64 = np.asarray(c, dtype=np.float32).astype(np.float64)
+    p = a64 * b64
+    with np.errstate(invalid="ignore", over="ignore"):
+        s = p + c64
+        bv = s - c64
+        err = (c64 - (s - bv)) + (p - bv)  # x - s exactly (TwoSum)
+        inexact = np.isfinite(s) & (err != 0)
+        t = np.where(inexact & ((err < 0) != (s < 0)), np.nextafter(s, 0.0), s)  # toward zero
+        ti = t.view(np.int64)
+        t = np.where(inexact, ti | 1, ti).view(np.float64)
+        return t.astype(np.float32)
+
+
 def _elem_strides(a: np.ndarray) -> list[int]:
     return [s // a.itemsize for s in a.strides]
 
@@ -237,7 +260,15 @@ class TensorRef:
 
     def __init__(self, arr: np.ndarray):
         self.arr = arr
-        self.root = _root(arr)
+        root = _root(arr)
+        if not root.flags.c_contiguous:
+            # a dense buffer in another axis order (e.g. ``transpose(...).astype(...)``, which keeps the permuted
+            # layout): address it as the flat run of its memory
+            flat = root.ravel(order="K")
+            if not np.may_share_memory(flat, root):  # ravel copies when the memory is not one run
+                raise ValueError("tensor memory is not one dense buffer")
+            root = flat
+        self.root = root
         self.itemsize = arr.itemsize
         self.dtype = arr.dtype
         self.base_off = arr.__array_interface__["data"][0] - self.root.__array_interface__["data"][0]
@@ -447,11 +478,14 @@ class _KernelRun:
             if ex:
                 a = self.load_param(a_id) if ap else self.tiles[a_id]
                 b = self.load_param(b_id) if bp else self.tiles[b_id]
+                # sequential-k f32 accumulation, one fused multiply-add per step (separately rounded products
+                # would fail the reference's llama example check on one element where res1 + mlp cancels:
+                # error 1.3e-6 against its 1.04e-6 bound; f16 inputs give exact products either way)
                 acc = np.zeros((m, n), dtype=np.float32)
                 a32 = np.asarray(a, dtype=np.float32)
                 b32 = np.asarray(b, dtype=np.float32)
-                for kk_i in range(kk):  # sequential-k f32 accumulation
-                    acc += np.outer(a32[:, kk_i], b32[kk_i, :]).astype(np.float32)
+                for kk_i in range(kk):
+                    acc = fma_f32(a32[:, kk_i, None], b32[None, kk_i, :], acc)
                 self.tiles[rid] = acc
             else:
                 self.tiles[rid] = None

@@ -341,14 +341,14 @@ __global__ void __launch_bounds__(256) tile_program_kernel(TaskBatch b, const Ti
                     break;
                 }
                 case TP_MATMUL: {
-                    // f32 accumulation in k order with separate multiply and add roundings.
+                    // f32 accumulation in k order, one fused multiply-add (single rounding) per step.
                     const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], bb = prog->slots[in.b];
                     for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
                         const int r = e / in.cols, c = e - r * in.cols;
                         float acc = 0.f;
                         for (int kk = 0; kk < in.k; ++kk)
-                            acc = __fadd_rn(acc, __fmul_rn(__uint_as_float(sm[a.off + r * a.pitch + kk]),
-                                                           __uint_as_float(sm[bb.off + kk * bb.pitch + c])));
+                            acc = __fmaf_rn(__uint_as_float(sm[a.off + r * a.pitch + kk]),
+                                            __uint_as_float(sm[bb.off + kk * bb.pitch + c]), acc);
                         sm[d.off + r * d.pitch + c] = __float_as_uint(acc);
                     }
                     break;

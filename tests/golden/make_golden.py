@@ -51,14 +51,19 @@ def _root(a: np.ndarray) -> np.ndarray:
 
 
 def _layout(arrays: list[np.ndarray], prefix: str) -> tuple[list[dict], list[np.ndarray]]:
-    roots: list[np.ndarray] = []
-    descs = []
+    owners: list[np.ndarray] = []  # the arrays owning the memory (identity: views of one buffer share it)
+    roots: list[np.ndarray] = []   # the same memory as saved: C-contiguous, or a dense buffer in another axis
+    descs = []                     # order (``transpose(...).astype(...)``) flattened in memory order
     for a in arrays:
         r = _root(a)
-        ri = next((i for i, x in enumerate(roots) if x is r), None)
+        ri = next((i for i, x in enumerate(owners) if x is r), None)
         if ri is None:
-            roots.append(r)
+            owners.append(r)
+            flat = r if r.flags.c_contiguous else r.ravel(order="K")
+            assert np.may_share_memory(flat, r), "tensor memory is not one dense buffer"
+            roots.append(flat)
             ri = len(roots) - 1
+        r = roots[ri]
         off = a.__array_interface__["data"][0] - r.__array_interface__["data"][0]
         descs.append({"root": ri, "dtype": a.dtype.str, "shape": list(a.shape), "strides": list(a.strides),
                       "offset": int(off)})
@@ -111,6 +116,11 @@ def _redirect_cpu_sim():
 
 
 EXAMPLES = [
+    ("attention", (1e-2, 1e-2)),
+    ("llama", (1e-5, 1e-6)),
+    ("deepseek_v3", (1e-5, 1e-6)),
+    ("validated_matmul", (1e-5, 1e-6)),
+    ("tensor_data", (1e-5, 1e-6)),
     ("e2e_rmsnorm", (1e-5, 1e-6)),
     ("softmax", (1e-2, 1e-2)),
     ("bgemm", (1e-2, 1e-2)),

@@ -14,7 +14,7 @@
 
 import numpy as np
 import pytest
-from cpu_sim import CpuSim, Scheduler, stable_topk
+from cpu_sim import CpuSim, Scheduler, fma_f32, stable_topk
 
 from golden_cases import case_index, expected_roots, load_cases, materialize
 
@@ -26,6 +26,13 @@ EXPECTED_EXAMPLE_CYCLES = {
     "example:bgemm#0": 275968,
     "example:flashinfer_decode#0": 4514,
     "example:deepseek_lightning_indexer#0": 800,
+    "example:attention#0": 1680,  # examples/attention/attention_example.py:34
+    "example:llama#0": 4752,  # examples/llama/llama_example.py:35
+    "example:deepseek_v3#0": 1408,  # examples/deepseek_v3/deepseek_v3_example.py:35
+    "example:validated_matmul#0": 4864,  # examples/validated_matmul/validated_matmul_example.py:33
+    "example:tensor_data#0": 8192,  # examples/tensor_data/tensor_data_example.py:37
+    "example:tensor_data#1": 6144,  # examples/tensor_data/tensor_data_example.py:45
+    "example:csp_pipeline#0": 114688,  # examples/csp_pipeline/csp_pipeline_example.py:32
 }
 
 
@@ -68,3 +75,26 @@ def test_stable_topk_tie_rule():
     x = rng.integers(-4, 4, size=1000).astype(np.float32)
     order = np.lexsort((np.arange(x.size), -x.astype(np.float64)))
     assert stable_topk(x, 100).tolist() == order[:100].tolist()
+
+
+def test_fma_f32_rounds_once():
+    # f32 TMATMUL steps are fused multiply-adds: compare with exact rational arithmetic rounded to nearest even
+    from fractions import Fraction
+
+    def exact(a, b, c):
+        x = Fraction(float(a)) * Fraction(float(b)) + Fraction(float(c))
+        f = np.float32(float(x))
+        cands = [f, np.nextafter(f, np.float32(np.inf)), np.nextafter(f, np.float32(-np.inf))]
+        return min(cands, key=lambda y: (abs(Fraction(float(y)) - x), int(np.array(y).view(np.int32)) & 1))
+
+    rng = np.random.default_rng(1)
+    n = 3000
+    a = rng.standard_normal(n).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    c = (rng.standard_normal(n) * np.exp2(rng.integers(-30, 30, n))).astype(np.float32)
+    c[:1000] = -(a[:1000] * b[:1000])  # results that are the product's rounding error
+    got = fma_f32(a, b, c)
+    assert all(got[i] == exact(a[i], b[i], c[i]) for i in range(n))
+    # double rounding through f64 would land on the midpoint 1 + 2^-23 + 2^-24 and round to even (1 + 2^-22)
+    a1, b1, c1 = np.float32(2**-12 * (1 + 2**-23)), np.float32(2**-12 * (1 - 2**-23)), np.float32(1 + 2**-23)
+    assert fma_f32(np.array([a1]), np.array([b1]), np.array([c1]))[0] == c1
