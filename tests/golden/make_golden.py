@@ -13,7 +13,9 @@ the oracle's output buffers and its cycle count.
 
     python tests/golden/make_golden.py      # writes tests/golden/ref_cases.{json,npz}
 
-Kernels with CPU C++ bodies (``cpp_src``) are skipped: the CUDA target rejects them.
+Kernels with CPU C++ bodies (``cpp_src``) are skipped: the CUDA target rejects them.  That includes
+``@ptoisa_kernel`` kernels (``tests/test_ptoisa_kernel_jit.py``), whose traced PTO-ISA calls reach the plan
+only as generated C++ source.
 """
 
 from __future__ import annotations
@@ -130,6 +132,7 @@ EXAMPLES = [
 ]
 
 REF_TESTS = [
+    ("test_e2e.py", (0.0, 0.0)),
     ("test_codegen_execute_basic.py", (0.0, 0.0)),
     ("test_codegen_dynamic_axes.py", (0.0, 0.0)),
     ("test_codegen_schedule_dispatch_window.py", (0.0, 0.0)),
