@@ -24,6 +24,7 @@ const char* impl_name(ImplKind k) {
         case ImplKind::PagedDecode: return "paged_decode_gqa";
         case ImplKind::IndexerScore: return "lightning_indexer_score";
         case ImplKind::TopK: return "topk_select";
+        case ImplKind::Staged: return "staged_matmul+row_programs";
     }
     return "?";
 }
@@ -798,6 +799,28 @@ std::unique_ptr<Program> compile_program(const char* text, size_t len, int devic
         else if (int f = matmul_form(kd)) ki.kind = f == 1 ? ImplKind::Matmul : ImplKind::MatmulAcc;
         else ki.kind = ImplKind::TileProgram;
         if (ki.kind == ImplKind::TileProgram && split_matmul_epilogue(ki, kd, static_cast<int>(i))) continue;
+        if (ki.kind == ImplKind::TileProgram && split_stages(ki, kd)) {
+            // stages (matmuls + fused row programs over HBM scratch) when the tiles exceed shared memory or a
+            // contraction is large enough to want its own kernel; small kernels keep the one-launch tile program
+            bool staged = !ki.tp_ok;
+            for (const auto& st : ki.stages)
+                if (st.mm && int64_t(st.m) * st.n * st.k >= int64_t(128) * 128 * 64) staged = true;
+            for (size_t si = 0; staged && si < ki.stages.size(); ++si) {
+                Stage& st = ki.stages[si];
+                if (st.mm) continue;
+                std::string note;
+                const std::string name = "ptowsp_st_k" + std::to_string(i) + "_" + std::to_string(si);
+                if (build_stage_program(st.tp, kd, name, &st.cubin, &note)) st.jit_state = 2;
+                else staged = false;
+            }
+            if (staged) {
+                ki.kind = ImplKind::Staged;
+                ki.jit_note = "cut at its contractions: matmul kernels and fused row programs over HBM scratch";
+                continue;
+            }
+            ki.stages.clear();
+            ki.scratch_tiles.clear();
+        }
         if (ki.kind == ImplKind::TileProgram && !ki.tp_ok)
             throw Error(PTOWSP_ERR_UNSUPPORTED, "kernel '" + kd.name + "': " + ki.tp_error);
         // a generic kernel gets its fused row kernel built now (NVRTC, no GPU needed), and so does a fast row op
@@ -827,7 +850,19 @@ std::string describe_program(const Program& p) {
         const char* row = ki.jit_state == 1 ? "loaded" : ki.jit_state == 2 ? "compiled" : ki.jit_state == 0 ? "not built" : "interpreter";
         o << "{\"name\":\"" << p.plan.kernels[i].name << "\",\"impl\":\"" << impl_name(ki.kind)
           << "\",\"cycles\":" << ki.cycles << ",\"tile_program_smem\":" << ki.tp_smem << ",\"row_kernel\":\"" << row
-          << "\",\"row_kernel_note\":\"" << note << "\"}";
+          << "\",\"row_kernel_note\":\"" << note << "\"";
+        if (ki.kind == ImplKind::Staged) {  // e.g. ["matmul 128x256x128 tcgen05", "rows 128", "matmul ... cuda_cores"]
+            o << ",\"stages\":[";
+            for (size_t si = 0; si < ki.stages.size(); ++si) {
+                const Stage& st = ki.stages[si];
+                o << (si ? "," : "") << "\"";
+                if (st.mm) o << "matmul " << st.m << "x" << st.n << "x" << st.k << (st.tc ? " tcgen05" : " cuda_cores");
+                else o << "rows " << st.rows;
+                o << "\"";
+            }
+            o << "],\"scratch_tiles\":" << ki.scratch_tiles.size();
+        }
+        o << "}";
     }
     o << "]";
     if (p.cached) {

@@ -109,6 +109,9 @@ cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev,
                                 cudaStream_t s);
 int tile_program_max_smem();
 
+// Matmul on CUDA cores, any shape: C[M,N] (f32) = A[M,K] . B[K,N] (f16 or f32) per task, records [oa, ob, oc],
+// each output accumulated over k in order with fused multiply-adds (the tile program's arithmetic).
+cudaError_t launch_matmul_simt(const TaskBatch& b, int M, int N, int K, int workers, cudaStream_t s);
 // Matmul tile task: C[M,N] (f32) = A[M,K] (f16) . B[K,N] (f16) (+ C if accumulate).
 // Params: 0 = A, 1 = B, 2 = C (same tensor for InOut).
 cudaError_t launch_matmul_tiles(const TaskBatch& b, int accumulate, int workers, cudaStream_t s);

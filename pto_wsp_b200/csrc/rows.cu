@@ -418,6 +418,95 @@ cudaError_t launch_softmax_rows(const TaskBatch& b, int workers, cudaStream_t s)
 
 int tile_program_max_smem() { return 227 * 1024; }
 
+namespace {
+
+// Matmul stage on CUDA cores: C[M,N] (f32) = A[M,K] . B[K,N] per task, records [oa, ob, oc].  Every output
+// accumulates over k in order with one fused multiply-add per step, as the tile program does, so a staged
+// kernel reproduces its results bit for bit; A and B may be f16 (exactly widened) or f32.  One 64 x 64 block of
+// one task per CTA iteration (16 x 16 threads, 4 x 4 outputs each), k staged through shared memory 16 at a time.
+constexpr int kSimtBM = 64, kSimtBN = 64, kSimtBK = 16;
+
+__global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, int N, int K) {
+    __shared__ float As[kSimtBK][kSimtBM + 4];
+    __shared__ float Bs[kSimtBK][kSimtBN + 4];
+    const ParamDesc &A = b.p[0], &B = b.p[1], &C = b.p[2];
+    const int bm_n = (M + kSimtBM - 1) / kSimtBM, bn_n = (N + kSimtBN - 1) / kSimtBN;
+    const int64_t per_task = static_cast<int64_t>(bm_n) * bn_n;
+    const int64_t units = b.ntasks * per_task;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+        const int64_t t = u / per_task;
+        const int rem = static_cast<int>(u - t * per_task);
+        const int m0 = (rem / bn_n) * kSimtBM, n0 = (rem % bn_n) * kSimtBN;
+        const int64_t* rec = b.rec + t * b.stride;
+        const int64_t oa = rec[0], ob = rec[1], oc = rec[2];
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+        for (int k0 = 0; k0 < K; k0 += kSimtBK) {
+            for (int e = threadIdx.x; e < kSimtBK * kSimtBM; e += 256) {
+                const int mm = e / kSimtBK, kk = e % kSimtBK;  // consecutive threads: consecutive k of a row of A
+                const int r = m0 + mm, kq = k0 + kk;
+                float v = 0.f;
+                if (r < M && kq < K) {
+                    const int64_t off = oa + r * A.s3 + kq * A.s4;
+                    if (off >= 0 && off < A.numel_span) v = load_elem_f(A, off);
+                    else atomicOr(b.err, kErrBounds);
+                }
+                As[kk][mm] = v;
+            }
+            for (int e = threadIdx.x; e < kSimtBK * kSimtBN; e += 256) {
+                const int kk = e / kSimtBN, nn = e % kSimtBN;  // consecutive threads: consecutive n of a row of B
+                const int c = n0 + nn, kq = k0 + kk;
+                float v = 0.f;
+                if (c < N && kq < K) {
+                    const int64_t off = ob + kq * B.s3 + c * B.s4;
+                    if (off >= 0 && off < B.numel_span) v = load_elem_f(B, off);
+                    else atomicOr(b.err, kErrBounds);
+                }
+                Bs[kk][nn] = v;
+            }
+            __syncthreads();
+            const int kn = min(kSimtBK, K - k0);
+            for (int kk = 0; kk < kn; ++kk) {
+                float av[4], bv[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int r = m0 + ty * 4 + i, c = n0 + tx * 4 + j;
+                if (r >= M || c >= N) continue;
+                const int64_t off = oc + r * C.s3 + c * C.s4;
+                if (off >= 0 && off < C.numel_span) store_elem(C, off, __float_as_uint(acc[i][j]), W_F32);
+                else atomicOr(b.err, kErrBounds);
+            }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_matmul_simt(const TaskBatch& b, int M, int N, int K, int workers, cudaStream_t s) {
+    const int64_t units = b.ntasks * ((M + kSimtBM - 1) / kSimtBM) * ((N + kSimtBN - 1) / kSimtBN);
+    int64_t blocks = std::min<int64_t>(units, static_cast<int64_t>(sm_count()) * 8);
+    if (workers > 0) blocks = std::min<int64_t>(blocks, workers);
+    blocks = std::max<int64_t>(blocks, 1);
+    matmul_simt_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(b, M, N, K);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev, int smem_bytes, int workers,
                                 cudaStream_t s) {
     if (smem_bytes > 48 * 1024) {

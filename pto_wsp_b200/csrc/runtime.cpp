@@ -812,6 +812,7 @@ Batch::~Batch() {
     if (ep_mm_rec_dev) cudaFree(ep_mm_rec_dev);
     if (ep_rec_dev) cudaFree(ep_rec_dev);
     if (ep_unit_rec_dev) cudaFree(ep_unit_rec_dev);
+    if (st_rec_dev) cudaFree(st_rec_dev);
     if (sel_dev) cudaFree(sel_dev);
     if (sel_tree_dev) cudaFree(sel_tree_dev);
 }
@@ -1143,7 +1144,132 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
         }
         if (B.ep_ok != 1 || ki.ep_jit_state != 1) kind = ImplKind::TileProgram;  // the generic tile program
     }
+    // Staged: f32 scratch tiles, one per task and crossing value, and the stage records (built once per batch)
+    const int st_np = kd.num_tensor_params;
+    const int st_S = static_cast<int>(ki.scratch_tiles.size());
+    std::vector<int64_t> st_base(static_cast<size_t>(st_S) + 1, 0);
+    char* st_scr = nullptr;
+    auto st_tile = [&](int j) { return int64_t(ki.scratch_tiles[j].first) * ki.scratch_tiles[j].second; };
+    auto st_desc = [&](int j) {
+        dev::ParamDesc d{};
+        d.base = st_scr;
+        d.s3 = ki.scratch_tiles[j].second;
+        d.s4 = 1;
+        d.numel_span = st_base[st_S];
+        d.rows = ki.scratch_tiles[j].first;
+        d.cols = ki.scratch_tiles[j].second;
+        d.type = dev::PT_F32;
+        d.elem_bytes = 4;
+        return d;
+    };
+    const int st_stride = B.stride + st_S;
+    bool st_rows_ok = rows_ok;
+    if (kind == ImplKind::Staged) {
+        for (int j = 0; j < st_S; ++j) {
+            st_base[j + 1] = st_base[j] + B.ntasks * st_tile(j);
+            if (ki.scratch_tiles[j].second % 4) st_rows_ok = false;
+        }
+        st_scr = static_cast<char*>(ensure_scratch(P, static_cast<size_t>(st_base[st_S]) * sizeof(float)));
+        if (B.st_ok < 0) {
+            // records of every stage, from the host records (read back once when a cached table dropped them)
+            std::vector<int64_t> back;
+            const int64_t* rec = B.rec.data();
+            if (B.rec.empty()) {
+                back.resize(static_cast<size_t>(B.ntasks) * B.stride);
+                PW_CUDA(cudaMemcpyAsync(back.data(), rec_dev + B.dev_off, back.size() * sizeof(int64_t),
+                                        cudaMemcpyDeviceToHost, P.stream));
+                PW_CUDA(cudaStreamSynchronize(P.stream));
+                rec = back.data();
+            }
+            int nmm = 0;
+            for (const auto& st : ki.stages) nmm += st.mm ? 1 : 0;
+            std::vector<int64_t> all(static_cast<size_t>(B.ntasks) * (st_stride + 3 * nmm));
+            for (int64_t t = 0; t < B.ntasks; ++t) {
+                const int64_t* r = rec + t * B.stride;
+                int64_t* o = &all[t * st_stride];
+                for (int j = 0; j < st_np; ++j) o[j] = r[j];
+                for (int j = 0; j < st_S; ++j) o[st_np + j] = st_base[j] + t * st_tile(j);
+                for (int j = st_np; j < B.stride; ++j) o[j + st_S] = r[j];
+            }
+            B.st_tc_mask = 0;
+            int q = 0;
+            for (const auto& st : ki.stages) {
+                if (!st.mm) continue;
+                int64_t* m = &all[static_cast<size_t>(B.ntasks) * (st_stride + 3 * q)];
+                auto off = [&](int src, int64_t t, const int64_t* r) {
+                    return src >= 0 ? r[src] : st_base[~src] + t * st_tile(~src);
+                };
+                for (int64_t t = 0; t < B.ntasks; ++t) {
+                    const int64_t* r = rec + t * B.stride;
+                    m[t * 3] = off(st.a, t, r);
+                    m[t * 3 + 1] = off(st.b, t, r);
+                    m[t * 3 + 2] = st_base[st.c] + t * st_tile(st.c);
+                }
+                if (st.tc) {  // the tcgen05 tile kernel's layout conditions, for every task
+                    dev::TaskBatch mtb{};
+                    mtb.p[0] = tb.p[st.a];
+                    mtb.p[1] = tb.p[st.b];
+                    mtb.p[2] = st_desc(st.c);
+                    bool ok = dev::matmul_tiles_supported(mtb);
+                    const dev::ParamDesc &A = mtb.p[0], &Bm = mtb.p[1];
+                    const int64_t a_rows = ok ? (A.numel_span + A.s3 - 1) / A.s3 : 0;
+                    const int64_t b_rows = ok ? (Bm.numel_span + Bm.s3 - 1) / Bm.s3 : 0;
+                    for (int64_t t = 0; ok && t < B.ntasks; ++t) {
+                        const int64_t oa = m[t * 3], ob = m[t * 3 + 1];
+                        ok = oa >= 0 && ob >= 0 && oa % 8 == 0 && ob % 8 == 0 && (oa % A.s3) + st.k <= A.s3 &&
+                             (oa / A.s3) + 128 <= a_rows && (ob % Bm.s3) + st.n <= Bm.s3 && (ob / Bm.s3) + st.k <= b_rows;
+                    }
+                    if (ok) B.st_tc_mask |= 1u << q;
+                }
+                ++q;
+            }
+            PW_CUDA(cudaMalloc(&B.st_rec_dev, all.size() * sizeof(int64_t)));
+            PW_CUDA(cudaMemcpy(B.st_rec_dev, all.data(), all.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
+            B.st_ok = 1;
+        }
+        for (size_t si = 0; si < ki.stages.size(); ++si) {
+            Stage& st = ki.stages[si];
+            if (st.mm || st.jit_state != 2) continue;
+            const std::string name = "ptowsp_st_k" + std::to_string(B.kernel) + "_" + std::to_string(si);
+            std::string note;
+            if (!jit::load_cubin(st.cubin, name, &st.fn, &note))
+                throw Error(PTOWSP_ERR_CUDA, "kernel '" + kd.name + "': stage " + std::to_string(si) + ": " + note);
+            st.jit_state = 1;
+            if (!jit::load_cubin(st.cubin, name + "_v", &st.fn_vec, &note)) st.fn_vec = nullptr;
+        }
+    }
     switch (kind) {
+        case ImplKind::Staged: {
+            int q = 0;
+            for (size_t si = 0; si < ki.stages.size(); ++si) {
+                const Stage& st = ki.stages[si];
+                if (st.mm) {
+                    dev::TaskBatch mtb{};
+                    mtb.p[0] = st.a >= 0 ? tb.p[st.a] : st_desc(~st.a);
+                    mtb.p[1] = st.b >= 0 ? tb.p[st.b] : st_desc(~st.b);
+                    mtb.p[2] = st_desc(st.c);
+                    mtb.rec = B.st_rec_dev + static_cast<size_t>(B.ntasks) * (st_stride + 3 * q);
+                    mtb.ntasks = B.ntasks;
+                    mtb.stride = 3;
+                    mtb.nparams = 3;
+                    mtb.err = P.err_dev;
+                    e = ((B.st_tc_mask >> q) & 1u) ? dev::launch_matmul_tiles(mtb, 0, workers, P.stream)
+                                                   : dev::launch_matmul_simt(mtb, st.m, st.n, st.k, workers, P.stream);
+                    ++q;
+                } else {
+                    dev::TaskBatch etb = tb;
+                    for (int j = 0; j < st_S; ++j) etb.p[st_np + j] = st_desc(j);
+                    etb.nparams = st_np + st_S;
+                    etb.stride = st_stride;
+                    etb.rec = B.st_rec_dev;
+                    e = jit::launch_row_kernel(st_rows_ok && st.fn_vec ? st.fn_vec : st.fn, etb, st.rows, workers,
+                                               P.stream);
+                }
+                if (e != cudaSuccess) break;
+                if (si + 1 < ki.stages.size()) launches++;
+            }
+            break;
+        }
         case ImplKind::MatmulEpilogue: {
             const int np = kd.num_tensor_params;
             dev::TaskBatch mtb{};
@@ -1621,6 +1747,189 @@ bool split_matmul_epilogue(KernelImpl& ki, const KernelDef& kd, int k) {
     ki.ep_jit_state = 2;
     ki.kind = ImplKind::MatmulEpilogue;
     ki.jit_note = "matmul on tcgen05, the rest as a fused row program";
+    return true;
+}
+
+bool build_stage_program(const dev::TileProgram& tp, const KernelDef& kd, const std::string& name, std::string* cubin,
+                         std::string* note) {
+    return build_row_program(tp, kd, kd.num_tensor_params, name, cubin, note);
+}
+
+bool split_stages(KernelImpl& ki, const KernelDef& kd) {
+    const dev::TileProgram& tp = ki.tp;
+    const int np = kd.num_tensor_params;
+    const int nslots = tp.nslots;
+    std::vector<int> def(nslots, -1);  // defining instruction of each slot (one at most)
+    std::vector<int*> f;
+    int nmm = 0;
+    for (int i = 0; i < tp.ninstr; ++i) {
+        dev::TPInstr in = tp.ins[i];
+        if (!slot_fields(in, f)) return false;  // ops without a row form (iota, sort, extract)
+        if (in.op == dev::TP_MATMUL) ++nmm;
+        if (in.op == dev::TP_STORE) continue;
+        if (in.dst < 0 || in.dst >= nslots || def[in.dst] >= 0) return false;
+        def[in.dst] = i;
+    }
+    if (nmm == 0) return false;
+    auto param_dtype = [&](int ti) {
+        for (const auto& kp : kd.params)
+            if (kp.tensor_index == ti) return kp.v.dtype;
+        return DType::F32;
+    };
+    // stage of each instruction: row stages 0, 2, 4, ... around matmul stages 1, 3, ...
+    std::vector<int> stage_of(tp.ninstr);
+    int st = 0;
+    for (int i = 0; i < tp.ninstr; ++i) {
+        if (tp.ins[i].op == dev::TP_MATMUL) {
+            stage_of[i] = st | 1;
+            st = (st | 1) + 1;
+        } else {
+            stage_of[i] = st;
+        }
+    }
+    const int nstages = st + 1;
+    // a slot loaded straight from a param (no transposed load) is re-read from the param wherever it is needed
+    auto param_load = [&](int slot) {
+        const int d = def[slot];
+        return d >= 0 && tp.ins[d].op == dev::TP_LOAD && tp.ins[d].k == 0 ? d : -1;
+    };
+    // uses of each slot by stage
+    std::vector<std::vector<int>> used_in(nslots);
+    for (int i = 0; i < tp.ninstr; ++i) {
+        dev::TPInstr in = tp.ins[i];
+        slot_fields(in, f);
+        for (size_t j = (in.op == dev::TP_STORE ? 0 : 1); j < f.size(); ++j) used_in[*f[j]].push_back(stage_of[i]);
+    }
+    // matmul operands: the param itself when the slot is a plain param load of the operand's shape
+    std::vector<Stage> stages;
+    std::vector<int> scratch_of(nslots, -1);
+    std::vector<std::pair<int, int>> scratch;
+    auto need_scratch = [&](int slot) {
+        if (scratch_of[slot] < 0) {
+            scratch_of[slot] = static_cast<int>(scratch.size());
+            scratch.emplace_back(tp.slots[slot].rows, tp.slots[slot].cols);
+        }
+        return scratch_of[slot];
+    };
+    for (int i = 0; i < tp.ninstr; ++i) {
+        const dev::TPInstr& in = tp.ins[i];
+        if (in.op != dev::TP_MATMUL) continue;
+        if (tp.slots[in.dst].word != dev::W_F32 || tp.slots[in.a].word != dev::W_F32 ||
+            tp.slots[in.b].word != dev::W_F32)
+            return false;
+        Stage S;
+        S.mm = true;
+        S.m = in.rows;
+        S.n = in.cols;
+        S.k = in.k;
+        const int la = param_load(in.a), lb = param_load(in.b);
+        const bool pa = la >= 0 && tp.ins[la].rows == S.m && tp.ins[la].cols == S.k;
+        const bool pb = lb >= 0 && tp.ins[lb].rows == S.k && tp.ins[lb].cols == S.n;
+        S.a = pa ? tp.ins[la].param : ~need_scratch(in.a);
+        S.b = pb ? tp.ins[lb].param : ~need_scratch(in.b);
+        S.c = need_scratch(in.dst);
+        S.tc = pa && pb && S.a != S.b && param_dtype(S.a) == DType::F16 && param_dtype(S.b) == DType::F16 &&
+               S.m == 128 && (S.n == 64 || S.n == 128 || S.n == 256) && S.k >= 64 && S.k % 64 == 0;
+        S.rows = stage_of[i];  // the stage number until the list is assembled
+        stages.push_back(S);
+    }
+    // values crossing from a row stage to a later stage (other than plain param loads, which are re-read)
+    for (int sl = 0; sl < nslots; ++sl) {
+        if (def[sl] < 0 || tp.ins[def[sl]].op == dev::TP_MATMUL) continue;
+        const int ds = stage_of[def[sl]];
+        bool later = false;
+        for (int u : used_in[sl]) later = later || u > ds;
+        if (later && param_load(sl) < 0) need_scratch(sl);
+    }
+    if (np + static_cast<int>(scratch.size()) > dev::kMaxParams) return false;
+    // row stages: the stage's own instructions, led by loads of what earlier stages left in scratch or in params,
+    // followed by stores of what later stages need
+    std::vector<Stage> out;
+    size_t next_mm = 0;
+    for (int sg = 0; sg < nstages; ++sg) {
+        if (sg & 1) {
+            out.push_back(stages[next_mm++]);
+            continue;
+        }
+        dev::TileProgram rp{};
+        rp.ninstr = 0;
+        std::vector<char> have(nslots, 0);
+        auto emit = [&](const dev::TPInstr& x) {
+            if (rp.ninstr >= dev::kTPMaxInstr) return false;
+            rp.ins[rp.ninstr++] = x;
+            return true;
+        };
+        auto bring = [&](int slot) {  // make an earlier stage's value available in this stage
+            if (have[slot]) return true;
+            have[slot] = 1;
+            const int pl = param_load(slot);
+            if (pl >= 0) return emit(tp.ins[pl]);
+            if (scratch_of[slot] < 0) return false;
+            dev::TPInstr ld{};
+            ld.op = dev::TP_LOAD;
+            ld.dst = slot;
+            ld.param = np + scratch_of[slot];
+            ld.rows = tp.slots[slot].rows;
+            ld.cols = tp.slots[slot].cols;
+            return emit(ld);
+        };
+        bool any = false;  // an instruction besides re-reads of params for matmuls
+        for (int i = 0; i < tp.ninstr; ++i) {
+            if (stage_of[i] != sg) continue;
+            dev::TPInstr in = tp.ins[i];
+            slot_fields(in, f);
+            for (size_t j = (in.op == dev::TP_STORE ? 0 : 1); j < f.size(); ++j)
+                if (def[*f[j]] < 0 || stage_of[def[*f[j]]] < sg)
+                    if (!bring(*f[j])) return false;
+            if (in.op == dev::TP_LOAD && param_load(in.dst) == i) {
+                // a param load is emitted where a row op of this stage uses it (or a later stage needs it in
+                // scratch); loads only the matmuls read are dropped
+                bool row_use = scratch_of[in.dst] >= 0;
+                for (int u : used_in[in.dst]) row_use = row_use || (u == sg);
+                if (!row_use) continue;
+                have[in.dst] = 1;
+            } else if (in.op != dev::TP_STORE) {
+                have[in.dst] = 1;
+            }
+            if (!emit(in)) return false;
+            any = true;
+        }
+        for (int sl = 0; sl < nslots; ++sl)  // values of this stage that later stages read from scratch
+            if (def[sl] >= 0 && stage_of[def[sl]] == sg && scratch_of[sl] >= 0 && tp.ins[def[sl]].op != dev::TP_MATMUL) {
+                dev::TPInstr stv{};
+                stv.op = dev::TP_STORE;
+                stv.a = sl;
+                stv.param = np + scratch_of[sl];
+                stv.rows = tp.slots[sl].rows;
+                stv.cols = tp.slots[sl].cols;
+                if (!emit(stv)) return false;
+                any = true;
+            }
+        if (!any) continue;
+        // keep only the slots the stage uses, renumbered in order
+        std::vector<int> remap(nslots, -1);
+        rp.nslots = 0;
+        for (int i = 0; i < rp.ninstr; ++i) {
+            slot_fields(rp.ins[i], f);
+            for (int* x : f) {
+                if (remap[*x] < 0) {
+                    remap[*x] = rp.nslots;
+                    rp.slots[rp.nslots++] = tp.slots[*x];
+                }
+                *x = remap[*x];
+            }
+        }
+        for (int i = 0; i < dev::kMaxParams; ++i) rp.scalar_types[i] = tp.scalar_types[i];
+        rp.smem_words = 0;
+        std::string why;
+        if (!jit::row_local(rp, &why)) return false;
+        Stage S;
+        S.tp = rp;
+        S.rows = jit::program_rows(rp);
+        out.push_back(S);
+    }
+    ki.stages = std::move(out);
+    ki.scratch_tiles = std::move(scratch);
     return true;
 }
 

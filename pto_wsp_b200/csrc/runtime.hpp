@@ -17,7 +17,25 @@
 namespace ptowsp {
 
 enum class ImplKind : uint8_t { RmsNorm, Softmax, TileProgram, Matmul, MatmulAcc, MatmulEpilogue, PagedDecode,
-                                IndexerScore, TopK };
+                                IndexerScore, TopK, Staged };
+
+// One stage of a generic kernel cut at its contractions: a matmul (tcgen05 tile kernel for f16 params of its
+// shapes, else the CUDA-core kernel with the tile program's fused multiply-add order) or a fused row program.
+// Values that cross stages live in f32 scratch tiles in HBM, one per task; a row program sees them as params
+// num_tensor_params + j.
+struct Stage {
+    bool mm = false;
+    int a = 0, b = 0;            // matmul operands: a tensor param (>= 0) or ~scratch tile (< 0)
+    int c = 0;                   // matmul result: scratch tile
+    int m = 0, n = 0, k = 0;     // 128 x n = (128 x k) . (k x n) for the tile kernel; any shape on CUDA cores
+    bool tc = false;             // f16 params in the tcgen05 tile kernel's shapes
+    dev::TileProgram tp{};       // row stage
+    int rows = 0;                // its rows per task
+    int jit_state = 0;           // 2 compiled (cubin), 1 loaded, -1 failed
+    std::string cubin;
+    void* fn = nullptr;
+    void* fn_vec = nullptr;
+};
 
 const char* impl_name(ImplKind k);
 
@@ -48,6 +66,9 @@ struct KernelImpl {
     std::string ep_cubin;
     void* ep_fn = nullptr;
     void* ep_fn_vec = nullptr;
+    // Staged: the stages in order and the [rows, cols] of each f32 scratch tile
+    std::vector<Stage> stages;
+    std::vector<std::pair<int, int>> scratch_tiles;
 };
 
 // Build (NVRTC) the fused row kernel of kernel `k` when its tile program is row-local (jit_state -> 2 or -1).
@@ -55,6 +76,12 @@ void jit_prepare(KernelImpl& ki, const KernelDef& kd, int k);
 // Split a generic kernel into a tcgen05 matmul and a fused row-program epilogue when its shape allows
 // (kind -> MatmulEpilogue); false leaves the kernel as it is.
 bool split_matmul_epilogue(KernelImpl& ki, const KernelDef& kd, int k);
+// Cut a generic kernel with contractions into stages (matmuls and fused row programs over f32 scratch tiles) when
+// every stage between two contractions is row-local; fills ki.stages (the kind is left to the caller).
+bool split_stages(KernelImpl& ki, const KernelDef& kd);
+// NVRTC build of a row stage as kernel `name` (+ `name`_v); params past the kernel's own are f32 scratch tiles.
+bool build_stage_program(const dev::TileProgram& tp, const KernelDef& kd, const std::string& name, std::string* cubin,
+                         std::string* note);
 
 // Per-tensor binding of one run.
 struct TensorBinding {
@@ -105,6 +132,11 @@ struct Batch {  // tasks of one kernel inside one wave
     int chunk_n = 0;
     std::vector<int64_t> chunk_ranges;
     std::vector<uint8_t> chunk_exact;  // per param: every chunk's tiles cover its range exactly once
+    // Staged: [row-stage records (the batch's records with the scratch offsets after the view offsets) |
+    // [oa, ob, oc] per task for each matmul stage] (-1 not built, 1 built)
+    int64_t* st_rec_dev = nullptr;
+    int8_t st_ok = -1;
+    uint32_t st_tc_mask = 0;           // matmul stages (in order) that run on the tcgen05 tile kernel
     Batch() = default;
     Batch(Batch&& o) noexcept { *this = std::move(o); }
     Batch& operator=(Batch&& o) noexcept {
@@ -116,6 +148,8 @@ struct Batch {  // tasks of one kernel inside one wave
         ep_mm_rec_dev = o.ep_mm_rec_dev; ep_rec_dev = o.ep_rec_dev; ep_ok = o.ep_ok;
         ep_unit_rec_dev = o.ep_unit_rec_dev; ep_nunits = o.ep_nunits;
         o.ep_unit_rec_dev = nullptr;
+        st_rec_dev = o.st_rec_dev; st_ok = o.st_ok; st_tc_mask = o.st_tc_mask;
+        o.st_rec_dev = nullptr;
         sel = o.sel; sel_tensor = o.sel_tensor; sel_rows = std::move(o.sel_rows); sel_row_words = o.sel_row_words;
         sel_dev = o.sel_dev; sel_tree_dev = o.sel_tree_dev;
         o.sel_dev = nullptr;

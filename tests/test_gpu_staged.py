@@ -1,0 +1,63 @@
+"""Generic kernels cut at their contractions (-m gpu): matmul stages (tcgen05 for f16 tiles of its shapes, CUDA-core
+fused multiply-adds otherwise) and fused row programs, with the values between them in HBM scratch.  The f32 MLP's
+stages do the tile program's arithmetic in its order, so it matches the oracle bit for bit; the attention kernel's
+first contraction runs on tensor cores and is held to the f16-contraction tolerance, 2e-3 relative."""
+
+import numpy as np
+import pytest
+from _staged import attention_arrays, attention_plan, mlp_arrays, mlp_plan
+from cpu_sim import CpuSim
+
+from pto_wsp_b200.runtime import CudaExecutable
+
+pytestmark = pytest.mark.gpu
+
+
+def test_f32_mlp_stages_bit_exact(require_cuda):
+    rng = np.random.default_rng(11)
+    T, rows, d, hidden = 6, 64, 512, 256  # x tile 128 KB, W1 512 KB: far beyond one CTA's shared memory
+    plan = mlp_plan(T, rows, d, hidden)
+    arrays = mlp_arrays(rng, T, rows, d, hidden)
+    ref = [a.copy() for a in arrays]
+    cyc = CpuSim(plan).run(ref)
+    ex = CudaExecutable(plan)
+    k = ex.describe()["kernels"][0]
+    assert k["impl"] == "staged_matmul+row_programs"
+    assert k["stages"] == ["matmul 64x256x512 cuda_cores", "rows 64", "matmul 64x512x256 cuda_cores", "rows 64"]
+    for _ in range(2):  # the second run replays the cached task table and stage records
+        got = [a.copy() for a in arrays]
+        assert ex.run_with_symbols(got, {}, {}, {}) == cyc
+        assert np.array_equal(got[3], ref[3])
+    assert ex.timing()["launches"] == 4
+    torch = pytest.importorskip("torch")
+    dev = [torch.from_numpy(a.copy()).cuda() for a in arrays]
+    ex.run_with_symbols(dev, {}, {}, {})
+    assert np.array_equal(dev[3].cpu().numpy(), ref[3])
+
+
+@pytest.mark.parametrize("kv_len", [256, 128])
+def test_attention_stages_vs_oracle(kv_len, require_cuda):
+    rng = np.random.default_rng(kv_len)
+    B, H, QT = 2, 3, 2
+    plan = attention_plan(B, H, QT, kv_len)
+    arrays = attention_arrays(rng, B, H, QT, kv_len)
+    ref = [a.copy() for a in arrays]
+    cyc = CpuSim(plan).run(ref)
+    ex = CudaExecutable(plan)
+    k = ex.describe()["kernels"][0]
+    assert k["stages"][0] == f"matmul 128x{kv_len}x128 tcgen05"
+    assert k["stages"][2] == f"matmul 128x128x{kv_len} cuda_cores"
+    got = [a.copy() for a in arrays]
+    assert ex.run_with_symbols(got, {}, {}, {}) == cyc
+    o, r = got[3].astype(np.float64), ref[3].astype(np.float64)
+    scale = np.sqrt(np.mean(r * r))
+    assert np.all(np.abs(o - r) <= 2e-3 * (np.abs(r) + scale)), float((np.abs(o - r) / (np.abs(r) + scale)).max())
+    # fp64 recompute of one tile: softmax(scale * q . k^T) . v
+    q = arrays[0][1, 2, 1].astype(np.float64)
+    kt = arrays[1][1, 2].astype(np.float64)
+    v = arrays[2][1, 2].astype(np.float64)
+    s = (q @ kt) * np.float64(np.float32(0.088))
+    w = np.exp(s - s.max(axis=1, keepdims=True))
+    w /= w.sum(axis=1, keepdims=True)
+    o64 = w @ v
+    assert np.all(np.abs(got[3][1, 2, 1] - o64) <= 2e-3 * (np.abs(o64) + np.sqrt(np.mean(o64 * o64))))

@@ -97,3 +97,24 @@ def test_matmul_with_row_local_epilogue_is_split():
         pytest.skip("NVRTC not installed")
     d = CudaExecutable(mm_epilogue_plan(1, 256, 256, 256)).describe()["kernels"][0]
     assert d["impl"] == "matmul_tcgen05+row_program", d
+
+
+def test_kernels_with_contractions_split_into_stages():
+    # big tiles: matmul stages (tcgen05 where the operands are f16 params of its shapes, else CUDA cores) and row
+    # programs between them; the cycle model is the kernel's own, equal to the oracle's
+    import numpy as np
+    from _staged import attention_arrays, attention_plan, mlp_arrays, mlp_plan
+    from cpu_sim import CpuSim
+
+    for plan, arrays, stages in [
+        (attention_plan(1, 1, 1, 256), attention_arrays(np.random.default_rng(0), 1, 1, 1, 256),
+         ["matmul 128x256x128 tcgen05", "rows 128", "matmul 128x128x256 cuda_cores", "rows 128"]),
+        (mlp_plan(2, 64, 512, 256), mlp_arrays(np.random.default_rng(1), 2, 64, 512, 256),
+         ["matmul 64x256x512 cuda_cores", "rows 64", "matmul 64x512x256 cuda_cores", "rows 64"]),
+    ]:
+        ex = CudaExecutable(plan)
+        k = ex.describe()["kernels"][0]
+        assert k["impl"] == "staged_matmul+row_programs" and k["stages"] == stages and k["scratch_tiles"] == 3
+        ex.set_option("dry_run", 1)
+        assert ex.run_with_symbols([a.copy() for a in arrays], {}, {}, {}) == CpuSim(plan).run(arrays)
+        assert ex.timing()["launches"] == 1  # one batch (its stages launch in order on the GPU)
