@@ -856,8 +856,12 @@ std::string describe_program(const Program& p) {
             for (size_t si = 0; si < ki.stages.size(); ++si) {
                 const Stage& st = ki.stages[si];
                 o << (si ? "," : "") << "\"";
-                if (st.mm) o << "matmul " << st.m << "x" << st.n << "x" << st.k << (st.tc ? " tcgen05" : " cuda_cores");
-                else o << "rows " << st.rows;
+                if (!st.mm) {
+                    o << "rows " << st.rows;
+                } else {
+                    o << "matmul " << st.m << "x" << st.n << "x" << st.k << (st.tc ? " tcgen05" : " cuda_cores");
+                    if (st.tc && st.tn != st.n) o << " (" << st.n / st.tn << " tiles of " << st.tn << ")";
+                }
                 o << "\"";
             }
             o << "],\"scratch_tiles\":" << ki.scratch_tiles.size();

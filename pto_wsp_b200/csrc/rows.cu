@@ -422,31 +422,35 @@ namespace {
 
 // Matmul stage on CUDA cores: C[M,N] (f32) = A[M,K] . B[K,N] per task, records [oa, ob, oc].  Every output
 // accumulates over k in order with one fused multiply-add per step, as the tile program does, so a staged
-// kernel reproduces its results bit for bit; A and B may be f16 (exactly widened) or f32.  One 64 x 64 block of
-// one task per CTA iteration (16 x 16 threads, 4 x 4 outputs each), k staged through shared memory 16 at a time.
-constexpr int kSimtBM = 64, kSimtBN = 64, kSimtBK = 16;
+// kernel reproduces its results bit for bit; A and B may be f16 (exactly widened) or f32.  One BM x BN block of
+// one task per CTA iteration (16 x 16 threads; a thread owns the rows h*64 + 4*ty + i and the columns
+// g*64 + 4*tx + j, so its shared-memory reads are float4s that no two lanes of a quarter-warp share), k staged
+// through shared memory 16 at a time.
+constexpr int kSimtBK = 16;
 
+template <int BM, int BN>
 __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, int N, int K) {
-    __shared__ float As[kSimtBK][kSimtBM + 4];
-    __shared__ float Bs[kSimtBK][kSimtBN + 4];
+    constexpr int HM = BM / 64, HN = BN / 64;  // 64-row / 64-column halves per thread
+    __shared__ __align__(16) float As[kSimtBK][BM + 4];
+    __shared__ __align__(16) float Bs[kSimtBK][BN + 4];
     const ParamDesc &A = b.p[0], &B = b.p[1], &C = b.p[2];
-    const int bm_n = (M + kSimtBM - 1) / kSimtBM, bn_n = (N + kSimtBN - 1) / kSimtBN;
+    const int bm_n = (M + BM - 1) / BM, bn_n = (N + BN - 1) / BN;
     const int64_t per_task = static_cast<int64_t>(bm_n) * bn_n;
     const int64_t units = b.ntasks * per_task;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
         const int64_t t = u / per_task;
         const int rem = static_cast<int>(u - t * per_task);
-        const int m0 = (rem / bn_n) * kSimtBM, n0 = (rem % bn_n) * kSimtBN;
+        const int m0 = (rem / bn_n) * BM, n0 = (rem % bn_n) * BN;
         const int64_t* rec = b.rec + t * b.stride;
         const int64_t oa = rec[0], ob = rec[1], oc = rec[2];
-        float acc[4][4];
+        float acc[4 * HM][4 * HN];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4 * HM; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+            for (int j = 0; j < 4 * HN; ++j) acc[i][j] = 0.f;
         for (int k0 = 0; k0 < K; k0 += kSimtBK) {
-            for (int e = threadIdx.x; e < kSimtBK * kSimtBM; e += 256) {
+            for (int e = threadIdx.x; e < kSimtBK * BM; e += 256) {
                 const int mm = e / kSimtBK, kk = e % kSimtBK;  // consecutive threads: consecutive k of a row of A
                 const int r = m0 + mm, kq = k0 + kk;
                 float v = 0.f;
@@ -457,8 +461,8 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
                 }
                 As[kk][mm] = v;
             }
-            for (int e = threadIdx.x; e < kSimtBK * kSimtBN; e += 256) {
-                const int kk = e / kSimtBN, nn = e % kSimtBN;  // consecutive threads: consecutive n of a row of B
+            for (int e = threadIdx.x; e < kSimtBK * BN; e += 256) {
+                const int kk = e / BN, nn = e % BN;  // consecutive threads: consecutive n of a row of B
                 const int c = n0 + nn, kq = k0 + kk;
                 float v = 0.f;
                 if (c < N && kq < K) {
@@ -471,23 +475,29 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
             __syncthreads();
             const int kn = min(kSimtBK, K - k0);
             for (int kk = 0; kk < kn; ++kk) {
-                float av[4], bv[4];
+                float av[4 * HM], bv[4 * HN];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+                for (int h = 0; h < HM; ++h) {
+                    const float4 x = *reinterpret_cast<const float4*>(&As[kk][h * 64 + ty * 4]);
+                    av[4 * h] = x.x; av[4 * h + 1] = x.y; av[4 * h + 2] = x.z; av[4 * h + 3] = x.w;
+                }
 #pragma unroll
-                for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+                for (int g = 0; g < HN; ++g) {
+                    const float4 x = *reinterpret_cast<const float4*>(&Bs[kk][g * 64 + tx * 4]);
+                    bv[4 * g] = x.x; bv[4 * g + 1] = x.y; bv[4 * g + 2] = x.z; bv[4 * g + 3] = x.w;
+                }
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
+                for (int i = 0; i < 4 * HM; ++i)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+                    for (int j = 0; j < 4 * HN; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
             }
             __syncthreads();
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4 * HM; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int r = m0 + ty * 4 + i, c = n0 + tx * 4 + j;
+            for (int j = 0; j < 4 * HN; ++j) {
+                const int r = m0 + (i / 4) * 64 + ty * 4 + (i % 4), c = n0 + (j / 4) * 64 + tx * 4 + (j % 4);
                 if (r >= M || c >= N) continue;
                 const int64_t off = oc + r * C.s3 + c * C.s4;
                 if (off >= 0 && off < C.numel_span) store_elem(C, off, __float_as_uint(acc[i][j]), W_F32);
@@ -496,15 +506,26 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
     }
 }
 
+template <int BM, int BN>
+cudaError_t launch_simt(const TaskBatch& b, int M, int N, int K, int workers, cudaStream_t s) {
+    const int64_t units = b.ntasks * ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, matmul_simt_kernel<BM, BN>, 256, 0);
+    int64_t blocks = std::min<int64_t>(units, static_cast<int64_t>(std::max(per_sm, 1)) * sm_count());
+    if (workers > 0) blocks = std::min<int64_t>(blocks, workers);
+    blocks = std::max<int64_t>(blocks, 1);
+    matmul_simt_kernel<BM, BN><<<static_cast<unsigned>(blocks), 256, 0, s>>>(b, M, N, K);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_matmul_simt(const TaskBatch& b, int M, int N, int K, int workers, cudaStream_t s) {
-    const int64_t units = b.ntasks * ((M + kSimtBM - 1) / kSimtBM) * ((N + kSimtBN - 1) / kSimtBN);
-    int64_t blocks = std::min<int64_t>(units, static_cast<int64_t>(sm_count()) * 8);
-    if (workers > 0) blocks = std::min<int64_t>(blocks, workers);
-    blocks = std::max<int64_t>(blocks, 1);
-    matmul_simt_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(b, M, N, K);
-    return cudaGetLastError();
+    // Measured on B200: a 64-row tile with N >= 128 runs best as 64 x 128 blocks (llama-style MLP, 64 x 512 x 256:
+    // 1.02 ms against 1.25 with 64 x 64); 128-row tiles run best as 64 x 64 blocks (attention P.V, 128 x 128 x
+    // 1024: 128 x 128 blocks were 14 % slower -- two CTAs per SM hide the element-wise global loads less well)
+    if (M < 128 && N >= 128) return launch_simt<64, 128>(b, M, N, K, workers, s);
+    return launch_simt<64, 64>(b, M, N, K, workers, s);
 }
 
 cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev, int smem_bytes, int workers,

@@ -1163,6 +1163,12 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
         return d;
     };
     const int st_stride = B.stride + st_S;
+    auto st_mm_records = [&](int64_t ntasks) {  // matmul-stage records: n / tn per task for tcgen05 candidates
+        int64_t n = 0;
+        for (const auto& st : ki.stages)
+            if (st.mm) n += ntasks * (st.tc ? st.n / st.tn : 1);
+        return n;
+    };
     bool st_rows_ok = rows_ok;
     if (kind == ImplKind::Staged) {
         for (int j = 0; j < st_S; ++j) {
@@ -1181,9 +1187,7 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                 PW_CUDA(cudaStreamSynchronize(P.stream));
                 rec = back.data();
             }
-            int nmm = 0;
-            for (const auto& st : ki.stages) nmm += st.mm ? 1 : 0;
-            std::vector<int64_t> all(static_cast<size_t>(B.ntasks) * (st_stride + 3 * nmm));
+            std::vector<int64_t> all(static_cast<size_t>(B.ntasks) * st_stride + 3 * st_mm_records(B.ntasks));
             for (int64_t t = 0; t < B.ntasks; ++t) {
                 const int64_t* r = rec + t * B.stride;
                 int64_t* o = &all[t * st_stride];
@@ -1193,34 +1197,52 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
             }
             B.st_tc_mask = 0;
             int q = 0;
+            size_t mo = static_cast<size_t>(B.ntasks) * st_stride;  // this matmul stage's records
             for (const auto& st : ki.stages) {
                 if (!st.mm) continue;
-                int64_t* m = &all[static_cast<size_t>(B.ntasks) * (st_stride + 3 * q)];
+                int64_t* m = &all[mo];
                 auto off = [&](int src, int64_t t, const int64_t* r) {
                     return src >= 0 ? r[src] : st_base[~src] + t * st_tile(~src);
                 };
-                for (int64_t t = 0; t < B.ntasks; ++t) {
-                    const int64_t* r = rec + t * B.stride;
-                    m[t * 3] = off(st.a, t, r);
-                    m[t * 3 + 1] = off(st.b, t, r);
-                    m[t * 3 + 2] = st_base[st.c] + t * st_tile(st.c);
-                }
-                if (st.tc) {  // the tcgen05 tile kernel's layout conditions, for every task
+                bool ok = st.tc;
+                if (ok) {
+                    // tcgen05 tile kernel: each task's n columns as n / tn tiles [oa, ob + j tn, oc + j tn], under
+                    // the kernel's layout conditions for every tile
+                    const int ns = st.n / st.tn;
                     dev::TaskBatch mtb{};
                     mtb.p[0] = tb.p[st.a];
                     mtb.p[1] = tb.p[st.b];
+                    mtb.p[1].cols = st.tn;
                     mtb.p[2] = st_desc(st.c);
-                    bool ok = dev::matmul_tiles_supported(mtb);
+                    mtb.p[2].cols = st.tn;
+                    ok = dev::matmul_tiles_supported(mtb) && mtb.p[1].s4 == 1;
                     const dev::ParamDesc &A = mtb.p[0], &Bm = mtb.p[1];
                     const int64_t a_rows = ok ? (A.numel_span + A.s3 - 1) / A.s3 : 0;
                     const int64_t b_rows = ok ? (Bm.numel_span + Bm.s3 - 1) / Bm.s3 : 0;
                     for (int64_t t = 0; ok && t < B.ntasks; ++t) {
-                        const int64_t oa = m[t * 3], ob = m[t * 3 + 1];
+                        const int64_t* r = rec + t * B.stride;
+                        const int64_t oa = off(st.a, t, r), ob = off(st.b, t, r);
+                        const int64_t oc = st_base[st.c] + t * st_tile(st.c);
                         ok = oa >= 0 && ob >= 0 && oa % 8 == 0 && ob % 8 == 0 && (oa % A.s3) + st.k <= A.s3 &&
                              (oa / A.s3) + 128 <= a_rows && (ob % Bm.s3) + st.n <= Bm.s3 && (ob / Bm.s3) + st.k <= b_rows;
+                        for (int j = 0; ok && j < ns; ++j) {
+                            int64_t* x = &m[(t * ns + j) * 3];
+                            x[0] = oa;
+                            x[1] = ob + static_cast<int64_t>(j) * st.tn;
+                            x[2] = oc + static_cast<int64_t>(j) * st.tn;
+                        }
                     }
                     if (ok) B.st_tc_mask |= 1u << q;
                 }
+                if (!ok) {  // CUDA-core kernel: one record per task
+                    for (int64_t t = 0; t < B.ntasks; ++t) {
+                        const int64_t* r = rec + t * B.stride;
+                        m[t * 3] = off(st.a, t, r);
+                        m[t * 3 + 1] = off(st.b, t, r);
+                        m[t * 3 + 2] = st_base[st.c] + t * st_tile(st.c);
+                    }
+                }
+                mo += 3 * static_cast<size_t>(B.ntasks) * (st.tc ? st.n / st.tn : 1);
                 ++q;
             }
             PW_CUDA(cudaMalloc(&B.st_rec_dev, all.size() * sizeof(int64_t)));
@@ -1241,20 +1263,28 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
     switch (kind) {
         case ImplKind::Staged: {
             int q = 0;
+            size_t mo = static_cast<size_t>(B.ntasks) * st_stride;
             for (size_t si = 0; si < ki.stages.size(); ++si) {
                 const Stage& st = ki.stages[si];
                 if (st.mm) {
+                    const bool tc = (B.st_tc_mask >> q) & 1u;
                     dev::TaskBatch mtb{};
                     mtb.p[0] = st.a >= 0 ? tb.p[st.a] : st_desc(~st.a);
                     mtb.p[1] = st.b >= 0 ? tb.p[st.b] : st_desc(~st.b);
                     mtb.p[2] = st_desc(st.c);
-                    mtb.rec = B.st_rec_dev + static_cast<size_t>(B.ntasks) * (st_stride + 3 * q);
-                    mtb.ntasks = B.ntasks;
+                    mtb.rec = B.st_rec_dev + mo;
+                    mtb.ntasks = B.ntasks * (tc ? st.n / st.tn : 1);
                     mtb.stride = 3;
                     mtb.nparams = 3;
                     mtb.err = P.err_dev;
-                    e = ((B.st_tc_mask >> q) & 1u) ? dev::launch_matmul_tiles(mtb, 0, workers, P.stream)
-                                                   : dev::launch_matmul_simt(mtb, st.m, st.n, st.k, workers, P.stream);
+                    if (tc) {
+                        mtb.p[1].cols = st.tn;
+                        mtb.p[2].cols = st.tn;
+                        e = dev::launch_matmul_tiles(mtb, 0, workers, P.stream);
+                    } else {
+                        e = dev::launch_matmul_simt(mtb, st.m, st.n, st.k, workers, P.stream);
+                    }
+                    mo += 3 * static_cast<size_t>(B.ntasks) * (st.tc ? st.n / st.tn : 1);
                     ++q;
                 } else {
                     dev::TaskBatch etb = tb;
@@ -1829,7 +1859,8 @@ bool split_stages(KernelImpl& ki, const KernelDef& kd) {
         S.b = pb ? tp.ins[lb].param : ~need_scratch(in.b);
         S.c = need_scratch(in.dst);
         S.tc = pa && pb && S.a != S.b && param_dtype(S.a) == DType::F16 && param_dtype(S.b) == DType::F16 &&
-               S.m == 128 && (S.n == 64 || S.n == 128 || S.n == 256) && S.k >= 64 && S.k % 64 == 0;
+               S.m == 128 && S.n % 64 == 0 && S.k >= 64 && S.k % 64 == 0;
+        S.tn = S.n % 256 == 0 ? 256 : (S.n % 128 == 0 ? 128 : 64);
         S.rows = stage_of[i];  // the stage number until the list is assembled
         stages.push_back(S);
     }

@@ -29,6 +29,7 @@ struct Stage {
     int c = 0;                   // matmul result: scratch tile
     int m = 0, n = 0, k = 0;     // 128 x n = (128 x k) . (k x n) for the tile kernel; any shape on CUDA cores
     bool tc = false;             // f16 params in the tcgen05 tile kernel's shapes
+    int tn = 0;                  // its tile width: each task's n columns run as n / tn tiles of 128 x tn
     dev::TileProgram tp{};       // row stage
     int rows = 0;                // its rows per task
     int jit_state = 0;           // 2 compiled (cubin), 1 loaded, -1 failed

@@ -35,17 +35,20 @@ def test_f32_mlp_stages_bit_exact(require_cuda):
     assert np.array_equal(dev[3].cpu().numpy(), ref[3])
 
 
-@pytest.mark.parametrize("kv_len", [256, 128])
-def test_attention_stages_vs_oracle(kv_len, require_cuda):
+@pytest.mark.parametrize("B,H,QT,kv_len,first", [
+    (2, 3, 2, 256, "matmul 128x256x128 tcgen05"),
+    (2, 3, 2, 128, "matmul 128x128x128 tcgen05"),
+    (1, 2, 1, 1024, "matmul 128x1024x128 tcgen05 (4 tiles of 256)"),  # each task's scores as four 128 x 256 tiles
+])
+def test_attention_stages_vs_oracle(B, H, QT, kv_len, first, require_cuda):
     rng = np.random.default_rng(kv_len)
-    B, H, QT = 2, 3, 2
     plan = attention_plan(B, H, QT, kv_len)
     arrays = attention_arrays(rng, B, H, QT, kv_len)
     ref = [a.copy() for a in arrays]
     cyc = CpuSim(plan).run(ref)
     ex = CudaExecutable(plan)
     k = ex.describe()["kernels"][0]
-    assert k["stages"][0] == f"matmul 128x{kv_len}x128 tcgen05"
+    assert k["stages"][0] == first
     assert k["stages"][2] == f"matmul 128x128x{kv_len} cuda_cores"
     got = [a.copy() for a in arrays]
     assert ex.run_with_symbols(got, {}, {}, {}) == cyc
@@ -53,11 +56,12 @@ def test_attention_stages_vs_oracle(kv_len, require_cuda):
     scale = np.sqrt(np.mean(r * r))
     assert np.all(np.abs(o - r) <= 2e-3 * (np.abs(r) + scale)), float((np.abs(o - r) / (np.abs(r) + scale)).max())
     # fp64 recompute of one tile: softmax(scale * q . k^T) . v
-    q = arrays[0][1, 2, 1].astype(np.float64)
-    kt = arrays[1][1, 2].astype(np.float64)
-    v = arrays[2][1, 2].astype(np.float64)
+    b, h, qt = B - 1, H - 1, QT - 1
+    q = arrays[0][b, h, qt].astype(np.float64)
+    kt = arrays[1][b, h].astype(np.float64)
+    v = arrays[2][b, h].astype(np.float64)
     s = (q @ kt) * np.float64(np.float32(0.088))
     w = np.exp(s - s.max(axis=1, keepdims=True))
     w /= w.sum(axis=1, keepdims=True)
     o64 = w @ v
-    assert np.all(np.abs(got[3][1, 2, 1] - o64) <= 2e-3 * (np.abs(o64) + np.sqrt(np.mean(o64 * o64))))
+    assert np.all(np.abs(got[3][b, h, qt] - o64) <= 2e-3 * (np.abs(o64) + np.sqrt(np.mean(o64 * o64))))
