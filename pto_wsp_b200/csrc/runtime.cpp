@@ -1818,10 +1818,15 @@ bool split_stages(KernelImpl& ki, const KernelDef& kd) {
         }
     }
     const int nstages = st + 1;
-    // a slot loaded straight from a param (no transposed load) is re-read from the param wherever it is needed
+    // a slot loaded straight from a param (no transposed load) is re-read from the param wherever it is needed --
+    // unless the kernel stores to that param, when a later stage would read the stored values instead
+    std::vector<char> stored(dev::kMaxParams, 0);
+    for (int i = 0; i < tp.ninstr; ++i)
+        if (tp.ins[i].op == dev::TP_STORE && tp.ins[i].param >= 0 && tp.ins[i].param < dev::kMaxParams)
+            stored[tp.ins[i].param] = 1;
     auto param_load = [&](int slot) {
         const int d = def[slot];
-        return d >= 0 && tp.ins[d].op == dev::TP_LOAD && tp.ins[d].k == 0 ? d : -1;
+        return d >= 0 && tp.ins[d].op == dev::TP_LOAD && tp.ins[d].k == 0 && !stored[tp.ins[d].param] ? d : -1;
     };
     // uses of each slot by stage
     std::vector<std::vector<int>> used_in(nslots);

@@ -71,3 +71,21 @@ def mlp_arrays(rng, tiles, rows, d, hidden):
     w1 = (rng.standard_normal((d, hidden)) / np.sqrt(d)).astype(np.float32)
     w2 = (rng.standard_normal((hidden, d)) / np.sqrt(hidden)).astype(np.float32)
     return [x, w1, w2, np.full((tiles, rows, d), np.nan, np.float32)]
+
+
+def inout_plan(tiles, n=128):
+    """Per tile: p <- 2 p, then q = A . B + (p as it was): a param stored before a later stage needs its old value,
+    which must come from scratch, not from the param.  Tensors: 0 = P, 1 = A, 2 = B, 3 = Q, all [T, n, n] f32."""
+    kb = KernelBuilder("inout_tile")
+    p = kb.param("p", "f32", n, n)
+    a = kb.param("a", "f32", n, n)
+    b = kb.param("b", "f32", n, n)
+    q = kb.param("q", "f32", n, n)
+    two = kb.op("Constant", [], ("f32", -1, -1), value=2.0)
+    kb.store(p, kb.op("Mul", [p, two], ("f32", n, n)))
+    m = kb.op("Matmul", [a, b], ("f32", n, n))
+    kb.store(q, kb.op("Add", [m, p], ("f32", n, n)))
+    body = _pfor("t", tiles, _task("inout_tile", ["t"], [
+        _targ("p", 0, 3, ["t"]), _targ("a", 1, 3, ["t"]), _targ("b", 2, 3, ["t"]), _targ("q", 3, 3, ["t"])]))
+    tensors = [("f32", [tiles, n, n])] * 4
+    return _plan("inout", tensors, [kb.build()], body, _schedule())

@@ -5,7 +5,7 @@ first contraction runs on tensor cores and is held to the f16-contraction tolera
 
 import numpy as np
 import pytest
-from _staged import attention_arrays, attention_plan, mlp_arrays, mlp_plan
+from _staged import attention_arrays, attention_plan, inout_plan, mlp_arrays, mlp_plan
 from cpu_sim import CpuSim
 
 from pto_wsp_b200.runtime import CudaExecutable
@@ -65,3 +65,18 @@ def test_attention_stages_vs_oracle(B, H, QT, kv_len, first, require_cuda):
     w /= w.sum(axis=1, keepdims=True)
     o64 = w @ v
     assert np.all(np.abs(got[3][b, h, qt] - o64) <= 2e-3 * (np.abs(o64) + np.sqrt(np.mean(o64 * o64))))
+
+
+def test_param_stored_before_a_later_stage_reads_its_old_value(require_cuda):
+    # p is doubled in the first row stage; the last stage adds the old p, kept in scratch (not re-read)
+    rng = np.random.default_rng(5)
+    plan = inout_plan(3)
+    arrays = [rng.standard_normal((3, 128, 128)).astype(np.float32) for _ in range(3)]
+    arrays.append(np.full((3, 128, 128), np.nan, np.float32))
+    ref = [a.copy() for a in arrays]
+    cyc = CpuSim(plan).run(ref)
+    ex = CudaExecutable(plan)
+    assert ex.describe()["kernels"][0]["scratch_tiles"] == 2
+    got = [a.copy() for a in arrays]
+    assert ex.run_with_symbols(got, {}, {}, {}) == cyc
+    assert np.array_equal(got[0], ref[0]) and np.array_equal(got[3], ref[3])

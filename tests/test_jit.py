@@ -118,3 +118,8 @@ def test_kernels_with_contractions_split_into_stages():
         ex.set_option("dry_run", 1)
         assert ex.run_with_symbols([a.copy() for a in arrays], {}, {}, {}) == CpuSim(plan).run(arrays)
         assert ex.timing()["launches"] == 1  # one batch (its stages launch in order on the GPU)
+    # a param the kernel stores to is not re-read by a later stage: its loaded value crosses in scratch
+    from _staged import inout_plan
+
+    k = CudaExecutable(inout_plan(2)).describe()["kernels"][0]
+    assert k["stages"] == ["rows 128", "matmul 128x128x128 cuda_cores", "rows 128"] and k["scratch_tiles"] == 2
