@@ -438,6 +438,7 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
     const int64_t per_task = static_cast<int64_t>(bm_n) * bn_n;
     const int64_t units = b.ntasks * per_task;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const bool a_f32 = A.type == PT_F32, b_f32 = B.type == PT_F32;  // f32 operands: plain loads, no type switch
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
         const int64_t t = u / per_task;
         const int rem = static_cast<int>(u - t * per_task);
@@ -456,7 +457,8 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
                 float v = 0.f;
                 if (r < M && kq < K) {
                     const int64_t off = oa + r * A.s3 + kq * A.s4;
-                    if (off >= 0 && off < A.numel_span) v = load_elem_f(A, off);
+                    if (off >= 0 && off < A.numel_span)
+                        v = a_f32 ? __ldg(reinterpret_cast<const float*>(A.base) + off) : load_elem_f(A, off);
                     else atomicOr(b.err, kErrBounds);
                 }
                 As[kk][mm] = v;
@@ -467,7 +469,8 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
                 float v = 0.f;
                 if (c < N && kq < K) {
                     const int64_t off = ob + kq * B.s3 + c * B.s4;
-                    if (off >= 0 && off < B.numel_span) v = load_elem_f(B, off);
+                    if (off >= 0 && off < B.numel_span)
+                        v = b_f32 ? __ldg(reinterpret_cast<const float*>(B.base) + off) : load_elem_f(B, off);
                     else atomicOr(b.err, kErrBounds);
                 }
                 Bs[kk][nn] = v;
