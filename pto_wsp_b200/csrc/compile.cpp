@@ -798,8 +798,10 @@ std::unique_ptr<Program> compile_program(const char* text, size_t len, int devic
         else if (is_softmax(kd)) ki.kind = ImplKind::Softmax;
         else if (int f = matmul_form(kd)) ki.kind = f == 1 ? ImplKind::Matmul : ImplKind::MatmulAcc;
         else ki.kind = ImplKind::TileProgram;
-        if (ki.kind == ImplKind::TileProgram && split_matmul_epilogue(ki, kd, static_cast<int>(i))) continue;
-        if (ki.kind == ImplKind::TileProgram && split_stages(ki, kd)) {
+        if (ki.kind == ImplKind::TileProgram && w.error.empty() && split_matmul_epilogue(ki, kd, static_cast<int>(i)))
+            continue;
+        // (only a complete tile program is cut: a walker error means an op is missing from it)
+        if (ki.kind == ImplKind::TileProgram && w.error.empty() && split_stages(ki, kd)) {
             // stages (matmuls + fused row programs over HBM scratch) when the tiles exceed shared memory or a
             // contraction is large enough to want its own kernel; small kernels keep the one-launch tile program
             bool staged = !ki.tp_ok;
