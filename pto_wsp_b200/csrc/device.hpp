@@ -78,8 +78,8 @@ struct TPInstr {
     int ival;
 };
 
-constexpr int kTPMaxSlots = 32;
-constexpr int kTPMaxInstr = 64;
+constexpr int kTPMaxSlots = 64;
+constexpr int kTPMaxInstr = 128;
 
 struct TileProgram {
     int ninstr, nslots, smem_words;

@@ -8,7 +8,7 @@ so RMSNorm / softmax of odd widths are checked with the 1e-5 fp32 bar.
 import numpy as np
 import pytest
 from cpu_sim import CpuSim
-from test_jit import rowmax_shift_plan
+from test_jit import long_chain_plan, rowmax_shift_plan
 
 from pto_wsp_b200 import workloads
 from pto_wsp_b200.runtime import CudaExecutable
@@ -109,5 +109,18 @@ def test_one_row_operand_broadcast_over_rows_bit_exact(R, C, require_cuda):
     got = np.full_like(ref, np.nan)
     ex = CudaExecutable(plan)
     assert ex.run_with_symbols([x, v, got], {}, {}, {}) == cyc
+    assert ex.describe()["kernels"][0]["row_kernel"] == "loaded"
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_long_op_chain_bit_exact(require_cuda):
+    rng = np.random.default_rng(9)
+    plan = long_chain_plan(5, 8, 96)
+    x = rng.standard_normal((5, 8, 96)).astype(np.float32)
+    ref = np.full_like(x, np.nan)
+    cyc = CpuSim(plan).run([x, ref])
+    got = np.full_like(x, np.nan)
+    ex = CudaExecutable(plan)
+    assert ex.run_with_symbols([x, got], {}, {}, {}) == cyc
     assert ex.describe()["kernels"][0]["row_kernel"] == "loaded"
     np.testing.assert_array_equal(got, ref)

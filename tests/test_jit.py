@@ -123,3 +123,30 @@ def test_kernels_with_contractions_split_into_stages():
 
     k = CudaExecutable(inout_plan(2)).describe()["kernels"][0]
     assert k["stages"] == ["rows 128", "matmul 128x128x128 cuda_cores", "rows 128"] and k["scratch_tiles"] == 2
+
+
+def long_chain_plan(B, R, C, n_ops=45):
+    """y = x + (x * 1.5 - ...) over a chain of n_ops element-wise ops (more values than a 32-slot program holds)."""
+    kb = KernelBuilder("long_chain")
+    x = kb.param("x", "f32", R, C)
+    y = kb.param("y", "f32", R, C)
+    v = x
+    for i in range(n_ops):
+        c = kb.op("Constant", [], ("f32", -1, -1), value=1.0 + 0.01 * i)
+        v = kb.op(["Mul", "Add", "Sub"][i % 3], [v, c], ("f32", R, C))
+    kb.store(y, kb.op("Add", [v, x], ("f32", R, C)))
+    body = _pfor("b", B, _task("long_chain", ["b"], [_targ("x", 0, 3, ["b"]), _targ("y", 1, 3, ["b"])]))
+    return _plan("long_chain", [("f32", [B, R, C]), ("f32", [B, R, C])], [kb.build()], body, _schedule())
+
+
+def test_long_op_chains_compile():
+    import numpy as np
+    from cpu_sim import CpuSim
+
+    plan = long_chain_plan(3, 8, 64)
+    ex = CudaExecutable(plan)
+    k = ex.describe()["kernels"][0]
+    assert k["impl"] == "tile_program" and k["row_kernel"] == "compiled"
+    x = np.random.default_rng(0).standard_normal((3, 8, 64)).astype(np.float32)
+    ex.set_option("dry_run", 1)
+    assert ex.run_with_symbols([x, np.zeros_like(x)], {}, {}, {}) == CpuSim(plan).run([x, np.zeros_like(x)])
