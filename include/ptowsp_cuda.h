@@ -152,6 +152,9 @@ typedef struct ptowsp_timing {
     uint64_t d2h_bytes;   /* device->host bytes staged */
     uint64_t slot_syncs;  /* device reads made for slot_load_u64 (one per device input read, one per load of
                              data that an enqueued task writes, after those tasks finish) */
+    uint64_t chunks;      /* chunks of an overlapped host-staged run (copies, kernels and copies back on three
+                             streams); 0: staged copies and kernels ran back to back.  A dry run reports the
+                             chunks a run with the same buffers would use. */
 } ptowsp_timing;
 
 PTOWSP_API int ptowsp_cuda_last_timing(const ptowsp_program* prog, ptowsp_timing* out);

@@ -1429,8 +1429,9 @@ bool pipelinable_kind(const KernelImpl& ki, const Batch& B) {
 
 // Per chunk and tensor param, the [lo, hi) element range the chunk's tasks touch, and whether the tiles of a param
 // cover each chunk's range exactly once (dense tiles, sorted offsets adjacent).
-void chunk_ranges(Program& P, LaunchProgram& L, const std::vector<TensorBinding>& T, Batch* B, int C) {
-    if (B->chunk_n == C) return;
+bool chunk_ranges(Program& P, LaunchProgram& L, const std::vector<TensorBinding>& T, Batch* B, int C, bool dry) {
+    if (B->chunk_n == C) return true;
+    if (dry && B->rec.empty()) return false;  // a host-only walk reads no device memory
     const KernelDef& kd = P.plan.kernels[B->kernel];
     const Node& node = *B->node;
     const int np = kd.num_tensor_params;
@@ -1486,11 +1487,20 @@ void chunk_ranges(Program& P, LaunchProgram& L, const std::vector<TensorBinding>
         }
     }
     B->chunk_n = C;
+    return true;
 }
 
-bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, uint64_t& launches) {
+// Whether and how a host-staged run overlaps: the chain of batches, the wave producing each host tensor, the chunk
+// count.  No CUDA call, except reading back the records of a cached task table once (never when `dry`).
+struct PipePlan {
+    std::vector<Batch*> chain;
+    std::vector<int> producer;
+    int C = 0;
+};
+
+bool plan_pipeline(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, bool dry, PipePlan& pp) {
     if (!P.cacheable || P.opt_chunks < 2 || L.waves.empty() || L.waves.size() > 8) return false;
-    std::vector<Batch*> chain;  // one batch per wave
+    std::vector<Batch*>& chain = pp.chain;  // one batch per wave
     int64_t min_tasks = INT64_MAX;
     for (auto& w : L.waves) {
         if (w.batches.size() != 1) return false;
@@ -1504,7 +1514,9 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
     struct Use {
         int wave, param;
     };
-    std::vector<int> producer(T.size(), -1), producer_param(T.size(), -1), first_read(T.size(), INT_MAX);
+    pp.producer.assign(T.size(), -1);
+    std::vector<int>& producer = pp.producer;
+    std::vector<int> producer_param(T.size(), -1), first_read(T.size(), INT_MAX);
     std::vector<std::vector<Use>> reads(T.size());
     size_t host_bytes = 0;
     std::vector<uint8_t> counted(T.size(), 0);
@@ -1539,7 +1551,8 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
     // chunks of at least 4 MiB of host traffic: smaller copies do not reach the copy engines' rate
     const int64_t by_size = std::max<int64_t>(2, static_cast<int64_t>(host_bytes >> 22));
     const int C = static_cast<int>(std::min<int64_t>(std::min<int64_t>(P.opt_chunks, min_tasks), by_size));
-    for (Batch* B : chain) chunk_ranges(P, L, T, B, C);
+    for (Batch* B : chain)
+        if (!chunk_ranges(P, L, T, B, C, dry)) return false;
     auto range = [&](const Batch* B, int c, int ti, int k) {
         const int np = P.plan.kernels[B->kernel].num_tensor_params;
         return B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2 + k];
@@ -1566,6 +1579,22 @@ bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
                     range(chain[u.wave], c, u.param, 1) > range(Wb, c, wp, 1))
                     return false;
     }
+    pp.C = C;
+    return true;
+}
+
+bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, uint64_t& launches) {
+    PipePlan pp;
+    if (!plan_pipeline(P, L, T, false, pp)) return false;
+    const std::vector<Batch*>& chain = pp.chain;
+    const std::vector<int>& producer = pp.producer;
+    const int C = pp.C;
+    const int nw = static_cast<int>(chain.size());
+    auto range = [&](const Batch* B, int c, int ti, int k) {
+        const int np = P.plan.kernels[B->kernel].num_tensor_params;
+        return B->chunk_ranges[(static_cast<size_t>(c) * np + ti) * 2 + k];
+    };
+    P.timing.chunks = static_cast<uint64_t>(C);
 
     if (!P.h2d_stream) {
         PW_CUDA(cudaStreamCreateWithFlags(&P.h2d_stream, cudaStreamNonBlocking));
@@ -2186,6 +2215,9 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
             P.timing.waves += w.batches.empty() ? 0 : 1;
             P.timing.launches += w.batches.size();
         }
+        PipePlan pp;  // would a run with these host buffers overlap its copies (kernels with a layout check on their
+                      // first launch -- tcgen05 matmul, indexer scoring -- pipeline from their second run)?
+        if (P.cacheable && plan_pipeline(P, *L, T, true, pp)) P.timing.chunks = static_cast<uint64_t>(pp.C);
         return L->makespan;
     }
 

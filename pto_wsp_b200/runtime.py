@@ -73,6 +73,7 @@ class Timing(C.Structure):
         ("h2d_bytes", C.c_uint64),
         ("d2h_bytes", C.c_uint64),
         ("slot_syncs", C.c_uint64),
+        ("chunks", C.c_uint64),
     ]
 
 

@@ -201,3 +201,70 @@ def test_tensor_driven_tiers_are_device_selected_and_cacheable():
     want = CpuSim(plan).run([sel, x, out.copy()])
     ex.set_option("dry_run", 1)
     assert ex.run_with_symbols([sel, x, out], {}, {}, {}) == want
+
+
+def _two_wave_plan(B, T, R, C, swap=False, write_back_x=False):
+    """Wave 0: M[b, t] = X[b, t] * 2; wave 1: Y[b, t] = M[b, t] + 1 (loops t-outer when `swap`; when
+    `write_back_x` the second kernel writes X instead of Y).  Tensors: 0 = X, 1 = M, 2 = Y, all [B, T, R, C] f32."""
+    from pto_wsp_b200.workloads import KernelBuilder, _pfor, _plan, _schedule, _targ, _task
+
+    k1 = KernelBuilder("scale")
+    x = k1.param("x", "f32", R, C)
+    m = k1.param("m", "f32", R, C)
+    two = k1.op("Constant", [], ("f32", -1, -1), value=2.0)
+    k1.store(m, k1.op("Mul", [x, two], ("f32", R, C)))
+    k2 = KernelBuilder("shift")
+    m2 = k2.param("m", "f32", R, C)
+    y = k2.param("y", "f32", R, C)
+    one = k2.op("Constant", [], ("f32", -1, -1), value=1.0)
+    k2.store(y, k2.op("Add", [m2, one], ("f32", R, C)))
+    n1 = _pfor("b", B, _pfor("t", T, _task("scale", ["b", "t"], [_targ("x", 0, 4, ["b", "t"]),
+                                                                 _targ("m", 1, 4, ["b", "t"])])))
+    task2 = _task("shift", ["b2", "t2"], [_targ("m", 1, 4, ["b2", "t2"]),
+                                          _targ("y", 0 if write_back_x else 2, 4, ["b2", "t2"])])
+    n2 = _pfor("t2", T, _pfor("b2", B, task2)) if swap else _pfor("b2", B, _pfor("t2", T, task2))
+    shape = [B, T, R, C]
+    return _plan("two_wave", [("f32", shape)] * 3, [k1.build(), k2.build()], {"kind": "combine", "children": [n1, n2]},
+                 _schedule())
+
+
+def test_dry_run_reports_overlapped_chunks():
+    import numpy as np
+
+    # one batch, 64 MiB in + 64 MiB out: 32 chunks (4 MiB of host traffic each at least, at most 32)
+    ex = runtime.CudaExecutable(workloads.softmax_plan(2, 1024))
+    ex.set_option("dry_run", 1)
+    x = np.zeros((2, 1024, 32, 256), np.float32)
+    ex.run_with_symbols([x, np.zeros_like(x)], {}, {}, {})
+    assert ex.timing()["chunks"] == 32
+    ex.set_option("pipeline_chunks", 8)
+    ex.run_with_symbols([x, np.zeros_like(x)], {}, {}, {})
+    assert ex.timing()["chunks"] == 8
+    ex.set_option("pipeline_chunks", 1)
+    ex.run_with_symbols([x, np.zeros_like(x)], {}, {}, {})
+    assert ex.timing()["chunks"] == 0
+    # small host buffers: not worth the extra streams
+    ex = runtime.CudaExecutable(workloads.softmax_plan(2, 16))
+    ex.set_option("dry_run", 1)
+    x = np.zeros((2, 16, 32, 256), np.float32)
+    ex.run_with_symbols([x, np.zeros_like(x)], {}, {}, {})
+    assert ex.timing()["chunks"] == 0
+
+
+@pytest.mark.parametrize("swap,write_back_x,chunks", [(False, False, 16), (True, False, 0), (False, True, 0)])
+def test_dry_run_chain_pipelining_rules(swap, write_back_x, chunks):
+    # two waves chunk by chunk when chunk c of the reader reads inside what chunk c of the writer wrote (same loop
+    # order); not when the reader walks the intermediate in another order, nor when a wave writes what an
+    # earlier wave read
+    import numpy as np
+
+    B, T, R, C = 8, 128, 32, 256  # 32 MiB per tensor
+    ex = runtime.CudaExecutable(_two_wave_plan(B, T, R, C, swap, write_back_x))
+    ex.set_option("dry_run", 1)
+    ex.set_option("pipeline_chunks", 16)
+    arrays = [np.zeros((B, T, R, C), np.float32) for _ in range(3)]
+    ex.run_with_symbols(arrays, {}, {}, {})
+    t = ex.timing()
+    assert t["waves"] == 2 and t["chunks"] == chunks
+    if not write_back_x:  # M is written in full before it is read: never staged in
+        assert t["h2d_bytes"] == arrays[0].nbytes

@@ -102,6 +102,7 @@ def test_pipelined_bgemm(require_cuda):
         t = ex.timing()
         assert t["h2d_bytes"] == a.nbytes + b.nbytes and t["d2h_bytes"] == c.nbytes
         assert (t["launches"] == 16) == (i == 1)  # pipelined once the layout check has run
+        assert t["chunks"] == (16 if i == 1 else 0)
         np.testing.assert_allclose(c, c1, rtol=1e-5, atol=1e-5)
     ref = a[0].astype(np.float64) @ b[0].astype(np.float64)
     assert np.max(np.abs(c[0] - ref) / (np.abs(ref) + np.sqrt(np.mean(ref ** 2)))) < 2e-3
@@ -127,5 +128,6 @@ def test_pipelined_indexer_chain(require_cuda):
         assert t["h2d_bytes"] == sum(a.nbytes for a in arrays[:3])
         assert t["d2h_bytes"] == arrays[3].nbytes + arrays[4].nbytes
         assert (t["launches"] == 16) == (i == 1)  # 8 chunks x (scoring, top-k) once the layout check has run
+        assert t["chunks"] == (8 if i == 1 else 0)
         np.testing.assert_allclose(got[3], serial[3], rtol=1e-6, atol=1e-6)
         assert np.array_equal(got[4], serial[4])
