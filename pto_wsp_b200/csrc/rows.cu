@@ -450,8 +450,13 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
         for (int i = 0; i < 4 * HM; ++i)
 #pragma unroll
             for (int j = 0; j < 4 * HN; ++j) acc[i][j] = 0.f;
-        for (int k0 = 0; k0 < K; k0 += kSimtBK) {
-            for (int e = threadIdx.x; e < kSimtBK * BM; e += 256) {
+        // the next k slice's global loads are issued before the current slice's FMAs (registers ra / rb)
+        constexpr int NA = kSimtBK * BM / 256, NB = kSimtBK * BN / 256;
+        float ra[NA], rb[NB];
+        auto fetch = [&](int k0) {
+#pragma unroll
+            for (int q = 0; q < NA; ++q) {
+                const int e = threadIdx.x + q * 256;
                 const int mm = e / kSimtBK, kk = e % kSimtBK;  // consecutive threads: consecutive k of a row of A
                 const int r = m0 + mm, kq = k0 + kk;
                 float v = 0.f;
@@ -461,9 +466,11 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
                         v = a_f32 ? __ldg(reinterpret_cast<const float*>(A.base) + off) : load_elem_f(A, off);
                     else atomicOr(b.err, kErrBounds);
                 }
-                As[kk][mm] = v;
+                ra[q] = v;
             }
-            for (int e = threadIdx.x; e < kSimtBK * BN; e += 256) {
+#pragma unroll
+            for (int q = 0; q < NB; ++q) {
+                const int e = threadIdx.x + q * 256;
                 const int kk = e / BN, nn = e % BN;  // consecutive threads: consecutive n of a row of B
                 const int c = n0 + nn, kq = k0 + kk;
                 float v = 0.f;
@@ -473,9 +480,23 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(TaskBatch b, int M, in
                         v = b_f32 ? __ldg(reinterpret_cast<const float*>(B.base) + off) : load_elem_f(B, off);
                     else atomicOr(b.err, kErrBounds);
                 }
-                Bs[kk][nn] = v;
+                rb[q] = v;
+            }
+        };
+        fetch(0);
+        for (int k0 = 0; k0 < K; k0 += kSimtBK) {
+#pragma unroll
+            for (int q = 0; q < NA; ++q) {
+                const int e = threadIdx.x + q * 256;
+                As[e % kSimtBK][e / kSimtBK] = ra[q];
+            }
+#pragma unroll
+            for (int q = 0; q < NB; ++q) {
+                const int e = threadIdx.x + q * 256;
+                Bs[e / BN][e % BN] = rb[q];
             }
             __syncthreads();
+            if (k0 + kSimtBK < K) fetch(k0 + kSimtBK);
             const int kn = min(kSimtBK, K - k0);
             for (int kk = 0; kk < kn; ++kk) {
                 float av[4 * HM], bv[4 * HN];
