@@ -1907,6 +1907,8 @@ bool split_stages(KernelImpl& ki, const KernelDef& kd) {
         if (later && param_load(sl) < 0) need_scratch(sl);
     }
     if (np + static_cast<int>(scratch.size()) > dev::kMaxParams) return false;
+    for (int sl = 0; sl < nslots; ++sl)  // scratch tiles hold f32 values only
+        if (scratch_of[sl] >= 0 && tp.slots[sl].word != dev::W_F32) return false;
     // row stages: the stage's own instructions, led by loads of what earlier stages left in scratch or in params,
     // followed by stores of what later stages need
     std::vector<Stage> out;
