@@ -130,12 +130,15 @@ PTOWSP_API const char* ptowsp_cuda_last_error(void);
  * Until this is called a program uses a private non-blocking stream. */
 PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
 
-/* Integer options: "pipeline_chunks" (a static single-batch workload whose
- * host tensors hold 64 MiB or more, with outputs that are fully overwritten and
- * not read, runs as up to this many chunks of tasks whose host->device copies,
+/* Integer options: "pipeline_chunks" (a static workload with one batch per
+ * wave whose host tensors hold 64 MiB or more, with written tensors fully
+ * overwritten by one wave and read only by later ones, runs as up to this many
+ * chunks of tasks whose host->device copies,
  * kernels and device->host copies overlap on three streams; chunks carry at
  * least 4 MiB of host traffic; 1 turns it off; default 32.  Pinned host memory
- * is needed for the copies to overlap), "cache_plans" (reuse the task table
+ * is needed for the copies to overlap), "stage_scratch_mb" (the HBM scratch a
+ * kernel cut into stages may use: its stages run over groups of tasks whose
+ * crossing values fit, default 2048), "cache_plans" (reuse the task table
  * of static workloads across runs, default 1), "sync" (0: when every tensor
  * is device memory, return without waiting; errors surface at the next
  * synchronous run, default 1), "dry_run" (1: walk the task loop on the host

@@ -88,6 +88,7 @@ int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value)
     if (!prog || !prog->p || !key) return PTOWSP_ERR_ARG;
     auto& p = *prog->p;
     if (!std::strcmp(key, "pipeline_chunks")) p.opt_chunks = value < 1 ? 1 : value;
+    else if (!std::strcmp(key, "stage_scratch_mb")) p.opt_stage_scratch_mb = value < 1 ? 1 : value;
     else if (!std::strcmp(key, "cache_plans")) {
         p.opt_cache = value != 0;
         if (!p.opt_cache) p.cached.reset();

@@ -1170,9 +1170,18 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
         return n;
     };
     bool st_rows_ok = rows_ok;
+    // the stages run over groups of st_group tasks, so that the scratch stays within the stage_scratch_mb budget
+    // (2 GiB by default) whatever the batch; the group is fixed when the batch's records are built
+    int64_t st_group = B.ntasks;
     if (kind == ImplKind::Staged) {
+        int64_t per_task = 0;
+        for (int j = 0; j < st_S; ++j) per_task += st_tile(j);
+        const int64_t budget = (P.opt_stage_scratch_mb << 20) / static_cast<int64_t>(sizeof(float));
+        st_group = std::max<int64_t>(1, std::min<int64_t>(B.ntasks, budget / std::max<int64_t>(per_task, 1)));
+        if (B.st_ok > 0) st_group = B.st_group;
+        B.st_group = st_group;
         for (int j = 0; j < st_S; ++j) {
-            st_base[j + 1] = st_base[j] + B.ntasks * st_tile(j);
+            st_base[j + 1] = st_base[j] + st_group * st_tile(j);
             if (ki.scratch_tiles[j].second % 4) st_rows_ok = false;
         }
         st_scr = static_cast<char*>(ensure_scratch(P, static_cast<size_t>(st_base[st_S]) * sizeof(float)));
@@ -1192,7 +1201,7 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                 const int64_t* r = rec + t * B.stride;
                 int64_t* o = &all[t * st_stride];
                 for (int j = 0; j < st_np; ++j) o[j] = r[j];
-                for (int j = 0; j < st_S; ++j) o[st_np + j] = st_base[j] + t * st_tile(j);
+                for (int j = 0; j < st_S; ++j) o[st_np + j] = st_base[j] + (t % st_group) * st_tile(j);
                 for (int j = st_np; j < B.stride; ++j) o[j + st_S] = r[j];
             }
             B.st_tc_mask = 0;
@@ -1202,7 +1211,7 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                 if (!st.mm) continue;
                 int64_t* m = &all[mo];
                 auto off = [&](int src, int64_t t, const int64_t* r) {
-                    return src >= 0 ? r[src] : st_base[~src] + t * st_tile(~src);
+                    return src >= 0 ? r[src] : st_base[~src] + (t % st_group) * st_tile(~src);
                 };
                 bool ok = st.tc;
                 if (ok) {
@@ -1222,7 +1231,7 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                     for (int64_t t = 0; ok && t < B.ntasks; ++t) {
                         const int64_t* r = rec + t * B.stride;
                         const int64_t oa = off(st.a, t, r), ob = off(st.b, t, r);
-                        const int64_t oc = st_base[st.c] + t * st_tile(st.c);
+                        const int64_t oc = st_base[st.c] + (t % st_group) * st_tile(st.c);
                         ok = oa >= 0 && ob >= 0 && oa % 8 == 0 && ob % 8 == 0 && (oa % A.s3) + st.k <= A.s3 &&
                              (oa / A.s3) + 128 <= a_rows && (ob % Bm.s3) + st.n <= Bm.s3 && (ob / Bm.s3) + st.k <= b_rows;
                         for (int j = 0; ok && j < ns; ++j) {
@@ -1239,7 +1248,7 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
                         const int64_t* r = rec + t * B.stride;
                         m[t * 3] = off(st.a, t, r);
                         m[t * 3 + 1] = off(st.b, t, r);
-                        m[t * 3 + 2] = st_base[st.c] + t * st_tile(st.c);
+                        m[t * 3 + 2] = st_base[st.c] + (t % st_group) * st_tile(st.c);
                     }
                 }
                 mo += 3 * static_cast<size_t>(B.ntasks) * (st.tc ? st.n / st.tn : 1);
@@ -1262,41 +1271,48 @@ void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBind
     }
     switch (kind) {
         case ImplKind::Staged: {
-            int q = 0;
-            size_t mo = static_cast<size_t>(B.ntasks) * st_stride;
-            for (size_t si = 0; si < ki.stages.size(); ++si) {
-                const Stage& st = ki.stages[si];
-                if (st.mm) {
-                    const bool tc = (B.st_tc_mask >> q) & 1u;
-                    dev::TaskBatch mtb{};
-                    mtb.p[0] = st.a >= 0 ? tb.p[st.a] : st_desc(~st.a);
-                    mtb.p[1] = st.b >= 0 ? tb.p[st.b] : st_desc(~st.b);
-                    mtb.p[2] = st_desc(st.c);
-                    mtb.rec = B.st_rec_dev + mo;
-                    mtb.ntasks = B.ntasks * (tc ? st.n / st.tn : 1);
-                    mtb.stride = 3;
-                    mtb.nparams = 3;
-                    mtb.err = P.err_dev;
-                    if (tc) {
-                        mtb.p[1].cols = st.tn;
-                        mtb.p[2].cols = st.tn;
-                        e = dev::launch_matmul_tiles(mtb, 0, workers, P.stream);
+            bool first = true;
+            for (int64_t t0 = 0; t0 < B.ntasks && e == cudaSuccess; t0 += st_group) {
+                const int64_t n = std::min<int64_t>(st_group, B.ntasks - t0);
+                int q = 0;
+                size_t mo = static_cast<size_t>(B.ntasks) * st_stride;
+                for (size_t si = 0; si < ki.stages.size(); ++si) {
+                    const Stage& st = ki.stages[si];
+                    if (!first) launches++;  // every launch but the last is counted here, the last below
+                    first = false;
+                    if (st.mm) {
+                        const bool tc = (B.st_tc_mask >> q) & 1u;
+                        const int64_t split = tc ? st.n / st.tn : 1;
+                        dev::TaskBatch mtb{};
+                        mtb.p[0] = st.a >= 0 ? tb.p[st.a] : st_desc(~st.a);
+                        mtb.p[1] = st.b >= 0 ? tb.p[st.b] : st_desc(~st.b);
+                        mtb.p[2] = st_desc(st.c);
+                        mtb.rec = B.st_rec_dev + mo + static_cast<size_t>(t0 * split) * 3;
+                        mtb.ntasks = n * split;
+                        mtb.stride = 3;
+                        mtb.nparams = 3;
+                        mtb.err = P.err_dev;
+                        if (tc) {
+                            mtb.p[1].cols = st.tn;
+                            mtb.p[2].cols = st.tn;
+                            e = dev::launch_matmul_tiles(mtb, 0, workers, P.stream);
+                        } else {
+                            e = dev::launch_matmul_simt(mtb, st.m, st.n, st.k, workers, P.stream);
+                        }
+                        mo += 3 * static_cast<size_t>(B.ntasks) * (st.tc ? st.n / st.tn : 1);
+                        ++q;
                     } else {
-                        e = dev::launch_matmul_simt(mtb, st.m, st.n, st.k, workers, P.stream);
+                        dev::TaskBatch etb = tb;
+                        for (int j = 0; j < st_S; ++j) etb.p[st_np + j] = st_desc(j);
+                        etb.nparams = st_np + st_S;
+                        etb.stride = st_stride;
+                        etb.rec = B.st_rec_dev + static_cast<size_t>(t0) * st_stride;
+                        etb.ntasks = n;
+                        e = jit::launch_row_kernel(st_rows_ok && st.fn_vec ? st.fn_vec : st.fn, etb, st.rows, workers,
+                                                   P.stream);
                     }
-                    mo += 3 * static_cast<size_t>(B.ntasks) * (st.tc ? st.n / st.tn : 1);
-                    ++q;
-                } else {
-                    dev::TaskBatch etb = tb;
-                    for (int j = 0; j < st_S; ++j) etb.p[st_np + j] = st_desc(j);
-                    etb.nparams = st_np + st_S;
-                    etb.stride = st_stride;
-                    etb.rec = B.st_rec_dev;
-                    e = jit::launch_row_kernel(st_rows_ok && st.fn_vec ? st.fn_vec : st.fn, etb, st.rows, workers,
-                                               P.stream);
+                    if (e != cudaSuccess) break;
                 }
-                if (e != cudaSuccess) break;
-                if (si + 1 < ki.stages.size()) launches++;
             }
             break;
         }

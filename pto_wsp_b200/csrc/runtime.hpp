@@ -138,6 +138,7 @@ struct Batch {  // tasks of one kernel inside one wave
     int64_t* st_rec_dev = nullptr;
     int8_t st_ok = -1;
     uint32_t st_tc_mask = 0;           // matmul stages (in order) that run on the tcgen05 tile kernel
+    int64_t st_group = 0;              // tasks per group of stage launches (scratch offsets repeat per group)
     Batch() = default;
     Batch(Batch&& o) noexcept { *this = std::move(o); }
     Batch& operator=(Batch&& o) noexcept {
@@ -149,7 +150,7 @@ struct Batch {  // tasks of one kernel inside one wave
         ep_mm_rec_dev = o.ep_mm_rec_dev; ep_rec_dev = o.ep_rec_dev; ep_ok = o.ep_ok;
         ep_unit_rec_dev = o.ep_unit_rec_dev; ep_nunits = o.ep_nunits;
         o.ep_unit_rec_dev = nullptr;
-        st_rec_dev = o.st_rec_dev; st_ok = o.st_ok; st_tc_mask = o.st_tc_mask;
+        st_rec_dev = o.st_rec_dev; st_ok = o.st_ok; st_tc_mask = o.st_tc_mask; st_group = o.st_group;
         o.st_rec_dev = nullptr;
         sel = o.sel; sel_tensor = o.sel_tensor; sel_rows = std::move(o.sel_rows); sel_row_words = o.sel_row_words;
         sel_dev = o.sel_dev; sel_tree_dev = o.sel_tree_dev;
@@ -201,7 +202,7 @@ struct Program {
     std::vector<cudaEvent_t> pipe_events;
     int* err_dev = nullptr;
     int status = 0;
-    int64_t opt_cache = 1, opt_chunks = 32, opt_sync = 1, opt_dry = 0;
+    int64_t opt_cache = 1, opt_chunks = 32, opt_sync = 1, opt_dry = 0, opt_stage_scratch_mb = 2048;
     std::vector<char*> dev_bufs;         // host-staged tensor buffers (by tensor id)
     std::vector<size_t> dev_caps;
     void* scratch = nullptr;

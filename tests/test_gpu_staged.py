@@ -33,6 +33,13 @@ def test_f32_mlp_stages_bit_exact(require_cuda):
     dev = [torch.from_numpy(a.copy()).cuda() for a in arrays]
     ex.run_with_symbols(dev, {}, {}, {})
     assert np.array_equal(dev[3].cpu().numpy(), ref[3])
+    # a 1 MiB scratch budget: 256 KB of crossing values per task, so the stages run over groups of 4 tasks
+    ex = CudaExecutable(plan)
+    ex.set_option("stage_scratch_mb", 1)
+    got = [a.copy() for a in arrays]
+    assert ex.run_with_symbols(got, {}, {}, {}) == cyc
+    assert np.array_equal(got[3], ref[3])
+    assert ex.timing()["launches"] == 8  # groups of 4 and 2 tasks x 4 stages
 
 
 @pytest.mark.parametrize("B,H,QT,kv_len,first", [
