@@ -1,25 +1,37 @@
 #!/usr/bin/env python3
-"""Benchmark of the PTO-WSP cuda_sm100a task loop (one JSON line on rank 0).
+"""Benchmark of the PTO-WSP cuda_sm100a task loop: all five BASELINE configs, one JSON line on rank 0.
 
-Default workload: BASELINE config 2, the row-softmax tile workload
-X[32,2048,32,256] f32 (Tile[32,256], P(batch) x P(tiles)), through the
-reference-facing C ABI.  A *step* is one pass of the task loop over the whole
-workload.
+A *step* is one pass of the task loop over one whole config (its global batch).  The headline line is config 2
+(row softmax, X[32,2048,32,256] f32); configs 1, 3, 4 and 5 ride in the same line under ``workloads``, each with
+its own ``value``, ``ms_per_step``, ``roofline``, ``e2e``, ``cpu_baseline`` and ``clocks``.  ``--workload NAME``
+runs one config alone.
 
-* ``value``  -- GB/s (algorithmic bytes: 2 x 4 B per element) with X and Y
-  resident in HBM; K back-to-back steps timed with CUDA events on the launch
-  stream, max over ranks.  Inputs (2 GiB) exceed L2 (126 MB), so no flush.
-* ``e2e``    -- the same metric through the same call with pinned host numpy
-  buffers: every step stages X host->device and Y device->host.
-* ``roofline`` -- achieved bytes per launch / measured launch time vs the
-  measured HBM copy peak (MEASURED_PEAKS.json); ``traffic`` from the ncu
-  summary in profiles/ when one exists.
-* ``cpu_baseline`` -- the C port of the CPU-sim loops (oracle/cpu_kernels.c) on
-  the host cores, rank 0 at N=1, bounded sample.
+* ``value`` -- whole-job throughput (algorithmic GB/s or TFLOP/s, formulas per config below) with every input
+  already in HBM: K back-to-back steps through ``ShardedExecutable.run_with_symbols`` (the reference-facing
+  ``CodegenExecutable`` surface over the C ABI), timed with CUDA events on the launch stream between a barrier +
+  synchronize on both sides, max over ranks.  Every config's inputs exceed L2 (126 MB) except config 5's keys
+  (128 MiB), so no flush is needed.
+* ``e2e``   -- the same metric through the same call with pinned host numpy buffers: each step stages the
+  inputs host->device and the outputs device->host (bytes per step from the runtime's own counters).
+* ``roofline`` -- the dominant kernel: its algorithmic work per launch / its average launch time, measured with
+  CUDA events bracketing its launches on the launch stream during the timed region (runtime option
+  ``kernel_events``), against the measured peak in MEASURED_PEAKS.json; ``traffic`` = ncu DRAM bytes per launch
+  from profiles/traffic.json (scaled to this rank's share of the units).
+* ``cpu_baseline`` -- the C port of the CPU-sim task bodies (oracle/cpu_kernels.c) on the host cores, rank 0 at
+  N=1, bounded sample.
+* ``--impl reference`` -- the reference arm: the CPU implementation of the same task loops on the host cores
+  (all threads), same metric and config, one line with the same ``workloads`` layout; rank 0 only.
 
-``--impl reference`` times only that CPU implementation (all host threads) and
-prints its own line.  Multi-GPU (torchrun): each rank runs the same per-rank
-shard (weak scaling, no data-path collective).
+Multi-GPU (torchrun, one rank per GPU): every rank runs its ``ShardedExecutable`` share of the ONE global config
+(strong scaling): contiguous blocks of the outer ``P(batch)`` axis for configs 1, 2, 3 and 5, greedy LPT by KV
+length for config 4.  No data-path collective: NCCL carries only the barriers and the max-over-ranks timing.
+
+Algorithmic work per step (global):
+  1 RMSNorm   8 B per element (read x, write y), 64 x 4096 x 16 x 128 elements
+  2 softmax   8 B per element, 32 x 2048 x 32 x 256 elements
+  3 bgemm     2 M N K flop per batch element, 64 x 2048^3
+  4 decode    K + V bytes of every request's tokens (L x 8 heads x 128 x 2 B x 2) + Q and O (64 x 32 x 128 x 2 B x 2)
+  5 indexer   scoring flop 2 x 512 x 128 per key per batch element (16 x 32768 keys); the top-k runs in the step
 """
 
 from __future__ import annotations
@@ -31,26 +43,15 @@ import json
 import os
 import statistics
 import subprocess
-import threading
 import sys
+import threading
 import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-WORKLOADS = {
-    "softmax": {"config": "config 2: row softmax Tile[32,256] f32, X[32,2048,32,256]", "batch": 32, "tiles": 2048,
-                "rows": 32, "cols": 256},
-    "rmsnorm": {"config": "config 1: RMSNorm Tile[16,128] f32, X[64,4096,16,128] (GPU scale)", "batch": 64,
-                "tiles": 4096, "rows": 16, "cols": 128},
-    "bgemm": {"config": "config 3: bgemm 64 x (2048x2048x2048), f16 in, f32 acc/out, 128x128 output tiles",
-              "batch": 64, "m": 2048, "n": 2048, "k": 2048},
-    "decode": {"config": "config 4: paged GQA decode, 64 requests, 32 q / 8 kv heads, d=128, f16, page 16, "
-                         "KV len U[512,8192]", "batch": 64},
-    "indexer": {"config": "config 5: lightning indexer 16 batches x 8 queries, 64 heads, d=128, 32768 keys, "
-                          "top-2048", "batch": 16, "context": 32768, "topk": 2048},
-}
+ORDER = ["softmax", "rmsnorm", "bgemm", "decode", "indexer"]  # the first is the headline
 
 
 def _env_int(k: str, d: int) -> int:
@@ -70,22 +71,26 @@ def peaks(key: str = "hbm_gbs") -> tuple[float, str]:
     return (6650.0 if key == "hbm_gbs" else 1590.0), "fallback"
 
 
-def traffic_from_profiles(kernel: str, workload: str, batch_override=None) -> float | None:
-    """DRAM bytes per launch of the full workload from the committed ncu summaries (None for --batch runs)."""
+def traffic_from_profiles(key: str) -> float | None:
+    """ncu DRAM bytes of one full-config launch of the dominant kernel (profiles/traffic.json)."""
     p = ROOT / "profiles" / "traffic.json"
-    if batch_override is not None or not p.exists():
+    if not p.exists():
         return None
     try:
-        d = json.loads(p.read_text())
-        v = d.get(f"{workload}:{kernel}")
+        v = json.loads(p.read_text()).get(key)
         return float(v["bytes_per_launch"]) if v else None
     except Exception:  # noqa: BLE001
         return None
 
 
+# ---------------------------------------------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------------------------------------------
+
+
 class NvmlClockSampler:
     """SM clock, power and clock-event reasons read through NVML every millisecond while the timed region runs
-    (read-only queries; short timed regions still get several samples).  Falls back to nvidia-smi."""
+    (read-only queries).  Falls back to nvidia-smi."""
 
     REASONS = [("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
                ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
@@ -199,7 +204,6 @@ class ClockSampler:
 
 
 def _pci_bus_id(torch, dev) -> str | None:
-    """The NVML-style PCI bus id of a torch CUDA device, when torch exposes it."""
     try:
         p = torch.cuda.get_device_properties(dev)
         return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
@@ -216,598 +220,731 @@ def gpu_index(local_rank: int) -> int:
     return local_rank
 
 
-def make_softmax_inputs(torch, B, T, R, Cc, device, seed=0):
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    x = torch.randn((B, T, R, Cc), generator=g, device=device, dtype=torch.float32) * 4.0
-    mask = torch.rand((B, T, R, Cc), generator=g, device=device) < 0.01
-    x[mask] = 30.0
-    return x
-
-
-def make_rmsnorm_inputs(torch, B, T, R, Cc, device, seed=0):
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    return torch.randn((B, T, R, Cc), generator=g, device=device, dtype=torch.float32)
-
-
-def cpu_baseline(kind: str, x_host, rows: int, cols: int, budget_s: float = 12.0) -> dict:
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
-
-    import cpu_native
-
-    nth = cpu_native.threads()
-    tiles_total = x_host.size // (rows * cols)
-    flat = x_host.reshape(tiles_total, rows, cols)
-    n = min(tiles_total, 2048)
-    y = np.empty_like(flat[:n])
-    t0 = time.perf_counter()
-    cpu_native.row_tiles(kind, np.ascontiguousarray(flat[:n]), y, rows, cols, nth)
-    dt = time.perf_counter() - t0
-    # grow the sample to ~budget_s of CPU work (bounded by the workload)
-    n2 = int(min(tiles_total, max(n, n * budget_s / max(dt, 1e-6) * 0.5)))
-    passes = max(1, min(8, int(budget_s / max(dt * n2 / n, 1e-6))))
-    y = np.empty((n2, rows, cols), np.float32)
-    t0 = time.perf_counter()
-    for _ in range(passes):
-        cpu_native.row_tiles(kind, flat[:n2], y, rows, cols, nth)
-    dt = time.perf_counter() - t0
-    gbs = passes * n2 * rows * cols * 8 / dt / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": nth, "kind": "port",
-            "sample": f"{passes} pass(es) over {n2} of {tiles_total} tiles ({n2 * rows * cols * 4 / 2**20:.0f} MiB in), "
-                      f"{dt:.2f} s, C port of the CPU-sim tile loop (oracle/cpu_kernels.c), {nth} threads"}
-
-
-def run_reference(args, wl: dict, rank: int) -> None:
-    if rank != 0:
-        return
-    import numpy as np
-
+def _cpu_native():
     sys.path.insert(0, str(ROOT / "oracle"))
     import cpu_native
 
-    rows, cols = wl["rows"], wl["cols"]
-    tiles = wl["batch"] * wl["tiles"]
-    sample_tiles = min(tiles, 8192)
-    rng = np.random.default_rng(0)
-    x = (rng.standard_normal((sample_tiles, rows, cols), dtype=np.float32) * (4.0 if args.workload == "softmax" else 1.0))
-    if args.workload == "softmax":
-        x[rng.random(x.shape) < 0.01] = 30.0
-    y = np.empty_like(x)
-    nth = cpu_native.threads()
-    for _ in range(args.warmup):
-        cpu_native.row_tiles(args.workload, x, y, rows, cols, nth)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        cpu_native.row_tiles(args.workload, x, y, rows, cols, nth)
-    dt = time.perf_counter() - t0
-    gbs = sample_tiles * rows * cols * 8 * args.steps / dt / 1e9
-    line = {
-        "impl": "reference", "metric": f"{args.workload} task-loop throughput (algorithmic HBM bytes)",
-        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy)",
-        "config": {"workload": wl["config"], "sample_tiles_per_step": sample_tiles},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nth, "kind": "port",
-                         "sample": f"{sample_tiles} tiles per step of {tiles}; C port of the CPU-sim tile loop "
-                                   f"(oracle/cpu_kernels.c), {nth} threads (reference CPU-sim needs the absent pto-isa)"},
-        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    return cpu_native
 
 
-def gemm_cpu_baseline(a_host, b_host, tiles: int = 128, budget_s: float = 10.0) -> dict:
-    """C port of the CPU-sim gemm task (TLOAD, TMATMUL f32 acc, TSTORE) on a bounded batch sample."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
-
-    import cpu_native
-
-    nth = cpu_native.threads()
-    B, M, K = a_host.shape
-    N = b_host.shape[2]
-    nb = 1
-    t0 = time.perf_counter()
-    c = np.empty((nb, M, N), np.float32)
-    cpu_native.gemm_tiles(a_host[:nb], b_host[:nb], c, tiles, tiles, nth)
-    dt = time.perf_counter() - t0
-    nb2 = int(max(1, min(B, budget_s / max(dt, 1e-6))))
-    if nb2 > 1:
-        c = np.empty((nb2, M, N), np.float32)
-        t0 = time.perf_counter()
-        cpu_native.gemm_tiles(a_host[:nb2], b_host[:nb2], c, tiles, tiles, nth)
-        dt = time.perf_counter() - t0
-    else:
-        nb2 = nb
-    tf = 2.0 * nb2 * M * N * K / dt / 1e12
-    return {"value": round(tf, 5), "unit": "TFLOP/s", "cores": nth, "kind": "port",
-            "sample": f"{nb2} of {B} batch elements ({dt:.2f} s), C port of the CPU-sim gemm tile task "
-                      f"(oracle/cpu_kernels.c, f32 accumulation), {nth} threads"}
+# ---------------------------------------------------------------------------------------------------------------
+# the five configs
+# ---------------------------------------------------------------------------------------------------------------
 
 
-def run_bgemm(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
-    B, M, N, K = wl["batch"], wl["m"], wl["n"], wl["k"]
-    flops = 2.0 * B * M * N * K
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        import numpy as np
+class Case:
+    """One BASELINE config: its global plan, seeded inputs, work formula, shard method and CPU legs."""
 
-        sys.path.insert(0, str(ROOT / "oracle"))
-        import cpu_native
+    name = ""
+    unit = "GB/s"
+    bound = "hbm"
+    dtype = "f32"
+    kernel = ""          # plan kernel name of the dominant kernel
+    traffic_key = ""     # profiles/traffic.json key (full-config launch)
+    method = "block"
 
-        rng = np.random.default_rng(0)
-        nb = 1
-        a = rng.uniform(-1, 1, (nb, M, K)).astype(np.float16)
-        b = rng.uniform(-1, 1, (nb, K, N)).astype(np.float16)
-        c = np.empty((nb, M, N), np.float32)
-        nth = cpu_native.threads()
-        # bounded step: a 512-row slab of one batch element per step
-        rows = 512
-        for _ in range(args.warmup):
-            cpu_native.gemm_tiles(a[:, :rows], b, c[:, :rows], 128, 128, nth)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            cpu_native.gemm_tiles(a[:, :rows], b, c[:, :rows], 128, 128, nth)
-        dt = time.perf_counter() - t0
-        tf = 2.0 * rows * N * K * args.steps / dt / 1e12
-        print(json.dumps({
-            "impl": "reference", "metric": "bgemm task-loop throughput", "value": round(tf, 5), "unit": "TFLOP/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16 in / f32 acc", "data": "synthetic (seeded numpy)",
-            "config": {"workload": wl["config"], "sample_per_step": f"{rows}x{N}x{K} slab of one batch element"},
-            "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOP/s", "cores": nth, "kind": "port",
-                             "sample": f"{rows}-row slab per step; C port of the CPU-sim gemm task, {nth} threads"},
-            "e2e": {"value": round(tf, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
-            flush=True)
-        return
+    def __init__(self, args):
+        self.args = args
 
-    import numpy as np
-    import torch
+    @property
+    def scale(self) -> float:
+        return 1e9 if self.unit == "GB/s" else 1e12
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    dist = None
-    if world > 1:
-        import datetime
+    def costs(self):
+        return None
 
-        import torch.distributed as dist
+    def axis(self, n_local: int | None = None) -> dict:
+        return {}
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    from pto_wsp_b200 import workloads
-    from pto_wsp_b200.runtime import CudaExecutable
+    def outputs(self, darr) -> list:
+        return []
 
-    g = torch.Generator(device=dev)
-    g.manual_seed(2000 + rank)
-    a = (torch.rand((B, M, K), generator=g, device=dev) * 2 - 1).half()
-    b = (torch.rand((B, K, N), generator=g, device=dev) * 2 - 1).half()
-    c = torch.empty((B, M, N), device=dev, dtype=torch.float32)
-    ex = CudaExecutable(workloads.bgemm_plan(B, M, N, K), device=local_rank)
-    stream = torch.cuda.current_stream(dev)
-    ex.set_stream(stream)
-    ex.set_option("sync", 0)
-    views = list(workloads.bgemm_views(a, b, c))
+    def unit_work(self, units: list[int]) -> float:
+        """Algorithmic work of the dominant kernel over these outer-axis units (one launch per step)."""
+        return self.work() * len(units) / self.n_units
 
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local_rank])
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    for _ in range(args.warmup):
-        ex.run_with_symbols(views, {}, {}, {})
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches = 0
-    with NvmlClockSampler(gpu_index(local_rank), _pci_bus_id(torch, dev)) as clk:
-        barrier()
-        e0.record(stream)
-        for _ in range(args.steps):
-            ex.run_with_symbols(views, {}, {}, {})
-            launches += int(ex.timing()["launches"])
-        e1.record(stream)
-        barrier()
-        ms = e0.elapsed_time(e1)
-        ms_max = max_over_ranks(ms)
-        # end to end with pinned host buffers
-        ex.set_option("sync", 1)
-        ah_t = torch.empty(a.shape, dtype=a.dtype, pin_memory=True)
-        bh_t = torch.empty(b.shape, dtype=b.dtype, pin_memory=True)
-        ch_t = torch.empty(c.shape, dtype=c.dtype, pin_memory=True)
-        ah_t.copy_(a)
-        bh_t.copy_(b)
-        ah, bh, ch = ah_t.numpy(), bh_t.numpy(), ch_t.numpy()
-        hviews = list(workloads.bgemm_views(ah, bh, ch))
-        ex.run_with_symbols(hviews, {}, {}, {})
-        e2e_steps = args.e2e_steps or min(args.steps, 10)
-        barrier()
-        t0 = time.perf_counter()
-        h2d = d2h = 0
-        for _ in range(e2e_steps):
-            ex.run_with_symbols(hviews, {}, {}, {})
-            tm = ex.timing()
-            h2d += tm["h2d_bytes"]
-            d2h += tm["d2h_bytes"]
-        barrier()
-        e2e_s = max_over_ranks(time.perf_counter() - t0)
-    clocks = clk.summary()
-    value = world * flops * args.steps / (ms_max / 1e3) / 1e12
-    e2e = world * flops * e2e_steps / e2e_s / 1e12
-    peak, peak_kind = peaks("bf16_tflops")
-    achieved = flops / (ms / args.steps / 1e3) / 1e12
-    ref = (a[0].double() @ b[0].double())
-    err = float(((c[0].double() - ref).abs() / (ref.abs() + ref.pow(2).mean().sqrt())).max())
-    if rank == 0:
-        line = {
-            "metric": "bgemm task-loop throughput", "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 acc",
-            "data": "synthetic (seeded torch.rand on device, U(-1,1))",
-            "config": {"workload": wl["config"], "global_batch": B * world, "per_rank_batch": B,
-                       "parallelism": f"P(batch) sharded, {world} rank(s)",
-                       "l2": "operands 1 GiB > 126 MB L2 (no flush needed)"},
-            "gpu_launches": launches,
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles("matmul_tcgen05", "bgemm", args.batch),
-                         "peak_kind": peak_kind + " (cuBLAS bf16 burst; fp16 runs at the same tensor rate)",
-                         "kernel": "matmul_tcgen05", "flops_per_launch": flops},
-            "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d // e2e_steps,
-                    "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps},
-            "clocks": clocks,
-            "max_rel_err_vs_fp64_batch0": err,
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = gemm_cpu_baseline(ah, bh)
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier(device_ids=[local_rank])
-        dist.destroy_process_group()
+    def check(self, darr) -> dict:
+        return {}
 
 
-def _dist_setup(world: int, local_rank: int):
-    import torch
+class RowCase(Case):
+    rows = cols = 0
+    batch = tiles = 0
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    dist = None
-    if world > 1:
-        import datetime
+    def __init__(self, args):
+        super().__init__(args)
+        if args.batch:
+            self.batch = args.batch
+        if args.cols:
+            self.cols = args.cols
+        self.n_units = self.batch
 
-        import torch.distributed as dist
+    @property
+    def config(self) -> str:
+        return (f"{self.cfg_name}: X[{self.batch},{self.tiles},{self.rows},{self.cols}] f32, Tile[{self.rows},"
+                f"{self.cols}], P(batch) x P(tiles)")
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    return torch, dev, dist
+    def elems(self) -> int:
+        return self.batch * self.tiles * self.rows * self.cols
 
+    def work(self) -> float:
+        return float(self.elems() * 8)
 
-def run_builtin(args, wl: dict, rank: int, world: int, local_rank: int) -> None:
-    """Configs 4 (paged decode, GB/s) and 5 (indexer scoring + top-k, TFLOP/s of the scoring)."""
-    import numpy as np
-
-    sys.path.insert(0, str(ROOT / "oracle"))
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        from cpu_sim import CpuSim
-
+    def plan(self):
         from pto_wsp_b200 import workloads
 
-        rng = np.random.default_rng(0)
-        if args.workload == "decode":
-            plan, arrays = workloads.decode_inputs(rng, 4)  # bounded sample: 4 requests x 8 kv heads per step
-            unit_bytes = int(arrays[4].astype(np.int64).sum()) * 8 * 128 * 2 * 2
-            work, unit = unit_bytes, "GB/s"
-            axis = {"b": 4}
+        fn = workloads.softmax_plan if self.name == "softmax" else workloads.rmsnorm_plan
+        return fn(self.batch, self.tiles, self.rows, self.cols)
+
+    def device_inputs(self, torch, dev):
+        g = torch.Generator(device=dev)
+        g.manual_seed(self.seed)
+        shape = (self.batch, self.tiles, self.rows, self.cols)
+        x = torch.randn(shape, generator=g, device=dev, dtype=torch.float32)
+        if self.name == "softmax":
+            x *= 4.0
+            x[torch.rand(shape, generator=g, device=dev) < 0.01] = 30.0
+        return [x, torch.empty_like(x)]
+
+    def outputs(self, darr):
+        return [1]
+
+    def check(self, darr) -> dict:
+        import numpy as np
+
+        x, y = darr
+        xs = x.reshape(-1, self.rows, self.cols)[:64].double().cpu().numpy()
+        ys = y.reshape(-1, self.rows, self.cols)[:64].double().cpu().numpy()
+        if self.name == "softmax":
+            ref = np.exp(xs - xs.max(-1, keepdims=True))
+            ref /= ref.sum(-1, keepdims=True)
         else:
-            plan, arrays = workloads.indexer_inputs(rng, 1, wl["context"], wl["topk"])
-            work, unit = 2.0 * 512 * 128 * wl["context"], "TFLOP/s"
-            axis = {}
-        sim = CpuSim(plan)
-        for _ in range(min(args.warmup, 1)):
-            sim.run([a.copy() for a in arrays], axis_sizes=axis)
-        steps = max(1, min(args.steps, 5))
+            ref = xs / np.sqrt((xs * xs).mean(-1, keepdims=True))
+        return {"max_rel_err_vs_fp64_64_tiles": float(np.max(np.abs(ys - ref) / (np.abs(ref) + 1e-30)))}
+
+    def _tiles(self, hx, n: int):
+        import numpy as np
+
+        return np.ascontiguousarray(hx.reshape(-1, self.rows, self.cols)[:n])
+
+    def cpu_baseline(self, host, budget_s: float) -> dict:
+        import numpy as np
+
+        cn = _cpu_native()
+        nth = cn.threads()
+        total = self.batch * self.tiles
+        n = min(total, 4096)
+        x = self._tiles(host[0], n)
+        y = np.empty_like(x)
+        t0 = time.perf_counter()
+        cn.row_tiles(self.name, x, y, self.rows, self.cols, nth)
+        dt = time.perf_counter() - t0
+        n2 = int(min(total, max(n, n * budget_s / max(dt, 1e-6) * 0.5)))
+        x = self._tiles(host[0], n2)
+        y = np.empty_like(x)
+        t0 = time.perf_counter()
+        cn.row_tiles(self.name, x, y, self.rows, self.cols, nth)
+        dt = time.perf_counter() - t0
+        return {"value": round(n2 * self.rows * self.cols * 8 / dt / 1e9, 3), "unit": "GB/s", "cores": nth,
+                "kind": "port", "sample": f"{n2} of {total} tiles ({n2 * self.rows * self.cols * 4 / 2**20:.0f} MiB "
+                                          f"in), {dt:.2f} s, C port of the CPU-sim tile loop (oracle/cpu_kernels.c)"}
+
+    def reference(self, steps: int, warmup: int) -> dict:
+        """The whole config per step (all tiles), C port on all host threads."""
+        import numpy as np
+
+        cn = _cpu_native()
+        nth = cn.threads()
+        total = self.batch * self.tiles
+        rng = np.random.default_rng(self.seed)
+        x = np.empty((total, self.rows, self.cols), np.float32)
+        for t0 in range(0, total, 4096):  # in slices: the mask of the whole tensor would take 4 GiB
+            xs = x[t0:t0 + 4096]
+            xs[...] = rng.standard_normal(xs.shape, dtype=np.float32)
+            if self.name == "softmax":
+                xs *= 4.0
+                xs[rng.random(xs.shape, dtype=np.float32) < 0.01] = 30.0
+        y = np.empty_like(x)
+        for _ in range(warmup):
+            cn.row_tiles(self.name, x, y, self.rows, self.cols, nth)
         t0 = time.perf_counter()
         for _ in range(steps):
-            sim.run([a.copy() for a in arrays], axis_sizes=axis)
+            cn.row_tiles(self.name, x, y, self.rows, self.cols, nth)
         dt = time.perf_counter() - t0
-        v = work * steps / dt / (1e9 if unit == "GB/s" else 1e12)
-        sample = ("4 requests x 8 kv heads per step" if args.workload == "decode" else "1 batch element per step")
-        print(json.dumps({
-            "impl": "reference", "metric": f"{args.workload} task-loop throughput", "value": round(v, 5), "unit": unit,
-            "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": round(dt / steps * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32",
-            "data": "synthetic (seeded numpy)", "config": {"workload": wl["config"], "sample_per_step": sample},
-            "cpu_baseline": {"value": round(v, 5), "unit": unit, "cores": 1, "kind": "port",
-                             "sample": sample + "; numpy restatement of the CPU-sim task (oracle/cpu_sim.py)"},
-            "e2e": {"value": round(v, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
-            flush=True)
-        return
+        v = self.work() * steps / dt / 1e9
+        return {"value": round(v, 3), "unit": "GB/s", "steps": steps, "ms_per_step": round(dt / steps * 1e3, 3),
+                "same_config": True, "cpu_baseline": {
+                    "value": round(v, 3), "unit": "GB/s", "cores": nth, "kind": "port",
+                    "sample": f"the whole config per step ({total} tiles); C port of the CPU-sim tile loop "
+                              f"(oracle/cpu_kernels.c), {nth} threads"}}
 
-    torch, dev, dist = _dist_setup(world, local_rank)
-    from pto_wsp_b200 import workloads
-    from pto_wsp_b200.runtime import CudaExecutable
 
-    rng = np.random.default_rng(3000 + rank)
-    if args.workload == "decode":
-        R = wl["batch"]
-        plan, host = workloads.decode_inputs(rng, R)
-        lens = host[4].astype(np.int64).reshape(-1)
-        work = float(lens.sum() * 8 * 128 * 2 * 2 + R * 32 * 128 * 2 * 2)  # K+V of every token + Q + O
-        unit, scale, kname, bound = "GB/s", 1e9, "paged_decode_tma", "hbm"
-        axis = {"b": R}
-    else:
-        B, T, K = wl["batch"], wl["context"], wl["topk"]
-        plan, host = workloads.indexer_inputs(rng, B, T, K)
-        work = 2.0 * B * 512 * 128 * T
-        unit, scale, kname, bound = "TFLOP/s", 1e12, "indexer_score", "tensor"
-        axis = {}
-    ex = CudaExecutable(plan, device=local_rank)
+class SoftmaxCase(RowCase):
+    name, cfg_name, kernel, traffic_key = "softmax", "config 2: row softmax", "softmax_tile", "softmax:softmax_rows"
+    batch, tiles, rows, cols, seed = 32, 2048, 32, 256, 1000
+    metric = "row-softmax task-loop throughput (algorithmic HBM bytes)"
+
+
+class RmsNormCase(RowCase):
+    name, cfg_name, kernel, traffic_key = "rmsnorm", "config 1: RMSNorm (GPU scale)", "rmsnorm_tile", "rmsnorm:rmsnorm_rows"
+    batch, tiles, rows, cols, seed = 64, 4096, 16, 128, 1001
+    metric = "RMSNorm task-loop throughput (algorithmic HBM bytes)"
+
+
+class BgemmCase(Case):
+    name, kernel, traffic_key = "bgemm", "gemm_tile", "bgemm:matmul_tcgen05"
+    unit, bound, dtype = "TFLOP/s", "tensor", "f16 in / f32 acc"
+    metric = "bgemm task-loop throughput"
+    B, M, N, K = 64, 2048, 2048, 2048
+
+    def __init__(self, args):
+        super().__init__(args)
+        if args.batch:
+            self.B = args.batch
+        self.n_units = self.B
+
+    @property
+    def config(self) -> str:
+        return (f"config 3: bgemm {self.B} x ({self.M}x{self.N}x{self.K}), f16 in, f32 acc/out, 128x128 output tiles, "
+                f"K inside the kernel")
+
+    def work(self) -> float:
+        return 2.0 * self.B * self.M * self.N * self.K
+
+    def plan(self):
+        from pto_wsp_b200 import workloads
+
+        return workloads.bgemm_plan(self.B, self.M, self.N, self.K)
+
+    def device_inputs(self, torch, dev):
+        from pto_wsp_b200 import workloads
+
+        g = torch.Generator(device=dev)
+        g.manual_seed(2000)
+        self._abc = ((torch.rand((self.B, self.M, self.K), generator=g, device=dev) * 2 - 1).half(),
+                     (torch.rand((self.B, self.K, self.N), generator=g, device=dev) * 2 - 1).half(),
+                     torch.empty((self.B, self.M, self.N), device=dev, dtype=torch.float32))
+        return list(workloads.bgemm_views(*self._abc))
+
+    def host_views(self, torch):
+        """Pinned host copies of A, B, C and the plan's views of them."""
+        from pto_wsp_b200 import workloads
+
+        hs = []
+        for t in self._abc:
+            h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            h.copy_(t)
+            hs.append(h.numpy())
+        self._host_abc = hs
+        return list(workloads.bgemm_views(*hs))
+
+    def outputs(self, darr):
+        return [2]
+
+    def check(self, darr) -> dict:
+        a, b, c = self._abc
+        ref = a[0].double() @ b[0].double()
+        big = ref.abs() > 1e-2 * ref.abs().max()
+        rel = ((c[0].double() - ref).abs() / ref.abs())[big]
+        return {"max_rel_err_vs_fp64_batch0": float(rel.max())}
+
+    def cpu_baseline(self, host, budget_s: float) -> dict:
+        import numpy as np
+
+        cn = _cpu_native()
+        nth = cn.threads()
+        a, b = self._host_abc[0], self._host_abc[1]
+        rows = 128
+        c = np.empty((1, rows, self.N), np.float32)
+        t0 = time.perf_counter()
+        cn.gemm_tiles(a[:1, :rows], b[:1], c, 128, 128, nth)
+        dt = time.perf_counter() - t0
+        reps = max(1, min(int(budget_s / max(dt, 1e-6)), self.M // rows))
+        rows2 = rows * reps
+        c = np.empty((1, rows2, self.N), np.float32)
+        t0 = time.perf_counter()
+        cn.gemm_tiles(np.ascontiguousarray(a[:1, :rows2]), b[:1], c, 128, 128, nth)
+        dt = time.perf_counter() - t0
+        return {"value": round(2.0 * rows2 * self.N * self.K / dt / 1e12, 6), "unit": "TFLOP/s", "cores": nth,
+                "kind": "port", "sample": f"{rows2}x{self.N}x{self.K} rows of batch element 0 ({dt:.2f} s), C port "
+                                          f"of the CPU-sim gemm tile task (oracle/cpu_kernels.c, f32 accumulation)"}
+
+    def reference(self, steps: int, warmup: int) -> dict:
+        import numpy as np
+
+        cn = _cpu_native()
+        nth = cn.threads()
+        rng = np.random.default_rng(0)
+        rows = 512
+        a = rng.uniform(-1, 1, (1, rows, self.K)).astype(np.float16)
+        b = rng.uniform(-1, 1, (1, self.K, self.N)).astype(np.float16)
+        c = np.empty((1, rows, self.N), np.float32)
+        for _ in range(min(warmup, 1)):
+            cn.gemm_tiles(a, b, c, 128, 128, nth)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            cn.gemm_tiles(a, b, c, 128, 128, nth)
+        dt = time.perf_counter() - t0
+        v = 2.0 * rows * self.N * self.K * steps / dt / 1e12
+        return {"value": round(v, 6), "unit": "TFLOP/s", "steps": steps, "ms_per_step": round(dt / steps * 1e3, 3),
+                "same_config": False, "cpu_baseline": {
+                    "value": round(v, 6), "unit": "TFLOP/s", "cores": nth, "kind": "port",
+                    "sample": f"a {rows}x{self.N}x{self.K} slab (4 of 16 m-tile rows of one batch element) per step; "
+                              f"the full config is {self.B * self.M // rows}x that; C port of the CPU-sim gemm tile "
+                              f"task, {nth} threads"}}
+
+
+class DecodeCase(Case):
+    name, kernel, traffic_key, method = "decode", "paged_decode", "decode:paged_decode_tma", "lpt"
+    unit, bound, dtype = "GB/s", "hbm", "f16 in / f32 softmax / f16 out"
+    metric = "paged GQA decode task-loop throughput (algorithmic HBM bytes)"
+    R, KVH, G, D, PS = 64, 8, 4, 128, 16
+
+    def __init__(self, args):
+        super().__init__(args)
+        import numpy as np
+
+        if args.batch:
+            self.R = args.batch
+        self.n_units = self.R
+        rng = np.random.default_rng(3000)
+        self.lens = rng.integers(512, 8192 + 1, size=self.R).astype(np.int64)
+        self.npages = (self.lens + self.PS - 1) // self.PS
+        self.maxp = int(self.npages.max())
+        self.total_pages = int(self.npages.sum())
+        perm = rng.permutation(self.total_pages).astype(np.int32)
+        self.pt = np.zeros((self.R, self.maxp), np.int32)
+        off = 0
+        for r in range(self.R):
+            self.pt[r, : self.npages[r]] = perm[off: off + self.npages[r]]
+            off += int(self.npages[r])
+
+    @property
+    def config(self) -> str:
+        return (f"config 4: paged GQA decode, {self.R} requests, 32 q / 8 kv heads, d=128, f16, page 16, KV len "
+                f"U[512,8192] (sum {int(self.lens.sum())} tokens), random page permutation")
+
+    def costs(self):
+        return [float(x) for x in self.lens]
+
+    def axis(self, n_local=None):
+        return {"b": int(n_local if n_local is not None else self.R)}
+
+    def _work(self, units) -> float:
+        L = float(self.lens[list(units)].sum())
+        return L * self.KVH * self.D * 2 * 2 + len(units) * self.KVH * self.G * self.D * 2 * 2
+
+    def work(self) -> float:
+        return self._work(range(self.R))
+
+    def unit_work(self, units):
+        return self._work(units)
+
+    def plan(self):
+        from pto_wsp_b200 import workloads
+
+        return workloads.decode_plan(self.R, self.KVH, self.G, self.D, self.total_pages, self.maxp, self.PS)
+
+    def device_inputs(self, torch, dev):
+        g = torch.Generator(device=dev)
+        g.manual_seed(3001)
+        q = torch.randn((self.R, self.KVH, self.G, self.D), generator=g, device=dev).half()
+        kc = torch.randn((self.total_pages, self.PS, self.KVH, self.D), generator=g, device=dev).half()
+        vc = torch.randn((self.total_pages, self.PS, self.KVH, self.D), generator=g, device=dev).half()
+        pt = torch.from_numpy(self.pt).to(dev)
+        kl = torch.tensor(self.lens.reshape(self.R, 1), dtype=torch.int32, device=dev)
+        out = torch.zeros((self.R, self.KVH, self.G, self.D), dtype=torch.float16, device=dev)
+        return [q, kc, vc, pt, kl, out]
+
+    def outputs(self, darr):
+        return [5]
+
+    def check(self, darr) -> dict:
+        import math
+
+        torch = sys.modules["torch"]
+        q, kc, vc, pt, kl, out = darr
+        worst = 0.0
+        for r in (0, self.R // 2, self.R - 1):
+            L = int(self.lens[r])
+            pages = pt[r, : (L + self.PS - 1) // self.PS].long()
+            k = kc[pages].reshape(-1, self.KVH, self.D)[:L].double()
+            v = vc[pages].reshape(-1, self.KVH, self.D)[:L].double()
+            s = torch.einsum("hgd,thd->hgt", q[r].double(), k) / math.sqrt(self.D)
+            ref = torch.einsum("hgt,thd->hgd", torch.softmax(s, -1), v)
+            err = ((out[r].double() - ref).abs() / (ref.abs() + ref.pow(2).mean().sqrt())).max()
+            worst = max(worst, float(err))
+        return {"max_err_vs_fp64_3_requests": worst}
+
+    def _body_sample(self, host, reqs: list[int]):
+        """Inputs of a few requests as their own small decode problem (pages renumbered)."""
+        import numpy as np
+
+        q, kc, vc, pt, kl, _ = host
+        pages = np.concatenate([pt[r, : self.npages[r]] for r in reqs])
+        maxp = int(max(self.npages[r] for r in reqs))
+        spt = np.zeros((len(reqs), maxp), np.int32)
+        off = 0
+        for i, r in enumerate(reqs):
+            n = int(self.npages[r])
+            spt[i, :n] = np.arange(off, off + n, dtype=np.int32)
+            off += n
+        return (np.ascontiguousarray(q[reqs]), np.ascontiguousarray(kc[pages]), np.ascontiguousarray(vc[pages]), spt,
+                self.lens[reqs].astype(np.int32), np.zeros((len(reqs), self.KVH, self.G, self.D), np.float16))
+
+    def cpu_baseline(self, host, budget_s: float) -> dict:
+        cn = _cpu_native()
+        nth = cn.threads()
+        reqs = [0, 1]
+        t0 = time.perf_counter()
+        s = self._body_sample(host, reqs)
+        cn.paged_decode(*s, self.PS, nth)
+        dt = time.perf_counter() - t0
+        n = int(max(2, min(self.R, len(reqs) * budget_s / max(dt, 1e-6) * 0.5)))
+        reqs = list(range(n))
+        s = self._body_sample(host, reqs)
+        t0 = time.perf_counter()
+        cn.paged_decode(*s, self.PS, nth)
+        dt = time.perf_counter() - t0
+        return {"value": round(self._work(reqs) / dt / 1e9, 4), "unit": "GB/s", "cores": nth, "kind": "port",
+                "sample": f"{n} of {self.R} requests x 8 kv heads ({dt:.2f} s), C port of the paged-decode task body "
+                          f"(oracle/cpu_kernels.c: online softmax per query head, f32)"}
+
+    def reference(self, steps: int, warmup: int) -> dict:
+        import numpy as np
+
+        cn = _cpu_native()
+        nth = cn.threads()
+        rng = np.random.default_rng(1)
+        host = [rng.standard_normal((self.R, self.KVH, self.G, self.D), dtype=np.float32).astype(np.float16),
+                rng.standard_normal((self.total_pages, self.PS, self.KVH, self.D), dtype=np.float32).astype(np.float16),
+                rng.standard_normal((self.total_pages, self.PS, self.KVH, self.D), dtype=np.float32).astype(np.float16),
+                self.pt, self.lens.astype(np.int32).reshape(-1, 1), None]
+        reqs = list(range(min(self.R, 16)))
+        s = self._body_sample(host, reqs)
+        for _ in range(min(warmup, 1)):
+            cn.paged_decode(*s, self.PS, nth)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            cn.paged_decode(*s, self.PS, nth)
+        dt = time.perf_counter() - t0
+        v = self._work(reqs) * steps / dt / 1e9
+        return {"value": round(v, 4), "unit": "GB/s", "steps": steps, "ms_per_step": round(dt / steps * 1e3, 3),
+                "same_config": False, "cpu_baseline": {
+                    "value": round(v, 4), "unit": "GB/s", "cores": nth, "kind": "port",
+                    "sample": f"{len(reqs)} of {self.R} requests x 8 kv heads per step (same lengths and pages); "
+                              f"C port of the paged-decode task body, {nth} threads"}}
+
+
+class IndexerCase(Case):
+    name, kernel, traffic_key = "indexer", "indexer_score", "indexer:indexer_score"
+    unit, bound, dtype = "TFLOP/s", "tensor", "f16 in / f32 scores / i32 indices"
+    metric = "lightning-indexer task-loop throughput (scoring flop; step = scoring + top-2048)"
+    B, Q, H, D, T, TOPK = 16, 8, 64, 128, 32768, 2048
+
+    def __init__(self, args):
+        super().__init__(args)
+        if args.batch:
+            self.B = args.batch
+        self.n_units = self.B
+
+    @property
+    def config(self) -> str:
+        return (f"config 5: lightning indexer {self.B} batches x {self.Q} queries, {self.H} heads, d={self.D}, "
+                f"{self.T} keys, top-{self.TOPK}")
+
+    def work(self) -> float:
+        return 2.0 * self.B * self.Q * self.H * self.D * self.T
+
+    def plan(self):
+        from pto_wsp_b200 import workloads
+
+        return workloads.indexer_plan(self.B, self.Q, self.H, self.D, self.T, self.TOPK)
+
+    def device_inputs(self, torch, dev):
+        g = torch.Generator(device=dev)
+        g.manual_seed(4000)
+        q = torch.randn((self.B, self.Q * self.H, self.D), generator=g, device=dev).half()
+        k = torch.randn((self.B, self.T, self.D), generator=g, device=dev).half()
+        w = torch.rand((self.B, self.Q, self.H), generator=g, device=dev)
+        s = torch.zeros((self.B, self.Q, self.T), device=dev)
+        idx = torch.zeros((self.B, self.Q, self.TOPK), dtype=torch.int32, device=dev)
+        return [q, k, w, s, idx]
+
+    def outputs(self, darr):
+        return [3, 4]
+
+    def check(self, darr) -> dict:
+        torch = sys.modules["torch"]
+        q, k, w, s, idx = darr
+        qd = q[0].double().reshape(self.Q, self.H, self.D)
+        ref = (torch.relu(torch.einsum("qhd,td->qht", qd, k[0].double())) * w[0].double()[:, :, None]).sum(1)
+        err = float(((s[0].double() - ref).abs() / (ref.abs() + ref.abs().mean())).max())
+        # the indices must be the stable top-k of the GPU's own scores (score descending, ties -> lower index)
+        sc = s[0]
+        order = torch.sort(-sc.double(), dim=-1, stable=True).indices[:, : self.TOPK].int()
+        exact = bool(torch.equal(order, idx[0]))
+        return {"score_err_vs_fp64_batch0": err, "topk_exact_on_gpu_scores_batch0": exact}
+
+    def cpu_baseline(self, host, budget_s: float) -> dict:
+        import numpy as np
+
+        cn = _cpu_native()
+        nth = cn.threads()
+        q, k, w = host[0], host[1], host[2]
+        n = 1
+        s = np.zeros((n, self.Q, self.T), np.float32)
+        idx = np.zeros((n, self.Q, self.TOPK), np.int32)
+        t0 = time.perf_counter()
+        cn.indexer(q[:n], k[:n], w[:n], s, idx, self.H, nth)
+        dt = time.perf_counter() - t0
+        n2 = int(max(1, min(self.B, budget_s / max(dt, 1e-6) * 0.5)))
+        if n2 > n:
+            s = np.zeros((n2, self.Q, self.T), np.float32)
+            idx = np.zeros((n2, self.Q, self.TOPK), np.int32)
+            t0 = time.perf_counter()
+            cn.indexer(q[:n2], k[:n2], w[:n2], s, idx, self.H, nth)
+            dt = time.perf_counter() - t0
+        return {"value": round(2.0 * n2 * self.Q * self.H * self.D * self.T / dt / 1e12, 6), "unit": "TFLOP/s",
+                "cores": nth, "kind": "port",
+                "sample": f"{n2} of {self.B} batch elements, scoring + top-{self.TOPK} ({dt:.2f} s), C port of the "
+                          f"indexer task bodies (oracle/cpu_kernels.c)"}
+
+    def reference(self, steps: int, warmup: int) -> dict:
+        import numpy as np
+
+        cn = _cpu_native()
+        nth = cn.threads()
+        rng = np.random.default_rng(1)
+        n = 1
+        q = rng.standard_normal((n, self.Q * self.H, self.D), dtype=np.float32).astype(np.float16)
+        k = rng.standard_normal((n, self.T, self.D), dtype=np.float32).astype(np.float16)
+        w = rng.uniform(0, 1, (n, self.Q, self.H)).astype(np.float32)
+        s = np.zeros((n, self.Q, self.T), np.float32)
+        idx = np.zeros((n, self.Q, self.TOPK), np.int32)
+        for _ in range(min(warmup, 1)):
+            cn.indexer(q, k, w, s, idx, self.H, nth)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            cn.indexer(q, k, w, s, idx, self.H, nth)
+        dt = time.perf_counter() - t0
+        v = 2.0 * n * self.Q * self.H * self.D * self.T * steps / dt / 1e12
+        return {"value": round(v, 6), "unit": "TFLOP/s", "steps": steps, "ms_per_step": round(dt / steps * 1e3, 3),
+                "same_config": False, "cpu_baseline": {
+                    "value": round(v, 6), "unit": "TFLOP/s", "cores": nth, "kind": "port",
+                    "sample": f"1 of {self.B} batch elements per step (scoring + top-{self.TOPK}); C port of the "
+                              f"indexer task bodies, {nth} threads"}}
+
+
+CASES = {"softmax": SoftmaxCase, "rmsnorm": RmsNormCase, "bgemm": BgemmCase, "decode": DecodeCase,
+         "indexer": IndexerCase}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------------------------------
+
+
+class Dist:
+    def __init__(self, world: int, local_rank: int):
+        import torch
+
+        self.torch = torch
+        torch.cuda.set_device(local_rank)
+        self.dev = torch.device("cuda", local_rank)
+        self.local_rank = local_rank
+        self.dist = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier(device_ids=[self.local_rank])
+        self.torch.cuda.synchronize(self.dev)
+
+    def max(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier(device_ids=[self.local_rank])
+            self.dist.destroy_process_group()
+
+
+def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
+    import numpy as np
+
+    from pto_wsp_b200.shard import ShardedExecutable
+
+    torch, dev = D.torch, D.dev
+    plan = case.plan()
+    darr = case.device_inputs(torch, dev)
+    sh = ShardedExecutable(plan, rank=rank, world=world, device=D.local_rank, method=case.method,
+                           costs=case.costs())
+    units = sh.local_units(case.n_units)
+    ex = sh.executable(len(units))
     stream = torch.cuda.current_stream(dev)
     ex.set_stream(stream)
     ex.set_option("sync", 0)
-    darr = [torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in host]
+    axis = case.axis(case.n_units)
 
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local_rank])
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    def step(arrays):
+        return sh.run_with_symbols(arrays, axis)
 
     for _ in range(args.warmup):
-        ex.run_with_symbols(darr, axis, {}, {})
-    barrier()
+        step(darr)
+    D.barrier()
+    ex.set_option("kernel_events", 1)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches = 0
-    with NvmlClockSampler(gpu_index(local_rank), _pci_bus_id(torch, dev)) as clk:
-        barrier()
+    with NvmlClockSampler(gpu_index(D.local_rank), _pci_bus_id(torch, dev)) as clk:
+        D.barrier()
         e0.record(stream)
         for _ in range(args.steps):
-            ex.run_with_symbols(darr, axis, {}, {})
+            step(darr)
             launches += int(ex.timing()["launches"])
         e1.record(stream)
-        barrier()
-        ms = e0.elapsed_time(e1)
-        ms_max = max_over_ranks(ms)
-        ex.set_option("sync", 1)
-        pinned = []
-        for a in host:
-            t = torch.empty(a.shape, dtype=torch.from_numpy(a[:0].copy()).dtype, pin_memory=True)
-            t.copy_(torch.from_numpy(np.ascontiguousarray(a)))
-            pinned.append(t.numpy())
-        ex.run_with_symbols(pinned, axis, {}, {})
-        e2e_steps = args.e2e_steps or min(args.steps, 10)
-        barrier()
-        t0 = time.perf_counter()
-        h2d = d2h = 0
-        for _ in range(e2e_steps):
-            ex.run_with_symbols(pinned, axis, {}, {})
-            tm = ex.timing()
-            h2d += tm["h2d_bytes"]
-            d2h += tm["d2h_bytes"]
-        barrier()
-        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        D.barrier()
     clocks = clk.summary()
-    value = world * work * args.steps / (ms_max / 1e3) / scale
-    e2e = world * work * e2e_steps / e2e_s / scale
-    peak, peak_kind = peaks("hbm_gbs" if bound == "hbm" else "bf16_tflops")
-    achieved = work / (ms / args.steps / 1e3) / scale
-    if rank == 0:
-        line = {
-            "metric": f"{args.workload} task-loop throughput", "value": round(value, 3), "unit": unit,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 softmax|acc",
-            "data": "synthetic (seeded numpy, BASELINE.json distributions)",
-            "config": {"workload": wl["config"], "per_rank_batch": wl["batch"], "global_batch": wl["batch"] * world,
-                       "parallelism": f"P(batch) sharded, {world} rank(s)",
-                       "l2": "KV / keys > 126 MB L2 (no flush needed)"},
-            "gpu_launches": launches,
-            "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
-                         "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(kname, args.workload, args.batch),
-                         "peak_kind": peak_kind, "kernel": kname,
-                         ("bytes_per_launch" if bound == "hbm" else "flops_per_launch"): work,
-                         "note": "step = all work of the task loop (decode: counter memset + TMA kernel with fused merge; indexer: scoring + "
-                                 "top-k); achieved uses the whole step time"},
-            "e2e": {"value": round(e2e, 4), "unit": unit, "h2d_bytes_per_step": h2d // e2e_steps,
-                    "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps},
-            "clocks": clocks,
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            from cpu_sim import CpuSim
+    ms = e0.elapsed_time(e1)
+    ms_max = D.max(ms)
+    ktimes = ex.kernel_times()
+    ex.set_option("kernel_events", 0)
+    check = case.check(darr)
 
-            if args.workload == "decode":
-                sub_plan, sub = workloads.decode_inputs(np.random.default_rng(1), 2)
-                sub_work = float(sub[4].astype(np.int64).sum() * 8 * 128 * 2 * 2)
-                ax = {"b": 2}
-                what = "2 requests x 8 kv heads"
-            else:
-                sub_plan, sub = workloads.indexer_inputs(np.random.default_rng(1), 1, wl["context"], wl["topk"])
-                sub_work = 2.0 * 512 * 128 * wl["context"]
-                ax = {}
-                what = "1 batch element (scoring + top-k)"
-            t0 = time.perf_counter()
-            CpuSim(sub_plan).run(sub, axis_sizes=ax)
-            dt = time.perf_counter() - t0
-            line["cpu_baseline"] = {"value": round(sub_work / dt / scale, 6), "unit": unit, "cores": 1,
-                                    "kind": "port", "sample": f"{what}, {dt:.2f} s, numpy restatement of the "
-                                                              f"CPU-sim task (oracle/cpu_sim.py)"}
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier(device_ids=[local_rank])
-        dist.destroy_process_group()
+    # end to end: pinned host buffers through the same call, copies inside the timed region
+    ex.set_option("sync", 1)
+    if isinstance(case, BgemmCase):
+        harr = case.host_views(torch)
+    else:
+        harr = []
+        for t in darr:
+            h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            h.copy_(t)
+            harr.append(h.numpy())
+    step(harr)  # device staging buffers and layout checks
+    e2e_steps = args.e2e_steps or min(args.steps, 10)
+    D.barrier()
+    t0 = time.perf_counter()
+    h2d = d2h = 0
+    for _ in range(e2e_steps):
+        step(harr)
+        tm = ex.timing()
+        h2d += tm["h2d_bytes"]
+        d2h += tm["d2h_bytes"]
+    D.barrier()
+    e2e_s = D.max(time.perf_counter() - t0)
+
+    work = case.work()
+    value = work * args.steps / (ms_max / 1e3) / case.scale
+    e2e = work * e2e_steps / e2e_s / case.scale
+    peak, peak_kind = peaks("hbm_gbs" if case.bound == "hbm" else "bf16_tflops")
+    kt = ktimes.get(case.kernel, {"launches": 0, "ms": 0.0})
+    kwork = case.unit_work(units)
+    per_launch_ms = kt["ms"] / max(kt["launches"], 1)
+    achieved = kwork / (per_launch_ms / 1e3) / case.scale if per_launch_ms > 0 else 0.0
+    traffic = traffic_from_profiles(case.traffic_key)
+    if traffic is not None and not args.batch and not args.cols:
+        traffic = traffic * kwork / case.unit_work(list(range(case.n_units)))
+    else:
+        traffic = None
+    line = {
+        "metric": case.metric, "value": round(value, 3), "unit": case.unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": case.dtype,
+        "data": "synthetic (seeded torch generators on device; BASELINE.json shapes and distributions)",
+        "config": {"workload": case.config, "global_batch": case.n_units, "rank_units": len(units),
+                   "parallelism": f"P(batch) over {world} rank(s), {case.method} shares (ShardedExecutable)",
+                   "l2": "every step reads inputs larger than the 126 MB L2 (no flush)"},
+        "gpu_launches": launches,
+        "roofline": {"bound": case.bound, "achieved": round(achieved, 2), "peak": peak, "unit": case.unit,
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": case.kernel,
+                     ("bytes_per_launch" if case.bound == "hbm" else "flops_per_launch"): kwork,
+                     "launch_ms": round(per_launch_ms, 5), "launches_timed": kt["launches"],
+                     "timing": "CUDA events around the kernel's launches on the launch stream, timed region"},
+        "kernel_ms": {k: {"launches": v["launches"], "ms_per_launch": round(v["ms"] / max(v["launches"], 1), 5)}
+                      for k, v in ktimes.items()},
+        "e2e": {"value": round(e2e, 4), "unit": case.unit, "h2d_bytes_per_step": h2d // e2e_steps,
+                "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps,
+                "path": "ShardedExecutable.run_with_symbols (CodegenExecutable surface) with pinned numpy buffers"},
+        "clocks": clocks,
+        "check": check,
+    }
+    if case.bound == "tensor":
+        line["roofline"]["peak_kind"] += " (cuBLAS bf16 burst; f16 runs at the same tensor rate)"
+    if isinstance(case, IndexerCase):
+        step_ach = case.unit_work(units) / (ms / args.steps / 1e3) / 1e12
+        line["roofline"]["step_frac"] = round(step_ach / peak, 4)
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = case.cpu_baseline(harr, args.cpu_budget)
+    del darr, harr
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_gpu(args, names: list[str], rank: int, world: int, local_rank: int) -> None:
+    D = Dist(world, local_rank)
+    lines = {}
+    for n in names:
+        lines[n] = run_case(CASES[n](args), args, D, rank, world)
+    if rank == 0:
+        head = dict(lines[names[0]])
+        if len(names) > 1:
+            head["workloads"] = {n: lines[n] for n in names[1:]}
+        print(json.dumps(head), flush=True)
+    D.close()
+
+
+def run_reference(args, names: list[str], rank: int) -> None:
+    if rank != 0:
+        return
+    lines = {}
+    for n in names:
+        case = CASES[n](args)
+        r = case.reference(args.steps, args.warmup)
+        lines[n] = {"impl": "reference", "metric": case.metric, "value": r["value"], "unit": r["unit"],
+                    "n_gpus": args.gpus, "steps": r["steps"], "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                    "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": case.dtype,
+                    "data": "synthetic (seeded numpy)", "config": {"workload": case.config,
+                                                                   "same_config": r["same_config"]},
+                    "cpu_baseline": r["cpu_baseline"],
+                    "e2e": {"value": r["value"], "unit": r["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    head = dict(lines[names[0]])
+    if len(names) > 1:
+        head["workloads"] = {n: lines[n] for n in names[1:]}
+    print(json.dumps(head), flush=True)
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="softmax", choices=sorted(WORKLOADS))
-    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default: --steps, max 20)")
+    ap.add_argument("--workload", default="all", choices=["all"] + ORDER)
+    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default min(steps, 10))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=None, help="override the per-rank batch (small profiling cases)")
-    ap.add_argument("--cols", type=int, default=None,
-                    help="rmsnorm/softmax: tile width other than the config's (widths without a hand-written row "
-                         "kernel run the fused row-program kernel built at run time)")
+    ap.add_argument("--cpu-budget", type=float, default=4.0, help="seconds of CPU work per cpu_baseline sample")
+    ap.add_argument("--batch", type=int, default=None, help="override the outer batch (small profiling cases)")
+    ap.add_argument("--cols", type=int, default=None, help="rmsnorm/softmax: another tile width (row-program kernel)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    wl = dict(WORKLOADS[args.workload])
-    if args.batch:
-        wl["batch"] = args.batch
-        wl["config"] += f" [batch overridden to {args.batch}]"
-    if args.cols and "cols" in wl:
-        wl["cols"] = args.cols
-        wl["config"] += f" [tile width overridden to {args.cols}]"
-
-    rank = _env_int("RANK", 0)
-    world = _env_int("WORLD_SIZE", 1)
-    local_rank = _env_int("LOCAL_RANK", 0)
-
-    if args.workload == "bgemm":
-        run_bgemm(args, wl, rank, world, local_rank)
-        return
-    if args.workload in ("decode", "indexer"):
-        run_builtin(args, wl, rank, world, local_rank)
-        return
+    names = ORDER if args.workload == "all" else [args.workload]
+    rank, world, local_rank = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1), _env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
-        run_reference(args, wl, rank)
-        return
-
-    import numpy as np
-    import torch
-
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-
-    from pto_wsp_b200 import workloads
-    from pto_wsp_b200.runtime import CudaExecutable
-
-    B, T, R, Cc = wl["batch"], wl["tiles"], wl["rows"], wl["cols"]
-    plan = (workloads.softmax_plan if args.workload == "softmax" else workloads.rmsnorm_plan)(B, T, R, Cc)
-    ex = CudaExecutable(plan, device=local_rank)
-    stream = torch.cuda.current_stream(dev)
-    ex.set_stream(stream)
-    ex.set_option("sync", 0)
-    mk = make_softmax_inputs if args.workload == "softmax" else make_rmsnorm_inputs
-    x = mk(torch, B, T, R, Cc, dev, seed=1000 + rank)
-    y = torch.empty_like(x)
-    elems = x.numel()
-    alg_bytes = elems * 8  # read x + write y, f32
-
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local_rank])
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # ---- device-resident value ----
-    for _ in range(args.warmup):
-        ex.run_with_symbols([x, y], {}, {}, {})
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches = 0
-    with NvmlClockSampler(gpu_index(local_rank), _pci_bus_id(torch, dev)) as clk:
-        barrier()
-        e0.record(stream)
-        for _ in range(args.steps):
-            ex.run_with_symbols([x, y], {}, {}, {})
-            launches += int(ex.timing()["launches"])
-        e1.record(stream)
-        barrier()
-        ms = e0.elapsed_time(e1)
-        ms_max = max_over_ranks(ms)
-
-        # ---- end-to-end through the same call with pinned host buffers ----
-        ex.set_option("sync", 1)
-        xh_t = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
-        yh_t = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
-        xh_t.copy_(x)
-        xh, yh = xh_t.numpy(), yh_t.numpy()
-        e2e_steps = args.e2e_steps or min(args.steps, 20)
-        ex.run_with_symbols([xh, yh], {}, {}, {})  # warm: device staging buffers
-        barrier()
-        t0 = time.perf_counter()
-        h2d = d2h = 0
-        for _ in range(e2e_steps):
-            ex.run_with_symbols([xh, yh], {}, {}, {})
-            tm = ex.timing()
-            h2d += tm["h2d_bytes"]
-            d2h += tm["d2h_bytes"]
-        barrier()
-        e2e_s = max_over_ranks(time.perf_counter() - t0)
-    clocks = clk.summary()
-
-    value = world * alg_bytes * args.steps / (ms_max / 1e3) / 1e9
-    e2e = world * alg_bytes * e2e_steps / e2e_s / 1e9
-    peak, peak_kind = peaks()
-    per_launch_ms = ms / args.steps
-    achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
-    kernel_name = "softmax_rows" if args.workload == "softmax" else "rmsnorm_rows"
-    if ex.describe()["kernels"][0].get("row_kernel") == "loaded":
-        kernel_name = "ptowsp_rows_k0 (row program built with NVRTC)"
-    traffic = traffic_from_profiles(kernel_name, args.workload, args.batch or args.cols)
-
-    # spot-check the last device result against the numpy definition on a few tiles
-    xs = x.reshape(-1, R, Cc)[:64].double().cpu().numpy()
-    ys = y.reshape(-1, R, Cc)[:64].double().cpu().numpy()
-    if args.workload == "softmax":
-        ref = np.exp(xs - xs.max(-1, keepdims=True))
-        ref /= ref.sum(-1, keepdims=True)
+        run_reference(args, names, rank)
     else:
-        ref = xs / np.sqrt((xs * xs).mean(-1, keepdims=True))
-    check = float(np.max(np.abs(ys - ref) / (np.abs(ref) + 1e-30)))
-
-    if rank == 0:
-        line = {
-            "metric": f"{args.workload} task-loop throughput (algorithmic HBM bytes)",
-            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded torch.randn on device)",
-            "config": {"workload": wl["config"], "global_batch": B * world, "per_rank_batch": B, "tiles": T,
-                       "tile": [R, Cc], "parallelism": f"P(batch) sharded, {world} rank(s)",
-                       "l2": "inputs 2 GiB > 126 MB L2 (no flush needed)"},
-            "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": kernel_name, "bytes_per_launch": alg_bytes},
-            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d // e2e_steps,
-                    "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps,
-                    "path": "CodegenExecutable-style run_with_symbols with pinned numpy buffers"},
-            "clocks": clocks,
-            "max_rel_err_vs_fp64_sample": check,
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args.workload, xh, R, Cc)
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier(device_ids=[local_rank])
-        dist.destroy_process_group()
+        run_gpu(args, names, rank, world, local_rank)
 
 
 if __name__ == "__main__":

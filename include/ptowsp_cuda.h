@@ -142,8 +142,19 @@ PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
  * of static workloads across runs, default 1), "sync" (0: when every tensor
  * is device memory, return without waiting; errors surface at the next
  * synchronous run, default 1), "dry_run" (1: walk the task loop on the host
- * only -- makespan, task and wave counts -- with no CUDA call, default 0). */
+ * only -- makespan, task and wave counts -- with no CUDA call, default 0),
+ * "kernel_events" (1: bracket every kernel's launches with CUDA events on the
+ * launch stream and sum their device time per kernel, read by
+ * ptowsp_cuda_kernel_times; setting it clears the sums; default 0).
+ * "stage_scratch_mb" is clamped to 1 .. 1048576; changing it drops the cached
+ * task tables, which were grouped for the old budget. */
 PTOWSP_API int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value);
+
+/* Per-kernel device time since "kernel_events" was last set, as JSON
+ * {"<kernel>": {"launches": n, "ms": t}, ...} (waits for the recorded events).
+ * No counterpart in the reference, whose CPU-sim reports model cycles only.
+ * Owned by `prog`, valid until the next call. */
+PTOWSP_API const char* ptowsp_cuda_kernel_times(ptowsp_program* prog);
 
 typedef struct ptowsp_timing {
     double gpu_ms;        /* kernel time of the last run (CUDA events; overlapped runs: first to last kernel, copies between them included) */

@@ -88,7 +88,16 @@ int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value)
     if (!prog || !prog->p || !key) return PTOWSP_ERR_ARG;
     auto& p = *prog->p;
     if (!std::strcmp(key, "pipeline_chunks")) p.opt_chunks = value < 1 ? 1 : value;
-    else if (!std::strcmp(key, "stage_scratch_mb")) p.opt_stage_scratch_mb = value < 1 ? 1 : value;
+    else if (!std::strcmp(key, "stage_scratch_mb")) {
+        // 1 MiB .. 1 TiB: the byte count (value << 20) stays far inside int64.  A batch keeps the task groups it
+        // was planned with, so a changed budget drops the cached task tables (the next run plans again).
+        const int64_t mb = value < 1 ? 1 : (value > (int64_t{1} << 20) ? (int64_t{1} << 20) : value);
+        if (mb != p.opt_stage_scratch_mb) p.cached.reset();
+        p.opt_stage_scratch_mb = mb;
+    } else if (!std::strcmp(key, "kernel_events")) {
+        p.opt_kernel_events = value != 0;
+        guarded(prog, [&] { ptowsp::reset_kernel_times(p); return 0; }, 0);
+    }
     else if (!std::strcmp(key, "cache_plans")) {
         p.opt_cache = value != 0;
         if (!p.opt_cache) p.cached.reset();
@@ -105,6 +114,12 @@ int ptowsp_cuda_last_timing(const ptowsp_program* prog, ptowsp_timing* out) {
     if (!prog || !prog->p || !out) return PTOWSP_ERR_ARG;
     *out = prog->p->timing;
     return PTOWSP_OK;
+}
+
+const char* ptowsp_cuda_kernel_times(ptowsp_program* prog) {
+    if (!prog || !prog->p) return "{}";
+    prog->p->kernel_times_json = guarded(prog, [&] { return ptowsp::kernel_times(*prog->p); }, std::string("{}"));
+    return prog->p->kernel_times_json.c_str();
 }
 
 const char* ptowsp_cuda_describe(ptowsp_program* prog) {

@@ -838,6 +838,11 @@ Program::~Program() {
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     for (auto e : pipe_events) cudaEventDestroy(e);
+    for (auto& ke : kev_pending) {
+        cudaEventDestroy(ke.start);
+        cudaEventDestroy(ke.end);
+    }
+    for (auto e : kev_free) cudaEventDestroy(e);
     if (h2d_stream) cudaStreamDestroy(h2d_stream);
     if (d2h_stream) cudaStreamDestroy(d2h_stream);
     if (own_stream) cudaStreamDestroy(own_stream);
@@ -876,8 +881,8 @@ void* ensure_scratch(Program& p, size_t bytes) {
 }
 
 // Launch one batch.  `node` is the task node whose tensor bindings the batch uses.
-void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBinding>& T, const int64_t* rec_dev,
-                  uint64_t& launches) {
+void launch_batch_body(Program& P, Batch& B, const Node& node, std::vector<TensorBinding>& T, const int64_t* rec_dev,
+                       uint64_t& launches) {
     const KernelDef& kd = P.plan.kernels[B.kernel];
     KernelImpl& ki = P.impls[B.kernel];
     dev::TaskBatch tb{};
@@ -1597,6 +1602,31 @@ bool plan_pipeline(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, 
     }
     pp.C = C;
     return true;
+}
+
+// launch_batch_body, bracketed by CUDA events on the launch stream when the "kernel_events" option is on
+// (per-kernel device time, read by ptowsp_cuda_kernel_times).
+void launch_batch(Program& P, Batch& B, const Node& node, std::vector<TensorBinding>& T, const int64_t* rec_dev,
+                  uint64_t& launches) {
+    if (!P.opt_kernel_events) {
+        launch_batch_body(P, B, node, T, rec_dev, launches);
+        return;
+    }
+    auto take = [&P]() {
+        cudaEvent_t e = nullptr;
+        if (!P.kev_free.empty()) {
+            e = P.kev_free.back();
+            P.kev_free.pop_back();
+        } else {
+            PW_CUDA(cudaEventCreate(&e));
+        }
+        return e;
+    };
+    Program::KernelEvent ke{B.kernel, take(), take()};
+    PW_CUDA(cudaEventRecord(ke.start, P.stream));
+    launch_batch_body(P, B, node, T, rec_dev, launches);
+    PW_CUDA(cudaEventRecord(ke.end, P.stream));
+    P.kev_pending.push_back(ke);
 }
 
 bool run_pipelined(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, uint64_t& launches) {
@@ -2352,6 +2382,42 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
                                            ((err_host & dev::kErrShape) ? " (size beyond kernel limit)" : ""));
     }
     return makespan;
+}
+
+std::string kernel_times(Program& P) {
+    PW_CUDA(cudaSetDevice(P.device));
+    if (P.kev_totals.size() < P.plan.kernels.size()) P.kev_totals.resize(P.plan.kernels.size(), {0, 0.0});
+    for (auto& ke : P.kev_pending) {
+        PW_CUDA(cudaEventSynchronize(ke.end));
+        float ms = 0.f;
+        PW_CUDA(cudaEventElapsedTime(&ms, ke.start, ke.end));
+        auto& t = P.kev_totals[static_cast<size_t>(ke.kernel)];
+        t.first += 1;
+        t.second += ms;
+        P.kev_free.push_back(ke.start);
+        P.kev_free.push_back(ke.end);
+    }
+    P.kev_pending.clear();
+    std::string out = "{";
+    for (size_t k = 0; k < P.plan.kernels.size(); ++k) {
+        if (k) out += ",";
+        char buf[160];
+        std::snprintf(buf, sizeof buf, "\"launches\":%llu,\"ms\":%.6f}", static_cast<unsigned long long>(P.kev_totals[k].first),
+                      P.kev_totals[k].second);
+        out += "\"" + P.plan.kernels[k].name + "\":{" + buf;
+    }
+    return out + "}";
+}
+
+void reset_kernel_times(Program& P) {
+    // unread events are dropped; they go back to the pool once their work is done
+    for (auto& ke : P.kev_pending) {
+        cudaEventSynchronize(ke.end);
+        P.kev_free.push_back(ke.start);
+        P.kev_free.push_back(ke.end);
+    }
+    P.kev_pending.clear();
+    P.kev_totals.assign(P.plan.kernels.size(), {0, 0.0});
 }
 
 uint64_t run_single_task(Program& P, const std::string& kernel, const KernelTaskDesc* task) {

@@ -203,6 +203,12 @@ struct Program {
     int* err_dev = nullptr;
     int status = 0;
     int64_t opt_cache = 1, opt_chunks = 32, opt_sync = 1, opt_dry = 0, opt_stage_scratch_mb = 2048;
+    int64_t opt_kernel_events = 0;       // bracket every batch launch with CUDA events (per-kernel device time)
+    struct KernelEvent { int kernel; cudaEvent_t start, end; };
+    std::vector<KernelEvent> kev_pending;  // recorded, not yet read
+    std::vector<cudaEvent_t> kev_free;     // event pool
+    std::vector<std::pair<uint64_t, double>> kev_totals;  // per kernel: launches, device ms
+    std::string kernel_times_json;
     std::vector<char*> dev_bufs;         // host-staged tensor buffers (by tensor id)
     std::vector<size_t> dev_caps;
     void* scratch = nullptr;
@@ -218,6 +224,8 @@ std::unique_ptr<Program> compile_program(const char* text, size_t len, int devic
 uint64_t run_program(Program& p, RuntimeContext* ctx);
 uint64_t run_single_task(Program& p, const std::string& kernel, const KernelTaskDesc* task);
 std::string describe_program(const Program& p);
+std::string kernel_times(Program& p);   // per-kernel launches and device ms since the last reset (JSON)
+void reset_kernel_times(Program& p);
 
 // Error helpers (thread-local message).
 void set_error(const std::string& msg);

@@ -109,6 +109,8 @@ def load_library() -> C.CDLL:
     lib.ptowsp_cuda_set_option.restype = C.c_int
     lib.ptowsp_cuda_last_timing.argtypes = [C.c_void_p, C.POINTER(Timing)]
     lib.ptowsp_cuda_last_timing.restype = C.c_int
+    lib.ptowsp_cuda_kernel_times.argtypes = [C.c_void_p]
+    lib.ptowsp_cuda_kernel_times.restype = C.c_char_p
     lib.ptowsp_cuda_describe.argtypes = [C.c_void_p]
     lib.ptowsp_cuda_describe.restype = C.c_char_p
     lib.ptowsp_cuda_destroy.argtypes = [C.c_void_p]
@@ -272,6 +274,10 @@ class CudaExecutable:
         t = Timing()
         self._lib.ptowsp_cuda_last_timing(self._h, C.byref(t))
         return {k: getattr(t, k) for k, _ in Timing._fields_}
+
+    def kernel_times(self) -> dict:
+        """Per-kernel ``{"launches": n, "ms": t}`` since ``set_option("kernel_events", 1)`` (CUDA events)."""
+        return json.loads(self._lib.ptowsp_cuda_kernel_times(self._h).decode())
 
     def describe(self) -> dict:
         return json.loads(self._lib.ptowsp_cuda_describe(self._h).decode())
