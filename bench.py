@@ -802,18 +802,20 @@ def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
 
     for _ in range(args.warmup):
         step(darr)
+    launches_per_step = int(ex.timing()["launches"])  # a replayed step launches the same kernels every time
     D.barrier()
     ex.set_option("kernel_events", 1)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches = 0
     with NvmlClockSampler(gpu_index(D.local_rank), _pci_bus_id(torch, dev)) as clk:
         D.barrier()
+        h0 = time.perf_counter()
         e0.record(stream)
         for _ in range(args.steps):
             step(darr)
-            launches += int(ex.timing()["launches"])
         e1.record(stream)
+        host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
         D.barrier()
+    launches = launches_per_step * args.steps
     clocks = clk.summary()
     ms = e0.elapsed_time(e1)
     ms_max = D.max(ms)
@@ -866,6 +868,7 @@ def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
                    "parallelism": f"P(batch) over {world} rank(s), {case.method} shares (ShardedExecutable)",
                    "l2": "every step reads inputs larger than the 126 MB L2 (no flush)"},
         "gpu_launches": launches,
+        "host_ms_per_step": round(host_ms, 4),
         "roofline": {"bound": case.bound, "achieved": round(achieved, 2), "peak": peak, "unit": case.unit,
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": case.kernel,

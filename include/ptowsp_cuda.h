@@ -204,8 +204,10 @@ PTOWSP_API void ptowsp_cuda_destroy(ptowsp_program* prog);
 /* (ptowsp_cuda_noalloc_scratch_bytes tells how much it needs),                */
 /* PTOWSP_ERR_DEVICE for a page id outside the cache or a length beyond the   */
 /* page table.  Calls share the array: two calls that overlap on the GPU race. */
-/* The first call on a device looks up the array's address; make it before    */
-/* any stream capture.                                                         */
+/* The first call on a device looks up the array's address and loads the     */
+/* code of every kernel this entry point can launch (with lazy module loading  */
+/* that takes device memory once); make it before any stream capture.  Calls  */
+/* after the first take no device memory, whatever their GQA group.           */
 PTOWSP_API int ptowsp_cuda_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                                 const int32_t* page_table, const int32_t* kv_len, void* out,
                                                 int num_requests, int num_kv_heads, int group, int head_dim,

@@ -1324,7 +1324,10 @@ namespace ptowsp::dev {
 //    writes first -- but two calls whose work overlaps on the GPU (different
 //    streams, or different host threads) race on the array;
 //  * the first call on a device looks up the array's device address (with that
-//    device current); make that first call before any stream capture.
+//    device current) and loads every kernel the entry point can launch (lazy
+//    module loading would otherwise load code, and take device memory, at a
+//    later call); make that first call before any stream capture, and count
+//    on later calls, not the first, to take no device memory.
 // ===========================================================================
 
 namespace {
@@ -1367,6 +1370,22 @@ void* noalloc_scratch_address(int device, cudaError_t* err) {
         void* p = nullptr;
         *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // device `device` is current here
         if (*err != cudaSuccess) return nullptr;
+        // With lazy module loading a kernel's code is put on the device at its first launch, which takes device
+        // memory.  Load every kernel this entry point can launch now, at the first call on the device, so that no
+        // later call -- whatever its GQA group or launch path -- loads anything.
+        cudaFuncAttributes fa;
+        const void* kernels[] = {
+            reinterpret_cast<const void*>(noalloc_fill_records),
+            reinterpret_cast<const void*>(paged_decode_tma_kernel<1>), reinterpret_cast<const void*>(paged_decode_tma_kernel<2>),
+            reinterpret_cast<const void*>(paged_decode_tma_kernel<4>), reinterpret_cast<const void*>(paged_decode_tma_kernel<8>),
+            reinterpret_cast<const void*>(paged_decode_chunk_kernel<1>), reinterpret_cast<const void*>(paged_decode_chunk_kernel<2>),
+            reinterpret_cast<const void*>(paged_decode_chunk_kernel<4>), reinterpret_cast<const void*>(paged_decode_chunk_kernel<8>),
+            reinterpret_cast<const void*>(paged_decode_merge_kernel<1>), reinterpret_cast<const void*>(paged_decode_merge_kernel<2>),
+            reinterpret_cast<const void*>(paged_decode_merge_kernel<4>), reinterpret_cast<const void*>(paged_decode_merge_kernel<8>)};
+        for (const void* k : kernels) {
+            *err = cudaFuncGetAttributes(&fa, k);
+            if (*err != cudaSuccess) return nullptr;
+        }
         addr[device] = p;
     }
     *err = cudaSuccess;

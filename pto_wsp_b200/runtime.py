@@ -189,48 +189,63 @@ class CudaExecutable:
     def run(self, arrays, axis_sizes) -> int:
         return self.run_with_symbols(arrays, axis_sizes, {}, {})
 
+    def _context(self) -> RuntimeContext:
+        """The RuntimeContext of this executable: its callbacks are made once and read ``self._call``, the
+        current call's tensors, axis sizes, symbols and slots (the reference builds the same struct per run,
+        ``pto_codegen.cpp:3453-3505``)."""
+        if getattr(self, "_ctx", None) is None:
+            st = self._call = {"infos": [], "axis": {}, "syms": {}, "sptr": {}, "slots": [0] * 256}
+
+            def get_axis_size(_ctx, name):
+                return st["axis"].get(name, 0)
+
+            def get_symbol_u64(_ctx, sid):
+                return st["syms"].get(sid, 0)
+
+            def get_symbol_ptr(_ctx, sid):
+                return st["sptr"].get(sid, None)
+
+            def get_slot_u64(_ctx, i):
+                return st["slots"][i] if i < 256 else 0
+
+            def set_slot_u64(_ctx, i, v):
+                if i < 256:
+                    st["slots"][i] = v
+
+            def get_tensor_ptr(_ctx, tid):
+                infos = st["infos"]
+                return infos[tid][0] if tid < len(infos) else None
+
+            def get_tensor_stride(_ctx, tid, dim):
+                infos = st["infos"]
+                if tid >= len(infos) or dim >= len(infos[tid][1]):
+                    return 0
+                return infos[tid][1][dim] & 0xFFFFFFFFFFFFFFFF
+
+            def get_kernel(_ctx, kid):
+                return None
+
+            self._cbs = (_AXIS_FN(get_axis_size), _SYMU_FN(get_symbol_u64), _SYMP_FN(get_symbol_ptr),
+                         _SLOTG_FN(get_slot_u64), _SLOTS_FN(set_slot_u64), _TPTR_FN(get_tensor_ptr),
+                         _TSTR_FN(get_tensor_stride), _KERN_FN(get_kernel))
+            self._ctx = RuntimeContext(*self._cbs, None)
+        return self._ctx
+
     def run_with_symbols(self, arrays, axis_sizes, symbols_u64, symbols_ptr) -> int:
-        infos = [_array_info(a) for a in arrays]
-        axis = {str(k).encode(): int(v) for k, v in (axis_sizes or {}).items()}
-        syms = {int(k) & 0xFFFFFFFFFFFFFFFF: int(v) & 0xFFFFFFFFFFFFFFFF for k, v in (symbols_u64 or {}).items()}
-        sptr = {int(k) & 0xFFFFFFFFFFFFFFFF: _array_info(v)[0] for k, v in (symbols_ptr or {}).items()}
-        keep = list(arrays) + list((symbols_ptr or {}).values())  # alive for the call
-        slots = [0] * 256
-
-        def get_axis_size(_ctx, name):
-            return axis.get(name, 0)
-
-        def get_symbol_u64(_ctx, sid):
-            return syms.get(sid, 0)
-
-        def get_symbol_ptr(_ctx, sid):
-            return sptr.get(sid, None)
-
-        def get_slot_u64(_ctx, i):
-            return slots[i] if i < 256 else 0
-
-        def set_slot_u64(_ctx, i, v):
-            if i < 256:
-                slots[i] = v
-
-        def get_tensor_ptr(_ctx, tid):
-            return infos[tid][0] if tid < len(infos) else None
-
-        def get_tensor_stride(_ctx, tid, dim):
-            if tid >= len(infos) or dim >= len(infos[tid][1]):
-                return 0
-            return infos[tid][1][dim] & 0xFFFFFFFFFFFFFFFF
-
-        def get_kernel(_ctx, kid):
-            return None
-
-        cbs = (_AXIS_FN(get_axis_size), _SYMU_FN(get_symbol_u64), _SYMP_FN(get_symbol_ptr),
-               _SLOTG_FN(get_slot_u64), _SLOTS_FN(set_slot_u64), _TPTR_FN(get_tensor_ptr),
-               _TSTR_FN(get_tensor_stride), _KERN_FN(get_kernel))
-        ctx = RuntimeContext(*cbs, None)
-        cycles = self._lib.ptowsp_cuda_main(self._h, C.byref(ctx), None)
+        ctx = self._context()
+        st = self._call
+        st["infos"] = [_array_info(a) for a in arrays]
+        st["axis"] = {str(k).encode(): int(v) for k, v in (axis_sizes or {}).items()}
+        st["syms"] = {int(k) & 0xFFFFFFFFFFFFFFFF: int(v) & 0xFFFFFFFFFFFFFFFF for k, v in (symbols_u64 or {}).items()}
+        st["sptr"] = {int(k) & 0xFFFFFFFFFFFFFFFF: _array_info(v)[0] for k, v in (symbols_ptr or {}).items()}
+        st["slots"] = [0] * 256  # slots start at zero every run
+        keep = (arrays, symbols_ptr)  # alive for the call
+        try:
+            cycles = self._lib.ptowsp_cuda_main(self._h, C.byref(ctx), None)
+        finally:
+            st["infos"], st["sptr"] = [], {}
+            del keep
         rc = self._lib.ptowsp_cuda_status(self._h)
-        del keep
         if rc != PTOWSP_OK:
             raise PtoWspCudaError(rc, _last_error())
         return int(cycles)

@@ -331,7 +331,9 @@ class ShardedExecutable:
         if self.n_static is None:
             if n is None:
                 raise ShardError("the outer axis is DenseDyn: give its size in axis_sizes")
-            self.units = partition(n, self.world, self.costs[:n] if self.costs is not None else None, self.method)
+            if getattr(self, "_units_n", None) != n:  # the split depends only on n (and the fixed costs)
+                self.units = partition(n, self.world, self.costs[:n] if self.costs is not None else None, self.method)
+                self._units_n = n
         return self.units[self.rank]
 
     def executable(self, n_local: int) -> Any:

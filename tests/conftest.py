@@ -8,22 +8,24 @@
 
 from __future__ import annotations
 
-import os
 import sys
 from pathlib import Path
 
 import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
-REF = Path(os.environ.get("PTOWSP_REFERENCE", "/root/reference"))
 for p in (ROOT, ROOT / "oracle"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
 
+from refpath import reference_root  # noqa: E402
+
+REF = reference_root()  # PTOWSP_REFERENCE, else a `reference` checkout beside the repo; None: tests skip
+
 
 def reference_available() -> bool:
     ext = list((ROOT / "oracle" / "_ref").glob("pto_ir_cpp*.so"))
-    return (REF / "python" / "pto_wsp").is_dir() and bool(ext)
+    return REF is not None and (REF / "python" / "pto_wsp").is_dir() and bool(ext)
 
 
 def import_reference():

@@ -33,8 +33,13 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("PTOWSP_REFERENCE", "/root/reference"))
-sys.path[:0] = [str(ROOT), str(ROOT / "oracle"), str(ROOT / "oracle" / "_ref"), str(REF / "python")]
+sys.path[:0] = [str(ROOT), str(ROOT / "oracle")]
+from refpath import reference_root  # noqa: E402
+
+REF = reference_root()
+if REF is None:
+    raise SystemExit("reference checkout not found: set PTOWSP_REFERENCE")
+sys.path[:0] = [str(ROOT / "oracle" / "_ref"), str(REF / "python")]
 
 from cpu_sim import CpuSim  # noqa: E402
 

@@ -1,25 +1,25 @@
 """bgemm on tcgen05 vs the oracle and an fp64 recompute (-m gpu).
 
 Tolerance (north_star): fp16 contractions within 2e-3 relative of an fp64
-recompute -- checked element-wise as |C - C64| <= 2e-3 * (|C64| + rms(C64)).
+recompute -- checked element-wise as a plain relative error on every element
+with |C64| >= 1e-2 rms(C64) (smaller ones: absolute 2e-3 x that floor).  At
+full size all 64 batch elements are recomputed in fp64 on the GPU.
 """
 
 import numpy as np
 import pytest
 from cpu_sim import CpuSim
 
+from tolerance import RTOL_F16_MMA, assert_rel, rms
+
 from pto_wsp_b200 import workloads
 from pto_wsp_b200.runtime import CudaExecutable
 
 pytestmark = pytest.mark.gpu
-RTOL = 2e-3
 
 
 def check(c, ref):
-    ref = np.asarray(ref, np.float64)
-    scale = np.sqrt(np.mean(ref * ref)) + 1e-30
-    err = np.abs(np.asarray(c, np.float64) - ref)
-    assert np.all(err <= RTOL * (np.abs(ref) + scale)), float((err / (np.abs(ref) + scale)).max())
+    return assert_rel(c, ref, RTOL_F16_MMA, 1e-2 * rms(ref))
 
 
 def inputs(rng, B, M, N, K):
@@ -77,7 +77,16 @@ def test_bgemm_config3_full_size(require_cuda):
     c = torch.full((B, M, N), float("nan"), device="cuda")
     ex = CudaExecutable(workloads.bgemm_plan(B, M, N, K))
     ex.run_with_symbols(list(workloads.bgemm_views(a, b, c)), {}, {}, {})
-    for bi in (0, 37, 63):
-        ref = (a[bi].double() @ b[bi].double()).cpu().numpy()
-        check(c[bi].cpu().numpy(), ref)
     assert not torch.isnan(c).any()
+    worst = 0.0
+    for b0 in range(0, B, 8):  # every batch element, recomputed in fp64 on the GPU, 8 at a time
+        ref = torch.bmm(a[b0:b0 + 8].double(), b[b0:b0 + 8].double())
+        floor = 1e-2 * float(ref.pow(2).mean().sqrt())
+        err = (c[b0:b0 + 8].double() - ref).abs()
+        big = ref.abs() >= floor
+        rel = float((err[big] / ref.abs()[big]).max())
+        assert rel <= RTOL_F16_MMA, (b0, rel)
+        assert float(err[~big].max()) <= RTOL_F16_MMA * floor if bool((~big).any()) else True
+        worst = max(worst, rel)
+        del ref, err, big
+    print(f"bgemm config 3: worst relative error over all 64 batch elements {worst:.3g}")

@@ -1,25 +1,26 @@
 """Paged GQA decode vs the oracle / fp64 (-m gpu).
 
-Tolerance: f16 output of an f32 softmax over f16 K/V: |O - O64| <= 2e-3 * (|O64| + rms(O64))
-(the north_star's 2e-3 relative bar for f16 contractions).
+Tolerance: f16 output of an f32 softmax over f16 K/V, against the oracle's fp64 task: plain relative error
+<= 2e-3 (the north_star's bar for f16 contractions) on every element with |O64| >= 5e-2 rms(O64); smaller
+elements within 2e-3 x that floor.  At full size every request is recomputed in fp64 on the GPU.
 """
 
 import numpy as np
 import pytest
 from cpu_sim import CpuSim
 
+from tolerance import RTOL_F16_MMA, assert_rel, rms
+
 from pto_wsp_b200 import workloads
 from pto_wsp_b200.runtime import CudaExecutable
 
 pytestmark = pytest.mark.gpu
+FLOOR = 5e-2
 
 
 def check(got, ref):
-    got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
-    scale = np.sqrt(np.mean(ref * ref)) + 1e-12
-    err = np.abs(got - ref)
-    assert np.all(err <= 2e-3 * (np.abs(ref) + scale)), float((err / (np.abs(ref) + scale)).max())
+    return assert_rel(got, ref, RTOL_F16_MMA, FLOOR * rms(ref))
 
 
 @pytest.mark.parametrize("lengths", [[0, 1, 16, 17, 512, 513, 1024, 1500], [700, 33, 2049]])
@@ -79,21 +80,33 @@ def test_decode_dense_dyn_axis_of_size_zero(require_cuda):
 
 
 def test_decode_config4_full_size(require_cuda):
+    import math
+
     torch = pytest.importorskip("torch")
     rng = np.random.default_rng(4)
     R = 64
     plan, arrays = workloads.decode_inputs(rng, R)  # KV lengths U{512..8192}, 8 kv heads, GQA 4, d=128
     dev = [torch.from_numpy(a).cuda() for a in arrays]
+    dev[5].fill_(float("nan"))
     ex = CudaExecutable(plan)
     ex.run_with_symbols(dev, {"b": R}, {}, {})
     out = dev[5].cpu().numpy()
-    # fp64 recompute of a few requests through the oracle's task (same page walk)
-    sub = [0, 17, 63]
-    for r in sub:
+    # the oracle's own task (numpy, fp64) on two requests ...
+    for r in (0, 63):
         one = [a.copy() for a in arrays]
-        CpuSim(workloads.decode_plan(R, 8, 4, 128, arrays[1].shape[0], arrays[3].shape[1])).run(
-            one, axis_sizes={"b": r + 1})
+        CpuSim(plan).run(one, axis_sizes={"b": r + 1})
         check(out[r], one[5][r])
+    # ... and every request recomputed in fp64 on the GPU through the same page walk
+    q, kc, vc, pt, kl = dev[:5]
+    lens = arrays[4].reshape(-1)
+    for r in range(R):
+        L = int(lens[r])
+        pages = pt[r, : (L + 15) // 16].long()
+        k = kc[pages].reshape(-1, 8, 128)[:L].double()
+        v = vc[pages].reshape(-1, 8, 128)[:L].double()
+        s = torch.einsum("hgd,thd->hgt", q[r].double(), k) / math.sqrt(128)
+        ref = torch.einsum("hgt,thd->hgd", torch.softmax(s, -1), v).cpu().numpy()
+        check(out[r], ref)
 
 
 @pytest.mark.parametrize("group", [1, 2, 8])

@@ -62,13 +62,15 @@ def test_softmax_vs_oracle(B, T, R, C, require_cuda):
 
 
 @pytest.mark.parametrize("C", [96, 200])
-def test_row_ops_with_odd_widths_take_the_tile_program(C, require_cuda):
+def test_row_ops_with_odd_widths_run_the_nvrtc_row_program(C, require_cuda):
     rng = np.random.default_rng(2)
     x = softmax_input(rng, (2, 3, 8, C))
     plan = workloads.softmax_plan(2, 3, 8, C)
     y = np.zeros_like(x)
-    CudaExecutable(plan).run_with_symbols([x, y], {}, {}, {})
+    ex = CudaExecutable(plan)
+    ex.run_with_symbols([x, y], {}, {}, {})
     np.testing.assert_allclose(y, softmax64(x), rtol=RTOL, atol=1e-30)
+    assert ex.describe()["kernels"][0].get("row_kernel") == "loaded"
 
 
 def test_device_resident_tensors_run_in_place(require_cuda):
@@ -126,5 +128,14 @@ def test_full_size_config_properties(workload, require_cuda):
     ys = y.reshape(B * T, R, C)[idx].cpu().numpy()
     ref = softmax64(xs) if workload == "softmax" else rms64(xs)
     np.testing.assert_allclose(ys, ref, rtol=RTOL, atol=1e-30 if workload == "softmax" else 1e-7)
+    # every tile against the C port of the CPU-sim task (reference op order, all host threads), 1e-5 relative
+    import cpu_native
+
+    xh, yh = x.reshape(B * T, R, C).cpu().numpy(), y.reshape(B * T, R, C).cpu().numpy()
     del x, y
     torch.cuda.empty_cache()
+    port = np.empty_like(xh)
+    cpu_native.row_tiles(workload, xh, port, R, C)
+    for t0 in range(0, B * T, 8192):
+        np.testing.assert_allclose(yh[t0:t0 + 8192], port[t0:t0 + 8192], rtol=RTOL,
+                                   atol=1e-30 if workload == "softmax" else 1e-7)

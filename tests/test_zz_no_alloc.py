@@ -8,16 +8,20 @@ fixed array of device memory owned by the library.
 
 This test calls it through the C ABI twice in a row (the second call with other
 lengths, so stale scratch from the first call would show) and checks each
-result against the regular entry point (`ptowsp_cuda_main` on the decode plan)
-with the decode tests' tolerance.  It also checks that the second call takes no
-device memory, and that a workload too big for the fixed array is refused.
-The file name makes pytest collect it last.
+result against the CPU oracle's decode task (the decode tests' tolerance) and
+bit for bit against the regular entry point (`ptowsp_cuda_main` on the decode
+plan, same kernels).  It also checks that calls after the first take no device
+memory, a later one with another GQA group included, and that a workload too
+big for the fixed array is refused.  The file name makes pytest collect it last.
 """
 
 import ctypes as C
 
 import numpy as np
 import pytest
+from cpu_sim import CpuSim
+
+from tolerance import RTOL_F16_MMA, assert_rel, rms
 
 from pto_wsp_b200 import workloads
 from pto_wsp_b200.runtime import CudaExecutable, load_library
@@ -26,10 +30,14 @@ pytestmark = pytest.mark.gpu
 
 
 def check(got, ref):
-    got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
-    scale = np.sqrt(np.mean(ref * ref)) + 1e-12
-    assert np.all(np.abs(got - ref) <= 2e-3 * (np.abs(ref) + scale))
+    assert_rel(got, ref, RTOL_F16_MMA, 5e-2 * rms(ref))
+
+
+def oracle(plan, arrays, R):
+    ref = [a.copy() for a in arrays]
+    CpuSim(plan).run(ref, axis_sizes={"b": R})
+    return ref[5]
 
 
 def noalloc_fn():
@@ -62,7 +70,7 @@ def run_regular(plan, arrays, R):
     return got[5]
 
 
-def test_noalloc_matches_regular_entry_point_twice(require_cuda):
+def test_noalloc_matches_oracle_and_regular_entry_point_twice(require_cuda):
     torch = pytest.importorskip("torch")
     lib, f, need = noalloc_fn()
     rng = np.random.default_rng(7)
@@ -75,7 +83,9 @@ def test_noalloc_matches_regular_entry_point_twice(require_cuda):
     d1 = to_device(torch, a1)
     rc = call_noalloc(f, torch, d1, R)
     assert rc == 0, lib.ptowsp_cuda_last_error()
-    check(d1[5].cpu().numpy(), run_regular(plan1, a1, R))
+    out1 = d1[5].cpu().numpy()
+    check(out1, oracle(plan1, a1, R))
+    np.testing.assert_array_equal(out1, run_regular(plan1, a1, R))
 
     d2 = to_device(torch, a2)  # inputs of the second call are allocated by the test, before measuring
     free_before = torch.cuda.mem_get_info()[0]
@@ -84,8 +94,30 @@ def test_noalloc_matches_regular_entry_point_twice(require_cuda):
     assert rc == 0, lib.ptowsp_cuda_last_error()
     assert free_after == free_before  # the call itself took no device memory
     out2 = d2[5].cpu().numpy()
-    check(out2, run_regular(plan2, a2, R))
     assert not np.isnan(out2.astype(np.float32)).any()
+    check(out2, oracle(plan2, a2, R))
+    np.testing.assert_array_equal(out2, run_regular(plan2, a2, R))
+
+
+def test_noalloc_other_group_takes_no_memory(require_cuda):
+    torch = pytest.importorskip("torch")
+    lib, f, need = noalloc_fn()
+    rng = np.random.default_rng(9)
+    # a first call with GQA group 4 (the first on this device when the test runs alone: it sets the device up)
+    _, a4 = workloads.decode_inputs(rng, 3, lengths=[10, 600, 2000])
+    d4 = to_device(torch, a4)
+    assert call_noalloc(f, torch, d4, 3) == 0, lib.ptowsp_cuda_last_error()
+    # then group 2 and group 8, which no earlier call launched: no device memory either
+    for KVH, G in ((4, 2), (2, 8)):
+        R = 5
+        plan, arrays = workloads.decode_inputs(rng, R, kv_heads=KVH, group=G, lengths=[1, 700, 1600, 33, 4000])
+        d = to_device(torch, arrays)
+        free_before = torch.cuda.mem_get_info()[0]
+        rc = call_noalloc(f, torch, d, R, KVH=KVH, G=G)
+        free_after = torch.cuda.mem_get_info()[0]
+        assert rc == 0, lib.ptowsp_cuda_last_error()
+        assert free_after == free_before, (G, free_before - free_after)
+        check(d[5].cpu().numpy(), oracle(plan, arrays, R))
 
 
 def test_noalloc_rejects_work_beyond_the_fixed_array(require_cuda):
