@@ -601,9 +601,30 @@ void collect_depths(const Plan& plan, const Node& n, std::vector<int>& depth) {
             collect_depths(plan, *n.then_n, depth);
             collect_depths(plan, *n.else_n, depth);
             break;
-        case Node::Kind::Task:
+        case Node::Kind::Task: {
             for (auto& ta : n.tensor_args) see(ta);
+            // A tile larger than its view reaches into the neighbouring views (the reference walks such tasks in
+            // program order, so the overlap is ordered): the tensor's hazard key is then the whole tensor.
+            if (n.kernel_index < 0 || n.kernel_index >= static_cast<int>(plan.kernels.size())) break;
+            const KernelDef& kd = plan.kernels[n.kernel_index];
+            for (const auto& kp : kd.params) {
+                if (kp.tensor_index < 0 || kp.tensor_index >= static_cast<int>(n.param_to_arg.size())) continue;
+                const TensorArg& ta = n.tensor_args[n.param_to_arg[kp.tensor_index]];
+                const auto& shape = plan.tensors[ta.tensor].shape;
+                const int first = ta.base_rank - ta.view_rank;  // the view's first dimension
+                int64_t vr = 1, vc = 1;
+                if (ta.view_rank >= 2) {
+                    vr = first < static_cast<int>(shape.size()) ? shape[first] : -1;
+                    vc = first + 1 < static_cast<int>(shape.size()) ? shape[first + 1] : -1;
+                } else if (ta.view_rank == 1) {
+                    vc = first < static_cast<int>(shape.size()) ? shape[first] : -1;
+                }
+                const bool known = vr > 0 && vc > 0;
+                const bool rows_over = ta.view_rank >= 2 && kp.v.rows > vr;  // a 1-D view repeats its row (s3 = 0)
+                if (known && (rows_over || kp.v.cols > vc)) depth[ta.tensor] = 0;
+            }
             break;
+        }
         case Node::Kind::SlotLoad:
             see(n.slot_tensor);
             break;

@@ -305,8 +305,9 @@ constexpr int kStageBytes = 4 * kHalfBox;     // K lo, K hi, V lo, V hi
 constexpr int kRingBytes = kMmaStages * kStageBytes;
 constexpr int kBarOffset = kRingBytes;  // full[S], empty[S], abort, last flag
 constexpr int kPageIdsOffset = kBarOffset + ((16 * kMmaStages + 8 + 127) / 128) * 128;  // the chunk's page ids
-constexpr int kPbufOffset = kPageIdsOffset + ((kChunk / 16 * 4 + 127) / 128) * 128;  // per-warp P, 16 tok x 8 q f16
-constexpr int kMmaSmemBytes = kPbufOffset + kMmaConsumers * 256 + 1024;  // + 1024-byte alignment slack
+// per-warp P as two f16 parts (high, then low), 16 tok x 8 q each
+constexpr int kPbufOffset = kPageIdsOffset + ((kChunk / 16 * 4 + 127) / 128) * 128;
+constexpr int kMmaSmemBytes = kPbufOffset + kMmaConsumers * 512 + 1024;  // + 1024-byte alignment slack
 
 template <int G>
 struct MmaCombine {  // per consumer warp, aliased onto the ring once every page has been consumed
@@ -335,6 +336,11 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);
+}
+// The rounding remainder of pack_h2: x - f16(x), itself rounded to f16.  P = high + low carries ~22 bits of each
+// probability into the P.V contraction (f16 alone carries 11, which shows as a 5e-4 relative error of the terms).
+__device__ __forceinline__ uint32_t pack_h2_rem(float lo, float hi) {
+    return pack_h2(lo - __half2float(__float2half_rn(lo)), hi - __half2float(__float2half_rn(hi)));
 }
 // Byte offset of (token, dim) inside one page's 128-byte-swizzled K or V slice.
 __device__ __forceinline__ uint32_t swz(int tok, int d) {
@@ -456,7 +462,7 @@ __global__ void __launch_bounds__(kMmaThreads) paged_decode_tma_kernel(const __g
             }
         }
         const float sc = 1.4426950408889634f / sqrtf(static_cast<float>(kHeadDim));  // log2(e) / sqrt(D)
-        uint8_t* pbuf = dsm + kPbufOffset + warp * 256;
+        uint8_t* pbuf = dsm + kPbufOffset + warp * 512;  // [high part | low part]
         const uint32_t pbuf_u = tc::smem_u32(pbuf);
         const int mi = lane >> 3, r8 = lane & 7;
         for (int j = warp; j < npages && !*abort_flag; j += kMmaConsumers) {
@@ -501,17 +507,22 @@ __global__ void __launch_bounds__(kMmaThreads) paged_decode_tma_kernel(const __g
                     o[mt][3] *= c1;
                 }
             }
-            // P (token-major, 16 B per token row) -> B operand P^T via a transposing fragment load
+            // P (token-major, 16 B per token row) -> B operand P^T via a transposing fragment load, as a high
+            // and a low f16 part; both multiply the same V^T fragments
             *reinterpret_cast<uint32_t*>(pbuf + g * 16 + tq * 4) = pack_h2(p00, p01);
             *reinterpret_cast<uint32_t*>(pbuf + (g + 8) * 16 + tq * 4) = pack_h2(p10, p11);
+            *reinterpret_cast<uint32_t*>(pbuf + 256 + g * 16 + tq * 4) = pack_h2_rem(p00, p01);
+            *reinterpret_cast<uint32_t*>(pbuf + 256 + (g + 8) * 16 + tq * 4) = pack_h2_rem(p10, p11);
             __syncwarp();
-            uint32_t pb0, pb1;
+            uint32_t pb0, pb1, pl0, pl1;
             ldsm_x2_t(pbuf_u + (lane & 15) * 16, pb0, pb1);
+            ldsm_x2_t(pbuf_u + 256 + (lane & 15) * 16, pl0, pl1);
             // O^T (128 dims x 8 queries) += V^T P^T: A = V^T through transposing loads of the token-major rows
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) {
                 uint32_t a[4];
                 ldsm_x4_t(vb + swz(r8 + 8 * (mi >> 1), 16 * mt + 8 * (mi & 1)), a);
+                mma_16816(o[mt], a, pl0, pl1);
                 mma_16816(o[mt], a, pb0, pb1);
             }
             __syncwarp();

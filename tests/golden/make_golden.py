@@ -4,14 +4,21 @@ Runs, unchanged, the reference's example drivers (``examples/*/*_example.py``)
 and its codegen execution tests (``tests/test_codegen_*.py``) with the CUDA
 target redirected through ``pto_wsp_b200.frontend``: the reference frontend
 builds each workload and ``ir::Module``, the plan is recorded, and the CPU
-oracle (``oracle/cpu_sim.py``) executes it in place of the CPU-sim artifact
-(whose pto-isa dependency is absent).  The reference scripts then apply their
-own checks -- numpy goldens, exact ``atol=0`` outputs, exact cycle counts --
-to the oracle's results, which pins the oracle.  Every run is saved as a case:
-plan, input buffers (with the exact numpy view layout), axis sizes, symbols,
-the oracle's output buffers and its cycle count.
+oracle (``oracle/cpu_sim.py``) executes it.  The reference scripts then apply
+their own checks -- numpy goldens, exact ``atol=0`` outputs, exact cycle counts
+-- to the oracle's results, which pins the oracle.
 
-    python tests/golden/make_golden.py      # writes tests/golden/ref_cases.{json,npz}
+Every module is also compiled by the reference's own codegen into its CPU-sim
+artifact (``workload_main.cpp`` + ``kernel_*.cpp``, built by oracle/Makefile's
+``ref`` module with the clean-room pto-isa stand-in ``oracle/ptoisa``) and run
+through the reference's own ``CodegenExecutable`` on a copy of the same
+inputs: its cycle count must equal the oracle's, and its output buffers are
+saved beside the oracle's (``c<i>_art<j>``) so that the CPU tests hold the two
+against each other.  Every run is saved as a case: plan, input buffers (with
+the exact numpy view layout), axis sizes, symbols, the oracle's and the
+artifact's output buffers and the cycle count.
+
+    PTOWSP_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Kernels with CPU C++ bodies (``cpp_src``) are skipped: the CUDA target rejects them.  That includes
 ``@ptoisa_kernel`` kernels (``tests/test_ptoisa_kernel_jit.py``), whose traced PTO-ISA calls reach the plan
@@ -48,6 +55,7 @@ from pto_wsp_b200 import frontend  # noqa: E402
 CASES: list[dict] = []
 ARRAYS: dict[str, np.ndarray] = {}
 CURRENT = {"name": "?", "tol": (0.0, 0.0)}
+LAST_MODULE: dict = {}  # the ir::Module of the workload being compiled (for its CPU-sim artifact)
 
 
 def _root(a: np.ndarray) -> np.ndarray:
@@ -77,6 +85,21 @@ def _layout(arrays: list[np.ndarray], prefix: str) -> tuple[list[dict], list[np.
     return descs, roots
 
 
+def _artifact(module):
+    """The reference CPU-sim artifact of `module`, loaded through the reference's own CodegenExecutable."""
+    from pto_wsp.ir_bridge import cpp
+
+    opts = cpp.CompileOptions()
+    opts.target = "cpu_sim"
+    res = cpp.compile_codegen(module, opts)
+    return cpp.CodegenExecutable(str(res["so_path"]), str(res["entrypoint"]))
+
+
+def _views_on(descs, roots):
+    return [np.ndarray(shape=tuple(d["shape"]), dtype=np.dtype(d["dtype"]), buffer=roots[d["root"]],
+                       offset=d["offset"], strides=tuple(d["strides"])) for d in descs]
+
+
 class RecordingExecutable:
     so_path = "<oracle>"
 
@@ -84,6 +107,7 @@ class RecordingExecutable:
         self.plan = plan
         self.entrypoint = f"{plan.get('name', 'main')}_main"
         self.sim = CpuSim(plan)
+        self.art = _artifact(LAST_MODULE["module"])
 
     def run_with_symbols(self, arrays, axis_sizes, symbols_u64, symbols_ptr):
         arrays = list(arrays)
@@ -94,9 +118,18 @@ class RecordingExecutable:
         name = f"{CURRENT['name']}#{sum(1 for c in CASES if c['name'].startswith(CURRENT['name'] + '#'))}"
         for i, r in enumerate(roots):
             ARRAYS[f"c{idx}_in{i}"] = np.frombuffer(r.tobytes(), dtype=np.uint8).copy()
+        # the reference's own artifact first, on a copy laid out exactly like the caller's buffers
+        art_roots = [r.copy() for r in roots]
+        art_views = _views_on(descs, art_roots)
+        art_cycles = int(self.art.run_with_symbols(
+            art_views[: len(arrays)], dict(axis_sizes), dict(symbols_u64),
+            {k: v for k, v in zip(sp_keys, art_views[len(arrays):])}))
         cycles = self.sim.run(arrays, axis_sizes, symbols_u64, symbols_ptr)
+        if art_cycles != int(cycles):
+            raise SystemExit(f"{name}: CPU-sim artifact cycles {art_cycles} != oracle {cycles}")
         for i, r in enumerate(roots):
             ARRAYS[f"c{idx}_out{i}"] = np.frombuffer(r.tobytes(), dtype=np.uint8).copy()
+            ARRAYS[f"c{idx}_art{i}"] = np.frombuffer(art_roots[i].tobytes(), dtype=np.uint8).copy()
             ARRAYS[f"c{idx}_dtype{i}"] = np.frombuffer(r.dtype.str.encode(), dtype=np.uint8).copy()
         CASES.append({
             "name": name, "plan": self.plan, "arrays": descs[: len(arrays)], "symbols_ptr": [
@@ -120,6 +153,15 @@ def _redirect_cpu_sim():
         return orig(self, target="cuda_sm100a" if target == "cpu_sim" else target, **kw)
 
     W.Workload.compile = comp
+    B = importlib.import_module("pto_wsp.ir_bridge")
+    orig_w2ir = B.workload_to_codegen_ir
+
+    def w2ir(*a, **kw):
+        build = orig_w2ir(*a, **kw)
+        LAST_MODULE["module"] = build.module
+        return build
+
+    B.workload_to_codegen_ir = w2ir
 
 
 EXAMPLES = [

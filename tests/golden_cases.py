@@ -51,3 +51,11 @@ def materialize(case: dict, idx: int):
 def expected_roots(case: dict, idx: int) -> list[np.ndarray]:
     z = _npz()
     return [z[f"c{idx}_out{i}"].view(np.dtype(r["dtype"])).reshape(r["shape"]) for i, r in enumerate(case["roots"])]
+
+
+def artifact_roots(case: dict, idx: int) -> list[np.ndarray] | None:
+    """Output buffers of the reference's own CPU-sim artifact on the same inputs (None for older fixtures)."""
+    z = _npz()
+    if f"c{idx}_art0" not in z:
+        return None
+    return [z[f"c{idx}_art{i}"].view(np.dtype(r["dtype"])).reshape(r["shape"]) for i, r in enumerate(case["roots"])]

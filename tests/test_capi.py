@@ -268,3 +268,19 @@ def test_dry_run_chain_pipelining_rules(swap, write_back_x, chunks):
     assert t["waves"] == 2 and t["chunks"] == chunks
     if not write_back_x:  # M is written in full before it is read: never staged in
         assert t["h2d_bytes"] == arrays[0].nbytes
+
+
+def test_tiles_larger_than_their_views_are_ordered():
+    """The reference softmax example indexes its tiles one dimension too shallow, so each [8, 64] tile reaches
+    8 rows from a [4, 64] view into the next views.  The CPU-sim runs tasks in program order; here every task
+    that writes such a tensor gets its own wave (whole-tensor hazard key): 4 max-update steps (P.seq over v) +
+    16 exp/accumulate + 16 rescale tasks."""
+    from golden_cases import case_index, load_cases, materialize
+
+    cases = load_cases()
+    idx = case_index(cases, "example:softmax#0")
+    roots, arrays, axis, syms, sptr = materialize(cases[idx], idx)
+    ex = runtime.CudaExecutable(cases[idx]["plan"])
+    ex.set_option("dry_run", 1)
+    assert ex.run_with_symbols(arrays, axis, syms, sptr) == cases[idx]["cycles"]
+    assert ex.timing()["waves"] == 36 and ex.timing()["tasks"] == 48
