@@ -19,8 +19,10 @@ runs one config alone.
   from profiles/traffic.json (scaled to this rank's share of the units).
 * ``cpu_baseline`` -- the C port of the CPU-sim task bodies (oracle/cpu_kernels.c) on the host cores, rank 0 at
   N=1, bounded sample.
-* ``--impl reference`` -- the reference arm: the CPU implementation of the same task loops on the host cores
-  (all threads), same metric and config, one line with the same ``workloads`` layout; rank 0 only.
+* ``--impl reference`` -- the reference arm: the reference's own CPU-sim artifact of each config (its generated
+  task loop and kernels, oracle/_ref, built with the clean-room pto-isa stand-in) through its own
+  ``CodegenExecutable``, one single-threaded process per host core, same metric and config, one line with the same
+  ``workloads`` layout; rank 0 only.  Without the built artifacts it times the C port instead.
 
 Multi-GPU (torchrun, one rank per GPU): every rank runs its ``ShardedExecutable`` share of the ONE global config
 (strong scaling): contiguous blocks of the outer ``P(batch)`` axis for configs 1, 2, 3 and 5, greedy LPT by KV
@@ -908,13 +910,78 @@ def run_gpu(args, names: list[str], rank: int, world: int, local_rank: int) -> N
     D.close()
 
 
+def artifact_units(case: Case, procs: int) -> tuple[list[dict], str, bool] | None:
+    """The units of one reference step (each one artifact call), what they are, and whether they are the whole
+    config; None when the built artifact does not have this case's unit shape."""
+    if case.args.batch or case.args.cols:
+        return None
+    if isinstance(case, RowCase):
+        return [{"index": i} for i in range(case.batch)], f"the whole config ({case.batch} batch elements)", True
+    if isinstance(case, BgemmCase):
+        n = min(procs, case.B * case.M // 128)
+        return ([{"index": i} for i in range(n)],
+                f"{n} of the config's {case.B * case.M // 128} 128-row slabs (one per process)", False)
+    if isinstance(case, DecodeCase):
+        return ([{"index": r, "length": int(case.lens[r])} for r in range(case.R)],
+                f"the whole config ({case.R} requests, the bench's KV lengths)", True)
+    if isinstance(case, IndexerCase):
+        n = min(procs, case.B)
+        return [{"index": i} for i in range(n)], f"{n} of the config's {case.B} batch elements", n == case.B
+    return None
+
+
+def unit_work(case: Case, unit: dict) -> float:
+    if isinstance(case, RowCase):
+        return case.tiles * case.rows * case.cols * 8.0
+    if isinstance(case, BgemmCase):
+        return 2.0 * 128 * case.N * case.K
+    if isinstance(case, DecodeCase):
+        return case.unit_work([unit["index"]])
+    return case.work() / case.B
+
+
+def reference_artifact(case: Case, args, budget_s: float = 20.0) -> dict | None:
+    """The reference's own CPU-sim artifact of this config (oracle/_ref), one process per host core."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import ref_runner
+
+    if ref_runner.manifest() is None:
+        return None
+    procs = ref_runner.host_cores()
+    spec = artifact_units(case, procs)
+    if spec is None:
+        return None
+    units, what, whole = spec
+    work = sum(unit_work(case, u) for u in units)
+    pool = ref_runner.Pool(case.name, units, procs, seed=7)
+    try:
+        warm = [pool.step()[0]]  # one warm-up step: the artifact has nothing to compile, this pages it in
+        steps = max(1, min(args.steps, int(budget_s / max(min(warm), 1e-3))))
+        busy = 0.0
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            busy += sum(pool.step()[1])
+        dt = time.perf_counter() - t0
+    finally:
+        pool.close()
+    v = work * steps / dt / case.scale
+    one_core = work * steps / busy / case.scale
+    sample = (f"{what} per step; the reference's own CPU-sim artifact (its generated task loop and kernels, built "
+              f"with the clean-room pto-isa stand-in) through its CodegenExecutable, {pool.procs} processes "
+              f"(single-threaded each, as the CPU-sim is); 1-core rate {one_core:.6g} {case.unit}")
+    return {"value": round(v, 6), "unit": case.unit, "steps": steps, "ms_per_step": round(dt / steps * 1e3, 3),
+            "same_config": whole, "single_core": round(one_core, 6),
+            "cpu_baseline": {"value": round(v, 6), "unit": case.unit, "cores": pool.procs, "kind": "reference",
+                             "sample": sample}}
+
+
 def run_reference(args, names: list[str], rank: int) -> None:
     if rank != 0:
         return
     lines = {}
     for n in names:
         case = CASES[n](args)
-        r = case.reference(args.steps, args.warmup)
+        r = reference_artifact(case, args) or case.reference(args.steps, args.warmup)
         lines[n] = {"impl": "reference", "metric": case.metric, "value": r["value"], "unit": r["unit"],
                     "n_gpus": args.gpus, "steps": r["steps"], "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
                     "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": case.dtype,
@@ -922,6 +989,8 @@ def run_reference(args, names: list[str], rank: int) -> None:
                                                                    "same_config": r["same_config"]},
                     "cpu_baseline": r["cpu_baseline"],
                     "e2e": {"value": r["value"], "unit": r["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        if "single_core" in r:
+            lines[n]["single_core"] = {"value": r["single_core"], "unit": r["unit"], "cores": 1}
     head = dict(lines[names[0]])
     if len(names) > 1:
         head["workloads"] = {n: lines[n] for n in names[1:]}
