@@ -14,9 +14,10 @@ runs one config alone.
 * ``e2e``   -- the same metric through the same call with pinned host numpy buffers: each step stages the
   inputs host->device and the outputs device->host (bytes per step from the runtime's own counters).
 * ``roofline`` -- the dominant kernel: its algorithmic work per launch / its average launch time, measured with
-  CUDA events bracketing its launches on the launch stream during the timed region (runtime option
-  ``kernel_events``), against the measured peak in MEASURED_PEAKS.json; ``traffic`` = ncu DRAM bytes per launch
-  from profiles/traffic.json (scaled to this rank's share of the units).
+  CUDA events bracketing each of its launches on the launch stream (runtime option ``kernel_events``) over a
+  second pass of the same K steps, right after the first, inside the clock-sampled region (the event records would
+  stretch the steps of the ``value`` pass), against the measured peak in MEASURED_PEAKS.json; ``traffic`` = ncu
+  DRAM bytes per launch from profiles/traffic.json (scaled to this rank's share of the units).
 * ``cpu_baseline`` -- the C port of the CPU-sim task bodies (oracle/cpu_kernels.c) on the host cores, rank 0 at
   N=1, bounded sample.
 * ``--impl reference`` -- the reference arm: the reference's own CPU-sim artifact of each config (its generated
@@ -806,9 +807,9 @@ def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
         step(darr)
     launches_per_step = int(ex.timing()["launches"])  # a replayed step launches the same kernels every time
     D.barrier()
-    ex.set_option("kernel_events", 1)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with NvmlClockSampler(gpu_index(D.local_rank), _pci_bus_id(torch, dev)) as clk:
+        # the timed region: K steps back to back, CUDA events on the launch stream around all of them
         D.barrier()
         h0 = time.perf_counter()
         e0.record(stream)
@@ -817,12 +818,19 @@ def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
         e1.record(stream)
         host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
         D.barrier()
+        # the same K steps again with every kernel launch bracketed by CUDA events on the launch stream: the
+        # dominant kernel's own launch time for the roofline (kept out of the pass above, whose steps the
+        # extra event records would stretch)
+        ex.set_option("kernel_events", 1)
+        for _ in range(args.steps):
+            step(darr)
+        D.barrier()
+        ktimes = ex.kernel_times()
+        ex.set_option("kernel_events", 0)
     launches = launches_per_step * args.steps
     clocks = clk.summary()
     ms = e0.elapsed_time(e1)
     ms_max = D.max(ms)
-    ktimes = ex.kernel_times()
-    ex.set_option("kernel_events", 0)
     check = case.check(darr)
 
     # end to end: pinned host buffers through the same call, copies inside the timed region
@@ -876,7 +884,8 @@ def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
                      "kernel": case.kernel,
                      ("bytes_per_launch" if case.bound == "hbm" else "flops_per_launch"): kwork,
                      "launch_ms": round(per_launch_ms, 5), "launches_timed": kt["launches"],
-                     "timing": "CUDA events around the kernel's launches on the launch stream, timed region"},
+                     "timing": "CUDA events around each of the kernel's launches on the launch stream, over a second "
+                               "pass of the K timed steps"},
         "kernel_ms": {k: {"launches": v["launches"], "ms_per_launch": round(v["ms"] / max(v["launches"], 1), 5)}
                       for k, v in ktimes.items()},
         "e2e": {"value": round(e2e, 4), "unit": case.unit, "h2d_bytes_per_step": h2d // e2e_steps,

@@ -260,14 +260,27 @@ def _dist():
     return dist if dist.is_available() and dist.is_initialized() else None
 
 
+_INDEX_CACHE: dict = {}  # (device, units) -> index tensor on that device (made once, not per run)
+
+
+def _index(units: list[int], device: Any) -> Any:
+    import torch
+
+    key = (str(device), tuple(units))
+    t = _INDEX_CACHE.get(key)
+    if t is None:
+        if len(_INDEX_CACHE) > 256:
+            _INDEX_CACHE.clear()
+        t = _INDEX_CACHE[key] = torch.as_tensor(units, device=device, dtype=torch.long)
+    return t
+
+
 def _take(a: Any, units: list[int]) -> Any:
     if _contiguous(units):
         lo = units[0] if units else 0
         return a[lo:lo + len(units)]
     if hasattr(a, "index_select"):
-        import torch
-
-        return a.index_select(0, torch.as_tensor(units, device=a.device, dtype=torch.long))
+        return a.index_select(0, _index(units, a.device))
     import numpy as np
 
     return np.ascontiguousarray(a[np.asarray(units, dtype=np.int64)])
@@ -277,9 +290,7 @@ def _put(a: Any, units: list[int], local: Any) -> None:
     if _contiguous(units):
         return  # the rank wrote through a view
     if hasattr(a, "index_copy_"):
-        import torch
-
-        a.index_copy_(0, torch.as_tensor(units, device=a.device, dtype=torch.long), local)
+        a.index_copy_(0, _index(units, a.device), local)
         return
     import numpy as np
 
