@@ -51,6 +51,8 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
@@ -739,8 +741,82 @@ class IndexerCase(Case):
                               f"indexer task bodies, {nth} threads"}}
 
 
+class AttentionCase(Case):
+    """Not a BASELINE config: the reference attention example's kernel at full tile sizes (f16 Q and K^T, f32 V and
+    output, 128-row tiles), run by the fused tcgen05 kernel.  ``--workload attention``."""
+
+    name, kernel, traffic_key = "attention", "attention_tile", ""
+    unit, bound, dtype = "TFLOP/s", "tensor", "f16 Q.K^T / f32 softmax and W.V (3-term tf32) / f32 out"
+    metric = "attention-tile task-loop throughput (both contractions)"
+    B, H, QT, L = 8, 16, 8, 1024
+
+    def __init__(self, args):
+        super().__init__(args)
+        if args.batch:
+            self.B = args.batch
+        self.n_units = self.B
+
+    @property
+    def config(self) -> str:
+        return (f"attention tiles {self.B}x{self.H}x{self.QT} (128 query rows each), {self.L} keys, d=128, "
+                f"softmax(0.088 Q.K^T).V")
+
+    def work(self) -> float:
+        return 4.0 * self.B * self.H * self.QT * 128 * self.L * 128
+
+    def plan(self):
+        from pto_wsp_b200 import workloads
+
+        return workloads.attention_plan(self.B, self.H, self.QT, self.L)
+
+    def device_inputs(self, torch, dev):
+        g = torch.Generator(device=dev)
+        g.manual_seed(5000)
+        q = torch.randn((self.B, self.H, self.QT, 128, 128), generator=g, device=dev).half()
+        kt = torch.randn((self.B, self.H, 128, self.L), generator=g, device=dev).half()
+        v = torch.randn((self.B, self.H, self.L, 128), generator=g, device=dev)
+        o = torch.empty((self.B, self.H, self.QT, 128, 128), device=dev)
+        return [q, kt, v, o]
+
+    def check(self, darr) -> dict:
+        torch = sys.modules["torch"]
+        q, kt, v, o = darr
+        s = torch.einsum("trd,dk->trk", q[0, 0].double(), kt[0, 0].double()) * float(np.float32(0.088))
+        ref = torch.einsum("trk,kd->trd", torch.softmax(s, -1), v[0, 0].double())
+        big = ref.abs() >= 1e-2 * ref.pow(2).mean().sqrt()
+        return {"max_rel_err_vs_fp64_head0": float(((o[0, 0].double() - ref).abs() / ref.abs())[big].max())}
+
+    def cpu_baseline(self, host, budget_s: float) -> dict:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        from cpu_sim import CpuSim
+
+        from pto_wsp_b200 import workloads
+
+        sub = workloads.attention_plan(1, 1, 1, self.L)
+        arrays = [np.ascontiguousarray(host[0][:1, :1, :1]), np.ascontiguousarray(host[1][:1, :1]),
+                  np.ascontiguousarray(host[2][:1, :1]), np.zeros((1, 1, 1, 128, 128), np.float32)]
+        t0 = time.perf_counter()
+        CpuSim(sub).run(arrays)
+        dt = time.perf_counter() - t0
+        return {"value": round(4.0 * 128 * self.L * 128 / dt / 1e12, 7), "unit": "TFLOP/s", "cores": 1,
+                "kind": "port", "sample": f"1 tile ({dt:.2f} s), numpy restatement of the tile program "
+                                         f"(oracle/cpu_sim.py)"}
+
+    def reference(self, steps: int, warmup: int) -> dict:
+        b = self.cpu_baseline(workloads_attention_host(self), 0.0)
+        return {"value": b["value"], "unit": "TFLOP/s", "steps": 1, "ms_per_step": None, "same_config": False,
+                "cpu_baseline": b}
+
+
+def workloads_attention_host(case: "AttentionCase"):
+    rng = np.random.default_rng(5)
+    return [rng.standard_normal((1, 1, 1, 128, 128)).astype(np.float16),
+            rng.standard_normal((1, 1, 128, case.L)).astype(np.float16),
+            rng.standard_normal((1, 1, case.L, 128)).astype(np.float32)]
+
+
 CASES = {"softmax": SoftmaxCase, "rmsnorm": RmsNormCase, "bgemm": BgemmCase, "decode": DecodeCase,
-         "indexer": IndexerCase}
+         "indexer": IndexerCase, "attention": AttentionCase}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -1012,7 +1088,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all"] + ORDER)
+    ap.add_argument("--workload", default="all", choices=["all"] + ORDER + ["attention"])
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default min(steps, 10))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=4.0, help="seconds of CPU work per cpu_baseline sample")

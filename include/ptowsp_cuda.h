@@ -145,7 +145,10 @@ PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
  * only -- makespan, task and wave counts -- with no CUDA call, default 0),
  * "kernel_events" (1: bracket every kernel's launches with CUDA events on the
  * launch stream and sum their device time per kernel, read by
- * ptowsp_cuda_kernel_times; setting it clears the sums; default 0).
+ * ptowsp_cuda_kernel_times; setting it clears the sums; default 0),
+ * "fused_attention" (0: kernels of the attention pattern run as their stages
+ * -- matmul kernels and row programs over HBM scratch -- instead of the fused
+ * tcgen05 kernel; default 1).
  * "stage_scratch_mb" is clamped to 1 .. 1048576; changing it drops the cached
  * task tables, which were grouped for the old budget. */
 PTOWSP_API int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value);

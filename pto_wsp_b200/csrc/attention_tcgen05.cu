@@ -1,0 +1,456 @@
+// Fused attention tile task on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), flash form.
+//
+// A task is a generic `pto.*` kernel of the shape the reference attention example writes
+// (examples/attention/pto_wsp_impl.py:51-68; emitter ops src/python/pto_codegen.cpp:817-1219):
+//
+//     S = Q . K^T  [* scale]      Q [128, 128] f16, K^T [128, L] f16 (the task's tile views)
+//     W = exp(S - rowmax(S)) / rowsum(...)     f32
+//     O = W . V                   V [L, 128] f32, O [128, 128] f32 (stored to the `out` view)
+//
+// (pto has no cast, so W, the f32 result of the softmax, multiplies an f32 V: the emitter takes a matmul only with
+// both operands f16 or both f32.)  The staged form runs this as four launches with S and W in HBM scratch and the
+// second contraction on CUDA cores; here S and O live in TMEM and W in shared memory, and both contractions run
+// on the tensor cores:
+//   * S_j = Q . K^T_j: tcgen05.mma kind::f16 (exact f16 products, f32 accumulation);
+//   * O += W_j . V_j: kind::tf32 on a three-term split, P_hi.V_hi + P_hi.V_lo + P_lo.V_hi, where x_hi is x with the
+//     low 13 mantissa bits cleared (exactly a tf32) and x_lo = x - x_hi: each product carries ~22 bits, the f32
+//     tile program's accuracy (a single tf32 pass would give the terms a 2^-11 relative error).
+// Keys go in blocks of 64 with an online softmax in the base-2 domain; the running row max is kept lazily (a row's O
+// and sum are rescaled only when its max grows by more than 2^8), which changes no result beyond rounding.  The row
+// sum uses the f32 probabilities and divides O once at the end.
+//
+// One CTA per task, 10 warps:
+//   warp 0      TMA producer: Q once (two 128 x 64 K-major f16 boxes), per key block a K^T block (two 64 x 64
+//               MN-major f16 boxes, two stages) and a V block (four 32 x 64 MN-major f32 boxes), 128-byte swizzle.
+//   warp 1      owns TMEM (S double buffer: columns 0-127; O: 128-255) and issues the MMAs from one thread,
+//               S_{j+1} before O += W_j.V_j so that the tensor pipe works while the softmax runs.
+//   warps 2-5   softmax and epilogue, one row per thread (warp w reads TMEM lanes 32 (w % 4) ..): tcgen05.ld of
+//               the S row (twice: max, then exponentials), P_hi / P_lo written to shared memory in the swizzled
+//               K-major layout the MMA reads; at the end O / sum stored to the out row.
+//   warps 6-9   split each V block into V_hi / V_lo, element for element in the TMA layout.
+// Every mbarrier wait is bounded (~2 s of %globaltimer): on timeout the CTA records kErrTimeout, drains its own
+// copies and MMAs, frees TMEM and returns.  No cluster multicast (loads read this GPU's memory only).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "device.hpp"
+#include "tc_common.cuh"
+
+namespace ptowsp::dev {
+
+namespace {
+
+using namespace tc;
+
+constexpr int AT_THREADS = 320;
+constexpr int AT_ROWS = 128;   // query rows of a task
+constexpr int AT_D = 128;      // head dim
+constexpr int AT_BN = 64;      // keys per block
+constexpr int BOX = 8192;      // one TMA box: 64 x 64 f16 or 32 x 64 f32
+constexpr int Q_BYTES = AT_ROWS * AT_D * 2;   // 32 KB
+constexpr int K_BYTES = AT_D * AT_BN * 2;     // 16 KB per stage
+constexpr int V_BYTES = AT_BN * AT_D * 4;     // 32 KB
+constexpr int P_BYTES = AT_ROWS * AT_BN * 4;  // 32 KB per part
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + Q_BYTES;        // 2 stages
+constexpr int OFF_VRAW = OFF_K + 2 * K_BYTES;
+constexpr int OFF_VHI = OFF_VRAW + V_BYTES;
+constexpr int OFF_VLO = OFF_VHI + V_BYTES;
+constexpr int OFF_PHI = OFF_VLO + V_BYTES;
+constexpr int OFF_PLO = OFF_PHI + P_BYTES;
+constexpr int OFF_BAR = OFF_PLO + P_BYTES;    // 224 KB
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers / flags + 1024-byte alignment slack
+static_assert(SMEM_BYTES <= 232448, "attention tile exceeds the 227 KB of shared memory per CTA");
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TMEM_O = 128;
+constexpr float kRescaleLog2 = 8.f;  // a row's reference max moves when its max grows by more than this
+
+// Instruction descriptor, kind::tf32: D f32 [4,6)=1, A tf32 [7,10)=2, B tf32 [10,13)=2, A K-major [15]=0,
+// B MN-major [16]=1, N>>3 [17,23), M>>4 [24,29).
+constexpr uint32_t idesc_tf32(int m, int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (1u << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// x with its low 13 mantissa bits cleared: exactly a tf32 value (sign, exponent, 10 mantissa bits).
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+
+struct AttnArgs {
+    const int64_t* rec;
+    int64_t ntasks;
+    int stride;
+    int q_p, kt_p, v_p, o_p;      // tensor param positions in the records
+    int64_t q_pitch, kt_pitch, v_pitch;
+    float* out;
+    int64_t o_pitch;
+    int nblocks;                  // L / 64
+    int scale_mode;               // 0 none, 1 constant, 2 f32 bits in the record at scale_pos
+    int scale_pos;
+    float scale_const;
+    int* err;
+};
+
+__global__ void __launch_bounds__(AT_THREADS, 1)
+    attention_tcgen05_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mkt,
+                             const __grid_constant__ CUtensorMap mv, AttnArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;      // [2]
+    uint64_t* k_empty = bars + 3;     // [2]
+    uint64_t* vraw_full = bars + 5;   // TMA landed the V block
+    uint64_t* vraw_empty = bars + 6;  // the splitters read it
+    uint64_t* vsp_full = bars + 7;    // V_hi / V_lo written
+    uint64_t* vsp_empty = bars + 8;   // the MMAs read them
+    uint64_t* s_full = bars + 9;      // [2]
+    uint64_t* s_empty = bars + 11;    // [2]
+    uint64_t* p_full = bars + 13;
+    uint64_t* p_empty = bars + 14;
+    uint64_t* o_full = bars + 15;
+    uint64_t* drain = bars + 16;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t task = blockIdx.x;
+    if (task >= args.ntasks) return;  // whole CTA: nothing initialised yet
+    const int64_t* rec = args.rec + task * args.stride;
+    const int nb = args.nblocks;
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(q_full), 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&k_full[s]), 1);
+            mbar_init(smem_u32(&k_empty[s]), 1);
+            mbar_init(smem_u32(&s_full[s]), 1);
+            mbar_init(smem_u32(&s_empty[s]), 128);
+        }
+        mbar_init(smem_u32(vraw_full), 1);
+        mbar_init(smem_u32(vraw_empty), 128);
+        mbar_init(smem_u32(vsp_full), 128);
+        mbar_init(smem_u32(vsp_empty), 1);
+        mbar_init(smem_u32(p_full), 128);
+        mbar_init(smem_u32(p_empty), 1);
+        mbar_init(smem_u32(o_full), 1);
+        mbar_init(smem_u32(drain), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mq)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mkt)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mv)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t sQ = smem_u32(smem + OFF_Q), sK = smem_u32(smem + OFF_K), sVraw = smem_u32(smem + OFF_VRAW);
+    const uint32_t sVhi = smem_u32(smem + OFF_VHI), sVlo = smem_u32(smem + OFF_VLO);
+    const uint32_t sPhi = smem_u32(smem + OFF_PHI), sPlo = smem_u32(smem + OFF_PLO);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            const int64_t oq = rec[args.q_p], okt = rec[args.kt_p], ov = rec[args.v_p];
+            const int32_t qx = static_cast<int32_t>(oq % args.q_pitch), qy = static_cast<int32_t>(oq / args.q_pitch);
+            const int32_t kx = static_cast<int32_t>(okt % args.kt_pitch), ky = static_cast<int32_t>(okt / args.kt_pitch);
+            const int32_t vx = static_cast<int32_t>(ov % args.v_pitch), vy = static_cast<int32_t>(ov / args.v_pitch);
+            mbar_expect_tx(smem_u32(q_full), Q_BYTES);
+            tma_load_2d(sQ, &mq, qx, qy, smem_u32(q_full));
+            tma_load_2d(sQ + 16384, &mq, qx + 64, qy, smem_u32(q_full));
+            int last_k[2] = {-1, -1}, last_v = -1;  // the block last loaded into each buffer
+            for (int j = 0; j < nb && !*abort_flag; ++j) {
+                const int st = j & 1;
+                if (j >= 2 && !mbar_wait(smem_u32(&k_empty[st]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
+                mbar_expect_tx(smem_u32(&k_full[st]), K_BYTES);
+                for (int kc = 0; kc < 2; ++kc)  // head-dim rows of K^T, 64 keys per box
+                    tma_load_2d(sK + st * K_BYTES + kc * BOX, &mkt, kx + j * AT_BN, ky + kc * 64, smem_u32(&k_full[st]));
+                last_k[st] = j;
+                if (j >= 1 && !mbar_wait(smem_u32(vraw_empty), (j - 1) & 1, abort_flag, args.err)) break;
+                mbar_expect_tx(smem_u32(vraw_full), V_BYTES);
+                for (int nc = 0; nc < 4; ++nc)  // 32 head dims per box, 64 keys
+                    tma_load_2d(sVraw + nc * BOX, &mv, vx + nc * 32, vy + j * AT_BN, smem_u32(vraw_full));
+                last_v = j;
+            }
+            // drain: every copy issued has landed before shared memory goes away (block j completes phase j / 2
+            // of its K stage and phase j of the V barrier)
+            const uint64_t start = globaltimer();
+            auto settle = [&](uint32_t bar, uint32_t parity) {
+                while (!mbar_try_wait(bar, parity))
+                    if (globaltimer() - start > kTimeoutNs) {
+                        atomicOr(args.err, kErrTimeout);
+                        return;
+                    }
+            };
+            settle(smem_u32(q_full), 0);
+            for (int st = 0; st < 2; ++st)
+                if (last_k[st] >= 0) settle(smem_u32(&k_full[st]), (last_k[st] >> 1) & 1);
+            if (last_v >= 0) settle(smem_u32(vraw_full), last_v & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc_s = idesc_f16(AT_ROWS, AT_BN, 1);  // A K-major, B MN-major, M = 128, N = 64
+            constexpr uint32_t idesc_o = idesc_tf32(AT_ROWS, AT_D);     // M = N = 128
+            bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, args.err);
+            bool issued = false;
+            auto pv = [&](int i) -> bool {  // O += P_i . V_i as P_hi.V_hi + P_hi.V_lo + P_lo.V_hi
+                if (!mbar_wait(smem_u32(p_full), i & 1, abort_flag, args.err)) return false;
+                if (!mbar_wait(smem_u32(vsp_full), i & 1, abort_flag, args.err)) return false;
+                tc_fence_after();
+                const uint32_t pa[3] = {sPlo, sPhi, sPhi}, vb[3] = {sVhi, sVlo, sVhi};  // small terms first
+                for (int t = 0; t < 3; ++t)
+#pragma unroll
+                    for (int k8 = 0; k8 < AT_BN / 8; ++k8) {
+                        // A: K-major f32 rows of 32 keys (128 B) per 16 KB chunk; 8 keys = 32 B per step
+                        const uint64_t a = smem_desc(pa[t] + (k8 >> 2) * 16384 + (k8 & 3) * 32, 16, 1024);
+                        // B: MN-major, 32-dim (128 B) N chunks 8 KB apart (LBO), 8 key rows (1 KB) per step
+                        const uint64_t b = smem_desc(vb[t] + k8 * 1024, BOX, 1024);
+                        mma_tf32(tmem_base + TMEM_O, a, b, idesc_o, (i > 0 || t > 0 || k8 > 0) ? 1u : 0u);
+                    }
+                mma_commit(smem_u32(vsp_empty));
+                mma_commit(smem_u32(p_empty));
+                return true;
+            };
+            for (int j = 0; ok && j < nb; ++j) {
+                const int st = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(smem_u32(&k_full[st]), ph, abort_flag, args.err)) break;
+                if (j >= 2 && !mbar_wait(smem_u32(&s_empty[st]), ph ^ 1u, abort_flag, args.err)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < AT_D / 16; ++kk) {  // S_j = Q . K^T_j over the head dims
+                    const uint64_t a = smem_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+                    const uint64_t b = smem_desc(sK + st * K_BYTES + (kk >> 2) * BOX + (kk & 3) * 2048, BOX, 1024);
+                    mma_f16(tmem_base + static_cast<uint32_t>(st * AT_BN), a, b, idesc_s, kk > 0 ? 1u : 0u);
+                }
+                issued = true;
+                mma_commit(smem_u32(&k_empty[st]));
+                mma_commit(smem_u32(&s_full[st]));
+                if (j >= 1 && !pv(j - 1)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (ok && !*abort_flag && pv(nb - 1)) mma_commit(smem_u32(o_full));
+            if (issued) {  // drain: every MMA issued has completed before TMEM is freed
+                mma_commit(smem_u32(drain));
+                const uint64_t start = globaltimer();
+                while (!mbar_try_wait(smem_u32(drain), 0))
+                    if (globaltimer() - start > kTimeoutNs) {
+                        atomicOr(args.err, kErrTimeout);
+                        break;
+                    }
+            }
+        }
+    } else if (warp >= 6) {
+        // ---------------- V splitters (warps 6..9) ----------------
+        const int t = threadIdx.x - 6 * 32;  // 0..127
+        const float4* raw = reinterpret_cast<const float4*>(smem + OFF_VRAW);
+        float4* hi = reinterpret_cast<float4*>(smem + OFF_VHI);
+        float4* lo = reinterpret_cast<float4*>(smem + OFF_VLO);
+        for (int j = 0; j < nb; ++j) {
+            if (!mbar_wait(smem_u32(vraw_full), j & 1, abort_flag, args.err)) break;
+            if (j >= 1 && !mbar_wait(smem_u32(vsp_empty), (j - 1) & 1, abort_flag, args.err)) break;
+#pragma unroll 4
+            for (int i = t; i < V_BYTES / 16; i += 128) {  // the same swizzled position in every buffer
+                const float4 x = raw[i];
+                const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+                hi[i] = h;
+                lo[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+            }
+            mbar_arrive(smem_u32(vraw_empty));
+            fence_proxy_async_smem();  // V_hi / V_lo become visible to the tensor core's reads
+            mbar_arrive(smem_u32(vsp_full));
+        }
+    } else {
+        // ---------------- softmax + epilogue (warps 2..5, one row per thread) ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        float scale = 1.f;
+        if (args.scale_mode == 1) scale = args.scale_const;
+        else if (args.scale_mode == 2) scale = __uint_as_float(static_cast<uint32_t>(rec[args.scale_pos]));
+        const float c2 = scale * 1.4426950408889634f;  // into the base-2 domain
+        float m_ref = -INFINITY, l = 0.f;
+        bool ok = true;
+        uint8_t* phi_row = smem + OFF_PHI + row * 128;  // 128-byte rows, 8-row swizzle atoms of 1 KB
+        uint8_t* plo_row = smem + OFF_PLO + row * 128;
+        for (int j = 0; j < nb; ++j) {
+            const int st = j & 1;
+            if (!mbar_wait(smem_u32(&s_full[st]), (j >> 1) & 1, abort_flag, args.err)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t s_addr = tmem_base + lane_addr + static_cast<uint32_t>(st * AT_BN);
+            // pass 1: the row max (S_j stays in TMEM; pass 2 reads it again)
+            float mx = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < AT_BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32_async(s_addr + c * 32, r);
+                tmem_wait_ld();
+                reg_fence(r);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]) * c2);
+            }
+            float corr = 1.f;
+            const bool grow = j == 0 || mx > m_ref + kRescaleLog2;
+            if (grow) {
+                const float m_new = j == 0 ? mx : fmaxf(m_ref, mx);
+                corr = j == 0 ? 1.f : exp2f(m_ref - m_new);
+                m_ref = m_new;
+            }
+            // P_{j-1} has been read and O updated by its MMAs before P_j overwrites the buffers (and O is rescaled)
+            if (j > 0 && !mbar_wait(smem_u32(p_empty), (j - 1) & 1, abort_flag, args.err)) {
+                ok = false;
+                break;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < AT_D / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32_async(tmem_base + lane_addr + TMEM_O + c * 32, r);
+                    tmem_wait_ld();
+                    reg_fence(r);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+                    tmem_st32(tmem_base + lane_addr + TMEM_O + c * 32, r);
+                }
+                tmem_wait_st();
+            }
+            l *= corr;
+            // pass 2: p = 2^(x - max) in f32 for the sum, as P_hi + P_lo into the P tiles
+            float sum = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < AT_BN / 32; ++c) {  // 32 keys = one 128-byte row of a 16 KB chunk
+                uint32_t r[32];
+                tmem_ld32_async(s_addr + c * 32, r);
+                tmem_wait_ld();
+                reg_fence(r);
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {  // 4 keys = one 16-byte unit of the row
+                    float p[4], h[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        p[e] = exp2f(__uint_as_float(r[4 * g + e]) * c2 - m_ref);
+                        sum += p[e];
+                        h[e] = tf32_hi(p[e]);
+                    }
+                    // K-major, 128-byte swizzle: unit g of the row at g ^ (row % 8)
+                    const int off = c * 16384 + ((g ^ (row & 7)) << 4);
+                    *reinterpret_cast<float4*>(phi_row + off) = make_float4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<float4*>(plo_row + off) =
+                        make_float4(p[0] - h[0], p[1] - h[1], p[2] - h[2], p[3] - h[3]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&s_empty[st]));  // S_j has been read: its TMEM buffer may take S_{j+2}
+            l += sum;
+            fence_proxy_async_smem();  // the P writes become visible to the tensor core's reads
+            mbar_arrive(smem_u32(p_full));
+        }
+        if (ok && mbar_wait(smem_u32(o_full), 0, abort_flag, args.err)) {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            float* orow = args.out + rec[args.o_p] + static_cast<int64_t>(row) * args.o_pitch;
+#pragma unroll 1
+            for (int c = 0; c < AT_D / 32; ++c) {
+                float v[32];
+                tmem_ld32(tmem_base + lane_addr + TMEM_O + c * 32, v);
+                float4* dst = reinterpret_cast<float4*>(orow + c * 32);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    dst[i] = make_float4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+}  // namespace
+
+bool attention_tiles_supported(const TaskBatch& b, int q_p, int kt_p, int v_p, int o_p, int L) {
+    const ParamDesc &Q = b.p[q_p], &KT = b.p[kt_p], &V = b.p[v_p], &O = b.p[o_p];
+    auto rows16 = [](const ParamDesc& p, int type, int eb) {
+        return p.type == type && p.s4 == 1 && p.s3 > 0 && (p.s3 * eb) % 16 == 0 &&
+               (reinterpret_cast<uintptr_t>(p.base) & 15) == 0;
+    };
+    return rows16(Q, PT_F16, 2) && rows16(KT, PT_F16, 2) && rows16(V, PT_F32, 4) && rows16(O, PT_F32, 4) &&
+           Q.rows == AT_ROWS && Q.cols == AT_D && KT.rows == AT_D && KT.cols == L && V.rows == L && V.cols == AT_D &&
+           O.rows == AT_ROWS && O.cols == AT_D && L >= AT_BN && L % AT_BN == 0;
+}
+
+bool attention_task_ok(const TaskBatch& b, int q_p, int kt_p, int v_p, int o_p, int L, const int64_t* r) {
+    const ParamDesc &Q = b.p[q_p], &KT = b.p[kt_p], &V = b.p[v_p], &O = b.p[o_p];
+    const int64_t oq = r[q_p], ok = r[kt_p], ov = r[v_p], oo = r[o_p];
+    const int64_t q_rows = (Q.numel_span + Q.s3 - 1) / Q.s3, k_rows = (KT.numel_span + KT.s3 - 1) / KT.s3;
+    const int64_t v_rows = (V.numel_span + V.s3 - 1) / V.s3;
+    // TMA x coordinates on 16-byte boundaries (8 f16 / 4 f32), every tile inside its tensor
+    return oq >= 0 && ok >= 0 && ov >= 0 && oo >= 0 && oo % 4 == 0 && (oq % Q.s3) % 8 == 0 &&
+           (ok % KT.s3) % 8 == 0 && (ov % V.s3) % 4 == 0 && (oq % Q.s3) + AT_D <= Q.s3 &&
+           (oq / Q.s3) + AT_ROWS <= q_rows && (ok % KT.s3) + L <= KT.s3 && (ok / KT.s3) + AT_D <= k_rows &&
+           (ov % V.s3) + AT_D <= V.s3 && (ov / V.s3) + L <= v_rows && oo + (AT_ROWS - 1) * O.s3 + AT_D <= O.numel_span;
+}
+
+cudaError_t launch_attention(const TaskBatch& b, int q_p, int kt_p, int v_p, int o_p, int L, int scale_mode,
+                             int scale_pos, float scale_const, cudaStream_t s) {
+    if (b.ntasks <= 0) return cudaSuccess;
+    if (b.ntasks > 0x7fffffff) return cudaErrorInvalidValue;
+    const ParamDesc &Q = b.p[q_p], &KT = b.p[kt_p], &V = b.p[v_p], &O = b.p[o_p];
+    CUtensorMap mq, mkt, mv;
+    if (!make_map_f16(&mq, Q.base, Q.s3, (Q.numel_span + Q.s3 - 1) / Q.s3, 64, AT_ROWS)) return cudaErrorInvalidValue;
+    if (!make_map_f16(&mkt, KT.base, KT.s3, (KT.numel_span + KT.s3 - 1) / KT.s3, 64, 64)) return cudaErrorInvalidValue;
+    if (!make_map_f32(&mv, V.base, V.s3, (V.numel_span + V.s3 - 1) / V.s3, 32, 64)) return cudaErrorInvalidValue;
+    AttnArgs a;
+    a.rec = b.rec;
+    a.ntasks = b.ntasks;
+    a.stride = b.stride;
+    a.q_p = q_p;
+    a.kt_p = kt_p;
+    a.v_p = v_p;
+    a.o_p = o_p;
+    a.q_pitch = Q.s3;
+    a.kt_pitch = KT.s3;
+    a.v_pitch = V.s3;
+    a.out = reinterpret_cast<float*>(O.base);
+    a.o_pitch = O.s3;
+    a.nblocks = L / AT_BN;
+    a.scale_mode = scale_mode;
+    a.scale_pos = scale_pos;
+    a.scale_const = scale_const;
+    a.err = b.err;
+    cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attention_tcgen05_kernel<<<static_cast<unsigned>(b.ntasks), AT_THREADS, SMEM_BYTES, s>>>(mq, mkt, mv, a);
+    return cudaGetLastError();
+}
+
+}  // namespace ptowsp::dev

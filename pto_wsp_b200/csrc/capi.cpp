@@ -94,6 +94,8 @@ int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value)
         const int64_t mb = value < 1 ? 1 : (value > (int64_t{1} << 20) ? (int64_t{1} << 20) : value);
         if (mb != p.opt_stage_scratch_mb) p.cached.reset();
         p.opt_stage_scratch_mb = mb;
+    } else if (!std::strcmp(key, "fused_attention")) {
+        p.opt_fused_attention = value != 0;
     } else if (!std::strcmp(key, "kernel_events")) {
         p.opt_kernel_events = value != 0;
         guarded(prog, [&] { ptowsp::reset_kernel_times(p); return 0; }, 0);

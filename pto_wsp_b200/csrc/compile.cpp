@@ -25,6 +25,7 @@ const char* impl_name(ImplKind k) {
         case ImplKind::IndexerScore: return "lightning_indexer_score";
         case ImplKind::TopK: return "topk_select";
         case ImplKind::Staged: return "staged_matmul+row_programs";
+        case ImplKind::Attention: return "attention_tcgen05";
     }
     return "?";
 }
@@ -819,6 +820,25 @@ std::unique_ptr<Program> compile_program(const char* text, size_t len, int devic
         else if (is_softmax(kd)) ki.kind = ImplKind::Softmax;
         else if (int f = matmul_form(kd)) ki.kind = f == 1 ? ImplKind::Matmul : ImplKind::MatmulAcc;
         else ki.kind = ImplKind::TileProgram;
+        // the attention pattern runs fused on tcgen05, its stages built as the fallback for views it does not take
+        if (ki.kind == ImplKind::TileProgram && w.error.empty() && match_attention(ki, kd) && split_stages(ki, kd)) {
+            bool built = true;
+            for (size_t si = 0; built && si < ki.stages.size(); ++si) {
+                Stage& st = ki.stages[si];
+                if (st.mm) continue;
+                std::string note;
+                const std::string name = "ptowsp_st_k" + std::to_string(i) + "_" + std::to_string(si);
+                if (build_stage_program(st.tp, kd, name, &st.cubin, &note)) st.jit_state = 2;
+                else built = false;
+            }
+            if (built) {
+                ki.kind = ImplKind::Attention;
+                ki.jit_note = "fused attention on tcgen05 (the stages run views it does not take)";
+                continue;
+            }
+            ki.stages.clear();
+            ki.scratch_tiles.clear();
+        }
         if (ki.kind == ImplKind::TileProgram && w.error.empty() && split_matmul_epilogue(ki, kd, static_cast<int>(i)))
             continue;
         // (only a complete tile program is cut: a walker error means an op is missing from it)
@@ -874,7 +894,7 @@ std::string describe_program(const Program& p) {
         o << "{\"name\":\"" << p.plan.kernels[i].name << "\",\"impl\":\"" << impl_name(ki.kind)
           << "\",\"cycles\":" << ki.cycles << ",\"tile_program_smem\":" << ki.tp_smem << ",\"row_kernel\":\"" << row
           << "\",\"row_kernel_note\":\"" << note << "\"";
-        if (ki.kind == ImplKind::Staged) {  // e.g. ["matmul 128x256x128 tcgen05", "rows 128", "matmul ... cuda_cores"]
+        if (ki.kind == ImplKind::Staged || ki.kind == ImplKind::Attention) {  // e.g. ["matmul 128x256x128 tcgen05", "rows 128", ...]
             o << ",\"stages\":[";
             for (size_t si = 0; si < ki.stages.size(); ++si) {
                 const Stage& st = ki.stages[si];

@@ -122,6 +122,14 @@ bool matmul_tiles_supported(const TaskBatch& b);
 bool launch_matmul_pairs(const TaskBatch& b, const int64_t* units, int64_t nunits, int accumulate, int workers,
                          cudaStream_t s, cudaError_t* err);
 
+// Fused attention tile tasks (attention_tcgen05.cu): per task O[128,128] f32 = softmax(scale * Q . K^T) . V with
+// Q [128,128], K^T [128,L] f16 and V [L,128] f32 views (tensor params q_p, kt_p, v_p, o_p), L a multiple of 64; the
+// scale is none (mode 0), `scale_const` (1) or the f32 scalar at record position `scale_pos` (2).
+bool attention_tiles_supported(const TaskBatch& b, int q_p, int kt_p, int v_p, int o_p, int L);
+bool attention_task_ok(const TaskBatch& b, int q_p, int kt_p, int v_p, int o_p, int L, const int64_t* rec);
+cudaError_t launch_attention(const TaskBatch& b, int q_p, int kt_p, int v_p, int o_p, int L, int scale_mode,
+                             int scale_pos, float scale_const, cudaStream_t s);
+
 // Built-ins.
 cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int num_kv_heads, int workers, void* scratch,
                                 size_t scratch_bytes, cudaStream_t s);

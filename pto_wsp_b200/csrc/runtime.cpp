@@ -1175,6 +1175,27 @@ void launch_batch_body(Program& P, Batch& B, const Node& node, std::vector<Tenso
         return n;
     };
     bool st_rows_ok = rows_ok;
+    if (kind == ImplKind::Attention && !P.opt_fused_attention) kind = ImplKind::Staged;
+    if (kind == ImplKind::Attention) {
+        // the fused kernel takes the batch when every task's views meet its layout conditions (checked once per
+        // batch, from the host records or, when a cached task table dropped them, a copy read back)
+        if (B.at_ok < 0) {
+            bool ok = dev::attention_tiles_supported(tb, ki.at_q, ki.at_kt, ki.at_v, ki.at_o, ki.at_L);
+            std::vector<int64_t> back;
+            const int64_t* rec = B.rec.data();
+            if (ok && B.rec.empty() && B.ntasks > 0) {
+                back.resize(static_cast<size_t>(B.ntasks) * B.stride);
+                PW_CUDA(cudaMemcpyAsync(back.data(), rec_dev + B.dev_off, back.size() * sizeof(int64_t),
+                                        cudaMemcpyDeviceToHost, P.stream));
+                PW_CUDA(cudaStreamSynchronize(P.stream));
+                rec = back.data();
+            }
+            for (int64_t t = 0; ok && t < B.ntasks; ++t)
+                ok = dev::attention_task_ok(tb, ki.at_q, ki.at_kt, ki.at_v, ki.at_o, ki.at_L, rec + t * B.stride);
+            B.at_ok = ok ? 1 : 0;
+        }
+        if (!B.at_ok) kind = ImplKind::Staged;
+    }
     // the stages run over groups of st_group tasks, so that the scratch stays within the stage_scratch_mb budget
     // (2 GiB by default) whatever the batch; the group is fixed when the batch's records are built
     int64_t st_group = B.ntasks;
@@ -1275,6 +1296,11 @@ void launch_batch_body(Program& P, Batch& B, const Node& node, std::vector<Tenso
         }
     }
     switch (kind) {
+        case ImplKind::Attention:
+            e = dev::launch_attention(tb, ki.at_q, ki.at_kt, ki.at_v, ki.at_o, ki.at_L, ki.at_scale_mode,
+                                      kd.num_tensor_params + tb.naxis + std::max(ki.at_scale_index, 0),
+                                      ki.at_scale_const, P.stream);
+            break;
         case ImplKind::Staged: {
             bool first = true;
             for (int64_t t0 = 0; t0 < B.ntasks && e == cudaSuccess; t0 += st_group) {
@@ -1858,6 +1884,94 @@ bool split_matmul_epilogue(KernelImpl& ki, const KernelDef& kd, int k) {
 bool build_stage_program(const dev::TileProgram& tp, const KernelDef& kd, const std::string& name, std::string* cubin,
                          std::string* note) {
     return build_row_program(tp, kd, kd.num_tensor_params, name, cubin, note);
+}
+
+bool match_attention(KernelImpl& ki, const KernelDef& kd) {
+    // value id -> the kernel param it is (through Load ops), and the Constant ops' values
+    std::map<int, const KernelParam*> param_of;
+    for (const auto& kp : kd.params) param_of[kp.id] = &kp;
+    std::map<int, double> constant;
+    std::vector<const OpInfo*> seq;
+    for (const auto& op : kd.ops) {
+        if (op.kind == "Constant" && op.result >= 0) {
+            const json::Value* v = op.attrs.get("value");
+            if (!v) return false;
+            constant[op.result] = v->as_f64();
+        } else if (op.kind == "Load" && op.result >= 0 && op.operands.size() == 1 && param_of.count(op.operands[0])) {
+            param_of[op.result] = param_of[op.operands[0]];
+        } else {
+            seq.push_back(&op);
+        }
+    }
+    auto tensor = [&](int id) -> const KernelParam* {
+        auto it = param_of.find(id);
+        return it != param_of.end() && it->second->tensor_index >= 0 ? it->second : nullptr;
+    };
+    auto is_op = [&](size_t i, const char* kind, size_t nops) {
+        return i < seq.size() && seq[i]->kind == kind && seq[i]->operands.size() == nops &&
+               (nops == 0 || seq[i]->result >= 0 || std::string(kind) == "Store");
+    };
+    size_t i = 0;
+    if (!is_op(i, "Matmul", 2)) return false;
+    const KernelParam* q = tensor(seq[i]->operands[0]);
+    const KernelParam* kt = tensor(seq[i]->operands[1]);
+    int s = seq[i++]->result;
+    int mode = 0, sidx = -1;
+    double sconst = 1.0;
+    if (is_op(i, "Mul", 2)) {  // S * scale: a scalar param or a constant, on either side
+        const int a = seq[i]->operands[0], b = seq[i]->operands[1];
+        const int other = a == s ? b : (b == s ? a : -1);
+        if (other < 0) return false;
+        auto pit = param_of.find(other);
+        if (pit != param_of.end() && pit->second->scalar_index >= 0 && pit->second->v.dtype == DType::F32) {
+            mode = 2;
+            sidx = pit->second->scalar_index;
+        } else if (constant.count(other)) {
+            mode = 1;
+            sconst = constant[other];
+        } else {
+            return false;
+        }
+        s = seq[i++]->result;
+    }
+    if (!is_op(i, "RowMax", 1) || seq[i]->operands[0] != s) return false;
+    const int m = seq[i++]->result;
+    if (!is_op(i, "Sub", 2) || seq[i]->operands[0] != s || seq[i]->operands[1] != m) return false;
+    const int d = seq[i++]->result;
+    if (!is_op(i, "Exp", 1) || seq[i]->operands[0] != d) return false;
+    const int e = seq[i++]->result;
+    if (!is_op(i, "RowSum", 1) || seq[i]->operands[0] != e) return false;
+    const int l = seq[i++]->result;
+    if (!is_op(i, "Div", 2) || seq[i]->operands[0] != e || seq[i]->operands[1] != l) return false;
+    const int w = seq[i++]->result;
+    if (!is_op(i, "Matmul", 2) || seq[i]->operands[0] != w) return false;
+    const KernelParam* v = tensor(seq[i]->operands[1]);
+    const int o = seq[i++]->result;
+    if (!is_op(i, "Store", 2) || seq[i]->operands[1] != o) return false;
+    const KernelParam* out = tensor(seq[i++]->operands[0]);
+    if (i != seq.size() || !q || !kt || !v || !out) return false;
+    const int L = kt->v.cols;
+    auto shape = [](const KernelParam* p, DType t, int r, int c) { return p->v.dtype == t && p->v.rows == r && p->v.cols == c; };
+    if (!shape(q, DType::F16, 128, 128) || !shape(kt, DType::F16, 128, L) || !shape(v, DType::F32, L, 128) ||
+        !shape(out, DType::F32, 128, 128) || L < 64 || L % 64 != 0)
+        return false;
+    // the inputs are read only, the output written only (the one Store)
+    if (ki.param_write[q->tensor_index] || ki.param_write[kt->tensor_index] || ki.param_write[v->tensor_index] ||
+        out == q || out == kt || out == v)
+        return false;
+    for (int id : {s, m, d, e, l, w, o}) {
+        auto it = kd.values.find(id);
+        if (it == kd.values.end() || it->second.dtype != DType::F32) return false;
+    }
+    ki.at_q = q->tensor_index;
+    ki.at_kt = kt->tensor_index;
+    ki.at_v = v->tensor_index;
+    ki.at_o = out->tensor_index;
+    ki.at_L = L;
+    ki.at_scale_mode = mode;
+    ki.at_scale_index = sidx;
+    ki.at_scale_const = static_cast<float>(sconst);
+    return true;
 }
 
 bool split_stages(KernelImpl& ki, const KernelDef& kd) {

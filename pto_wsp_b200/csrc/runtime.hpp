@@ -17,7 +17,7 @@
 namespace ptowsp {
 
 enum class ImplKind : uint8_t { RmsNorm, Softmax, TileProgram, Matmul, MatmulAcc, MatmulEpilogue, PagedDecode,
-                                IndexerScore, TopK, Staged };
+                                IndexerScore, TopK, Staged, Attention };
 
 // One stage of a generic kernel cut at its contractions: a matmul (tcgen05 tile kernel for f16 params of its
 // shapes, else the CUDA-core kernel with the tile program's fused multiply-add order) or a fused row program.
@@ -70,7 +70,16 @@ struct KernelImpl {
     // Staged: the stages in order and the [rows, cols] of each f32 scratch tile
     std::vector<Stage> stages;
     std::vector<std::pair<int, int>> scratch_tiles;
+    // Attention (fused tcgen05 kernel; the stages above stay as the fallback for views it does not take): tensor
+    // param indices of Q, K^T, V and the output, the key count, and the score scale (0 none, 1 the constant
+    // at_scale_const, 2 scalar param at_scale_index)
+    int at_q = -1, at_kt = -1, at_v = -1, at_o = -1, at_L = 0;
+    int at_scale_mode = 0, at_scale_index = -1;
+    float at_scale_const = 1.f;
 };
+// Whether a kernel is the fused attention pattern (Q.K^T [* scale] -> row softmax -> . V -> store; f16 Q and K^T,
+// f32 V and output, 128 x 128 Q / output tiles, L keys a multiple of 64); fills the at_* fields.
+bool match_attention(KernelImpl& ki, const KernelDef& kd);
 
 // Build (NVRTC) the fused row kernel of kernel `k` when its tile program is row-local (jit_state -> 2 or -1).
 void jit_prepare(KernelImpl& ki, const KernelDef& kd, int k);
@@ -136,6 +145,7 @@ struct Batch {  // tasks of one kernel inside one wave
     // Staged: [row-stage records (the batch's records with the scratch offsets after the view offsets) |
     // [oa, ob, oc] per task for each matmul stage] (-1 not built, 1 built)
     int64_t* st_rec_dev = nullptr;
+    int8_t at_ok = -1;               // Attention: every task's views meet the fused kernel's conditions
     int8_t st_ok = -1;
     uint32_t st_tc_mask = 0;           // matmul stages (in order) that run on the tcgen05 tile kernel
     int64_t st_group = 0;              // tasks per group of stage launches (scratch offsets repeat per group)
@@ -204,6 +214,7 @@ struct Program {
     int status = 0;
     int64_t opt_cache = 1, opt_chunks = 32, opt_sync = 1, opt_dry = 0, opt_stage_scratch_mb = 2048;
     int64_t opt_kernel_events = 0;       // bracket every batch launch with CUDA events (per-kernel device time)
+    int64_t opt_fused_attention = 1;     // 0: attention kernels run their stages instead of the fused kernel
     struct KernelEvent { int kernel; cudaEvent_t start, end; };
     std::vector<KernelEvent> kev_pending;  // recorded, not yet read
     std::vector<cudaEvent_t> kev_free;     // event pool

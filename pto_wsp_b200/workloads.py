@@ -365,6 +365,70 @@ def indexer_plan(batch: int, queries: int, heads: int, head_dim: int, context: i
     return _plan(name, [*tensors], [ks.build(), kt.build()], {"kind": "combine", "children": [n1, n2]}, _schedule())
 
 
+# ---------------------------------------------------------------------------
+# Attention tiles (the reference attention example's kernel at full tile sizes)
+# ---------------------------------------------------------------------------
+
+
+def attention_plan(batch: int, heads: int, q_tiles: int, kv_len: int, d: int = 128, scale: float | None = 0.088,
+                   v_dtype: str = "f32", name: str = "attention") -> dict:
+    """Frontend form (``examples/attention/pto_wsp_impl.py:51-68`` with f16 Q / K^T tiles)::
+
+        @kernel
+        def attention_tile(q: In[Tile[128, D, F16]], k_t: In[Tile[D, L, F16]], v: In[Tile[L, D, F32]],
+                           out: Out[Tile[128, D, F32]], scale: Scalar[F32]):
+            s = pto.mul(pto.matmul(q, k_t), scale)
+            w = pto.div(pto.exp(pto.sub(s, pto.rowmax(s))), pto.rowsum(...))
+            pto.store(out, pto.matmul(w, v))
+        for b in P(Dense[B]()):
+            for h in P(Dense[H]()):
+                for s in P(Dense[QT]()):
+                    attention_tile[b, h, s](q=Q[b][h][s], k_t=KT[b][h], v=V[b][h], out=O[b][h][s], scale=scale)
+
+    The softmax result is f32 (pto has no cast), so V is f32 too: the emitter takes a matmul only with both
+    operands f16 or both f32.  With d = 128 and L a multiple of 64 this is the fused tcgen05 attention kernel's
+    pattern; ``scale=None`` leaves the multiply out.  Tensors: 0 = Q [B, H, QT, 128, d] f16, 1 = K^T [B, H, d, L]
+    f16, 2 = V [B, H, L, d] f32, 3 = O [B, H, QT, 128, d] f32.
+    """
+    import struct
+
+    kb = KernelBuilder("attention_tile")
+    q = kb.param("q", "f16", 128, d)
+    kt = kb.param("k_t", "f16", d, kv_len)
+    v = kb.param("v", v_dtype, kv_len, d)
+    out = kb.param("out", "f32", 128, d)
+    scalars = []
+    s = kb.op("Matmul", [q, kt], ("f32", 128, kv_len))
+    if scale is not None:
+        sc = kb.param("scale", "f32")
+        s = kb.op("Mul", [s, sc], ("f32", 128, kv_len))
+        scalars = [{"u64": hex(struct.unpack("<I", struct.pack("<f", scale))[0])}]
+    mx = kb.op("RowMax", [s], ("f32", 128, 1))
+    s = kb.op("Sub", [s, mx], ("f32", 128, kv_len))
+    e = kb.op("Exp", [s], ("f32", 128, kv_len))
+    sm = kb.op("RowSum", [e], ("f32", 128, 1))
+    w = kb.op("Div", [e, sm], ("f32", 128, kv_len))
+    kb.store(out, kb.op("Matmul", [w, v], ("f32", 128, d)))
+    body = _pfor("b", batch, _pfor("h", heads, _pfor("s", q_tiles, _task("attention_tile", ["b", "h", "s"], [
+        _targ("q", 0, 5, ["b", "h", "s"]), _targ("k_t", 1, 4, ["b", "h"]), _targ("v", 2, 4, ["b", "h"]),
+        _targ("out", 3, 5, ["b", "h", "s"])], scalars))))
+    tensors = [("f16", [batch, heads, q_tiles, 128, d]), ("f16", [batch, heads, d, kv_len]),
+               (v_dtype, [batch, heads, kv_len, d]), ("f32", [batch, heads, q_tiles, 128, d])]
+    return _plan(name, tensors, [kb.build()], body, _schedule())
+
+
+def attention_inputs(rng, batch: int, heads: int, q_tiles: int, kv_len: int, d: int = 128, v_dtype: str = "f32"):
+    """Q, K^T, V ~ N(0,1) (f16, V in `v_dtype`), O filled with NaN."""
+    import numpy as np
+
+    q = rng.standard_normal((batch, heads, q_tiles, 128, d), dtype=np.float32).astype(np.float16)
+    kt = rng.standard_normal((batch, heads, d, kv_len), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((batch, heads, kv_len, d), dtype=np.float32).astype(
+        np.float16 if v_dtype == "f16" else np.float32)
+    o = np.full((batch, heads, q_tiles, 128, d), np.nan, np.float32)
+    return [q, kt, v, o]
+
+
 def bgemm_views(a, b, c, tile_m: int = 128, tile_n: int = 128):
     """The bgemm plan's tensor views of contiguous A[B,M,K], B[B,K,N], C[B,M,N] (numpy or torch)."""
     Bn, M, K = a.shape

@@ -1,0 +1,92 @@
+"""The fused tcgen05 attention kernel (-m gpu) against the oracle and an fp64 recompute.
+
+The kernel pattern is the reference attention tile at full size: S = Q.K^T (f16) [* scale], a row softmax in f32,
+O = W.V with V f32 (pto has no cast, so the softmax result and V are both f32), stored f32.  The oracle runs the
+tile program's arithmetic (fused multiply-adds in k order); the fused kernel runs Q.K^T on kind::f16 and W.V on
+kind::tf32 with a three-term split, which keeps each product to ~22 bits.  Tolerance: plain relative error 1e-4
+on every output element with |O| >= 1e-2 rms(O) (smaller ones: absolute 1e-4 x that floor) against the oracle,
+and the north_star's 2e-3 contraction bar against fp64.
+"""
+
+import numpy as np
+import pytest
+from cpu_sim import CpuSim
+
+from tolerance import RTOL_F16_MMA, assert_rel, rms
+
+from pto_wsp_b200 import workloads
+from pto_wsp_b200.runtime import CudaExecutable
+
+pytestmark = pytest.mark.gpu
+
+
+def fp64_attention(arrays, scale):
+    q, kt, v = (a.astype(np.float64) for a in arrays[:3])
+    s = np.einsum("bhtrd,bhdk->bhtrk", q, kt) * (np.float64(np.float32(scale)) if scale is not None else 1.0)
+    w = np.exp(s - s.max(-1, keepdims=True))
+    w /= w.sum(-1, keepdims=True)
+    return np.einsum("bhtrk,bhkd->bhtrd", w, v)
+
+
+@pytest.mark.parametrize("B,H,QT,L,scale", [(1, 2, 2, 64, 0.088), (2, 1, 2, 256, None), (1, 2, 1, 1024, 0.088),
+                                            (1, 1, 1, 448, 0.125)])
+def test_fused_attention_vs_oracle(B, H, QT, L, scale, require_cuda):
+    rng = np.random.default_rng(L)
+    plan = workloads.attention_plan(B, H, QT, L, scale=scale)
+    arrays = workloads.attention_inputs(rng, B, H, QT, L)
+    ref = [a.copy() for a in arrays]
+    cyc = CpuSim(plan).run(ref)
+    ex = CudaExecutable(plan)
+    assert ex.describe()["kernels"][0]["impl"] == "attention_tcgen05"
+    for _ in range(2):  # the second run replays the cached task table
+        got = [a.copy() for a in arrays]
+        assert ex.run_with_symbols(got, {}, {}, {}) == cyc
+        assert ex.timing()["launches"] == 1
+        assert_rel(got[3], ref[3], 1e-4, 1e-2 * rms(ref[3]))
+        o64 = fp64_attention(arrays, scale)
+        assert_rel(got[3], o64, RTOL_F16_MMA, 1e-2 * rms(o64))
+
+
+def test_fused_attention_large_logits_rescale(require_cuda):
+    # logits that grow from block to block force the lazy row-max updates (O and the sum rescaled in TMEM)
+    rng = np.random.default_rng(3)
+    B, H, QT, L = 1, 1, 1, 512
+    plan = workloads.attention_plan(B, H, QT, L, scale=1.0)
+    arrays = workloads.attention_inputs(rng, B, H, QT, L)
+    ramp = np.linspace(0.0, 6.0, L, dtype=np.float32)  # scores rise by ~20 over the keys
+    arrays[1] = (arrays[1].astype(np.float32) * 0.05 + ramp[None, None, None, :] * 0.25).astype(np.float16)
+    arrays[0] = (np.abs(arrays[0].astype(np.float32)) * 0.2 + 0.5).astype(np.float16)
+    ref = [a.copy() for a in arrays]
+    CpuSim(plan).run(ref)
+    got = [a.copy() for a in arrays]
+    CudaExecutable(plan).run_with_symbols(got, {}, {}, {})
+    assert_rel(got[3], ref[3], 1e-4, 1e-2 * rms(ref[3]))
+
+
+def test_fused_and_staged_forms_agree(require_cuda):
+    rng = np.random.default_rng(5)
+    plan = workloads.attention_plan(2, 2, 1, 256)
+    arrays = workloads.attention_inputs(rng, 2, 2, 1, 256)
+    fused, staged = [a.copy() for a in arrays], [a.copy() for a in arrays]
+    CudaExecutable(plan).run_with_symbols(fused, {}, {}, {})
+    ex = CudaExecutable(plan)
+    ex.set_option("fused_attention", 0)
+    ex.run_with_symbols(staged, {}, {}, {})
+    assert ex.timing()["launches"] == 4
+    assert_rel(fused[3], staged[3], 1e-4, 1e-2 * rms(staged[3]))
+
+
+def test_unaligned_output_view_runs_the_stages(require_cuda):
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(6)
+    plan = workloads.attention_plan(1, 1, 2, 128)
+    arrays = workloads.attention_inputs(rng, 1, 1, 2, 128)
+    ref = [a.copy() for a in arrays]
+    CpuSim(plan).run(ref)
+    dev = [torch.from_numpy(a.copy()).cuda() for a in arrays[:3]]
+    flat = torch.full((arrays[3].size + 1,), float("nan"), device="cuda")
+    out = flat[1:].view(arrays[3].shape)  # 4 bytes off a 16-byte boundary: not a TMA / vector-store base
+    ex = CudaExecutable(plan)
+    ex.run_with_symbols(dev + [out], {}, {}, {})
+    assert ex.timing()["launches"] == 4  # the staged form ran
+    assert_rel(out.cpu().numpy(), ref[3], 1e-4, 1e-2 * rms(ref[3]))
