@@ -27,7 +27,7 @@
 //   warps 2-5   softmax and epilogue, one row per thread (warp w reads TMEM lanes 32 (w % 4) ..): tcgen05.ld of
 //               the S row (twice: max, then exponentials), P_hi / P_lo written to shared memory in the swizzled
 //               K-major layout the MMA reads; at the end O / sum stored to the out row.
-//   warps 6-9   split each V block into V_hi / V_lo, element for element in the TMA layout.
+//   warps 6-9   split each V block into V_hi / V_lo and transpose it into the K-major layout the MMA reads.
 // Every mbarrier wait is bounded (~2 s of %globaltimer): on timeout the CTA records kErrTimeout, drains its own
 // copies and MMAs, frees TMEM and returns.  No cluster multicast (loads read this GPU's memory only).
 #include <cuda.h>
@@ -68,10 +68,11 @@ constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t TMEM_O = 128;
 constexpr float kRescaleLog2 = 8.f;  // a row's reference max moves when its max grows by more than this
 
-// Instruction descriptor, kind::tf32: D f32 [4,6)=1, A tf32 [7,10)=2, B tf32 [10,13)=2, A K-major [15]=0,
-// B MN-major [16]=1, N>>3 [17,23), M>>4 [24,29).
+// Instruction descriptor, kind::tf32: D f32 [4,6)=1, A tf32 [7,10)=2, B tf32 [10,13)=2, A and B K-major
+// ([15] = [16] = 0), N>>3 [17,23), M>>4 [24,29).  (An MN-major B of 32-bit elements would need the 32-byte-atom
+// variant of the 128-byte swizzle; the splitters write V transposed instead.)
 constexpr uint32_t idesc_tf32(int m, int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (1u << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(m >> 4) << 24);
 }
 
@@ -223,8 +224,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     for (int k8 = 0; k8 < AT_BN / 8; ++k8) {
                         // A: K-major f32 rows of 32 keys (128 B) per 16 KB chunk; 8 keys = 32 B per step
                         const uint64_t a = smem_desc(pa[t] + (k8 >> 2) * 16384 + (k8 & 3) * 32, 16, 1024);
-                        // B: MN-major, 32-dim (128 B) N chunks 8 KB apart (LBO), 8 key rows (1 KB) per step
-                        const uint64_t b = smem_desc(vb[t] + k8 * 1024, BOX, 1024);
+                        // B: V^T, K-major like A (rows = head dims)
+                        const uint64_t b = smem_desc(vb[t] + (k8 >> 2) * 16384 + (k8 & 3) * 32, 16, 1024);
                         mma_tf32(tmem_base + TMEM_O, a, b, idesc_o, (i > 0 || t > 0 || k8 > 0) ? 1u : 0u);
                     }
                 mma_commit(smem_u32(vsp_empty));
@@ -264,19 +265,45 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
     } else if (warp >= 6) {
         // ---------------- V splitters (warps 6..9) ----------------
+        // The TMA lands V as [64 keys][128 dims] (four 32-dim chunks of 8 KB, 128-byte rows, 16-byte unit u of key
+        // row k at u ^ (k % 8)); the MMA reads V^T K-major: [128 dims][64 keys] as two 32-key chunks of 16 KB,
+        // unit u of dim row n at u ^ (n % 8).  Each thread moves 4 x 4 blocks (4 keys x 4 dims): four 16-byte
+        // reads along the dims, a register transpose, four 16-byte writes along the keys, per part.
         const int t = threadIdx.x - 6 * 32;  // 0..127
-        const float4* raw = reinterpret_cast<const float4*>(smem + OFF_VRAW);
-        float4* hi = reinterpret_cast<float4*>(smem + OFF_VHI);
-        float4* lo = reinterpret_cast<float4*>(smem + OFF_VLO);
+        const uint8_t* raw = smem + OFF_VRAW;
+        uint8_t* hi = smem + OFF_VHI;
+        uint8_t* lo = smem + OFF_VLO;
         for (int j = 0; j < nb; ++j) {
             if (!mbar_wait(smem_u32(vraw_full), j & 1, abort_flag, args.err)) break;
             if (j >= 1 && !mbar_wait(smem_u32(vsp_empty), (j - 1) & 1, abort_flag, args.err)) break;
-#pragma unroll 4
-            for (int i = t; i < V_BYTES / 16; i += 128) {  // the same swizzled position in every buffer
-                const float4 x = raw[i];
-                const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-                hi[i] = h;
-                lo[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+#pragma unroll 1
+            for (int blk = t; blk < (AT_BN / 4) * (AT_D / 4); blk += 128) {
+                const int kq = blk % (AT_BN / 4), dq = blk / (AT_BN / 4);  // keys 4kq.., dims 4dq..
+                float x[4][4];                                             // [key][dim]
+#pragma unroll
+                for (int a = 0; a < 4; ++a) {
+                    const int k = 4 * kq + a;
+                    const int u = dq & 7;  // 16-byte unit of the dims inside their 32-dim chunk
+                    const float4 v = *reinterpret_cast<const float4*>(raw + (dq >> 3) * BOX + k * 128 + ((u ^ (k & 7)) << 4));
+                    x[a][0] = v.x;
+                    x[a][1] = v.y;
+                    x[a][2] = v.z;
+                    x[a][3] = v.w;
+                }
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int n = 4 * dq + b;
+                    const int u = kq & 7;  // 16-byte unit of the keys inside their 32-key chunk
+                    const int off = (kq >> 3) * 16384 + n * 128 + ((u ^ (n & 7)) << 4);
+                    float h[4], l[4];
+#pragma unroll
+                    for (int a = 0; a < 4; ++a) {
+                        h[a] = tf32_hi(x[a][b]);
+                        l[a] = x[a][b] - h[a];
+                    }
+                    *reinterpret_cast<float4*>(hi + off) = make_float4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<float4*>(lo + off) = make_float4(l[0], l[1], l[2], l[3]);
+                }
             }
             mbar_arrive(smem_u32(vraw_empty));
             fence_proxy_async_smem();  // V_hi / V_lo become visible to the tensor core's reads
