@@ -172,6 +172,10 @@ typedef struct ptowsp_timing {
     uint64_t chunks;      /* chunks of an overlapped host-staged run (copies, kernels and copies back on three
                              streams); 0: staged copies and kernels ran back to back.  A dry run reports the
                              chunks a run with the same buffers would use. */
+    uint64_t walks;       /* host walks of the task loop in the last run (0: a cached task table was replayed, or
+                             its records were rebuilt on the device) */
+    uint64_t expansions;  /* loops whose task records the device rebuilt for new ragged lengths or a new sparse
+                             selection, with no host walk and no record upload */
 } ptowsp_timing;
 
 PTOWSP_API int ptowsp_cuda_last_timing(const ptowsp_program* prog, ptowsp_timing* out);

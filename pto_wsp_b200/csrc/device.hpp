@@ -101,6 +101,11 @@ cudaError_t launch_select_scalars(int64_t* rec, int stride, int scalar_pos, cons
                                   int row_words, const int* tree, int nconds, int nscalars, const void* src,
                                   int src_type, int64_t src_span, int* err, cudaStream_t s);
 
+// Task records rebuilt on the device: rec[t][w] = base_delta[w] + var_t * base_delta[stride + w] for t < n, with
+// var_t = t (vars == nullptr) or vars[t].
+cudaError_t launch_expand_records(int64_t* rec, int stride, int64_t n, const int64_t* base_delta, const int32_t* vars,
+                                  cudaStream_t s);
+
 // Tile widths the hand-written RMSNorm / softmax row kernels take (others run the fused row program).
 inline bool row_width_supported(int cols) { return cols == 128 || cols == 256 || cols == 512 || cols == 1024; }
 cudaError_t launch_rmsnorm_rows(const TaskBatch& b, int workers, cudaStream_t s);

@@ -640,4 +640,26 @@ cudaError_t launch_select_scalars(int64_t* rec, int stride, int scalar_pos, cons
     return cudaGetLastError();
 }
 
+
+namespace {
+__global__ void expand_records_kernel(int64_t* rec, int stride, int64_t n, const int64_t* bd, const int32_t* vars) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * stride) return;
+    const int64_t t = i / stride;
+    const int w = static_cast<int>(i % stride);
+    const int64_t var = vars ? static_cast<int64_t>(vars[t]) : t;
+    rec[i] = bd[w] + var * bd[stride + w];
+}
+}  // namespace
+
+cudaError_t launch_expand_records(int64_t* rec, int stride, int64_t n, const int64_t* base_delta, const int32_t* vars,
+                                  cudaStream_t s) {
+    const int64_t total = n * stride;
+    if (total <= 0) return cudaSuccess;
+    const int64_t blocks = (total + 255) / 256;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
+    expand_records_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(rec, stride, n, base_delta, vars);
+    return cudaGetLastError();
+}
+
 }  // namespace ptowsp::dev

@@ -169,6 +169,14 @@ struct Walker {
     void note(std::string q) {
         if (seen.insert(q).second) log.push_back(std::move(q));
     }
+    // loops over a ragged axis or a selection whose body is one task (candidates for device-side expansion)
+    struct LoopNote {
+        const Node* node;
+        char kind;
+        std::string key_name;
+        std::vector<int64_t> vars;  // selection: the loop variable of each iteration
+    };
+    std::vector<LoopNote> loops;
     uint64_t symbol_u64(uint64_t id) {
         uint64_t v = ctx->get_symbol_u64 ? ctx->get_symbol_u64(ctx->ctx, id) : 0;
         note("s" + std::to_string(id) + "=" + std::to_string(v));
@@ -370,8 +378,9 @@ struct Walker {
                                               : nullptr;
                     if (lens)
                         for (int64_t i = 0; i < outer; ++i) ub += lens[i];
-                    note("r" + std::to_string(n.axis.lengths_sym) + ":" + std::to_string(n.axis.outer_sym) + "=" +
-                         std::to_string(ub));
+                    const std::string kn = "r" + std::to_string(n.axis.lengths_sym) + ":" + std::to_string(n.axis.outer_sym);
+                    note(kn + "=" + std::to_string(ub));
+                    if (n.body && n.body->kind == Node::Kind::Task) loops.push_back({&n, 'r', kn, {}});
                 }
                 uint64_t done = ready, cur = ready;
                 env.push_back({&n.var, 0});
@@ -389,8 +398,13 @@ struct Walker {
                 const int32_t* indices = ctx->get_symbol_ptr ? static_cast<const int32_t*>(ctx->get_symbol_ptr(ctx->ctx, n.indices_sym)) : nullptr;
                 int64_t nnz = indptr ? indptr[outer] : 0;
                 // the walk depends on the CSR arrays themselves: key a cached task table on their contents
-                note("c" + std::to_string(n.indptr_sym) + ":" + std::to_string(n.indices_sym) + ":" +
-                     std::to_string(n.outer_sym) + "=" + std::to_string(csr_hash(indptr, indices, outer)));
+                const std::string kn = "c" + std::to_string(n.indptr_sym) + ":" + std::to_string(n.indices_sym) + ":" +
+                                       std::to_string(n.outer_sym);
+                note(kn + "=" + std::to_string(csr_hash(indptr, indices, outer)));
+                if (n.body && n.body->kind == Node::Kind::Task) {
+                    loops.push_back({&n, 'c', kn, {}});
+                    for (int64_t p = 0; p < nnz; ++p) loops.back().vars.push_back(indices ? indices[p] : 0);
+                }
                 uint64_t done = ready;
                 env.push_back({&n.var, 0});
                 for (int64_t p = 0; p < nnz; ++p) {
@@ -819,6 +833,10 @@ Batch::~Batch() {
 
 LaunchProgram::~LaunchProgram() {
     if (rec_dev) cudaFree(rec_dev);
+    if (expand) {
+        if (expand->base_delta_dev) cudaFree(expand->base_delta_dev);
+        if (expand->vars_dev) cudaFree(expand->vars_dev);
+    }
 }
 
 void set_error(const std::string& msg) { g_err = msg; }
@@ -1546,7 +1564,7 @@ struct PipePlan {
 };
 
 bool plan_pipeline(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, bool dry, PipePlan& pp) {
-    if (!P.cacheable || P.opt_chunks < 2 || L.waves.empty() || L.waves.size() > 8) return false;
+    if (!P.cacheable || P.opt_chunks < 2 || L.waves.empty() || L.waves.size() > 8 || L.no_pipeline) return false;
     std::vector<Batch*>& chain = pp.chain;  // one batch per wave
     int64_t min_tasks = INT64_MAX;
     for (auto& w : L.waves) {
@@ -2160,6 +2178,155 @@ bool split_stages(KernelImpl& ki, const KernelDef& kd) {
     return true;
 }
 
+// After a walk: when the workload is one loop over a ragged axis or a sparse selection with one task as its body
+// (the reference's ParallelFor over Ragged, pto_codegen.cpp:2305-2416, and Select, :2417-2457), and its task
+// records are affine in the loop variable, keep what a later run with other lengths or another selection needs
+// to rebuild them on the device.  Only kernels whose launch reads nothing but the records qualify (row programs,
+// row kernels, the tile-program interpreter), with round-robin or no dispatch (the makespan is then recomputed
+// from the task count alone).
+void plan_expand(Program& P, LaunchProgram& L, const std::vector<Walker::LoopNote>& loops) {
+    if (loops.size() != 1 || L.waves.size() != 1 || L.waves[0].batches.size() != 1) return;
+    const auto& ln = loops[0];
+    if (ln.node != P.plan.body.get()) return;
+    Batch& B = L.waves[0].batches[0];
+    if (B.node != ln.node->body.get() || B.sel || B.ntasks < 2 || B.rec.empty()) return;
+    const KernelImpl& ki = P.impls[B.kernel];
+    if (ki.kind != ImplKind::TileProgram && ki.kind != ImplKind::RmsNorm && ki.kind != ImplKind::Softmax) return;
+    const std::string& pol = P.plan.schedule.dispatch_policy;
+    if (!pol.empty() && pol != "round_robin" && pol != "work_steal") return;
+    // exactly one data-dependent key entry, this loop's
+    size_t idx = SIZE_MAX;
+    for (size_t i = 0; i + 1 < L.key.size(); ++i) {
+        const char k = L.key[i][0];
+        if (k != 'r' && k != 'c') continue;
+        if (idx != SIZE_MAX || L.key[i].compare(0, ln.key_name.size() + 1, ln.key_name + "=") != 0) return;
+        idx = i;
+    }
+    if (idx == SIZE_MAX) return;
+    const int64_t n = B.ntasks, stride = B.stride;
+    auto var = [&](int64_t t) { return ln.kind == 'r' ? t : ln.vars[static_cast<size_t>(t)]; };
+    if (ln.kind == 'c' && static_cast<int64_t>(ln.vars.size()) != n) return;
+    int64_t t1 = 1;
+    while (t1 < n && var(t1) == var(0)) ++t1;
+    if (t1 >= n) return;
+    std::vector<int64_t> base(static_cast<size_t>(stride)), delta(static_cast<size_t>(stride));
+    const int64_t dv = var(t1) - var(0);
+    for (int64_t w = 0; w < stride; ++w) {
+        const int64_t d = B.rec[t1 * stride + w] - B.rec[w];
+        if (d % dv) return;
+        delta[w] = d / dv;
+        base[w] = B.rec[w] - var(0) * delta[w];
+    }
+    for (int64_t t = 0; t < n; ++t)
+        for (int64_t w = 0; w < stride; ++w)
+            if (B.rec[t * stride + w] != base[w] + var(t) * delta[w]) return;
+    for (int w = 0; w < P.plan.kernels[B.kernel].num_tensor_params; ++w)
+        if ((base[w] & 3) || (delta[w] & 3)) B.aligned_rows = false;  // some var may give an unaligned view
+    auto X = std::make_unique<LoopExpand>();
+    X->kind = ln.kind;
+    X->key_index = idx;
+    X->key_name = ln.key_name;
+    X->parallel = ln.node->kind != Node::Kind::ForEach;
+    if (ln.kind == 'r') {
+        X->lengths_sym = ln.node->axis.lengths_sym;
+        X->outer_sym = ln.node->axis.outer_sym;
+    } else {
+        X->indptr_sym = ln.node->indptr_sym;
+        X->indices_sym = ln.node->indices_sym;
+        X->outer_sym = ln.node->outer_sym;
+    }
+    for (uint8_t w : ki.param_write) X->writes = X->writes || w;
+    X->base = base;
+    X->delta = delta;
+    std::vector<int64_t> bd(base);
+    bd.insert(bd.end(), delta.begin(), delta.end());
+    PW_CUDA(cudaMalloc(&X->base_delta_dev, bd.size() * sizeof(int64_t)));
+    PW_CUDA(cudaMemcpy(X->base_delta_dev, bd.data(), bd.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
+    L.expand = std::move(X);
+}
+
+// A run whose only changed runtime answer is the expandable loop's: rebuild its task records on the device from
+// the new count (ragged: the sum of the lengths; selection: the indices, uploaded), recompute the makespan with the
+// same Scheduler::issue model over that many tasks, and keep the cached table.  False (nothing changed) when the
+// new run does not fit: no task, or a selection that repeats an index while the kernel writes (its tasks would
+// conflict: the host walk orders them).
+bool expand_on_device(Program& P, LaunchProgram& L, RuntimeContext* ctx, size_t ntensors) {
+    LoopExpand& X = *L.expand;
+    auto sym_u64 = [&](uint64_t id) { return ctx->get_symbol_u64 ? ctx->get_symbol_u64(ctx->ctx, id) : 0; };
+    auto sym_ptr = [&](uint64_t id) {
+        return ctx->get_symbol_ptr ? static_cast<const int32_t*>(ctx->get_symbol_ptr(ctx->ctx, id)) : nullptr;
+    };
+    int64_t n = 0;
+    uint64_t key_value = 0;
+    const int32_t* vars = nullptr;
+    const int64_t outer = static_cast<int64_t>(sym_u64(X.outer_sym));
+    if (X.kind == 'r') {
+        const int32_t* lens = sym_ptr(X.lengths_sym);
+        if (!lens) return false;
+        for (int64_t i = 0; i < outer; ++i) n += lens[i];
+        key_value = static_cast<uint64_t>(n);
+    } else {
+        const int32_t* indptr = sym_ptr(X.indptr_sym);
+        vars = sym_ptr(X.indices_sym);
+        if (!indptr || !vars) return false;
+        n = indptr[outer];
+        key_value = csr_hash(indptr, vars, outer);
+        if (X.writes) {
+            std::unordered_set<int32_t> seen;
+            for (int64_t p = 0; p < n; ++p)
+                if (!seen.insert(vars[p]).second) return false;
+        }
+    }
+    if (n < 1) return false;
+    Batch& B = L.waves[0].batches[0];
+    const size_t need = static_cast<size_t>(n) * static_cast<size_t>(B.stride);
+    if (need > L.rec_cap) {
+        int64_t* nb = nullptr;
+        PW_CUDA(cudaStreamSynchronize(P.stream));  // earlier runs may still read the old table
+        PW_CUDA(cudaMalloc(&nb, need * sizeof(int64_t)));
+        if (L.rec_dev) PW_CUDA(cudaFree(L.rec_dev));
+        L.rec_dev = nb;
+        L.rec_cap = need;
+    }
+    const int32_t* vars_dev = nullptr;
+    if (vars) {
+        if (X.vars_cap < static_cast<size_t>(n)) {
+            PW_CUDA(cudaStreamSynchronize(P.stream));
+            if (X.vars_dev) PW_CUDA(cudaFree(X.vars_dev));
+            X.vars_dev = nullptr;
+            PW_CUDA(cudaMalloc(&X.vars_dev, static_cast<size_t>(n) * sizeof(int32_t)));
+            X.vars_cap = static_cast<size_t>(n);
+        }
+        PW_CUDA(cudaMemcpyAsync(X.vars_dev, vars, static_cast<size_t>(n) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                P.stream));
+        PW_CUDA(cudaStreamSynchronize(P.stream));  // the indices are the caller's memory
+        vars_dev = X.vars_dev;
+    }
+    PW_CUDA(dev::launch_expand_records(L.rec_dev, B.stride, n, X.base_delta_dev, vars_dev, P.stream));
+    B.ntasks = n;
+    B.dev_off = 0;
+    L.rec_elems = need;
+    L.tasks = static_cast<uint64_t>(n);
+    // makespan: the walk's Scheduler::issue sequence for n tasks of this kernel (pto_codegen.cpp:2679-2692)
+    const Schedule& sc = P.plan.schedule;
+    Scheduler sched(static_cast<uint32_t>(sc.num_targets > 0 ? sc.num_targets : (sc.streams > 0 ? sc.streams : 1)),
+                    static_cast<uint64_t>(sc.window_tasks));
+    const uint64_t cyc = P.impls[B.kernel].cycles;
+    uint64_t done = 0, cur = 0;
+    for (int64_t t = 0; t < n; ++t) {
+        const uint32_t wid = sc.dispatch_policy.empty() ? 0u : static_cast<uint32_t>(static_cast<uint64_t>(t) % sched.n);
+        if (X.parallel) done = std::max(done, sched.issue(cyc, wid, 0));
+        else cur = sched.issue(cyc, wid, cur);
+    }
+    L.makespan = X.parallel ? done : cur;
+    L.key[X.key_index] = X.key_name + "=" + std::to_string(key_value);
+    // which elements the loop writes changed: stage every host tensor in and out
+    L.full_write.assign(ntensors, 0);
+    L.write_first.assign(ntensors, 0);
+    L.no_pipeline = true;
+    return true;
+}
+
 uint64_t run_program(Program& P, RuntimeContext* ctx) {
     auto t_start = std::chrono::steady_clock::now();
     if (!ctx) throw Error(PTOWSP_ERR_ARG, "RuntimeContext is null");
@@ -2245,6 +2412,7 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
     for (auto& b : T)
         for (auto s : b.strides) stride_sig += std::to_string(s) + ",";
     bool replay = false;
+    size_t mismatches = 0, mismatch_at = SIZE_MAX;
     if (P.cacheable && P.opt_cache && P.cached) {
         replay = !P.cached->key.empty() && P.cached->key.back() == stride_sig;
         for (size_t i = 0; replay && i + 1 < P.cached->key.size(); ++i) {
@@ -2276,7 +2444,17 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
             } else {
                 replay = false;
             }
-            if (got != want) replay = false;
+            if (got != want) {
+                ++mismatches;
+                mismatch_at = i;
+            }
+        }
+        if (mismatches) {
+            // only the expandable loop's ragged lengths or selection changed: rebuild its records on the device
+            const bool one_loop = replay && mismatches == 1 && P.cached->expand &&
+                                  mismatch_at == P.cached->expand->key_index && !dry;
+            replay = one_loop && expand_on_device(P, *P.cached, ctx, T.size());
+            if (replay) P.timing.expansions = 1;
         }
     }
 
@@ -2352,6 +2530,8 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         L->write_first.assign(T.size(), 0);
         for (size_t tid = 0; tid < T.size(); ++tid)
             L->write_first[tid] = L->full_write[tid] && any_w[tid] && last_w[tid] < first_r[tid] ? 1 : 0;
+        P.timing.walks = 1;
+        if (!dry) plan_expand(P, *L, W->loops);
     }
 
     if (dry) {
@@ -2361,6 +2541,7 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
             W = std::make_unique<Walker>(P, ctx, T, *L, log);
             W->flush = [] {};
             W->dry = true;
+            P.timing.walks = 1;
             L->makespan = W->node(*plan.body, 0);
             W->close_wave();
             L->full_write.assign(T.size(), 0);
@@ -2442,6 +2623,7 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         fresh = std::make_unique<LaunchProgram>();
         L = fresh.get();
         W = std::make_unique<Walker>(P, ctx, T, *L, log);
+        P.timing.walks = 1;
         W->flush = [&]() {
             W->close_wave();
             upload_and_launch(L->waves.size());

@@ -182,8 +182,26 @@ struct Wave {
     std::unordered_map<const Node*, size_t> by_node;  // task node -> batch index
 };
 
+// A loop over a ragged axis or a sparse selection whose body is one task, in a workload of that loop alone: its
+// task records are affine in the loop variable (record = base + var * delta), so a run with other lengths or
+// another selection rebuilds them on the device (expand_records_kernel) instead of walking the loop on the host.
+struct LoopExpand {
+    char kind = 0;              // 'r' ragged (var = 0 .. sum of lengths - 1), 'c' selection (var = indices[p])
+    size_t key_index = 0;       // its entry in LaunchProgram::key
+    std::string key_name;       // that entry up to '='
+    uint64_t lengths_sym = 0, outer_sym = 0, indptr_sym = 0, indices_sym = 0;
+    bool parallel = true;       // ParallelFor (tasks issued from the same ready time) or ForEach (chained)
+    bool writes = false;        // the kernel writes a tensor (a selection with repeated indices must be walked)
+    std::vector<int64_t> base, delta;  // per record word
+    int64_t* base_delta_dev = nullptr; // [base | delta] on the device
+    int32_t* vars_dev = nullptr;       // selection indices of the last expanded run
+    size_t vars_cap = 0;
+};
+
 struct LaunchProgram {  // result of one walk, reusable for static workloads
     std::vector<Wave> waves;
+    std::unique_ptr<LoopExpand> expand;  // set when the workload is one loop whose records the device can rebuild
+    bool no_pipeline = false;            // records rebuilt on the device: no host copy for chunk planning
     uint64_t makespan = 0;
     uint64_t tasks = 0;
     size_t rec_elems = 0;

@@ -74,6 +74,8 @@ class Timing(C.Structure):
         ("d2h_bytes", C.c_uint64),
         ("slot_syncs", C.c_uint64),
         ("chunks", C.c_uint64),
+        ("walks", C.c_uint64),
+        ("expansions", C.c_uint64),
     ]
 
 
