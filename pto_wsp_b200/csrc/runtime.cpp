@@ -2226,6 +2226,10 @@ void plan_expand(Program& P, LaunchProgram& L, const std::vector<Walker::LoopNot
     X->kind = ln.kind;
     X->key_index = idx;
     X->key_name = ln.key_name;
+    const uint64_t outer_sym = ln.kind == 'r' ? ln.node->axis.outer_sym : ln.node->outer_sym;
+    const std::string outer_name = "s" + std::to_string(outer_sym) + "=";
+    for (size_t i = 0; i + 1 < L.key.size(); ++i)
+        if (L.key[i].compare(0, outer_name.size(), outer_name) == 0) X->outer_key_index = i;
     X->parallel = ln.node->kind != Node::Kind::ForEach;
     if (ln.kind == 'r') {
         X->lengths_sym = ln.node->axis.lengths_sym;
@@ -2320,6 +2324,8 @@ bool expand_on_device(Program& P, LaunchProgram& L, RuntimeContext* ctx, size_t 
     }
     L.makespan = X.parallel ? done : cur;
     L.key[X.key_index] = X.key_name + "=" + std::to_string(key_value);
+    if (X.outer_key_index != SIZE_MAX)
+        L.key[X.outer_key_index] = "s" + std::to_string(X.outer_sym) + "=" + std::to_string(static_cast<uint64_t>(outer));
     // which elements the loop writes changed: stage every host tensor in and out
     L.full_write.assign(ntensors, 0);
     L.write_first.assign(ntensors, 0);
@@ -2412,7 +2418,7 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
     for (auto& b : T)
         for (auto s : b.strides) stride_sig += std::to_string(s) + ",";
     bool replay = false;
-    size_t mismatches = 0, mismatch_at = SIZE_MAX;
+    size_t mismatches = 0, loop_mismatches = 0;
     if (P.cacheable && P.opt_cache && P.cached) {
         replay = !P.cached->key.empty() && P.cached->key.back() == stride_sig;
         for (size_t i = 0; replay && i + 1 < P.cached->key.size(); ++i) {
@@ -2446,13 +2452,13 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
             }
             if (got != want) {
                 ++mismatches;
-                mismatch_at = i;
+                const LoopExpand* X = P.cached->expand.get();
+                if (X && (i == X->key_index || i == X->outer_key_index)) ++loop_mismatches;
             }
         }
         if (mismatches) {
             // only the expandable loop's ragged lengths or selection changed: rebuild its records on the device
-            const bool one_loop = replay && mismatches == 1 && P.cached->expand &&
-                                  mismatch_at == P.cached->expand->key_index && !dry;
+            const bool one_loop = replay && mismatches == loop_mismatches && !dry;
             replay = one_loop && expand_on_device(P, *P.cached, ctx, T.size());
             if (replay) P.timing.expansions = 1;
         }

@@ -189,6 +189,7 @@ struct LoopExpand {
     char kind = 0;              // 'r' ragged (var = 0 .. sum of lengths - 1), 'c' selection (var = indices[p])
     size_t key_index = 0;       // its entry in LaunchProgram::key
     std::string key_name;       // that entry up to '='
+    size_t outer_key_index = SIZE_MAX;  // the entry of its outer-size symbol (which may change with it)
     uint64_t lengths_sym = 0, outer_sym = 0, indptr_sym = 0, indices_sym = 0;
     bool parallel = true;       // ParallelFor (tasks issued from the same ready time) or ForEach (chained)
     bool writes = false;        // the kernel writes a tensor (a selection with repeated indices must be walked)
