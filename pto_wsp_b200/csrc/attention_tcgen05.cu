@@ -14,7 +14,8 @@
 //   * S_j = Q . K^T_j: tcgen05.mma kind::f16 (exact f16 products, f32 accumulation);
 //   * O += W_j . V_j: kind::tf32 on a three-term split, P_hi.V_hi + P_hi.V_lo + P_lo.V_hi, where x_hi is x with the
 //     low 13 mantissa bits cleared (exactly a tf32) and x_lo = x - x_hi: each product carries ~22 bits, the f32
-//     tile program's accuracy (a single tf32 pass would give the terms a 2^-11 relative error).
+//     tile program's accuracy (a single tf32 pass would give the terms a 2^-11 relative error).  P is the A
+//     operand straight from TMEM (double-buffered next to S and O), V^T the B operand from shared memory.
 // Keys go in blocks of 64 with an online softmax in the base-2 domain; the running row max is kept lazily (a row's O
 // and sum are rescaled only when its max grows by more than 2^8), which changes no result beyond rounding.  The row
 // sum uses the f32 probabilities and divides O once at the end.
@@ -22,12 +23,14 @@
 // One CTA per task, 10 warps:
 //   warp 0      TMA producer: Q once (two 128 x 64 K-major f16 boxes), per key block a K^T block (two 64 x 64
 //               MN-major f16 boxes, two stages) and a V block (four 32 x 64 MN-major f32 boxes), 128-byte swizzle.
-//   warp 1      owns TMEM (S double buffer: columns 0-127; O: 128-255) and issues the MMAs from one thread,
-//               S_{j+1} before O += W_j.V_j so that the tensor pipe works while the softmax runs.
+//   warp 1      owns TMEM (S double buffer: columns 0-127; O: 128-255; P double buffer: 256-511) and issues the
+//               MMAs from one thread, S_{j+1} before O += W_j.V_j so that the tensor pipe works while the softmax
+//               runs.
 //   warps 2-5   softmax and epilogue, one row per thread (warp w reads TMEM lanes 32 (w % 4) ..): tcgen05.ld of
-//               the S row (twice: max, then exponentials), P_hi / P_lo written to shared memory in the swizzled
-//               K-major layout the MMA reads; at the end O / sum stored to the out row.
-//   warps 6-9   split each V block into V_hi / V_lo and transpose it into the K-major layout the MMA reads.
+//               the S row (twice: max, then exponentials), P_hi / P_lo stored into the row's TMEM lane with
+//               tcgen05.st; at the end O / sum stored to the out row.
+//   warps 6-9   split each V block into V_hi / V_lo and transpose it into the K-major layout the MMA reads (two
+//               buffers, so the next block's split overlaps this block's MMAs).
 // Every mbarrier wait is bounded (~2 s of %globaltimer): on timeout the CTA records kErrTimeout, drains its own
 // copies and MMAs, frees TMEM and returns.  No cluster multicast (loads read this GPU's memory only).
 #include <cuda.h>
@@ -53,19 +56,18 @@ constexpr int BOX = 8192;      // one TMA box: 64 x 64 f16 or 32 x 64 f32
 constexpr int Q_BYTES = AT_ROWS * AT_D * 2;   // 32 KB
 constexpr int K_BYTES = AT_D * AT_BN * 2;     // 16 KB per stage
 constexpr int V_BYTES = AT_BN * AT_D * 4;     // 32 KB
-constexpr int P_BYTES = AT_ROWS * AT_BN * 4;  // 32 KB per part
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + Q_BYTES;        // 2 stages
 constexpr int OFF_VRAW = OFF_K + 2 * K_BYTES;
-constexpr int OFF_VHI = OFF_VRAW + V_BYTES;
-constexpr int OFF_VLO = OFF_VHI + V_BYTES;
-constexpr int OFF_PHI = OFF_VLO + V_BYTES;
-constexpr int OFF_PLO = OFF_PHI + P_BYTES;
-constexpr int OFF_BAR = OFF_PLO + P_BYTES;    // 224 KB
+constexpr int OFF_VSP = OFF_VRAW + V_BYTES;   // 2 buffers of [V_hi^T | V_lo^T]
+constexpr int VSP_BYTES = 2 * V_BYTES;
+constexpr int OFF_BAR = OFF_VSP + 2 * VSP_BYTES;  // 224 KB
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers / flags + 1024-byte alignment slack
 static_assert(SMEM_BYTES <= 232448, "attention tile exceeds the 227 KB of shared memory per CTA");
-constexpr uint32_t TMEM_COLS = 256;
+// TMEM columns: S double buffer 0-127, O 128-255, P double buffer 256-511 ([P_hi | P_lo] of 64 columns each)
+constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TMEM_O = 128;
+constexpr uint32_t TMEM_P = 256;
 constexpr float kRescaleLog2 = 8.f;  // a row's reference max moves when its max grows by more than this
 
 // Instruction descriptor, kind::tf32: D f32 [4,6)=1, A tf32 [7,10)=2, B tf32 [10,13)=2, A and B K-major
@@ -76,12 +78,14 @@ constexpr uint32_t idesc_tf32(int m, int n) {
            (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+// D (TMEM) += A (TMEM: row i in lane i, k in consecutive columns) x B (shared memory, descriptor), kind::tf32.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t accum) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
         : "memory");
 }
 
@@ -114,16 +118,16 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint64_t* k_empty = bars + 3;     // [2]
     uint64_t* vraw_full = bars + 5;   // TMA landed the V block
     uint64_t* vraw_empty = bars + 6;  // the splitters read it
-    uint64_t* vsp_full = bars + 7;    // V_hi / V_lo written
-    uint64_t* vsp_empty = bars + 8;   // the MMAs read them
-    uint64_t* s_full = bars + 9;      // [2]
-    uint64_t* s_empty = bars + 11;    // [2]
-    uint64_t* p_full = bars + 13;
-    uint64_t* p_empty = bars + 14;
-    uint64_t* o_full = bars + 15;
-    uint64_t* drain = bars + 16;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+    uint64_t* vsp_full = bars + 7;    // [2] V_hi / V_lo written
+    uint64_t* vsp_empty = bars + 9;   // [2] the MMAs read them
+    uint64_t* s_full = bars + 11;     // [2]
+    uint64_t* s_empty = bars + 13;    // [2]
+    uint64_t* p_full = bars + 15;     // [2] P written to TMEM
+    uint64_t* p_empty = bars + 17;    // [2] the MMAs read it (and O holds that block's contribution)
+    uint64_t* o_full = bars + 19;
+    uint64_t* drain = bars + 20;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 21);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -139,13 +143,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             mbar_init(smem_u32(&k_empty[s]), 1);
             mbar_init(smem_u32(&s_full[s]), 1);
             mbar_init(smem_u32(&s_empty[s]), 128);
+            mbar_init(smem_u32(&vsp_full[s]), 128);
+            mbar_init(smem_u32(&vsp_empty[s]), 1);
+            mbar_init(smem_u32(&p_full[s]), 128);
+            mbar_init(smem_u32(&p_empty[s]), 1);
         }
         mbar_init(smem_u32(vraw_full), 1);
         mbar_init(smem_u32(vraw_empty), 128);
-        mbar_init(smem_u32(vsp_full), 128);
-        mbar_init(smem_u32(vsp_empty), 1);
-        mbar_init(smem_u32(p_full), 128);
-        mbar_init(smem_u32(p_empty), 1);
         mbar_init(smem_u32(o_full), 1);
         mbar_init(smem_u32(drain), 1);
         *abort_flag = 0;
@@ -165,8 +169,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t sQ = smem_u32(smem + OFF_Q), sK = smem_u32(smem + OFF_K), sVraw = smem_u32(smem + OFF_VRAW);
-    const uint32_t sVhi = smem_u32(smem + OFF_VHI), sVlo = smem_u32(smem + OFF_VLO);
-    const uint32_t sPhi = smem_u32(smem + OFF_PHI), sPlo = smem_u32(smem + OFF_PLO);
+    const uint32_t sVsp = smem_u32(smem + OFF_VSP);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -214,22 +217,24 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             constexpr uint32_t idesc_o = idesc_tf32(AT_ROWS, AT_D);     // M = N = 128
             bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, args.err);
             bool issued = false;
-            auto pv = [&](int i) -> bool {  // O += P_i . V_i as P_hi.V_hi + P_hi.V_lo + P_lo.V_hi
-                if (!mbar_wait(smem_u32(p_full), i & 1, abort_flag, args.err)) return false;
-                if (!mbar_wait(smem_u32(vsp_full), i & 1, abort_flag, args.err)) return false;
+            auto pv = [&](int i) -> bool {  // O += P_i . V_i as P_lo.V_hi + P_hi.V_lo + P_hi.V_hi
+                const int b = i & 1;
+                const uint32_t ph = (i >> 1) & 1;
+                if (!mbar_wait(smem_u32(&p_full[b]), ph, abort_flag, args.err)) return false;
+                if (!mbar_wait(smem_u32(&vsp_full[b]), ph, abort_flag, args.err)) return false;
                 tc_fence_after();
-                const uint32_t pa[3] = {sPlo, sPhi, sPhi}, vb[3] = {sVhi, sVlo, sVhi};  // small terms first
+                const uint32_t p_hi = tmem_base + TMEM_P + static_cast<uint32_t>(b * 2 * AT_BN);
+                const uint32_t v_hi = sVsp + b * VSP_BYTES;
+                const uint32_t pa[3] = {p_hi + AT_BN, p_hi, p_hi}, vb[3] = {v_hi, v_hi + V_BYTES, v_hi};
                 for (int t = 0; t < 3; ++t)
 #pragma unroll
                     for (int k8 = 0; k8 < AT_BN / 8; ++k8) {
-                        // A: K-major f32 rows of 32 keys (128 B) per 16 KB chunk; 8 keys = 32 B per step
-                        const uint64_t a = smem_desc(pa[t] + (k8 >> 2) * 16384 + (k8 & 3) * 32, 16, 1024);
-                        // B: V^T, K-major like A (rows = head dims)
-                        const uint64_t b = smem_desc(vb[t] + (k8 >> 2) * 16384 + (k8 & 3) * 32, 16, 1024);
-                        mma_tf32(tmem_base + TMEM_O, a, b, idesc_o, (i > 0 || t > 0 || k8 > 0) ? 1u : 0u);
+                        // A: P in TMEM, 8 keys = 8 columns per step; B: V^T K-major, 32 keys (128 B) per 16 KB chunk
+                        const uint64_t bd = smem_desc(vb[t] + (k8 >> 2) * 16384 + (k8 & 3) * 32, 16, 1024);
+                        mma_tf32_ts(tmem_base + TMEM_O, pa[t] + k8 * 8, bd, idesc_o, (i > 0 || t > 0 || k8 > 0) ? 1u : 0u);
                     }
-                mma_commit(smem_u32(vsp_empty));
-                mma_commit(smem_u32(p_empty));
+                mma_commit(smem_u32(&vsp_empty[b]));
+                mma_commit(smem_u32(&p_empty[b]));
                 return true;
             };
             for (int j = 0; ok && j < nb; ++j) {
@@ -271,11 +276,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         // reads along the dims, a register transpose, four 16-byte writes along the keys, per part.
         const int t = threadIdx.x - 6 * 32;  // 0..127
         const uint8_t* raw = smem + OFF_VRAW;
-        uint8_t* hi = smem + OFF_VHI;
-        uint8_t* lo = smem + OFF_VLO;
         for (int j = 0; j < nb; ++j) {
+            const int b = j & 1;
+            uint8_t* hi = smem + OFF_VSP + b * VSP_BYTES;
+            uint8_t* lo = hi + V_BYTES;
             if (!mbar_wait(smem_u32(vraw_full), j & 1, abort_flag, args.err)) break;
-            if (j >= 1 && !mbar_wait(smem_u32(vsp_empty), (j - 1) & 1, abort_flag, args.err)) break;
+            if (j >= 2 && !mbar_wait(smem_u32(&vsp_empty[b]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
 #pragma unroll 1
             for (int blk = t; blk < (AT_BN / 4) * (AT_D / 4); blk += 128) {
                 const int kq = blk % (AT_BN / 4), dq = blk / (AT_BN / 4);  // keys 4kq.., dims 4dq..
@@ -307,7 +313,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             }
             mbar_arrive(smem_u32(vraw_empty));
             fence_proxy_async_smem();  // V_hi / V_lo become visible to the tensor core's reads
-            mbar_arrive(smem_u32(vsp_full));
+            mbar_arrive(smem_u32(&vsp_full[b]));
         }
     } else {
         // ---------------- softmax + epilogue (warps 2..5, one row per thread) ----------------
@@ -320,8 +326,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         const float c2 = scale * 1.4426950408889634f;  // into the base-2 domain
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
-        uint8_t* phi_row = smem + OFF_PHI + row * 128;  // 128-byte rows, 8-row swizzle atoms of 1 KB
-        uint8_t* plo_row = smem + OFF_PLO + row * 128;
         for (int j = 0; j < nb; ++j) {
             const int st = j & 1;
             if (!mbar_wait(smem_u32(&s_full[st]), (j >> 1) & 1, abort_flag, args.err)) {
@@ -348,12 +352,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 corr = j == 0 ? 1.f : exp2f(m_ref - m_new);
                 m_ref = m_new;
             }
-            // P_{j-1} has been read and O updated by its MMAs before P_j overwrites the buffers (and O is rescaled)
-            if (j > 0 && !mbar_wait(smem_u32(p_empty), (j - 1) & 1, abort_flag, args.err)) {
+            const int b = j & 1;
+            // P_{j-2} has been read before P_j overwrites its TMEM buffer
+            if (j >= 2 && !mbar_wait(smem_u32(&p_empty[b]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) {
                 ok = false;
                 break;
             }
             if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                // O holds block j-1's contribution (its MMAs are done) before it is rescaled
+                if (!mbar_wait(smem_u32(&p_empty[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort_flag, args.err)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
 #pragma unroll 1
                 for (int c = 0; c < AT_D / 32; ++c) {
@@ -368,35 +378,31 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 tmem_wait_st();
             }
             l *= corr;
-            // pass 2: p = 2^(x - max) in f32 for the sum, as P_hi + P_lo into the P tiles
+            // pass 2: p = 2^(x - max) in f32 for the sum, as P_hi + P_lo into this row's TMEM lane
             float sum = 0.f;
+            const uint32_t p_addr = tmem_base + lane_addr + TMEM_P + static_cast<uint32_t>(b * 2 * AT_BN);
 #pragma unroll 1
-            for (int c = 0; c < AT_BN / 32; ++c) {  // 32 keys = one 128-byte row of a 16 KB chunk
-                uint32_t r[32];
+            for (int c = 0; c < AT_BN / 32; ++c) {
+                uint32_t r[32], h[32];
                 tmem_ld32_async(s_addr + c * 32, r);
                 tmem_wait_ld();
                 reg_fence(r);
 #pragma unroll
-                for (int g = 0; g < 8; ++g) {  // 4 keys = one 16-byte unit of the row
-                    float p[4], h[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        p[e] = exp2f(__uint_as_float(r[4 * g + e]) * c2 - m_ref);
-                        sum += p[e];
-                        h[e] = tf32_hi(p[e]);
-                    }
-                    // K-major, 128-byte swizzle: unit g of the row at g ^ (row % 8)
-                    const int off = c * 16384 + ((g ^ (row & 7)) << 4);
-                    *reinterpret_cast<float4*>(phi_row + off) = make_float4(h[0], h[1], h[2], h[3]);
-                    *reinterpret_cast<float4*>(plo_row + off) =
-                        make_float4(p[0] - h[0], p[1] - h[1], p[2] - h[2], p[3] - h[3]);
+                for (int i = 0; i < 32; ++i) {
+                    const float p = exp2f(__uint_as_float(r[i]) * c2 - m_ref);
+                    sum += p;
+                    const float hv = tf32_hi(p);
+                    h[i] = __float_as_uint(hv);
+                    r[i] = __float_as_uint(p - hv);
                 }
+                tmem_st32(p_addr + c * 32, h);
+                tmem_st32(p_addr + AT_BN + c * 32, r);
             }
+            tmem_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&s_empty[st]));  // S_j has been read: its TMEM buffer may take S_{j+2}
             l += sum;
-            fence_proxy_async_smem();  // the P writes become visible to the tensor core's reads
-            mbar_arrive(smem_u32(p_full));
+            mbar_arrive(smem_u32(&p_full[b]));
         }
         if (ok && mbar_wait(smem_u32(o_full), 0, abort_flag, args.err)) {
             tc_fence_after();
