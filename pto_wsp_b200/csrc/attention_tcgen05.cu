@@ -22,15 +22,16 @@
 //
 // One CTA per task, 10 warps:
 //   warp 0      TMA producer: Q once (two 128 x 64 K-major f16 boxes), per key block a K^T block (two 64 x 64
-//               MN-major f16 boxes, two stages) and a V block (four 32 x 64 MN-major f32 boxes), 128-byte swizzle.
+//               MN-major f16 boxes, four stages), 128-byte swizzle.
 //   warp 1      owns TMEM (S double buffer: columns 0-127; O: 128-255; P double buffer: 256-511) and issues the
 //               MMAs from one thread, S_{j+1} before O += W_j.V_j so that the tensor pipe works while the softmax
 //               runs.
 //   warps 2-5   softmax and epilogue, one row per thread (warp w reads TMEM lanes 32 (w % 4) ..): tcgen05.ld of
 //               the S row (twice: max, then exponentials), P_hi / P_lo stored into the row's TMEM lane with
 //               tcgen05.st; at the end O / sum stored to the out row.
-//   warps 6-9   split each V block into V_hi / V_lo and transpose it into the K-major layout the MMA reads (two
-//               buffers, so the next block's split overlaps this block's MMAs).
+//   warps 6-9   read each V block from global memory (the next one's loads in flight), split it into V_hi / V_lo
+//               and write it transposed into the K-major layout the MMA reads (two buffers, so the next block's
+//               split overlaps this block's MMAs).
 // Every mbarrier wait is bounded (~2 s of %globaltimer): on timeout the CTA records kErrTimeout, drains its own
 // copies and MMAs, frees TMEM and returns.  No cluster multicast (loads read this GPU's memory only).
 #include <cuda.h>
@@ -57,9 +58,9 @@ constexpr int Q_BYTES = AT_ROWS * AT_D * 2;   // 32 KB
 constexpr int K_BYTES = AT_D * AT_BN * 2;     // 16 KB per stage
 constexpr int V_BYTES = AT_BN * AT_D * 4;     // 32 KB
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + Q_BYTES;        // 2 stages
-constexpr int OFF_VRAW = OFF_K + 2 * K_BYTES;
-constexpr int OFF_VSP = OFF_VRAW + V_BYTES;   // 2 buffers of [V_hi^T | V_lo^T]
+constexpr int OFF_K = OFF_Q + Q_BYTES;
+constexpr int KST = 4;                        // K^T stages
+constexpr int OFF_VSP = OFF_K + KST * K_BYTES;  // 2 buffers of [V_hi^T | V_lo^T]
 constexpr int VSP_BYTES = 2 * V_BYTES;
 constexpr int OFF_BAR = OFF_VSP + 2 * VSP_BYTES;  // 224 KB
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers / flags + 1024-byte alignment slack
@@ -98,6 +99,7 @@ struct AttnArgs {
     int stride;
     int q_p, kt_p, v_p, o_p;      // tensor param positions in the records
     int64_t q_pitch, kt_pitch, v_pitch;
+    const float* v;               // V base (the splitters read it directly)
     float* out;
     int64_t o_pitch;
     int nblocks;                  // L / 64
@@ -109,25 +111,23 @@ struct AttnArgs {
 
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attention_tcgen05_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mkt,
-                             const __grid_constant__ CUtensorMap mv, AttnArgs args) {
+                             AttnArgs args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;      // [2]
-    uint64_t* k_empty = bars + 3;     // [2]
-    uint64_t* vraw_full = bars + 5;   // TMA landed the V block
-    uint64_t* vraw_empty = bars + 6;  // the splitters read it
-    uint64_t* vsp_full = bars + 7;    // [2] V_hi / V_lo written
-    uint64_t* vsp_empty = bars + 9;   // [2] the MMAs read them
-    uint64_t* s_full = bars + 11;     // [2]
-    uint64_t* s_empty = bars + 13;    // [2]
-    uint64_t* p_full = bars + 15;     // [2] P written to TMEM
-    uint64_t* p_empty = bars + 17;    // [2] the MMAs read it (and O holds that block's contribution)
-    uint64_t* o_full = bars + 19;
-    uint64_t* drain = bars + 20;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 21);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+    uint64_t* k_full = bars + 1;      // [KST]
+    uint64_t* k_empty = bars + 5;     // [KST]
+    uint64_t* vsp_full = bars + 9;    // [2] V_hi / V_lo written
+    uint64_t* vsp_empty = bars + 11;  // [2] the MMAs read them
+    uint64_t* s_full = bars + 13;     // [2]
+    uint64_t* s_empty = bars + 15;    // [2]
+    uint64_t* p_full = bars + 17;     // [2] P written to TMEM
+    uint64_t* p_empty = bars + 19;    // [2] the MMAs read it (and O holds that block's contribution)
+    uint64_t* o_full = bars + 21;
+    uint64_t* drain = bars + 22;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 23);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -138,9 +138,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(q_full), 1);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < KST; ++s) {
             mbar_init(smem_u32(&k_full[s]), 1);
             mbar_init(smem_u32(&k_empty[s]), 1);
+        }
+        for (int s = 0; s < 2; ++s) {
             mbar_init(smem_u32(&s_full[s]), 1);
             mbar_init(smem_u32(&s_empty[s]), 128);
             mbar_init(smem_u32(&vsp_full[s]), 128);
@@ -148,15 +150,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             mbar_init(smem_u32(&p_full[s]), 128);
             mbar_init(smem_u32(&p_empty[s]), 1);
         }
-        mbar_init(smem_u32(vraw_full), 1);
-        mbar_init(smem_u32(vraw_empty), 128);
         mbar_init(smem_u32(o_full), 1);
         mbar_init(smem_u32(drain), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mq)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mkt)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mv)) : "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -168,35 +167,30 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t sQ = smem_u32(smem + OFF_Q), sK = smem_u32(smem + OFF_K), sVraw = smem_u32(smem + OFF_VRAW);
+    const uint32_t sQ = smem_u32(smem + OFF_Q), sK = smem_u32(smem + OFF_K);
     const uint32_t sVsp = smem_u32(smem + OFF_VSP);
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
-            const int64_t oq = rec[args.q_p], okt = rec[args.kt_p], ov = rec[args.v_p];
+            const int64_t oq = rec[args.q_p], okt = rec[args.kt_p];
             const int32_t qx = static_cast<int32_t>(oq % args.q_pitch), qy = static_cast<int32_t>(oq / args.q_pitch);
             const int32_t kx = static_cast<int32_t>(okt % args.kt_pitch), ky = static_cast<int32_t>(okt / args.kt_pitch);
-            const int32_t vx = static_cast<int32_t>(ov % args.v_pitch), vy = static_cast<int32_t>(ov / args.v_pitch);
             mbar_expect_tx(smem_u32(q_full), Q_BYTES);
             tma_load_2d(sQ, &mq, qx, qy, smem_u32(q_full));
             tma_load_2d(sQ + 16384, &mq, qx + 64, qy, smem_u32(q_full));
-            int last_k[2] = {-1, -1}, last_v = -1;  // the block last loaded into each buffer
+            int last_k[KST];  // the block last loaded into each stage
+            for (int st = 0; st < KST; ++st) last_k[st] = -1;
             for (int j = 0; j < nb && !*abort_flag; ++j) {
-                const int st = j & 1;
-                if (j >= 2 && !mbar_wait(smem_u32(&k_empty[st]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
+                const int st = j % KST;
+                if (j >= KST && !mbar_wait(smem_u32(&k_empty[st]), ((j / KST) & 1) ^ 1u, abort_flag, args.err)) break;
                 mbar_expect_tx(smem_u32(&k_full[st]), K_BYTES);
                 for (int kc = 0; kc < 2; ++kc)  // head-dim rows of K^T, 64 keys per box
                     tma_load_2d(sK + st * K_BYTES + kc * BOX, &mkt, kx + j * AT_BN, ky + kc * 64, smem_u32(&k_full[st]));
                 last_k[st] = j;
-                if (j >= 1 && !mbar_wait(smem_u32(vraw_empty), (j - 1) & 1, abort_flag, args.err)) break;
-                mbar_expect_tx(smem_u32(vraw_full), V_BYTES);
-                for (int nc = 0; nc < 4; ++nc)  // 32 head dims per box, 64 keys
-                    tma_load_2d(sVraw + nc * BOX, &mv, vx + nc * 32, vy + j * AT_BN, smem_u32(vraw_full));
-                last_v = j;
             }
-            // drain: every copy issued has landed before shared memory goes away (block j completes phase j / 2
-            // of its K stage and phase j of the V barrier)
+            // drain: every copy issued has landed before shared memory goes away (block j completes phase
+            // j / KST of its stage's barrier)
             const uint64_t start = globaltimer();
             auto settle = [&](uint32_t bar, uint32_t parity) {
                 while (!mbar_try_wait(bar, parity))
@@ -206,9 +200,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     }
             };
             settle(smem_u32(q_full), 0);
-            for (int st = 0; st < 2; ++st)
-                if (last_k[st] >= 0) settle(smem_u32(&k_full[st]), (last_k[st] >> 1) & 1);
-            if (last_v >= 0) settle(smem_u32(vraw_full), last_v & 1);
+            for (int st = 0; st < KST; ++st)
+                if (last_k[st] >= 0) settle(smem_u32(&k_full[st]), (last_k[st] / KST) & 1);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -238,19 +231,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 return true;
             };
             for (int j = 0; ok && j < nb; ++j) {
-                const int st = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(smem_u32(&k_full[st]), ph, abort_flag, args.err)) break;
-                if (j >= 2 && !mbar_wait(smem_u32(&s_empty[st]), ph ^ 1u, abort_flag, args.err)) break;
+                const int st = j & 1, kst = j % KST;
+                if (!mbar_wait(smem_u32(&k_full[kst]), (j / KST) & 1, abort_flag, args.err)) break;
+                if (j >= 2 && !mbar_wait(smem_u32(&s_empty[st]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < AT_D / 16; ++kk) {  // S_j = Q . K^T_j over the head dims
                     const uint64_t a = smem_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-                    const uint64_t b = smem_desc(sK + st * K_BYTES + (kk >> 2) * BOX + (kk & 3) * 2048, BOX, 1024);
+                    const uint64_t b = smem_desc(sK + kst * K_BYTES + (kk >> 2) * BOX + (kk & 3) * 2048, BOX, 1024);
                     mma_f16(tmem_base + static_cast<uint32_t>(st * AT_BN), a, b, idesc_s, kk > 0 ? 1u : 0u);
                 }
                 issued = true;
-                mma_commit(smem_u32(&k_empty[st]));
+                mma_commit(smem_u32(&k_empty[kst]));
                 mma_commit(smem_u32(&s_full[st]));
                 if (j >= 1 && !pv(j - 1)) {
                     ok = false;
@@ -270,50 +262,53 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
     } else if (warp >= 6) {
         // ---------------- V splitters (warps 6..9) ----------------
-        // The TMA lands V as [64 keys][128 dims] (four 32-dim chunks of 8 KB, 128-byte rows, 16-byte unit u of key
-        // row k at u ^ (k % 8)); the MMA reads V^T K-major: [128 dims][64 keys] as two 32-key chunks of 16 KB,
-        // unit u of dim row n at u ^ (n % 8).  Each thread moves 4 x 4 blocks (4 keys x 4 dims): four 16-byte
-        // reads along the dims, a register transpose, four 16-byte writes along the keys, per part.
+        // Each V block [64 keys][128 dims] f32 is read straight from global memory (a warp reads whole 512-byte
+        // key rows: lane l the 16 bytes of dims 4l..4l+3), split into V_hi / V_lo and written transposed into the
+        // K-major layout the MMA reads: [128 dims][64 keys] as two 32-key chunks of 16 KB, 16-byte unit u of dim row
+        // n at u ^ (n % 8).  The next block's loads are in flight while this block is written.
         const int t = threadIdx.x - 6 * 32;  // 0..127
-        const uint8_t* raw = smem + OFF_VRAW;
-        for (int j = 0; j < nb; ++j) {
-            const int b = j & 1;
-            uint8_t* hi = smem + OFF_VSP + b * VSP_BYTES;
-            uint8_t* lo = hi + V_BYTES;
-            if (!mbar_wait(smem_u32(vraw_full), j & 1, abort_flag, args.err)) break;
-            if (j >= 2 && !mbar_wait(smem_u32(&vsp_empty[b]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
-#pragma unroll 1
-            for (int blk = t; blk < (AT_BN / 4) * (AT_D / 4); blk += 128) {
-                const int kq = blk % (AT_BN / 4), dq = blk / (AT_BN / 4);  // keys 4kq.., dims 4dq..
-                float x[4][4];                                             // [key][dim]
+        const int dq = t & 31, kg = t >> 5;  // dims 4dq..4dq+3; key quads kg, kg + 4, kg + 8, kg + 12
+        const float* vbase = args.v + rec[args.v_p];
+        auto load = [&](int j, float4 (&x)[16]) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
 #pragma unroll
                 for (int a = 0; a < 4; ++a) {
-                    const int k = 4 * kq + a;
-                    const int u = dq & 7;  // 16-byte unit of the dims inside their 32-dim chunk
-                    const float4 v = *reinterpret_cast<const float4*>(raw + (dq >> 3) * BOX + k * 128 + ((u ^ (k & 7)) << 4));
-                    x[a][0] = v.x;
-                    x[a][1] = v.y;
-                    x[a][2] = v.z;
-                    x[a][3] = v.w;
+                    const int k = j * AT_BN + 4 * (kg + 4 * i) + a;
+                    x[4 * i + a] = __ldg(reinterpret_cast<const float4*>(vbase + static_cast<int64_t>(k) * args.v_pitch) + dq);
                 }
+        };
+        float4 cur[16], nxt[16];
+        if (nb > 0) load(0, cur);
+        for (int j = 0; j < nb; ++j) {
+            const int b = j & 1;
+            if (j + 1 < nb) load(j + 1, nxt);
+            uint8_t* hi = smem + OFF_VSP + b * VSP_BYTES;
+            uint8_t* lo = hi + V_BYTES;
+            if (j >= 2 && !mbar_wait(smem_u32(&vsp_empty[b]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int n = 4 * dq + b;
-                    const int u = kq & 7;  // 16-byte unit of the keys inside their 32-key chunk
-                    const int off = (kq >> 3) * 16384 + n * 128 + ((u ^ (n & 7)) << 4);
+            for (int i = 0; i < 4; ++i) {
+                const int kq = kg + 4 * i;  // keys 4kq..4kq+3 of the block
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {  // dim n = 4dq + c
+                    const int n = 4 * dq + c;
+                    const int off = (kq >> 3) * 16384 + n * 128 + (((kq & 7) ^ (n & 7)) << 4);
                     float h[4], l[4];
 #pragma unroll
                     for (int a = 0; a < 4; ++a) {
-                        h[a] = tf32_hi(x[a][b]);
-                        l[a] = x[a][b] - h[a];
+                        const float4 v = cur[4 * i + a];
+                        const float x = c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
+                        h[a] = tf32_hi(x);
+                        l[a] = x - h[a];
                     }
                     *reinterpret_cast<float4*>(hi + off) = make_float4(h[0], h[1], h[2], h[3]);
                     *reinterpret_cast<float4*>(lo + off) = make_float4(l[0], l[1], l[2], l[3]);
                 }
             }
-            mbar_arrive(smem_u32(vraw_empty));
             fence_proxy_async_smem();  // V_hi / V_lo become visible to the tensor core's reads
             mbar_arrive(smem_u32(&vsp_full[b]));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
         }
     } else {
         // ---------------- softmax + epilogue (warps 2..5, one row per thread) ----------------
@@ -457,10 +452,9 @@ cudaError_t launch_attention(const TaskBatch& b, int q_p, int kt_p, int v_p, int
     if (b.ntasks <= 0) return cudaSuccess;
     if (b.ntasks > 0x7fffffff) return cudaErrorInvalidValue;
     const ParamDesc &Q = b.p[q_p], &KT = b.p[kt_p], &V = b.p[v_p], &O = b.p[o_p];
-    CUtensorMap mq, mkt, mv;
+    CUtensorMap mq, mkt;
     if (!make_map_f16(&mq, Q.base, Q.s3, (Q.numel_span + Q.s3 - 1) / Q.s3, 64, AT_ROWS)) return cudaErrorInvalidValue;
     if (!make_map_f16(&mkt, KT.base, KT.s3, (KT.numel_span + KT.s3 - 1) / KT.s3, 64, 64)) return cudaErrorInvalidValue;
-    if (!make_map_f32(&mv, V.base, V.s3, (V.numel_span + V.s3 - 1) / V.s3, 32, 64)) return cudaErrorInvalidValue;
     AttnArgs a;
     a.rec = b.rec;
     a.ntasks = b.ntasks;
@@ -472,6 +466,7 @@ cudaError_t launch_attention(const TaskBatch& b, int q_p, int kt_p, int v_p, int
     a.q_pitch = Q.s3;
     a.kt_pitch = KT.s3;
     a.v_pitch = V.s3;
+    a.v = reinterpret_cast<const float*>(V.base);
     a.out = reinterpret_cast<float*>(O.base);
     a.o_pitch = O.s3;
     a.nblocks = L / AT_BN;
@@ -482,7 +477,7 @@ cudaError_t launch_attention(const TaskBatch& b, int q_p, int kt_p, int v_p, int
     cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attention_tcgen05_kernel<<<static_cast<unsigned>(b.ntasks), AT_THREADS, SMEM_BYTES, s>>>(mq, mkt, mv, a);
+    attention_tcgen05_kernel<<<static_cast<unsigned>(b.ntasks), AT_THREADS, SMEM_BYTES, s>>>(mq, mkt, a);
     return cudaGetLastError();
 }
 
