@@ -27,7 +27,7 @@
 //               MMAs from one thread, S_{j+1} before O += W_j.V_j so that the tensor pipe works while the softmax
 //               runs.
 //   warps 2-5   softmax and epilogue, one row per thread (warp w reads TMEM lanes 32 (w % 4) ..): tcgen05.ld of
-//               the S row (twice: max, then exponentials), P_hi / P_lo stored into the row's TMEM lane with
+//               the S row into registers, max, exponentials, P_hi / P_lo stored into the row's TMEM lane with
 //               tcgen05.st; at the end O / sum stored to the out row.
 //   warps 6-9   read each V block from global memory (the next one's loads in flight), split it into V_hi / V_lo
 //               and write it transposed into the K-major layout the MMA reads (two buffers, so the next block's
@@ -262,19 +262,24 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
     } else if (warp >= 6) {
         // ---------------- V splitters (warps 6..9) ----------------
-        // Each V block [64 keys][128 dims] f32 is read straight from global memory (a warp reads whole 512-byte
-        // key rows: lane l the 16 bytes of dims 4l..4l+3), split into V_hi / V_lo and written transposed into the
+        // Each V block [64 keys][128 dims] f32 is read straight from global memory (lane l of a warp reads the 16
+        // bytes of dims 4l..4l+3 of its keys), split into V_hi / V_lo and written transposed into the
         // K-major layout the MMA reads: [128 dims][64 keys] as two 32-key chunks of 16 KB, 16-byte unit u of dim row
         // n at u ^ (n % 8).  The next block's loads are in flight while this block is written.
+        // A thread holds 4 keys x 4 dims per store.  Its key quads are 4i + kr, kr = (t / 32 + dq / 2) % 4 for its
+        // index t among the 128: the eight lanes of one 128-byte store phase (dq = 8p .. 8p+7) then cover the eight
+        // 16-byte bank groups (kr sets the unit's low two bits, dq % 2 its third), where one key quad per warp would
+        // put them on two.  A lane pair still reads one whole 32-byte sector of a key row per load.
         const int t = threadIdx.x - 6 * 32;  // 0..127
-        const int dq = t & 31, kg = t >> 5;  // dims 4dq..4dq+3; key quads kg, kg + 4, kg + 8, kg + 12
+        const int dq = t & 31;               // dims 4dq..4dq+3
+        const int kr = ((t >> 5) + (dq >> 1)) & 3;
         const float* vbase = args.v + rec[args.v_p];
         auto load = [&](int j, float4 (&x)[16]) {
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
                 for (int a = 0; a < 4; ++a) {
-                    const int k = j * AT_BN + 4 * (kg + 4 * i) + a;
+                    const int k = j * AT_BN + 4 * (4 * i + kr) + a;
                     x[4 * i + a] = __ldg(reinterpret_cast<const float4*>(vbase + static_cast<int64_t>(k) * args.v_pitch) + dq);
                 }
         };
@@ -288,7 +293,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             if (j >= 2 && !mbar_wait(smem_u32(&vsp_empty[b]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int kq = kg + 4 * i;  // keys 4kq..4kq+3 of the block
+                const int kq = 4 * i + kr;  // keys 4kq..4kq+3 of the block
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {  // dim n = 4dq + c
                     const int n = 4 * dq + c;
@@ -329,17 +334,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             }
             tc_fence_after();
             const uint32_t s_addr = tmem_base + lane_addr + static_cast<uint32_t>(st * AT_BN);
-            // pass 1: the row max (S_j stays in TMEM; pass 2 reads it again)
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < AT_BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32_async(s_addr + c * 32, r);
-                tmem_wait_ld();
-                reg_fence(r);
+            // the S row into registers (both 32-column loads in flight, one wait); its TMEM buffer is free then
+            uint32_t r[2][32];
+            tmem_ld32_async(s_addr, r[0]);
+            tmem_ld32_async(s_addr + 32, r[1]);
+            tmem_wait_ld();
+            reg_fence(r[0]);
+            reg_fence(r[1]);
+            tc_fence_before();
+            mbar_arrive(smem_u32(&s_empty[st]));  // S_j has been read: its TMEM buffer may take S_{j+2}
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four chains: latency, not one long one
 #pragma unroll
-                for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]) * c2);
-            }
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(r[c][i]) * c2);
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             float corr = 1.f;
             const bool grow = j == 0 || mx > m_ref + kRescaleLog2;
             if (grow) {
@@ -373,29 +382,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 tmem_wait_st();
             }
             l *= corr;
-            // pass 2: p = 2^(x - max) in f32 for the sum, as P_hi + P_lo into this row's TMEM lane
-            float sum = 0.f;
+            // p = 2^(x - max) in f32 for the sum, as P_hi + P_lo into this row's TMEM lane
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
             const uint32_t p_addr = tmem_base + lane_addr + TMEM_P + static_cast<uint32_t>(b * 2 * AT_BN);
-#pragma unroll 1
-            for (int c = 0; c < AT_BN / 32; ++c) {
-                uint32_t r[32], h[32];
-                tmem_ld32_async(s_addr + c * 32, r);
-                tmem_wait_ld();
-                reg_fence(r);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t h[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const float p = exp2f(__uint_as_float(r[i]) * c2 - m_ref);
-                    sum += p;
+                    const float p = exp2f(__uint_as_float(r[c][i]) * c2 - m_ref);
+                    sum4[i & 3] += p;
                     const float hv = tf32_hi(p);
                     h[i] = __float_as_uint(hv);
-                    r[i] = __float_as_uint(p - hv);
+                    r[c][i] = __float_as_uint(p - hv);
                 }
                 tmem_st32(p_addr + c * 32, h);
-                tmem_st32(p_addr + AT_BN + c * 32, r);
+                tmem_st32(p_addr + AT_BN + c * 32, r[c]);
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(smem_u32(&s_empty[st]));  // S_j has been read: its TMEM buffer may take S_{j+2}
+            const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
             l += sum;
             mbar_arrive(smem_u32(&p_full[b]));
         }
