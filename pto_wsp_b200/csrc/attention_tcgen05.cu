@@ -15,7 +15,7 @@
 //   * O += W_j . V_j: kind::tf32 on a three-term split, P_hi.V_hi + P_hi.V_lo + P_lo.V_hi, where x_hi is x with the
 //     low 13 mantissa bits cleared (exactly a tf32) and x_lo = x - x_hi: each product carries ~22 bits, the f32
 //     tile program's accuracy (a single tf32 pass would give the terms a 2^-11 relative error).  P is the A
-//     operand straight from TMEM (double-buffered next to S and O), V^T the B operand from shared memory.
+//     operand straight from TMEM (written over the S block it came from), V^T the B operand from shared memory.
 // Keys go in blocks of 64 with an online softmax in the base-2 domain; the running row max is kept lazily (a row's O
 // and sum are rescaled only when its max grows by more than 2^8), which changes no result beyond rounding.  The row
 // sum uses the f32 probabilities and divides O once at the end.
@@ -23,9 +23,11 @@
 // One CTA per task, 10 warps:
 //   warp 0      TMA producer: Q once (two 128 x 64 K-major f16 boxes), per key block a K^T block (two 64 x 64
 //               MN-major f16 boxes, four stages), 128-byte swizzle.
-//   warp 1      owns TMEM (S double buffer: columns 0-127; O: 128-255; P double buffer: 256-511) and issues the
-//               MMAs from one thread, S_{j+1} before O += W_j.V_j so that the tensor pipe works while the softmax
-//               runs.
+//   warp 1      owns TMEM (three S/P buffers of 128 columns: S_j in the first 64 columns of buffer j % 3, then
+//               [P_hi | P_lo] over all 128; O: columns 384-511) and issues the MMAs from one thread, S two blocks
+//               ahead: S_0 S_1 S_2 PV_0 S_3 PV_1 S_4 ...  The softmax of block j then overlaps PV_{j-1} and
+//               S_{j+2}, and never waits for an S.  S_{j+3} reuses buffer j % 3: it is issued after PV_j, and
+//               the tensor pipe runs one thread's MMAs in order, so PV_j has read P_j before S_{j+3} lands.
 //   warps 2-5   softmax and epilogue, one row per thread (warp w reads TMEM lanes 32 (w % 4) ..): tcgen05.ld of
 //               the S row into registers, max, exponentials, P_hi / P_lo stored into the row's TMEM lane with
 //               tcgen05.st; at the end O / sum stored to the out row.
@@ -65,10 +67,12 @@ constexpr int VSP_BYTES = 2 * V_BYTES;
 constexpr int OFF_BAR = OFF_VSP + 2 * VSP_BYTES;  // 224 KB
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers / flags + 1024-byte alignment slack
 static_assert(SMEM_BYTES <= 232448, "attention tile exceeds the 227 KB of shared memory per CTA");
-// TMEM columns: S double buffer 0-127, O 128-255, P double buffer 256-511 ([P_hi | P_lo] of 64 columns each)
+// TMEM columns: three S/P buffers of 128 (S_j: the first 64 columns of buffer j % 3; P_j: [P_hi | P_lo] over all
+// 128 once S_j has been read), O 384-511
+constexpr int SPB = 3;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TMEM_O = 128;
-constexpr uint32_t TMEM_P = 256;
+constexpr uint32_t TMEM_SP = 128;  // columns per S/P buffer
+constexpr uint32_t TMEM_O = 384;
 constexpr float kRescaleLog2 = 8.f;  // a row's reference max moves when its max grows by more than this
 
 // Instruction descriptor, kind::tf32: D f32 [4,6)=1, A tf32 [7,10)=2, B tf32 [10,13)=2, A and B K-major
@@ -79,14 +83,64 @@ constexpr uint32_t idesc_tf32(int m, int n) {
            (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// D (TMEM) += A (TMEM: row i in lane i, k in consecutive columns) x B (shared memory, descriptor), kind::tf32.
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+// One S block, S_j = Q . K^T_j over the 128 head dims: eight kind::f16 MMAs (M = 128, N = 64, K = 16) in one asm
+// block, so that the single issuing thread spends one add per operand per MMA.  `a` is the descriptor of Q's
+// first 16 dims (K-major, 128-byte swizzle: +32 B per 16 dims inside a 64-dim box, +16 KB per box), `b` that of
+// the K^T block's first 16 dims (MN-major: +2 KB per 16 dims, +8 KB per box); descriptor address fields count
+// 16-byte units.  The first MMA overwrites D (`accum` = 0), the rest accumulate.
+__device__ __forceinline__ void mma_s_block(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t.reg .b64 bd;\n\t"
+        ".reg .b64 ad;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.b32 q, %4, %4;\n\t"
+        "add.s64 ad, %1, 0;\n\tadd.s64 bd, %2, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, p;\n\t"
+        "add.s64 ad, %1, 2;\n\tadd.s64 bd, %2, 128;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, q;\n\t"
+        "add.s64 ad, %1, 4;\n\tadd.s64 bd, %2, 256;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, q;\n\t"
+        "add.s64 ad, %1, 6;\n\tadd.s64 bd, %2, 384;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, q;\n\t"
+        "add.s64 ad, %1, 1024;\n\tadd.s64 bd, %2, 512;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, q;\n\t"
+        "add.s64 ad, %1, 1026;\n\tadd.s64 bd, %2, 640;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, q;\n\t"
+        "add.s64 ad, %1, 1028;\n\tadd.s64 bd, %2, 768;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, q;\n\t"
+        "add.s64 ad, %1, 1030;\n\tadd.s64 bd, %2, 896;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, q;}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// One term of O += P_j . V_j over the block's 64 keys: eight kind::tf32 MMAs (M = N = 128, K = 8) with A from TMEM
+// (`a_tmem`: 8 key columns per MMA) and B = V^T from shared memory (`b`: K-major, 128-byte swizzle, +32 B per 8
+// keys, +16 KB per 32 keys).  The first MMA accumulates only if `accum` is set.
+__device__ __forceinline__ void mma_pv_term(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
                                             uint32_t accum) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, q;\n\t.reg .b64 bd;\n\t"
+        ".reg .b32 ta;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
+        "setp.eq.b32 q, %4, %4;\n\t"
+        "add.u32 ta, %1, 0;\n\tadd.s64 bd, %2, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, p;\n\t"
+        "add.u32 ta, %1, 8;\n\tadd.s64 bd, %2, 2;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
+        "add.u32 ta, %1, 16;\n\tadd.s64 bd, %2, 4;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
+        "add.u32 ta, %1, 24;\n\tadd.s64 bd, %2, 6;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
+        "add.u32 ta, %1, 32;\n\tadd.s64 bd, %2, 1024;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
+        "add.u32 ta, %1, 40;\n\tadd.s64 bd, %2, 1026;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
+        "add.u32 ta, %1, 48;\n\tadd.s64 bd, %2, 1028;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
+        "add.u32 ta, %1, 56;\n\tadd.s64 bd, %2, 1030;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
         : "memory");
 }
 
@@ -120,10 +174,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint64_t* k_empty = bars + 5;     // [KST]
     uint64_t* vsp_full = bars + 9;    // [2] V_hi / V_lo written
     uint64_t* vsp_empty = bars + 11;  // [2] the MMAs read them
-    uint64_t* s_full = bars + 13;     // [2]
-    uint64_t* s_empty = bars + 15;    // [2]
-    uint64_t* p_full = bars + 17;     // [2] P written to TMEM
-    uint64_t* p_empty = bars + 19;    // [2] the MMAs read it (and O holds that block's contribution)
+    uint64_t* s_full = bars + 13;     // [3] S_j in its buffer
+    uint64_t* p_full = bars + 16;     // [3] P_j written over it
+    uint64_t* pv_done = bars + 19;    // [2] O holds block j's contribution
     uint64_t* o_full = bars + 21;
     uint64_t* drain = bars + 22;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 23);
@@ -142,13 +195,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             mbar_init(smem_u32(&k_full[s]), 1);
             mbar_init(smem_u32(&k_empty[s]), 1);
         }
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < SPB; ++s) {
             mbar_init(smem_u32(&s_full[s]), 1);
-            mbar_init(smem_u32(&s_empty[s]), 128);
+            mbar_init(smem_u32(&p_full[s]), 128);
+        }
+        for (int s = 0; s < 2; ++s) {
             mbar_init(smem_u32(&vsp_full[s]), 128);
             mbar_init(smem_u32(&vsp_empty[s]), 1);
-            mbar_init(smem_u32(&p_full[s]), 128);
-            mbar_init(smem_u32(&p_empty[s]), 1);
+            mbar_init(smem_u32(&pv_done[s]), 1);
         }
         mbar_init(smem_u32(o_full), 1);
         mbar_init(smem_u32(drain), 1);
@@ -210,46 +264,44 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             constexpr uint32_t idesc_o = idesc_tf32(AT_ROWS, AT_D);     // M = N = 128
             bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, args.err);
             bool issued = false;
-            auto pv = [&](int i) -> bool {  // O += P_i . V_i as P_lo.V_hi + P_hi.V_lo + P_hi.V_hi
-                const int b = i & 1;
-                const uint32_t ph = (i >> 1) & 1;
-                if (!mbar_wait(smem_u32(&p_full[b]), ph, abort_flag, args.err)) return false;
-                if (!mbar_wait(smem_u32(&vsp_full[b]), ph, abort_flag, args.err)) return false;
+            // descriptors of the operands' first steps; the MMA blocks add constant offsets
+            const uint64_t q_desc = smem_desc(sQ, 16, 1024), k_desc = smem_desc(sK, BOX, 1024);
+            const uint64_t v_desc = smem_desc(sVsp, 16, 1024);
+            auto sblock = [&](int j) -> bool {  // S_j = Q . K^T_j into buffer j % 3
+                const int kst = j % KST;
+                if (!mbar_wait(smem_u32(&k_full[kst]), (j / KST) & 1, abort_flag, args.err)) return false;
                 tc_fence_after();
-                const uint32_t p_hi = tmem_base + TMEM_P + static_cast<uint32_t>(b * 2 * AT_BN);
-                const uint32_t v_hi = sVsp + b * VSP_BYTES;
-                const uint32_t pa[3] = {p_hi + AT_BN, p_hi, p_hi}, vb[3] = {v_hi, v_hi + V_BYTES, v_hi};
-                for (int t = 0; t < 3; ++t)
-#pragma unroll
-                    for (int k8 = 0; k8 < AT_BN / 8; ++k8) {
-                        // A: P in TMEM, 8 keys = 8 columns per step; B: V^T K-major, 32 keys (128 B) per 16 KB chunk
-                        const uint64_t bd = smem_desc(vb[t] + (k8 >> 2) * 16384 + (k8 & 3) * 32, 16, 1024);
-                        mma_tf32_ts(tmem_base + TMEM_O, pa[t] + k8 * 8, bd, idesc_o, (i > 0 || t > 0 || k8 > 0) ? 1u : 0u);
-                    }
-                mma_commit(smem_u32(&vsp_empty[b]));
-                mma_commit(smem_u32(&p_empty[b]));
-                return true;
-            };
-            for (int j = 0; ok && j < nb; ++j) {
-                const int st = j & 1, kst = j % KST;
-                if (!mbar_wait(smem_u32(&k_full[kst]), (j / KST) & 1, abort_flag, args.err)) break;
-                if (j >= 2 && !mbar_wait(smem_u32(&s_empty[st]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < AT_D / 16; ++kk) {  // S_j = Q . K^T_j over the head dims
-                    const uint64_t a = smem_desc(sQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-                    const uint64_t b = smem_desc(sK + kst * K_BYTES + (kk >> 2) * BOX + (kk & 3) * 2048, BOX, 1024);
-                    mma_f16(tmem_base + static_cast<uint32_t>(st * AT_BN), a, b, idesc_s, kk > 0 ? 1u : 0u);
-                }
+                mma_s_block(tmem_base + static_cast<uint32_t>((j % SPB) * TMEM_SP), q_desc,
+                            k_desc + static_cast<uint64_t>(kst * (K_BYTES >> 4)), idesc_s, 0u);
                 issued = true;
                 mma_commit(smem_u32(&k_empty[kst]));
-                mma_commit(smem_u32(&s_full[st]));
-                if (j >= 1 && !pv(j - 1)) {
-                    ok = false;
-                    break;
-                }
+                mma_commit(smem_u32(&s_full[j % SPB]));
+                return true;
+            };
+            // PV_i's inputs: P_i written over S_i, V_i split
+            auto pv_ready = [&](int i) -> bool {
+                return mbar_wait(smem_u32(&p_full[i % SPB]), (i / SPB) & 1, abort_flag, args.err) &&
+                       mbar_wait(smem_u32(&vsp_full[i & 1]), (i >> 1) & 1, abort_flag, args.err);
+            };
+            auto pv = [&](int i) {  // O += P_i . V_i as P_lo.V_hi + P_hi.V_lo + P_hi.V_hi
+                const int b = i & 1;
+                tc_fence_after();
+                const uint32_t p_hi = tmem_base + static_cast<uint32_t>((i % SPB) * TMEM_SP);
+                const uint64_t vd = v_desc + static_cast<uint64_t>(b * (VSP_BYTES >> 4));
+                mma_pv_term(tmem_base + TMEM_O, p_hi + AT_BN, vd, idesc_o, i > 0 ? 1u : 0u);  // P_lo . V_hi
+                mma_pv_term(tmem_base + TMEM_O, p_hi, vd + (V_BYTES >> 4), idesc_o, 1u);   // P_hi . V_lo
+                mma_pv_term(tmem_base + TMEM_O, p_hi, vd, idesc_o, 1u);                    // P_hi . V_hi
+                mma_commit(smem_u32(&vsp_empty[b]));
+                mma_commit(smem_u32(&pv_done[b]));
+            };
+            // issue order S_0 S_1 S_2 | PV_0 S_3 | PV_1 S_4 | ...
+            for (int j = 0; ok && j < nb && j < SPB; ++j) ok = sblock(j);
+            for (int j = 0; ok && j < nb; ++j) {
+                ok = pv_ready(j);
+                if (ok) pv(j);
+                if (ok && j + SPB < nb) ok = sblock(j + SPB);
             }
-            if (ok && !*abort_flag && pv(nb - 1)) mma_commit(smem_u32(o_full));
+            if (ok && !*abort_flag) mma_commit(smem_u32(o_full));
             if (issued) {  // drain: every MMA issued has completed before TMEM is freed
                 mma_commit(smem_u32(drain));
                 const uint64_t start = globaltimer();
@@ -327,22 +379,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nb; ++j) {
-            const int st = j & 1;
-            if (!mbar_wait(smem_u32(&s_full[st]), (j >> 1) & 1, abort_flag, args.err)) {
+            const int sb = j % SPB;
+            if (!mbar_wait(smem_u32(&s_full[sb]), (j / SPB) & 1, abort_flag, args.err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t s_addr = tmem_base + lane_addr + static_cast<uint32_t>(st * AT_BN);
-            // the S row into registers (both 32-column loads in flight, one wait); its TMEM buffer is free then
+            // the S row into registers (both 32-column loads in flight, one wait); P_j then goes over it
+            const uint32_t sp_addr = tmem_base + lane_addr + static_cast<uint32_t>(sb * TMEM_SP);
             uint32_t r[2][32];
-            tmem_ld32_async(s_addr, r[0]);
-            tmem_ld32_async(s_addr + 32, r[1]);
+            tmem_ld32_async(sp_addr, r[0]);
+            tmem_ld32_async(sp_addr + 32, r[1]);
             tmem_wait_ld();
             reg_fence(r[0]);
             reg_fence(r[1]);
-            tc_fence_before();
-            mbar_arrive(smem_u32(&s_empty[st]));  // S_j has been read: its TMEM buffer may take S_{j+2}
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four chains: latency, not one long one
 #pragma unroll
             for (int c = 0; c < 2; ++c)
@@ -356,15 +406,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 corr = j == 0 ? 1.f : exp2f(m_ref - m_new);
                 m_ref = m_new;
             }
-            const int b = j & 1;
-            // P_{j-2} has been read before P_j overwrites its TMEM buffer
-            if (j >= 2 && !mbar_wait(smem_u32(&p_empty[b]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) {
-                ok = false;
-                break;
-            }
             if (j > 0 && __any_sync(0xffffffffu, grow)) {
                 // O holds block j-1's contribution (its MMAs are done) before it is rescaled
-                if (!mbar_wait(smem_u32(&p_empty[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort_flag, args.err)) {
+                if (!mbar_wait(smem_u32(&pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort_flag, args.err)) {
                     ok = false;
                     break;
                 }
@@ -384,7 +428,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             l *= corr;
             // p = 2^(x - max) in f32 for the sum, as P_hi + P_lo into this row's TMEM lane
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-            const uint32_t p_addr = tmem_base + lane_addr + TMEM_P + static_cast<uint32_t>(b * 2 * AT_BN);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t h[32];
@@ -396,14 +439,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     h[i] = __float_as_uint(hv);
                     r[c][i] = __float_as_uint(p - hv);
                 }
-                tmem_st32(p_addr + c * 32, h);
-                tmem_st32(p_addr + AT_BN + c * 32, r[c]);
+                tmem_st32(sp_addr + c * 32, h);
+                tmem_st32(sp_addr + AT_BN + c * 32, r[c]);
             }
             tmem_wait_st();
             tc_fence_before();
             const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
             l += sum;
-            mbar_arrive(smem_u32(&p_full[b]));
+            mbar_arrive(smem_u32(&p_full[sb]));
         }
         if (ok && mbar_wait(smem_u32(o_full), 0, abort_flag, args.err)) {
             tc_fence_after();
