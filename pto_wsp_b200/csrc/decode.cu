@@ -978,6 +978,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     __shared__ uint32_t s_prefix, s_need, s_eq, s_ncand, s_nwin, s_ntie;
     const int64_t task = blockIdx.x;
     if (task >= b.ntasks) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the scores' producer has completed (dependent launch)
     const int64_t* rec = b.rec + task * b.stride;
     const ParamDesc& S = b.p[0];
     const ParamDesc& O = b.p[1];
@@ -1305,8 +1306,20 @@ cudaError_t launch_topk_select(const TaskBatch& b, int, void*, size_t, cudaStrea
     if (b.ntasks <= 0) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    topk_select_kernel<<<static_cast<unsigned>(b.ntasks), kTopkThreads, smem, s>>>(b);
-    return cudaGetLastError();
+    // Programmatic dependent launch: the grid may be scheduled while the kernel before it on the stream (the
+    // indexer's scoring, which allows it) finishes; every CTA waits for that kernel's completion and memory
+    // (griddepcontrol.wait) before it reads a score.  After any other kernel it behaves as a plain launch.
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(b.ntasks));
+    cfg.blockDim = dim3(kTopkThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, topk_select_kernel, b);
 }
 
 }  // namespace ptowsp::dev

@@ -370,6 +370,9 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
+    // a kernel launched after this one as a programmatic dependent (the top-k) may be scheduled now; it waits
+    // for this grid's completion before it reads a score
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t lead_bars = mapa_shared(smem_u32(bars), 0);  // the leader's barrier block

@@ -2616,7 +2616,8 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         }
     }
 
-    if (!pipelined) PW_CUDA(cudaEventRecord(P.ev0, P.stream));
+    // the run's GPU time (`gpu_ms`) is only read back by a synchronous run
+    if (!pipelined && !async_run) PW_CUDA(cudaEventRecord(P.ev0, P.stream));
     if (pipelined) {
         // kernels and copies were enqueued by run_pipelined
     } else if (replay) {
@@ -2639,7 +2640,7 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         W->close_wave();
         upload_and_launch(L->waves.size());
     }
-    if (!pipelined) PW_CUDA(cudaEventRecord(P.ev1, P.stream));
+    if (!pipelined && !async_run) PW_CUDA(cudaEventRecord(P.ev1, P.stream));
 
     // ---- bring written host tensors back ----
     for (size_t tid = 0; tid < T.size() && !pipelined; ++tid) {
