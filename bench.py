@@ -26,8 +26,9 @@ runs one config alone.
   ``workloads`` layout; rank 0 only.  Without the built artifacts it times the C port instead.
 
 Multi-GPU (torchrun, one rank per GPU): every rank runs its ``ShardedExecutable`` share of the ONE global config
-(strong scaling): contiguous blocks of the outer ``P(batch)`` axis for configs 1, 2, 3 and 5, greedy LPT by KV
-length for config 4.  No data-path collective: NCCL carries only the barriers and the max-over-ranks timing.
+(strong scaling): contiguous blocks of the outer ``P(batch)`` axis for configs 1, 2, 3 and 5, contiguous blocks
+balanced by KV length for config 4 (``--partition`` overrides).  No data-path collective: NCCL carries only the
+barriers and the max-over-ranks timing.
 
 Algorithmic work per step (global):
   1 RMSNorm   8 B per element (read x, write y), 64 x 4096 x 16 x 128 elements
@@ -500,7 +501,10 @@ class BgemmCase(Case):
 
 
 class DecodeCase(Case):
-    name, kernel, traffic_key, method = "decode", "paged_decode", "decode:paged_decode_tma", "lpt"
+    # contiguous shares balanced by KV length: the rank works on views of the global tensors.  (LPT balances a
+    # little better, but its non-contiguous shares cost a gather of Q / page table / lengths and a scatter of the
+    # output per step: 0.141 against 0.112 ms per step at 2 ranks.)
+    name, kernel, traffic_key, method = "decode", "paged_decode", "decode:paged_decode_tma", "balanced"
     unit, bound, dtype = "GB/s", "hbm", "f16 in / f32 softmax / f16 out"
     metric = "paged GQA decode task-loop throughput (algorithmic HBM bytes)"
     R, KVH, G, D, PS = 64, 8, 4, 128, 16
@@ -867,6 +871,8 @@ def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
     torch, dev = D.torch, D.dev
     plan = case.plan()
     darr = case.device_inputs(torch, dev)
+    if args.partition:
+        case.method = args.partition
     sh = ShardedExecutable(plan, rank=rank, world=world, device=D.local_rank, method=case.method,
                            costs=case.costs())
     units = sh.local_units(case.n_units)
@@ -1093,6 +1099,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=4.0, help="seconds of CPU work per cpu_baseline sample")
     ap.add_argument("--batch", type=int, default=None, help="override the outer batch (small profiling cases)")
+    ap.add_argument("--partition", default=None, choices=["block", "balanced", "lpt"],
+                    help="override the workloads' share method over the ranks")
     ap.add_argument("--cols", type=int, default=None, help="rmsnorm/softmax: another tile width (row-program kernel)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

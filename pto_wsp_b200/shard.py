@@ -213,24 +213,30 @@ def partition(n: int, world: int, costs: Sequence[float] | None = None, method: 
         raise ValueError(f"method {method!r} needs one cost per unit")
     c = [float(x) for x in costs]
     if method == "balanced":
-        total = sum(c)
-        out, lo, acc = [], 0, 0.0
-        for r in range(world):
-            if r == world - 1:
-                hi = n
+        # the contiguous split whose largest share is smallest: bisection on that largest share, each probe a
+        # greedy left-to-right fill, then the greedy split at the bound found
+        def fill(cap: float) -> list[int]:
+            cuts, acc = [], 0.0
+            for i, x in enumerate(c):
+                if acc + x > cap and acc > 0.0:
+                    cuts.append(i)
+                    acc = 0.0
+                acc += x
+            return cuts
+
+        lo_cap, hi_cap = max(c, default=0.0), sum(c)
+        for _ in range(60):
+            mid = (lo_cap + hi_cap) / 2
+            if len(fill(mid)) <= world - 1:
+                hi_cap = mid
             else:
-                target = total * (r + 1) / world
-                hi = lo
-                while hi < n and (acc + c[hi] <= target or hi == lo):
-                    acc += c[hi]
-                    hi += 1
-                # leave at least one unit for every later rank when there are enough units
-                hi = min(hi, n - (world - 1 - r)) if n >= world else hi
-                hi = max(hi, lo)
-                acc = sum(c[:hi])
-            out.append(list(range(lo, hi)))
-            lo = hi
-        return out
+                lo_cap = mid
+        cuts = fill(hi_cap)
+        if n >= world:  # every rank gets a unit: extra cuts split segments, which raises no share
+            taken = set(cuts)
+            cuts = sorted(cuts + [i for i in range(1, n) if i not in taken][: world - 1 - len(cuts)])
+        bounds = [0] + cuts + [n] * (world - len(cuts))
+        return [list(range(bounds[r], bounds[r + 1])) for r in range(world)]
     if method == "lpt":
         order = sorted(range(n), key=lambda i: (-c[i], i))
         load = [0.0] * world

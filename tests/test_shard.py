@@ -47,6 +47,23 @@ def test_balanced_and_lpt_partitions():
     assert bal == [[0, 1, 2], [3]]
 
 
+def test_balanced_partition_minimises_the_largest_share():
+    import itertools
+
+    rng = np.random.default_rng(5)
+    for _ in range(30):
+        n = int(rng.integers(3, 11))
+        world = int(rng.integers(2, min(n, 4) + 1))
+        costs = rng.integers(1, 100, n).tolist()
+        parts = shard.partition(n, world, costs, "balanced")
+        assert [u for p in parts for u in p] == list(range(n))  # contiguous, in order
+        assert all(parts)  # every rank has a unit (n >= world here)
+        got = max(sum(costs[u] for u in p) for p in parts)
+        best = min(max(sum(costs[a:b]) for a, b in zip((0,) + cut, cut + (n,)))
+                   for cut in itertools.combinations(range(1, n), world - 1))
+        assert got == best
+
+
 def test_analysis_of_the_config_plans():
     assert shard.analyze(workloads.rmsnorm_plan(4, 8)) == ({0, 1}, set(), {1})
     assert shard.analyze(workloads.softmax_plan(4, 8)) == ({0, 1}, set(), {1})
