@@ -896,6 +896,22 @@ __device__ __forceinline__ void bitonic_sort_store(unsigned long long* comp, int
     }
 }
 
+// The warp's 32 values sorted in descending order across the lanes (bitonic network over shuffles): lane i gets
+// the (i+1)-th largest.
+__device__ __forceinline__ uint32_t warp_sort_desc(uint32_t v, int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+        const bool desc = size == 32 || (lane & size) == 0;
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const uint32_t o = __shfl_xor_sync(0xffffffffu, v, stride);
+            const bool keep_max = ((lane & stride) == 0) == desc;
+            v = keep_max ? max(v, o) : min(v, o);
+        }
+    }
+    return v;
+}
+
 // Radix-select digit choice from 256 bin totals: the digit d (bits shift .. shift+7) with
 // count(digit > d) < need <= count(digit >= d); every thread gets back the prefix extended by d and the rank
 // still needed inside that digit, s_eq the digit's count.  Call with bin_tot complete and visible to warp 0;
@@ -975,7 +991,8 @@ __device__ __forceinline__ void topk_radix_digit(const uint32_t* hist, uint32_t*
 __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) {
     extern __shared__ __align__(16) uint8_t tsm[];
     __shared__ uint32_t bin_tot[256];
-    __shared__ uint32_t s_prefix, s_need, s_eq, s_ncand, s_nwin, s_ntie;
+    __shared__ uint32_t s_prefix, s_need, s_eq, s_ncand, s_nwin, s_ntie, s_nsmall;
+    __shared__ uint32_t s_small[32];  // the last few keys of the selection (listed path)
     const int64_t task = blockIdx.x;
     if (task >= b.ntasks) return;
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the scores' producer has completed (dependent launch)
@@ -1039,26 +1056,28 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     }
     __syncthreads();
 
-    // (2) A lower bound for the threshold from an evenly spaced sample of 1024 keys: the 16-bit bucket of the
-    // sample's r-th largest key, with r four standard deviations above the expected number of winners in the
-    // sample.  Every key at or above it is listed; when that gives between K and the list's capacity keys, the
-    // exact selection runs over the list alone.  Otherwise (a skewed row) the full-row passes below run.
+    // (2) A lower bound for the threshold from an evenly spaced sample of 1024 keys, one per thread: every warp
+    // sorts its 32 and takes its c-th largest, c = r / 32 rounded up, with r four standard deviations above the
+    // expected number of winners in the sample; the bound is the median of the 32 warps' values (about the
+    // quantile of r / 1024, where a warp's c-th largest falls below it as often as above).  Every key at or above
+    // it is listed; when that gives between K and the list's capacity keys, the exact selection runs over the
+    // list alone.  Otherwise (a skewed row) the full-row passes below run.
     bool from_cand = false;
     {
         const float expect = static_cast<float>(K) * kTopkThreads / static_cast<float>(N);
         const int r = static_cast<int>(ceilf(expect + 4.f * sqrtf(expect) + 4.f));
         if (N >= 4 * kTopkThreads && r < kTopkThreads / 4 && cand_cap >= static_cast<uint32_t>(K)) {
-            const uint32_t smp = ks[static_cast<int64_t>(threadIdx.x) * N / kTopkThreads];
-            uint32_t sp = 0, sn = static_cast<uint32_t>(r);
-            for (int pass = 0; pass < 2; ++pass) {
-                const int shift = 24 - 8 * pass;
-                const uint32_t hmask = pass == 0 ? 0u : 0xff000000u;
-                for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
-                __syncthreads();
-                if ((smp & hmask) == sp) atomicAdd(hl + ((smp >> shift) & 255u) * kHistCopies, 1u);
-                topk_radix_digit(hist, bin_tot, &s_prefix, &s_need, &s_eq, shift, sp, sn, lane, wid);
+            const int c = (r + 31) / 32;  // 1 .. 8
+            const uint32_t smp = warp_sort_desc(ks[static_cast<int64_t>(threadIdx.x) * N / kTopkThreads], lane);
+            const uint32_t wc_th = __shfl_sync(0xffffffffu, smp, c - 1);
+            if (lane == 0) bin_tot[wid] = wc_th;
+            __syncthreads();
+            if (wid == 0) {
+                const uint32_t m = warp_sort_desc(bin_tot[lane], lane);
+                if (lane == kTopkWarps / 2) s_prefix = m;  // the lower median of the warps' values
             }
-            const uint32_t lo = sp;  // lowest key of that 16-bit bucket
+            __syncthreads();
+            const uint32_t lo = s_prefix;
             // every warp lists its keys >= lo into its own segment of the list (no shared counter), then the
             // segments are packed to the front
             const unsigned below = (1u << lane) - 1u;
@@ -1115,7 +1134,33 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
     // row out: keys above the 16-bit prefix go straight to the composite buffer, keys matching it are listed for
     // pass 3 and the gather)
     uint32_t prefix = 0, need = static_cast<uint32_t>(K);
-    for (int pass = 0; pass < 4; ++pass) {
+    int first_pass = 0;
+    if (from_cand) {
+        // the leading bytes every listed key shares need no pass: each would pick that byte, `need` unchanged
+        const int nc = static_cast<int>(s_ncand);
+        uint32_t ka = 0xffffffffu, ko = 0u;
+        for (int i = threadIdx.x; i < nc; i += kTopkThreads) {
+            const uint32_t k = static_cast<uint32_t>(cand[i] >> 32);
+            ka &= k;
+            ko |= k;
+        }
+        ka = __reduce_and_sync(0xffffffffu, ka);
+        ko = __reduce_or_sync(0xffffffffu, ko);
+        if (lane == 0) {
+            bin_tot[wid] = ka;
+            bin_tot[kTopkWarps + wid] = ko;
+        }
+        __syncthreads();
+        ka = bin_tot[lane];
+        ko = bin_tot[kTopkWarps + lane];
+        ka = __reduce_and_sync(0xffffffffu, ka);
+        ko = __reduce_or_sync(0xffffffffu, ko);
+        first_pass = (ka ^ ko) == 0u ? 4 : __clz(static_cast<int>(ka ^ ko)) / 8;
+        if (first_pass > 0) prefix = ka & (0xffffffffu << (32 - 8 * first_pass));
+        if (first_pass == 4 && threadIdx.x == 0) s_eq = static_cast<uint32_t>(nc);  // one key value: all equal it
+        __syncthreads();  // the totals area is free again; s_eq set
+    }
+    for (int pass = first_pass; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
         const uint32_t hmask = pass == 0 ? 0u : (0xffffffffu << (shift + 8));
         for (int i = threadIdx.x; i < 256 * kHistCopies; i += kTopkThreads) hist[i] = 0u;
@@ -1149,6 +1194,36 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(TaskBatch b) 
             }
         }
         topk_radix_digit(hist, bin_tot, &s_prefix, &s_need, &s_eq, shift, prefix, need, lane, wid);
+        if (from_cand && pass < 3 && s_eq <= 32u) {
+            // at most 32 listed keys still match the decided prefix: list them and let one warp sort them and
+            // pick the need-th largest, instead of the remaining passes
+            const uint32_t pm = 0xffffffffu << shift;
+            const int nc = static_cast<int>(s_ncand);
+            if (threadIdx.x == 0) s_nsmall = 0u;
+            __syncthreads();
+            for (int i = threadIdx.x; i < nc; i += kTopkThreads) {
+                const uint32_t k = static_cast<uint32_t>(cand[i] >> 32);
+                if ((k & pm) == prefix) s_small[atomicAdd(&s_nsmall, 1u) & 31u] = k;
+            }
+            __syncthreads();
+            if (wid == 0) {
+                const uint32_t m = s_eq;  // == the number listed
+                const bool in = static_cast<uint32_t>(lane) < m;
+                const uint32_t v = warp_sort_desc(in ? s_small[lane] : 0u, lane);
+                const uint32_t t = __shfl_sync(0xffffffffu, v, static_cast<int>(need) - 1);
+                const unsigned gt = __ballot_sync(0xffffffffu, in && v > t), eq = __ballot_sync(0xffffffffu, in && v == t);
+                if (lane == 0) {
+                    s_prefix = t;
+                    s_need = need - static_cast<uint32_t>(__popc(gt));
+                    s_eq = static_cast<uint32_t>(__popc(eq));
+                }
+            }
+            __syncthreads();
+            prefix = s_prefix;
+            need = s_need;
+            __syncthreads();  // before the shared words are reused
+            break;
+        }
     }
     const uint32_t thr = prefix;       // the K-th largest key; `need` keys equal to it are taken
     const bool all_eq = s_eq == need;  // no tie to break: every key equal to the threshold is taken
