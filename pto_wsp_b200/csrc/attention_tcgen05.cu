@@ -12,28 +12,36 @@
 // second contraction on CUDA cores; here S and O live in TMEM and W in shared memory, and both contractions run
 // on the tensor cores:
 //   * S_j = Q . K^T_j: tcgen05.mma kind::f16 (exact f16 products, f32 accumulation);
-//   * O += W_j . V_j: kind::tf32 on a three-term split, P_hi.V_hi + P_hi.V_lo + P_lo.V_hi, where x_hi is x with the
-//     low 13 mantissa bits cleared (exactly a tf32) and x_lo = x - x_hi: each product carries ~22 bits, the f32
-//     tile program's accuracy (a single tf32 pass would give the terms a 2^-11 relative error).  P is the A
-//     operand straight from TMEM (written over the S block it came from), V^T the B operand from shared memory.
+//   * O += W_j . V_j: kind::f16 on f16 operands in a three-term split, P_hi.V_hi + P_hi.V_lo + P_lo.V_hi, where
+//     x_hi = x with its low 13 mantissa bits cleared (an exact f16) and x_lo = f16(x - x_hi): the pair carries
+//     ~22 bits of x, so every product keeps the f32 tile program's accuracy (one f16 pass would leave 2^-11
+//     relative error per term; a bf16 split, 2^-17).  f16's exponent range is narrow, so both operands are scaled by powers of two: P (at most
+//     2^8, see the lazy max below) by 2^7, and V by 2^k with k chosen from the largest |V| seen so far in the
+//     task (|V| 2^k < 2^15).  A V block that raises that maximum lowers k, and O is rescaled by the exact power
+//     of two before the block's terms accumulate; values far below the maximum lose only bits far below the
+//     result's rounding.  The twelve MMAs per block (M = N = 128, K = 16) run at the f16 tensor rate.  P is the
+//     A operand straight from TMEM (packed f16 pairs written over the S block it came from), V the B operand
+//     from shared memory in its own row-major layout (MN-major).
 // Keys go in blocks of 64 with an online softmax in the base-2 domain; the running row max is kept lazily (a row's O
 // and sum are rescaled only when its max grows by more than 2^8), which changes no result beyond rounding.  The row
-// sum uses the f32 probabilities and divides O once at the end.
+// sum uses the f32 probabilities and divides O once at the end, together with the two scales.
 //
 // One CTA per task, 10 warps:
 //   warp 0      TMA producer: Q once (two 128 x 64 K-major f16 boxes), per key block a K^T block (two 64 x 64
 //               MN-major f16 boxes, four stages), 128-byte swizzle.
 //   warp 1      owns TMEM (three S/P buffers of 128 columns: S_j in the first 64 columns of buffer j % 3, then
-//               [P_hi | P_lo] over all 128; O: columns 384-511) and issues the MMAs from one thread, S two blocks
-//               ahead: S_0 S_1 S_2 PV_0 S_3 PV_1 S_4 ...  The softmax of block j then overlaps PV_{j-1} and
+//               [P_hi | P_lo] over those 64, two f16 per column; O: columns 384-511) and issues the MMAs from
+//               one thread, S two blocks ahead: S_0 S_1 S_2 PV_0 S_3 PV_1 S_4 ...  The softmax of block j then
+//               overlaps PV_{j-1} and
 //               S_{j+2}, and never waits for an S.  S_{j+3} reuses buffer j % 3: it is issued after PV_j, and
 //               the tensor pipe runs one thread's MMAs in order, so PV_j has read P_j before S_{j+3} lands.
 //   warps 2-5   softmax and epilogue, one row per thread (warp w reads TMEM lanes 32 (w % 4) ..): tcgen05.ld of
 //               the S row into registers, max, exponentials, P_hi / P_lo stored into the row's TMEM lane with
-//               tcgen05.st; at the end O / sum stored to the out row.
-//   warps 6-9   read each V block from global memory (the next one's loads in flight), split it into V_hi / V_lo
-//               and write it transposed into the K-major layout the MMA reads (two buffers, so the next block's
-//               split overlaps this block's MMAs).
+//               tcgen05.st (and O rescaled in TMEM when the row max or V's scale moves); at the end O / sum
+//               stored to the out row.
+//   warps 6-9   read each V block from global memory (the next one's loads in flight), find its largest |V|,
+//               scale it, split it into f16 V_hi / V_lo and write both in the 128-byte-swizzled row layout the
+//               MMA reads (two buffers, so the next block's split overlaps this block's MMAs).
 // Every mbarrier wait is bounded (~2 s of %globaltimer): on timeout the CTA records kErrTimeout, drains its own
 // copies and MMAs, frees TMEM and returns.  No cluster multicast (loads read this GPU's memory only).
 #include <cuda.h>
@@ -55,33 +63,28 @@ constexpr int AT_THREADS = 320;
 constexpr int AT_ROWS = 128;   // query rows of a task
 constexpr int AT_D = 128;      // head dim
 constexpr int AT_BN = 64;      // keys per block
-constexpr int BOX = 8192;      // one TMA box: 64 x 64 f16 or 32 x 64 f32
+constexpr int BOX = 8192;      // one TMA box / one V chunk: 64 x 64 16-bit elements, 128-byte rows
 constexpr int Q_BYTES = AT_ROWS * AT_D * 2;   // 32 KB
 constexpr int K_BYTES = AT_D * AT_BN * 2;     // 16 KB per stage
-constexpr int V_BYTES = AT_BN * AT_D * 4;     // 32 KB
+constexpr int V_BYTES = AT_BN * AT_D * 2;     // 16 KB: one f16 part of a V block (two 64-dim chunks)
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + Q_BYTES;
 constexpr int KST = 4;                        // K^T stages
-constexpr int OFF_VSP = OFF_K + KST * K_BYTES;  // 2 buffers of [V_hi^T | V_lo^T]
+constexpr int NVB = 4;                        // V buffers: the splitters run up to four blocks ahead of the MMAs
+constexpr int OFF_VSP = OFF_K + KST * K_BYTES;  // NVB buffers of [V_hi | V_lo]
 constexpr int VSP_BYTES = 2 * V_BYTES;
-constexpr int OFF_BAR = OFF_VSP + 2 * VSP_BYTES;  // 224 KB
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers / flags + 1024-byte alignment slack
+constexpr int OFF_BAR = OFF_VSP + NVB * VSP_BYTES;  // 224 KB
+constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;  // + barriers / flags / V scales + 1024-byte alignment slack
 static_assert(SMEM_BYTES <= 232448, "attention tile exceeds the 227 KB of shared memory per CTA");
-// TMEM columns: three S/P buffers of 128 (S_j: the first 64 columns of buffer j % 3; P_j: [P_hi | P_lo] over all
-// 128 once S_j has been read), O 384-511
+// TMEM columns: three S/P buffers of 128 (S_j: the first 64 columns of buffer j % 3; P_j: [P_hi | P_lo] over those
+// 64 once S_j has been read, two f16 keys per column), O 384-511
 constexpr int SPB = 3;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TMEM_SP = 128;  // columns per S/P buffer
 constexpr uint32_t TMEM_O = 384;
 constexpr float kRescaleLog2 = 8.f;  // a row's reference max moves when its max grows by more than this
-
-// Instruction descriptor, kind::tf32: D f32 [4,6)=1, A tf32 [7,10)=2, B tf32 [10,13)=2, A and B K-major
-// ([15] = [16] = 0), N>>3 [17,23), M>>4 [24,29).  (An MN-major B of 32-bit elements would need the 32-byte-atom
-// variant of the 128-byte swizzle; the splitters write V transposed instead.)
-constexpr uint32_t idesc_tf32(int m, int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-           (static_cast<uint32_t>(m >> 4) << 24);
-}
+constexpr int kPScaleLog2 = 7;       // P (at most 2^8) enters the MMA as P * 2^7 (< 2^15, inside f16's range)
+constexpr int kVScaleMax = 100;      // V's scale 2^k keeps |k| <= 100 (all-zero or non-finite blocks included)
 
 // One S block, S_j = Q . K^T_j over the 128 head dims: eight kind::f16 MMAs (M = 128, N = 64, K = 16) in one asm
 // block, so that the single issuing thread spends one add per operand per MMA.  `a` is the descriptor of Q's
@@ -114,38 +117,84 @@ __device__ __forceinline__ void mma_s_block(uint32_t d_tmem, uint64_t a, uint64_
         : "memory");
 }
 
-// One term of O += P_j . V_j over the block's 64 keys: eight kind::tf32 MMAs (M = N = 128, K = 8) with A from TMEM
-// (`a_tmem`: 8 key columns per MMA) and B = V^T from shared memory (`b`: K-major, 128-byte swizzle, +32 B per 8
-// keys, +16 KB per 32 keys).  The first MMA accumulates only if `accum` is set.
-__device__ __forceinline__ void mma_pv_term(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                            uint32_t accum) {
+// O += P_j . V_j over the block's 64 keys as three terms, P_lo.V_hi + P_hi.V_lo + P_hi.V_hi, each four kind::f16
+// MMAs (M = N = 128, K = 16) on f16 operands: A from TMEM (`p_tmem`: P_hi in columns 0-31, P_lo in 32-63, two
+// keys per column, 8 columns per MMA), B from shared memory (`vh` / `vl`: the V_hi / V_lo descriptors, MN-major,
+// 128-byte swizzle, 64-dim chunks 8 KB apart, +2 KB per 16 keys).  The first MMA accumulates only if `accum` is set.
+__device__ __forceinline__ void mma_pv_block(uint32_t d_tmem, uint32_t p_tmem, uint64_t vh, uint64_t vl, uint32_t idesc,
+                                             uint32_t accum) {
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t.reg .b64 bd;\n\t"
         ".reg .b32 ta;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "setp.eq.b32 q, %4, %4;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "setp.eq.b32 q, %5, %5;\n\t"
+        "add.u32 ta, %1, 32;\n\tadd.s64 bd, %2, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, p;\n\t"
+        "add.u32 ta, %1, 40;\n\tadd.s64 bd, %2, 128;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 48;\n\tadd.s64 bd, %2, 256;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 56;\n\tadd.s64 bd, %2, 384;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 0;\n\tadd.s64 bd, %3, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 8;\n\tadd.s64 bd, %3, 128;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 16;\n\tadd.s64 bd, %3, 256;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 24;\n\tadd.s64 bd, %3, 384;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
         "add.u32 ta, %1, 0;\n\tadd.s64 bd, %2, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, p;\n\t"
-        "add.u32 ta, %1, 8;\n\tadd.s64 bd, %2, 2;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
-        "add.u32 ta, %1, 16;\n\tadd.s64 bd, %2, 4;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
-        "add.u32 ta, %1, 24;\n\tadd.s64 bd, %2, 6;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
-        "add.u32 ta, %1, 32;\n\tadd.s64 bd, %2, 1024;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
-        "add.u32 ta, %1, 40;\n\tadd.s64 bd, %2, 1026;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
-        "add.u32 ta, %1, 48;\n\tadd.s64 bd, %2, 1028;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;\n\t"
-        "add.u32 ta, %1, 56;\n\tadd.s64 bd, %2, 1030;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [ta], bd, %3, q;}"
-        ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 8;\n\tadd.s64 bd, %2, 128;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 16;\n\tadd.s64 bd, %2, 256;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;\n\t"
+        "add.u32 ta, %1, 24;\n\tadd.s64 bd, %2, 384;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], bd, %4, q;}"
+        ::"r"(d_tmem), "r"(p_tmem), "l"(vh), "l"(vl), "r"(idesc), "r"(accum)
         : "memory");
 }
 
-// x with its low 13 mantissa bits cleared: exactly a tf32 value (sign, exponent, 10 mantissa bits).
-__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+// Two f32 values rounded to f16 and packed into one 32-bit word, `lo` in the low half (the lower key / dim).
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+// x with its low 13 mantissa bits cleared: 11 significant bits, exactly an f16 value inside f16's normal range.  The
+// split x = hi + (x - hi) then needs no conversion back from f16: hi packs exactly, and x - hi (exact in f32,
+// below 2^-10 |x|) loses only bits under 2^-21 |x| when it is rounded to f16.
+__device__ __forceinline__ float f16_hi_part(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+
+// 2^x by the hardware approximation (PTX ex2.approx.ftz.f32: relative error ~2^-22, results below 2^-126 flush to
+// zero).  The probabilities it makes stay far inside the contraction's 2e-3 bar, and it is a quarter of the cost
+// of exp2f(), which dominated the softmax warps' time per key block.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 2^e as an f32 for -126 <= e <= 127 (exact; no exp2 evaluation).
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
+
+// tcgen05.st of 16 columns of this warp's 32 TMEM lanes (one register per lane and column).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// V's scale exponent for a largest |V| whose f32 bits are `mbits` (a non-negative float; NaN sorts above inf): the
+// k with |V| 2^k < 2^15, clamped to [-kVScaleMax, kVScaleMax].
+__device__ __forceinline__ int v_scale_log2(uint32_t mbits) {
+    const int be = static_cast<int>(min(mbits, 0x7f800000u) >> 23);  // |V| < 2^(be - 126)
+    return max(-kVScaleMax, min(kVScaleMax, 141 - be));
+}
 
 struct AttnArgs {
     const int64_t* rec;
@@ -172,15 +221,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint64_t* q_full = bars + 0;
     uint64_t* k_full = bars + 1;      // [KST]
     uint64_t* k_empty = bars + 5;     // [KST]
-    uint64_t* vsp_full = bars + 9;    // [2] V_hi / V_lo written
-    uint64_t* vsp_empty = bars + 11;  // [2] the MMAs read them
-    uint64_t* s_full = bars + 13;     // [3] S_j in its buffer
-    uint64_t* p_full = bars + 16;     // [3] P_j written over it
-    uint64_t* pv_done = bars + 19;    // [2] O holds block j's contribution
-    uint64_t* o_full = bars + 21;
-    uint64_t* drain = bars + 22;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 23);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+    uint64_t* vsp_full = bars + 9;    // [NVB] V_hi / V_lo written
+    uint64_t* vsp_empty = bars + 13;  // [NVB] the MMAs read them
+    uint64_t* s_full = bars + 17;     // [3] S_j in its buffer
+    uint64_t* p_full = bars + 20;     // [3] P_j written over it
+    uint64_t* pv_done = bars + 23;    // [2] O holds block j's contribution
+    uint64_t* o_full = bars + 25;
+    uint64_t* drain = bars + 26;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 27);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
+    volatile int* v_log2 = reinterpret_cast<volatile int*>(bars + 29);  // [NVB] V's scale exponent of buffer b's block
+    uint32_t* v_part = reinterpret_cast<uint32_t*>(bars + 31);           // [2][4] splitter warps' largest |V| bits
+    uint64_t* vmax_ready = bars + 35;  // [2] the four splitter warps posted their parts of a block's largest |V|
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -199,12 +251,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             mbar_init(smem_u32(&s_full[s]), 1);
             mbar_init(smem_u32(&p_full[s]), 128);
         }
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < NVB; ++s) {
             mbar_init(smem_u32(&vsp_full[s]), 128);
             mbar_init(smem_u32(&vsp_empty[s]), 1);
+        }
+        for (int s = 0; s < 2; ++s) {
             mbar_init(smem_u32(&pv_done[s]), 1);
         }
         mbar_init(smem_u32(o_full), 1);
+        for (int s = 0; s < 2; ++s) mbar_init(smem_u32(&vmax_ready[s]), 4);
         mbar_init(smem_u32(drain), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -261,12 +316,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
             constexpr uint32_t idesc_s = idesc_f16(AT_ROWS, AT_BN, 1);  // A K-major, B MN-major, M = 128, N = 64
-            constexpr uint32_t idesc_o = idesc_tf32(AT_ROWS, AT_D);     // M = N = 128
+            constexpr uint32_t idesc_o = idesc_f16(AT_ROWS, AT_D, 1);  // A from TMEM (K-major), B MN-major, M = N = 128
             bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, args.err);
             bool issued = false;
             // descriptors of the operands' first steps; the MMA blocks add constant offsets
             const uint64_t q_desc = smem_desc(sQ, 16, 1024), k_desc = smem_desc(sK, BOX, 1024);
-            const uint64_t v_desc = smem_desc(sVsp, 16, 1024);
+            const uint64_t v_desc = smem_desc(sVsp, BOX, 1024);  // MN-major: 64-dim chunks 8 KB apart
             auto sblock = [&](int j) -> bool {  // S_j = Q . K^T_j into buffer j % 3
                 const int kst = j % KST;
                 if (!mbar_wait(smem_u32(&k_full[kst]), (j / KST) & 1, abort_flag, args.err)) return false;
@@ -281,18 +336,16 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             // PV_i's inputs: P_i written over S_i, V_i split
             auto pv_ready = [&](int i) -> bool {
                 return mbar_wait(smem_u32(&p_full[i % SPB]), (i / SPB) & 1, abort_flag, args.err) &&
-                       mbar_wait(smem_u32(&vsp_full[i & 1]), (i >> 1) & 1, abort_flag, args.err);
+                       mbar_wait(smem_u32(&vsp_full[i % NVB]), (i / NVB) & 1, abort_flag, args.err);
             };
             auto pv = [&](int i) {  // O += P_i . V_i as P_lo.V_hi + P_hi.V_lo + P_hi.V_hi
-                const int b = i & 1;
+                const int b = i % NVB;
                 tc_fence_after();
-                const uint32_t p_hi = tmem_base + static_cast<uint32_t>((i % SPB) * TMEM_SP);
-                const uint64_t vd = v_desc + static_cast<uint64_t>(b * (VSP_BYTES >> 4));
-                mma_pv_term(tmem_base + TMEM_O, p_hi + AT_BN, vd, idesc_o, i > 0 ? 1u : 0u);  // P_lo . V_hi
-                mma_pv_term(tmem_base + TMEM_O, p_hi, vd + (V_BYTES >> 4), idesc_o, 1u);   // P_hi . V_lo
-                mma_pv_term(tmem_base + TMEM_O, p_hi, vd, idesc_o, 1u);                    // P_hi . V_hi
+                const uint64_t vh = v_desc + static_cast<uint64_t>(b * (VSP_BYTES >> 4));
+                mma_pv_block(tmem_base + TMEM_O, tmem_base + static_cast<uint32_t>((i % SPB) * TMEM_SP), vh,
+                             vh + (V_BYTES >> 4), idesc_o, i > 0 ? 1u : 0u);
                 mma_commit(smem_u32(&vsp_empty[b]));
-                mma_commit(smem_u32(&pv_done[b]));
+                mma_commit(smem_u32(&pv_done[i & 1]));
             };
             // issue order S_0 S_1 S_2 | PV_0 S_3 | PV_1 S_4 | ...
             for (int j = 0; ok && j < nb && j < SPB; ++j) ok = sblock(j);
@@ -314,56 +367,82 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
     } else if (warp >= 6) {
         // ---------------- V splitters (warps 6..9) ----------------
-        // Each V block [64 keys][128 dims] f32 is read straight from global memory (lane l of a warp reads the 16
-        // bytes of dims 4l..4l+3 of its keys), split into V_hi / V_lo and written transposed into the
-        // K-major layout the MMA reads: [128 dims][64 keys] as two 32-key chunks of 16 KB, 16-byte unit u of dim row
-        // n at u ^ (n % 8).  The next block's loads are in flight while this block is written.
-        // A thread holds 4 keys x 4 dims per store.  Its key quads are 4i + kr, kr = (t / 32 + dq / 2) % 4 for its
-        // index t among the 128: the eight lanes of one 128-byte store phase (dq = 8p .. 8p+7) then cover the eight
-        // 16-byte bank groups (kr sets the unit's low two bits, dq % 2 its third), where one key quad per warp would
-        // put them on two.  A lane pair still reads one whole 32-byte sector of a key row per load.
+        // Each V block [64 keys][128 dims] f32 is read straight from global memory, scaled by 2^k (k from the
+        // largest |V| of the task so far) and split into f16 V_hi / V_lo, each written in the layout the MMA reads
+        // as an MN-major B: two 64-dim chunks of 8 KB, key k's 128-byte row at k * 128, 16-byte unit u (dims
+        // 8u..8u+7 of the chunk) at u ^ (k % 8).  Thread t owns the dims 8(t % 16) .. 8(t % 16)+7 of keys
+        // t / 16 + 8i, i = 0..7: sixteen lanes read one key's 512-byte row, and the eight lanes of a 128-byte
+        // store phase fill one swizzled row.  The next block's loads are in flight while this block is written.
+        // The block maximum: once block j+1's loads have landed (after block j is handed over), every warp posts
+        // its part of that block's largest |V| and arrives on vmax_ready[(j+1) % 2]; before block j+1 is split,
+        // every warp reads the four parts after that barrier's phase completes.
         const int t = threadIdx.x - 6 * 32;  // 0..127
-        const int dq = t & 31;               // dims 4dq..4dq+3
-        const int kr = ((t >> 5) + (dq >> 1)) & 3;
-        const float* vbase = args.v + rec[args.v_p];
+        const int sw = warp - 6;             // 0..3
+        const int u = t & 15;                // dims 8u..8u+7
+        const int kb = t >> 4;               // keys kb + 8i
+        const int st_off = (u >> 3) * BOX + kb * 128 + (((u & 7) ^ kb) << 4);  // (kb + 8i) % 8 == kb
+        const float* vbase = args.v + rec[args.v_p] + 8 * u;
         auto load = [&](int j, float4 (&x)[16]) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 8; ++i) {
+                const float4* src =
+                    reinterpret_cast<const float4*>(vbase + static_cast<int64_t>(j * AT_BN + kb + 8 * i) * args.v_pitch);
+                x[2 * i] = __ldg(src);
+                x[2 * i + 1] = __ldg(src + 1);
+            }
+        };
+        auto post_max = [&](int j, const float4 (&x)[16]) {  // this warp's part of block j's largest |V|
+            uint32_t m = 0u;  // bits of a non-negative float; NaN orders above inf
 #pragma unroll
-                for (int a = 0; a < 4; ++a) {
-                    const int k = j * AT_BN + 4 * (4 * i + kr) + a;
-                    x[4 * i + a] = __ldg(reinterpret_cast<const float4*>(vbase + static_cast<int64_t>(k) * args.v_pitch) + dq);
-                }
+            for (int i = 0; i < 16; ++i)
+                m = max(m, max(max(__float_as_uint(x[i].x) & 0x7fffffffu, __float_as_uint(x[i].y) & 0x7fffffffu),
+                               max(__float_as_uint(x[i].z) & 0x7fffffffu, __float_as_uint(x[i].w) & 0x7fffffffu)));
+            m = __reduce_max_sync(0xffffffffu, m);
+            if (lane == 0) {
+                v_part[(j & 1) * 4 + sw] = m;
+                mbar_arrive(smem_u32(&vmax_ready[j & 1]));
+            }
         };
         float4 cur[16], nxt[16];
-        if (nb > 0) load(0, cur);
+        uint32_t vmax_bits = 0u;  // largest |V| of the task so far
+        if (nb > 0) {
+            load(0, cur);
+            post_max(0, cur);
+        }
         for (int j = 0; j < nb; ++j) {
-            const int b = j & 1;
+            const int b = j % NVB, pb = j & 1;  // V buffer; partial-maximum slot
             if (j + 1 < nb) load(j + 1, nxt);
-            uint8_t* hi = smem + OFF_VSP + b * VSP_BYTES;
+            // block j's four parts; the slot was last read in block j-2, which every warp finished before it
+            // posted block j-1's part (the phase this warp waited for in block j-1)
+            if (!mbar_wait(smem_u32(&vmax_ready[pb]), (j >> 1) & 1, abort_flag, args.err)) break;
+            vmax_bits =
+                max(vmax_bits, max(max(v_part[pb * 4], v_part[pb * 4 + 1]), max(v_part[pb * 4 + 2], v_part[pb * 4 + 3])));
+            const int k2 = v_scale_log2(vmax_bits);
+            const float vs = pow2f(k2);
+            if (j >= NVB && !mbar_wait(smem_u32(&vsp_empty[b]), ((j / NVB) & 1) ^ 1u, abort_flag, args.err)) break;
+            uint8_t* hi = smem + OFF_VSP + b * VSP_BYTES + st_off;
             uint8_t* lo = hi + V_BYTES;
-            if (j >= 2 && !mbar_wait(smem_u32(&vsp_empty[b]), ((j >> 1) & 1) ^ 1u, abort_flag, args.err)) break;
+            // one pair of dims: scaled, split, packed into `h` / `l`
+            auto split2 = [vs](float a, float c, uint32_t& h, uint32_t& l) {
+                const float x0 = a * vs, x1 = c * vs;
+                const float h0 = f16_hi_part(x0), h1 = f16_hi_part(x1);
+                h = pack_f16(h0, h1);
+                l = pack_f16(x0 - h0, x1 - h1);
+            };
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int kq = 4 * i + kr;  // keys 4kq..4kq+3 of the block
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {  // dim n = 4dq + c
-                    const int n = 4 * dq + c;
-                    const int off = (kq >> 3) * 16384 + n * 128 + (((kq & 7) ^ (n & 7)) << 4);
-                    float h[4], l[4];
-#pragma unroll
-                    for (int a = 0; a < 4; ++a) {
-                        const float4 v = cur[4 * i + a];
-                        const float x = c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w;
-                        h[a] = tf32_hi(x);
-                        l[a] = x - h[a];
-                    }
-                    *reinterpret_cast<float4*>(hi + off) = make_float4(h[0], h[1], h[2], h[3]);
-                    *reinterpret_cast<float4*>(lo + off) = make_float4(l[0], l[1], l[2], l[3]);
-                }
+            for (int i = 0; i < 8; ++i) {
+                uint4 h, l;
+                split2(cur[2 * i].x, cur[2 * i].y, h.x, l.x);
+                split2(cur[2 * i].z, cur[2 * i].w, h.y, l.y);
+                split2(cur[2 * i + 1].x, cur[2 * i + 1].y, h.z, l.z);
+                split2(cur[2 * i + 1].z, cur[2 * i + 1].w, h.w, l.w);
+                *reinterpret_cast<uint4*>(hi + i * 8 * 128) = h;
+                *reinterpret_cast<uint4*>(lo + i * 8 * 128) = l;
             }
-            fence_proxy_async_smem();  // V_hi / V_lo become visible to the tensor core's reads
+            if (t == 0) v_log2[b] = k2;  // read by the softmax warps after they wait for this block
+            fence_proxy_async_smem();    // V_hi / V_lo become visible to the tensor core's reads
             mbar_arrive(smem_u32(&vsp_full[b]));
+            if (j + 1 < nb) post_max(j + 1, nxt);
 #pragma unroll
             for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
         }
@@ -377,6 +456,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         else if (args.scale_mode == 2) scale = __uint_as_float(static_cast<uint32_t>(rec[args.scale_pos]));
         const float c2 = scale * 1.4426950408889634f;  // into the base-2 domain
         float m_ref = -INFINITY, l = 0.f;
+        int k_v = 0;  // V's scale exponent in O so far
         bool ok = true;
         for (int j = 0; j < nb; ++j) {
             const int sb = j % SPB;
@@ -406,7 +486,42 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 corr = j == 0 ? 1.f : exp2f(m_ref - m_new);
                 m_ref = m_new;
             }
-            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+            l *= corr;
+            // p = 2^(x - max) in f32 for the sum; p * 2^7 as f16 P_hi + P_lo (key pairs packed) into this row's TMEM
+            // lane
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {  // keys 32c .. 32c+31: P_hi columns 16c.., P_lo columns 32 + 16c..
+                uint32_t ph[16], pl[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float p0 = ex2_approx(__uint_as_float(r[c][2 * i]) * c2 - m_ref);
+                    const float p1 = ex2_approx(__uint_as_float(r[c][2 * i + 1]) * c2 - m_ref);
+                    sum4[(2 * i) & 3] += p0;
+                    sum4[(2 * i + 1) & 3] += p1;
+                    const float q0 = p0 * static_cast<float>(1 << kPScaleLog2), q1 = p1 * static_cast<float>(1 << kPScaleLog2);
+                    const float h0 = f16_hi_part(q0), h1 = f16_hi_part(q1);
+                    ph[i] = pack_f16(h0, h1);
+                    pl[i] = pack_f16(q0 - h0, q1 - h1);
+                }
+                tmem_st16(sp_addr + 16 * c, ph);
+                tmem_st16(sp_addr + 32 + 16 * c, pl);
+            }
+            tmem_wait_st();
+            const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+            l += sum;
+            // V's scale for this block (set by the splitters before they released its buffer), read after P_j is
+            // out; when it drops, O moves to the new scale together with the row-max correction, before PV_j
+            // (which waits for p_full) accumulates
+            if (!mbar_wait(smem_u32(&vsp_full[j % NVB]), (j / NVB) & 1, abort_flag, args.err)) {
+                ok = false;
+                break;
+            }
+            const int k_j = v_log2[j % NVB];
+            const bool v_moved = j > 0 && k_j != k_v;  // the same in every thread
+            const float ofac = v_moved ? corr * (k_j - k_v >= -126 ? pow2f(k_j - k_v) : 0.f) : corr;  // k only falls
+            k_v = k_j;
+            if (j > 0 && (v_moved || __any_sync(0xffffffffu, grow))) {
                 // O holds block j-1's contribution (its MMAs are done) before it is rescaled
                 if (!mbar_wait(smem_u32(&pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort_flag, args.err)) {
                     ok = false;
@@ -420,37 +535,17 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     tmem_wait_ld();
                     reg_fence(r);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * ofac);
                     tmem_st32(tmem_base + lane_addr + TMEM_O + c * 32, r);
                 }
                 tmem_wait_st();
             }
-            l *= corr;
-            // p = 2^(x - max) in f32 for the sum, as P_hi + P_lo into this row's TMEM lane
-            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t h[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float p = exp2f(__uint_as_float(r[c][i]) * c2 - m_ref);
-                    sum4[i & 3] += p;
-                    const float hv = tf32_hi(p);
-                    h[i] = __float_as_uint(hv);
-                    r[c][i] = __float_as_uint(p - hv);
-                }
-                tmem_st32(sp_addr + c * 32, h);
-                tmem_st32(sp_addr + AT_BN + c * 32, r[c]);
-            }
-            tmem_wait_st();
             tc_fence_before();
-            const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-            l += sum;
             mbar_arrive(smem_u32(&p_full[sb]));
         }
         if (ok && mbar_wait(smem_u32(o_full), 0, abort_flag, args.err)) {
             tc_fence_after();
-            const float inv = 1.f / l;
+            const float inv = pow2f(-(kPScaleLog2 + k_v)) / l;  // the two scales and the sum
             float* orow = args.out + rec[args.o_p] + static_cast<int64_t>(row) * args.o_pitch;
 #pragma unroll 1
             for (int c = 0; c < AT_D / 32; ++c) {

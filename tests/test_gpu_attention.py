@@ -3,8 +3,9 @@
 The kernel pattern is the reference attention tile at full size: S = Q.K^T (f16) [* scale], a row softmax in f32,
 O = W.V with V f32 (pto has no cast, so the softmax result and V are both f32), stored f32.  The oracle runs the
 tile program's arithmetic (fused multiply-adds in k order); the fused kernel runs Q.K^T on kind::f16 and W.V on
-kind::tf32 with a three-term split, which keeps each product to ~22 bits; its exponentials are base 2 from a
-pre-scaled score.  Tolerance: the north_star's contraction bar, plain relative error 2e-3 on every output element
+kind::f16 with bf16 operands in a three-term split (W_hi.V_hi + W_hi.V_lo + W_lo.V_hi, x_hi = bf16(x), x_lo =
+bf16(x - x_hi)), which keeps each product to ~2^-17 relative error; its exponentials are base 2 from a pre-scaled
+score.  Tolerance: the north_star's contraction bar, plain relative error 2e-3 on every output element
 with |O| >= 1e-2 rms(O) (smaller ones: absolute 2e-3 x that floor), against the oracle and against fp64.  The
 measured worst against the oracle is 7e-4, on elements near the floor where the softmax-weighted sum cancels, and
 comes from the f32 accumulation order of Q.K^T (tensor-core blocks against the tile program's k order): unscaled
@@ -65,6 +66,31 @@ def test_fused_attention_large_logits_rescale(require_cuda):
     got = [a.copy() for a in arrays]
     CudaExecutable(plan).run_with_symbols(got, {}, {}, {})
     assert_rel(got[3], ref[3], ORACLE_RTOL, 1e-2 * rms(ref[3]))
+
+
+@pytest.mark.parametrize("pattern", ["rising", "tiny_then_huge", "zero_blocks"])
+def test_fused_attention_v_scale(pattern, require_cuda):
+    # W.V runs on f16 operands with V scaled by a power of two chosen from the largest |V| seen so far: blocks whose
+    # magnitudes rise move the scale (O rescaled in TMEM), tiny values sit far below it, all-zero blocks leave it
+    rng = np.random.default_rng(11)
+    B, H, QT, L = 1, 1, 1, 512
+    plan = workloads.attention_plan(B, H, QT, L, scale=0.088)
+    arrays = workloads.attention_inputs(rng, B, H, QT, L)
+    blk = np.repeat(np.arange(L // 64), 64).astype(np.float64)[None, None, :, None]
+    if pattern == "rising":  # each 64-key block 2^5 larger than the one before: the scale drops at every block
+        arrays[2] = (arrays[2] * 2.0 ** (5 * blk - 20)).astype(np.float32)
+    elif pattern == "tiny_then_huge":  # 1e-30-sized values, then 1e30-sized ones
+        arrays[2] = (arrays[2] * np.where(blk < 4, 1e-30, 1e30)).astype(np.float32)
+    else:  # every other block exactly zero
+        arrays[2] = (arrays[2] * (blk % 2)).astype(np.float32)
+    ref = [a.copy() for a in arrays]
+    CpuSim(plan).run(ref)
+    got = [a.copy() for a in arrays]
+    CudaExecutable(plan).run_with_symbols(got, {}, {}, {})
+    assert np.isfinite(got[3]).all()
+    assert_rel(got[3], ref[3], ORACLE_RTOL, 1e-2 * rms(ref[3]))
+    o64 = fp64_attention(arrays, 0.088)
+    assert_rel(got[3], o64, RTOL_F16_MMA, 1e-2 * rms(o64))
 
 
 def test_fused_and_staged_forms_agree(require_cuda):
