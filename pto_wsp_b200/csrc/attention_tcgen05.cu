@@ -219,20 +219,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;      // [KST]
-    uint64_t* k_empty = bars + 5;     // [KST]
-    uint64_t* vsp_full = bars + 9;    // [NVB] V_hi / V_lo written
-    uint64_t* vsp_empty = bars + 13;  // [NVB] the MMAs read them
-    uint64_t* s_full = bars + 17;     // [3] S_j in its buffer
-    uint64_t* p_full = bars + 20;     // [3] P_j written over it
-    uint64_t* pv_done = bars + 23;    // [2] O holds block j's contribution
-    uint64_t* o_full = bars + 25;
-    uint64_t* drain = bars + 26;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 27);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
-    volatile int* v_log2 = reinterpret_cast<volatile int*>(bars + 29);  // [NVB] V's scale exponent of buffer b's block
-    uint32_t* v_part = reinterpret_cast<uint32_t*>(bars + 31);           // [2][4] splitter warps' largest |V| bits
-    uint64_t* vmax_ready = bars + 35;  // [2] the four splitter warps posted their parts of a block's largest |V|
+    uint64_t* k_full = q_full + 1;          // [KST]
+    uint64_t* k_empty = k_full + KST;       // [KST]
+    uint64_t* vsp_full = k_empty + KST;     // [NVB] V_hi / V_lo written
+    uint64_t* vsp_empty = vsp_full + NVB;   // [NVB] the MMAs read them
+    uint64_t* s_full = vsp_empty + NVB;     // [3] S_j in its buffer
+    uint64_t* p_full = s_full + SPB;        // [3] P_j written over it
+    uint64_t* pv_done = p_full + SPB;       // [2] O holds block j's contribution
+    uint64_t* o_full = pv_done + 2;
+    uint64_t* drain = o_full + 1;
+    uint64_t* vmax_ready = drain + 1;       // [2] the four splitter warps posted their parts of a block's largest |V|
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(vmax_ready + 2);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(vmax_ready + 3);
+    volatile int* v_log2 = reinterpret_cast<volatile int*>(vmax_ready + 4);         // [NVB] V's scale exponent of buffer b
+    uint32_t* v_part = reinterpret_cast<uint32_t*>(vmax_ready + 4 + (NVB + 1) / 2);  // [2][4] splitter warps' largest |V| bits
+    static_assert((1 + 2 * KST + 2 * NVB + 2 * SPB + 6 + (NVB + 1) / 2 + 4) * 8 <= 512, "barrier block exceeds its 512 bytes");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
