@@ -148,7 +148,10 @@ PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
  * ptowsp_cuda_kernel_times; setting it clears the sums; default 0),
  * "fused_attention" (0: kernels of the attention pattern run as their stages
  * -- matmul kernels and row programs over HBM scratch -- instead of the fused
- * tcgen05 kernel; default 1).
+ * tcgen05 kernel; default 1), "csp_device" (0: a CSP pipeline body runs as
+ * dependency waves instead of one CTA per process with device channels;
+ * changing it drops the cached task tables; default 1 -- ptowsp_cuda_describe
+ * reports the form a run took and, for waves, why).
  * "stage_scratch_mb" is clamped to 1 .. 1048576; changing it drops the cached
  * task tables, which were grouped for the old budget. */
 PTOWSP_API int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value);

@@ -96,6 +96,10 @@ int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value)
         p.opt_stage_scratch_mb = mb;
     } else if (!std::strcmp(key, "fused_attention")) {
         p.opt_fused_attention = value != 0;
+    } else if (!std::strcmp(key, "csp_device")) {
+        // a cached device-process program has no wave records on the device (and waves none for processes)
+        if ((value != 0) != (p.opt_csp_device != 0)) p.cached.reset();
+        p.opt_csp_device = value != 0;
     } else if (!std::strcmp(key, "kernel_events")) {
         p.opt_kernel_events = value != 0;
         guarded(prog, [&] { ptowsp::reset_kernel_times(p); return 0; }, 0);

@@ -915,6 +915,11 @@ std::string describe_program(const Program& p) {
     if (p.cached) {
         o << ",\"waves\":" << p.cached->waves.size() << ",\"tasks\":" << p.cached->tasks;
     }
+    if (!p.csp_mode.empty()) {  // a CSP pipeline body: device processes, or waves and why
+        std::string m;
+        for (char c : p.csp_mode.substr(0, 200)) m += (c == '"' || c == '\\' || c < 32) ? ' ' : c;
+        o << ",\"csp\":\"" << m << "\"";
+    }
     o << "}";
     return o.str();
 }

@@ -114,6 +114,30 @@ cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev,
                                 cudaStream_t s);
 int tile_program_max_smem();
 
+// CSP pipeline on the device (reference CSPT processes, src/python/pto_codegen.cpp:1759-2220): one CTA per
+// process runs the process's operations in order -- its tasks through the tile-program interpreter, its sends and
+// receives as per-channel counters in global memory (release / acquire at GPU scope, one sender and one receiver
+// per channel; a send waits while `cap` tokens are unreceived).  All CTAs are resident together (cooperative
+// launch); every wait is bounded (~2 s), after which the status word gets kErrTimeout and the CTA stops.
+enum CspOpKind : int { CSP_TASK = 0, CSP_SEND = 1, CSP_RECV = 2 };
+struct CspOp {
+    int32_t kind;  // CspOpKind
+    int32_t arg;   // task: kernel slot; send / receive: channel
+    int64_t rec;   // task: word offset of its record in the slot's batch records
+};
+struct CspArgs {
+    const CspOp* ops;                  // every process's operations, process after process
+    const int32_t* proc_first;         // [nproc + 1]: each process's first operation
+    const TaskBatch* batches;          // per kernel slot: params and record layout (rec = the records' base)
+    const TileProgram* const* progs;   // per kernel slot
+    unsigned* counts;                  // [2 * nchan]: tokens sent, tokens received (zero before the launch)
+    const int32_t* caps;               // [nchan]: tokens a sender may have outstanding (>= 1)
+    int nproc, nchan;
+    int* err;
+};
+// False (nothing launched) when the processes cannot all be resident at once.
+bool launch_csp_pipeline(const CspArgs& a, int smem_bytes, cudaStream_t s, cudaError_t* err);
+
 // Matmul on CUDA cores, any shape: C[M,N] (f32) = A[M,K] . B[K,N] (f16 or f32) per task, records [oa, ob, oc],
 // each output accumulated over k in order with fused multiply-adds (the tile program's arithmetic).
 cudaError_t launch_matmul_simt(const TaskBatch& b, int M, int N, int K, int workers, cudaStream_t s);

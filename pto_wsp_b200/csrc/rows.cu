@@ -225,174 +225,242 @@ __device__ __forceinline__ int32_t bin_i(int op, int32_t a, int32_t b) {
     }
 }
 
-__global__ void __launch_bounds__(256) tile_program_kernel(TaskBatch b, const TileProgram* __restrict__ prog) {
-    extern __shared__ uint32_t sm[];
+// One task of a tile program: its instructions in order over this CTA's shared memory, a block barrier after each
+// (every thread of the block calls it).  The record `rec` holds the task's view offsets, axis args and scalars.
+__device__ __forceinline__ void tp_run_task(const TaskBatch& b, const TileProgram* __restrict__ prog, const int64_t* rec,
+                                            uint32_t* sm) {
     const int ninstr = prog->ninstr;
-    for (int64_t task = blockIdx.x; task < b.ntasks; task += gridDim.x) {
-        const int64_t* rec = b.rec + task * b.stride;
-        for (int ii = 0; ii < ninstr; ++ii) {
-            const TPInstr in = prog->ins[ii];
-            switch (in.op) {
-                case TP_LOAD: {
-                    const TPSlot d = prog->slots[in.dst];
-                    const ParamDesc& p = b.p[in.param];
-                    const int64_t base = rec[in.param];
-                    for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
-                        const int r = e / in.cols, c = e - r * in.cols;
-                        const int64_t off = base + r * p.s3 + c * p.s4;
-                        uint32_t w = 0;
-                        if (off >= 0 && off < p.numel_span) w = load_elem_w(p, off, d.word);
-                        else atomicOr(b.err, kErrBounds);
-                        sm[d.off + r * d.pitch + c] = w;
-                    }
-                    break;
+    for (int ii = 0; ii < ninstr; ++ii) {
+        const TPInstr in = prog->ins[ii];
+        switch (in.op) {
+            case TP_LOAD: {
+                const TPSlot d = prog->slots[in.dst];
+                const ParamDesc& p = b.p[in.param];
+                const int64_t base = rec[in.param];
+                for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
+                    const int r = e / in.cols, c = e - r * in.cols;
+                    const int64_t off = base + r * p.s3 + c * p.s4;
+                    uint32_t w = 0;
+                    if (off >= 0 && off < p.numel_span) w = load_elem_w(p, off, d.word);
+                    else atomicOr(b.err, kErrBounds);
+                    sm[d.off + r * d.pitch + c] = w;
                 }
-                case TP_STORE: {
-                    const TPSlot a = prog->slots[in.a];
-                    const ParamDesc& p = b.p[in.param];
-                    const int64_t base = rec[in.param];
-                    for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
-                        const int r = e / in.cols, c = e - r * in.cols;
-                        const int64_t off = base + r * p.s3 + c * p.s4;
-                        const uint32_t w = (r < a.rows && c < a.cols) ? sm[a.off + r * a.pitch + c] : 0u;
-                        if (off >= 0 && off < p.numel_span) store_elem(p, off, w, a.word);
-                        else atomicOr(b.err, kErrBounds);
-                    }
-                    break;
-                }
-                case TP_MOV: {
-                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
-                    for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
-                        const int r = e / d.cols, c = e - r * d.cols;
-                        sm[d.off + r * d.pitch + c] = sm[a.off + r * a.pitch + c];
-                    }
-                    break;
-                }
-                case TP_BIN: {
-                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], bb = prog->slots[in.b];
-                    for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
-                        const int r = e / d.cols, c = e - r * d.cols;
-                        const uint32_t wa = sm[a.off + r * a.pitch + c];
-                        const int bi = in.mode == MODE_FULL ? (bb.off + r * bb.pitch + c)
-                                       : in.mode == MODE_ROW ? (bb.off + r) : (bb.off + c);
-                        const uint32_t wb = sm[bi];
-                        uint32_t out;
-                        if (d.word == W_F32) out = __float_as_uint(bin_f(in.sub, __uint_as_float(wa), __uint_as_float(wb)));
-                        else out = static_cast<uint32_t>(bin_i(in.sub, static_cast<int32_t>(wa), static_cast<int32_t>(wb)));
-                        sm[d.off + r * d.pitch + c] = out;
-                    }
-                    break;
-                }
-                case TP_BINS: {
-                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
-                    float fs = in.fval;
-                    int32_t is = in.ival;
-                    if (in.scalar_src >= 0) {
-                        const uint64_t raw = static_cast<uint64_t>(rec[b.nparams + b.naxis + in.scalar_src]);
-                        const int st = prog->scalar_types[in.scalar_src];
-                        if (st == 0) {
-                            fs = __uint_as_float(static_cast<uint32_t>(raw));
-                            is = static_cast<int32_t>(fs);
-                        } else {
-                            is = static_cast<int32_t>(raw);
-                            fs = st == 2 ? static_cast<float>(static_cast<int64_t>(raw)) : static_cast<float>(is);
-                        }
-                    }
-                    for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
-                        const int r = e / d.cols, c = e - r * d.cols;
-                        const uint32_t wa = sm[a.off + r * a.pitch + c];
-                        uint32_t out;
-                        if (d.word == W_F32) {
-                            const float x = __uint_as_float(wa);
-                            out = __float_as_uint(in.scalar_first ? bin_f(in.sub, fs, x) : bin_f(in.sub, x, fs));
-                        } else {
-                            const int32_t x = static_cast<int32_t>(wa);
-                            out = static_cast<uint32_t>(in.scalar_first ? bin_i(in.sub, is, x) : bin_i(in.sub, x, is));
-                        }
-                        sm[d.off + r * d.pitch + c] = out;
-                    }
-                    break;
-                }
-                case TP_EXP:
-                case TP_RSQRT: {
-                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
-                    for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
-                        const int r = e / d.cols, c = e - r * d.cols;
-                        const float x = __uint_as_float(sm[a.off + r * a.pitch + c]);
-                        const float y = in.op == TP_EXP ? expf(x) : __fdiv_rn(1.0f, sqrtf(x));
-                        sm[d.off + r * d.pitch + c] = __float_as_uint(y);
-                    }
-                    break;
-                }
-                case TP_ROWSUM:
-                case TP_ROWMAX:
-                case TP_ROWMEAN: {
-                    // Sequential column order per row (one thread per row).
-                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
-                    for (int r = threadIdx.x; r < d.rows; r += blockDim.x) {
-                        float acc = in.op == TP_ROWMAX ? -INFINITY : 0.f;
-                        for (int c = 0; c < a.cols; ++c) {
-                            const float x = __uint_as_float(sm[a.off + r * a.pitch + c]);
-                            acc = in.op == TP_ROWMAX ? fmaxf(acc, x) : __fadd_rn(acc, x);
-                        }
-                        if (in.op == TP_ROWMEAN) acc = __fdiv_rn(acc, static_cast<float>(in.k));
-                        sm[d.off + r * d.pitch] = __float_as_uint(acc);
-                    }
-                    break;
-                }
-                case TP_MATMUL: {
-                    // f32 accumulation in k order, one fused multiply-add (single rounding) per step.
-                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], bb = prog->slots[in.b];
-                    for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
-                        const int r = e / in.cols, c = e - r * in.cols;
-                        float acc = 0.f;
-                        for (int kk = 0; kk < in.k; ++kk)
-                            acc = __fmaf_rn(__uint_as_float(sm[a.off + r * a.pitch + kk]),
-                                            __uint_as_float(sm[bb.off + kk * bb.pitch + c]), acc);
-                        sm[d.off + r * d.pitch + c] = __float_as_uint(acc);
-                    }
-                    break;
-                }
-                case TP_IOTA: {
-                    const TPSlot d = prog->slots[in.dst];
-                    for (int c = threadIdx.x; c < d.cols; c += blockDim.x) sm[d.off + c] = static_cast<uint32_t>(c);
-                    break;
-                }
-                case TP_TSORT32: {
-                    // Stable descending sort of n (<= rows*cols) scores with their indices:
-                    // rank_i = #{j : s_j > s_i or (s_j == s_i and j < i)}; dst = interleaved (score, index).
-                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], ix = prog->slots[in.b];
-                    const int n = in.k;
-                    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-                        const float si = __uint_as_float(sm[a.off + (i / a.cols) * a.pitch + (i % a.cols)]);
-                        int rank = 0;
-                        for (int j = 0; j < n; ++j) {
-                            const float sj = __uint_as_float(sm[a.off + (j / a.cols) * a.pitch + (j % a.cols)]);
-                            rank += (sj > si) || (sj == si && j < i);
-                        }
-                        const uint32_t idx = sm[ix.off + (i / ix.cols) * ix.pitch + (i % ix.cols)];
-                        const int p0 = 2 * rank, p1 = 2 * rank + 1;
-                        if (p1 < d.rows * d.cols) {
-                            sm[d.off + (p0 / d.cols) * d.pitch + (p0 % d.cols)] = __float_as_uint(si);
-                            sm[d.off + (p1 / d.cols) * d.pitch + (p1 % d.cols)] = __float_as_uint(static_cast<float>(idx));
-                        }
-                    }
-                    break;
-                }
-                case TP_EXTRACT: {
-                    const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
-                    for (int i = threadIdx.x; i < in.k; i += blockDim.x) {
-                        const int p = 2 * i + 1;
-                        const float f = __uint_as_float(sm[a.off + (p / a.cols) * a.pitch + (p % a.cols)]);
-                        if (i < d.rows * d.cols) sm[d.off + (i / d.cols) * d.pitch + (i % d.cols)] = static_cast<uint32_t>(static_cast<int32_t>(f));
-                    }
-                    break;
-                }
-                default:
-                    break;
+                break;
             }
-            __syncthreads();
+            case TP_STORE: {
+                const TPSlot a = prog->slots[in.a];
+                const ParamDesc& p = b.p[in.param];
+                const int64_t base = rec[in.param];
+                for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
+                    const int r = e / in.cols, c = e - r * in.cols;
+                    const int64_t off = base + r * p.s3 + c * p.s4;
+                    const uint32_t w = (r < a.rows && c < a.cols) ? sm[a.off + r * a.pitch + c] : 0u;
+                    if (off >= 0 && off < p.numel_span) store_elem(p, off, w, a.word);
+                    else atomicOr(b.err, kErrBounds);
+                }
+                break;
+            }
+            case TP_MOV: {
+                const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
+                    const int r = e / d.cols, c = e - r * d.cols;
+                    sm[d.off + r * d.pitch + c] = sm[a.off + r * a.pitch + c];
+                }
+                break;
+            }
+            case TP_BIN: {
+                const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], bb = prog->slots[in.b];
+                for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
+                    const int r = e / d.cols, c = e - r * d.cols;
+                    const uint32_t wa = sm[a.off + r * a.pitch + c];
+                    const int bi = in.mode == MODE_FULL ? (bb.off + r * bb.pitch + c)
+                                   : in.mode == MODE_ROW ? (bb.off + r) : (bb.off + c);
+                    const uint32_t wb = sm[bi];
+                    uint32_t out;
+                    if (d.word == W_F32) out = __float_as_uint(bin_f(in.sub, __uint_as_float(wa), __uint_as_float(wb)));
+                    else out = static_cast<uint32_t>(bin_i(in.sub, static_cast<int32_t>(wa), static_cast<int32_t>(wb)));
+                    sm[d.off + r * d.pitch + c] = out;
+                }
+                break;
+            }
+            case TP_BINS: {
+                const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                float fs = in.fval;
+                int32_t is = in.ival;
+                if (in.scalar_src >= 0) {
+                    const uint64_t raw = static_cast<uint64_t>(rec[b.nparams + b.naxis + in.scalar_src]);
+                    const int st = prog->scalar_types[in.scalar_src];
+                    if (st == 0) {
+                        fs = __uint_as_float(static_cast<uint32_t>(raw));
+                        is = static_cast<int32_t>(fs);
+                    } else {
+                        is = static_cast<int32_t>(raw);
+                        fs = st == 2 ? static_cast<float>(static_cast<int64_t>(raw)) : static_cast<float>(is);
+                    }
+                }
+                for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
+                    const int r = e / d.cols, c = e - r * d.cols;
+                    const uint32_t wa = sm[a.off + r * a.pitch + c];
+                    uint32_t out;
+                    if (d.word == W_F32) {
+                        const float x = __uint_as_float(wa);
+                        out = __float_as_uint(in.scalar_first ? bin_f(in.sub, fs, x) : bin_f(in.sub, x, fs));
+                    } else {
+                        const int32_t x = static_cast<int32_t>(wa);
+                        out = static_cast<uint32_t>(in.scalar_first ? bin_i(in.sub, is, x) : bin_i(in.sub, x, is));
+                    }
+                    sm[d.off + r * d.pitch + c] = out;
+                }
+                break;
+            }
+            case TP_EXP:
+            case TP_RSQRT: {
+                const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                for (int e = threadIdx.x; e < d.rows * d.cols; e += blockDim.x) {
+                    const int r = e / d.cols, c = e - r * d.cols;
+                    const float x = __uint_as_float(sm[a.off + r * a.pitch + c]);
+                    const float y = in.op == TP_EXP ? expf(x) : __fdiv_rn(1.0f, sqrtf(x));
+                    sm[d.off + r * d.pitch + c] = __float_as_uint(y);
+                }
+                break;
+            }
+            case TP_ROWSUM:
+            case TP_ROWMAX:
+            case TP_ROWMEAN: {
+                // Sequential column order per row (one thread per row).
+                const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                for (int r = threadIdx.x; r < d.rows; r += blockDim.x) {
+                    float acc = in.op == TP_ROWMAX ? -INFINITY : 0.f;
+                    for (int c = 0; c < a.cols; ++c) {
+                        const float x = __uint_as_float(sm[a.off + r * a.pitch + c]);
+                        acc = in.op == TP_ROWMAX ? fmaxf(acc, x) : __fadd_rn(acc, x);
+                    }
+                    if (in.op == TP_ROWMEAN) acc = __fdiv_rn(acc, static_cast<float>(in.k));
+                    sm[d.off + r * d.pitch] = __float_as_uint(acc);
+                }
+                break;
+            }
+            case TP_MATMUL: {
+                // f32 accumulation in k order, one fused multiply-add (single rounding) per step.
+                const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], bb = prog->slots[in.b];
+                for (int e = threadIdx.x; e < in.rows * in.cols; e += blockDim.x) {
+                    const int r = e / in.cols, c = e - r * in.cols;
+                    float acc = 0.f;
+                    for (int kk = 0; kk < in.k; ++kk)
+                        acc = __fmaf_rn(__uint_as_float(sm[a.off + r * a.pitch + kk]),
+                                        __uint_as_float(sm[bb.off + kk * bb.pitch + c]), acc);
+                    sm[d.off + r * d.pitch + c] = __float_as_uint(acc);
+                }
+                break;
+            }
+            case TP_IOTA: {
+                const TPSlot d = prog->slots[in.dst];
+                for (int c = threadIdx.x; c < d.cols; c += blockDim.x) sm[d.off + c] = static_cast<uint32_t>(c);
+                break;
+            }
+            case TP_TSORT32: {
+                // Stable descending sort of n (<= rows*cols) scores with their indices:
+                // rank_i = #{j : s_j > s_i or (s_j == s_i and j < i)}; dst = interleaved (score, index).
+                const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a], ix = prog->slots[in.b];
+                const int n = in.k;
+                for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                    const float si = __uint_as_float(sm[a.off + (i / a.cols) * a.pitch + (i % a.cols)]);
+                    int rank = 0;
+                    for (int j = 0; j < n; ++j) {
+                        const float sj = __uint_as_float(sm[a.off + (j / a.cols) * a.pitch + (j % a.cols)]);
+                        rank += (sj > si) || (sj == si && j < i);
+                    }
+                    const uint32_t idx = sm[ix.off + (i / ix.cols) * ix.pitch + (i % ix.cols)];
+                    const int p0 = 2 * rank, p1 = 2 * rank + 1;
+                    if (p1 < d.rows * d.cols) {
+                        sm[d.off + (p0 / d.cols) * d.pitch + (p0 % d.cols)] = __float_as_uint(si);
+                        sm[d.off + (p1 / d.cols) * d.pitch + (p1 % d.cols)] = __float_as_uint(static_cast<float>(idx));
+                    }
+                }
+                break;
+            }
+            case TP_EXTRACT: {
+                const TPSlot d = prog->slots[in.dst], a = prog->slots[in.a];
+                for (int i = threadIdx.x; i < in.k; i += blockDim.x) {
+                    const int p = 2 * i + 1;
+                    const float f = __uint_as_float(sm[a.off + (p / a.cols) * a.pitch + (p % a.cols)]);
+                    if (i < d.rows * d.cols) sm[d.off + (i / d.cols) * d.pitch + (i % d.cols)] = static_cast<uint32_t>(static_cast<int32_t>(f));
+                }
+                break;
+            }
+            default:
+                break;
         }
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(256) tile_program_kernel(const __grid_constant__ TaskBatch b,
+                                                           const TileProgram* __restrict__ prog) {
+    extern __shared__ uint32_t sm[];
+    for (int64_t task = blockIdx.x; task < b.ntasks; task += gridDim.x) tp_run_task(b, prog, b.rec + task * b.stride, sm);
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t csp_clock_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// One CTA per CSP process (see CspArgs).  A send makes the CTA's earlier task writes visible before its token
+// (block barrier, then thread 0's fence and release store); a receive's acquire load, fence and block barrier
+// make the sender's writes visible to every thread of the receiving CTA before its next task.
+__global__ void __launch_bounds__(256) csp_pipeline_kernel(const __grid_constant__ CspArgs a) {
+    extern __shared__ uint32_t sm[];
+    __shared__ int s_stop;
+    const int p = blockIdx.x;
+    if (threadIdx.x == 0) s_stop = 0;
+    __syncthreads();
+    constexpr uint64_t kWaitNs = 2000000000ull;
+    for (int i = a.proc_first[p]; i < a.proc_first[p + 1]; ++i) {
+        const CspOp op = a.ops[i];
+        if (op.kind == CSP_TASK) {
+            const TaskBatch& b = a.batches[op.arg];
+            tp_run_task(b, a.progs[op.arg], b.rec + op.rec, sm);  // ends with a block barrier
+            continue;
+        }
+        __syncthreads();  // every thread's writes of the tasks before a send precede the token
+        if (threadIdx.x == 0) {
+            unsigned* sent = a.counts + 2 * op.arg;
+            unsigned* recvd = sent + 1;
+            const uint64_t t0 = csp_clock_ns();
+            if (op.kind == CSP_SEND) {
+                __threadfence();
+                const unsigned k = ld_acquire_gpu(sent);  // this CTA is the channel's only sender
+                while (k - ld_acquire_gpu(recvd) >= static_cast<unsigned>(a.caps[op.arg]))
+                    if (csp_clock_ns() - t0 > kWaitNs) {
+                        atomicOr(a.err, kErrTimeout);
+                        s_stop = 1;
+                        break;
+                    }
+                if (!s_stop) st_release_gpu(sent, k + 1);
+            } else {
+                const unsigned k = ld_acquire_gpu(recvd);  // this CTA is the channel's only receiver
+                while (ld_acquire_gpu(sent) <= k)
+                    if (csp_clock_ns() - t0 > kWaitNs) {
+                        atomicOr(a.err, kErrTimeout);
+                        s_stop = 1;
+                        break;
+                    }
+                __threadfence();
+                if (!s_stop) st_release_gpu(recvd, k + 1);
+            }
+        }
+        __syncthreads();
+        if (s_stop) break;
     }
 }
 
@@ -550,6 +618,26 @@ cudaError_t launch_matmul_simt(const TaskBatch& b, int M, int N, int K, int work
     // 1024: 128 x 128 blocks were 14 % slower -- two CTAs per SM hide the element-wise global loads less well)
     if (M < 128 && N >= 128) return launch_simt<64, 128>(b, M, N, K, workers, s);
     return launch_simt<64, 64>(b, M, N, K, workers, s);
+}
+
+bool launch_csp_pipeline(const CspArgs& a, int smem_bytes, cudaStream_t s, cudaError_t* err) {
+    if (smem_bytes > 48 * 1024 &&
+        cudaFuncSetAttribute(csp_pipeline_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, csp_pipeline_kernel, 256, smem_bytes) != cudaSuccess ||
+        static_cast<int64_t>(per_sm) * sm_count() < a.nproc || a.nproc < 1) {
+        cudaGetLastError();
+        return false;
+    }
+    // cooperative launch: the runtime guarantees that all CTAs are resident together (processes wait on one another)
+    CspArgs args = a;
+    void* params[] = {&args};
+    *err = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(csp_pipeline_kernel), dim3(static_cast<unsigned>(a.nproc)),
+                                       dim3(256), params, static_cast<size_t>(smem_bytes), s);
+    return true;
 }
 
 cudaError_t launch_tile_program(const TaskBatch& b, const TileProgram* prog_dev, int smem_bytes, int workers,

@@ -138,6 +138,93 @@ struct Walker {
         return written_any[tid] && !write_partial[tid] && write_elems[tid] == numel;
     }
 
+    // ---- a pipeline body as device processes: per-process operations, checked as the walk goes ----
+    struct CspCapture {
+        int nproc = 0, cur = -1;
+        bool ok = true;
+        std::string why;
+        std::vector<std::vector<dev::CspOp>> ops;      // per process
+        std::vector<int64_t> rec;
+        std::unordered_map<const Node*, int> slot_of;
+        std::vector<const Node*> slot_node;
+        std::vector<int> sender, receiver;             // per channel: its one sending / receiving process
+        std::vector<int32_t> cap;                      // per channel: device capacity
+        std::vector<std::vector<uint32_t>> vc;         // per process: tasks of each process ordered before this point
+        std::vector<std::vector<std::vector<uint32_t>>> sent_vc, recv_vc;  // per channel: clock at each send / receive
+        struct Access {
+            int proc;
+            uint32_t idx;
+        };
+        std::unordered_map<uint64_t, Access> last_w;
+        std::unordered_map<uint64_t, std::vector<Access>> readers;  // since the last write
+        uint64_t checks = 0;
+        void fail(const std::string& w) {
+            if (ok) why = w;
+            ok = false;
+        }
+        bool ordered(const Access& a, int p) const { return a.proc == p || vc[p][a.proc] > a.idx; }
+    };
+    std::unique_ptr<CspCapture> csp;
+
+    void csp_task(const Node& n, const Batch& b, const uint64_t* rkeys, int nr, const uint64_t* wkeys, int nw) {
+        CspCapture& C = *csp;
+        if (!C.ok || C.cur < 0) return;
+        const int p = C.cur;
+        const KernelImpl& ki = P.impls[n.kernel_index];
+        if (!ki.tp_ok) return C.fail("kernel '" + P.plan.kernels[n.kernel_index].name + "' has no interpreter program");
+        if (extra_read_key) return C.fail("a task reads a device-selected condition");
+        const uint32_t idx = C.vc[p][p];
+        constexpr uint64_t kMaxChecks = 20000000;
+        for (int i = 0; i < nr; ++i) {
+            if (auto f = C.last_w.find(rkeys[i]); f != C.last_w.end() && !C.ordered(f->second, p))
+                return C.fail("a read is not ordered after another process's write by the channels");
+            C.readers[rkeys[i]].push_back({p, idx});
+        }
+        for (int i = 0; i < nw; ++i) {
+            if (auto f = C.last_w.find(wkeys[i]); f != C.last_w.end() && !C.ordered(f->second, p))
+                return C.fail("two processes write a tile in an order the channels do not fix");
+            auto& rd = C.readers[wkeys[i]];
+            C.checks += rd.size();
+            for (const auto& a : rd)
+                if (!C.ordered(a, p)) return C.fail("a write is not ordered after another process's read by the channels");
+            rd.clear();
+            C.last_w[wkeys[i]] = {p, idx};
+        }
+        if (C.checks > kMaxChecks) return C.fail("too many hazards to check");
+        auto [it, fresh] = C.slot_of.emplace(&n, static_cast<int>(C.slot_node.size()));
+        if (fresh) C.slot_node.push_back(&n);
+        const size_t words = static_cast<size_t>(b.stride);
+        dev::CspOp op{dev::CSP_TASK, it->second, static_cast<int64_t>(C.rec.size())};
+        C.rec.insert(C.rec.end(), b.rec.end() - static_cast<std::ptrdiff_t>(words), b.rec.end());
+        C.ops[p].push_back(op);
+        C.vc[p][p]++;
+    }
+    void csp_channel(int c, bool send) {
+        CspCapture& C = *csp;
+        if (!C.ok || C.cur < 0) return;
+        const int p = C.cur;
+        int& who = send ? C.sender[c] : C.receiver[c];
+        if (who >= 0 && who != p) return C.fail("a channel with more than one " + std::string(send ? "sender" : "receiver"));
+        who = p;
+        auto join = [&](const std::vector<uint32_t>& o) {
+            for (int q = 0; q < C.nproc; ++q) C.vc[p][q] = std::max(C.vc[p][q], o[q]);
+        };
+        if (send) {
+            const size_t k = C.sent_vc[c].size();  // a send waits for the receive cap tokens before it
+            if (k >= static_cast<size_t>(C.cap[c])) {
+                if (C.recv_vc[c].size() <= k - C.cap[c]) return C.fail("a send runs ahead of its channel's receives");
+                join(C.recv_vc[c][k - C.cap[c]]);
+            }
+            C.sent_vc[c].push_back(C.vc[p]);
+        } else {
+            const size_t k = C.recv_vc[c].size();  // a receive waits for its send
+            if (C.sent_vc[c].size() <= k) return C.fail("a receive without its send");
+            join(C.sent_vc[c][k]);
+            C.recv_vc[c].push_back(C.vc[p]);
+        }
+        C.ops[p].push_back(dev::CspOp{send ? dev::CSP_SEND : dev::CSP_RECV, c, 0});
+    }
+
     Walker(Program& p, RuntimeContext* c, std::vector<TensorBinding>& t, LaunchProgram& l, std::vector<std::string>& lg)
         : P(p), ctx(c), T(t), L(l),
           sched(static_cast<uint32_t>(p.plan.schedule.num_targets > 0 ? p.plan.schedule.num_targets
@@ -577,6 +664,7 @@ struct Walker {
         b.ntasks++;
         L.tasks++;
         last_batch = &b;
+        if (csp) csp_task(n, b, rkeys, nr, wkeys, nw);
         return args;
     }
 
@@ -616,6 +704,19 @@ struct Walker {
         std::vector<Chan> ch(n.channels.size());
         for (size_t c = 0; c < ch.size(); ++c) ch[c].cap = n.channels[c].capacity;
         std::vector<Proc> pr(n.processes.size());
+        if (&n == P.plan.body.get() && P.opt_csp_device && P.cacheable) {  // the whole body: a device-process candidate
+            csp = std::make_unique<CspCapture>();
+            CspCapture& C = *csp;
+            C.nproc = static_cast<int>(pr.size());
+            C.ops.resize(pr.size());
+            C.vc.assign(pr.size(), std::vector<uint32_t>(pr.size(), 0));
+            C.sender.assign(ch.size(), -1);
+            C.receiver.assign(ch.size(), -1);
+            C.sent_vc.resize(ch.size());
+            C.recv_vc.resize(ch.size());
+            for (size_t c = 0; c < ch.size(); ++c)
+                C.cap.push_back(static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(n.channels[c].capacity, 1 << 30))));
+        }
         for (size_t p = 0; p < pr.size(); ++p) pr[p].stack.push_back(Frame{n.children[p].get()});
         auto wake_senders = [&](int c) {
             for (auto& q : pr)
@@ -642,7 +743,9 @@ struct Walker {
             }
             Proc& p = pr[pick];
             env = std::move(p.env);
+            if (csp) csp->cur = static_cast<int>(pick);
             const Step st = step(p, ch, latency, wake_senders, wake_receivers);
+            if (csp) csp->cur = -1;
             p.env = std::move(env);
             if (st == Step::Done) {
                 p.done = true;
@@ -654,6 +757,26 @@ struct Walker {
             }
         }
         env = std::move(saved);
+        if (csp) {
+            CspCapture& C = *csp;
+            if (C.ok) {
+                auto D = std::make_unique<CspDevice>();
+                for (auto& ops : C.ops) {
+                    D->proc_first.push_back(static_cast<int32_t>(D->ops.size()));
+                    D->ops.insert(D->ops.end(), ops.begin(), ops.end());
+                }
+                D->proc_first.push_back(static_cast<int32_t>(D->ops.size()));
+                D->rec = std::move(C.rec);
+                D->slot_node = C.slot_node;
+                D->caps = C.cap;
+                for (const Node* sn : D->slot_node) D->smem = std::max(D->smem, P.impls[sn->kernel_index].tp_smem);
+                L.csp = std::move(D);
+                L.csp_note.clear();
+            } else {
+                L.csp_note = C.why;
+            }
+            csp.reset();
+        }
         uint64_t makespan = 0;
         for (auto& q : pr) makespan = std::max(makespan, q.t);
         return makespan;
@@ -669,6 +792,7 @@ struct Walker {
             switch (n.kind) {
                 case Node::Kind::SlotSet:
                 case Node::Kind::SlotLoad:
+                    if (csp) csp->fail("slot operations in a process");
                     node(n, 0);
                     p.stack.pop_back();
                     break;
@@ -727,6 +851,7 @@ struct Walker {
                             return Step::Blocked;
                         }
                         c.buf.push_back({p.token, p.t});
+                        if (csp) csp_channel(n.channel, true);
                         wake_receivers(n.channel);
                         p.stack.pop_back();
                         return Step::Yield;
@@ -745,6 +870,7 @@ struct Walker {
                         }
                         c.rdv = {p.token, p.t};
                         c.has_rdv = true;
+                        if (csp) csp_channel(n.channel, true);
                         wake_receivers(n.channel);
                         f.state = 3;
                     }
@@ -799,6 +925,7 @@ struct Walker {
                         p.stack.pop_back();
                         break;
                     }
+                    if (csp) csp_channel(n.channel, false);
                     const uint64_t deliver = ts + latency;
                     if (deliver > p.t) p.t = deliver;
                     c.last_pop = p.t;
@@ -829,6 +956,13 @@ Batch::~Batch() {
     if (st_rec_dev) cudaFree(st_rec_dev);
     if (sel_dev) cudaFree(sel_dev);
     if (sel_tree_dev) cudaFree(sel_tree_dev);
+}
+
+CspDevice::~CspDevice() {
+    for (void* q : {static_cast<void*>(ops_dev), static_cast<void*>(first_dev), static_cast<void*>(rec_dev),
+                    static_cast<void*>(caps_dev), static_cast<void*>(tb_dev), static_cast<void*>(prog_dev),
+                    static_cast<void*>(counts_dev)})
+        if (q) cudaFree(q);
 }
 
 LaunchProgram::~LaunchProgram() {
@@ -899,20 +1033,17 @@ void* ensure_scratch(Program& p, size_t bytes) {
 }
 
 // Launch one batch.  `node` is the task node whose tensor bindings the batch uses.
-void launch_batch_body(Program& P, Batch& B, const Node& node, std::vector<TensorBinding>& T, const int64_t* rec_dev,
-                       uint64_t& launches) {
-    const KernelDef& kd = P.plan.kernels[B.kernel];
-    KernelImpl& ki = P.impls[B.kernel];
-    dev::TaskBatch tb{};
-    tb.rec = rec_dev + B.dev_off;
-    tb.ntasks = B.ntasks;
-    tb.stride = B.stride;
+// The record layout and tensor params of kernel `kernel`'s tasks under task node `node` with the current tensor
+// bindings; rows_ok becomes false when a param's rows are not 16-byte aligned with unit column stride.
+void fill_task_params(Program& P, int kernel, const Node& node, std::vector<TensorBinding>& T, dev::TaskBatch& tb,
+                      bool& rows_ok) {
+    const KernelDef& kd = P.plan.kernels[kernel];
+    tb.stride = kd.num_tensor_params + static_cast<int>(node.axis_args.size()) + kd.num_scalar_params;
     tb.nparams = kd.num_tensor_params;
     tb.naxis = static_cast<int>(node.axis_args.size());
     tb.nscalar = kd.num_scalar_params;
     tb.err = P.err_dev;
     if (kd.num_tensor_params > dev::kMaxParams) throw Error(PTOWSP_ERR_LIMIT, "kernel has more than 8 tile params");
-    bool rows_ok = B.aligned_rows;
     for (const auto& kp : kd.params) {
         if (kp.tensor_index < 0) continue;
         const TensorArg& ta = node.tensor_args[node.param_to_arg[kp.tensor_index]];
@@ -936,6 +1067,18 @@ void launch_batch_body(Program& P, Batch& B, const Node& node, std::vector<Tenso
         pd.elem_bytes = dtype_bytes(kp.v.dtype);
         if (pd.s4 != 1 || (pd.s3 & 3) != 0 || (reinterpret_cast<uintptr_t>(pd.base) & 15) != 0) rows_ok = false;
     }
+}
+
+void launch_batch_body(Program& P, Batch& B, const Node& node, std::vector<TensorBinding>& T, const int64_t* rec_dev,
+                       uint64_t& launches) {
+    const KernelDef& kd = P.plan.kernels[B.kernel];
+    KernelImpl& ki = P.impls[B.kernel];
+    dev::TaskBatch tb{};
+    bool rows_ok = B.aligned_rows;
+    fill_task_params(P, B.kernel, node, T, tb, rows_ok);
+    tb.rec = rec_dev + B.dev_off;
+    tb.ntasks = B.ntasks;
+    tb.stride = B.stride;
     const int workers = P.plan.schedule.window_tasks > 0 ? static_cast<int>(std::min<int64_t>(P.plan.schedule.window_tasks, 1 << 30)) : 0;
     cudaError_t e = cudaSuccess;
     ImplKind kind = ki.kind;
@@ -2333,6 +2476,63 @@ bool expand_on_device(Program& P, LaunchProgram& L, RuntimeContext* ctx, size_t 
     return true;
 }
 
+// The workload's CSP pipeline as one CTA per process (dev::launch_csp_pipeline).  Uploads the operations, records and
+// programs at the first launch; every launch builds the slots' tensor params from the current bindings and zeroes
+// the channel counters.  False (nothing launched) when the processes cannot all be resident at once.
+bool launch_csp(Program& P, LaunchProgram& L, std::vector<TensorBinding>& T, uint64_t& launches) {
+    CspDevice& D = *L.csp;
+    const size_t nslot = D.slot_node.size(), nchan = D.caps.size();
+    const int nproc = static_cast<int>(D.proc_first.size()) - 1;
+    if (!D.ops_dev) {
+        auto up = [&](auto** dst, const auto& v) {
+            using E = typename std::decay_t<decltype(v)>::value_type;
+            const size_t bytes = std::max<size_t>(v.size(), 1) * sizeof(E);
+            PW_CUDA(cudaMalloc(reinterpret_cast<void**>(dst), bytes));
+            if (!v.empty())
+                PW_CUDA(cudaMemcpyAsync(*dst, v.data(), v.size() * sizeof(E), cudaMemcpyHostToDevice, P.stream));
+        };
+        up(&D.ops_dev, D.ops);
+        up(&D.first_dev, D.proc_first);
+        up(&D.rec_dev, D.rec);
+        up(&D.caps_dev, D.caps);
+        std::vector<const dev::TileProgram*> progs;
+        for (const Node* n : D.slot_node) progs.push_back(P.impls[n->kernel_index].tp_dev);
+        up(&D.prog_dev, progs);
+        PW_CUDA(cudaMalloc(&D.tb_dev, std::max<size_t>(nslot, 1) * sizeof(dev::TaskBatch)));
+        PW_CUDA(cudaMalloc(&D.counts_dev, std::max<size_t>(2 * nchan, 1) * sizeof(unsigned)));
+        PW_CUDA(cudaStreamSynchronize(P.stream));  // the host vectors stay; the copies must not race a later change
+    }
+    std::vector<dev::TaskBatch> tbs(nslot);
+    for (size_t k = 0; k < nslot; ++k) {
+        bool rows_ok = true;
+        fill_task_params(P, D.slot_node[k]->kernel_index, *D.slot_node[k], T, tbs[k], rows_ok);
+        tbs[k].rec = D.rec_dev;
+        tbs[k].ntasks = 0;
+    }
+    if (nslot)
+        PW_CUDA(cudaMemcpyAsync(D.tb_dev, tbs.data(), nslot * sizeof(dev::TaskBatch), cudaMemcpyHostToDevice, P.stream));
+    if (nchan) PW_CUDA(cudaMemsetAsync(D.counts_dev, 0, 2 * nchan * sizeof(unsigned), P.stream));
+    dev::CspArgs a{};
+    a.ops = D.ops_dev;
+    a.proc_first = D.first_dev;
+    a.batches = D.tb_dev;
+    a.progs = D.prog_dev;
+    a.counts = D.counts_dev;
+    a.caps = D.caps_dev;
+    a.nproc = nproc;
+    a.nchan = static_cast<int>(nchan);
+    a.err = P.err_dev;
+    cudaError_t e = cudaSuccess;
+    if (!dev::launch_csp_pipeline(a, D.smem, P.stream, &e)) {
+        if (nslot) PW_CUDA(cudaStreamSynchronize(P.stream));  // the param copy reads `tbs`
+        return false;
+    }
+    if (e != cudaSuccess) throw Error(PTOWSP_ERR_CUDA, std::string("CSP pipeline launch: ") + cudaGetErrorString(e));
+    launches++;
+    if (nslot) PW_CUDA(cudaStreamSynchronize(P.stream));  // `tbs` is a host temporary of the param copy
+    return true;
+}
+
 uint64_t run_program(Program& P, RuntimeContext* ctx) {
     auto t_start = std::chrono::steady_clock::now();
     if (!ctx) throw Error(PTOWSP_ERR_ARG, "RuntimeContext is null");
@@ -2567,12 +2767,17 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
         PipePlan pp;  // would a run with these host buffers overlap its copies (kernels with a layout check on their
                       // first launch -- tcgen05 matmul, indexer scoring -- pipeline from their second run)?
         if (P.cacheable && plan_pipeline(P, *L, T, true, pp)) P.timing.chunks = static_cast<uint64_t>(pp.C);
+        if (plan.body && plan.body->kind == Node::Kind::Pipeline)  // what a run would do
+            P.csp_mode = L->csp && P.opt_csp_device ? std::string("device_processes")
+                         : "waves: " + (!P.opt_csp_device ? std::string("csp_device option is 0")
+                                        : !P.cacheable   ? std::string("data-dependent control flow")
+                                                         : L->csp_note);
         return L->makespan;
     }
 
     // ---- overlapped copy / compute for host-staged single-batch workloads ----
     bool pipelined = false;
-    if (L && !all_device) {
+    if (L && !all_device && !(L->csp && P.opt_csp_device)) {
         if (replay || P.cacheable) {
             if (!replay) {
                 // records must be on the device before any chunk launches
@@ -2618,8 +2823,20 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
 
     // the run's GPU time (`gpu_ms`) is only read back by a synchronous run
     if (!pipelined && !async_run) PW_CUDA(cudaEventRecord(P.ev0, P.stream));
-    if (pipelined) {
-        // kernels and copies were enqueued by run_pipelined
+    bool csp_ran = false;
+    if (!pipelined && L && L->csp && P.opt_csp_device) {
+        csp_ran = launch_csp(P, *L, T, launches);
+        if (!csp_ran) {
+            L->csp_note = "the processes cannot all be resident on the GPU at once";
+            L->csp.reset();  // later replays run the waves, whose records the fallback below uploads
+            if (replay) {
+                // a replay of a device-process program: its waves' records were never uploaded
+                throw Error(PTOWSP_ERR_CUDA, "CSP pipeline: device processes no longer fit; recompile the program");
+            }
+        }
+    }
+    if (pipelined || csp_ran) {
+        // kernels and copies were enqueued by run_pipelined, or the pipeline ran as device processes
     } else if (replay) {
         for (size_t wi = 0; wi < L->waves.size(); ++wi)
             for (auto& b : L->waves[wi].batches) launch_batch(P, b, *b.node, T, L->rec_dev, launches);
@@ -2651,6 +2868,12 @@ uint64_t run_program(Program& P, RuntimeContext* ctx) {
     }
     P.timing.launches = launches;
     P.timing.tasks = L->tasks;
+    P.csp_mode = plan.body && plan.body->kind == Node::Kind::Pipeline
+                     ? (csp_ran ? std::string("device_processes")
+                                : "waves: " + (!P.opt_csp_device ? std::string("csp_device option is 0")
+                                               : !P.cacheable   ? std::string("data-dependent control flow")
+                                               : L->csp_note.empty() ? std::string("not analysed") : L->csp_note))
+                     : std::string();
     for (auto& w : L->waves) P.timing.waves += w.batches.empty() ? 0 : 1;
     const uint64_t makespan = L->makespan;
     int err_host = 0;

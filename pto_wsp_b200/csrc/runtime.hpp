@@ -199,6 +199,30 @@ struct LoopExpand {
     size_t vars_cap = 0;
 };
 
+// A CSP pipeline run on the device: one CTA per process (dev::CspArgs).  The walk builds it when the workload's body
+// is one pipeline whose tasks the tile-program interpreter runs, whose channels have one sender and one receiver
+// each, and whose data hazards between processes are all ordered by the channels (checked with vector clocks over
+// the device's channel semantics: a receive waits for its send, a send for the receive `cap` tokens earlier).
+struct CspDevice {
+    std::vector<dev::CspOp> ops;            // every process's operations, process after process
+    std::vector<int32_t> proc_first;        // [nproc + 1]
+    std::vector<int64_t> rec;               // task records (op.rec: word offset)
+    std::vector<const Node*> slot_node;     // per kernel slot: a task node of that slot (params, tensor bindings)
+    std::vector<int32_t> caps;              // per channel: device capacity (>= 1)
+    int smem = 0;                           // interpreter shared memory, the largest slot's
+    dev::CspOp* ops_dev = nullptr;
+    int32_t* first_dev = nullptr;
+    int64_t* rec_dev = nullptr;
+    int32_t* caps_dev = nullptr;
+    dev::TaskBatch* tb_dev = nullptr;
+    const dev::TileProgram** prog_dev = nullptr;
+    unsigned* counts_dev = nullptr;
+    CspDevice() = default;
+    CspDevice(const CspDevice&) = delete;
+    CspDevice& operator=(const CspDevice&) = delete;
+    ~CspDevice();
+};
+
 struct LaunchProgram {  // result of one walk, reusable for static workloads
     std::vector<Wave> waves;
     std::unique_ptr<LoopExpand> expand;  // set when the workload is one loop whose records the device can rebuild
@@ -211,6 +235,8 @@ struct LaunchProgram {  // result of one walk, reusable for static workloads
     std::vector<std::string> key;  // replay log of runtime queries
     std::vector<uint8_t> full_write;  // per tensor: every element overwritten
     std::vector<uint8_t> write_first; // per tensor: every element overwritten in waves before any task reads it
+    std::unique_ptr<CspDevice> csp;   // the body is a CSP pipeline the device runs as processes (else waves)
+    std::string csp_note;             // why a pipeline body runs as waves (empty when it runs as processes)
     LaunchProgram() = default;
     LaunchProgram(const LaunchProgram&) = delete;
     LaunchProgram& operator=(const LaunchProgram&) = delete;
@@ -234,6 +260,8 @@ struct Program {
     int64_t opt_cache = 1, opt_chunks = 32, opt_sync = 1, opt_dry = 0, opt_stage_scratch_mb = 2048;
     int64_t opt_kernel_events = 0;       // bracket every batch launch with CUDA events (per-kernel device time)
     int64_t opt_fused_attention = 1;     // 0: attention kernels run their stages instead of the fused kernel
+    int64_t opt_csp_device = 1;          // 0: CSP pipelines run as dependency waves instead of device processes
+    std::string csp_mode;                // last run's CSP execution: "" (no pipeline), "device_processes", "waves: why"
     struct KernelEvent { int kernel; cudaEvent_t start, end; };
     std::vector<KernelEvent> kev_pending;  // recorded, not yet read
     std::vector<cudaEvent_t> kev_free;     // event pool

@@ -76,3 +76,43 @@ def test_pipeline_deadlock_is_an_error():
     ex.set_option("dry_run", 1)
     with pytest.raises(PtoWspCudaError, match="deadlock"):
         ex.run_with_symbols(arrays, axis, syms, sptr)
+
+
+# ---- device processes: which pipelines the runtime runs as one CTA per process (dry run, no CUDA call) ----
+
+
+def _dry_describe(plan, idx):
+    roots, arrays, axis, syms, sptr = materialize(CASES[idx], idx)
+    ex = CudaExecutable(plan)
+    ex.set_option("dry_run", 1)
+    cycles = ex.run_with_symbols(arrays, axis, syms, sptr)
+    return cycles, ex.describe().get("csp"), ex
+
+
+@pytest.mark.parametrize("name", ["example:csp_pipeline#0", "reftest:test_codegen_cspt_pipeline.py#0",
+                                  "reftest:test_codegen_cspt_pipeline.py#2", "reftest:test_codegen_cspt_pipeline.py#3"])
+def test_reference_pipelines_run_as_device_processes(name):
+    # interpreter-runnable tasks, one sender and one receiver per channel, every cross-process hazard ordered by
+    # the channels (vector clocks over the device's channel rules): one CTA per process, the walk's clock unchanged
+    idx = case_index(CASES, name)
+    cycles, mode, ex = _dry_describe(CASES[idx]["plan"], idx)
+    assert mode == "device_processes" and cycles == CASES[idx]["cycles"]
+    ex.set_option("csp_device", 0)
+    assert ex.run_with_symbols(*materialize(CASES[idx], idx)[1:]) == CASES[idx]["cycles"]
+    assert ex.describe()["csp"] == "waves: csp_device option is 0"
+
+
+def test_racy_pipeline_runs_as_waves():
+    # the producer runs ahead of a 4-deep channel and stores into the tile the consumer also stores after its first
+    # receive: nothing orders those stores on the device, so the pipeline keeps the walk's order as waves
+    from _cspt_cases import racy_case
+
+    idx = case_index(CASES, "reftest:test_codegen_cspt_pipeline.py#0")
+    cycles, mode, _ = _dry_describe(racy_case()["plan"], idx)
+    assert mode == "waves: two processes write a tile in an order the channels do not fix"
+
+
+def test_non_pipeline_body_has_no_csp_mode():
+    idx = case_index(CASES, "reftest:test_codegen_cspt_pipeline.py#1")
+    _, mode, _ = _dry_describe(CASES[idx]["plan"], idx)
+    assert mode is None
