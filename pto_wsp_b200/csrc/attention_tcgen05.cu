@@ -22,19 +22,20 @@
 //     result's rounding.  The twelve MMAs per block (M = N = 128, K = 16) run at the f16 tensor rate.  P is the
 //     A operand straight from TMEM (packed f16 pairs written over the S block it came from), V the B operand
 //     from shared memory in its own row-major layout (MN-major).
-// Keys go in blocks of 64 with an online softmax in the base-2 domain; the running row max is kept lazily (a row's O
+// Keys go in blocks of 64 (S in blocks of 128: the N = 128 MMA reads Q once for two key blocks and runs at twice the
+// rate of N = 64, whose operand reads saturate shared memory) with an online softmax in the base-2 domain; the running row max is kept lazily (a row's O
 // and sum are rescaled only when its max grows by more than 2^8), which changes no result beyond rounding.  The row
 // sum uses the f32 probabilities and divides O once at the end, together with the two scales.
 //
 // One CTA per task, 10 warps:
-//   warp 0      TMA producer: Q once (two 128 x 64 K-major f16 boxes), per key block a K^T block (two 64 x 64
-//               MN-major f16 boxes, four stages), 128-byte swizzle.
-//   warp 1      owns TMEM (three S/P buffers of 128 columns: S_j in the first 64 columns of buffer j % 3, then
-//               [P_hi | P_lo] over those 64, two f16 per column; O: columns 384-511) and issues the MMAs from
-//               one thread, S two blocks ahead: S_0 S_1 S_2 PV_0 S_3 PV_1 S_4 ...  The softmax of block j then
-//               overlaps PV_{j-1} and
-//               S_{j+2}, and never waits for an S.  S_{j+3} reuses buffer j % 3: it is issued after PV_j, and
-//               the tensor pipe runs one thread's MMAs in order, so PV_j has read P_j before S_{j+3} lands.
+//   warp 0      TMA producer: Q once (two 128 x 64 K-major f16 boxes), per S block the K^T of its two key blocks
+//               (four 64 x 64 MN-major f16 boxes, two stages of 32 KB), 128-byte swizzle.
+//   warp 1      owns TMEM (three S/P buffers of 128 columns: S block J in buffer J % 3, key block j's S in its
+//               columns 64 (j % 2) .. +63, then [P_hi | P_lo] over those 64, two f16 per column; O: columns
+//               384-511) and issues the MMAs from one thread, S blocks up to three ahead:
+//               S_0 S_1 S_2 PV_0 PV_1 S_3 PV_2 PV_3 S_4 ...  The softmax never waits for an S.  S block J+3 reuses
+//               buffer J % 3: it is issued after PV_{2J+1}, and the tensor pipe runs one thread's MMAs in order, so
+//               both P.V blocks have read their P before S block J+3 lands.
 //   warps 2-5   softmax and epilogue, one row per thread (warp w reads TMEM lanes 32 (w % 4) ..): tcgen05.ld of
 //               the S row into registers, max, exponentials, P_hi / P_lo stored into the row's TMEM lane with
 //               tcgen05.st (and O rescaled in TMEM when the row max or V's scale moves); at the end O / sum
@@ -62,22 +63,25 @@ using namespace tc;
 constexpr int AT_THREADS = 320;
 constexpr int AT_ROWS = 128;   // query rows of a task
 constexpr int AT_D = 128;      // head dim
-constexpr int AT_BN = 64;      // keys per block
+constexpr int AT_BN = 64;      // keys per block (softmax, V split, P.V)
+constexpr int AT_SN = 128;     // keys per S block: two key blocks in one N = 128 MMA chain
 constexpr int BOX = 8192;      // one TMA box / one V chunk: 64 x 64 16-bit elements, 128-byte rows
 constexpr int Q_BYTES = AT_ROWS * AT_D * 2;   // 32 KB
-constexpr int K_BYTES = AT_D * AT_BN * 2;     // 16 KB per stage
+constexpr int K_BYTES = AT_D * AT_BN * 2;     // 16 KB: the K^T of one key block
+constexpr int KS_BYTES = 2 * K_BYTES;         // 32 KB per stage: one S block's two key blocks, 16 KB apart
 constexpr int V_BYTES = AT_BN * AT_D * 2;     // 16 KB: one f16 part of a V block (two 64-dim chunks)
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + Q_BYTES;
-constexpr int KST = 4;                        // K^T stages
+constexpr int KST = 2;                        // K^T stages (S blocks of 128 keys)
 constexpr int NVB = 4;                        // V buffers: the splitters run up to four blocks ahead of the MMAs
-constexpr int OFF_VSP = OFF_K + KST * K_BYTES;  // NVB buffers of [V_hi | V_lo]
+constexpr int OFF_VSP = OFF_K + KST * KS_BYTES;  // NVB buffers of [V_hi | V_lo]
 constexpr int VSP_BYTES = 2 * V_BYTES;
 constexpr int OFF_BAR = OFF_VSP + NVB * VSP_BYTES;  // 224 KB
 constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;  // + barriers / flags / V scales + 1024-byte alignment slack
 static_assert(SMEM_BYTES <= 232448, "attention tile exceeds the 227 KB of shared memory per CTA");
-// TMEM columns: three S/P buffers of 128 (S_j: the first 64 columns of buffer j % 3; P_j: [P_hi | P_lo] over those
-// 64 once S_j has been read, two f16 keys per column), O 384-511
+// TMEM columns: three S/P buffers of 128 (S block J, key blocks 2J and 2J+1, in buffer J % 3; key block j's S in
+// the 64 columns at 64 (j % 2), and P_j, [P_hi | P_lo] with two f16 keys per column, over them once S_j has been
+// read), O 384-511
 constexpr int SPB = 3;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TMEM_SP = 128;  // columns per S/P buffer
@@ -86,11 +90,12 @@ constexpr float kRescaleLog2 = 8.f;  // a row's reference max moves when its max
 constexpr int kPScaleLog2 = 7;       // P (at most 2^8) enters the MMA as P * 2^7 (< 2^15, inside f16's range)
 constexpr int kVScaleMax = 100;      // V's scale 2^k keeps |k| <= 100 (all-zero or non-finite blocks included)
 
-// One S block, S_j = Q . K^T_j over the 128 head dims: eight kind::f16 MMAs (M = 128, N = 64, K = 16) in one asm
-// block, so that the single issuing thread spends one add per operand per MMA.  `a` is the descriptor of Q's
-// first 16 dims (K-major, 128-byte swizzle: +32 B per 16 dims inside a 64-dim box, +16 KB per box), `b` that of
-// the K^T block's first 16 dims (MN-major: +2 KB per 16 dims, +8 KB per box); descriptor address fields count
-// 16-byte units.  The first MMA overwrites D (`accum` = 0), the rest accumulate.
+// One S block, S_J = Q . K^T_J over the 128 head dims: eight kind::f16 MMAs (M = 128, N = 128 -- two key blocks --
+// or 64 for a last lone key block, from `idesc`, K = 16) in one asm block, so that the single issuing thread
+// spends one add per operand per MMA.  `a` is the descriptor of Q's first 16 dims (K-major, 128-byte swizzle: +32 B
+// per 16 dims inside a 64-dim box, +16 KB per box), `b` that of the K^T stage's first 16 dims (MN-major: +2 KB per
+// 16 dims, +8 KB per box, the second key block 16 KB on as the descriptor's leading offset); descriptor address
+// fields count 16-byte units.  The first MMA overwrites D (`accum` = 0), the rest accumulate.
 __device__ __forceinline__ void mma_s_block(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t.reg .b64 bd;\n\t"
@@ -223,9 +228,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint64_t* k_empty = k_full + KST;       // [KST]
     uint64_t* vsp_full = k_empty + KST;     // [NVB] V_hi / V_lo written
     uint64_t* vsp_empty = vsp_full + NVB;   // [NVB] the MMAs read them
-    uint64_t* s_full = vsp_empty + NVB;     // [3] S_j in its buffer
-    uint64_t* p_full = s_full + SPB;        // [3] P_j written over it
-    uint64_t* pv_done = p_full + SPB;       // [2] O holds block j's contribution
+    uint64_t* s_full = vsp_empty + NVB;     // [3] S block J in buffer J % 3
+    uint64_t* p_full = s_full + SPB;        // [6] P_j written over S_j (key block j: j % 6)
+    uint64_t* pv_done = p_full + 2 * SPB;   // [2] O holds block j's contribution
     uint64_t* o_full = pv_done + 2;
     uint64_t* drain = o_full + 1;
     uint64_t* vmax_ready = drain + 1;       // [2] the four splitter warps posted their parts of a block's largest |V|
@@ -233,7 +238,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(vmax_ready + 3);
     volatile int* v_log2 = reinterpret_cast<volatile int*>(vmax_ready + 4);         // [NVB] V's scale exponent of buffer b
     uint32_t* v_part = reinterpret_cast<uint32_t*>(vmax_ready + 4 + (NVB + 1) / 2);  // [2][4] splitter warps' largest |V| bits
-    static_assert((1 + 2 * KST + 2 * NVB + 2 * SPB + 6 + (NVB + 1) / 2 + 4) * 8 <= 512, "barrier block exceeds its 512 bytes");
+    static_assert((1 + 2 * KST + 2 * NVB + 3 * SPB + 8 + (NVB + 1) / 2 + 4) * 8 <= 512, "barrier block exceeds its 512 bytes");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -241,6 +246,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     if (task >= args.ntasks) return;  // whole CTA: nothing initialised yet
     const int64_t* rec = args.rec + task * args.stride;
     const int nb = args.nblocks;
+    const int ns = (nb + 1) / 2;  // S blocks
 
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(q_full), 1);
@@ -248,10 +254,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             mbar_init(smem_u32(&k_full[s]), 1);
             mbar_init(smem_u32(&k_empty[s]), 1);
         }
-        for (int s = 0; s < SPB; ++s) {
-            mbar_init(smem_u32(&s_full[s]), 1);
-            mbar_init(smem_u32(&p_full[s]), 128);
-        }
+        for (int s = 0; s < SPB; ++s) mbar_init(smem_u32(&s_full[s]), 1);
+        for (int s = 0; s < 2 * SPB; ++s) mbar_init(smem_u32(&p_full[s]), 128);
         for (int s = 0; s < NVB; ++s) {
             mbar_init(smem_u32(&vsp_full[s]), 128);
             mbar_init(smem_u32(&vsp_empty[s]), 1);
@@ -289,18 +293,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             mbar_expect_tx(smem_u32(q_full), Q_BYTES);
             tma_load_2d(sQ, &mq, qx, qy, smem_u32(q_full));
             tma_load_2d(sQ + 16384, &mq, qx + 64, qy, smem_u32(q_full));
-            int last_k[KST];  // the block last loaded into each stage
+            int last_k[KST];  // the S block last loaded into each stage
             for (int st = 0; st < KST; ++st) last_k[st] = -1;
-            for (int j = 0; j < nb && !*abort_flag; ++j) {
-                const int st = j % KST;
-                if (j >= KST && !mbar_wait(smem_u32(&k_empty[st]), ((j / KST) & 1) ^ 1u, abort_flag, args.err)) break;
-                mbar_expect_tx(smem_u32(&k_full[st]), K_BYTES);
-                for (int kc = 0; kc < 2; ++kc)  // head-dim rows of K^T, 64 keys per box
-                    tma_load_2d(sK + st * K_BYTES + kc * BOX, &mkt, kx + j * AT_BN, ky + kc * 64, smem_u32(&k_full[st]));
-                last_k[st] = j;
+            for (int jp = 0; jp < ns && !*abort_flag; ++jp) {
+                const int st = jp % KST;
+                if (jp >= KST && !mbar_wait(smem_u32(&k_empty[st]), ((jp / KST) & 1) ^ 1u, abort_flag, args.err)) break;
+                const int nk = min(2, nb - 2 * jp);  // key blocks in this S block
+                mbar_expect_tx(smem_u32(&k_full[st]), nk * K_BYTES);
+                for (int h = 0; h < nk; ++h)
+                    for (int kc = 0; kc < 2; ++kc)  // head-dim rows of K^T, 64 keys per box
+                        tma_load_2d(sK + st * KS_BYTES + h * K_BYTES + kc * BOX, &mkt, kx + (2 * jp + h) * AT_BN,
+                                    ky + kc * 64, smem_u32(&k_full[st]));
+                last_k[st] = jp;
             }
-            // drain: every copy issued has landed before shared memory goes away (block j completes phase
-            // j / KST of its stage's barrier)
+            // drain: every copy issued has landed before shared memory goes away (S block J completes phase
+            // J / KST of its stage's barrier)
             const uint64_t start = globaltimer();
             auto settle = [&](uint32_t bar, uint32_t parity) {
                 while (!mbar_try_wait(bar, parity))
@@ -316,44 +323,47 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            constexpr uint32_t idesc_s = idesc_f16(AT_ROWS, AT_BN, 1);  // A K-major, B MN-major, M = 128, N = 64
+            constexpr uint32_t idesc_s = idesc_f16(AT_ROWS, AT_SN, 1);  // A K-major, B MN-major, M = 128, N = 128
+            constexpr uint32_t idesc_s1 = idesc_f16(AT_ROWS, AT_BN, 1); // N = 64: a last S block of one key block
             constexpr uint32_t idesc_o = idesc_f16(AT_ROWS, AT_D, 1);  // A from TMEM (K-major), B MN-major, M = N = 128
             bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, args.err);
             bool issued = false;
             // descriptors of the operands' first steps; the MMA blocks add constant offsets
-            const uint64_t q_desc = smem_desc(sQ, 16, 1024), k_desc = smem_desc(sK, BOX, 1024);
+            // K^T: MN-major, a stage's two key blocks (64-key atoms of the N dimension) 16 KB apart
+            const uint64_t q_desc = smem_desc(sQ, 16, 1024), k_desc = smem_desc(sK, K_BYTES, 1024);
             const uint64_t v_desc = smem_desc(sVsp, BOX, 1024);  // MN-major: 64-dim chunks 8 KB apart
-            auto sblock = [&](int j) -> bool {  // S_j = Q . K^T_j into buffer j % 3
-                const int kst = j % KST;
-                if (!mbar_wait(smem_u32(&k_full[kst]), (j / KST) & 1, abort_flag, args.err)) return false;
+            auto sblock = [&](int jp) -> bool {  // S block J = Q . K^T of key blocks 2J, 2J+1 into buffer J % 3
+                const int kst = jp % KST;
+                if (!mbar_wait(smem_u32(&k_full[kst]), (jp / KST) & 1, abort_flag, args.err)) return false;
                 tc_fence_after();
-                mma_s_block(tmem_base + static_cast<uint32_t>((j % SPB) * TMEM_SP), q_desc,
-                            k_desc + static_cast<uint64_t>(kst * (K_BYTES >> 4)), idesc_s, 0u);
+                mma_s_block(tmem_base + static_cast<uint32_t>((jp % SPB) * TMEM_SP), q_desc,
+                            k_desc + static_cast<uint64_t>(kst * (KS_BYTES >> 4)), 2 * jp + 1 < nb ? idesc_s : idesc_s1,
+                            0u);
                 issued = true;
                 mma_commit(smem_u32(&k_empty[kst]));
-                mma_commit(smem_u32(&s_full[j % SPB]));
+                mma_commit(smem_u32(&s_full[jp % SPB]));
                 return true;
             };
             // PV_i's inputs: P_i written over S_i, V_i split
             auto pv_ready = [&](int i) -> bool {
-                return mbar_wait(smem_u32(&p_full[i % SPB]), (i / SPB) & 1, abort_flag, args.err) &&
+                return mbar_wait(smem_u32(&p_full[i % (2 * SPB)]), (i / (2 * SPB)) & 1, abort_flag, args.err) &&
                        mbar_wait(smem_u32(&vsp_full[i % NVB]), (i / NVB) & 1, abort_flag, args.err);
             };
             auto pv = [&](int i) {  // O += P_i . V_i as P_lo.V_hi + P_hi.V_lo + P_hi.V_hi
                 const int b = i % NVB;
                 tc_fence_after();
                 const uint64_t vh = v_desc + static_cast<uint64_t>(b * (VSP_BYTES >> 4));
-                mma_pv_block(tmem_base + TMEM_O, tmem_base + static_cast<uint32_t>((i % SPB) * TMEM_SP), vh,
-                             vh + (V_BYTES >> 4), idesc_o, i > 0 ? 1u : 0u);
+                mma_pv_block(tmem_base + TMEM_O, tmem_base + static_cast<uint32_t>(((i >> 1) % SPB) * TMEM_SP + (i & 1) * AT_BN),
+                             vh, vh + (V_BYTES >> 4), idesc_o, i > 0 ? 1u : 0u);
                 mma_commit(smem_u32(&vsp_empty[b]));
                 mma_commit(smem_u32(&pv_done[i & 1]));
             };
-            // issue order S_0 S_1 S_2 | PV_0 S_3 | PV_1 S_4 | ...
-            for (int j = 0; ok && j < nb && j < SPB; ++j) ok = sblock(j);
+            // issue order (S blocks by S block, P.V by key block) S_0 S_1 S_2 | PV_0 PV_1 S_3 | PV_2 PV_3 S_4 | ...
+            for (int jp = 0; ok && jp < ns && jp < SPB; ++jp) ok = sblock(jp);
             for (int j = 0; ok && j < nb; ++j) {
                 ok = pv_ready(j);
                 if (ok) pv(j);
-                if (ok && j + SPB < nb) ok = sblock(j + SPB);
+                if (ok && (j & 1) && (j >> 1) + SPB < ns) ok = sblock((j >> 1) + SPB);
             }
             if (ok && !*abort_flag) mma_commit(smem_u32(o_full));
             if (issued) {  // drain: every MMA issued has completed before TMEM is freed
@@ -460,14 +470,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         int k_v = 0;  // V's scale exponent in O so far
         bool ok = true;
         for (int j = 0; j < nb; ++j) {
-            const int sb = j % SPB;
-            if (!mbar_wait(smem_u32(&s_full[sb]), (j / SPB) & 1, abort_flag, args.err)) {
+            const int sb = (j >> 1) % SPB;  // S block j / 2's buffer (its phase is still the current one for j odd)
+            if (!mbar_wait(smem_u32(&s_full[sb]), ((j >> 1) / SPB) & 1, abort_flag, args.err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             // the S row into registers (both 32-column loads in flight, one wait); P_j then goes over it
-            const uint32_t sp_addr = tmem_base + lane_addr + static_cast<uint32_t>(sb * TMEM_SP);
+            const uint32_t sp_addr = tmem_base + lane_addr + static_cast<uint32_t>(sb * TMEM_SP + (j & 1) * AT_BN);
             uint32_t r[2][32];
             tmem_ld32_async(sp_addr, r[0]);
             tmem_ld32_async(sp_addr + 32, r[1]);
@@ -542,7 +552,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 tmem_wait_st();
             }
             tc_fence_before();
-            mbar_arrive(smem_u32(&p_full[sb]));
+            mbar_arrive(smem_u32(&p_full[j % (2 * SPB)]));
         }
         if (ok && mbar_wait(smem_u32(o_full), 0, abort_flag, args.err)) {
             tc_fence_after();
