@@ -750,7 +750,7 @@ class AttentionCase(Case):
     output, 128-row tiles), run by the fused tcgen05 kernel.  ``--workload attention``."""
 
     name, kernel, traffic_key = "attention", "attention_tile", ""
-    unit, bound, dtype = "TFLOP/s", "tensor", "f16 Q.K^T / f32 softmax / W.V as 3 bf16 terms / f32 out"
+    unit, bound, dtype = "TFLOP/s", "tensor", "f16 Q.K^T / f32 softmax / W.V as 3 f16 terms / f32 out"
     metric = "attention-tile task-loop throughput (both contractions)"
     B, H, QT, L = 8, 16, 8, 1024
 
