@@ -151,7 +151,11 @@ PTOWSP_API int ptowsp_cuda_set_stream(ptowsp_program* prog, void* cuda_stream);
  * tcgen05 kernel; default 1), "csp_device" (0: a CSP pipeline body runs as
  * dependency waves instead of one CTA per process with device channels;
  * changing it drops the cached task tables; default 1 -- ptowsp_cuda_describe
- * reports the form a run took and, for waves, why).
+ * reports the form a run took and, for waves, why), "decode_chunk" (the
+ * split-KV chunk of the built-in paged decode, in tokens, taken as a multiple
+ * of 16 inside 512 .. 1536; 0, the default, chooses it per launch: 1536
+ * unless the launch has too few tasks for 1.5 chunks per SM, then shorter
+ * chunks).
  * "stage_scratch_mb" is clamped to 1 .. 1048576; changing it drops the cached
  * task tables, which were grouped for the old budget. */
 PTOWSP_API int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value);

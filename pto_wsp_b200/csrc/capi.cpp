@@ -100,6 +100,9 @@ int ptowsp_cuda_set_option(ptowsp_program* prog, const char* key, int64_t value)
         // a cached device-process program has no wave records on the device (and waves none for processes)
         if ((value != 0) != (p.opt_csp_device != 0)) p.cached.reset();
         p.opt_csp_device = value != 0;
+    } else if (!std::strcmp(key, "decode_chunk")) {
+        // 0 (automatic) or a token count, taken as a multiple of 16 inside 512 .. 1536 by the launch
+        p.opt_decode_chunk = value < 0 ? 0 : (value > 65536 ? 65536 : value);
     } else if (!std::strcmp(key, "kernel_events")) {
         p.opt_kernel_events = value != 0;
         guarded(prog, [&] { ptowsp::reset_kernel_times(p); return 0; }, 0);

@@ -8,9 +8,12 @@
 // softmax(q K^T / sqrt(D)) V, f32 softmax, f16 output (round to nearest even).
 //
 // HBM-bound: every K/V byte is used for 2*G FLOP (G = 4: ~4 FLOP/B).
-// Split-KV: each task is cut into chunks (1536 tokens for the TMA kernel, the
-// best of 1024 / 1536 / 2048 measured on config 4; 512 for the CUDA-core
-// kernel), one CTA each; empty chunks exit at once.  For the usual pool layout (16-token pages, 16-byte
+// Split-KV: each task is cut into chunks, one CTA each; empty chunks exit at
+// once.  The TMA kernel takes 1536 tokens per chunk (the best of 1024 / 1536 /
+// 2048 measured on config 4) unless the launch has so few tasks that long
+// chunks would leave SMs with one CTA each (a rank's share of config 4 on
+// eight GPUs): then shorter ones, down to 512 (decode_chunk_tokens).  The
+// CUDA-core kernel takes 512.  For the usual pool layout (16-token pages, 16-byte
 // aligned rows) a TMA producer warp streams the pages and four consumer warps
 // run both contractions of a page on warp-level MMAs (paged_decode_tma_kernel,
 // below); the last CTA of a task merges its chunk partials.  Other layouts use
@@ -44,8 +47,11 @@ namespace {
 #ifndef PTOWSP_DECODE_STAGES
 #define PTOWSP_DECODE_STAGES 8
 #endif
-constexpr int kChunk = PTOWSP_DECODE_CHUNK;  // tokens per split-KV chunk of the TMA kernel
+constexpr int kChunk = PTOWSP_DECODE_CHUNK;  // longest split-KV chunk of the TMA kernel (tokens)
 constexpr int kFbChunk = 512;                // tokens per split-KV chunk of the CUDA-core kernel
+constexpr int kMinChunk = 512;               // shortest: the scratch of every launch is sized for 512-token chunks
+static_assert(kChunk % 16 == 0 && kMinChunk % 16 == 0 && kMinChunk <= kChunk && kMinChunk >= std::min(kChunk, kFbChunk),
+              "chunks hold whole 16-token pages, and no chunk is shorter than the one the scratch is sized for");
 constexpr int kDecThreads = 128;  // 4 warps
 constexpr int kHeadDim = 128;
 
@@ -350,7 +356,8 @@ __device__ __forceinline__ uint32_t swz(int tok, int d) {
 template <int G>
 __global__ void __launch_bounds__(kMmaThreads) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap mk,
                                                                      const __grid_constant__ CUtensorMap mv, TaskBatch b,
-                                                                     int chunks, float* __restrict__ partials,
+                                                                     int chunks, int chunk_tokens,
+                                                                     float* __restrict__ partials,
                                                                      unsigned* __restrict__ arrivals) {
     using CB = MmaCombine<G>;
     extern __shared__ uint8_t dsm_raw[];
@@ -373,7 +380,7 @@ __global__ void __launch_bounds__(kMmaThreads) paged_decode_tma_kernel(const __g
         if (chunk == 0 && threadIdx.x == 0) atomicOr(b.err, kErrShape);
         L = Ppt.cols * kMmaPage;
     }
-    const int t0 = chunk * kChunk;
+    const int t0 = chunk * chunk_tokens;
     if (L <= 0 && chunk == 0) {  // no cached tokens: the output is zero
         __half* out = reinterpret_cast<__half*>(b.p[5].base) + rec[5];
         for (int e = threadIdx.x; e < G * kHeadDim; e += kMmaThreads)
@@ -381,8 +388,8 @@ __global__ void __launch_bounds__(kMmaThreads) paged_decode_tma_kernel(const __g
         return;
     }
     if (t0 >= L) return;  // whole CTA leaves together: no barrier has been touched
-    const int nch = (L + kChunk - 1) / kChunk;
-    const int n = min(kChunk, L - t0);
+    const int nch = (L + chunk_tokens - 1) / chunk_tokens;
+    const int n = min(chunk_tokens, L - t0);
     const int npages = (n + kMmaPage - 1) / kMmaPage;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -705,13 +712,32 @@ bool decode_tma_ok(const TaskBatch& b, int page_size) {
 // Scratch of one decode launch: [arrival counters, one per task, 256-byte padded | chunk partials].
 size_t decode_arrivals_bytes(int64_t ntasks) { return (static_cast<size_t>(ntasks) * sizeof(unsigned) + 255) & ~size_t(255); }
 
+// Tokens per chunk of the TMA kernel: `requested` (a multiple of 16 in [kMinChunk, kChunk]) when it is not 0;
+// otherwise the longest of 1536 / 1024 / 768 / 512 that still gives the launch at least 1.5 chunks with work per
+// SM, counting half of each task's longest possible length as its mean.  Shorter chunks only pay when the long ones
+// leave SMs with a single CTA (one CTA's 8-page ring cannot draw an SM's share of HBM); above that their extra
+// CTAs and merges cost more than the shorter tail gains.  Measured on config-4 request mixes (ms per launch, chunk
+// 512 / 768 / 1024 / 1536): 64 requests 0.207 / 0.196 / 0.190 / 0.188, 32 requests 0.115 / 0.112 / 0.108 / 0.107,
+// 16 requests 0.067 / 0.063 / 0.068 / 0.054, 8 requests 0.042 / 0.034 / 0.038 / 0.047 -- the rule takes 1536 for
+// the first three (16 requests: ~305 chunks with work at 1536 on 148 SMs) and 768 for the last (a rank's share of
+// config 4 on eight GPUs: ~134 at 1536, ~201 at 1024, ~268 at 768).
+int decode_chunk_tokens(const TaskBatch& b, int page_size, int requested) {
+    if (requested > 0) return std::min(kChunk, std::max(kMinChunk, requested / 16 * 16));
+    const double max_tokens = static_cast<double>(b.p[3].cols) * page_size;
+    const double want = 1.5 * sm_count();
+    for (int c : {1536, 1024, 768})
+        if (c <= kChunk && static_cast<double>(b.ntasks) * max_tokens / (2.0 * c) >= want) return c;
+    return kMinChunk;
+}
+
 template <int G>
-cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cudaStream_t s) {
+cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cudaStream_t s, int chunk_request) {
     if (b.ntasks <= 0) return cudaSuccess;
     unsigned* arrivals = static_cast<unsigned*>(scratch);
     float* partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + decode_arrivals_bytes(b.ntasks));
     if (decode_tma_ok(b, page_size)) {
-        const int chunks = decode_chunks(b, page_size, kChunk);
+        const int chunk_tokens = decode_chunk_tokens(b, page_size, chunk_request);
+        const int chunks = decode_chunks(b, page_size, chunk_tokens);
         const int64_t grid = b.ntasks * chunks;
         if (grid > 0x7fffffff) return cudaErrorInvalidValue;
         const ParamDesc& K = b.p[1];
@@ -730,7 +756,7 @@ cudaError_t launch_decode_g(const TaskBatch& b, int page_size, void* scratch, cu
                                          cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
             paged_decode_tma_kernel<G><<<static_cast<unsigned>(grid), kMmaThreads, kMmaSmemBytes, s>>>(
-                mk, mv, b, chunks, partials, arrivals);
+                mk, mv, b, chunks, chunk_tokens, partials, arrivals);
             return cudaGetLastError();
         }
     }
@@ -1351,14 +1377,14 @@ size_t paged_decode_scratch_bytes(const TaskBatch& b, int page_size) {
                (G * kHeadDim + 2 * G) * sizeof(float);
 }
 
-cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int, int, void* scratch, size_t scratch_bytes,
-                                cudaStream_t s) {
+cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int chunk_tokens, int, void* scratch,
+                                size_t scratch_bytes, cudaStream_t s) {
     if (scratch_bytes < paged_decode_scratch_bytes(b, page_size)) return cudaErrorInvalidValue;
     switch (b.p[0].rows) {
-        case 1: return launch_decode_g<1>(b, page_size, scratch, s);
-        case 2: return launch_decode_g<2>(b, page_size, scratch, s);
-        case 4: return launch_decode_g<4>(b, page_size, scratch, s);
-        case 8: return launch_decode_g<8>(b, page_size, scratch, s);
+        case 1: return launch_decode_g<1>(b, page_size, scratch, s, chunk_tokens);
+        case 2: return launch_decode_g<2>(b, page_size, scratch, s, chunk_tokens);
+        case 4: return launch_decode_g<4>(b, page_size, scratch, s, chunk_tokens);
+        case 8: return launch_decode_g<8>(b, page_size, scratch, s, chunk_tokens);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1585,10 +1611,10 @@ int paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache
     b.p[4] = param(const_cast<int32_t*>(kv_len), 0, 1, requests, 1, 1, PT_I32, 4);
     b.p[5] = param(out, kHeadDim, 1, qspan, group, kHeadDim, PT_F16, 2);
     switch (group) {
-        case 1: e = launch_decode_g<1>(b, page_size, dec_scratch, s); break;
-        case 2: e = launch_decode_g<2>(b, page_size, dec_scratch, s); break;
-        case 4: e = launch_decode_g<4>(b, page_size, dec_scratch, s); break;
-        default: e = launch_decode_g<8>(b, page_size, dec_scratch, s); break;
+        case 1: e = launch_decode_g<1>(b, page_size, dec_scratch, s, 0); break;
+        case 2: e = launch_decode_g<2>(b, page_size, dec_scratch, s, 0); break;
+        case 4: e = launch_decode_g<4>(b, page_size, dec_scratch, s, 0); break;
+        default: e = launch_decode_g<8>(b, page_size, dec_scratch, s, 0); break;
     }
     if (e != cudaSuccess) {
         *msg = cudaGetErrorString(e);

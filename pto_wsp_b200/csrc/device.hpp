@@ -159,8 +159,8 @@ bool attention_task_ok(const TaskBatch& b, int q_p, int kt_p, int v_p, int o_p, 
 cudaError_t launch_attention(const TaskBatch& b, int q_p, int kt_p, int v_p, int o_p, int L, int scale_mode,
                              int scale_pos, float scale_const, cudaStream_t s);
 
-// Built-ins.
-cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int num_kv_heads, int workers, void* scratch,
+// Built-ins.  `chunk_tokens`: split-KV chunk length of the paged decode (0: chosen from the launch's size).
+cudaError_t launch_paged_decode(const TaskBatch& b, int page_size, int chunk_tokens, int workers, void* scratch,
                                 size_t scratch_bytes, cudaStream_t s);
 size_t paged_decode_scratch_bytes(const TaskBatch& b, int page_size);
 cudaError_t launch_indexer_score(const TaskBatch& b, int workers, cudaStream_t s);

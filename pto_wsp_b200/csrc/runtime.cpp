@@ -1581,7 +1581,7 @@ void launch_batch_body(Program& P, Batch& B, const Node& node, std::vector<Tenso
                 throw Error(PTOWSP_ERR_UNSUPPORTED, "paged_decode_gqa: q and KV cache rows must be 16-byte aligned");
             size_t sb = dev::paged_decode_scratch_bytes(tb, 16);
             void* s = ensure_scratch(P, sb);
-            e = dev::launch_paged_decode(tb, 16, 0, workers, s, sb, P.stream);
+            e = dev::launch_paged_decode(tb, 16, static_cast<int>(P.opt_decode_chunk), workers, s, sb, P.stream);
             break;
         }
         case ImplKind::IndexerScore: {

@@ -261,6 +261,7 @@ struct Program {
     int64_t opt_kernel_events = 0;       // bracket every batch launch with CUDA events (per-kernel device time)
     int64_t opt_fused_attention = 1;     // 0: attention kernels run their stages instead of the fused kernel
     int64_t opt_csp_device = 1;          // 0: CSP pipelines run as dependency waves instead of device processes
+    int64_t opt_decode_chunk = 0;        // paged decode split-KV chunk (tokens); 0: chosen per launch
     std::string csp_mode;                // last run's CSP execution: "" (no pipeline), "device_processes", "waves: why"
     struct KernelEvent { int kernel; cudaEvent_t start, end; };
     std::vector<KernelEvent> kev_pending;  // recorded, not yet read

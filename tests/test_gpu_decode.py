@@ -48,6 +48,25 @@ def test_decode_edge_lengths_vs_oracle(lengths, require_cuda):
     check(dev[5].cpu().numpy(), ref[5])
 
 
+@pytest.mark.parametrize("chunk", [512, 768, 1024, 1536, 1000])
+def test_decode_split_kv_chunk_lengths_vs_oracle(chunk, require_cuda):
+    """Every split-KV chunk length the launch may choose (the `decode_chunk` option forces one; 1000 is taken as
+    992, a multiple of 16), over lengths on either side of each chunk boundary: the chunk partials merge to the
+    oracle's result."""
+    lengths = [0, 1, 511, 512, 513, 767, 768, 769, 992, 993, 1535, 1536, 1537, 3000, 4097]
+    rng = np.random.default_rng(chunk)
+    plan, arrays = workloads.decode_inputs(rng, len(lengths), lengths=lengths)
+    ref = [a.copy() for a in arrays]
+    CpuSim(plan).run(ref, axis_sizes={"b": len(lengths)})
+    ex = CudaExecutable(plan)
+    ex.set_option("decode_chunk", chunk)
+    got = [a.copy() for a in arrays]
+    got[5][...] = np.float16(np.nan)
+    ex.run_with_symbols(got, {"b": len(lengths)}, {}, {})
+    check(got[5], ref[5])
+    assert not got[5][0].any()
+
+
 def test_decode_dense_dyn_axis_runs_fewer_requests(require_cuda):
     rng = np.random.default_rng(1)
     plan, arrays = workloads.decode_inputs(rng, 5, lengths=[100, 200, 300, 400, 500])
