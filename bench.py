@@ -863,6 +863,36 @@ class Dist:
             self.dist.destroy_process_group()
 
 
+def link_ceiling(D: Dist, h2d_bytes: int, d2h_bytes: int, reps: int = 3) -> dict:
+    """The host link's floor for one end-to-end step: the time to copy the step's host->device bytes and its
+    device->host bytes at once (pinned host buffers, one stream per direction, plain ``copy_``, best of ``reps``,
+    max over ranks, which copy at the same time as they do in the timed steps).  ``frac`` of the ``e2e`` line is
+    this floor over the measured step time."""
+    torch, dev = D.torch, D.dev
+    hin = torch.empty(max(h2d_bytes, 1), dtype=torch.uint8, pin_memory=True)
+    hout = torch.empty(max(d2h_bytes, 1), dtype=torch.uint8, pin_memory=True)
+    din = torch.empty(max(h2d_bytes, 1), dtype=torch.uint8, device=dev)
+    dout = torch.zeros(max(d2h_bytes, 1), dtype=torch.uint8, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    best = float("inf")
+    for _ in range(reps):
+        D.barrier()
+        t0 = time.perf_counter()
+        if h2d_bytes:
+            with torch.cuda.stream(s_in):
+                din.copy_(hin, non_blocking=True)
+        if d2h_bytes:
+            with torch.cuda.stream(s_out):
+                hout.copy_(dout, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        best = min(best, time.perf_counter() - t0)
+    best = D.max(best)
+    del hin, hout, din, dout
+    return {"ms": round(best * 1e3, 3),
+            "how": "the step's h2d and d2h bytes copied at once (pinned, one stream per direction, best of "
+                   f"{reps}, max over ranks)"}
+
+
 def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
     import numpy as np
 
@@ -937,6 +967,9 @@ def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
         d2h += tm["d2h_bytes"]
     D.barrier()
     e2e_s = D.max(time.perf_counter() - t0)
+    link = link_ceiling(D, h2d // e2e_steps, d2h // e2e_steps)
+    link["e2e_ms"] = round(e2e_s * 1e3 / e2e_steps, 3)
+    link["frac"] = round(link["ms"] / link["e2e_ms"], 4) if link["e2e_ms"] > 0 else None
 
     work = case.work()
     value = work * args.steps / (ms_max / 1e3) / case.scale
@@ -972,7 +1005,8 @@ def run_case(case: Case, args, D: Dist, rank: int, world: int) -> dict:
                       for k, v in ktimes.items()},
         "e2e": {"value": round(e2e, 4), "unit": case.unit, "h2d_bytes_per_step": h2d // e2e_steps,
                 "d2h_bytes_per_step": d2h // e2e_steps, "steps": e2e_steps,
-                "path": "ShardedExecutable.run_with_symbols (CodegenExecutable surface) with pinned numpy buffers"},
+                "path": "ShardedExecutable.run_with_symbols (CodegenExecutable surface) with pinned numpy buffers",
+                "link": link},
         "clocks": clocks,
         "check": check,
     }
