@@ -151,11 +151,23 @@ cudaError_t launch_rows_t(const TaskBatch& b, int workers, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// Rows in flight per warp for the 128- and 256-column widths (configs 1 and 2).  Measured on one B200 (CUDA events,
+// whole config, GB/s): 128 columns with 2 / 3 / 4 / 5 / 6 / 8 / 12 / 16 rows 6275 / 6132 / 6246 / 6222 / 6345 / 6068 /
+// 4969 / 5001 -- six rows take 62 registers, so four CTAs of 256 threads fit an SM (32 warps, 192 rows in flight),
+// where eight take 71 and leave three (24 warps, the same 192 rows); 256 columns with 2 / 3 / 4 / 5 / 6 / 8 rows
+// 5907 / 5232 / 6149 / 5079 / 5871 / 4100.
+#ifndef PTOWSP_ROWS_RPW128
+#define PTOWSP_ROWS_RPW128 6
+#endif
+#ifndef PTOWSP_ROWS_RPW256
+#define PTOWSP_ROWS_RPW256 4
+#endif
+
 template <class Op>
 cudaError_t launch_rows(const TaskBatch& b, int workers, cudaStream_t s) {
     switch (b.p[0].cols) {
-        case 128: return launch_rows_t<Op, 1, 8>(b, workers, s);
-        case 256: return launch_rows_t<Op, 2, 4>(b, workers, s);
+        case 128: return launch_rows_t<Op, 1, PTOWSP_ROWS_RPW128>(b, workers, s);
+        case 256: return launch_rows_t<Op, 2, PTOWSP_ROWS_RPW256>(b, workers, s);
         case 512: return launch_rows_t<Op, 4, 2>(b, workers, s);
         case 1024: return launch_rows_t<Op, 8, 1>(b, workers, s);
         default: return cudaErrorInvalidValue;
