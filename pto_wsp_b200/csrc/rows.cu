@@ -155,7 +155,9 @@ cudaError_t launch_rows_t(const TaskBatch& b, int workers, cudaStream_t s) {
 // whole config, GB/s): 128 columns with 2 / 3 / 4 / 5 / 6 / 8 / 12 / 16 rows 6275 / 6132 / 6246 / 6222 / 6345 / 6068 /
 // 4969 / 5001 -- six rows take 62 registers, so four CTAs of 256 threads fit an SM (32 warps, 192 rows in flight),
 // where eight take 71 and leave three (24 warps, the same 192 rows); 256 columns with 2 / 3 / 4 / 5 / 6 / 8 rows
-// 5907 / 5232 / 6149 / 5079 / 5871 / 4100.
+// 5907 / 5232 / 6149 / 5079 / 5871 / 4100; with a minimum of CTAs per SM forced by launch bounds (another box, where
+// four rows gave 5804): six rows at three CTAs 5858, five or six at four CTAs and eight at three spill (5052 / 4421 /
+// 3719), eight at two CTAs 4122.
 #ifndef PTOWSP_ROWS_RPW128
 #define PTOWSP_ROWS_RPW128 6
 #endif
